@@ -1,0 +1,194 @@
+/*
+ * oasr_b200.h -- C ABI of the B200 (sm_100a) backend for OpenASR's inference
+ * hot path: quantized-weight GGML_OP_MUL_MAT and f16-KV GGML_OP_FLASH_ATTN_EXT,
+ * plus the KV write (SET_ROWS) and the greedy first-max argmax that sit next
+ * to them in every decoder step.
+ *
+ * The reference reaches its device backends through ggml's backend/plugin C
+ * ABI declared in crates/openasr-core/src/ggml_runtime/ffi.rs:399-1057.  This
+ * header exposes the same operations as plain functions over plain pointers
+ * and sizes (no torch or ggml types), so the openasr-core side needs only a
+ * thin `extern "C"` block.  Each entry point names the
+ * reference interface it replaces.
+ *
+ * Conventions (identical to ggml's):
+ *   - a tensor is {type, data, ne[4], nb[4]}: ne0 is the fastest dimension,
+ *     nb are byte strides (ffi.rs:24-30, GgmlTensorLayoutPrefix);
+ *   - every function returns a ggml_status value (ffi.rs:102-117) and never
+ *     aborts the process;
+ *   - device tensors live in this device's memory; ops are enqueued on the
+ *     backend's stream and complete asynchronously; oasr_b200_synchronize()
+ *     returns the merged submit + completion status (ffi.rs:107-113);
+ *   - a device-side failure (CUDA error, kernel error word) poisons the
+ *     backend: later calls return OASR_STATUS_BACKEND_POISONED (cpu_graph.rs:7893-7935).
+ *   - one backend instance serves one stream at a time (ffi.rs:334-336,
+ *     "one graph compute per backend at a time"): its activation scratch is
+ *     shared by the ops it enqueues.
+ */
+#ifndef OASR_B200_H
+#define OASR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OASR_B200_ABI_VERSION 1
+
+/* enum ggml_status -- ffi.rs:102-117 */
+enum oasr_status {
+    OASR_STATUS_ALLOC_FAILED = -2,
+    OASR_STATUS_FAILED = -1,
+    OASR_STATUS_SUCCESS = 0,
+    OASR_STATUS_ABORTED = 1,
+    OASR_STATUS_EXECUTION_FAILED = 2,
+    OASR_STATUS_DEVICE_LOST = 3,
+    OASR_STATUS_BACKEND_POISONED = 4,
+};
+
+/* enum ggml_type ids -- ffi.rs:338-346 */
+enum oasr_type {
+    OASR_TYPE_F32 = 0,
+    OASR_TYPE_F16 = 1,
+    OASR_TYPE_Q4_0 = 2,
+    OASR_TYPE_Q8_0 = 8,
+    OASR_TYPE_Q4_K = 12,
+    OASR_TYPE_I32 = 26,
+    OASR_TYPE_I64 = 27,
+};
+
+/* ggml_prec -- ffi.rs:15-16 (GGML_PREC_DEFAULT / GGML_PREC_F32) */
+enum oasr_prec {
+    OASR_PREC_DEFAULT = 0,
+    OASR_PREC_F32 = 10,
+};
+
+/* ops answered by oasr_b200_supports_op (ggml_backend_dev_supports_op, ffi.rs:566-598) */
+enum oasr_op {
+    OASR_OP_MUL_MAT = 1,
+    OASR_OP_FLASH_ATTN_EXT = 2,
+    OASR_OP_SET_ROWS = 3,
+    OASR_OP_ARGMAX_FIRST = 4,
+};
+
+/* GGML_BACKEND_GRAPH_CANCEL_* -- ffi.rs:118-124 */
+enum oasr_cancel {
+    OASR_CANCEL_NATIVE = 1,
+    OASR_CANCEL_OBSERVATION_SUBMISSION_CHECKPOINT = 1,
+    OASR_CANCEL_OBSERVATION_GRAPH_COMPLETION = 2,
+};
+
+/* Prefix of struct ggml_tensor the reference reads (ffi.rs:24-30). */
+typedef struct oasr_tensor {
+    int32_t type;  /* enum oasr_type */
+    int32_t flags; /* reserved, 0 */
+    void *data;    /* device pointer (host pointer only where a function says so) */
+    int64_t ne[4]; /* elements per dimension, ne[0] fastest */
+    int64_t nb[4]; /* byte strides */
+} oasr_tensor;
+
+typedef struct oasr_device_props {
+    char name[64];          /* ggml_backend_dev_name, e.g. "CUDA0" */
+    char description[256];  /* ggml_backend_dev_description */
+    int32_t ordinal;
+    int32_t device_type;    /* GGML_BACKEND_DEVICE_TYPE_GPU = 1 (ffi.rs:93-97) */
+    int32_t sm_count;
+    int32_t cc_major, cc_minor;
+    int32_t cancel_mechanism;   /* OASR_CANCEL_NATIVE */
+    int32_t cancel_observation; /* OASR_CANCEL_OBSERVATION_SUBMISSION_CHECKPOINT */
+    uint64_t memory_total, memory_free; /* ggml_backend_dev_memory */
+} oasr_device_props;
+
+typedef struct oasr_mem_stats {
+    uint64_t weight_bytes;   /* resident weights (usage WEIGHTS, ffi.rs:141) */
+    uint64_t scratch_bytes;  /* activation scratch (usage COMPUTE, ffi.rs:142) */
+    uint64_t device_total, device_free;
+    int64_t n_weights;
+} oasr_mem_stats;
+
+/* ggml_abort_callback (ffi.rs:334-336): return nonzero to abort. Lock-free. */
+typedef int (*oasr_abort_callback)(void *data);
+
+typedef struct oasr_backend oasr_backend; /* one device + one stream */
+typedef struct oasr_weight oasr_weight;   /* a resident quantized weight */
+
+/* ---- device / backend lifecycle (ffi.rs:566-598: ggml_backend_dev_*) ------ */
+int oasr_b200_device_count(int32_t *count);
+int oasr_b200_init(int32_t ordinal, oasr_backend **out);       /* ggml_backend_dev_init */
+int oasr_b200_free(oasr_backend *be);                          /* ggml_backend_free */
+int oasr_b200_props(oasr_backend *be, oasr_device_props *out); /* ggml_backend_dev_get_props */
+/* 1 if supported, 0 if not (ggml_backend_dev_supports_op; probe in backend.rs:295-323) */
+int oasr_b200_supports_op(oasr_backend *be, int32_t op, const oasr_tensor *src0, const oasr_tensor *src1);
+/* Enqueue subsequent work on `stream` (a cudaStream_t of this device; NULL =
+ * the backend's own stream). */
+int oasr_b200_set_stream(oasr_backend *be, void *stream);
+void *oasr_b200_get_stream(oasr_backend *be);
+int oasr_b200_synchronize(oasr_backend *be);                   /* merged completion status */
+int oasr_b200_set_abort_callback(oasr_backend *be, oasr_abort_callback cb, void *data);
+int oasr_b200_mem_stats(oasr_backend *be, oasr_mem_stats *out);
+const char *oasr_b200_last_error(oasr_backend *be);
+/* Pre-size the activation scratch (bytes) so no later op allocates. */
+int oasr_b200_reserve_scratch(oasr_backend *be, size_t bytes);
+
+/* ---- resident weights (ggml_backend_dev_buffer_from_host_ptr, ffi.rs:588;
+ *      cpu_graph.rs:9497 maybe_allocate_weight_buffer_from_host_ptr) ------------
+ * `host` holds ggml row-major blocks for a [ne0=K, ne1=N, ne2, ne3] tensor of
+ * `type`; the raw blocks are copied to HBM and repacked without dequantizing
+ * (Q8_0/Q4_0: quants and fp16 scales split into two 16-byte-aligned planes;
+ * Q4_K and F16/F32 keep ggml's layout).  The host buffer may be freed after
+ * the call returns. */
+int oasr_b200_weight_upload(oasr_backend *be, const void *host, size_t bytes, int32_t type,
+                            const int64_t ne[4], oasr_weight **out);
+int oasr_b200_weight_free(oasr_backend *be, oasr_weight *w);
+/* Copy the resident weight back as ggml bytes (inverse of the repack). */
+int oasr_b200_weight_download(oasr_backend *be, const oasr_weight *w, void *host, size_t bytes);
+int oasr_b200_weight_info(const oasr_weight *w, int32_t *type, int64_t ne[4], uint64_t *device_bytes);
+
+/* ---- hot-path ops ------------------------------------------------------------ */
+/* GGML_OP_MUL_MAT (ggml_mul_mat ffi.rs:694; builder cpu_graph.rs:3616-3686):
+ * dst[n, m, i2, i3] = sum_k w[k, n, i2/r2, i3/r3] * x[k, m, i2, i3].
+ * x: f32 or f16 device tensor [K, M, ne2, ne3] with contiguous rows; dst: f32
+ * [N, M, ne2, ne3].  Activations are quantized to the weight type's ggml
+ * vec_dot type (Q8_0/Q4_0 -> q8_0 per 32, Q4_K -> q8_K per 256) and dotted
+ * with integer block arithmetic and f32 accumulation; prec = OASR_PREC_F32
+ * (ggml_mul_mat_set_prec, ffi.rs:699) keeps f32 activations for F16 weights. */
+int oasr_b200_mul_mat(oasr_backend *be, const oasr_weight *w, const oasr_tensor *x, oasr_tensor *dst,
+                      int32_t prec);
+
+/* GGML_OP_FLASH_ATTN_EXT (ggml_flash_attn_ext ffi.rs:755-764; builder
+ * cpu_graph.rs:4144-4220, checks :7476-7519).
+ * q f32 [D, n_q, H, S]; k, v f16 or f32 [D, n_kv, H_kv, S] (rows contiguous,
+ * other strides free: KV-cache views); mask NULL or f16 [>=n_kv, >=n_q, H|1, S|1];
+ * dst f32 [D, H, n_q, S] (ggml's permuted output).  H % H_kv == 0 (GQA).
+ * max_bias and logit_softcap must be 0 (every hot call site passes 0). */
+int oasr_b200_flash_attn_ext(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k,
+                             const oasr_tensor *v, const oasr_tensor *mask, float scale, float max_bias,
+                             float logit_softcap, int32_t prec, oasr_tensor *dst);
+
+/* GGML_OP_SET_ROWS (ggml_set_rows ffi.rs:884; cpu_graph.rs:4882): write f32 rows
+ * of src [D, n, ne2, ne3] into dst (f16|f32) rows rows[i] (I32 or I64 [n]). */
+int oasr_b200_set_rows(oasr_backend *be, oasr_tensor *dst, const oasr_tensor *src, const oasr_tensor *rows);
+
+/* First-max argmax (ggml_argmax_first ffi.rs:706; cpu_graph.rs:3750-3765): for
+ * each row of f32 logits [n, rows] the lowest index whose finite value is
+ * maximal; out I32 [rows]. */
+int oasr_b200_argmax_first(oasr_backend *be, const oasr_tensor *logits, oasr_tensor *out);
+
+/* ---- host-side helpers (no device work) --------------------------------------- */
+/* ggml_row_size (ffi.rs:619) */
+int64_t oasr_b200_row_size(int32_t type, int64_t ne0);
+/* ggml_quantize_chunk (ffi.rs:623): quantize nrows rows of n_per_row floats
+ * starting at row start_row into ggml blocks (Q8_0, Q4_0, Q4_K, F16). Returns
+ * bytes written or a negative status. */
+int64_t oasr_b200_quantize_chunk(int32_t type, const float *src, void *dst, int64_t start_row, int64_t nrows,
+                                 int64_t n_per_row);
+/* Deterministic synthetic data: x[i] = mean + std * N(0,1) from SplitMix64
+ * (state seed + (offset+i+1)*0x9E3779B97F4A7C15) and Box-Muller on pairs. */
+int oasr_b200_synth_normal(uint64_t seed, uint64_t offset, float *x, int64_t n, float mean, float std);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OASR_B200_H */

@@ -1,0 +1,349 @@
+"""Python host mirror of the backend operator interface.
+
+Mirrors the calls openasr-core's ggml runtime makes for the hot path
+(crates/openasr-core/src/ggml_runtime/cpu_graph.rs: mul_mat :3616,
+mul_mat_with_precision :3624, flash_attn_ext :4122,
+flash_attn_ext_with_precision :4144, set_rows :4882, top1_argmax_first_max
+:3752) and its status mapping (:8380-8405), over the C ABI in
+include/oasr_b200.h.  Device memory and streams come from PyTorch tensors; all
+arithmetic runs in liboasr_b200.so.  There is no CPU fallback: importing this
+module fails if the library is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboasr_b200.so")
+
+F32, F16, Q4_0, Q8_0, Q4_K, I32, I64 = 0, 1, 2, 8, 12, 26, 27
+PREC_DEFAULT, PREC_F32 = 0, 10
+OP_MUL_MAT, OP_FLASH_ATTN_EXT, OP_SET_ROWS, OP_ARGMAX_FIRST = 1, 2, 3, 4
+
+STATUS_ALLOC_FAILED, STATUS_FAILED, STATUS_SUCCESS = -2, -1, 0
+STATUS_ABORTED, STATUS_EXECUTION_FAILED, STATUS_DEVICE_LOST, STATUS_BACKEND_POISONED = 1, 2, 3, 4
+
+
+class GgmlBackendError(RuntimeError):
+    """Typed failure of a backend call (cpu_graph.rs:8380-8405 GgmlCpuGraphError)."""
+
+    def __init__(self, status: int, reason: str):
+        super().__init__(f"{self.__class__.__name__}(status={status}): {reason}")
+        self.status = status
+        self.reason = reason
+
+
+class UnsupportedInputs(GgmlBackendError):
+    pass
+
+
+class AllocFailed(GgmlBackendError):
+    pass
+
+
+class Aborted(GgmlBackendError):
+    pass
+
+
+class ExecutionFailed(GgmlBackendError):
+    pass
+
+
+class DeviceLost(GgmlBackendError):
+    pass
+
+
+class BackendPoisoned(GgmlBackendError):
+    pass
+
+
+_ERRORS = {
+    STATUS_FAILED: UnsupportedInputs,
+    STATUS_ALLOC_FAILED: AllocFailed,
+    STATUS_ABORTED: Aborted,
+    STATUS_EXECUTION_FAILED: ExecutionFailed,
+    STATUS_DEVICE_LOST: DeviceLost,
+    STATUS_BACKEND_POISONED: BackendPoisoned,
+}
+
+
+class OasrTensor(ctypes.Structure):
+    _fields_ = [
+        ("type", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
+        ("data", ctypes.c_void_p),
+        ("ne", ctypes.c_int64 * 4),
+        ("nb", ctypes.c_int64 * 4),
+    ]
+
+
+class OasrDeviceProps(ctypes.Structure):
+    _fields_ = [
+        ("name", ctypes.c_char * 64),
+        ("description", ctypes.c_char * 256),
+        ("ordinal", ctypes.c_int32),
+        ("device_type", ctypes.c_int32),
+        ("sm_count", ctypes.c_int32),
+        ("cc_major", ctypes.c_int32),
+        ("cc_minor", ctypes.c_int32),
+        ("cancel_mechanism", ctypes.c_int32),
+        ("cancel_observation", ctypes.c_int32),
+        ("memory_total", ctypes.c_uint64),
+        ("memory_free", ctypes.c_uint64),
+    ]
+
+
+class OasrMemStats(ctypes.Structure):
+    _fields_ = [
+        ("weight_bytes", ctypes.c_uint64),
+        ("scratch_bytes", ctypes.c_uint64),
+        ("device_total", ctypes.c_uint64),
+        ("device_free", ctypes.c_uint64),
+        ("n_weights", ctypes.c_int64),
+    ]
+
+
+ABORT_CB = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p)
+
+# every symbol include/oasr_b200.h declares, with (argtypes, restype)
+_P, _I32, _I64, _U64, _F, _SZ = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_uint64, ctypes.c_float, ctypes.c_size_t
+_TP = ctypes.POINTER(OasrTensor)
+SIGNATURES = {
+    "oasr_b200_device_count": ([ctypes.POINTER(_I32)], ctypes.c_int),
+    "oasr_b200_init": ([_I32, ctypes.POINTER(_P)], ctypes.c_int),
+    "oasr_b200_free": ([_P], ctypes.c_int),
+    "oasr_b200_props": ([_P, ctypes.POINTER(OasrDeviceProps)], ctypes.c_int),
+    "oasr_b200_supports_op": ([_P, _I32, _TP, _TP], ctypes.c_int),
+    "oasr_b200_set_stream": ([_P, _P], ctypes.c_int),
+    "oasr_b200_get_stream": ([_P], _P),
+    "oasr_b200_synchronize": ([_P], ctypes.c_int),
+    "oasr_b200_set_abort_callback": ([_P, ABORT_CB, _P], ctypes.c_int),
+    "oasr_b200_mem_stats": ([_P, ctypes.POINTER(OasrMemStats)], ctypes.c_int),
+    "oasr_b200_last_error": ([_P], ctypes.c_char_p),
+    "oasr_b200_reserve_scratch": ([_P, _SZ], ctypes.c_int),
+    "oasr_b200_weight_upload": ([_P, _P, _SZ, _I32, ctypes.POINTER(_I64), ctypes.POINTER(_P)], ctypes.c_int),
+    "oasr_b200_weight_free": ([_P, _P], ctypes.c_int),
+    "oasr_b200_weight_download": ([_P, _P, _P, _SZ], ctypes.c_int),
+    "oasr_b200_weight_info": ([_P, ctypes.POINTER(_I32), ctypes.POINTER(_I64), ctypes.POINTER(_U64)], ctypes.c_int),
+    "oasr_b200_mul_mat": ([_P, _P, _TP, _TP, _I32], ctypes.c_int),
+    "oasr_b200_flash_attn_ext": ([_P, _TP, _TP, _TP, _TP, _F, _F, _F, _I32, _TP], ctypes.c_int),
+    "oasr_b200_set_rows": ([_P, _TP, _TP, _TP], ctypes.c_int),
+    "oasr_b200_argmax_first": ([_P, _TP, _TP], ctypes.c_int),
+    "oasr_b200_row_size": ([_I32, _I64], _I64),
+    "oasr_b200_quantize_chunk": ([_I32, _P, _P, _I64, _I64, _I64], _I64),
+    "oasr_b200_synth_normal": ([_U64, _U64, _P, _I64, _F, _F], ctypes.c_int),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load liboasr_b200.so (raises if it has not been built: no fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing; build it with `python -m openasr_b200.build`")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (args, res) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes, fn.restype = args, res
+        _lib = L
+    return _lib
+
+
+# ---- host helpers (no device) -----------------------------------------------------------
+def row_size(ggml_type: int, ne0: int) -> int:
+    return int(lib().oasr_b200_row_size(ggml_type, ne0))
+
+
+def quantize(ggml_type: int, x: np.ndarray) -> np.ndarray:
+    """ggml_quantize_chunk over the rows of a 2-D f32 array -> uint8 (rows, row_bytes)."""
+    x = np.ascontiguousarray(x, np.float32)
+    if x.ndim == 1:
+        x = x[None]
+    rows, n = x.shape
+    rs = row_size(ggml_type, n)
+    if rs < 0:
+        raise UnsupportedInputs(STATUS_FAILED, f"row of {n} elements is not a multiple of the block size")
+    out = np.empty((rows, rs), np.uint8)
+    got = lib().oasr_b200_quantize_chunk(ggml_type, x.ctypes.data, out.ctypes.data, 0, rows, n)
+    if got != rows * rs:
+        raise UnsupportedInputs(STATUS_FAILED, f"quantize_chunk returned {got}")
+    return out
+
+
+def synth_normal(seed: int, n: int, mean: float = 0.0, std: float = 1.0, offset: int = 0) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    rc = lib().oasr_b200_synth_normal(seed & (2**64 - 1), offset, out.ctypes.data, n, mean, std)
+    if rc != 0:
+        raise UnsupportedInputs(rc, "synth_normal")
+    return out
+
+
+# ---- tensor descriptors -----------------------------------------------------------------
+_TORCH_TYPES = None
+
+
+def _torch_type(t) -> int:
+    import torch
+
+    m = {torch.float32: F32, torch.float16: F16, torch.int32: I32, torch.int64: I64}
+    if t.dtype not in m:
+        raise UnsupportedInputs(STATUS_FAILED, f"unsupported tensor dtype {t.dtype}")
+    return m[t.dtype]
+
+
+def describe(t, ggml_type: int | None = None) -> OasrTensor:
+    """oasr_tensor for a torch tensor: ne = reversed shape, nb = reversed byte strides."""
+    d = OasrTensor()
+    d.type = _torch_type(t) if ggml_type is None else ggml_type
+    d.flags = 0
+    d.data = t.data_ptr()
+    shape = list(t.shape)[::-1] + [1] * (4 - t.dim())
+    es = t.element_size()
+    strides = [s * es for s in list(t.stride())[::-1]]
+    while len(strides) < 4:
+        strides.append(strides[-1] * shape[len(strides) - 1] if strides else es)
+    d.ne[:] = shape[:4]
+    d.nb[:] = strides[:4]
+    return d
+
+
+class Weight:
+    """A resident quantized weight (ggml [K, N, ne2, ne3])."""
+
+    def __init__(self, backend: "Backend", handle: int, ggml_type: int, ne):
+        self.backend = backend
+        self.handle = ctypes.c_void_p(handle)
+        self.type = ggml_type
+        self.ne = list(ne)
+
+    @property
+    def K(self) -> int:
+        return self.ne[0]
+
+    @property
+    def N(self) -> int:
+        return self.ne[1]
+
+    def device_bytes(self) -> int:
+        nb = ctypes.c_uint64()
+        lib().oasr_b200_weight_info(self.handle, None, None, ctypes.byref(nb))
+        return nb.value
+
+    def download(self) -> np.ndarray:
+        rows = self.ne[1] * self.ne[2] * self.ne[3]
+        out = np.empty((rows, row_size(self.type, self.ne[0])), np.uint8)
+        self.backend._check(lib().oasr_b200_weight_download(self.backend.handle, self.handle, out.ctypes.data, out.nbytes))
+        return out
+
+    def free(self) -> None:
+        if self.handle:
+            lib().oasr_b200_weight_free(self.backend.handle, self.handle)
+            self.handle = ctypes.c_void_p(0)
+
+
+class Backend:
+    """One device + one stream (ggml_backend_dev_init / ggml_backend_t)."""
+
+    def __init__(self, ordinal: int = 0):
+        h = ctypes.c_void_p()
+        rc = lib().oasr_b200_init(ordinal, ctypes.byref(h))
+        if rc != 0:
+            raise _ERRORS.get(rc, GgmlBackendError)(rc, f"oasr_b200_init({ordinal}) failed")
+        self.handle = h
+        self.ordinal = ordinal
+        self._abort_cb = None
+
+    # -- status mapping (cpu_graph.rs:8380-8405) --
+    def _check(self, rc: int) -> None:
+        if rc != 0:
+            reason = lib().oasr_b200_last_error(self.handle)
+            raise _ERRORS.get(rc, GgmlBackendError)(rc, reason.decode() if reason else "")
+
+    def close(self) -> None:
+        if self.handle:
+            lib().oasr_b200_free(self.handle)
+            self.handle = ctypes.c_void_p(0)
+
+    def props(self) -> dict:
+        p = OasrDeviceProps()
+        self._check(lib().oasr_b200_props(self.handle, ctypes.byref(p)))
+        return {f: (getattr(p, f).decode() if isinstance(getattr(p, f), bytes) else getattr(p, f)) for f, _ in p._fields_}
+
+    def mem_stats(self) -> dict:
+        s = OasrMemStats()
+        self._check(lib().oasr_b200_mem_stats(self.handle, ctypes.byref(s)))
+        return {f: getattr(s, f) for f, _ in s._fields_}
+
+    def set_stream(self, stream) -> None:
+        """Enqueue on a torch.cuda.Stream (or raw cudaStream_t int); None = own stream."""
+        ptr = 0 if stream is None else (stream if isinstance(stream, int) else stream.cuda_stream)
+        self._check(lib().oasr_b200_set_stream(self.handle, ptr))
+
+    def stream_ptr(self) -> int:
+        return lib().oasr_b200_get_stream(self.handle) or 0
+
+    def synchronize(self) -> None:
+        self._check(lib().oasr_b200_synchronize(self.handle))
+
+    def reserve_scratch(self, nbytes: int) -> None:
+        self._check(lib().oasr_b200_reserve_scratch(self.handle, nbytes))
+
+    def set_abort_callback(self, fn) -> None:
+        """fn() -> bool; polled before every enqueue (ggml_abort_callback)."""
+        if fn is None:
+            self._abort_cb = None
+            self._check(lib().oasr_b200_set_abort_callback(self.handle, ABORT_CB(0), None))
+            return
+        self._abort_cb = ABORT_CB(lambda _data: 1 if fn() else 0)
+        self._check(lib().oasr_b200_set_abort_callback(self.handle, self._abort_cb, None))
+
+    def supports_op(self, op: int, src0: OasrTensor, src1: OasrTensor | None = None) -> bool:
+        return bool(lib().oasr_b200_supports_op(self.handle, op, ctypes.byref(src0),
+                                                ctypes.byref(src1) if src1 is not None else None))
+
+    def device_supports_matmul_for_type(self, ggml_type: int) -> bool:
+        """backend.rs:295-323: probe mul_mat(W[K=256, N=32] of type T, X f32 [256, 8])."""
+        w = OasrTensor(type=ggml_type, data=None)
+        w.ne[:] = [256, 32, 1, 1]
+        x = OasrTensor(type=F32, data=None)
+        x.ne[:] = [256, 8, 1, 1]
+        return self.supports_op(OP_MUL_MAT, w, x)
+
+    # -- weights (cpu_graph.rs:9497 maybe_allocate_weight_buffer_from_host_ptr) --
+    def upload_weight(self, blocks: np.ndarray, ggml_type: int, ne) -> Weight:
+        blocks = np.ascontiguousarray(blocks)
+        ne = list(ne) + [1] * (4 - len(ne))
+        arr = (ctypes.c_int64 * 4)(*ne)
+        h = ctypes.c_void_p()
+        self._check(lib().oasr_b200_weight_upload(self.handle, blocks.ctypes.data, blocks.nbytes, ggml_type, arr,
+                                                  ctypes.byref(h)))
+        return Weight(self, h.value, ggml_type, ne)
+
+    # -- ops --
+    def mul_mat(self, w: Weight, x, out, prec: int = PREC_DEFAULT) -> None:
+        self._check(lib().oasr_b200_mul_mat(self.handle, w.handle, ctypes.byref(describe(x)), ctypes.byref(describe(out)), prec))
+
+    def flash_attn_ext(self, q, k, v, mask, scale: float, out, max_bias: float = 0.0, logit_softcap: float = 0.0,
+                       prec: int = PREC_DEFAULT) -> None:
+        md = describe(mask) if mask is not None else None
+        self._check(lib().oasr_b200_flash_attn_ext(
+            self.handle, ctypes.byref(describe(q)), ctypes.byref(describe(k)), ctypes.byref(describe(v)),
+            ctypes.byref(md) if md is not None else None, scale, max_bias, logit_softcap, prec, ctypes.byref(describe(out))))
+
+    def set_rows(self, dst, src, rows) -> None:
+        self._check(lib().oasr_b200_set_rows(self.handle, ctypes.byref(describe(dst)), ctypes.byref(describe(src)),
+                                             ctypes.byref(describe(rows))))
+
+    def argmax_first(self, logits, out) -> None:
+        self._check(lib().oasr_b200_argmax_first(self.handle, ctypes.byref(describe(logits)), ctypes.byref(describe(out))))
+
+
+def device_count() -> int:
+    n = ctypes.c_int32()
+    lib().oasr_b200_device_count(ctypes.byref(n))
+    return n.value

@@ -1,0 +1,399 @@
+// backend.cu -- device/backend lifecycle, status and poisoning, activation
+// scratch, resident weight upload (raw quantized blocks, repacked without
+// dequantizing) and supports_op.  Mirrors the ggml backend device interface
+// the reference binds in crates/openasr-core/src/ggml_runtime/ffi.rs:566-598
+// and its status contract (ffi.rs:102-117, cpu_graph.rs:7893-7935, :8380-8405).
+
+#include <math.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <cstdlib>
+#include <vector>
+
+#include "common.cuh"
+
+using namespace oasr;
+
+namespace {
+constexpr size_t kCounterSlots = 1 << 16;  // flash-decode split counters
+constexpr size_t kDefaultScratch = 64ull << 20;
+
+uint16_t host_f32_to_f16(float f) { return __half_as_ushort(__float2half_rn(f)); }
+float host_f16_to_f32(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+// ggml CPU evaluates GELU through a 65536-entry fp16 table:
+// table[h] = fp16(0.5 x (1 + tanh(sqrt(2/pi) x (1 + 0.044715 x^2)))), x = fp32(h).
+void build_gelu_table(std::vector<uint16_t> &t) {
+    t.resize(65536);
+    const float A = 0.044715f, S = 0.79788456080286535587989211986876f;
+    for (uint32_t i = 0; i < 65536; ++i) {
+        const float x = host_f16_to_f32((uint16_t)i);
+        const float inner = S * x * (1.0f + A * x * x);
+        t[i] = host_f32_to_f16(0.5f * x * (1.0f + tanhf(inner)));
+    }
+}
+}  // namespace
+
+int oasr_internal_fail(oasr_backend *be, int status, const std::string &msg) {
+    if (be) be->last_error = msg;
+    return status;
+}
+
+int oasr_internal_cuda_fail(oasr_backend *be, cudaError_t e, const char *what, int line) {
+    char buf[512];
+    snprintf(buf, sizeof buf, "%s failed at backend.cu:%d: %s", what, line, cudaGetErrorString(e));
+    int st = e == cudaErrorMemoryAllocation ? OASR_STATUS_ALLOC_FAILED : OASR_STATUS_EXECUTION_FAILED;
+    if (e == cudaErrorIllegalAddress || e == cudaErrorLaunchFailure || e == cudaErrorIllegalInstruction ||
+        e == cudaErrorMisalignedAddress || e == cudaErrorHardwareStackError || e == cudaErrorECCUncorrectable ||
+        e == cudaErrorNoDevice || e == cudaErrorDevicesUnavailable)
+        st = OASR_STATUS_DEVICE_LOST;
+    if (be && st != OASR_STATUS_ALLOC_FAILED) {
+        int expected = 0;
+        be->poisoned.compare_exchange_strong(expected, st == OASR_STATUS_DEVICE_LOST ? OASR_STATUS_DEVICE_LOST
+                                                                                     : OASR_STATUS_BACKEND_POISONED);
+    }
+    return oasr_internal_fail(be, st, buf);
+}
+
+int oasr_internal_precheck(oasr_backend *be) {
+    if (!be) return OASR_STATUS_FAILED;
+    int p = be->poisoned.load();
+    if (p) return OASR_STATUS_BACKEND_POISONED;
+    if (be->abort_cb && be->abort_cb(be->abort_data)) return OASR_STATUS_ABORTED;
+    if (cudaSetDevice(be->device) != cudaSuccess) return OASR_STATUS_DEVICE_LOST;
+    return OASR_STATUS_SUCCESS;
+}
+
+int oasr_internal_launch_check(oasr_backend *be, const char *what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, what, __LINE__);
+    return OASR_STATUS_SUCCESS;
+}
+
+// Returns scratch of at least `bytes` (grows by reallocation outside any
+// capture; the stream is synchronised first because in-flight kernels may
+// still read the old buffer).
+void *oasr_internal_scratch(oasr_backend *be, size_t bytes, int *status) {
+    *status = OASR_STATUS_SUCCESS;
+    if (bytes <= be->scratch_bytes) return be->scratch;
+    size_t nb = std::max(bytes + (bytes >> 2), be->scratch_bytes * 2);
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(be->stream, &cs);
+    if (cs != cudaStreamCaptureStatusNone) {
+        *status = oasr_internal_fail(be, OASR_STATUS_ALLOC_FAILED,
+                                     "activation scratch too small during stream capture; call oasr_b200_reserve_scratch first");
+        return nullptr;
+    }
+    cudaError_t e = cudaStreamSynchronize(be->stream);
+    if (e != cudaSuccess) {
+        *status = oasr_internal_cuda_fail(be, e, "cudaStreamSynchronize(scratch grow)", __LINE__);
+        return nullptr;
+    }
+    if (be->scratch) cudaFree(be->scratch);
+    be->scratch = nullptr;
+    be->scratch_bytes = 0;
+    e = cudaMalloc(&be->scratch, nb);
+    if (e != cudaSuccess) {
+        *status = oasr_internal_cuda_fail(be, e, "cudaMalloc(scratch)", __LINE__);
+        return nullptr;
+    }
+    be->scratch_bytes = nb;
+    return be->scratch;
+}
+
+extern "C" {
+
+int oasr_b200_device_count(int32_t *count) {
+    if (!count) return OASR_STATUS_FAILED;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) n = 0;
+    *count = n;
+    return OASR_STATUS_SUCCESS;
+}
+
+int oasr_b200_init(int32_t ordinal, oasr_backend **out) {
+    if (!out) return OASR_STATUS_FAILED;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || ordinal < 0 || ordinal >= n) return OASR_STATUS_FAILED;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, ordinal) != cudaSuccess) return OASR_STATUS_DEVICE_LOST;
+    if (prop.major != 10) return OASR_STATUS_FAILED;  // kernels are built for sm_100a only
+    oasr_backend *be = new oasr_backend();
+    be->device = ordinal;
+    be->sm_count = prop.multiProcessorCount;
+    be->cc_major = prop.major;
+    be->cc_minor = prop.minor;
+    be->poisoned = 0;
+    be->abort_cb = nullptr;
+    be->abort_data = nullptr;
+    be->weight_bytes = 0;
+    be->n_weights = 0;
+    be->scratch = nullptr;
+    be->scratch_bytes = 0;
+    int st = OASR_STATUS_SUCCESS;
+    std::vector<uint16_t> gelu;
+    build_gelu_table(gelu);
+    cudaSetDevice(ordinal);
+    if (cudaStreamCreateWithFlags(&be->own_stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&be->counters, kCounterSlots * sizeof(unsigned)) != cudaSuccess ||
+        cudaMalloc(&be->err_word, sizeof(int)) != cudaSuccess ||
+        cudaMalloc(&be->gelu_table, 65536 * sizeof(uint16_t)) != cudaSuccess ||
+        cudaMemset(be->counters, 0, kCounterSlots * sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(be->err_word, 0, sizeof(int)) != cudaSuccess ||
+        cudaMemcpy(be->gelu_table, gelu.data(), 65536 * 2, cudaMemcpyHostToDevice) != cudaSuccess) {
+        delete be;
+        return OASR_STATUS_ALLOC_FAILED;
+    }
+    be->stream = be->own_stream;
+    oasr_internal_scratch(be, kDefaultScratch, &st);
+    if (st != OASR_STATUS_SUCCESS) {
+        oasr_b200_free(be);
+        return st;
+    }
+    *out = be;
+    return OASR_STATUS_SUCCESS;
+}
+
+int oasr_b200_free(oasr_backend *be) {
+    if (!be) return OASR_STATUS_SUCCESS;
+    cudaSetDevice(be->device);
+    cudaStreamSynchronize(be->stream);
+    if (be->scratch) cudaFree(be->scratch);
+    if (be->counters) cudaFree(be->counters);
+    if (be->err_word) cudaFree(be->err_word);
+    if (be->gelu_table) cudaFree(be->gelu_table);
+    if (be->own_stream) cudaStreamDestroy(be->own_stream);
+    delete be;
+    return OASR_STATUS_SUCCESS;
+}
+
+int oasr_b200_props(oasr_backend *be, oasr_device_props *out) {
+    if (!be || !out) return OASR_STATUS_FAILED;
+    memset(out, 0, sizeof *out);
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, be->device) != cudaSuccess) return OASR_STATUS_DEVICE_LOST;
+    snprintf(out->name, sizeof out->name, "CUDA%d", be->device);
+    snprintf(out->description, sizeof out->description, "%s (sm_%d%d, oasr_b200 abi %d)", prop.name, prop.major,
+             prop.minor, OASR_B200_ABI_VERSION);
+    out->ordinal = be->device;
+    out->device_type = 1;
+    out->sm_count = prop.multiProcessorCount;
+    out->cc_major = prop.major;
+    out->cc_minor = prop.minor;
+    out->cancel_mechanism = OASR_CANCEL_NATIVE;
+    out->cancel_observation = OASR_CANCEL_OBSERVATION_SUBMISSION_CHECKPOINT;
+    size_t fr = 0, tot = 0;
+    cudaSetDevice(be->device);
+    cudaMemGetInfo(&fr, &tot);
+    out->memory_free = fr;
+    out->memory_total = tot;
+    return OASR_STATUS_SUCCESS;
+}
+
+int oasr_b200_set_stream(oasr_backend *be, void *stream) {
+    if (!be) return OASR_STATUS_FAILED;
+    be->stream = stream ? (cudaStream_t)stream : be->own_stream;
+    return OASR_STATUS_SUCCESS;
+}
+
+void *oasr_b200_get_stream(oasr_backend *be) { return be ? (void *)be->stream : nullptr; }
+
+int oasr_b200_synchronize(oasr_backend *be) {
+    if (!be) return OASR_STATUS_FAILED;
+    int p = be->poisoned.load();
+    if (p) return OASR_STATUS_BACKEND_POISONED;
+    cudaSetDevice(be->device);
+    cudaError_t e = cudaStreamSynchronize(be->stream);
+    if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "cudaStreamSynchronize", __LINE__);
+    int err = 0;
+    e = cudaMemcpy(&err, be->err_word, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "read error word", __LINE__);
+    if (err) {
+        cudaMemset(be->err_word, 0, sizeof(int));
+        return oasr_internal_fail(be, OASR_STATUS_EXECUTION_FAILED,
+                                  err & ERR_BAD_INDEX ? "kernel rejected an out-of-range row index"
+                                                      : "kernel rejected inconsistent launch geometry");
+    }
+    return OASR_STATUS_SUCCESS;
+}
+
+int oasr_b200_set_abort_callback(oasr_backend *be, oasr_abort_callback cb, void *data) {
+    if (!be) return OASR_STATUS_FAILED;
+    be->abort_cb = cb;
+    be->abort_data = data;
+    return OASR_STATUS_SUCCESS;
+}
+
+int oasr_b200_mem_stats(oasr_backend *be, oasr_mem_stats *out) {
+    if (!be || !out) return OASR_STATUS_FAILED;
+    memset(out, 0, sizeof *out);
+    out->weight_bytes = be->weight_bytes;
+    out->scratch_bytes = be->scratch_bytes;
+    out->n_weights = be->n_weights;
+    size_t fr = 0, tot = 0;
+    cudaSetDevice(be->device);
+    cudaMemGetInfo(&fr, &tot);
+    out->device_free = fr;
+    out->device_total = tot;
+    return OASR_STATUS_SUCCESS;
+}
+
+const char *oasr_b200_last_error(oasr_backend *be) { return be ? be->last_error.c_str() : "null backend"; }
+
+int oasr_b200_reserve_scratch(oasr_backend *be, size_t bytes) {
+    int st = oasr_internal_precheck(be);
+    if (st) return st;
+    oasr_internal_scratch(be, bytes, &st);
+    return st;
+}
+
+// ---- resident weights ----------------------------------------------------------------
+int oasr_b200_weight_upload(oasr_backend *be, const void *host, size_t bytes, int32_t type, const int64_t ne[4],
+                            oasr_weight **out) {
+    if (!out) return OASR_STATUS_FAILED;
+    *out = nullptr;
+    int st = oasr_internal_precheck(be);
+    if (st) return st;
+    if (!host || !ne) return oasr_internal_fail(be, OASR_STATUS_FAILED, "weight_upload: null argument");
+    if (type != OASR_TYPE_Q8_0 && type != OASR_TYPE_Q4_0 && type != OASR_TYPE_Q4_K && type != OASR_TYPE_F16 &&
+        type != OASR_TYPE_F32)
+        return oasr_internal_fail(be, OASR_STATUS_FAILED, "weight_upload: unsupported type");
+    for (int i = 0; i < 4; ++i)
+        if (ne[i] <= 0) return oasr_internal_fail(be, OASR_STATUS_FAILED, "weight_upload: bad shape");
+    const int64_t rs = oasr_b200_row_size(type, ne[0]);
+    if (rs < 0) return oasr_internal_fail(be, OASR_STATUS_FAILED, "weight_upload: ne0 not a multiple of the block");
+    const int64_t rows = ne[1] * ne[2] * ne[3];
+    if ((size_t)(rs * rows) != bytes) return oasr_internal_fail(be, OASR_STATUS_FAILED, "weight_upload: byte count");
+    oasr_weight *w = new oasr_weight();
+    w->type = type;
+    for (int i = 0; i < 4; ++i) w->ne[i] = ne[i];
+    w->qs = nullptr;
+    w->d = nullptr;
+    const uint8_t *src = (const uint8_t *)host;
+    cudaError_t e;
+    if (type == OASR_TYPE_Q8_0 || type == OASR_TYPE_Q4_0) {
+        const int bb = type == OASR_TYPE_Q8_0 ? BYTES_Q8_0 : BYTES_Q4_0;
+        const int qb = bb - 2;  // quant bytes per block (32 or 16)
+        const int64_t nb = ne[0] / 32;
+        w->qs_row_bytes = nb * qb;
+        w->d_row_elems = nb;
+        std::vector<uint8_t> qs((size_t)(rows * w->qs_row_bytes));
+        std::vector<uint16_t> d((size_t)(rows * nb));
+        for (int64_t r = 0; r < rows; ++r)
+            for (int64_t b = 0; b < nb; ++b) {
+                const uint8_t *blk = src + r * rs + b * bb;
+                memcpy(&d[(size_t)(r * nb + b)], blk, 2);
+                memcpy(&qs[(size_t)(r * w->qs_row_bytes + b * qb)], blk + 2, qb);
+            }
+        w->device_bytes = qs.size() + d.size() * 2;
+        e = cudaMalloc(&w->qs, qs.size());
+        if (e == cudaSuccess) e = cudaMalloc(&w->d, d.size() * 2);
+        if (e == cudaSuccess) e = cudaMemcpy(w->qs, qs.data(), qs.size(), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(w->d, d.data(), d.size() * 2, cudaMemcpyHostToDevice);
+    } else {
+        w->qs_row_bytes = rs;
+        w->d_row_elems = 0;
+        w->device_bytes = bytes;
+        e = cudaMalloc(&w->qs, bytes);
+        if (e == cudaSuccess) e = cudaMemcpy(w->qs, src, bytes, cudaMemcpyHostToDevice);
+    }
+    if (e != cudaSuccess) {
+        if (w->qs) cudaFree(w->qs);
+        if (w->d) cudaFree(w->d);
+        delete w;
+        return oasr_internal_cuda_fail(be, e, "weight_upload", __LINE__);
+    }
+    be->weight_bytes += w->device_bytes;
+    be->n_weights += 1;
+    *out = w;
+    return OASR_STATUS_SUCCESS;
+}
+
+int oasr_b200_weight_free(oasr_backend *be, oasr_weight *w) {
+    if (!w) return OASR_STATUS_SUCCESS;
+    if (be) {
+        cudaSetDevice(be->device);
+        cudaStreamSynchronize(be->stream);
+        be->weight_bytes -= w->device_bytes;
+        be->n_weights -= 1;
+    }
+    if (w->qs) cudaFree(w->qs);
+    if (w->d) cudaFree(w->d);
+    delete w;
+    return OASR_STATUS_SUCCESS;
+}
+
+int oasr_b200_weight_download(oasr_backend *be, const oasr_weight *w, void *host, size_t bytes) {
+    int st = oasr_internal_precheck(be);
+    if (st) return st;
+    if (!w || !host) return OASR_STATUS_FAILED;
+    const int64_t rs = oasr_b200_row_size(w->type, w->ne[0]);
+    const int64_t rows = w->ne[1] * w->ne[2] * w->ne[3];
+    if ((size_t)(rs * rows) != bytes) return oasr_internal_fail(be, OASR_STATUS_FAILED, "weight_download: byte count");
+    OASR_CUDA_TRY(be, cudaStreamSynchronize(be->stream));
+    uint8_t *dst = (uint8_t *)host;
+    if (w->type == OASR_TYPE_Q8_0 || w->type == OASR_TYPE_Q4_0) {
+        const int bb = w->type == OASR_TYPE_Q8_0 ? BYTES_Q8_0 : BYTES_Q4_0, qb = bb - 2;
+        const int64_t nb = w->d_row_elems;
+        std::vector<uint8_t> qs((size_t)(rows * w->qs_row_bytes));
+        std::vector<uint16_t> d((size_t)(rows * nb));
+        OASR_CUDA_TRY(be, cudaMemcpy(qs.data(), w->qs, qs.size(), cudaMemcpyDeviceToHost));
+        OASR_CUDA_TRY(be, cudaMemcpy(d.data(), w->d, d.size() * 2, cudaMemcpyDeviceToHost));
+        for (int64_t r = 0; r < rows; ++r)
+            for (int64_t b = 0; b < nb; ++b) {
+                uint8_t *blk = dst + r * rs + b * bb;
+                memcpy(blk, &d[(size_t)(r * nb + b)], 2);
+                memcpy(blk + 2, &qs[(size_t)(r * w->qs_row_bytes + b * qb)], qb);
+            }
+    } else {
+        OASR_CUDA_TRY(be, cudaMemcpy(dst, w->qs, bytes, cudaMemcpyDeviceToHost));
+    }
+    return OASR_STATUS_SUCCESS;
+}
+
+int oasr_b200_weight_info(const oasr_weight *w, int32_t *type, int64_t ne[4], uint64_t *device_bytes) {
+    if (!w) return OASR_STATUS_FAILED;
+    if (type) *type = w->type;
+    if (ne)
+        for (int i = 0; i < 4; ++i) ne[i] = w->ne[i];
+    if (device_bytes) *device_bytes = w->device_bytes;
+    return OASR_STATUS_SUCCESS;
+}
+
+// ---- capability probe (backend.rs:295-323 probes mul_mat(W[256,32], X f32 [256,8])) ----
+int oasr_b200_supports_op(oasr_backend *be, int32_t op, const oasr_tensor *src0, const oasr_tensor *src1) {
+    if (!be || !src0) return 0;
+    switch (op) {
+    case OASR_OP_MUL_MAT: {
+        if (!src1) return 0;
+        const int t = src0->type;
+        if (t != OASR_TYPE_Q8_0 && t != OASR_TYPE_Q4_0 && t != OASR_TYPE_Q4_K && t != OASR_TYPE_F16 &&
+            t != OASR_TYPE_F32)
+            return 0;
+        if (src1->type != OASR_TYPE_F32 && src1->type != OASR_TYPE_F16) return 0;
+        if (src0->ne[0] != src1->ne[0] || oasr_b200_row_size(t, src0->ne[0]) < 0) return 0;
+        if (src0->ne[2] <= 0 || src0->ne[3] <= 0 || src1->ne[2] % src0->ne[2] || src1->ne[3] % src0->ne[3]) return 0;
+        return 1;
+    }
+    case OASR_OP_FLASH_ATTN_EXT: {
+        // src0 = q, src1 = k
+        if (!src1 || src0->type != OASR_TYPE_F32) return 0;
+        if (src1->type != OASR_TYPE_F16 && src1->type != OASR_TYPE_F32) return 0;
+        const int64_t D = src0->ne[0];
+        if (D != 64 && D != 128) return 0;
+        if (src1->ne[2] <= 0 || src0->ne[2] % src1->ne[2]) return 0;
+        return 1;
+    }
+    case OASR_OP_SET_ROWS:
+        return src0->type == OASR_TYPE_F16 || src0->type == OASR_TYPE_F32;
+    case OASR_OP_ARGMAX_FIRST:
+        return src0->type == OASR_TYPE_F32;
+    default:
+        return 0;
+    }
+}
+
+}  // extern "C"

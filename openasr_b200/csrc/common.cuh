@@ -1,0 +1,108 @@
+// common.cuh -- shared definitions of the B200 backend (host + device).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <string>
+
+#include "../../include/oasr_b200.h"
+
+namespace oasr {
+
+constexpr int QK8_0 = 32;
+constexpr int QK4_0 = 32;
+constexpr int QK_K = 256;
+constexpr int BYTES_Q8_0 = 34;
+constexpr int BYTES_Q4_0 = 18;
+constexpr int BYTES_Q4_K = 144;
+
+// ggml block layouts (host side; gguf/constants.py GGML_QUANT_SIZES)
+struct BlockQ8_0 { uint16_t d; int8_t qs[QK8_0]; };
+struct BlockQ4_0 { uint16_t d; uint8_t qs[QK4_0 / 2]; };
+struct BlockQ4_K { uint16_t d, dmin; uint8_t scales[12]; uint8_t qs[QK_K / 2]; };
+static_assert(sizeof(BlockQ8_0) == BYTES_Q8_0, "q8_0");
+static_assert(sizeof(BlockQ4_0) == BYTES_Q4_0, "q4_0");
+static_assert(sizeof(BlockQ4_K) == BYTES_Q4_K, "q4_K");
+
+// Device error word bits: a kernel that detects a bad input sets one and
+// returns instead of touching memory out of bounds.
+enum : int {
+    ERR_NONE = 0,
+    ERR_BAD_INDEX = 1,   // set_rows / get_rows index out of range
+    ERR_BAD_SHAPE = 2,   // launch geometry inconsistent with the descriptors
+};
+
+}  // namespace oasr
+
+// A resident weight: ggml [ne0=K, ne1=N, ne2, ne3] of `type`, repacked.
+struct oasr_weight {
+    int32_t type;
+    int64_t ne[4];
+    // Q8_0 / Q4_0: qs plane [slices][N][K or K/2] bytes + d plane [slices][N][K/32] fp16
+    // Q4_K / F16 / F32: ggml bytes in `qs`, d unused
+    uint8_t *qs;
+    uint16_t *d;
+    int64_t qs_row_bytes;    // bytes per row in the qs plane
+    int64_t d_row_elems;     // fp16 scales per row in the d plane
+    uint64_t device_bytes;
+};
+
+struct oasr_backend {
+    int device;
+    int sm_count;
+    int cc_major, cc_minor;
+    cudaStream_t own_stream;
+    cudaStream_t stream;
+    // activation scratch: quantized activations, flash-decode partials, counters
+    uint8_t *scratch;
+    size_t scratch_bytes;
+    unsigned int *counters;   // zero-initialised; kernels leave them at zero
+    int *err_word;            // device error word (oasr::ERR_*)
+    uint16_t *gelu_table;     // 65536-entry fp16 GELU table (ggml CPU semantics)
+    std::atomic<int> poisoned;  // sticky ggml_status once a device error is seen
+    oasr_abort_callback abort_cb;
+    void *abort_data;
+    uint64_t weight_bytes;
+    int64_t n_weights;
+    std::string last_error;
+};
+
+#define OASR_CUDA_TRY(be, expr)                                                          \
+    do {                                                                                 \
+        cudaError_t _e = (expr);                                                         \
+        if (_e != cudaSuccess) return oasr_internal_cuda_fail((be), _e, #expr, __LINE__);\
+    } while (0)
+
+int oasr_internal_cuda_fail(oasr_backend *be, cudaError_t e, const char *what, int line);
+int oasr_internal_fail(oasr_backend *be, int status, const std::string &msg);
+int oasr_internal_precheck(oasr_backend *be);  // poison / abort check before enqueueing
+int oasr_internal_launch_check(oasr_backend *be, const char *what);
+void *oasr_internal_scratch(oasr_backend *be, size_t bytes, int *status);
+
+// ---- device helpers --------------------------------------------------------------
+static __device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+static __device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+static __device__ __forceinline__ int4 ldg_stream(const void *p) {
+    int4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+static __device__ __forceinline__ float h2f(uint16_t h) {
+    return __half2float(__ushort_as_half(h));
+}

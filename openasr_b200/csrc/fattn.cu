@@ -1,0 +1,317 @@
+// fattn.cu -- K3: split-K flash attention over the f16 KV cache.
+//
+// Implements GGML_OP_FLASH_ATTN_EXT as built by
+// GgmlCpuGraphBuilder::flash_attn_ext_with_precision (cpu_graph.rs:4144-4220):
+//   O[:, h, iq, s] = softmax(scale * Q[:, iq, h, s] . K[:, :, h/G, s] + mask[:, iq]) V
+// with GQA by integer division of the head index (q.ne2 % k.ne2 == 0,
+// cpu_graph.rs:7476-7504), mask rows broadcast over ne2/ne3 (:7506-7519),
+// positions whose mask is -inf skipped, and the output permuted to
+// [D, H, n_q, S].  Q is rounded to K's type first (ggml converts Q to the
+// vec_dot type of K), the Q.K products of two halves are exact in f32, and the
+// softmax and V accumulation run in f32.
+//
+// Grid: (kv-head x seq x query-tile, split).  Each CTA streams a contiguous
+// range of KV positions once with 16-byte loads (8 halves per lane, D/8 lanes
+// per position, 32/(D/8) positions per warp step) for all query rows that
+// share the kv head, keeps per-lane-group online-softmax state, merges it
+// across lane groups and warps, and then either writes the output (one split)
+// or its (max, sum, acc) partial; the last CTA of a group (atomic ticket, no
+// waiting) merges the partials and resets the ticket.
+#include <float.h>
+
+#include "kernels.cuh"
+
+namespace oasr {
+
+struct FaArgs {
+    const char *q, *k, *v, *mask;
+    char *dst;
+    int64_t q_nb1, q_nb2, q_nb3;
+    int64_t k_nb1, k_nb2, k_nb3;
+    int64_t v_nb1, v_nb2, v_nb3;
+    int64_t m_nb0, m_nb1, m_nb2, m_nb3;
+    int64_t m_ne2, m_ne3;
+    int64_t d_nb1, d_nb2, d_nb3;
+    int NQ, H, HKV, S, NKV;
+    int G;          // H / HKV
+    int QG;         // G * NQ query rows per kv head
+    int n_qtiles;   // ceil(QG / QT)
+    int n_splits;
+    int kv_per_split;
+    float scale;
+    float *partials;          // [rows][n_splits][D + 2]
+    unsigned int *counters;   // one ticket per (kv head, seq, q tile)
+};
+
+template <bool F16>
+static __device__ __forceinline__ void load8(const char *p, float (&out)[8]) {
+    if (F16) {
+        const int4 r = *reinterpret_cast<const int4 *>(p);
+        const __half2 *h = reinterpret_cast<const __half2 *>(&r);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(h[i]);
+            out[2 * i] = f.x;
+            out[2 * i + 1] = f.y;
+        }
+    } else {
+        const float4 a = *reinterpret_cast<const float4 *>(p);
+        const float4 b = *reinterpret_cast<const float4 *>(p + 16);
+        out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+        out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+    }
+}
+
+template <int D, int QT, bool F16>
+__global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
+    constexpr int LPP = D / 8;        // lanes per KV position
+    constexpr int PPW = 32 / LPP;     // positions per warp step
+    constexpr int ES = F16 ? 2 : 4;   // element size
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int grp = lane / LPP, sl = lane % LPP;  // position group in warp, lane in group
+    const int split = blockIdx.y;
+    int gid = blockIdx.x;
+    const int qt = gid % a.n_qtiles;
+    gid /= a.n_qtiles;
+    const int hk = gid % a.HKV;
+    const int s = gid / a.HKV;
+
+    // query rows of this tile
+    int qh[QT], qi[QT];
+    bool qvalid[QT];
+    float qv[QT][8];
+#pragma unroll
+    for (int t = 0; t < QT; ++t) {
+        const int r = qt * QT + t;
+        qvalid[t] = r < a.QG;
+        const int rr = qvalid[t] ? r : 0;
+        qh[t] = hk * a.G + rr / a.NQ;
+        qi[t] = rr % a.NQ;
+        const float *qp = reinterpret_cast<const float *>(a.q + qi[t] * a.q_nb1 + qh[t] * a.q_nb2 + s * a.q_nb3) + sl * 8;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            float x = qvalid[t] ? qp[e] : 0.0f;
+            qv[t][e] = F16 ? __half2float(__float2half_rn(x)) : x;
+        }
+    }
+    const char *mrow[QT];
+#pragma unroll
+    for (int t = 0; t < QT; ++t)
+        mrow[t] = a.mask ? a.mask + qi[t] * a.m_nb1 + (qh[t] % a.m_ne2) * a.m_nb2 + (s % a.m_ne3) * a.m_nb3 : nullptr;
+
+    float mx[QT], sm[QT], acc[QT][8];
+#pragma unroll
+    for (int t = 0; t < QT; ++t) {
+        mx[t] = -INFINITY;
+        sm[t] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[t][e] = 0.0f;
+    }
+
+    const int kv0 = split * a.kv_per_split;
+    const int kv1 = min(a.NKV, kv0 + a.kv_per_split);
+    const char *kbase = a.k + hk * a.k_nb2 + s * a.k_nb3 + sl * 8 * ES;
+    const char *vbase = a.v + hk * a.v_nb2 + s * a.v_nb3 + sl * 8 * ES;
+    for (int p0 = kv0 + warp * PPW; p0 < kv1; p0 += 4 * PPW) {
+        const int p = p0 + grp;
+        const bool pv = p < kv1;
+        float kf[8], vf[8];
+        if (pv) {
+            load8<F16>(kbase + (int64_t)p * a.k_nb1, kf);
+            load8<F16>(vbase + (int64_t)p * a.v_nb1, vf);
+        }
+#pragma unroll
+        for (int t = 0; t < QT; ++t) {
+            float d = 0.0f;
+            if (pv) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) d = fmaf(qv[t][e], kf[e], d);
+            }
+#pragma unroll
+            for (int o = LPP / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+            if (!pv || !qvalid[t]) continue;
+            float sc = d * a.scale;
+            if (mrow[t]) {
+                const float mv = __half2float(*reinterpret_cast<const __half *>(mrow[t] + (int64_t)p * a.m_nb0));
+                if (mv == -INFINITY) continue;
+                sc += mv;
+            }
+            const float mnew = fmaxf(mx[t], sc);
+            const float corr = expf(mx[t] - mnew);  // mx = -inf -> 0
+            const float w = expf(sc - mnew);
+            sm[t] = sm[t] * corr + w;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[t][e] = fmaf(w, vf[e], acc[t][e] * corr);
+            mx[t] = mnew;
+        }
+    }
+
+    // merge the PPW position groups of each warp (same sl, different grp)
+#pragma unroll
+    for (int t = 0; t < QT; ++t) {
+#pragma unroll
+        for (int o = LPP; o < 32; o <<= 1) {
+            const float om = __shfl_xor_sync(0xffffffffu, mx[t], o);
+            const float os = __shfl_xor_sync(0xffffffffu, sm[t], o);
+            const float nm = fmaxf(mx[t], om);
+            const float f0 = mx[t] == -INFINITY ? 0.0f : expf(mx[t] - nm);
+            const float f1 = om == -INFINITY ? 0.0f : expf(om - nm);
+            sm[t] = sm[t] * f0 + os * f1;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float oa = __shfl_xor_sync(0xffffffffu, acc[t][e], o);
+                acc[t][e] = acc[t][e] * f0 + oa * f1;
+            }
+            mx[t] = nm;
+        }
+    }
+    // merge the 4 warps through shared memory
+    __shared__ float s_m[4][QT], s_s[4][QT];
+    __shared__ float s_acc[4][QT][D];
+    if (grp == 0) {
+#pragma unroll
+        for (int t = 0; t < QT; ++t) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) s_acc[warp][t][sl * 8 + e] = acc[t][e];
+            if (sl == 0) {
+                s_m[warp][t] = mx[t];
+                s_s[warp][t] = sm[t];
+            }
+        }
+    }
+    __syncthreads();
+    // thread layout for the epilogue: QT*D outputs over 128 threads
+    for (int o = threadIdx.x; o < QT * D; o += 128) {
+        const int t = o / D, e = o % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, s_m[w][t]);
+        float L = 0.0f, A = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const float f = s_m[w][t] == -INFINITY ? 0.0f : expf(s_m[w][t] - M);
+            L += s_s[w][t] * f;
+            A += s_acc[w][t][e] * f;
+        }
+        const int r = qt * QT + t;
+        if (r >= a.QG) continue;
+        const int h = hk * a.G + r / a.NQ, iq = r % a.NQ;
+        if (a.n_splits == 1) {
+            float *out = reinterpret_cast<float *>(a.dst + h * a.d_nb1 + iq * a.d_nb2 + s * a.d_nb3);
+            out[e] = L == 0.0f ? 0.0f : A / L;
+        } else {
+            const int64_t row = ((int64_t)s * a.H + h) * a.NQ + iq;
+            float *pp = a.partials + (row * a.n_splits + split) * (D + 2);
+            pp[e] = A;
+            if (e == 0) {
+                pp[D] = M;
+                pp[D + 1] = L;
+            }
+        }
+    }
+    if (a.n_splits == 1) return;
+
+    // last CTA of this (kv head, seq, q tile) merges the split partials
+    __shared__ bool s_last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned int *ctr = a.counters + blockIdx.x;
+        const unsigned int ticket = atomicAdd(ctr, 1u);
+        s_last = ticket == (unsigned)(a.n_splits - 1);
+        if (s_last) *ctr = 0u;  // every launch leaves the tickets at zero
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int o = threadIdx.x; o < QT * D; o += 128) {
+        const int t = o / D, e = o % D;
+        const int r = qt * QT + t;
+        if (r >= a.QG) continue;
+        const int h = hk * a.G + r / a.NQ, iq = r % a.NQ;
+        const int64_t row = ((int64_t)s * a.H + h) * a.NQ + iq;
+        const volatile float *pp = a.partials + row * a.n_splits * (D + 2);
+        float M = -INFINITY;
+        for (int sp = 0; sp < a.n_splits; ++sp) M = fmaxf(M, pp[sp * (D + 2) + D]);
+        float L = 0.0f, A = 0.0f;
+        for (int sp = 0; sp < a.n_splits; ++sp) {
+            const float m = pp[sp * (D + 2) + D];
+            const float f = m == -INFINITY ? 0.0f : expf(m - M);
+            L += pp[sp * (D + 2) + D + 1] * f;
+            A += pp[sp * (D + 2) + e] * f;
+        }
+        float *out = reinterpret_cast<float *>(a.dst + h * a.d_nb1 + iq * a.d_nb2 + s * a.d_nb3);
+        out[e] = L == 0.0f ? 0.0f : A / L;
+    }
+}
+
+template <int D, bool F16>
+static void launch_fa_d(const FaArgs &a, int QT, dim3 grid, cudaStream_t st) {
+    switch (QT) {
+    case 1: fattn_split_kernel<D, 1, F16><<<grid, 128, 0, st>>>(a); break;
+    case 2: fattn_split_kernel<D, 2, F16><<<grid, 128, 0, st>>>(a); break;
+    case 4: fattn_split_kernel<D, 4, F16><<<grid, 128, 0, st>>>(a); break;
+    default: fattn_split_kernel<D, 8, F16><<<grid, 128, 0, st>>>(a); break;
+    }
+}
+
+int launch_flash_attn(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
+                      const oasr_tensor *mask, float scale, oasr_tensor *dst) {
+    FaArgs a;
+    const int D = (int)q->ne[0];
+    a.q = (const char *)q->data;
+    a.k = (const char *)k->data;
+    a.v = (const char *)v->data;
+    a.mask = mask ? (const char *)mask->data : nullptr;
+    a.dst = (char *)dst->data;
+    a.q_nb1 = q->nb[1]; a.q_nb2 = q->nb[2]; a.q_nb3 = q->nb[3];
+    a.k_nb1 = k->nb[1]; a.k_nb2 = k->nb[2]; a.k_nb3 = k->nb[3];
+    a.v_nb1 = v->nb[1]; a.v_nb2 = v->nb[2]; a.v_nb3 = v->nb[3];
+    if (mask) {
+        a.m_nb0 = mask->nb[0]; a.m_nb1 = mask->nb[1]; a.m_nb2 = mask->nb[2]; a.m_nb3 = mask->nb[3];
+        a.m_ne2 = mask->ne[2]; a.m_ne3 = mask->ne[3];
+    } else {
+        a.m_nb0 = a.m_nb1 = a.m_nb2 = a.m_nb3 = 0;
+        a.m_ne2 = a.m_ne3 = 1;
+    }
+    a.d_nb1 = dst->nb[1]; a.d_nb2 = dst->nb[2]; a.d_nb3 = dst->nb[3];
+    a.NQ = (int)q->ne[1];
+    a.H = (int)q->ne[2];
+    a.S = (int)q->ne[3];
+    a.HKV = (int)k->ne[2];
+    a.NKV = (int)k->ne[1];
+    a.G = a.H / a.HKV;
+    a.QG = a.G * a.NQ;
+    const int QT = a.QG >= 8 ? 8 : (a.QG >= 4 ? 4 : (a.QG >= 2 ? 2 : 1));
+    a.n_qtiles = (a.QG + QT - 1) / QT;
+    a.scale = scale;
+    const int64_t groups = (int64_t)a.HKV * a.S * a.n_qtiles;
+    int n_splits = 1;
+    if (groups < 4LL * be->sm_count && groups <= (1 << 16)) {
+        n_splits = (int)((4LL * be->sm_count + groups - 1) / groups);
+        n_splits = std::min(n_splits, std::max(1, a.NKV / 64));
+    }
+    a.n_splits = n_splits;
+    a.kv_per_split = (a.NKV + n_splits - 1) / n_splits;
+    a.partials = nullptr;
+    a.counters = be->counters;
+    if (n_splits > 1) {
+        int st = 0;
+        const size_t bytes = (size_t)a.S * a.H * a.NQ * n_splits * (D + 2) * sizeof(float);
+        a.partials = (float *)oasr_internal_scratch(be, bytes, &st);
+        if (st) return st;
+    }
+    if (groups > 0x7fffffffLL) return oasr_internal_fail(be, OASR_STATUS_FAILED, "flash_attn: grid too large");
+    dim3 grid((unsigned)groups, n_splits);
+    const bool f16 = k->type == OASR_TYPE_F16;
+    if (D == 64) {
+        if (f16) launch_fa_d<64, true>(a, QT, grid, be->stream);
+        else launch_fa_d<64, false>(a, QT, grid, be->stream);
+    } else {
+        if (f16) launch_fa_d<128, true>(a, QT, grid, be->stream);
+        else launch_fa_d<128, false>(a, QT, grid, be->stream);
+    }
+    return oasr_internal_launch_check(be, "flash_attn");
+}
+
+}  // namespace oasr

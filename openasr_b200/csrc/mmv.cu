@@ -1,0 +1,359 @@
+// mmv.cu -- K1: dequant-fused decode GEMV / skinny GEMM (M <= 8 activation rows).
+//
+// Replaces ggml-cuda's mul_mat_vec_q for the decode mul_mat nodes built by
+// GgmlCpuGraphBuilder::mul_mat (cpu_graph.rs:3616-3686): weight rows stream
+// from HBM exactly once with 128-bit non-allocating loads, the int8/int4
+// quants are dotted against the pre-quantized activations with dp4a, and the
+// per-block f32 term is formed exactly as ggml's CPU vec_dot forms it:
+//   Q8_0 / Q4_0 (per 32):  (float)isum * (d_w * d_a)
+//   Q4_K       (per 256):  (d_w*d_a)*(float)isum - (dmin_w*d_a)*(float)msum
+// so GPU and CPU differ only in the order of the f32 sum over blocks.
+//
+// Work mapping: a row has `nitems` work items (Q8_0/Q4_0: one 32-block, Q4_K:
+// one 64-element half of a 4-item super-block).  LPR = 2^lpr_log2 lanes share
+// a row (LPR divides nitems, so every lane runs the same trip count and
+// full-warp shuffles are safe); a warp covers 32/LPR rows per pass and RP
+// passes, holding the RP weight items in registers while it loops over the M
+// activation rows (activations are small and L1-resident).
+#include "kernels.cuh"
+
+namespace oasr {
+
+static __device__ __forceinline__ int nib_lo(int v) { return v & 0x0F0F0F0F; }
+static __device__ __forceinline__ int nib_hi(int v) { return (v >> 4) & 0x0F0F0F0F; }
+
+template <int N>
+static __device__ __forceinline__ void reduce_lanes(float (&v)[N], int lpr) {
+    for (int o = lpr >> 1; o > 0; o >>= 1) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], o);
+    }
+}
+
+// ---- Q8_0 / Q4_0 -----------------------------------------------------------------------
+template <int M, int RP, bool Q4>
+__global__ void __launch_bounds__(128, 4)
+    mmv_q8_kernel(const uint8_t *__restrict__ wqs, const uint16_t *__restrict__ wd, int64_t qs_ld, int64_t d_ld,
+                  int64_t N, int nitems, int lpr_log2, const int8_t *__restrict__ aqs, const float *__restrict__ ad,
+                  int K, float *__restrict__ y, int64_t y_ld) {
+    constexpr int QB = Q4 ? 16 : 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lpr = 1 << lpr_log2, rpp = 32 >> lpr_log2;
+    const int sub = lane >> lpr_log2, j = lane & (lpr - 1);
+    const int64_t row0 = ((int64_t)blockIdx.x * 4 + warp) * (int64_t)(rpp * RP) + sub;
+    const int nb = K / 32;
+    float acc[RP * M];
+#pragma unroll
+    for (int i = 0; i < RP * M; ++i) acc[i] = 0.0f;
+
+    for (int it = j; it < nitems; it += lpr) {
+        int4 w0[RP], w1[RP];
+        float dw[RP];
+#pragma unroll
+        for (int p = 0; p < RP; ++p) {
+            const int64_t row = row0 + (int64_t)p * rpp;
+            if (row < N) {
+                const uint8_t *wp = wqs + row * qs_ld + (int64_t)it * QB;
+                w0[p] = ldg_stream(wp);
+                w1[p] = Q4 ? make_int4(0, 0, 0, 0) : ldg_stream(wp + 16);
+                dw[p] = h2f(wd[row * d_ld + it]);
+            } else {
+                w0[p] = w1[p] = make_int4(0, 0, 0, 0);
+                dw[p] = 0.0f;
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            const int8_t *ap = aqs + (int64_t)m * K + (int64_t)it * 32;
+            const int4 a0 = __ldg(reinterpret_cast<const int4 *>(ap));
+            const int4 a1 = __ldg(reinterpret_cast<const int4 *>(ap + 16));
+            const float da = __ldg(ad + (int64_t)m * nb + it);
+#pragma unroll
+            for (int p = 0; p < RP; ++p) {
+                int s = 0;
+                if (Q4) {
+                    const int4 w = w0[p];
+                    s = __dp4a((int)__vsub4(nib_lo(w.x), 0x08080808), a0.x, s);
+                    s = __dp4a((int)__vsub4(nib_lo(w.y), 0x08080808), a0.y, s);
+                    s = __dp4a((int)__vsub4(nib_lo(w.z), 0x08080808), a0.z, s);
+                    s = __dp4a((int)__vsub4(nib_lo(w.w), 0x08080808), a0.w, s);
+                    s = __dp4a((int)__vsub4(nib_hi(w.x), 0x08080808), a1.x, s);
+                    s = __dp4a((int)__vsub4(nib_hi(w.y), 0x08080808), a1.y, s);
+                    s = __dp4a((int)__vsub4(nib_hi(w.z), 0x08080808), a1.z, s);
+                    s = __dp4a((int)__vsub4(nib_hi(w.w), 0x08080808), a1.w, s);
+                } else {
+                    s = __dp4a(w0[p].x, a0.x, s);
+                    s = __dp4a(w0[p].y, a0.y, s);
+                    s = __dp4a(w0[p].z, a0.z, s);
+                    s = __dp4a(w0[p].w, a0.w, s);
+                    s = __dp4a(w1[p].x, a1.x, s);
+                    s = __dp4a(w1[p].y, a1.y, s);
+                    s = __dp4a(w1[p].z, a1.z, s);
+                    s = __dp4a(w1[p].w, a1.w, s);
+                }
+                acc[p * M + m] += __fmul_rn((float)s, __fmul_rn(dw[p], da));
+            }
+        }
+    }
+    reduce_lanes(acc, lpr);
+    if (j == 0) {
+#pragma unroll
+        for (int p = 0; p < RP; ++p) {
+            const int64_t row = row0 + (int64_t)p * rpp;
+            if (row < N) {
+#pragma unroll
+                for (int m = 0; m < M; ++m) y[(int64_t)m * y_ld + row] = acc[p * M + m];
+            }
+        }
+    }
+}
+
+// ---- Q4_K ---------------------------------------------------------------------------------
+static __device__ __forceinline__ int byte_of(const int4 &h, int i) {
+    const int w = i < 4 ? h.y : (i < 8 ? h.z : h.w);  // scales[0..11] live in h.y..h.w
+    return (w >> (8 * (i & 3))) & 0xFF;
+}
+
+// get_scale_min_k4 on the 12 packed scale bytes (layout: gguf/quants.py Q4_K.get_scale_min)
+static __device__ __forceinline__ void scale_min(const int4 &h, int j, int &sc, int &m) {
+    if (j < 4) {
+        sc = byte_of(h, j) & 63;
+        m = byte_of(h, j + 4) & 63;
+    } else {
+        sc = (byte_of(h, j + 4) & 0xF) | ((byte_of(h, j - 4) >> 6) << 4);
+        m = (byte_of(h, j + 4) >> 4) | ((byte_of(h, j) >> 6) << 4);
+    }
+}
+
+template <int M, int RP>
+__global__ void __launch_bounds__(128, 4)
+    mmv_q4k_kernel(const uint8_t *__restrict__ w, int64_t w_ld, int64_t N, int nitems, int lpr_log2,
+                   const int8_t *__restrict__ aqs, const float *__restrict__ ad, const int16_t *__restrict__ abs16,
+                   int K, float *__restrict__ y, int64_t y_ld) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lpr = 1 << lpr_log2, rpp = 32 >> lpr_log2;
+    const int sub = lane >> lpr_log2, j = lane & (lpr - 1);
+    const int64_t row0 = ((int64_t)blockIdx.x * 4 + warp) * (int64_t)(rpp * RP) + sub;
+    const int nsb = K / 256;
+    float acc[RP * M];
+#pragma unroll
+    for (int i = 0; i < RP * M; ++i) acc[i] = 0.0f;
+
+    for (int it = j; it < nitems; it += lpr) {
+        const int sb = it >> 2, c = it & 3;
+        int4 hdr[RP], q0[RP], q1[RP];
+#pragma unroll
+        for (int p = 0; p < RP; ++p) {
+            const int64_t row = row0 + (int64_t)p * rpp;
+            if (row < N) {
+                const uint8_t *wp = w + row * w_ld + (int64_t)sb * 144;
+                hdr[p] = ldg_stream(wp);
+                q0[p] = ldg_stream(wp + 16 + 32 * c);
+                q1[p] = ldg_stream(wp + 32 + 32 * c);
+            } else {
+                hdr[p] = q0[p] = q1[p] = make_int4(0, 0, 0, 0);
+            }
+        }
+        int sc0[RP], sc1[RP], mn0[RP], mn1[RP];
+#pragma unroll
+        for (int p = 0; p < RP; ++p) {
+            scale_min(hdr[p], 2 * c, sc0[p], mn0[p]);
+            scale_min(hdr[p], 2 * c + 1, sc1[p], mn1[p]);
+        }
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            const int8_t *ap = aqs + (int64_t)m * K + (int64_t)sb * 256 + 64 * c;
+            const int4 l0 = __ldg(reinterpret_cast<const int4 *>(ap));
+            const int4 l1 = __ldg(reinterpret_cast<const int4 *>(ap + 16));
+            const int4 h0 = __ldg(reinterpret_cast<const int4 *>(ap + 32));
+            const int4 h1 = __ldg(reinterpret_cast<const int4 *>(ap + 48));
+            const float da = __ldg(ad + (int64_t)m * nsb + sb);
+            const int2 bsv = __ldg(reinterpret_cast<const int2 *>(abs16 + (int64_t)m * (K / 16) + sb * 16 + 4 * c));
+            const int bsA = (int)(int16_t)(bsv.x & 0xFFFF) + (int)(int16_t)(bsv.x >> 16);
+            const int bsB = (int)(int16_t)(bsv.y & 0xFFFF) + (int)(int16_t)(bsv.y >> 16);
+#pragma unroll
+            for (int p = 0; p < RP; ++p) {
+                int dlo = 0, dhi = 0;
+                dlo = __dp4a(nib_lo(q0[p].x), l0.x, dlo);
+                dlo = __dp4a(nib_lo(q0[p].y), l0.y, dlo);
+                dlo = __dp4a(nib_lo(q0[p].z), l0.z, dlo);
+                dlo = __dp4a(nib_lo(q0[p].w), l0.w, dlo);
+                dlo = __dp4a(nib_lo(q1[p].x), l1.x, dlo);
+                dlo = __dp4a(nib_lo(q1[p].y), l1.y, dlo);
+                dlo = __dp4a(nib_lo(q1[p].z), l1.z, dlo);
+                dlo = __dp4a(nib_lo(q1[p].w), l1.w, dlo);
+                dhi = __dp4a(nib_hi(q0[p].x), h0.x, dhi);
+                dhi = __dp4a(nib_hi(q0[p].y), h0.y, dhi);
+                dhi = __dp4a(nib_hi(q0[p].z), h0.z, dhi);
+                dhi = __dp4a(nib_hi(q0[p].w), h0.w, dhi);
+                dhi = __dp4a(nib_hi(q1[p].x), h1.x, dhi);
+                dhi = __dp4a(nib_hi(q1[p].y), h1.y, dhi);
+                dhi = __dp4a(nib_hi(q1[p].z), h1.z, dhi);
+                dhi = __dp4a(nib_hi(q1[p].w), h1.w, dhi);
+                int isum = sc0[p] * dlo + sc1[p] * dhi;
+                int msum = mn0[p] * bsA + mn1[p] * bsB;
+                // the 4 items of a super-block sit on 4 aligned neighbouring lanes
+                isum += __shfl_xor_sync(0xffffffffu, isum, 1);
+                msum += __shfl_xor_sync(0xffffffffu, msum, 1);
+                isum += __shfl_xor_sync(0xffffffffu, isum, 2);
+                msum += __shfl_xor_sync(0xffffffffu, msum, 2);
+                if ((j & 3) == 0) {
+                    const float d = __fmul_rn(h2f((uint16_t)(hdr[p].x & 0xFFFF)), da);
+                    const float dm = __fmul_rn(h2f((uint16_t)((unsigned)hdr[p].x >> 16)), da);
+                    acc[p * M + m] += __fsub_rn(__fmul_rn(d, (float)isum), __fmul_rn(dm, (float)msum));
+                }
+            }
+        }
+    }
+    reduce_lanes(acc, lpr);
+    if (j == 0) {
+#pragma unroll
+        for (int p = 0; p < RP; ++p) {
+            const int64_t row = row0 + (int64_t)p * rpp;
+            if (row < N) {
+#pragma unroll
+                for (int m = 0; m < M; ++m) y[(int64_t)m * y_ld + row] = acc[p * M + m];
+            }
+        }
+    }
+}
+
+// ---- F16 / F32 weights (activations read directly; optional fp16 rounding) ------------
+template <int M, bool WF16, bool VEC>
+__global__ void __launch_bounds__(128)
+    mmv_float_kernel(const uint8_t *__restrict__ w, int64_t w_ld, int64_t N, int K, const char *__restrict__ x,
+                     int64_t x_ld, bool x_f16, bool round16, float *__restrict__ y, int64_t y_ld) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t row = (int64_t)blockIdx.x * 4 + warp;
+    if (row >= N) return;  // warp-uniform
+    constexpr int E = VEC ? 8 : 1;
+    float acc[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[m] = 0.0f;
+    const uint8_t *wr = w + row * w_ld;
+    for (int k0 = lane * E; k0 < K; k0 += 32 * E) {
+        float wv[E];
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+            wv[e] = WF16 ? h2f(reinterpret_cast<const uint16_t *>(wr)[k0 + e]) : reinterpret_cast<const float *>(wr)[k0 + e];
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            const char *xr = x + (int64_t)m * x_ld;
+#pragma unroll
+            for (int e = 0; e < E; ++e) {
+                float xv = x_f16 ? h2f(reinterpret_cast<const uint16_t *>(xr)[k0 + e]) : reinterpret_cast<const float *>(xr)[k0 + e];
+                if (round16) xv = __half2float(__float2half_rn(xv));
+                acc[m] = fmaf(wv[e], xv, acc[m]);
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[m] = warp_sum(acc[m]);
+    if (lane == 0) {
+#pragma unroll
+        for (int m = 0; m < M; ++m) y[(int64_t)m * y_ld + row] = acc[m];
+    }
+}
+
+// ---- launchers ------------------------------------------------------------------------
+static int pick_lpr_log2(int nitems, int min_log2) {
+    int l = 5;
+    while (l > min_log2 && (nitems % (1 << l)) != 0) --l;
+    return l;
+}
+
+template <int M>
+static void launch_q8(const oasr_weight *w, int64_t slice, const ActPlanes &a, int K, float *y, int64_t y_ld,
+                      cudaStream_t st, bool q4) {
+    const int64_t N = w->ne[1];
+    const int nitems = K / 32;
+    const int lg = pick_lpr_log2(nitems, 0);
+    constexpr int RP = M <= 2 ? 4 : 2;
+    const int rows_per_cta = 4 * (32 >> lg) * RP;
+    const unsigned grid = (unsigned)((N + rows_per_cta - 1) / rows_per_cta);
+    const uint8_t *wqs = w->qs + slice * N * w->qs_row_bytes;
+    const uint16_t *wd = w->d + slice * N * w->d_row_elems;
+    if (q4)
+        mmv_q8_kernel<M, RP, true><<<grid, 128, 0, st>>>(wqs, wd, w->qs_row_bytes, w->d_row_elems, N, nitems, lg,
+                                                         a.qs, a.d, K, y, y_ld);
+    else
+        mmv_q8_kernel<M, RP, false><<<grid, 128, 0, st>>>(wqs, wd, w->qs_row_bytes, w->d_row_elems, N, nitems, lg,
+                                                          a.qs, a.d, K, y, y_ld);
+}
+
+template <int M>
+static void launch_q4k(const oasr_weight *w, int64_t slice, const ActPlanes &a, int K, float *y, int64_t y_ld,
+                       cudaStream_t st) {
+    const int64_t N = w->ne[1];
+    const int nitems = K / 64;
+    const int lg = pick_lpr_log2(nitems, 2);  // nitems is a multiple of 4
+    constexpr int RP = M <= 2 ? 4 : 2;
+    const int rows_per_cta = 4 * (32 >> lg) * RP;
+    const unsigned grid = (unsigned)((N + rows_per_cta - 1) / rows_per_cta);
+    mmv_q4k_kernel<M, RP><<<grid, 128, 0, st>>>(w->qs + slice * N * w->qs_row_bytes, w->qs_row_bytes, N, nitems, lg,
+                                                a.qs, a.d, a.bs16, K, y, y_ld);
+}
+
+int launch_mmv_quant(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int M, int K,
+                     float *y, int64_t y_ld) {
+    cudaStream_t st = be->stream;
+    if (w->type == OASR_TYPE_Q4_K) {
+        switch (M) {
+        case 1: launch_q4k<1>(w, slice, a, K, y, y_ld, st); break;
+        case 2: launch_q4k<2>(w, slice, a, K, y, y_ld, st); break;
+        case 3: launch_q4k<3>(w, slice, a, K, y, y_ld, st); break;
+        case 4: launch_q4k<4>(w, slice, a, K, y, y_ld, st); break;
+        case 5: launch_q4k<5>(w, slice, a, K, y, y_ld, st); break;
+        case 6: launch_q4k<6>(w, slice, a, K, y, y_ld, st); break;
+        case 7: launch_q4k<7>(w, slice, a, K, y, y_ld, st); break;
+        default: launch_q4k<8>(w, slice, a, K, y, y_ld, st); break;
+        }
+    } else {
+        const bool q4 = w->type == OASR_TYPE_Q4_0;
+        switch (M) {
+        case 1: launch_q8<1>(w, slice, a, K, y, y_ld, st, q4); break;
+        case 2: launch_q8<2>(w, slice, a, K, y, y_ld, st, q4); break;
+        case 3: launch_q8<3>(w, slice, a, K, y, y_ld, st, q4); break;
+        case 4: launch_q8<4>(w, slice, a, K, y, y_ld, st, q4); break;
+        case 5: launch_q8<5>(w, slice, a, K, y, y_ld, st, q4); break;
+        case 6: launch_q8<6>(w, slice, a, K, y, y_ld, st, q4); break;
+        case 7: launch_q8<7>(w, slice, a, K, y, y_ld, st, q4); break;
+        default: launch_q8<8>(w, slice, a, K, y, y_ld, st, q4); break;
+        }
+    }
+    return oasr_internal_launch_check(be, "mmv_quant");
+}
+
+template <int M>
+static void launch_float_m(const oasr_weight *w, int64_t slice, const char *x, int64_t x_ld, bool x_f16, bool r16,
+                           int K, float *y, int64_t y_ld, cudaStream_t st) {
+    const int64_t N = w->ne[1];
+    const unsigned grid = (unsigned)((N + 3) / 4);
+    const uint8_t *wb = w->qs + slice * N * w->qs_row_bytes;
+    const bool vec = K % 8 == 0;
+    if (w->type == OASR_TYPE_F16) {
+        if (vec) mmv_float_kernel<M, true, true><<<grid, 128, 0, st>>>(wb, w->qs_row_bytes, N, K, x, x_ld, x_f16, r16, y, y_ld);
+        else mmv_float_kernel<M, true, false><<<grid, 128, 0, st>>>(wb, w->qs_row_bytes, N, K, x, x_ld, x_f16, r16, y, y_ld);
+    } else {
+        if (vec) mmv_float_kernel<M, false, true><<<grid, 128, 0, st>>>(wb, w->qs_row_bytes, N, K, x, x_ld, x_f16, r16, y, y_ld);
+        else mmv_float_kernel<M, false, false><<<grid, 128, 0, st>>>(wb, w->qs_row_bytes, N, K, x, x_ld, x_f16, r16, y, y_ld);
+    }
+}
+
+int launch_mmv_float(oasr_backend *be, const oasr_weight *w, int64_t slice, const char *x, int64_t x_ld_bytes,
+                     bool x_f16, bool round_x_f16, int M, int K, float *y, int64_t y_ld) {
+    cudaStream_t st = be->stream;
+    switch (M) {
+    case 1: launch_float_m<1>(w, slice, x, x_ld_bytes, x_f16, round_x_f16, K, y, y_ld, st); break;
+    case 2: launch_float_m<2>(w, slice, x, x_ld_bytes, x_f16, round_x_f16, K, y, y_ld, st); break;
+    case 3: launch_float_m<3>(w, slice, x, x_ld_bytes, x_f16, round_x_f16, K, y, y_ld, st); break;
+    case 4: launch_float_m<4>(w, slice, x, x_ld_bytes, x_f16, round_x_f16, K, y, y_ld, st); break;
+    case 5: launch_float_m<5>(w, slice, x, x_ld_bytes, x_f16, round_x_f16, K, y, y_ld, st); break;
+    case 6: launch_float_m<6>(w, slice, x, x_ld_bytes, x_f16, round_x_f16, K, y, y_ld, st); break;
+    case 7: launch_float_m<7>(w, slice, x, x_ld_bytes, x_f16, round_x_f16, K, y, y_ld, st); break;
+    default: launch_float_m<8>(w, slice, x, x_ld_bytes, x_f16, round_x_f16, K, y, y_ld, st); break;
+    }
+    return oasr_internal_launch_check(be, "mmv_float");
+}
+
+}  // namespace oasr

@@ -1,0 +1,147 @@
+"""GPU parity of GGML_OP_FLASH_ATTN_EXT against the CPU oracle, through the C ABI.
+
+Gate: max-abs-rel <= 2e-3 (north_star) against the oracle's f32-accumulator
+mode, plus TIGHT = 2e-5 to pin the arithmetic.  ggml's CPU kernel accumulates
+V in fp16 when V is f16; that accumulator is itself ~1e-2 away from exact at
+n_kv = 1500-2048 (measured by the oracle in both modes), so it is reported,
+not gated."""
+import numpy as np
+import pytest
+
+import openasr_b200 as ob
+from oracle import oracle as oo
+from tests.conftest import max_abs_rel
+
+TOL, TIGHT = 2e-3, 2e-5
+
+
+def _fa(be, q, k, v, mask, scale):
+    import torch
+
+    S, H, NQ, D = q.shape
+    qt = torch.from_numpy(np.ascontiguousarray(q)).cuda()
+    kt = torch.from_numpy(np.ascontiguousarray(k)).cuda()
+    vt = torch.from_numpy(np.ascontiguousarray(v)).cuda()
+    mt = torch.from_numpy(np.ascontiguousarray(mask)).cuda() if mask is not None else None
+    out = torch.empty((S, NQ, H, D), dtype=torch.float32, device="cuda")
+    be.flash_attn_ext(qt, kt, vt, mt, scale, out)
+    be.synchronize()
+    return out.cpu().numpy()
+
+
+def _case(seed, S, H, HKV, NQ, NKV, D, kv_dtype=np.float16):
+    rng = np.random.default_rng(seed)
+    q = rng.normal(0, 1, (S, H, NQ, D)).astype(np.float32)
+    k = rng.normal(0, 1, (S, HKV, NKV, D)).astype(kv_dtype)
+    v = rng.normal(0, 1, (S, HKV, NKV, D)).astype(kv_dtype)
+    return q, k, v
+
+
+def _causal_mask(S, NQ, NKV, valid):
+    m = np.zeros((S, 1, NQ, NKV), np.float16)
+    for s in range(S):
+        m[s, 0, :, valid[s]:] = -np.inf
+    return m
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("S", [1, 8])
+@pytest.mark.parametrize("NKV", [1, 17, 448, 1500])
+def test_whisper_decode_self_and_cross(gpu_backend, S, NKV):
+    q, k, v = _case(100 + NKV + S, S, 20, 20, 1, NKV, 64)
+    got = _fa(gpu_backend, q, k, v, None, 0.125)
+    ref = oo.flash_attn_ext(q, k, v, None, 0.125, oo.FA_F32)
+    err = max_abs_rel(got, ref)
+    assert err <= TOL and err <= TIGHT, err
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("S", [1, 4, 8])
+@pytest.mark.parametrize("NKV", [391, 2048])
+def test_qwen_gqa_decode_with_mask(gpu_backend, S, NKV):
+    q, k, v = _case(200 + NKV + S, S, 16, 8, 1, NKV, 128)
+    valid = [NKV - 3 * s for s in range(S)]
+    mask = _causal_mask(S, 1, NKV, valid)
+    got = _fa(gpu_backend, q, k, v, mask, 1 / np.sqrt(128))
+    ref = oo.flash_attn_ext(q, k, v, mask, float(np.float32(1 / np.sqrt(128))), oo.FA_F32)
+    err = max_abs_rel(got, ref)
+    assert err <= TOL and err <= TIGHT, err
+    ggml = oo.flash_attn_ext(q, k, v, mask, float(np.float32(1 / np.sqrt(128))), oo.FA_GGML)
+    assert max_abs_rel(got, ggml) < 5e-2  # ggml's own f16 V accumulator noise
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kv_dtype", [np.float16, np.float32])
+def test_encoder_self_attention_1500(gpu_backend, kv_dtype):
+    # whisper encoder: q,k,v [64, 1500, H, 1], no mask, scale 1/8 (ggml_executor.rs:1650-1695)
+    q, k, v = _case(300, 1, 6, 6, 1500, 1500, 64, kv_dtype)
+    got = _fa(gpu_backend, q, k, v, None, 0.125)
+    ref = oo.flash_attn_ext(q, k, v, None, 0.125, oo.FA_F32)
+    err = max_abs_rel(got, ref)
+    assert err <= TOL, err
+
+
+@pytest.mark.gpu
+def test_kv_cache_strided_views(gpu_backend):
+    import torch
+
+    # whisper self-KV cache [d_model, max_pos, n_seq] viewed per head as [64, n_kv, H, S]
+    S, H, D, max_pos, n_kv = 4, 6, 64, 448, 37
+    rng = np.random.default_rng(7)
+    cache_k = rng.normal(0, 1, (S, max_pos, H, D)).astype(np.float16)
+    cache_v = rng.normal(0, 1, (S, max_pos, H, D)).astype(np.float16)
+    q = rng.normal(0, 1, (S, H, 1, D)).astype(np.float32)
+    kt = torch.from_numpy(cache_k).cuda().permute(0, 2, 1, 3)[:, :, :n_kv, :]
+    vt = torch.from_numpy(cache_v).cuda().permute(0, 2, 1, 3)[:, :, :n_kv, :]
+    out = torch.empty((S, 1, H, D), dtype=torch.float32, device="cuda")
+    gpu_backend.flash_attn_ext(torch.from_numpy(q).cuda(), kt, vt, None, 0.125, out)
+    gpu_backend.synchronize()
+    ref = oo.flash_attn_ext(q, kt.cpu().numpy(), vt.cpu().numpy(), None, 0.125, oo.FA_F32)
+    assert max_abs_rel(out.cpu().numpy(), ref) <= TIGHT
+
+
+@pytest.mark.gpu
+def test_reference_kat_qwen_decode_flash_attention(gpu_backend):
+    # cpu_graph.rs:13900-13948 on the device: f32 q/k/v, head_dim 2 is below the
+    # kernel's 64/128 head sizes, so the KAT is embedded in a 64-wide head
+    scale = float(np.float32(1 / np.sqrt(2)))
+    q = np.zeros((1, 1, 1, 64), np.float32); q[..., 0] = 1
+    k = np.zeros((1, 1, 2, 64), np.float32); k[0, 0, 0, 0] = 1; k[0, 0, 1, 1] = 1
+    v = np.zeros((1, 1, 2, 64), np.float32); v[0, 0, 0, :2] = [10, 20]; v[0, 0, 1, :2] = [30, 40]
+    got = _fa(gpu_backend, q, k, v, None, scale).ravel()[:2]
+    w = np.exp(np.array([scale, 0.0]) - scale); w /= w.sum()
+    np.testing.assert_allclose(got, [w[0] * 10 + w[1] * 30, w[0] * 20 + w[1] * 40], atol=1e-4)
+
+
+@pytest.mark.gpu
+def test_reference_kat_batched_mask_planes(gpu_backend):
+    # cpu_graph.rs:13471-13540: per-sequence mask planes select one kv row each
+    q = np.zeros((2, 1, 1, 64), np.float32); q[0, 0, 0, 0] = 1; q[1, 0, 0, 1] = 1
+    k = np.zeros((2, 1, 2, 64), np.float32); k[:, 0, 0, 0] = 1; k[:, 0, 1, 1] = 1
+    v = np.zeros((2, 1, 2, 64), np.float32)
+    v[0, 0, 0, :2] = [10, 20]; v[0, 0, 1, :2] = [30, 40]; v[1, 0, 0, :2] = [-5, -6]; v[1, 0, 1, :2] = [50, 60]
+    mask = np.zeros((2, 1, 1, 2), np.float16); mask[0, 0, 0, 1] = -np.inf; mask[1, 0, 0, 0] = -np.inf
+    got = _fa(gpu_backend, q, k, v, mask, float(np.float32(1 / np.sqrt(2))))
+    np.testing.assert_allclose(got[:, 0, 0, :2].ravel(), [10, 20, 50, 60], atol=1e-4)
+
+
+@pytest.mark.gpu
+def test_fully_masked_rows_give_zero(gpu_backend):
+    q, k, v = _case(5, 2, 4, 4, 1, 300, 64)
+    mask = np.full((2, 1, 1, 300), -np.inf, np.float16)
+    mask[1, 0, 0, :10] = 0
+    got = _fa(gpu_backend, q, k, v, mask, 0.125)
+    assert np.all(got[0] == 0)
+    ref = oo.flash_attn_ext(q, k, v, mask, 0.125, oo.FA_F32)
+    assert max_abs_rel(got, ref) <= TIGHT
+
+
+@pytest.mark.gpu
+def test_flash_attn_rejects_bad_shapes(gpu_backend):
+    import torch
+
+    q = torch.zeros((1, 3, 1, 64), device="cuda")
+    k = torch.zeros((1, 2, 10, 64), device="cuda", dtype=torch.float16)
+    out = torch.zeros((1, 1, 3, 64), device="cuda")
+    with pytest.raises(ob.backend.UnsupportedInputs):
+        gpu_backend.flash_attn_ext(q, k, k, None, 1.0, out)  # 3 q heads over 2 kv heads

@@ -1,0 +1,157 @@
+"""GPU parity of GGML_OP_MUL_MAT (K1 decode GEMV, K2 GEMM) against the CPU
+oracle on seeded synthetic inputs, through the C ABI.
+
+Tolerance: north_star's max-abs-rel 2e-3.  Because the kernels form every
+per-block term exactly as ggml's CPU vec_dot does (same activation
+quantization, integer block dot, same f32 scale products), the observed gap
+is only the f32 summation order; TIGHT asserts that too, so a semantic drift
+(wrong rounding, wrong scale) cannot hide inside the 2e-3 budget."""
+import numpy as np
+import pytest
+
+import openasr_b200 as ob
+from oracle import oracle as oo
+from tests.conftest import max_abs_rel
+
+TOL = 2e-3
+TIGHT = 2e-5
+
+SHAPES = [(4096, 1024), (1024, 2048), (6144, 1024), (1024, 3072), (1280, 1280), (5120, 1280), (1280, 5120)]
+TYPES = [ob.Q8_0, ob.Q4_0, ob.Q4_K]
+
+
+def _weights(N, K, qt, seed):
+    w = oo.synth_normal(seed, N * K, 0.0, 0.02).reshape(N, K)
+    return oo.quantize(qt, w)
+
+
+def _run(be, wq, qt, N, K, x_np, prec=ob.PREC_DEFAULT):
+    import torch
+
+    W = be.upload_weight(wq, qt, [K, N])
+    try:
+        x = torch.from_numpy(x_np).cuda()
+        out = torch.empty((x_np.shape[0], N), dtype=torch.float32, device="cuda")
+        be.mul_mat(W, x, out, prec)
+        be.synchronize()
+        return out.cpu().numpy()
+    finally:
+        W.free()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qt", TYPES)
+@pytest.mark.parametrize("N,K", SHAPES)
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 8])
+def test_decode_gemv_matches_oracle(gpu_backend, qt, N, K, M):
+    if qt == ob.Q4_K and K % 256:
+        pytest.skip("Q4_K needs K % 256 == 0")
+    seed = 0x0A5A0002 + N * 7 + K + qt
+    wq = _weights(N, K, qt, seed)
+    x = oo.synth_normal(seed ^ 0xFFFF, M * K).reshape(M, K)
+    got = _run(gpu_backend, wq, qt, N, K, x)
+    ref = oo.mul_mat(wq, qt, K, N, x)
+    err = max_abs_rel(got, ref)
+    assert err <= TOL and err <= TIGHT, (qt, N, K, M, err)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qt", TYPES)
+def test_lm_head_gemv_matches_oracle(gpu_backend, qt):
+    N, K, M = 151936, 1024, 4
+    wq = _weights(N, K, qt, 0x0A5A0005)
+    x = oo.synth_normal(0x0A5A0006, M * K).reshape(M, K)
+    got = _run(gpu_backend, wq, qt, N, K, x)
+    ref = oo.mul_mat(wq, qt, K, N, x)
+    assert max_abs_rel(got, ref) <= TIGHT
+    # greedy token identity on the logits (first-max)
+    np.testing.assert_array_equal(oo.argmax_first(got), oo.argmax_first(ref))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qt", TYPES)
+@pytest.mark.parametrize("M", [9, 64, 512, 1500])
+def test_prefill_encoder_gemm_matches_oracle(gpu_backend, qt, M):
+    N, K = 1280, 1280
+    wq = _weights(N, K, qt, 0x0A5A0007 + qt)
+    x = oo.synth_normal(0x0A5A0008 + M, M * K).reshape(M, K)
+    got = _run(gpu_backend, wq, qt, N, K, x)
+    ref = oo.mul_mat(wq, qt, K, N, x)
+    err = max_abs_rel(got, ref)
+    assert err <= TOL and err <= TIGHT, (qt, M, err)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M", [1, 5, 8, 20])
+def test_f16_and_f32_weights(gpu_backend, M):
+    N, K = 96, 200
+    w = oo.synth_normal(21, N * K, 0, 0.5).reshape(N, K)
+    x = oo.synth_normal(22, M * K).reshape(M, K)
+    w16 = w.astype(np.float16)
+    got = _run(gpu_backend, w16.view(np.uint8).reshape(N, -1), ob.F16, N, K, x)
+    ref = oo.mul_mat(w16.view(np.uint16), oo.F16, K, N, x)
+    assert max_abs_rel(got, ref) <= 1e-5
+    got32 = _run(gpu_backend, w.view(np.uint8).reshape(N, -1), ob.F32, N, K, x)
+    ref32 = oo.mul_mat(w, oo.F32, K, N, x)
+    assert max_abs_rel(got32, ref32) <= 1e-5
+    # GGML_PREC_F32 keeps f32 activations against f16 weights
+    got_p = _run(gpu_backend, w16.view(np.uint8).reshape(N, -1), ob.F16, N, K, x, prec=ob.PREC_F32)
+    exact = x.astype(np.float64) @ w16.astype(np.float64).T
+    assert max_abs_rel(got_p, exact) <= 1e-5
+
+
+@pytest.mark.gpu
+def test_reference_kat_tiny_graph_mul_mat_success(gpu_backend):
+    # cpu_graph.rs:12827-12857 on the device: exact [17, 39, 23, 53]
+    lhs = np.array([[1, 2], [3, 4]], np.float32)
+    got = _run(gpu_backend, lhs.view(np.uint8).reshape(2, -1), ob.F32, 2, 2, np.array([[5, 6], [7, 8]], np.float32))
+    np.testing.assert_array_equal(got.ravel(), [17, 39, 23, 53])
+    w = np.array([0x3C00, 0, 0, 0x3C00], np.uint16).reshape(2, 2)  # :12860 identity f16
+    got = _run(gpu_backend, w.view(np.uint8).reshape(2, -1), ob.F16, 2, 2, np.array([[2, 3]], np.float32))
+    np.testing.assert_array_equal(got.ravel(), [2, 3])
+
+
+@pytest.mark.gpu
+def test_batched_broadcast_mul_mat(gpu_backend):
+    import torch
+
+    # weight [K, N, 2, 1] broadcast over rhs [K, M, 4, 1] (rhs.ne2 % lhs.ne2 == 0)
+    K, N, M = 256, 64, 3
+    w = oo.synth_normal(31, 2 * N * K, 0, 0.02).reshape(2 * N, K)
+    wq = oo.quantize(oo.Q8_0, w)
+    x = oo.synth_normal(32, 4 * M * K).reshape(4, M, K)
+    W = gpu_backend.upload_weight(wq, ob.Q8_0, [K, N, 2, 1])
+    xt = torch.from_numpy(x).cuda()
+    out = torch.empty((4, M, N), dtype=torch.float32, device="cuda")
+    gpu_backend.mul_mat(W, xt, out)
+    gpu_backend.synchronize()
+    W.free()
+    ref = oo.mul_mat(wq.reshape(2, N, -1), oo.Q8_0, K, N, x[None], w_batch=(1, 2))[0]
+    assert max_abs_rel(out.cpu().numpy(), ref) <= TIGHT
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qt", TYPES)
+def test_weight_upload_round_trip_is_bit_exact(gpu_backend, qt):
+    K, N = 1024, 48
+    wq = _weights(N, K, qt, 41)
+    W = gpu_backend.upload_weight(wq, qt, [K, N])
+    back = W.download()
+    W.free()
+    np.testing.assert_array_equal(back, wq)
+
+
+@pytest.mark.gpu
+def test_mul_mat_rejects_bad_shapes(gpu_backend):
+    import torch
+
+    wq = _weights(32, 256, ob.Q8_0, 1)
+    W = gpu_backend.upload_weight(wq, ob.Q8_0, [256, 32])
+    x = torch.zeros((2, 128), dtype=torch.float32, device="cuda")
+    out = torch.zeros((2, 32), dtype=torch.float32, device="cuda")
+    with pytest.raises(ob.backend.UnsupportedInputs, match="lhs.ne0 must equal rhs.ne0"):
+        gpu_backend.mul_mat(W, x, out)
+    W.free()
+    # capability probe of backend.rs:295-323
+    for t in (ob.Q4_0, ob.Q8_0, ob.Q4_K):
+        assert gpu_backend.device_supports_matmul_for_type(t)
