@@ -121,8 +121,9 @@ int oasr_b200_free(oasr_backend *be);                          /* ggml_backend_f
 int oasr_b200_props(oasr_backend *be, oasr_device_props *out); /* ggml_backend_dev_get_props */
 /* 1 if supported, 0 if not (ggml_backend_dev_supports_op; probe in backend.rs:295-323) */
 int oasr_b200_supports_op(oasr_backend *be, int32_t op, const oasr_tensor *src0, const oasr_tensor *src1);
-/* Enqueue subsequent work on `stream` (a cudaStream_t of this device; NULL =
- * the backend's own stream). */
+/* Enqueue subsequent work on `stream` (a cudaStream_t of this device; NULL is
+ * CUDA's legacy default stream).  A new backend starts on a non-blocking
+ * stream of its own, which oasr_b200_get_stream returns. */
 int oasr_b200_set_stream(oasr_backend *be, void *stream);
 void *oasr_b200_get_stream(oasr_backend *be);
 int oasr_b200_synchronize(oasr_backend *be);                   /* merged completion status */
@@ -156,6 +157,20 @@ int oasr_b200_weight_info(const oasr_weight *w, int32_t *type, int64_t ne[4], ui
  * (ggml_mul_mat_set_prec, ffi.rs:699) keeps f32 activations for F16 weights. */
 int oasr_b200_mul_mat(oasr_backend *be, const oasr_weight *w, const oasr_tensor *x, oasr_tensor *dst,
                       int32_t prec);
+
+/* The two halves of oasr_b200_mul_mat, for callers that feed one activation
+ * to several weights (fused QKV / gate+up read the same normed rows).  ggml's
+ * mul_mat first converts src1 into the weight's vec_dot type (its wdata
+ * buffer) and then runs the block dots; these expose that split.
+ * oasr_b200_act_bytes: device bytes of `rows` converted rows of K elements
+ * for weights of `weight_type` (negative status if unsupported).
+ * oasr_b200_quantize_act: convert x (f32|f16 [K, rows], contiguous rows) into
+ * the caller's device buffer `qact`.
+ * oasr_b200_mul_mat_qact: dst f32 [N, rows] = w . qact (qact from
+ * oasr_b200_quantize_act with the same weight type and K). */
+int64_t oasr_b200_act_bytes(int32_t weight_type, int64_t K, int64_t rows);
+int oasr_b200_quantize_act(oasr_backend *be, int32_t weight_type, const oasr_tensor *x, void *qact, size_t qact_bytes);
+int oasr_b200_mul_mat_qact(oasr_backend *be, const oasr_weight *w, const void *qact, int64_t rows, oasr_tensor *dst);
 
 /* GGML_OP_FLASH_ATTN_EXT (ggml_flash_attn_ext ffi.rs:755-764; builder
  * cpu_graph.rs:4144-4220, checks :7476-7519).

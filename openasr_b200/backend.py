@@ -129,6 +129,9 @@ SIGNATURES = {
     "oasr_b200_weight_download": ([_P, _P, _P, _SZ], ctypes.c_int),
     "oasr_b200_weight_info": ([_P, ctypes.POINTER(_I32), ctypes.POINTER(_I64), ctypes.POINTER(_U64)], ctypes.c_int),
     "oasr_b200_mul_mat": ([_P, _P, _TP, _TP, _I32], ctypes.c_int),
+    "oasr_b200_act_bytes": ([_I32, _I64, _I64], _I64),
+    "oasr_b200_quantize_act": ([_P, _I32, _TP, _P, _SZ], ctypes.c_int),
+    "oasr_b200_mul_mat_qact": ([_P, _P, _P, _I64, _TP], ctypes.c_int),
     "oasr_b200_flash_attn_ext": ([_P, _TP, _TP, _TP, _TP, _F, _F, _F, _I32, _TP], ctypes.c_int),
     "oasr_b200_set_rows": ([_P, _TP, _TP, _TP], ctypes.c_int),
     "oasr_b200_argmax_first": ([_P, _TP, _TP], ctypes.c_int),
@@ -257,6 +260,7 @@ class Backend:
         self.handle = h
         self.ordinal = ordinal
         self._abort_cb = None
+        self.own_stream = lib().oasr_b200_get_stream(h) or 0
 
     # -- status mapping (cpu_graph.rs:8380-8405) --
     def _check(self, rc: int) -> None:
@@ -280,8 +284,12 @@ class Backend:
         return {f: getattr(s, f) for f, _ in s._fields_}
 
     def set_stream(self, stream) -> None:
-        """Enqueue on a torch.cuda.Stream (or raw cudaStream_t int); None = own stream."""
-        ptr = 0 if stream is None else (stream if isinstance(stream, int) else stream.cuda_stream)
+        """Enqueue on a torch.cuda.Stream or a raw cudaStream_t (int; 0 is the
+        legacy default stream); None returns to the backend's own stream."""
+        if stream is None:
+            ptr = self.own_stream
+        else:
+            ptr = stream if isinstance(stream, int) else stream.cuda_stream
         self._check(lib().oasr_b200_set_stream(self.handle, ptr))
 
     def stream_ptr(self) -> int:
@@ -327,6 +335,21 @@ class Backend:
     # -- ops --
     def mul_mat(self, w: Weight, x, out, prec: int = PREC_DEFAULT) -> None:
         self._check(lib().oasr_b200_mul_mat(self.handle, w.handle, ctypes.byref(describe(x)), ctypes.byref(describe(out)), prec))
+
+    @staticmethod
+    def act_bytes(weight_type: int, K: int, rows: int) -> int:
+        n = int(lib().oasr_b200_act_bytes(weight_type, K, rows))
+        if n < 0:
+            raise UnsupportedInputs(n, "act_bytes: unsupported weight type or K")
+        return n
+
+    def quantize_act(self, weight_type: int, x, qact) -> None:
+        """Convert x (f32|f16 [rows, K]) into qact (a uint8 CUDA tensor of act_bytes)."""
+        self._check(lib().oasr_b200_quantize_act(self.handle, weight_type, ctypes.byref(describe(x)), qact.data_ptr(),
+                                                 qact.numel() * qact.element_size()))
+
+    def mul_mat_qact(self, w: Weight, qact, rows: int, out) -> None:
+        self._check(lib().oasr_b200_mul_mat_qact(self.handle, w.handle, qact.data_ptr(), rows, ctypes.byref(describe(out))))
 
     def flash_attn_ext(self, q, k, v, mask, scale: float, out, max_bias: float = 0.0, logit_softcap: float = 0.0,
                        prec: int = PREC_DEFAULT) -> None:

@@ -195,7 +195,7 @@ int oasr_b200_props(oasr_backend *be, oasr_device_props *out) {
 
 int oasr_b200_set_stream(oasr_backend *be, void *stream) {
     if (!be) return OASR_STATUS_FAILED;
-    be->stream = stream ? (cudaStream_t)stream : be->own_stream;
+    be->stream = (cudaStream_t)stream;  // NULL is CUDA's legacy default stream
     return OASR_STATUS_SUCCESS;
 }
 

@@ -142,6 +142,48 @@ int oasr_b200_mul_mat(oasr_backend *be, const oasr_weight *w, const oasr_tensor 
     return OASR_STATUS_SUCCESS;
 }
 
+int64_t oasr_b200_act_bytes(int32_t weight_type, int64_t K, int64_t rows) {
+    if (rows < 0 || K <= 0) return OASR_STATUS_FAILED;
+    if (weight_type == OASR_TYPE_Q8_0 || weight_type == OASR_TYPE_Q4_0)
+        return K % 32 ? OASR_STATUS_FAILED : (int64_t)act_planes_bytes(FAMILY_Q8_0, rows, K);
+    if (weight_type == OASR_TYPE_Q4_K) return K % 256 ? OASR_STATUS_FAILED : (int64_t)act_planes_bytes(FAMILY_Q8_K, rows, K);
+    return OASR_STATUS_FAILED;
+}
+
+int oasr_b200_quantize_act(oasr_backend *be, int32_t weight_type, const oasr_tensor *x, void *qact, size_t qact_bytes) {
+    int st = oasr_internal_precheck(be);
+    if (st) return st;
+    if (!x || !qact) return oasr_internal_fail(be, OASR_STATUS_FAILED, "quantize_act: null argument");
+    if ((x->type != OASR_TYPE_F32 && x->type != OASR_TYPE_F16) || x->nb[0] != type_size(x->type))
+        return oasr_internal_fail(be, OASR_STATUS_FAILED, "quantize_act: x must be f32/f16 with contiguous rows");
+    const int64_t R = x->ne[1] * x->ne[2] * x->ne[3];
+    const int64_t need = oasr_b200_act_bytes(weight_type, x->ne[0], R);
+    if (need < 0) return oasr_internal_fail(be, OASR_STATUS_FAILED, "quantize_act: unsupported weight type or K");
+    if ((size_t)need > qact_bytes || ((uintptr_t)qact & 255))
+        return oasr_internal_fail(be, OASR_STATUS_FAILED, "quantize_act: buffer too small or not 256-byte aligned");
+    const int family = weight_type == OASR_TYPE_Q4_K ? FAMILY_Q8_K : FAMILY_Q8_0;
+    return launch_quantize_act(be, x, family, act_planes_at(qact, family, R, x->ne[0]));
+}
+
+int oasr_b200_mul_mat_qact(oasr_backend *be, const oasr_weight *w, const void *qact, int64_t rows, oasr_tensor *dst) {
+    int st = oasr_internal_precheck(be);
+    if (st) return st;
+    if (!w || !qact || !dst) return oasr_internal_fail(be, OASR_STATUS_FAILED, "mul_mat_qact: null argument");
+    if (w->type != OASR_TYPE_Q8_0 && w->type != OASR_TYPE_Q4_0 && w->type != OASR_TYPE_Q4_K)
+        return oasr_internal_fail(be, OASR_STATUS_FAILED, "mul_mat_qact: weight must be Q8_0, Q4_0 or Q4_K");
+    if (w->ne[2] != 1 || w->ne[3] != 1) return oasr_internal_fail(be, OASR_STATUS_FAILED, "mul_mat_qact: 2-D weights only");
+    const int64_t K = w->ne[0], N = w->ne[1];
+    if (dst->type != OASR_TYPE_F32 || dst->ne[0] != N || dst->ne[1] != rows || dst->ne[2] != 1 || dst->ne[3] != 1 ||
+        dst->nb[0] != 4 || dst->nb[1] % 4)
+        return oasr_internal_fail(be, OASR_STATUS_FAILED, "mul_mat_qact: dst must be f32 [N, rows]");
+    if (rows == 0) return OASR_STATUS_SUCCESS;
+    const int family = w->type == OASR_TYPE_Q4_K ? FAMILY_Q8_K : FAMILY_Q8_0;
+    ActPlanes a = act_planes_at(const_cast<void *>(qact), family, rows, K);
+    float *y = (float *)dst->data;
+    if (rows <= 8) return launch_mmv_quant(be, w, 0, a, (int)rows, (int)K, y, dst->nb[1] / 4);
+    return launch_mmq(be, w, 0, a, rows, (int)K, y, dst->nb[1] / 4);
+}
+
 int oasr_b200_flash_attn_ext(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
                              const oasr_tensor *mask, float scale, float max_bias, float logit_softcap, int32_t prec,
                              oasr_tensor *dst) {

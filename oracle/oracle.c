@@ -59,7 +59,22 @@ uint16_t oo_f32_to_f16(float f) {
     return (uint16_t)(sign | h);
 }
 
+static float f16_table[65536];
+static pthread_once_t f16_once = PTHREAD_ONCE_INIT;
+static float f16_to_f32_bits(uint16_t h);
+static void f16_table_init(void) {
+    for (uint32_t i = 0; i < 65536; ++i) f16_table[i] = f16_to_f32_bits((uint16_t)i);
+}
+
+/* table lookup (like ggml's ggml_table_f32_f16), filled from the bit-level conversion below */
 float oo_f16_to_f32(uint16_t h) {
+    pthread_once(&f16_once, f16_table_init);
+    return f16_table[h];
+}
+
+static inline float f16(uint16_t h) { return f16_table[h]; }
+
+static float f16_to_f32_bits(uint16_t h) {
     uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
     uint32_t exp = (h >> 10) & 0x1fu;
     uint32_t mant = h & 0x3ffu;
@@ -375,7 +390,7 @@ static float dot_q8_0_q8_0(const blk_q8_0 *x, const blk_q8_0 *y, int64_t nb) {
     for (int64_t b = 0; b < nb; ++b) {
         int sumi = 0;
         for (int j = 0; j < QK8_0; ++j) sumi += (int)x[b].qs[j] * (int)y[b].qs[j];
-        const float dd = oo_f16_to_f32(x[b].d) * oo_f16_to_f32(y[b].d);
+        const float dd = f16(x[b].d) * f16(y[b].d);
         sumf += (float)sumi * dd;
     }
     return sumf;
@@ -389,7 +404,7 @@ static float dot_q4_0_q8_0(const blk_q4_0 *x, const blk_q8_0 *y, int64_t nb) {
             sumi += ((x[b].qs[j] & 0xF) - 8) * (int)y[b].qs[j];
             sumi += ((x[b].qs[j] >> 4) - 8) * (int)y[b].qs[j + QK4_0 / 2];
         }
-        const float dd = oo_f16_to_f32(x[b].d) * oo_f16_to_f32(y[b].d);
+        const float dd = f16(x[b].d) * f16(y[b].d);
         sumf += (float)sumi * dd;
     }
     return sumf;
@@ -413,8 +428,8 @@ static float dot_q4_K_q8_K(const blk_q4_K *x, const blk_q8_K *y, int64_t nb) {
             isum += sc * dot;
             msum += m * ((int)y[b].bsums[2 * j] + (int)y[b].bsums[2 * j + 1]);
         }
-        const float d = oo_f16_to_f32(x[b].d) * y[b].d;
-        const float dmin = oo_f16_to_f32(x[b].dmin) * y[b].d;
+        const float d = f16(x[b].d) * y[b].d;
+        const float dmin = f16(x[b].dmin) * y[b].d;
         const float t1 = d * (float)isum;
         const float t2 = dmin * (float)msum;
         sumf += t1 - t2;
@@ -424,7 +439,7 @@ static float dot_q4_K_q8_K(const blk_q4_K *x, const blk_q8_K *y, int64_t nb) {
 
 static float dot_f16_f16(const uint16_t *x, const uint16_t *y, int64_t n) {
     double s = 0.0;
-    for (int64_t i = 0; i < n; ++i) s += (double)(oo_f16_to_f32(x[i]) * oo_f16_to_f32(y[i]));
+    for (int64_t i = 0; i < n; ++i) s += (double)(f16(x[i]) * f16(y[i]));
     return (float)s;
 }
 
@@ -445,6 +460,7 @@ static int vec_dot_type(int wtype) {
 }
 
 int oo_mul_mat(const oo_tensor *w, const oo_tensor *x, oo_tensor *dst) {
+    pthread_once(&f16_once, f16_table_init);
     const int64_t K = w->ne[0], N = w->ne[1];
     if (x->ne[0] != K) return OO_STATUS_FAILED;
     if (x->ne[2] % w->ne[2] || x->ne[3] % w->ne[3]) return OO_STATUS_FAILED;

@@ -155,3 +155,28 @@ def test_mul_mat_rejects_bad_shapes(gpu_backend):
     # capability probe of backend.rs:295-323
     for t in (ob.Q4_0, ob.Q8_0, ob.Q4_K):
         assert gpu_backend.device_supports_matmul_for_type(t)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qt", TYPES)
+@pytest.mark.parametrize("M", [1, 8, 100])
+def test_shared_activation_quantization(gpu_backend, qt, M):
+    """quantize_act once, then mul_mat_qact on two weights == two plain mul_mats."""
+    import torch
+
+    K, N = 1024, 640
+    x = oo.synth_normal(51 + M, M * K).reshape(M, K)
+    xt = torch.from_numpy(x).cuda()
+    qact = torch.empty(gpu_backend.act_bytes(qt, K, M), dtype=torch.uint8, device="cuda")
+    gpu_backend.quantize_act(qt, xt, qact)
+    for seed in (52, 53):
+        wq = _weights(N, K, qt, seed)
+        W = gpu_backend.upload_weight(wq, qt, [K, N])
+        a = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        b = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        gpu_backend.mul_mat_qact(W, qact, M, a)
+        gpu_backend.mul_mat(W, xt, b)
+        gpu_backend.synchronize()
+        W.free()
+        np.testing.assert_array_equal(a.cpu().numpy(), b.cpu().numpy())
+        assert max_abs_rel(a.cpu().numpy(), oo.mul_mat(wq, qt, K, N, x)) <= TIGHT
