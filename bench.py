@@ -70,9 +70,11 @@ class ClockSampler:
 
     def start(self):
         try:
+            # stdbuf: nvidia-smi block-buffers into a pipe; line buffering lets samples through
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                ["stdbuf", "-oL", "nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                text=True)
         except OSError:
             self.proc = None
             return

@@ -9,19 +9,27 @@ namespace oasr {
 
 enum { FAMILY_Q8_0 = 0, FAMILY_Q8_K = 1 };
 
-// Planar quantized activations in scratch (see quant_act.cu).
+// Planar quantized activations in scratch (see quant_act.cu).  The q8_K
+// family also carries fp16 copies of the quants and 16-wide sums (exact
+// small integers) when the row count reaches the tensor-core GEMM (R > 8).
 struct ActPlanes {
-    int8_t *qs;    // [R][K]
-    float *d;      // [R][K/32] (q8_0) or [R][K/256] (q8_K)
-    int16_t *bs16; // [R][K/16] (q8_K only)
+    int8_t *qs;      // [R][K]
+    float *d;        // [R][K/32] (q8_0) or [R][K/256] (q8_K)
+    int16_t *bs16;   // [R][K/16] (q8_K only)
+    __half *qs16;    // [R][K]    (q8_K, R > 8)
+    __half *bs16h;   // [R][K/16] (q8_K, R > 8)
 };
 
 inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
+inline bool act_has_f16(int family, int64_t R) { return family == FAMILY_Q8_K && R > 8; }
+
 inline size_t act_planes_bytes(int family, int64_t R, int64_t K) {
     size_t b = align256((size_t)(R * K));
     if (family == FAMILY_Q8_0) return b + align256((size_t)(R * (K / 32)) * 4);
-    return b + align256((size_t)(R * (K / 256)) * 4) + align256((size_t)(R * (K / 16)) * 2);
+    b += align256((size_t)(R * (K / 256)) * 4) + align256((size_t)(R * (K / 16)) * 2);
+    if (act_has_f16(family, R)) b += align256((size_t)(R * K) * 2) + align256((size_t)(R * (K / 16)) * 2);
+    return b;
 }
 
 inline ActPlanes act_planes_at(void *base, int family, int64_t R, int64_t K) {
@@ -30,13 +38,31 @@ inline ActPlanes act_planes_at(void *base, int family, int64_t R, int64_t K) {
     a.qs = (int8_t *)p;
     p += align256((size_t)(R * K));
     a.d = (float *)p;
-    if (family == FAMILY_Q8_0) {
-        a.bs16 = nullptr;
-    } else {
+    a.bs16 = nullptr;
+    a.qs16 = nullptr;
+    a.bs16h = nullptr;
+    if (family == FAMILY_Q8_K) {
         p += align256((size_t)(R * (K / 256)) * 4);
         a.bs16 = (int16_t *)p;
+        p += align256((size_t)(R * (K / 16)) * 2);
+        if (act_has_f16(family, R)) {
+            a.qs16 = (__half *)p;
+            p += align256((size_t)(R * K) * 2);
+            a.bs16h = (__half *)p;
+        }
     }
     return a;
+}
+
+// row offset r0 into planes laid out for K-element rows
+inline ActPlanes act_planes_offset(const ActPlanes &a, int family, int64_t r0, int64_t K) {
+    ActPlanes s = a;
+    s.qs = a.qs + r0 * K;
+    s.d = a.d + r0 * (K / (family == FAMILY_Q8_0 ? 32 : 256));
+    if (a.bs16) s.bs16 = a.bs16 + r0 * (K / 16);
+    if (a.qs16) s.qs16 = a.qs16 + r0 * K;
+    if (a.bs16h) s.bs16h = a.bs16h + r0 * (K / 16);
+    return s;
 }
 
 int launch_quantize_act(oasr_backend *be, const oasr_tensor *x, int family, const ActPlanes &p);

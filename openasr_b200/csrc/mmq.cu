@@ -1,21 +1,331 @@
-// mmq.cu -- K2 entry: quantized GEMM for M > 8 activation rows (encoder,
-// prefill).  This first revision tiles the M rows into groups of 8 and runs
-// the K1 GEMV kernel per group (same exact per-block arithmetic, weights
-// re-read per group from L2).
+// mmq.cu -- K2: quantized GEMM for M > 8 activation rows (encoder, prefill).
+//
+// Q4_K weights run on the 5th-generation tensor cores (tcgen05, accumulators
+// in TMEM) with ggml's exact per-super-block arithmetic:
+//   ggml CPU (vec_dot_q4_K_q8_K) forms, per 256-element super-block,
+//     isum = sum_j sc_j * <q4_j, q8_j>          (integers)
+//     msum = sum_j m_j * bsum32_j               (integers)
+//     term = (d_w*d_a)*isum - (dmin_w*d_a)*msum (f32)
+//   Here the 6-bit sub-scales are folded into the weight operand (sc*q <= 945,
+//   exact in fp16) and the q8_K activations are fp16 integers, so one
+//   tcgen05.mma.kind::f16 chain over the super-block yields isum exactly in
+//   the f32 accumulator; a second K=16 MMA of the 16-wide activation sums
+//   against the duplicated mins yields msum.  The epilogue forms `term` with
+//   the same roundings as ggml and adds the super-blocks in order, so the
+//   result equals the CPU oracle's bit for bit.
+//
+// CTA = 128 activation rows x 128 weight rows, 14 warps:
+//   warp 0      TMA producer of the activation tiles (128 x 64 fp16, SW128)
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2-5   weight transform: raw Q4_K blocks -> fp16 sc*q in the SW128
+//               K-major layout, plus the per-super-block min tiles
+//   warps 6-13  epilogue: TMEM -> registers, per-super-block scaling
+// TMEM: two accumulator sets (isum 128 cols + msum 128 cols) so the epilogue
+// of super-block s overlaps the MMAs of s+1.  Every mbarrier wait is bounded.
+//
+// Q8_0 / Q4_0 (per-32 scales) still use the K1 GEMV kernel over groups of 8
+// rows in this revision.
+#include <cudaTypedefs.h>
+
 #include "kernels.cuh"
+#include "tc_common.cuh"
 
 namespace oasr {
+
+namespace q4k {
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int BK = 64;
+constexpr int STAGES = 3;
+constexpr int TILE = 128 * 128;  // bytes of one 128-row x 128-byte operand tile
+constexpr int NTHREADS = 448;
+constexpr int OFF_A = 0;
+constexpr int OFF_B = OFF_A + STAGES * TILE;
+constexpr int OFF_AMIN = OFF_B + STAGES * TILE;
+constexpr int OFF_BMIN = OFF_AMIN + 2 * TILE;
+constexpr int OFF_BAR = OFF_BMIN + 2 * TILE;
+constexpr int NBAR = 3 * STAGES + 9;
+constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
+}  // namespace q4k
+
+static __device__ __forceinline__ int q4k_byte(const int4 &h, int i) {
+    const int w = i < 4 ? h.y : (i < 8 ? h.z : h.w);
+    return (w >> (8 * (i & 3))) & 0xFF;
+}
+static __device__ __forceinline__ void q4k_scale_min(const int4 &h, int j, int &sc, int &m) {
+    if (j < 4) {
+        sc = q4k_byte(h, j) & 63;
+        m = q4k_byte(h, j + 4) & 63;
+    } else {
+        sc = (q4k_byte(h, j + 4) & 0xF) | ((q4k_byte(h, j - 4) >> 6) << 4);
+        m = (q4k_byte(h, j + 4) >> 4) | ((q4k_byte(h, j) >> 6) << 4);
+    }
+}
+
+__global__ void __launch_bounds__(448, 1)
+    mmq_q4k_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const uint8_t *__restrict__ w, int64_t w_ld, int N,
+                      const __half *__restrict__ bs16h, const float *__restrict__ ad, int M, int K,
+                      float *__restrict__ y, int64_t y_ld, int *err) {
+    using namespace q4k;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = (uint64_t *)(smem + OFF_BAR);
+    uint64_t *full_a = bars;
+    uint64_t *full_b = bars + STAGES;
+    uint64_t *empty = bars + 2 * STAGES;
+    uint64_t *full_min = bars + 3 * STAGES;
+    uint64_t *empty_min = full_min + 2;
+    uint64_t *tmem_full = empty_min + 2;
+    uint64_t *tmem_empty = tmem_full + 2;
+    uint64_t *done = tmem_empty + 2;
+    uint32_t *tmem_slot = (uint32_t *)(smem + OFF_MISC);
+    volatile int *abort_flag = (volatile int *)(smem + OFF_MISC + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int nkc = K / BK, nsb = K / 256;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&full_a[i], 1);
+            mbar_init(&full_b[i], 128);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&full_min[i], 128);
+            mbar_init(&empty_min[i], 1);
+            mbar_init(&tmem_full[i], 1);
+            mbar_init(&tmem_empty[i], 256);
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int issued = 0;
+            for (int kc = 0; kc < nkc; ++kc) {
+                const int s = kc % STAGES;
+                const uint32_t ph = (kc / STAGES) & 1;
+                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, err)) break;
+                mbar_arrive_expect_tx(&full_a[s], TILE);
+                tma_load_2d(smem + OFF_A + s * TILE, &tmap_a, &full_a[s], kc * BK, m0);
+                issued = kc + 1;
+            }
+            // no TMA write may still be in flight when the CTA exits
+            for (int kc = max(0, issued - STAGES); kc < issued; ++kc) {
+                const long long t0 = clock64();
+                while (!mbar_try_wait(&full_a[kc % STAGES], (kc / STAGES) & 1) && clock64() - t0 < (1LL << 31)) {
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16_f32(BM, BN);
+            bool ok = true;
+            for (int sb = 0; sb < nsb && ok; ++sb) {
+                const int ab = sb & 1;
+                const uint32_t aph = (sb >> 1) & 1;
+                if (!mbar_wait(&tmem_empty[ab], aph ^ 1, abort_flag, err)) break;
+                tc_fence_after();
+                const uint32_t d_isum = tmem + ab * 256, d_msum = tmem + ab * 256 + 128;
+                for (int c = 0; c < 4 && ok; ++c) {
+                    const int kc = sb * 4 + c, s = kc % STAGES;
+                    const uint32_t ph = (kc / STAGES) & 1;
+                    if (!mbar_wait(&full_a[s], ph, abort_flag, err) || !mbar_wait(&full_b[s], ph, abort_flag, err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t da = sw128_desc(smem_u32(smem + OFF_A + s * TILE));
+                    const uint64_t db = sw128_desc(smem_u32(smem + OFF_B + s * TILE));
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)  // 4 x K=16 (32 bytes) inside the 128-byte swizzle row
+                        umma_f16(d_isum, da + 2 * k, db + 2 * k, idesc, (c | k) != 0);
+                    umma_commit(&empty[s]);
+                }
+                if (!ok) break;
+                const int mb = sb & 1;
+                if (!mbar_wait(&full_min[mb], (sb >> 1) & 1, abort_flag, err)) break;
+                tc_fence_after();
+                umma_f16(d_msum, sw128_desc(smem_u32(smem + OFF_AMIN + mb * TILE)),
+                         sw128_desc(smem_u32(smem + OFF_BMIN + mb * TILE)), idesc, 0);
+                umma_commit(&empty_min[mb]);
+                umma_commit(&tmem_full[ab]);
+            }
+            // every MMA issued above completes before TMEM is released
+            umma_commit(done);
+            const long long t0 = clock64();
+            while (!mbar_try_wait(done, 0) && clock64() - t0 < (1LL << 31)) {
+            }
+        }
+    } else if (warp < 6) {
+        // ---- weight transform: one weight row (and one activation min row) per thread ----
+        const int t = threadIdx.x - 64;
+        const int n = n0 + t, m = m0 + t;
+        const bool nv = n < N, mv = m < M;
+        const uint8_t *wrow = w + (int64_t)(nv ? n : 0) * w_ld;
+        for (int kc = 0; kc < nkc; ++kc) {
+            const int s = kc % STAGES, sb = kc >> 2, c = kc & 3;
+            const uint32_t ph = (kc / STAGES) & 1;
+            if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, err)) break;
+            int4 hdr = make_int4(0, 0, 0, 0), q0 = hdr, q1 = hdr;
+            if (nv) {
+                const uint8_t *bp = wrow + (int64_t)sb * 144;
+                hdr = ldg_stream(bp);
+                q0 = ldg_stream(bp + 16 + 32 * c);
+                q1 = ldg_stream(bp + 32 + 32 * c);
+            }
+            int sc0, mn0, sc1, mn1;
+            q4k_scale_min(hdr, 2 * c, sc0, mn0);
+            q4k_scale_min(hdr, 2 * c + 1, sc1, mn1);
+            const uint32_t qw[8] = {(uint32_t)q0.x, (uint32_t)q0.y, (uint32_t)q0.z, (uint32_t)q0.w,
+                                    (uint32_t)q1.x, (uint32_t)q1.y, (uint32_t)q1.z, (uint32_t)q1.w};
+            uint8_t *bt = smem + OFF_B + s * TILE;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                // chunk j = K elements 8j..8j+7 of this 64-wide slice:
+                // j < 4: low nibbles of qs bytes 8j..8j+7 (sub-block 2c), else high nibbles (2c+1)
+                const int jj = j & 3, sh = j < 4 ? 0 : 4, sc = j < 4 ? sc0 : sc1;
+                const uint32_t w0 = qw[2 * jj], w1 = qw[2 * jj + 1];
+                __half2 h[4];
+                h[0] = __halves2half2(__int2half_rn(sc * (int)((w0 >> sh) & 15)), __int2half_rn(sc * (int)((w0 >> (8 + sh)) & 15)));
+                h[1] = __halves2half2(__int2half_rn(sc * (int)((w0 >> (16 + sh)) & 15)), __int2half_rn(sc * (int)((w0 >> (24 + sh)) & 15)));
+                h[2] = __halves2half2(__int2half_rn(sc * (int)((w1 >> sh) & 15)), __int2half_rn(sc * (int)((w1 >> (8 + sh)) & 15)));
+                h[3] = __halves2half2(__int2half_rn(sc * (int)((w1 >> (16 + sh)) & 15)), __int2half_rn(sc * (int)((w1 >> (24 + sh)) & 15)));
+                *reinterpret_cast<int4 *>(bt + sw128_off(t, j)) = *reinterpret_cast<int4 *>(h);
+            }
+            if (c == 0) {
+                const int mb = sb & 1;
+                if (!mbar_wait(&empty_min[mb], ((sb >> 1) & 1) ^ 1, abort_flag, err)) break;
+                int mn[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    int scj;
+                    q4k_scale_min(hdr, j, scj, mn[j]);
+                }
+                __half2 hb[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) hb[j] = __halves2half2(__int2half_rn(mn[j]), __int2half_rn(mn[j]));
+                uint8_t *bm = smem + OFF_BMIN + mb * TILE;
+                *reinterpret_cast<int4 *>(bm + sw128_off(t, 0)) = *reinterpret_cast<int4 *>(&hb[0]);
+                *reinterpret_cast<int4 *>(bm + sw128_off(t, 1)) = *reinterpret_cast<int4 *>(&hb[4]);
+                int4 a0 = make_int4(0, 0, 0, 0), a1 = a0;
+                if (mv) {
+                    const __half *ap = bs16h + (int64_t)m * (K / 16) + sb * 16;
+                    a0 = *reinterpret_cast<const int4 *>(ap);
+                    a1 = *reinterpret_cast<const int4 *>(ap + 8);
+                }
+                uint8_t *am = smem + OFF_AMIN + mb * TILE;
+                *reinterpret_cast<int4 *>(am + sw128_off(t, 0)) = a0;
+                *reinterpret_cast<int4 *>(am + sw128_off(t, 1)) = a1;
+                fence_proxy_async_smem();
+                mbar_arrive(&full_min[mb]);
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&full_b[s]);
+        }
+    } else {
+        // ---- epilogue ----
+        const int e = warp - 6, q = warp & 3, hcol = e >> 2;
+        const int row = m0 + 32 * q + lane;
+        const bool rv = row < M;
+        float acc[64];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) acc[i] = 0.0f;
+        for (int sb = 0; sb < nsb; ++sb) {
+            const int ab = sb & 1;
+            if (!mbar_wait(&tmem_full[ab], (sb >> 1) & 1, abort_flag, err)) break;
+            tc_fence_after();
+            const float da = rv ? __ldg(ad + (int64_t)row * nsb + sb) : 0.0f;
+            const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(ab * 256 + 64 * hcol);
+#pragma unroll
+            for (int cb = 0; cb < 4; ++cb) {
+                uint32_t ri[16], rm[16];
+                tmem_ld16(tb + 16 * cb, ri);
+                tmem_ld16(tb + 128 + 16 * cb, rm);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int n = n0 + 64 * hcol + 16 * cb + i;
+                    const uint32_t dd = n < N ? __ldg(reinterpret_cast<const uint32_t *>(w + (int64_t)n * w_ld + (int64_t)sb * 144)) : 0u;
+                    const float d = __fmul_rn(h2f((uint16_t)(dd & 0xFFFF)), da);
+                    const float dm = __fmul_rn(h2f((uint16_t)(dd >> 16)), da);
+                    acc[16 * cb + i] += __fsub_rn(__fmul_rn(d, __uint_as_float(ri[i])), __fmul_rn(dm, __uint_as_float(rm[i])));
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tmem_empty[ab]);
+        }
+        if (rv) {
+            float *yr = y + (int64_t)row * y_ld + n0 + 64 * hcol;
+#pragma unroll
+            for (int i = 0; i < 64; ++i)
+                if (n0 + 64 * hcol + i < N) yr[i] = acc[i];
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// ---- host side ----------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    }
+    return fn;
+}
+
+static int launch_q4k_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int64_t M, int K,
+                         float *y, int64_t y_ld) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return oasr_internal_fail(be, OASR_STATUS_FAILED, "cuTensorMapEncodeTiled unavailable");
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {64, 128};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)a.qs16, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return oasr_internal_fail(be, OASR_STATUS_FAILED, "cuTensorMapEncodeTiled failed");
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(mmq_q4k_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, q4k::SMEM_BYTES);
+        attr_set = true;
+    }
+    const int64_t N = w->ne[1];
+    dim3 grid((unsigned)((N + q4k::BN - 1) / q4k::BN), (unsigned)((M + q4k::BM - 1) / q4k::BM));
+    mmq_q4k_tc_kernel<<<grid, q4k::NTHREADS, q4k::SMEM_BYTES, be->stream>>>(
+        map, w->qs + slice * N * w->qs_row_bytes, w->qs_row_bytes, (int)N, a.bs16h, a.d, (int)M, K, y, y_ld,
+        be->err_word);
+    return oasr_internal_launch_check(be, "mmq_q4k_tc");
+}
 
 int launch_mmq(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int64_t M, int K,
                float *y, int64_t y_ld) {
     const bool k_family = w->type == OASR_TYPE_Q4_K;
+    if (k_family && a.qs16 && a.bs16h) return launch_q4k_tc(be, w, slice, a, M, K, y, y_ld);
+    const int family = k_family ? FAMILY_Q8_K : FAMILY_Q8_0;
     for (int64_t m0 = 0; m0 < M; m0 += 8) {
         const int mc = (int)std::min<int64_t>(8, M - m0);
-        ActPlanes s;
-        s.qs = a.qs + m0 * K;
-        s.d = a.d + m0 * (K / (k_family ? 256 : 32));
-        s.bs16 = k_family ? a.bs16 + m0 * (K / 16) : nullptr;
-        int st = launch_mmv_quant(be, w, slice, s, mc, K, y + m0 * y_ld, y_ld);
+        int st = launch_mmv_quant(be, w, slice, act_planes_offset(a, family, m0, K), mc, K, y + m0 * y_ld, y_ld);
         if (st) return st;
     }
     return OASR_STATUS_SUCCESS;

@@ -32,7 +32,7 @@ static __device__ __forceinline__ void reduce_lanes(float (&v)[N], int lpr) {
 
 // ---- Q8_0 / Q4_0 -----------------------------------------------------------------------
 template <int M, int RP, bool Q4>
-__global__ void __launch_bounds__(128, 4)
+__global__ void __launch_bounds__(128, 3)
     mmv_q8_kernel(const uint8_t *__restrict__ wqs, const uint16_t *__restrict__ wd, int64_t qs_ld, int64_t d_ld,
                   int64_t N, int nitems, int lpr_log2, const int8_t *__restrict__ aqs, const float *__restrict__ ad,
                   int K, float *__restrict__ y, int64_t y_ld) {
@@ -126,7 +126,7 @@ static __device__ __forceinline__ void scale_min(const int4 &h, int j, int &sc, 
 }
 
 template <int M, int RP>
-__global__ void __launch_bounds__(128, 4)
+__global__ void __launch_bounds__(128, 3)
     mmv_q4k_kernel(const uint8_t *__restrict__ w, int64_t w_ld, int64_t N, int nitems, int lpr_log2,
                    const int8_t *__restrict__ aqs, const float *__restrict__ ad, const int16_t *__restrict__ abs16,
                    int K, float *__restrict__ y, int64_t y_ld) {
@@ -268,7 +268,7 @@ static void launch_q8(const oasr_weight *w, int64_t slice, const ActPlanes &a, i
     const int64_t N = w->ne[1];
     const int nitems = K / 32;
     const int lg = pick_lpr_log2(nitems, 0);
-    constexpr int RP = M <= 2 ? 4 : 2;
+    constexpr int RP = 4;
     const int rows_per_cta = 4 * (32 >> lg) * RP;
     const unsigned grid = (unsigned)((N + rows_per_cta - 1) / rows_per_cta);
     const uint8_t *wqs = w->qs + slice * N * w->qs_row_bytes;
@@ -287,7 +287,7 @@ static void launch_q4k(const oasr_weight *w, int64_t slice, const ActPlanes &a, 
     const int64_t N = w->ne[1];
     const int nitems = K / 64;
     const int lg = pick_lpr_log2(nitems, 2);  // nitems is a multiple of 4
-    constexpr int RP = M <= 2 ? 4 : 2;
+    constexpr int RP = 4;
     const int rows_per_cta = 4 * (32 >> lg) * RP;
     const unsigned grid = (unsigned)((N + rows_per_cta - 1) / rows_per_cta);
     mmv_q4k_kernel<M, RP><<<grid, 128, 0, st>>>(w->qs + slice * N * w->qs_row_bytes, w->qs_row_bytes, N, nitems, lg,

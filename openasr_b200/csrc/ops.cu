@@ -114,10 +114,7 @@ int oasr_b200_mul_mat(oasr_backend *be, const oasr_weight *w, const oasr_tensor 
                 const int64_t slice = (i2 / r2) + (i3 / r3) * w->ne[2];
                 float *y = reinterpret_cast<float *>((char *)dst->data + i2 * dst->nb[2] + i3 * dst->nb[3]);
                 const int64_t y_ld = dst->nb[1] / 4;
-                ActPlanes a;
-                a.qs = all.qs + r0 * K;
-                a.d = all.d + r0 * (K / (family == FAMILY_Q8_0 ? 32 : 256));
-                a.bs16 = family == FAMILY_Q8_0 ? nullptr : all.bs16 + r0 * (K / 16);
+                const ActPlanes a = act_planes_offset(all, family, r0, K);
                 if (M <= 8) st = launch_mmv_quant(be, w, slice, a, (int)M, (int)K, y, y_ld);
                 else st = launch_mmq(be, w, slice, a, M, (int)K, y, y_ld);
                 if (st) return st;

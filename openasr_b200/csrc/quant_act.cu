@@ -66,7 +66,8 @@ __global__ void __launch_bounds__(256) quantize_q8_0_kernel(ActRows xr, int K, i
 // one warp per 256-element super-block, 8 elements per lane
 template <bool F16>
 __global__ void __launch_bounds__(256) quantize_q8_K_kernel(ActRows xr, int K, int64_t R, int8_t *__restrict__ qs,
-                                                            float *__restrict__ dsc, int16_t *__restrict__ bs16) {
+                                                            float *__restrict__ dsc, int16_t *__restrict__ bs16,
+                                                            __half *__restrict__ qs16, __half *__restrict__ bs16h) {
     const int lane = threadIdx.x & 31;
     const int64_t nsb = K / 256;
     const int64_t total = R * nsb;
@@ -117,6 +118,14 @@ __global__ void __launch_bounds__(256) quantize_q8_K_kernel(ActRows xr, int K, i
         *reinterpret_cast<uint2 *>(qs + r * K + k0) = pk;
         if ((lane & 1) == 0) bs16[r * (K / 16) + k0 / 16] = (int16_t)sum;
         if (lane == 0) dsc[r * nsb + sb] = d;
+        if (qs16) {
+            // exact fp16 copies (|q| <= 127, |16-sum| <= 2032) for the tensor-core GEMM
+            __half2 h[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) h[i] = __halves2half2(__int2half_rn(q[2 * i]), __int2half_rn(q[2 * i + 1]));
+            *reinterpret_cast<int4 *>(qs16 + r * K + k0) = *reinterpret_cast<int4 *>(h);
+            if ((lane & 1) == 0) bs16h[r * (K / 16) + k0 / 16] = __int2half_rn(sum);
+        }
     }
 }
 
@@ -137,9 +146,9 @@ int launch_quantize_act(oasr_backend *be, const oasr_tensor *x, int family, cons
         const int64_t work = R * (K / 256) * 32;
         const int blocks = (int)std::min<int64_t>((work + threads - 1) / threads, (int64_t)be->sm_count * 16);
         if (f16)
-            quantize_q8_K_kernel<true><<<blocks, threads, 0, be->stream>>>(xr, K, R, p.qs, p.d, p.bs16);
+            quantize_q8_K_kernel<true><<<blocks, threads, 0, be->stream>>>(xr, K, R, p.qs, p.d, p.bs16, p.qs16, p.bs16h);
         else
-            quantize_q8_K_kernel<false><<<blocks, threads, 0, be->stream>>>(xr, K, R, p.qs, p.d, p.bs16);
+            quantize_q8_K_kernel<false><<<blocks, threads, 0, be->stream>>>(xr, K, R, p.qs, p.d, p.bs16, p.qs16, p.bs16h);
     }
     return oasr_internal_launch_check(be, "quantize_act");
 }

@@ -180,3 +180,15 @@ def test_shared_activation_quantization(gpu_backend, qt, M):
         W.free()
         np.testing.assert_array_equal(a.cpu().numpy(), b.cpu().numpy())
         assert max_abs_rel(a.cpu().numpy(), oo.mul_mat(wq, qt, K, N, x)) <= TIGHT
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K", [(9, 128, 256), (128, 256, 1280), (300, 1280, 1280), (1500, 5120, 1280), (200, 1280, 5120), (77, 200, 512)])
+def test_q4k_tensor_core_gemm_is_bit_exact(gpu_backend, M, N, K):
+    """The tcgen05 Q4_K GEMM forms ggml's per-super-block term exactly and adds
+    the super-blocks in order, so it must equal the oracle bit for bit."""
+    wq = _weights(N, K, ob.Q4_K, 0x0A5A0009 + M)
+    x = oo.synth_normal(0x0A5A000A + N, M * K).reshape(M, K)
+    got = _run(gpu_backend, wq, ob.Q4_K, N, K, x)
+    ref = oo.mul_mat(wq, ob.Q4_K, K, N, x)
+    np.testing.assert_array_equal(got, ref)
