@@ -112,13 +112,31 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
     const int kv1 = min(a.NKV, kv0 + a.kv_per_split);
     const char *kbase = a.k + hk * a.k_nb2 + s * a.k_nb3 + sl * 8 * ES;
     const char *vbase = a.v + hk * a.v_nb2 + s * a.v_nb3 + sl * 8 * ES;
-    for (int p0 = kv0 + warp * PPW; p0 < kv1; p0 += 4 * PPW) {
-        const int p = p0 + grp;
+    // U warp-steps of K/V rows are loaded before any is consumed so that each
+    // lane keeps U x 2 16-byte (f16) loads in flight
+    constexpr int U = 4;
+    constexpr int RW = F16 ? 1 : 2;  // int4 words per lane per row
+    for (int pb = kv0 + warp * PPW; pb < kv1; pb += 4 * PPW * U) {
+        int4 kraw[U][RW], vraw[U][RW];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int p = pb + u * 4 * PPW + grp;
+            if (p < kv1) {
+#pragma unroll
+                for (int r = 0; r < RW; ++r) {
+                    kraw[u][r] = *reinterpret_cast<const int4 *>(kbase + (int64_t)p * a.k_nb1 + 16 * r);
+                    vraw[u][r] = *reinterpret_cast<const int4 *>(vbase + (int64_t)p * a.v_nb1 + 16 * r);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+        const int p = pb + u * 4 * PPW + grp;
         const bool pv = p < kv1;
         float kf[8], vf[8];
         if (pv) {
-            load8<F16>(kbase + (int64_t)p * a.k_nb1, kf);
-            load8<F16>(vbase + (int64_t)p * a.v_nb1, vf);
+            load8<F16>(reinterpret_cast<const char *>(kraw[u]), kf);
+            load8<F16>(reinterpret_cast<const char *>(vraw[u]), vf);
         }
 #pragma unroll
         for (int t = 0; t < QT; ++t) {
@@ -143,6 +161,7 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
 #pragma unroll
             for (int e = 0; e < 8; ++e) acc[t][e] = fmaf(w, vf[e], acc[t][e] * corr);
             mx[t] = mnew;
+        }
         }
     }
 

@@ -37,16 +37,20 @@ constexpr int BM = 128;
 constexpr int BN = 128;
 constexpr int BK = 64;
 constexpr int STAGES = 3;
+constexpr int WSTAGES = 3;       // raw Q4_K super-block ring
 constexpr int TILE = 128 * 128;  // bytes of one 128-row x 128-byte operand tile
+constexpr int WTILE = 128 * 144; // 128 weight rows x one raw super-block (18 KB)
 constexpr int NTHREADS = 448;
 constexpr int OFF_A = 0;
 constexpr int OFF_B = OFF_A + STAGES * TILE;
 constexpr int OFF_AMIN = OFF_B + STAGES * TILE;
 constexpr int OFF_BMIN = OFF_AMIN + 2 * TILE;
-constexpr int OFF_BAR = OFF_BMIN + 2 * TILE;
-constexpr int NBAR = 3 * STAGES + 9;
+constexpr int OFF_W = OFF_BMIN + 2 * TILE;
+constexpr int OFF_BAR = OFF_W + WSTAGES * WTILE;
+constexpr int NBAR = 3 * STAGES + 9 + 2 * WSTAGES;
 constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 }  // namespace q4k
 
 static __device__ __forceinline__ int q4k_byte(const int4 &h, int i) {
@@ -63,9 +67,27 @@ static __device__ __forceinline__ void q4k_scale_min(const int4 &h, int j, int &
     }
 }
 
+// two nibble-sized values -> fp16 pair: v | 0x6400 is the half 1024 + v (v < 1024), minus 1024
+static __device__ __forceinline__ uint32_t u16x2_to_h2(uint32_t v2) {
+    const uint32_t x = v2 | 0x64006400u;
+    const __half2 r = __hsub2(*reinterpret_cast<const __half2 *>(&x), __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400)));
+    return *reinterpret_cast<const uint32_t *>(&r);
+}
+
+// 8 consecutive K elements sc*nibble from 8 qs bytes (words w0, w1), low (sh=0) or high (sh=4) nibbles
+static __device__ __forceinline__ int4 q4k_chunk_f16(uint32_t w0, uint32_t w1, int sh, uint32_t sc) {
+    const uint32_t n0 = (w0 >> sh) & 0x0F0F0F0Fu, n1 = (w1 >> sh) & 0x0F0F0F0Fu;
+    int4 r;
+    r.x = (int)u16x2_to_h2(__byte_perm(n0, 0, 0x4140) * sc);
+    r.y = (int)u16x2_to_h2(__byte_perm(n0, 0, 0x4342) * sc);
+    r.z = (int)u16x2_to_h2(__byte_perm(n1, 0, 0x4140) * sc);
+    r.w = (int)u16x2_to_h2(__byte_perm(n1, 0, 0x4342) * sc);
+    return r;
+}
+
 __global__ void __launch_bounds__(448, 1)
-    mmq_q4k_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const uint8_t *__restrict__ w, int64_t w_ld, int N,
-                      const __half *__restrict__ bs16h, const float *__restrict__ ad, int M, int K,
+    mmq_q4k_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
+                      int N, const __half *__restrict__ bs16h, const float *__restrict__ ad, int M, int K,
                       float *__restrict__ y, int64_t y_ld, int *err) {
     using namespace q4k;
     extern __shared__ uint8_t smem_raw[];
@@ -79,6 +101,8 @@ __global__ void __launch_bounds__(448, 1)
     uint64_t *tmem_full = empty_min + 2;
     uint64_t *tmem_empty = tmem_full + 2;
     uint64_t *done = tmem_empty + 2;
+    uint64_t *full_w = done + 1;
+    uint64_t *empty_w = full_w + WSTAGES;
     uint32_t *tmem_slot = (uint32_t *)(smem + OFF_MISC);
     volatile int *abort_flag = (volatile int *)(smem + OFF_MISC + 4);
 
@@ -98,6 +122,10 @@ __global__ void __launch_bounds__(448, 1)
             mbar_init(&tmem_full[i], 1);
             mbar_init(&tmem_empty[i], 256);
         }
+        for (int i = 0; i < WSTAGES; ++i) {
+            mbar_init(&full_w[i], 1);
+            mbar_init(&empty_w[i], 128 + 256);  // transform + epilogue release a raw super-block
+        }
         mbar_init(done, 1);
         *abort_flag = 0;
         fence_mbar_init();
@@ -110,19 +138,32 @@ __global__ void __launch_bounds__(448, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            int issued = 0;
+            // TMA producer: raw weight super-blocks (ring of WSTAGES) and activation tiles (ring of STAGES)
+            int issued_a = 0, issued_w = 0;
             for (int kc = 0; kc < nkc; ++kc) {
+                const int sb = kc >> 2;
+                if ((kc & 3) == 0) {
+                    const int wb = sb % WSTAGES;
+                    if (!mbar_wait(&empty_w[wb], ((sb / WSTAGES) & 1) ^ 1, abort_flag, err)) break;
+                    mbar_arrive_expect_tx(&full_w[wb], WTILE);
+                    tma_load_2d(smem + OFF_W + wb * WTILE, &tmap_w, &full_w[wb], sb * 144, n0);
+                    issued_w = sb + 1;
+                }
                 const int s = kc % STAGES;
-                const uint32_t ph = (kc / STAGES) & 1;
-                if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, err)) break;
+                if (!mbar_wait(&empty[s], ((kc / STAGES) & 1) ^ 1, abort_flag, err)) break;
                 mbar_arrive_expect_tx(&full_a[s], TILE);
                 tma_load_2d(smem + OFF_A + s * TILE, &tmap_a, &full_a[s], kc * BK, m0);
-                issued = kc + 1;
+                issued_a = kc + 1;
             }
             // no TMA write may still be in flight when the CTA exits
-            for (int kc = max(0, issued - STAGES); kc < issued; ++kc) {
+            for (int kc = max(0, issued_a - STAGES); kc < issued_a; ++kc) {
                 const long long t0 = clock64();
                 while (!mbar_try_wait(&full_a[kc % STAGES], (kc / STAGES) & 1) && clock64() - t0 < (1LL << 31)) {
+                }
+            }
+            for (int sb = max(0, issued_w - WSTAGES); sb < issued_w; ++sb) {
+                const long long t0 = clock64();
+                while (!mbar_try_wait(&full_w[sb % WSTAGES], (sb / WSTAGES) & 1) && clock64() - t0 < (1LL << 31)) {
                 }
             }
         }
@@ -169,39 +210,37 @@ __global__ void __launch_bounds__(448, 1)
     } else if (warp < 6) {
         // ---- weight transform: one weight row (and one activation min row) per thread ----
         const int t = threadIdx.x - 64;
-        const int n = n0 + t, m = m0 + t;
-        const bool nv = n < N, mv = m < M;
-        const uint8_t *wrow = w + (int64_t)(nv ? n : 0) * w_ld;
+        const int m = m0 + t;
+        const bool mv = m < M;
+        // activation 16-wide sums of the next super-block, one super-block ahead
+        int4 nb0 = make_int4(0, 0, 0, 0), nb1 = nb0;
+        if (mv) {
+            const __half *ap = bs16h + (int64_t)m * (K / 16);
+            nb0 = *reinterpret_cast<const int4 *>(ap);
+            nb1 = *reinterpret_cast<const int4 *>(ap + 8);
+        }
         for (int kc = 0; kc < nkc; ++kc) {
-            const int s = kc % STAGES, sb = kc >> 2, c = kc & 3;
-            const uint32_t ph = (kc / STAGES) & 1;
-            if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, err)) break;
-            int4 hdr = make_int4(0, 0, 0, 0), q0 = hdr, q1 = hdr;
-            if (nv) {
-                const uint8_t *bp = wrow + (int64_t)sb * 144;
-                hdr = ldg_stream(bp);
-                q0 = ldg_stream(bp + 16 + 32 * c);
-                q1 = ldg_stream(bp + 32 + 32 * c);
-            }
+            const int s = kc % STAGES, sb = kc >> 2, c = kc & 3, wb = sb % WSTAGES;
+            if (c == 0 && !mbar_wait(&full_w[wb], (sb / WSTAGES) & 1, abort_flag, err)) break;
+            if (!mbar_wait(&empty[s], ((kc / STAGES) & 1) ^ 1, abort_flag, err)) break;
+            const uint8_t *wrow = smem + OFF_W + wb * WTILE + t * 144;  // rows past N are zero-filled by TMA
+            const int4 hdr = *reinterpret_cast<const int4 *>(wrow);
+            const int4 q0 = *reinterpret_cast<const int4 *>(wrow + 16 + 32 * c);
+            const int4 q1 = *reinterpret_cast<const int4 *>(wrow + 32 + 32 * c);
             int sc0, mn0, sc1, mn1;
             q4k_scale_min(hdr, 2 * c, sc0, mn0);
             q4k_scale_min(hdr, 2 * c + 1, sc1, mn1);
-            const uint32_t qw[8] = {(uint32_t)q0.x, (uint32_t)q0.y, (uint32_t)q0.z, (uint32_t)q0.w,
-                                    (uint32_t)q1.x, (uint32_t)q1.y, (uint32_t)q1.z, (uint32_t)q1.w};
             uint8_t *bt = smem + OFF_B + s * TILE;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                // chunk j = K elements 8j..8j+7 of this 64-wide slice:
-                // j < 4: low nibbles of qs bytes 8j..8j+7 (sub-block 2c), else high nibbles (2c+1)
-                const int jj = j & 3, sh = j < 4 ? 0 : 4, sc = j < 4 ? sc0 : sc1;
-                const uint32_t w0 = qw[2 * jj], w1 = qw[2 * jj + 1];
-                __half2 h[4];
-                h[0] = __halves2half2(__int2half_rn(sc * (int)((w0 >> sh) & 15)), __int2half_rn(sc * (int)((w0 >> (8 + sh)) & 15)));
-                h[1] = __halves2half2(__int2half_rn(sc * (int)((w0 >> (16 + sh)) & 15)), __int2half_rn(sc * (int)((w0 >> (24 + sh)) & 15)));
-                h[2] = __halves2half2(__int2half_rn(sc * (int)((w1 >> sh) & 15)), __int2half_rn(sc * (int)((w1 >> (8 + sh)) & 15)));
-                h[3] = __halves2half2(__int2half_rn(sc * (int)((w1 >> (16 + sh)) & 15)), __int2half_rn(sc * (int)((w1 >> (24 + sh)) & 15)));
-                *reinterpret_cast<int4 *>(bt + sw128_off(t, j)) = *reinterpret_cast<int4 *>(h);
-            }
+            // chunk j = K elements 8j..8j+7 of this 64-wide slice: j < 4 low nibbles of
+            // qs bytes 8j..8j+7 (sub-block 2c), j >= 4 high nibbles (sub-block 2c+1)
+            *reinterpret_cast<int4 *>(bt + sw128_off(t, 0)) = q4k_chunk_f16(q0.x, q0.y, 0, sc0);
+            *reinterpret_cast<int4 *>(bt + sw128_off(t, 1)) = q4k_chunk_f16(q0.z, q0.w, 0, sc0);
+            *reinterpret_cast<int4 *>(bt + sw128_off(t, 2)) = q4k_chunk_f16(q1.x, q1.y, 0, sc0);
+            *reinterpret_cast<int4 *>(bt + sw128_off(t, 3)) = q4k_chunk_f16(q1.z, q1.w, 0, sc0);
+            *reinterpret_cast<int4 *>(bt + sw128_off(t, 4)) = q4k_chunk_f16(q0.x, q0.y, 4, sc1);
+            *reinterpret_cast<int4 *>(bt + sw128_off(t, 5)) = q4k_chunk_f16(q0.z, q0.w, 4, sc1);
+            *reinterpret_cast<int4 *>(bt + sw128_off(t, 6)) = q4k_chunk_f16(q1.x, q1.y, 4, sc1);
+            *reinterpret_cast<int4 *>(bt + sw128_off(t, 7)) = q4k_chunk_f16(q1.z, q1.w, 4, sc1);
             if (c == 0) {
                 const int mb = sb & 1;
                 if (!mbar_wait(&empty_min[mb], ((sb >> 1) & 1) ^ 1, abort_flag, err)) break;
@@ -217,20 +256,20 @@ __global__ void __launch_bounds__(448, 1)
                 uint8_t *bm = smem + OFF_BMIN + mb * TILE;
                 *reinterpret_cast<int4 *>(bm + sw128_off(t, 0)) = *reinterpret_cast<int4 *>(&hb[0]);
                 *reinterpret_cast<int4 *>(bm + sw128_off(t, 1)) = *reinterpret_cast<int4 *>(&hb[4]);
-                int4 a0 = make_int4(0, 0, 0, 0), a1 = a0;
-                if (mv) {
-                    const __half *ap = bs16h + (int64_t)m * (K / 16) + sb * 16;
-                    a0 = *reinterpret_cast<const int4 *>(ap);
-                    a1 = *reinterpret_cast<const int4 *>(ap + 8);
-                }
                 uint8_t *am = smem + OFF_AMIN + mb * TILE;
-                *reinterpret_cast<int4 *>(am + sw128_off(t, 0)) = a0;
-                *reinterpret_cast<int4 *>(am + sw128_off(t, 1)) = a1;
+                *reinterpret_cast<int4 *>(am + sw128_off(t, 0)) = nb0;
+                *reinterpret_cast<int4 *>(am + sw128_off(t, 1)) = nb1;
+                if (mv && sb + 1 < nsb) {
+                    const __half *ap = bs16h + (int64_t)m * (K / 16) + (sb + 1) * 16;
+                    nb0 = *reinterpret_cast<const int4 *>(ap);
+                    nb1 = *reinterpret_cast<const int4 *>(ap + 8);
+                }
                 fence_proxy_async_smem();
                 mbar_arrive(&full_min[mb]);
             }
             fence_proxy_async_smem();
             mbar_arrive(&full_b[s]);
+            if (c == 3) mbar_arrive(&empty_w[wb]);
         }
     } else {
         // ---- epilogue ----
@@ -240,11 +279,17 @@ __global__ void __launch_bounds__(448, 1)
         float acc[64];
 #pragma unroll
         for (int i = 0; i < 64; ++i) acc[i] = 0.0f;
+        float da_next = rv ? __ldg(ad + (int64_t)row * nsb) : 0.0f;
         for (int sb = 0; sb < nsb; ++sb) {
-            const int ab = sb & 1;
+            const int ab = sb & 1, wb = sb % WSTAGES;
+            const float da = da_next;
+            if (rv && sb + 1 < nsb) da_next = __ldg(ad + (int64_t)row * nsb + sb + 1);
             if (!mbar_wait(&tmem_full[ab], (sb >> 1) & 1, abort_flag, err)) break;
+            // the raw super-block stays in its slot until this epilogue releases it, so its
+            // phase is still the one to observe (makes the TMA bytes visible to these threads)
+            if (!mbar_wait(&full_w[wb], (sb / WSTAGES) & 1, abort_flag, err)) break;
             tc_fence_after();
-            const float da = rv ? __ldg(ad + (int64_t)row * nsb + sb) : 0.0f;
+            const uint8_t *wsc = smem + OFF_W + wb * WTILE + 64 * hcol * 144;  // d, dmin of each weight row
             const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(ab * 256 + 64 * hcol);
 #pragma unroll
             for (int cb = 0; cb < 4; ++cb) {
@@ -254,8 +299,7 @@ __global__ void __launch_bounds__(448, 1)
                 tmem_ld_wait();
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const int n = n0 + 64 * hcol + 16 * cb + i;
-                    const uint32_t dd = n < N ? __ldg(reinterpret_cast<const uint32_t *>(w + (int64_t)n * w_ld + (int64_t)sb * 144)) : 0u;
+                    const uint32_t dd = *reinterpret_cast<const uint32_t *>(wsc + (16 * cb + i) * 144);
                     const float d = __fmul_rn(h2f((uint16_t)(dd & 0xFFFF)), da);
                     const float dm = __fmul_rn(h2f((uint16_t)(dd >> 16)), da);
                     acc[16 * cb + i] += __fsub_rn(__fmul_rn(d, __uint_as_float(ri[i])), __fmul_rn(dm, __uint_as_float(rm[i])));
@@ -263,12 +307,18 @@ __global__ void __launch_bounds__(448, 1)
             }
             tc_fence_before();
             mbar_arrive(&tmem_empty[ab]);
+            mbar_arrive(&empty_w[wb]);
         }
         if (rv) {
             float *yr = y + (int64_t)row * y_ld + n0 + 64 * hcol;
+            if (n0 + 64 * hcol + 64 <= N && (((uintptr_t)yr) & 15) == 0) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i)
-                if (n0 + 64 * hcol + i < N) yr[i] = acc[i];
+                for (int i = 0; i < 64; i += 4) *reinterpret_cast<float4 *>(yr + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 64; ++i)
+                    if (n0 + 64 * hcol + i < N) yr[i] = acc[i];
+            }
         }
     }
     tc_fence_before();
@@ -292,29 +342,40 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-static int launch_q4k_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int64_t M, int K,
-                         float *y, int64_t y_ld) {
+static int encode_2d(oasr_backend *be, CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner,
+                     uint64_t rows, uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw) {
     auto enc = tensor_map_encoder();
     if (!enc) return oasr_internal_fail(be, OASR_STATUS_FAILED, "cuTensorMapEncodeTiled unavailable");
-    CUtensorMap map;
-    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
-    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-    const cuuint32_t box[2] = {64, 128};
+    const cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)a.qs16, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = enc(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return oasr_internal_fail(be, OASR_STATUS_FAILED, "cuTensorMapEncodeTiled failed");
+    return OASR_STATUS_SUCCESS;
+}
+
+static int launch_q4k_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int64_t M, int K,
+                         float *y, int64_t y_ld) {
+    const int64_t N = w->ne[1];
+    CUtensorMap map_a, map_w;
+    // activations: fp16 [M][K], 128 rows x 64 elements (128 B) per box, 128B swizzle
+    int st = encode_2d(be, &map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.qs16, K, M, (uint64_t)K * 2, 64, 128,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    // raw Q4_K rows: bytes [N][K/256*144], 128 rows x one 144-byte super-block per box
+    st = encode_2d(be, &map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->qs + slice * N * w->qs_row_bytes, w->qs_row_bytes, N,
+                   w->qs_row_bytes, 144, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
     static bool attr_set = false;
     if (!attr_set) {
         cudaFuncSetAttribute(mmq_q4k_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, q4k::SMEM_BYTES);
         attr_set = true;
     }
-    const int64_t N = w->ne[1];
     dim3 grid((unsigned)((N + q4k::BN - 1) / q4k::BN), (unsigned)((M + q4k::BM - 1) / q4k::BM));
-    mmq_q4k_tc_kernel<<<grid, q4k::NTHREADS, q4k::SMEM_BYTES, be->stream>>>(
-        map, w->qs + slice * N * w->qs_row_bytes, w->qs_row_bytes, (int)N, a.bs16h, a.d, (int)M, K, y, y_ld,
-        be->err_word);
+    mmq_q4k_tc_kernel<<<grid, q4k::NTHREADS, q4k::SMEM_BYTES, be->stream>>>(map_a, map_w, (int)N, a.bs16h, a.d,
+                                                                            (int)M, K, y, y_ld, be->err_word);
     return oasr_internal_launch_check(be, "mmq_q4k_tc");
 }
 

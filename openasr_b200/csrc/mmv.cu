@@ -46,13 +46,17 @@ __global__ void __launch_bounds__(128, 3)
 #pragma unroll
     for (int i = 0; i < RP * M; ++i) acc[i] = 0.0f;
 
-    for (int it = j; it < nitems; it += lpr) {
+    // every lane runs the same trip count (shuffles below use the full warp);
+    // items past the end of the row contribute zero
+    const int nit_pad = (nitems + lpr - 1) & ~(lpr - 1);
+    for (int it = j; it < nit_pad; it += lpr) {
+        const bool itv = it < nitems;
         int4 w0[RP], w1[RP];
         float dw[RP];
 #pragma unroll
         for (int p = 0; p < RP; ++p) {
             const int64_t row = row0 + (int64_t)p * rpp;
-            if (row < N) {
+            if (itv && row < N) {
                 const uint8_t *wp = wqs + row * qs_ld + (int64_t)it * QB;
                 w0[p] = ldg_stream(wp);
                 w1[p] = Q4 ? make_int4(0, 0, 0, 0) : ldg_stream(wp + 16);
@@ -64,10 +68,11 @@ __global__ void __launch_bounds__(128, 3)
         }
 #pragma unroll
         for (int m = 0; m < M; ++m) {
-            const int8_t *ap = aqs + (int64_t)m * K + (int64_t)it * 32;
+            const int itc = itv ? it : 0;
+            const int8_t *ap = aqs + (int64_t)m * K + (int64_t)itc * 32;
             const int4 a0 = __ldg(reinterpret_cast<const int4 *>(ap));
             const int4 a1 = __ldg(reinterpret_cast<const int4 *>(ap + 16));
-            const float da = __ldg(ad + (int64_t)m * nb + it);
+            const float da = __ldg(ad + (int64_t)m * nb + itc);
 #pragma unroll
             for (int p = 0; p < RP; ++p) {
                 int s = 0;
@@ -139,13 +144,15 @@ __global__ void __launch_bounds__(128, 3)
 #pragma unroll
     for (int i = 0; i < RP * M; ++i) acc[i] = 0.0f;
 
-    for (int it = j; it < nitems; it += lpr) {
-        const int sb = it >> 2, c = it & 3;
+    const int nit_pad = (nitems + lpr - 1) & ~(lpr - 1);
+    for (int it = j; it < nit_pad; it += lpr) {
+        const bool itv = it < nitems;
+        const int sb = itv ? it >> 2 : 0, c = it & 3;
         int4 hdr[RP], q0[RP], q1[RP];
 #pragma unroll
         for (int p = 0; p < RP; ++p) {
             const int64_t row = row0 + (int64_t)p * rpp;
-            if (row < N) {
+            if (itv && row < N) {
                 const uint8_t *wp = w + row * w_ld + (int64_t)sb * 144;
                 hdr[p] = ldg_stream(wp);
                 q0[p] = ldg_stream(wp + 16 + 32 * c);
@@ -256,42 +263,69 @@ __global__ void __launch_bounds__(128)
 }
 
 // ---- launchers ------------------------------------------------------------------------
-static int pick_lpr_log2(int nitems, int min_log2) {
-    int l = 5;
-    while (l > min_log2 && (nitems % (1 << l)) != 0) --l;
+// Lanes per row: cover a row in as few passes as possible while keeping most
+// lanes busy (a power of two; 32 once the row has >= 24 items).
+static int pick_lpr_log2(int nitems) {
+    if (nitems >= 24) return 5;
+    int l = 0;
+    while ((1 << l) < nitems) ++l;
     return l;
 }
 
-template <int M>
-static void launch_q8(const oasr_weight *w, int64_t slice, const ActPlanes &a, int K, float *y, int64_t y_ld,
-                      cudaStream_t st, bool q4) {
+// Rows per warp pass: the largest RP in {4, 2, 1} that still gives >= 2 CTAs per SM.
+static int pick_rp(int64_t N, int lg, int sm_count) {
+    const int64_t rpp = 32 >> lg;
+    for (int rp = 4; rp > 1; rp >>= 1)
+        if ((N + 4 * rpp * rp - 1) / (4 * rpp * rp) >= 2LL * sm_count) return rp;
+    return 1;
+}
+
+template <int M, int RP>
+static void launch_q8_rp(const oasr_weight *w, int64_t slice, const ActPlanes &a, int K, float *y, int64_t y_ld,
+                         cudaStream_t st, bool q4, int lg) {
     const int64_t N = w->ne[1];
-    const int nitems = K / 32;
-    const int lg = pick_lpr_log2(nitems, 0);
-    constexpr int RP = 4;
     const int rows_per_cta = 4 * (32 >> lg) * RP;
     const unsigned grid = (unsigned)((N + rows_per_cta - 1) / rows_per_cta);
     const uint8_t *wqs = w->qs + slice * N * w->qs_row_bytes;
     const uint16_t *wd = w->d + slice * N * w->d_row_elems;
     if (q4)
-        mmv_q8_kernel<M, RP, true><<<grid, 128, 0, st>>>(wqs, wd, w->qs_row_bytes, w->d_row_elems, N, nitems, lg,
+        mmv_q8_kernel<M, RP, true><<<grid, 128, 0, st>>>(wqs, wd, w->qs_row_bytes, w->d_row_elems, N, K / 32, lg,
                                                          a.qs, a.d, K, y, y_ld);
     else
-        mmv_q8_kernel<M, RP, false><<<grid, 128, 0, st>>>(wqs, wd, w->qs_row_bytes, w->d_row_elems, N, nitems, lg,
+        mmv_q8_kernel<M, RP, false><<<grid, 128, 0, st>>>(wqs, wd, w->qs_row_bytes, w->d_row_elems, N, K / 32, lg,
                                                           a.qs, a.d, K, y, y_ld);
 }
 
 template <int M>
-static void launch_q4k(const oasr_weight *w, int64_t slice, const ActPlanes &a, int K, float *y, int64_t y_ld,
-                       cudaStream_t st) {
+static void launch_q8(const oasr_weight *w, int64_t slice, const ActPlanes &a, int K, float *y, int64_t y_ld,
+                      cudaStream_t st, bool q4, int sm_count) {
+    const int lg = pick_lpr_log2(K / 32);
+    switch (pick_rp(w->ne[1], lg, sm_count)) {
+    case 4: launch_q8_rp<M, 4>(w, slice, a, K, y, y_ld, st, q4, lg); break;
+    case 2: launch_q8_rp<M, 2>(w, slice, a, K, y, y_ld, st, q4, lg); break;
+    default: launch_q8_rp<M, 1>(w, slice, a, K, y, y_ld, st, q4, lg); break;
+    }
+}
+
+template <int M, int RP>
+static void launch_q4k_rp(const oasr_weight *w, int64_t slice, const ActPlanes &a, int K, float *y, int64_t y_ld,
+                          cudaStream_t st, int lg) {
     const int64_t N = w->ne[1];
-    const int nitems = K / 64;
-    const int lg = pick_lpr_log2(nitems, 2);  // nitems is a multiple of 4
-    constexpr int RP = 4;
     const int rows_per_cta = 4 * (32 >> lg) * RP;
     const unsigned grid = (unsigned)((N + rows_per_cta - 1) / rows_per_cta);
-    mmv_q4k_kernel<M, RP><<<grid, 128, 0, st>>>(w->qs + slice * N * w->qs_row_bytes, w->qs_row_bytes, N, nitems, lg,
+    mmv_q4k_kernel<M, RP><<<grid, 128, 0, st>>>(w->qs + slice * N * w->qs_row_bytes, w->qs_row_bytes, N, K / 64, lg,
                                                 a.qs, a.d, a.bs16, K, y, y_ld);
+}
+
+template <int M>
+static void launch_q4k(const oasr_weight *w, int64_t slice, const ActPlanes &a, int K, float *y, int64_t y_ld,
+                       cudaStream_t st, int sm_count) {
+    const int lg = std::max(2, pick_lpr_log2(K / 64));  // the 4 items of a super-block share aligned lanes
+    switch (pick_rp(w->ne[1], lg, sm_count)) {
+    case 4: launch_q4k_rp<M, 4>(w, slice, a, K, y, y_ld, st, lg); break;
+    case 2: launch_q4k_rp<M, 2>(w, slice, a, K, y, y_ld, st, lg); break;
+    default: launch_q4k_rp<M, 1>(w, slice, a, K, y, y_ld, st, lg); break;
+    }
 }
 
 int launch_mmv_quant(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int M, int K,
@@ -299,26 +333,26 @@ int launch_mmv_quant(oasr_backend *be, const oasr_weight *w, int64_t slice, cons
     cudaStream_t st = be->stream;
     if (w->type == OASR_TYPE_Q4_K) {
         switch (M) {
-        case 1: launch_q4k<1>(w, slice, a, K, y, y_ld, st); break;
-        case 2: launch_q4k<2>(w, slice, a, K, y, y_ld, st); break;
-        case 3: launch_q4k<3>(w, slice, a, K, y, y_ld, st); break;
-        case 4: launch_q4k<4>(w, slice, a, K, y, y_ld, st); break;
-        case 5: launch_q4k<5>(w, slice, a, K, y, y_ld, st); break;
-        case 6: launch_q4k<6>(w, slice, a, K, y, y_ld, st); break;
-        case 7: launch_q4k<7>(w, slice, a, K, y, y_ld, st); break;
-        default: launch_q4k<8>(w, slice, a, K, y, y_ld, st); break;
+        case 1: launch_q4k<1>(w, slice, a, K, y, y_ld, st, be->sm_count); break;
+        case 2: launch_q4k<2>(w, slice, a, K, y, y_ld, st, be->sm_count); break;
+        case 3: launch_q4k<3>(w, slice, a, K, y, y_ld, st, be->sm_count); break;
+        case 4: launch_q4k<4>(w, slice, a, K, y, y_ld, st, be->sm_count); break;
+        case 5: launch_q4k<5>(w, slice, a, K, y, y_ld, st, be->sm_count); break;
+        case 6: launch_q4k<6>(w, slice, a, K, y, y_ld, st, be->sm_count); break;
+        case 7: launch_q4k<7>(w, slice, a, K, y, y_ld, st, be->sm_count); break;
+        default: launch_q4k<8>(w, slice, a, K, y, y_ld, st, be->sm_count); break;
         }
     } else {
         const bool q4 = w->type == OASR_TYPE_Q4_0;
         switch (M) {
-        case 1: launch_q8<1>(w, slice, a, K, y, y_ld, st, q4); break;
-        case 2: launch_q8<2>(w, slice, a, K, y, y_ld, st, q4); break;
-        case 3: launch_q8<3>(w, slice, a, K, y, y_ld, st, q4); break;
-        case 4: launch_q8<4>(w, slice, a, K, y, y_ld, st, q4); break;
-        case 5: launch_q8<5>(w, slice, a, K, y, y_ld, st, q4); break;
-        case 6: launch_q8<6>(w, slice, a, K, y, y_ld, st, q4); break;
-        case 7: launch_q8<7>(w, slice, a, K, y, y_ld, st, q4); break;
-        default: launch_q8<8>(w, slice, a, K, y, y_ld, st, q4); break;
+        case 1: launch_q8<1>(w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
+        case 2: launch_q8<2>(w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
+        case 3: launch_q8<3>(w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
+        case 4: launch_q8<4>(w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
+        case 5: launch_q8<5>(w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
+        case 6: launch_q8<6>(w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
+        case 7: launch_q8<7>(w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
+        default: launch_q8<8>(w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
         }
     }
     return oasr_internal_launch_check(be, "mmv_quant");
