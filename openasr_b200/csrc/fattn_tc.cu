@@ -1,0 +1,342 @@
+// fattn_tc.cu -- K4: tiled flash attention on the tcgen05 tensor cores for the
+// encoder's self-attention (n_q = n_kv = 1500, head_dim 64, no mask).
+//
+// Semantics (cpu_graph.rs:4144-4220; encoder call site ggml_executor.rs:1650-1695):
+//   O[:, h, i, s] = softmax(scale * Q[:, i, h, s] . K[:, :, h/G, s]) V
+// Q, K and V are rounded to fp16 (the operand type of the tensor-core MMA;
+// ggml's CUDA backend makes the same conversion for f32 K/V), S = Q K^T and
+// O = P V accumulate in f32 in TMEM, P is rounded to fp16, and the softmax runs
+// in f32 with online rescaling.
+//
+// A pre-pass writes Q and K as fp16 [S*H][n][64] rows and V transposed as
+// fp16 [S*H_kv][64][n_pad] so that every MMA operand is a K-major tile in the
+// 128-byte swizzle layout fetched by TMA:
+//   MMA1  S(128 q x 128 keys)  = Q tile (128 x 64)      . K tile (128 keys x 64)^T
+//   MMA2  Ot(128 q x 64 dims)  = P tile (128 x 128 keys) . Vt tile (64 dims x 128 keys)^T
+// CTA = one 128-query tile of one head, 6 warps:
+//   warps 0-3  softmax (one query row per thread) + output accumulation in registers
+//   warp 4     TMA producer (Q once, then K / Vt tiles through a 2-slot ring)
+//   warp 5     TMEM allocator (256 columns) + single-thread MMA issuer
+// Two CTAs share an SM (112 KB shared memory, 256 TMEM columns each), so one
+// CTA's softmax overlaps the other's MMAs.  Every mbarrier wait is bounded.
+#include <cudaTypedefs.h>
+
+#include "kernels.cuh"
+#include "tc_common.cuh"
+
+namespace oasr {
+
+namespace fa4 {
+constexpr int BQ = 128, BKV = 128, D = 64;
+constexpr int QTILE = BQ * 128;              // 16 KB
+constexpr int KTILE = BKV * 128;             // 16 KB
+constexpr int VTILE = 64 * 128;              // 8 KB: 64 dims x 64 keys
+constexpr int SLOT = KTILE + 2 * VTILE;      // K tile + two Vt half-tiles
+constexpr int PTILE = BQ * 128;              // 16 KB: 128 q x 64 keys
+constexpr int OFF_Q = 0;
+constexpr int OFF_KV = OFF_Q + QTILE;
+constexpr int OFF_P = OFF_KV + 2 * SLOT;
+constexpr int OFF_BAR = OFF_P + 2 * PTILE;
+constexpr int NBAR = 10;
+constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+constexpr int SMEM_BYTES = OFF_MISC + 16;  // two CTAs per SM: <= (228 KB - 2 x 1 KB reserved) / 2
+static_assert(SMEM_BYTES <= 115712, "two CTAs per SM");
+constexpr int NTHREADS = 192;
+}  // namespace fa4
+
+// ---- pre-pass: q,k -> fp16 rows [S*H][n][64]; v -> fp16 [S*Hkv][64][n_pad] -------------
+template <bool F16IN>
+__global__ void fa_prep_kernel(const char *src, int64_t nb1, int64_t nb2, int64_t nb3, int n, int H, int S,
+                               __half *dst, bool transpose, int n_pad) {
+    const int64_t total = (int64_t)S * H * n * 64;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int d = (int)(i & 63);
+        const int64_t r = i >> 6;
+        const int p = (int)(r % n);
+        const int64_t hs = r / n;
+        const int h = (int)(hs % H), s = (int)(hs / H);
+        const char *e = src + p * nb1 + h * nb2 + s * nb3;
+        const float v = F16IN ? __half2float(reinterpret_cast<const __half *>(e)[d]) : reinterpret_cast<const float *>(e)[d];
+        if (transpose) dst[(hs * 64 + d) * n_pad + p] = __float2half_rn(v);
+        else dst[i] = __float2half_rn(v);
+    }
+}
+
+__global__ void fa_zero_pad_kernel(__half *vt, int64_t rows, int n, int n_pad) {
+    const int w = n_pad - n;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * w; i += (int64_t)gridDim.x * blockDim.x)
+        vt[(i / w) * n_pad + n + (i % w)] = __float2half_rn(0.0f);
+}
+
+__global__ void __launch_bounds__(192, 2)
+    fattn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_vt, int NQ, int NKV, int H, int HKV, float scale_log2,
+                    char *dst, int64_t d_nb1, int64_t d_nb2, int64_t d_nb3, int *err) {
+    using namespace fa4;
+    extern __shared__ __align__(1024) uint8_t smem_fa[];
+    uint8_t *smem = smem_fa;
+    // the 128-byte swizzle tiles need a 1024-byte aligned base; refuse (no waits, no TMEM) otherwise
+    if (smem_u32(smem) & 1023u) {
+        if (threadIdx.x == 0) atomicOr(err, ERR_BAD_SHAPE);
+        return;
+    }
+    uint64_t *bars = (uint64_t *)(smem + OFF_BAR);
+    uint64_t *q_full = bars + 0;
+    uint64_t *kv_full = bars + 1;   // [2]
+    uint64_t *kv_empty = bars + 3;  // [2]
+    uint64_t *s_full = bars + 5;
+    uint64_t *p_full = bars + 6;
+    uint64_t *o_full = bars + 7;
+    uint64_t *done = bars + 8;
+    uint32_t *tmem_slot = (uint32_t *)(smem + OFF_MISC);
+    volatile int *abort_flag = (volatile int *)(smem + OFF_MISC + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int qt = blockIdx.x;       // query tile
+    const int hs = blockIdx.y;       // s * H + h
+    const int h = hs % H, s = hs / H;
+    const int G = H / HKV;
+    const int hks = s * HKV + h / G;  // kv row block
+    const int q0 = qt * BQ;
+    const int ntiles = (NKV + BKV - 1) / BKV;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&kv_full[i], 1);
+            mbar_init(&kv_empty[i], 1);
+        }
+        mbar_init(s_full, 1);
+        mbar_init(p_full, 128);
+        mbar_init(o_full, 1);
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 5) tmem_alloc(tmem_slot, 256);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;  // S: cols [0,128), Ot: cols [128,192)
+
+    if (warp == 4) {
+        if (lane == 0) {
+            mbar_arrive_expect_tx(q_full, QTILE);
+            tma_load_2d(smem + OFF_Q, &tm_q, q_full, 0, hs * NQ + q0);
+            int issued = 0;
+            for (int j = 0; j < ntiles; ++j) {
+                const int b = j & 1;
+                if (!mbar_wait(&kv_empty[b], ((j >> 1) & 1) ^ 1, abort_flag, err)) break;
+                uint8_t *slot = smem + OFF_KV + b * SLOT;
+                mbar_arrive_expect_tx(&kv_full[b], SLOT);
+                tma_load_2d(slot, &tm_k, &kv_full[b], 0, hks * NKV + j * BKV);
+                tma_load_2d(slot + KTILE, &tm_vt, &kv_full[b], j * BKV, hks * 64);
+                tma_load_2d(slot + KTILE + VTILE, &tm_vt, &kv_full[b], j * BKV + 64, hks * 64);
+                issued = j + 1;
+            }
+            for (int j = max(0, issued - 2); j < issued; ++j) {
+                const long long t0 = clock64();
+                while (!mbar_try_wait(&kv_full[j & 1], (j >> 1) & 1) && clock64() - t0 < (1LL << 31)) {
+                }
+            }
+            const long long t0 = clock64();
+            while (!mbar_try_wait(q_full, 0) && clock64() - t0 < (1LL << 31)) {
+            }
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            constexpr uint32_t id1 = idesc_f16_f32(BQ, BKV);
+            constexpr uint32_t id2 = idesc_f16_f32(BQ, D);
+            const uint32_t t_s = tmem, t_o = tmem + 128;
+            bool ok = mbar_wait(q_full, 0, abort_flag, err);
+            const uint64_t dq = sw128_desc(smem_u32(smem + OFF_Q));
+            for (int j = 0; j < ntiles && ok; ++j) {
+                const int b = j & 1;
+                uint8_t *slot = smem + OFF_KV + b * SLOT;
+                if (!mbar_wait(&kv_full[b], (j >> 1) & 1, abort_flag, err)) break;
+                // S may be overwritten once the softmax of tile j-1 has read it (p_full of j-1)
+                if (j > 0 && !mbar_wait(p_full, (j - 1) & 1, abort_flag, err)) break;
+                tc_fence_after();
+                const uint64_t dk = sw128_desc(smem_u32(slot));
+#pragma unroll
+                for (int k = 0; k < 4; ++k) umma_f16(t_s, dq + 2 * k, dk + 2 * k, id1, k != 0);
+                umma_commit(s_full);
+                // O_tile = P . Vt^T once the softmax has written P for this tile
+                if (!mbar_wait(p_full, j & 1, abort_flag, err)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const uint64_t dp = sw128_desc(smem_u32(smem + OFF_P + (k >> 2) * PTILE)) + 2 * (k & 3);
+                    const uint64_t dv = sw128_desc(smem_u32(slot + KTILE + (k >> 2) * VTILE)) + 2 * (k & 3);
+                    umma_f16(t_o, dp, dv, id2, k != 0);
+                }
+                umma_commit(&kv_empty[b]);
+                umma_commit(o_full);
+            }
+            umma_commit(done);
+            const long long t0 = clock64();
+            while (!mbar_try_wait(done, 0) && clock64() - t0 < (1LL << 31)) {
+            }
+        }
+    } else {
+        // ---- softmax warpgroup: thread = query row q0 + 32*warp + lane ----
+        const int r = 32 * warp + lane;
+        const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
+        float m = -INFINITY, l = 0.0f;
+        float o[64];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) o[i] = 0.0f;
+        for (int j = 0; j < ntiles; ++j) {
+            if (!mbar_wait(s_full, j & 1, abort_flag, err)) break;
+            tc_fence_after();
+            const int nvalid = min(BKV, NKV - j * BKV);
+            // pass 1: row max of this tile
+            float tmax = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                uint32_t v[16];
+                tmem_ld16(trow + 16 * c, v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    if (16 * c + i < nvalid) tmax = fmaxf(tmax, __uint_as_float(v[i]) * scale_log2);
+            }
+            const float mnew = fmaxf(m, tmax);
+            const float alpha = exp2f(m - mnew);  // m = -inf on the first tile -> 0
+            // pass 2: p = 2^(s*scale*log2e - mnew), row sum, P (fp16) into the swizzled A tiles
+            float tsum = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                uint32_t v[16];
+                tmem_ld16(trow + 16 * c, v);
+                tmem_ld_wait();
+                uint32_t pk[8];
+#pragma unroll
+                for (int i = 0; i < 16; i += 2) {
+                    const float p0 = 16 * c + i < nvalid ? exp2f(__uint_as_float(v[i]) * scale_log2 - mnew) : 0.0f;
+                    const float p1 = 16 * c + i + 1 < nvalid ? exp2f(__uint_as_float(v[i + 1]) * scale_log2 - mnew) : 0.0f;
+                    tsum += p0 + p1;
+                    const __half2 hp = __floats2half2_rn(p0, p1);
+                    pk[i / 2] = *reinterpret_cast<const uint32_t *>(&hp);
+                }
+                // keys 16c..16c+15 = two 16-byte chunks of the 64-key tile c/4
+                uint8_t *pt = smem + OFF_P + (c >> 2) * PTILE;
+                const int ch = (c & 3) * 2;
+                *reinterpret_cast<int4 *>(pt + sw128_off(r, ch)) = make_int4(pk[0], pk[1], pk[2], pk[3]);
+                *reinterpret_cast<int4 *>(pt + sw128_off(r, ch + 1)) = make_int4(pk[4], pk[5], pk[6], pk[7]);
+            }
+            l = l * alpha + tsum;
+            m = mnew;
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(p_full);
+            // O = alpha * O + P V (tile)
+            if (!mbar_wait(o_full, j & 1, abort_flag, err)) break;
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t v[16];
+                tmem_ld16(trow + 128 + 16 * c, v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) o[16 * c + i] = fmaf(o[16 * c + i], alpha, __uint_as_float(v[i]));
+            }
+            tc_fence_before();
+        }
+        const int qi = q0 + r;
+        if (qi < NQ) {
+            const float inv = l == 0.0f ? 0.0f : 1.0f / l;
+            float *out = reinterpret_cast<float *>(dst + h * d_nb1 + qi * d_nb2 + s * d_nb3);
+#pragma unroll
+            for (int i = 0; i < 64; i += 4)
+                *reinterpret_cast<float4 *>(out + i) = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 256);
+    }
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 fa_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    }
+    return fn;
+}
+
+static bool encode_f16_2d(CUtensorMap *map, const void *base, uint64_t inner, uint64_t rows, uint32_t box_inner,
+                          uint32_t box_rows) {
+    auto enc = fa_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)inner * 2};
+    const cuuint32_t box[2] = {box_inner, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool flash_attn_tc_eligible(const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *mask,
+                            const oasr_tensor *dst) {
+    return q->ne[0] == 64 && q->ne[1] >= 64 && k->ne[1] >= 64 && mask == nullptr && dst->nb[1] % 16 == 0 &&
+           dst->nb[2] % 16 == 0 && dst->nb[3] % 16 == 0 && ((uintptr_t)dst->data & 15) == 0;
+}
+
+int launch_flash_attn_tc(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
+                         float scale, oasr_tensor *dst) {
+    const int NQ = (int)q->ne[1], H = (int)q->ne[2], S = (int)q->ne[3];
+    const int NKV = (int)k->ne[1], HKV = (int)k->ne[2];
+    const int n_pad = (NKV + 7) & ~7;
+    const size_t q_bytes = align256((size_t)S * H * NQ * 64 * 2);
+    const size_t k_bytes = align256((size_t)S * HKV * NKV * 64 * 2);
+    const size_t v_bytes = align256((size_t)S * HKV * 64 * n_pad * 2);
+    int st = 0;
+    uint8_t *scr = (uint8_t *)oasr_internal_scratch(be, q_bytes + k_bytes + v_bytes, &st);
+    if (st) return st;
+    __half *q16 = (__half *)scr, *k16 = (__half *)(scr + q_bytes), *vt16 = (__half *)(scr + q_bytes + k_bytes);
+    const bool f16k = k->type == OASR_TYPE_F16;
+    const int blocks = be->sm_count * 8;
+    fa_prep_kernel<false><<<blocks, 256, 0, be->stream>>>((const char *)q->data, q->nb[1], q->nb[2], q->nb[3], NQ, H, S,
+                                                          q16, false, 0);
+    if (f16k) {
+        fa_prep_kernel<true><<<blocks, 256, 0, be->stream>>>((const char *)k->data, k->nb[1], k->nb[2], k->nb[3], NKV,
+                                                             HKV, S, k16, false, 0);
+        fa_prep_kernel<true><<<blocks, 256, 0, be->stream>>>((const char *)v->data, v->nb[1], v->nb[2], v->nb[3], NKV,
+                                                             HKV, S, vt16, true, n_pad);
+    } else {
+        fa_prep_kernel<false><<<blocks, 256, 0, be->stream>>>((const char *)k->data, k->nb[1], k->nb[2], k->nb[3], NKV,
+                                                              HKV, S, k16, false, 0);
+        fa_prep_kernel<false><<<blocks, 256, 0, be->stream>>>((const char *)v->data, v->nb[1], v->nb[2], v->nb[3], NKV,
+                                                              HKV, S, vt16, true, n_pad);
+    }
+    if (n_pad > NKV) fa_zero_pad_kernel<<<64, 256, 0, be->stream>>>(vt16, (int64_t)S * HKV * 64, NKV, n_pad);
+    st = oasr_internal_launch_check(be, "fa_prep");
+    if (st) return st;
+    CUtensorMap mq, mk, mv;
+    if (!encode_f16_2d(&mq, q16, 64, (uint64_t)S * H * NQ, 64, 128) ||
+        !encode_f16_2d(&mk, k16, 64, (uint64_t)S * HKV * NKV, 64, 128) ||
+        !encode_f16_2d(&mv, vt16, (uint64_t)n_pad, (uint64_t)S * HKV * 64, 64, 64))
+        return oasr_internal_fail(be, OASR_STATUS_FAILED, "flash_attn_tc: tensor map encoding failed");
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(fattn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa4::SMEM_BYTES);
+        attr_set = true;
+    }
+    dim3 grid((unsigned)((NQ + fa4::BQ - 1) / fa4::BQ), (unsigned)(S * H));
+    const float scale_log2 = scale * 1.4426950408889634f;
+    fattn_tc_kernel<<<grid, fa4::NTHREADS, fa4::SMEM_BYTES, be->stream>>>(mq, mk, mv, NQ, NKV, H, HKV, scale_log2,
+                                                                         (char *)dst->data, dst->nb[1], dst->nb[2],
+                                                                         dst->nb[3], be->err_word);
+    return oasr_internal_launch_check(be, "fattn_tc");
+}
+
+}  // namespace oasr

@@ -78,6 +78,10 @@ int launch_mmq(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActP
                float *y, int64_t y_ld);
 
 // attention
+bool flash_attn_tc_eligible(const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *mask,
+                            const oasr_tensor *dst);
+int launch_flash_attn_tc(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
+                         float scale, oasr_tensor *dst);
 int launch_flash_attn(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
                       const oasr_tensor *mask, float scale, oasr_tensor *dst);
 

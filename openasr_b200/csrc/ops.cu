@@ -229,6 +229,7 @@ int oasr_b200_flash_attn_ext(oasr_backend *be, const oasr_tensor *q, const oasr_
                                                       D * 4, be->stream));
         return OASR_STATUS_SUCCESS;
     }
+    if (flash_attn_tc_eligible(q, k, mask, dst)) return launch_flash_attn_tc(be, q, k, v, scale, dst);
     return launch_flash_attn(be, q, k, v, mask, scale, dst);
 }
 

@@ -145,3 +145,17 @@ def test_flash_attn_rejects_bad_shapes(gpu_backend):
     out = torch.zeros((1, 1, 3, 64), device="cuda")
     with pytest.raises(ob.backend.UnsupportedInputs):
         gpu_backend.flash_attn_ext(q, k, k, None, 1.0, out)  # 3 q heads over 2 kv heads
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("S,H,HKV,NQ,NKV", [(1, 20, 20, 1500, 1500), (2, 4, 4, 200, 300), (1, 8, 2, 130, 1000), (3, 2, 1, 64, 64)])
+def test_tensor_core_flash_attention_shapes(gpu_backend, S, H, HKV, NQ, NKV):
+    """K4 (tcgen05) path: n_q >= 64, head_dim 64, no mask; ragged tile edges, batch, GQA."""
+    rng = np.random.default_rng(NQ * 7 + NKV)
+    q = rng.normal(0, 1, (S, H, NQ, 64)).astype(np.float32)
+    k = rng.normal(0, 1, (S, HKV, NKV, 64)).astype(np.float32)
+    v = rng.normal(0, 1, (S, HKV, NKV, 64)).astype(np.float32)
+    got = _fa(gpu_backend, q, k, v, None, 0.125)
+    ref = oo.flash_attn_ext(q, k, v, None, 0.125, oo.FA_F32)
+    err = max_abs_rel(got, ref)
+    assert err <= TOL, err
