@@ -191,6 +191,61 @@ int oasr_b200_set_rows(oasr_backend *be, oasr_tensor *dst, const oasr_tensor *sr
  * maximal; out I32 [rows]. */
 int oasr_b200_argmax_first(oasr_backend *be, const oasr_tensor *logits, oasr_tensor *out);
 
+/* ---- model drivers ------------------------------------------------------------------
+ * The graphs openasr-core builds around the hot ops (layer map L2/L3), restated
+ * natively so a whole encoder pass or decoder step runs on this device without
+ * a host round trip per node.  Weights arrive as named host tensors in the
+ * pack's ggml layouts (whisper.cpp / OpenAI tensor names). */
+typedef struct oasr_named_tensor {
+    const char *name;
+    int32_t type;   /* enum oasr_type */
+    int32_t _pad;
+    int64_t ne[4];
+    const void *data; /* host */
+    uint64_t bytes;
+} oasr_named_tensor;
+
+typedef struct oasr_whisper_config {
+    int32_t n_mels;        /* 80 | 128 */
+    int32_t d_model;       /* n_heads * 64 */
+    int32_t n_heads;
+    int32_t n_enc_layers, n_dec_layers;
+    int32_t n_vocab;
+    int32_t n_audio_ctx;   /* 1500 encoder frames (30 s) */
+    int32_t n_text_ctx;    /* 448 decoder positions */
+    int32_t max_batch;     /* sequences decoded in lockstep, <= 8 (MAX_BATCH_LIMIT, batched_decode.rs:53) */
+} oasr_whisper_config;
+
+typedef struct oasr_whisper oasr_whisper;
+
+/* Resident Whisper model (replaces the resident-weight session built by
+ * models/whisper/ggml_executor.rs:3024-3137 + ggml_decoder_graph.rs:1777-1866). */
+int oasr_b200_whisper_load(oasr_backend *be, const oasr_whisper_config *cfg, const oasr_named_tensor *tensors,
+                           int32_t n_tensors, oasr_whisper **out);
+int oasr_b200_whisper_free(oasr_whisper *m);
+/* Log-mel frontend (whisper/mel.rs) of n_utts host PCM clips (16 kHz, concatenated,
+ * n_samples[i] each; padded/trimmed to 30 s); mel_out (host, optional) gets
+ * [n_utts][n_mels][3000]. */
+int oasr_b200_whisper_mel(oasr_whisper *m, const float *pcm, const int64_t *n_samples, int32_t n_utts, float *mel_out);
+/* Conv prelude + encoder + cross-attention K/V for n_utts utterances
+ * (run_whisper_encoder_state, ggml_executor.rs:4020), from the device mel of the
+ * last oasr_b200_whisper_mel call or from host mel [n_utts][n_mels][3000];
+ * enc_out (host, optional) gets [n_utts][1500][d_model]. */
+int oasr_b200_whisper_encode(oasr_whisper *m, const float *mel_host, int32_t n_utts, float *enc_out);
+/* One batched decoder step at position pos (run_whisper_decoder_reused_batched_
+ * incremental_step_ggml_v0, ggml_decoder_graph.rs:3299): tokens[n_utts] in,
+ * logits [n_utts][n_vocab] (host, optional) and first-max next tokens out. */
+int oasr_b200_whisper_decode_step(oasr_whisper *m, const int32_t *tokens, int32_t n_utts, int32_t pos, float *logits,
+                                  int32_t *next);
+/* Whole greedy transcription (run_native_transcription, api/backend/
+ * native_transcribe.rs:1005): mel -> encoder -> prompt -> n_new greedy tokens
+ * (first-max argmax, seq2seq_greedy_decode.rs:418), decoder steps replayed from
+ * one CUDA graph; tokens_out [n_utts][n_new].  With stop_at_eot the loop ends
+ * once every sequence emitted `eot` (later entries are then undefined). */
+int oasr_b200_whisper_transcribe(oasr_whisper *m, const float *pcm, const int64_t *n_samples, int32_t n_utts,
+                                 const int32_t *prompt, int32_t n_prompt, int32_t n_new, int32_t eot,
+                                 int32_t stop_at_eot, int32_t *tokens_out);
+
 /* ---- host-side helpers (no device work) --------------------------------------- */
 /* ggml_row_size (ffi.rs:619) */
 int64_t oasr_b200_row_size(int32_t type, int64_t ne0);

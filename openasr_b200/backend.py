@@ -106,6 +106,23 @@ class OasrMemStats(ctypes.Structure):
     ]
 
 
+class OasrNamedTensor(ctypes.Structure):
+    _fields_ = [
+        ("name", ctypes.c_char_p),
+        ("type", ctypes.c_int32),
+        ("_pad", ctypes.c_int32),
+        ("ne", ctypes.c_int64 * 4),
+        ("data", ctypes.c_void_p),
+        ("bytes", ctypes.c_uint64),
+    ]
+
+
+class OasrWhisperConfig(ctypes.Structure):
+    _fields_ = [(f, ctypes.c_int32) for f in
+                ("n_mels", "d_model", "n_heads", "n_enc_layers", "n_dec_layers", "n_vocab", "n_audio_ctx",
+                 "n_text_ctx", "max_batch")]
+
+
 ABORT_CB = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p)
 
 # every symbol include/oasr_b200.h declares, with (argtypes, restype)
@@ -135,6 +152,13 @@ SIGNATURES = {
     "oasr_b200_flash_attn_ext": ([_P, _TP, _TP, _TP, _TP, _F, _F, _F, _I32, _TP], ctypes.c_int),
     "oasr_b200_set_rows": ([_P, _TP, _TP, _TP], ctypes.c_int),
     "oasr_b200_argmax_first": ([_P, _TP, _TP], ctypes.c_int),
+    "oasr_b200_whisper_load": ([_P, ctypes.POINTER(OasrWhisperConfig), ctypes.POINTER(OasrNamedTensor), _I32,
+                                ctypes.POINTER(_P)], ctypes.c_int),
+    "oasr_b200_whisper_free": ([_P], ctypes.c_int),
+    "oasr_b200_whisper_mel": ([_P, _P, _P, _I32, _P], ctypes.c_int),
+    "oasr_b200_whisper_encode": ([_P, _P, _I32, _P], ctypes.c_int),
+    "oasr_b200_whisper_decode_step": ([_P, _P, _I32, _I32, _P, _P], ctypes.c_int),
+    "oasr_b200_whisper_transcribe": ([_P, _P, _P, _I32, _P, _I32, _I32, _I32, _I32, _P], ctypes.c_int),
     "oasr_b200_row_size": ([_I32, _I64], _I64),
     "oasr_b200_quantize_chunk": ([_I32, _P, _P, _I64, _I64, _I64], _I64),
     "oasr_b200_synth_normal": ([_U64, _U64, _P, _I64, _F, _F], ctypes.c_int),

@@ -41,6 +41,8 @@ struct FaArgs {
     float scale;
     float *partials;          // [rows][n_splits][D + 2]
     unsigned int *counters;   // one ticket per (kv head, seq, q tile)
+    const float *q_bias;      // optional [H*D] added to q before the fp16 rounding
+    const int *nkv_dev;       // optional device-side KV length (<= NKV), for graph-captured decode
 };
 
 template <bool F16>
@@ -88,9 +90,11 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
         qh[t] = hk * a.G + rr / a.NQ;
         qi[t] = rr % a.NQ;
         const float *qp = reinterpret_cast<const float *>(a.q + qi[t] * a.q_nb1 + qh[t] * a.q_nb2 + s * a.q_nb3) + sl * 8;
+        const float *qb = a.q_bias ? a.q_bias + qh[t] * D + sl * 8 : nullptr;
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
             float x = qvalid[t] ? qp[e] : 0.0f;
+            if (qb) x = __fadd_rn(x, qb[e]);
             qv[t][e] = F16 ? __half2float(__float2half_rn(x)) : x;
         }
     }
@@ -108,8 +112,9 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
         for (int e = 0; e < 8; ++e) acc[t][e] = 0.0f;
     }
 
+    const int nkv = a.nkv_dev ? min(*a.nkv_dev, a.NKV) : a.NKV;
     const int kv0 = split * a.kv_per_split;
-    const int kv1 = min(a.NKV, kv0 + a.kv_per_split);
+    const int kv1 = min(nkv, kv0 + a.kv_per_split);
     const char *kbase = a.k + hk * a.k_nb2 + s * a.k_nb3 + sl * 8 * ES;
     const char *vbase = a.v + hk * a.v_nb2 + s * a.v_nb3 + sl * 8 * ES;
     // U warp-steps of K/V rows are loaded before any is consumed so that each
@@ -276,7 +281,16 @@ static void launch_fa_d(const FaArgs &a, int QT, dim3 grid, cudaStream_t st) {
 
 int launch_flash_attn(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
                       const oasr_tensor *mask, float scale, oasr_tensor *dst) {
+    return launch_flash_attn_ex(be, q, k, v, mask, scale, dst, nullptr, nullptr);
+}
+
+// q_bias: optional [H*D] f32 added to q; nkv_dev: optional device KV length (k->ne[1] is the maximum)
+int launch_flash_attn_ex(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
+                         const oasr_tensor *mask, float scale, oasr_tensor *dst, const float *q_bias,
+                         const int *nkv_dev) {
     FaArgs a;
+    a.q_bias = q_bias;
+    a.nkv_dev = nkv_dev;
     const int D = (int)q->ne[0];
     a.q = (const char *)q->data;
     a.k = (const char *)k->data;

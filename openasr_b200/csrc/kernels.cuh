@@ -84,5 +84,8 @@ int launch_flash_attn_tc(oasr_backend *be, const oasr_tensor *q, const oasr_tens
                          float scale, oasr_tensor *dst);
 int launch_flash_attn(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
                       const oasr_tensor *mask, float scale, oasr_tensor *dst);
+int launch_flash_attn_ex(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
+                         const oasr_tensor *mask, float scale, oasr_tensor *dst, const float *q_bias,
+                         const int *nkv_dev);
 
 }  // namespace oasr

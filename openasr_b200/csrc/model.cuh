@@ -1,0 +1,55 @@
+// model.cuh -- launchers shared by the model drivers (model_whisper.cu, model_qwen.cu).
+#pragma once
+
+#include "kernels.cuh"
+
+namespace oasr {
+
+int launch_resid_norm_quant(oasr_backend *be, float *x, const float *add, const float *add_bias, int64_t rows, int n,
+                            float eps, bool rms, const float *gamma, const float *beta, float *out_f32,
+                            const ActPlanes *q, int family);
+int launch_bias_gelu_quant(oasr_backend *be, const float *x, const float *bias, int64_t rows, int n, float *out_f32,
+                           const ActPlanes *q, int family);
+int launch_swiglu_quant(oasr_backend *be, const float *gu, int64_t rows, int n, int64_t gu_ld, float *out_f32,
+                        const ActPlanes *q, int family);
+int launch_qkv_split_kv_write(oasr_backend *be, const float *qkv, const float *bias3, int B, int d, float *q_out,
+                              __half *kc, __half *vc, int64_t cache_seq_stride, const int *pos_dev, int max_pos);
+int launch_embed_q8_0(oasr_backend *be, const oasr_weight *emb, const int *tokens, int B, const float *pos_emb,
+                      const int *pos_dev, int max_pos, float *x);
+int launch_add_rows(oasr_backend *be, float *x, const float *bias, const float *add, int64_t rows, int n);
+int launch_cast_f16(oasr_backend *be, const float *src, int64_t src_ld, const float *bias, int64_t rows, int cols,
+                    __half *dst, int64_t dst_ld);
+int launch_im2col_f16(oasr_backend *be, const float *src, int64_t s_b, int64_t s_ic, int64_t s_t, int B, int IC,
+                      int T_in, int T_out, int KW, int stride, int pad, __half *dst, int K_pad);
+int launch_mel(oasr_backend *be, const float *audio, int B, int n_samples, int n_frames, int n_mels,
+               const float *window, const float2 *twiddle, const float *filters, float *power, float *mel,
+               int *max_key);
+int launch_rope_neox(oasr_backend *be, float *x, int T, int H, int D, const int *pos, float freq_base);
+int launch_gemm_f16(oasr_backend *be, const __half *A, int64_t lda, const __half *B, int64_t ldb, int M, int N, int K,
+                    float *y, int64_t y_ld, const float *bias, bool gelu);
+int launch_argmax_rows(oasr_backend *be, const float *x, int64_t ld, int64_t n, int rows, int32_t *out);
+
+// y[rows][N] = w . activation planes (rows <= 8: GEMV, else tensor-core / chunked GEMM)
+int mul_mat_planes(oasr_backend *be, const oasr_weight *w, const ActPlanes &a, int64_t rows, float *y, int64_t y_ld);
+
+inline int weight_family(const oasr_weight *w) { return w->type == OASR_TYPE_Q4_K ? FAMILY_Q8_K : FAMILY_Q8_0; }
+
+// tensor descriptor helper: contiguous-row views with explicit byte strides
+inline oasr_tensor make_tensor(int type, const void *data, int64_t ne0, int64_t ne1, int64_t ne2, int64_t ne3,
+                               int64_t nb1, int64_t nb2, int64_t nb3) {
+    oasr_tensor t;
+    t.type = type;
+    t.flags = 0;
+    t.data = const_cast<void *>(data);
+    t.ne[0] = ne0; t.ne[1] = ne1; t.ne[2] = ne2; t.ne[3] = ne3;
+    t.nb[0] = type == OASR_TYPE_F16 ? 2 : 4;
+    t.nb[1] = nb1; t.nb[2] = nb2; t.nb[3] = nb3;
+    return t;
+}
+
+// Host-side helpers shared with the CPU oracle's frontend definition (whisper/mel.rs):
+// periodic Hann window (scale first), Slaney mel filterbank (ratio-first edges).
+void whisper_hann_window(float *w, int n);
+void whisper_mel_filters(float *f, int n_mels, int n_fft, float sample_rate);
+
+}  // namespace oasr

@@ -1,0 +1,636 @@
+// model_whisper.cu -- Whisper encoder-decoder on the B200 kernels.
+//
+// Restates the graphs the reference builds per utterance:
+//   frontend   whisper/mel.rs (pad/trim to 30 s, reflect-centred STFT n_fft 400
+//              hop 160 with a periodic Hann window, Slaney mel filterbank,
+//              log10 floor 1e-10, max-8 dynamic range, (x+4)/4)
+//   prelude    whisper/ggml_executor.rs:640-730 (conv1d k3 s1 p1 + GELU,
+//              conv1d k3 s2 p1 + GELU, + positional embedding); ggml_conv_1d =
+//              im2col to fp16 + fp16 dot with f32 accumulation
+//   encoder    ggml_executor.rs:1509-1810 (pre-LN blocks: LN -> q(+b), k, v(+b)
+//              -> flash_attn_ext(scale 1/sqrt(64)) -> out(+b) -> residual ->
+//              LN -> fc1(+b) -> GELU -> fc2(+b) -> residual), final LN
+//   decoder    ggml_decoder_graph.rs:2840-3010 (token + position embedding,
+//              self-attention over the f16 self-KV cache, cross-attention over
+//              the f16 cross-KV cache, MLP, final LN, logits) + first-max argmax
+// with the hot ops on the kernels of this library.  Per-layer q|k|v weights are
+// concatenated along N at load (raw blocks, exact) so one GEMV serves all three.
+// A decoder step is captured once into a CUDA graph; token ids, the position
+// and the KV length live in device memory, so the graph replays for every step
+// and the greedy argmax feeds the next step without a host round trip.
+#include <math.h>
+#include <string.h>
+
+#include <map>
+#include <string>
+#include <vector>
+
+#include "model.cuh"
+
+using namespace oasr;
+
+namespace {
+
+constexpr int N_FFT = 400, HOP = 160, N_SAMPLES_30S = 480000, N_MEL_FRAMES = 3000;
+constexpr float LN_EPS = 1e-5f;
+
+struct EncLayer {
+    oasr_weight *qkv = nullptr, *o = nullptr, *fc1 = nullptr, *fc2 = nullptr;
+    float *ln1_g, *ln1_b, *ln2_g, *ln2_b, *b_qkv, *b_o, *b_fc1, *b_fc2;
+};
+
+struct DecLayer {
+    oasr_weight *qkv = nullptr, *o = nullptr, *cq = nullptr, *ckv = nullptr, *co = nullptr, *fc1 = nullptr, *fc2 = nullptr;
+    float *ln1_g, *ln1_b, *lnc_g, *lnc_b, *ln2_g, *ln2_b;
+    float *b_qkv, *b_o, *b_cq, *b_ckv, *b_co, *b_fc1, *b_fc2;
+    __half *self_k, *self_v, *cross_kv;
+};
+
+}  // namespace
+
+struct oasr_whisper {
+    oasr_backend *be;
+    oasr_whisper_config cfg;
+    cudaStream_t stream;
+    int d, H, ffn, K1p, K2p, T_enc, B;
+    __half *conv1_w, *conv2_w;
+    float *conv1_b, *conv2_b, *enc_pos;
+    std::vector<EncLayer> enc;
+    float *lnp_g, *lnp_b;
+    oasr_weight *tok_emb;
+    float *dec_pos;
+    std::vector<DecLayer> dec;
+    float *lnd_g, *lnd_b;
+    // frontend
+    float *window, *filters, *audio, *power, *mel;
+    float2 *twiddle;
+    int *max_key;
+    // encoder activations, B * T_enc rows
+    __half *im2col;
+    float *c1, *x, *qkv, *attn, *t, *f;
+    void *qa_d, *qa_f;
+    // decoder activations, B rows
+    float *dx, *dqkv, *dq, *dattn, *dt, *df, *logits;
+    void *dqa_d, *dqa_f, *dqa_lm;
+    int *tokens, *pos, *nkv, *history;
+    int enc_family, dec_family;
+    cudaGraphExec_t graph;
+    int graph_batch;
+    std::vector<void *> allocs;
+    std::vector<oasr_weight *> weights;
+};
+
+namespace {
+
+struct StreamScope {
+    oasr_backend *be;
+    cudaStream_t saved;
+    StreamScope(oasr_whisper *m) : be(m->be), saved(m->be->stream) { be->stream = m->stream; }
+    ~StreamScope() { be->stream = saved; }
+};
+
+template <typename T>
+int dalloc(oasr_whisper *m, T **p, size_t bytes) {
+    *p = nullptr;
+    if (bytes == 0) bytes = 256;
+    cudaError_t e = cudaMalloc((void **)p, bytes);
+    if (e != cudaSuccess) return oasr_internal_cuda_fail(m->be, e, "cudaMalloc(whisper)", __LINE__);
+    m->allocs.push_back(*p);
+    return OASR_STATUS_SUCCESS;
+}
+
+const oasr_named_tensor *find(const std::map<std::string, const oasr_named_tensor *> &tm, const std::string &n) {
+    auto it = tm.find(n);
+    return it == tm.end() ? nullptr : it->second;
+}
+
+#define W_TRY(expr)                 \
+    do {                            \
+        int _st = (expr);           \
+        if (_st) return _st;        \
+    } while (0)
+
+int upload_f32(oasr_whisper *m, const oasr_named_tensor *t, int64_t n, float **out, const char *name) {
+    if (!t || t->type != OASR_TYPE_F32 || t->bytes != (uint64_t)n * 4)
+        return oasr_internal_fail(m->be, OASR_STATUS_FAILED, std::string("whisper: missing or bad f32 tensor ") + name);
+    W_TRY(dalloc(m, out, (size_t)n * 4));
+    cudaError_t e = cudaMemcpy(*out, t->data, (size_t)n * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return oasr_internal_cuda_fail(m->be, e, "upload f32", __LINE__);
+    return OASR_STATUS_SUCCESS;
+}
+
+// concatenate 2-D weights [K, N_i] of one type along N (raw rows) and upload
+int upload_cat(oasr_whisper *m, const std::vector<const oasr_named_tensor *> &parts, int64_t K, oasr_weight **out,
+               const std::string &what) {
+    int type = -1;
+    int64_t N = 0;
+    for (auto *p : parts) {
+        if (!p || p->ne[0] != K || p->ne[2] != 1 || p->ne[3] != 1)
+            return oasr_internal_fail(m->be, OASR_STATUS_FAILED, "whisper: missing or bad weight " + what);
+        if (type < 0) type = p->type;
+        if (p->type != type) return oasr_internal_fail(m->be, OASR_STATUS_FAILED, "whisper: mixed types in " + what);
+        N += p->ne[1];
+    }
+    const int64_t rs = oasr_b200_row_size(type, K);
+    std::vector<uint8_t> buf((size_t)(rs * N));
+    size_t off = 0;
+    for (auto *p : parts) {
+        if (p->bytes != (uint64_t)(rs * p->ne[1])) return oasr_internal_fail(m->be, OASR_STATUS_FAILED, "whisper: byte count " + what);
+        memcpy(buf.data() + off, p->data, p->bytes);
+        off += p->bytes;
+    }
+    const int64_t ne[4] = {K, N, 1, 1};
+    W_TRY(oasr_b200_weight_upload(m->be, buf.data(), buf.size(), type, ne, out));
+    m->weights.push_back(*out);
+    return OASR_STATUS_SUCCESS;
+}
+
+// [b_0 | b_1 | ...] with missing biases as zeros
+int upload_bias_cat(oasr_whisper *m, const std::vector<const oasr_named_tensor *> &parts, int64_t each, float **out) {
+    std::vector<float> b(parts.size() * each, 0.0f);
+    for (size_t i = 0; i < parts.size(); ++i) {
+        if (!parts[i]) continue;
+        if (parts[i]->type != OASR_TYPE_F32 || parts[i]->bytes != (uint64_t)each * 4)
+            return oasr_internal_fail(m->be, OASR_STATUS_FAILED, "whisper: bad bias tensor");
+        memcpy(b.data() + i * each, parts[i]->data, each * 4);
+    }
+    W_TRY(dalloc(m, out, b.size() * 4));
+    cudaError_t e = cudaMemcpy(*out, b.data(), b.size() * 4, cudaMemcpyHostToDevice);
+    return e == cudaSuccess ? OASR_STATUS_SUCCESS : oasr_internal_cuda_fail(m->be, e, "upload bias", __LINE__);
+}
+
+// conv weight ggml [KW=3, IC, OC] f16 -> f16 [OC][K_pad] (row oc: ic*3 + k), zero padded
+int upload_conv(oasr_whisper *m, const oasr_named_tensor *t, int IC, int OC, int K_pad, __half **out) {
+    if (!t || t->type != OASR_TYPE_F16 || t->ne[0] != 3 || t->ne[1] != IC || t->ne[2] != OC)
+        return oasr_internal_fail(m->be, OASR_STATUS_FAILED, "whisper: bad conv weight");
+    std::vector<uint16_t> w((size_t)OC * K_pad, 0);
+    const uint16_t *src = (const uint16_t *)t->data;
+    for (int oc = 0; oc < OC; ++oc)
+        memcpy(&w[(size_t)oc * K_pad], src + (size_t)oc * IC * 3, (size_t)IC * 3 * 2);
+    W_TRY(dalloc(m, out, w.size() * 2));
+    cudaError_t e = cudaMemcpy(*out, w.data(), w.size() * 2, cudaMemcpyHostToDevice);
+    return e == cudaSuccess ? OASR_STATUS_SUCCESS : oasr_internal_cuda_fail(m->be, e, "upload conv", __LINE__);
+}
+
+int alloc_planes(oasr_whisper *m, void **p, int family, int64_t R, int64_t K) {
+    return dalloc(m, (uint8_t **)p, act_planes_bytes(family, R, K));
+}
+
+// ---- encoder ----------------------------------------------------------------------------------
+int run_encoder(oasr_whisper *m, int n) {
+    oasr_backend *be = m->be;
+    const int d = m->d, H = m->H, T = m->T_enc, nm = m->cfg.n_mels;
+    const int64_t M = (int64_t)n * T;
+    const int ef = m->enc_family;
+    // conv stem: im2col (fp16) + fp16 tensor-core GEMM + bias + GELU, twice
+    W_TRY(launch_im2col_f16(be, m->mel, (int64_t)nm * N_MEL_FRAMES, N_MEL_FRAMES, 1, n, nm, N_MEL_FRAMES, N_MEL_FRAMES,
+                            3, 1, 1, m->im2col, m->K1p));
+    W_TRY(launch_gemm_f16(be, m->im2col, m->K1p, m->conv1_w, m->K1p, n * N_MEL_FRAMES, d, m->K1p, m->c1, d,
+                          m->conv1_b, true));
+    W_TRY(launch_im2col_f16(be, m->c1, (int64_t)N_MEL_FRAMES * d, 1, d, n, d, N_MEL_FRAMES, T, 3, 2, 1, m->im2col,
+                            m->K2p));
+    W_TRY(launch_gemm_f16(be, m->im2col, m->K2p, m->conv2_w, m->K2p, (int)M, d, m->K2p, m->x, d, m->conv2_b, true));
+    for (int b = 0; b < n; ++b) W_TRY(launch_add_rows(be, m->x + (int64_t)b * T * d, nullptr, m->enc_pos, T, d));
+
+    const ActPlanes qd = act_planes_at(m->qa_d, ef, M, d);
+    const ActPlanes qf = act_planes_at(m->qa_f, ef, M, m->ffn);
+    const float scale = 1.0f / sqrtf(64.0f);
+    for (size_t l = 0; l < m->enc.size(); ++l) {
+        const EncLayer &L = m->enc[l];
+        const float *pend = l == 0 ? nullptr : m->t;
+        const float *pend_b = l == 0 ? nullptr : m->enc[l - 1].b_fc2;
+        W_TRY(launch_resid_norm_quant(be, m->x, pend, pend_b, M, d, LN_EPS, false, L.ln1_g, L.ln1_b, nullptr, &qd, ef));
+        W_TRY(mul_mat_planes(be, L.qkv, qd, M, m->qkv, 3 * d));
+        W_TRY(launch_add_rows(be, m->qkv, L.b_qkv, nullptr, M, 3 * d));
+        const int64_t ld = 3 * d * 4;
+        oasr_tensor q = make_tensor(OASR_TYPE_F32, m->qkv, 64, T, H, n, ld, 256, ld * T);
+        oasr_tensor k = make_tensor(OASR_TYPE_F32, m->qkv + d, 64, T, H, n, ld, 256, ld * T);
+        oasr_tensor v = make_tensor(OASR_TYPE_F32, m->qkv + 2 * d, 64, T, H, n, ld, 256, ld * T);
+        oasr_tensor o = make_tensor(OASR_TYPE_F32, m->attn, 64, H, T, n, 256, (int64_t)d * 4, (int64_t)d * 4 * T);
+        W_TRY(oasr_b200_flash_attn_ext(be, &q, &k, &v, nullptr, scale, 0.0f, 0.0f, OASR_PREC_DEFAULT, &o));
+        oasr_tensor at = make_tensor(OASR_TYPE_F32, m->attn, d, M, 1, 1, (int64_t)d * 4, (int64_t)d * 4 * M, (int64_t)d * 4 * M);
+        W_TRY(launch_quantize_act(be, &at, ef, qd));
+        W_TRY(mul_mat_planes(be, L.o, qd, M, m->t, d));
+        W_TRY(launch_resid_norm_quant(be, m->x, m->t, L.b_o, M, d, LN_EPS, false, L.ln2_g, L.ln2_b, nullptr, &qd, ef));
+        W_TRY(mul_mat_planes(be, L.fc1, qd, M, m->f, m->ffn));
+        W_TRY(launch_bias_gelu_quant(be, m->f, L.b_fc1, M, m->ffn, nullptr, &qf, ef));
+        W_TRY(mul_mat_planes(be, L.fc2, qf, M, m->t, d));
+    }
+    // final LN -> encoder output (f32, kept in x) + quantized copy for the cross-KV projections
+    const int df = m->dec_family;
+    const ActPlanes qx = act_planes_at(m->qa_d, df, M, d);
+    W_TRY(launch_resid_norm_quant(be, m->x, m->t, m->enc.back().b_fc2, M, d, LN_EPS, false, m->lnp_g, m->lnp_b, m->x,
+                                  &qx, df));
+    // cross-attention K|V per decoder layer, stored fp16 [slot][T][2d]
+    for (size_t l = 0; l < m->dec.size(); ++l) {
+        const DecLayer &L = m->dec[l];
+        W_TRY(mul_mat_planes(be, L.ckv, qx, M, m->qkv, 2 * d));
+        W_TRY(launch_cast_f16(be, m->qkv, 2 * d, L.b_ckv, M, 2 * d, L.cross_kv, 2 * d));
+    }
+    return OASR_STATUS_SUCCESS;
+}
+
+// ---- one decoder step for n sequences at device position *pos -------------------------------
+int run_decode_step(oasr_whisper *m, int n) {
+    oasr_backend *be = m->be;
+    const int d = m->d, H = m->H, T = m->T_enc, P = m->cfg.n_text_ctx;
+    const int df = m->dec_family;
+    const ActPlanes qd = act_planes_at(m->dqa_d, df, n, d);
+    const ActPlanes qf = act_planes_at(m->dqa_f, df, n, m->ffn);
+    const ActPlanes ql = act_planes_at(m->dqa_lm, FAMILY_Q8_0, n, d);
+    const float scale = 1.0f / sqrtf(64.0f);
+    W_TRY(launch_embed_q8_0(be, m->tok_emb, m->tokens, n, m->dec_pos, m->pos, P, m->dx));
+    for (size_t l = 0; l < m->dec.size(); ++l) {
+        const DecLayer &L = m->dec[l];
+        const float *pend = l == 0 ? nullptr : m->dt;
+        const float *pend_b = l == 0 ? nullptr : m->dec[l - 1].b_fc2;
+        W_TRY(launch_resid_norm_quant(be, m->dx, pend, pend_b, n, d, LN_EPS, false, L.ln1_g, L.ln1_b, nullptr, &qd, df));
+        W_TRY(mul_mat_planes(be, L.qkv, qd, n, m->dqkv, 3 * d));
+        W_TRY(launch_qkv_split_kv_write(be, m->dqkv, L.b_qkv, n, d, m->dq, L.self_k, L.self_v, (int64_t)P * d, m->pos, P));
+        {
+            oasr_tensor q = make_tensor(OASR_TYPE_F32, m->dq, 64, 1, H, n, (int64_t)d * 4, 256, (int64_t)d * 4);
+            oasr_tensor k = make_tensor(OASR_TYPE_F16, L.self_k, 64, P, H, n, (int64_t)d * 2, 128, (int64_t)P * d * 2);
+            oasr_tensor v = make_tensor(OASR_TYPE_F16, L.self_v, 64, P, H, n, (int64_t)d * 2, 128, (int64_t)P * d * 2);
+            oasr_tensor o = make_tensor(OASR_TYPE_F32, m->dattn, 64, H, 1, n, 256, (int64_t)d * 4, (int64_t)d * 4);
+            W_TRY(launch_flash_attn_ex(be, &q, &k, &v, nullptr, scale, &o, nullptr, m->nkv));
+        }
+        oasr_tensor at = make_tensor(OASR_TYPE_F32, m->dattn, d, n, 1, 1, (int64_t)d * 4, (int64_t)d * 4 * n, (int64_t)d * 4 * n);
+        W_TRY(launch_quantize_act(be, &at, df, qd));
+        W_TRY(mul_mat_planes(be, L.o, qd, n, m->dt, d));
+        W_TRY(launch_resid_norm_quant(be, m->dx, m->dt, L.b_o, n, d, LN_EPS, false, L.lnc_g, L.lnc_b, nullptr, &qd, df));
+        W_TRY(mul_mat_planes(be, L.cq, qd, n, m->dq, d));
+        {
+            oasr_tensor q = make_tensor(OASR_TYPE_F32, m->dq, 64, 1, H, n, (int64_t)d * 4, 256, (int64_t)d * 4);
+            oasr_tensor k = make_tensor(OASR_TYPE_F16, L.cross_kv, 64, T, H, n, (int64_t)d * 4, 128, (int64_t)T * d * 4);
+            oasr_tensor v = make_tensor(OASR_TYPE_F16, L.cross_kv + d, 64, T, H, n, (int64_t)d * 4, 128, (int64_t)T * d * 4);
+            oasr_tensor o = make_tensor(OASR_TYPE_F32, m->dattn, 64, H, 1, n, 256, (int64_t)d * 4, (int64_t)d * 4);
+            W_TRY(launch_flash_attn_ex(be, &q, &k, &v, nullptr, scale, &o, L.b_cq, nullptr));
+        }
+        W_TRY(launch_quantize_act(be, &at, df, qd));
+        W_TRY(mul_mat_planes(be, L.co, qd, n, m->dt, d));
+        W_TRY(launch_resid_norm_quant(be, m->dx, m->dt, L.b_co, n, d, LN_EPS, false, L.ln2_g, L.ln2_b, nullptr, &qd, df));
+        W_TRY(mul_mat_planes(be, L.fc1, qd, n, m->df, m->ffn));
+        W_TRY(launch_bias_gelu_quant(be, m->df, L.b_fc1, n, m->ffn, nullptr, &qf, df));
+        W_TRY(mul_mat_planes(be, L.fc2, qf, n, m->dt, d));
+    }
+    W_TRY(launch_resid_norm_quant(be, m->dx, m->dt, m->dec.back().b_fc2, n, d, LN_EPS, false, m->lnd_g, m->lnd_b,
+                                  nullptr, &ql, FAMILY_Q8_0));
+    W_TRY(mul_mat_planes(be, m->tok_emb, ql, n, m->logits, m->cfg.n_vocab));
+    W_TRY(launch_argmax_rows(be, m->logits, m->cfg.n_vocab, m->cfg.n_vocab, n, m->tokens));
+    return OASR_STATUS_SUCCESS;
+}
+
+__global__ void advance_kernel(const int *tokens, int *pos, int *nkv, int *history, int n, int P) {
+    const int b = threadIdx.x;
+    const int p = *pos;
+    if (b < n && p + 1 < P) history[b * P + p + 1] = tokens[b];
+    __syncthreads();
+    if (b == 0) {
+        *pos = p + 1;
+        *nkv = p + 2;
+    }
+}
+
+int decode_step_graph(oasr_whisper *m, int n) {
+    oasr_backend *be = m->be;
+    if (m->graph && m->graph_batch != n) {
+        cudaGraphExecDestroy(m->graph);
+        m->graph = nullptr;
+    }
+    if (!m->graph) {
+        cudaGraph_t g;
+        OASR_CUDA_TRY(be, cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+        int st = run_decode_step(m, n);
+        if (st == OASR_STATUS_SUCCESS) advance_kernel<<<1, 32, 0, m->stream>>>(m->tokens, m->pos, m->nkv, m->history, n, m->cfg.n_text_ctx);
+        cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+        if (st) return st;
+        if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "cudaStreamEndCapture", __LINE__);
+        e = cudaGraphInstantiate(&m->graph, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "cudaGraphInstantiate", __LINE__);
+        m->graph_batch = n;
+    }
+    OASR_CUDA_TRY(be, cudaGraphLaunch(m->graph, m->stream));
+    return OASR_STATUS_SUCCESS;
+}
+
+int set_position(oasr_whisper *m, int pos) {
+    int v[2] = {pos, pos + 1};
+    OASR_CUDA_TRY(m->be, cudaMemcpyAsync(m->pos, &v[0], sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    OASR_CUDA_TRY(m->be, cudaMemcpyAsync(m->nkv, &v[1], sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    return OASR_STATUS_SUCCESS;
+}
+
+}  // namespace
+
+namespace oasr {
+
+void whisper_hann_window(float *w, int n) {
+    const float scale = 3.14159265358979323846f * 2.0f / (float)n;
+    for (int i = 0; i < n; ++i) w[i] = 0.5f - 0.5f * cosf(scale * (float)i);
+}
+
+static float hz_to_mel_slaney(float hz) {
+    const float f_sp = 200.0f / 3.0f, min_log_hz = 1000.0f;
+    const float min_log_mel = (min_log_hz - 0.0f) / f_sp;
+    const float logstep = logf(6.4f) / 27.0f;
+    return hz >= min_log_hz ? min_log_mel + logf(hz / min_log_hz) / logstep : (hz - 0.0f) / f_sp;
+}
+
+static float mel_to_hz_slaney(float mel) {
+    const float f_sp = 200.0f / 3.0f, min_log_hz = 1000.0f;
+    const float min_log_mel = (min_log_hz - 0.0f) / f_sp;
+    const float logstep = logf(6.4f) / 27.0f;
+    return mel >= min_log_mel ? min_log_hz * expf(logstep * (mel - min_log_mel)) : 0.0f + f_sp * mel;
+}
+
+void whisper_mel_filters(float *filt, int n_mels, int n_fft, float sr) {
+    const int bins = n_fft / 2 + 1;
+    const float mel_min = hz_to_mel_slaney(0.0f), mel_max = hz_to_mel_slaney(8000.0f);
+    std::vector<float> hz(n_mels + 2);
+    for (int i = 0; i < n_mels + 2; ++i) {
+        const float ratio = (float)i / (float)(n_mels + 1);
+        hz[i] = mel_to_hz_slaney(mel_min + ratio * (mel_max - mel_min));
+    }
+    for (int m = 0; m < n_mels; ++m) {
+        const float left = hz[m], center = hz[m + 1], right = hz[m + 2];
+        const float enorm = 2.0f / (right - left);
+        for (int b = 0; b < bins; ++b) {
+            const float f = (float)b * sr / (float)n_fft;
+            const float lower = (f - left) / (center - left), upper = (right - f) / (right - center);
+            float w = lower < upper ? lower : upper;
+            w = w > 0.0f ? w : 0.0f;
+            filt[m * bins + b] = w * enorm;
+        }
+    }
+}
+
+}  // namespace oasr
+
+extern "C" {
+
+int oasr_b200_whisper_free(oasr_whisper *m) {
+    if (!m) return OASR_STATUS_SUCCESS;
+    cudaSetDevice(m->be->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->graph) cudaGraphExecDestroy(m->graph);
+    for (auto *w : m->weights) oasr_b200_weight_free(m->be, w);
+    for (void *p : m->allocs) cudaFree(p);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+    return OASR_STATUS_SUCCESS;
+}
+
+int oasr_b200_whisper_load(oasr_backend *be, const oasr_whisper_config *cfg, const oasr_named_tensor *tensors,
+                           int32_t n_tensors, oasr_whisper **out) {
+    if (!out) return OASR_STATUS_FAILED;
+    *out = nullptr;
+    int st = oasr_internal_precheck(be);
+    if (st) return st;
+    if (!cfg || !tensors || cfg->d_model % 64 || cfg->n_heads * 64 != cfg->d_model || cfg->max_batch < 1 ||
+        cfg->max_batch > 8 || cfg->n_audio_ctx * 2 != N_MEL_FRAMES || cfg->n_enc_layers < 1 || cfg->n_dec_layers < 1)
+        return oasr_internal_fail(be, OASR_STATUS_FAILED, "whisper_load: unsupported config");
+    std::map<std::string, const oasr_named_tensor *> tm;
+    for (int i = 0; i < n_tensors; ++i) tm[tensors[i].name] = &tensors[i];
+    oasr_whisper *m = new oasr_whisper();
+    m->be = be;
+    m->cfg = *cfg;
+    m->d = cfg->d_model;
+    m->H = cfg->n_heads;
+    m->ffn = 4 * cfg->d_model;
+    m->T_enc = cfg->n_audio_ctx;
+    m->B = cfg->max_batch;
+    m->K1p = (3 * cfg->n_mels + 63) / 64 * 64;
+    m->K2p = (3 * cfg->d_model + 63) / 64 * 64;
+    m->graph = nullptr;
+    m->graph_batch = 0;
+    m->stream = nullptr;
+    auto fail = [&](int s) {
+        oasr_b200_whisper_free(m);
+        return s;
+    };
+    if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) return fail(OASR_STATUS_ALLOC_FAILED);
+    const int d = m->d, B = m->B, T = m->T_enc, P = cfg->n_text_ctx, nm = cfg->n_mels;
+    auto T_ = [&](const std::string &n) { return find(tm, n); };
+#define L_TRY(expr)                 \
+    do {                            \
+        int _s = (expr);            \
+        if (_s) return fail(_s);    \
+    } while (0)
+    // prelude
+    L_TRY(upload_conv(m, T_("encoder.conv1.weight"), nm, d, m->K1p, &m->conv1_w));
+    L_TRY(upload_conv(m, T_("encoder.conv2.weight"), d, d, m->K2p, &m->conv2_w));
+    L_TRY(upload_f32(m, T_("encoder.conv1.bias"), d, &m->conv1_b, "encoder.conv1.bias"));
+    L_TRY(upload_f32(m, T_("encoder.conv2.bias"), d, &m->conv2_b, "encoder.conv2.bias"));
+    L_TRY(upload_f32(m, T_("encoder.positional_embedding"), (int64_t)T * d, &m->enc_pos, "encoder.positional_embedding"));
+    for (int l = 0; l < cfg->n_enc_layers; ++l) {
+        const std::string p = "encoder.blocks." + std::to_string(l) + ".";
+        EncLayer L;
+        L_TRY(upload_cat(m, {T_(p + "attn.query.weight"), T_(p + "attn.key.weight"), T_(p + "attn.value.weight")}, d, &L.qkv, p + "attn.qkv"));
+        L_TRY(upload_cat(m, {T_(p + "attn.out.weight")}, d, &L.o, p + "attn.out"));
+        L_TRY(upload_cat(m, {T_(p + "mlp.0.weight")}, d, &L.fc1, p + "mlp.0"));
+        L_TRY(upload_cat(m, {T_(p + "mlp.2.weight")}, m->ffn, &L.fc2, p + "mlp.2"));
+        L_TRY(upload_bias_cat(m, {T_(p + "attn.query.bias"), nullptr, T_(p + "attn.value.bias")}, d, &L.b_qkv));
+        L_TRY(upload_f32(m, T_(p + "attn.out.bias"), d, &L.b_o, "attn.out.bias"));
+        L_TRY(upload_f32(m, T_(p + "mlp.0.bias"), m->ffn, &L.b_fc1, "mlp.0.bias"));
+        L_TRY(upload_f32(m, T_(p + "mlp.2.bias"), d, &L.b_fc2, "mlp.2.bias"));
+        L_TRY(upload_f32(m, T_(p + "attn_ln.weight"), d, &L.ln1_g, "attn_ln.weight"));
+        L_TRY(upload_f32(m, T_(p + "attn_ln.bias"), d, &L.ln1_b, "attn_ln.bias"));
+        L_TRY(upload_f32(m, T_(p + "mlp_ln.weight"), d, &L.ln2_g, "mlp_ln.weight"));
+        L_TRY(upload_f32(m, T_(p + "mlp_ln.bias"), d, &L.ln2_b, "mlp_ln.bias"));
+        m->enc.push_back(L);
+    }
+    L_TRY(upload_f32(m, T_("encoder.ln_post.weight"), d, &m->lnp_g, "encoder.ln_post.weight"));
+    L_TRY(upload_f32(m, T_("encoder.ln_post.bias"), d, &m->lnp_b, "encoder.ln_post.bias"));
+    // decoder
+    {
+        const oasr_named_tensor *te = T_("decoder.token_embedding.weight");
+        if (!te || te->type != OASR_TYPE_Q8_0 || te->ne[0] != d || te->ne[1] != cfg->n_vocab)
+            return fail(oasr_internal_fail(be, OASR_STATUS_FAILED, "whisper: token embedding must be Q8_0 [d, vocab]"));
+        L_TRY(upload_cat(m, {te}, d, &m->tok_emb, "decoder.token_embedding"));
+    }
+    L_TRY(upload_f32(m, T_("decoder.positional_embedding"), (int64_t)P * d, &m->dec_pos, "decoder.positional_embedding"));
+    for (int l = 0; l < cfg->n_dec_layers; ++l) {
+        const std::string p = "decoder.blocks." + std::to_string(l) + ".";
+        DecLayer L;
+        L_TRY(upload_cat(m, {T_(p + "attn.query.weight"), T_(p + "attn.key.weight"), T_(p + "attn.value.weight")}, d, &L.qkv, p + "attn.qkv"));
+        L_TRY(upload_cat(m, {T_(p + "attn.out.weight")}, d, &L.o, p + "attn.out"));
+        L_TRY(upload_cat(m, {T_(p + "cross_attn.query.weight")}, d, &L.cq, p + "cross_attn.query"));
+        L_TRY(upload_cat(m, {T_(p + "cross_attn.key.weight"), T_(p + "cross_attn.value.weight")}, d, &L.ckv, p + "cross_attn.kv"));
+        L_TRY(upload_cat(m, {T_(p + "cross_attn.out.weight")}, d, &L.co, p + "cross_attn.out"));
+        L_TRY(upload_cat(m, {T_(p + "mlp.0.weight")}, d, &L.fc1, p + "mlp.0"));
+        L_TRY(upload_cat(m, {T_(p + "mlp.2.weight")}, m->ffn, &L.fc2, p + "mlp.2"));
+        L_TRY(upload_bias_cat(m, {T_(p + "attn.query.bias"), nullptr, T_(p + "attn.value.bias")}, d, &L.b_qkv));
+        L_TRY(upload_f32(m, T_(p + "attn.out.bias"), d, &L.b_o, "attn.out.bias"));
+        L_TRY(upload_f32(m, T_(p + "cross_attn.query.bias"), d, &L.b_cq, "cross_attn.query.bias"));
+        L_TRY(upload_bias_cat(m, {nullptr, T_(p + "cross_attn.value.bias")}, d, &L.b_ckv));
+        L_TRY(upload_f32(m, T_(p + "cross_attn.out.bias"), d, &L.b_co, "cross_attn.out.bias"));
+        L_TRY(upload_f32(m, T_(p + "mlp.0.bias"), m->ffn, &L.b_fc1, "mlp.0.bias"));
+        L_TRY(upload_f32(m, T_(p + "mlp.2.bias"), d, &L.b_fc2, "mlp.2.bias"));
+        L_TRY(upload_f32(m, T_(p + "attn_ln.weight"), d, &L.ln1_g, "attn_ln.weight"));
+        L_TRY(upload_f32(m, T_(p + "attn_ln.bias"), d, &L.ln1_b, "attn_ln.bias"));
+        L_TRY(upload_f32(m, T_(p + "cross_attn_ln.weight"), d, &L.lnc_g, "cross_attn_ln.weight"));
+        L_TRY(upload_f32(m, T_(p + "cross_attn_ln.bias"), d, &L.lnc_b, "cross_attn_ln.bias"));
+        L_TRY(upload_f32(m, T_(p + "mlp_ln.weight"), d, &L.ln2_g, "mlp_ln.weight"));
+        L_TRY(upload_f32(m, T_(p + "mlp_ln.bias"), d, &L.ln2_b, "mlp_ln.bias"));
+        L_TRY(dalloc(m, &L.self_k, (size_t)B * P * d * 2));
+        L_TRY(dalloc(m, &L.self_v, (size_t)B * P * d * 2));
+        L_TRY(dalloc(m, &L.cross_kv, (size_t)B * T * 2 * d * 2));
+        m->dec.push_back(L);
+    }
+    L_TRY(upload_f32(m, T_("decoder.ln.weight"), d, &m->lnd_g, "decoder.ln.weight"));
+    L_TRY(upload_f32(m, T_("decoder.ln.bias"), d, &m->lnd_b, "decoder.ln.bias"));
+    m->enc_family = weight_family(m->enc[0].fc1);
+    m->dec_family = weight_family(m->dec[0].fc1);
+    if (weight_family(m->dec[0].ckv) != m->dec_family)
+        return fail(oasr_internal_fail(be, OASR_STATUS_FAILED, "whisper: decoder weights must share one type family"));
+    // frontend tables (host-computed like the reference's plan, whisper/mel.rs:64-96)
+    {
+        std::vector<float> win(N_FFT), filt((size_t)nm * (N_FFT / 2 + 1));
+        std::vector<float2> tw(N_FFT);
+        whisper_hann_window(win.data(), N_FFT);
+        whisper_mel_filters(filt.data(), nm, N_FFT, 16000.0f);
+        for (int j = 0; j < N_FFT; ++j) {
+            const double a = 2.0 * 3.14159265358979323846 * (double)j / (double)N_FFT;
+            tw[j] = make_float2((float)cos(a), (float)-sin(a));
+        }
+        L_TRY(dalloc(m, &m->window, N_FFT * 4));
+        L_TRY(dalloc(m, &m->filters, filt.size() * 4));
+        L_TRY(dalloc(m, &m->twiddle, N_FFT * sizeof(float2)));
+        cudaMemcpy(m->window, win.data(), N_FFT * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(m->filters, filt.data(), filt.size() * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(m->twiddle, tw.data(), N_FFT * sizeof(float2), cudaMemcpyHostToDevice);
+    }
+    const int64_t M = (int64_t)B * T;
+    L_TRY(dalloc(m, &m->audio, (size_t)B * N_SAMPLES_30S * 4));
+    L_TRY(dalloc(m, &m->power, (size_t)B * N_MEL_FRAMES * (N_FFT / 2 + 1) * 4));
+    L_TRY(dalloc(m, &m->mel, (size_t)B * nm * N_MEL_FRAMES * 4));
+    L_TRY(dalloc(m, &m->max_key, (size_t)B * 4));
+    L_TRY(dalloc(m, &m->im2col, (size_t)B * N_MEL_FRAMES * std::max(m->K1p, m->K2p) * 2));
+    L_TRY(dalloc(m, &m->c1, (size_t)B * N_MEL_FRAMES * d * 4));
+    L_TRY(dalloc(m, &m->x, (size_t)M * d * 4));
+    L_TRY(dalloc(m, &m->qkv, (size_t)M * 3 * d * 4));
+    L_TRY(dalloc(m, &m->attn, (size_t)M * d * 4));
+    L_TRY(dalloc(m, &m->t, (size_t)M * d * 4));
+    L_TRY(dalloc(m, &m->f, (size_t)M * m->ffn * 4));
+    L_TRY(alloc_planes(m, &m->qa_d, FAMILY_Q8_K, M, d));  // the larger family layout covers both
+    L_TRY(alloc_planes(m, &m->qa_f, FAMILY_Q8_K, M, m->ffn));
+    L_TRY(dalloc(m, &m->dx, (size_t)B * d * 4));
+    L_TRY(dalloc(m, &m->dqkv, (size_t)B * 3 * d * 4));
+    L_TRY(dalloc(m, &m->dq, (size_t)B * d * 4));
+    L_TRY(dalloc(m, &m->dattn, (size_t)B * d * 4));
+    L_TRY(dalloc(m, &m->dt, (size_t)B * d * 4));
+    L_TRY(dalloc(m, &m->df, (size_t)B * m->ffn * 4));
+    L_TRY(dalloc(m, &m->logits, (size_t)B * cfg->n_vocab * 4));
+    L_TRY(alloc_planes(m, &m->dqa_d, FAMILY_Q8_K, B, d));
+    L_TRY(alloc_planes(m, &m->dqa_f, FAMILY_Q8_K, B, m->ffn));
+    L_TRY(alloc_planes(m, &m->dqa_lm, FAMILY_Q8_0, B, d));
+    L_TRY(dalloc(m, &m->tokens, (size_t)B * 4));
+    L_TRY(dalloc(m, &m->pos, 4));
+    L_TRY(dalloc(m, &m->nkv, 4));
+    L_TRY(dalloc(m, &m->history, (size_t)B * P * 4));
+    // flash-decode partials for the largest split configuration seen by a decoder step
+    L_TRY(oasr_b200_reserve_scratch(be, (size_t)std::max<int64_t>(64ll << 20, (int64_t)B * m->H * 1024 * 66 * 4)));
+#undef L_TRY
+    *out = m;
+    return OASR_STATUS_SUCCESS;
+}
+
+int oasr_b200_whisper_mel(oasr_whisper *m, const float *pcm, const int64_t *n_samples, int32_t n_utts, float *mel_out) {
+    if (!m || !pcm || !n_samples || n_utts < 1 || n_utts > m->B) return OASR_STATUS_FAILED;
+    int st = oasr_internal_precheck(m->be);
+    if (st) return st;
+    StreamScope sc(m);
+    const int nm = m->cfg.n_mels;
+    // pad / trim every clip to 30 s (whisper/mel.rs pad_or_trim_audio)
+    int64_t off = 0;
+    OASR_CUDA_TRY(m->be, cudaMemsetAsync(m->audio, 0, (size_t)n_utts * N_SAMPLES_30S * 4, m->stream));
+    for (int b = 0; b < n_utts; ++b) {
+        if (n_samples[b] < 1) return oasr_internal_fail(m->be, OASR_STATUS_FAILED, "whisper_mel: empty clip");
+        const int64_t take = std::min<int64_t>(n_samples[b], N_SAMPLES_30S);
+        OASR_CUDA_TRY(m->be, cudaMemcpyAsync(m->audio + (int64_t)b * N_SAMPLES_30S, pcm + off, take * 4,
+                                             cudaMemcpyHostToDevice, m->stream));
+        off += n_samples[b];
+    }
+    W_TRY(launch_mel(m->be, m->audio, n_utts, N_SAMPLES_30S, N_MEL_FRAMES, nm, m->window, m->twiddle, m->filters,
+                     m->power, m->mel, m->max_key));
+    if (mel_out) {
+        OASR_CUDA_TRY(m->be, cudaMemcpyAsync(mel_out, m->mel, (size_t)n_utts * nm * N_MEL_FRAMES * 4,
+                                             cudaMemcpyDeviceToHost, m->stream));
+        OASR_CUDA_TRY(m->be, cudaStreamSynchronize(m->stream));
+    }
+    return OASR_STATUS_SUCCESS;
+}
+
+int oasr_b200_whisper_encode(oasr_whisper *m, const float *mel_host, int32_t n_utts, float *enc_out) {
+    if (!m || n_utts < 1 || n_utts > m->B) return OASR_STATUS_FAILED;
+    int st = oasr_internal_precheck(m->be);
+    if (st) return st;
+    StreamScope sc(m);
+    if (mel_host)
+        OASR_CUDA_TRY(m->be, cudaMemcpyAsync(m->mel, mel_host, (size_t)n_utts * m->cfg.n_mels * N_MEL_FRAMES * 4,
+                                             cudaMemcpyHostToDevice, m->stream));
+    W_TRY(run_encoder(m, n_utts));
+    if (enc_out)
+        OASR_CUDA_TRY(m->be, cudaMemcpyAsync(enc_out, m->x, (size_t)n_utts * m->T_enc * m->d * 4, cudaMemcpyDeviceToHost,
+                                             m->stream));
+    OASR_CUDA_TRY(m->be, cudaStreamSynchronize(m->stream));
+    return oasr_b200_synchronize(m->be);
+}
+
+int oasr_b200_whisper_decode_step(oasr_whisper *m, const int32_t *tokens, int32_t n_utts, int32_t pos, float *logits,
+                                  int32_t *next) {
+    if (!m || !tokens || n_utts < 1 || n_utts > m->B || pos < 0 || pos >= m->cfg.n_text_ctx) return OASR_STATUS_FAILED;
+    int st = oasr_internal_precheck(m->be);
+    if (st) return st;
+    StreamScope sc(m);
+    OASR_CUDA_TRY(m->be, cudaMemcpyAsync(m->tokens, tokens, n_utts * 4, cudaMemcpyHostToDevice, m->stream));
+    W_TRY(set_position(m, pos));
+    W_TRY(run_decode_step(m, n_utts));
+    if (logits)
+        OASR_CUDA_TRY(m->be, cudaMemcpyAsync(logits, m->logits, (size_t)n_utts * m->cfg.n_vocab * 4,
+                                             cudaMemcpyDeviceToHost, m->stream));
+    if (next) OASR_CUDA_TRY(m->be, cudaMemcpyAsync(next, m->tokens, n_utts * 4, cudaMemcpyDeviceToHost, m->stream));
+    OASR_CUDA_TRY(m->be, cudaStreamSynchronize(m->stream));
+    return oasr_b200_synchronize(m->be);
+}
+
+int oasr_b200_whisper_transcribe(oasr_whisper *m, const float *pcm, const int64_t *n_samples, int32_t n_utts,
+                                 const int32_t *prompt, int32_t n_prompt, int32_t n_new, int32_t eot, int32_t stop_at_eot,
+                                 int32_t *tokens_out) {
+    if (!m || !prompt || n_prompt < 1 || n_new < 1 || n_prompt + n_new > m->cfg.n_text_ctx || !tokens_out)
+        return OASR_STATUS_FAILED;
+    W_TRY(oasr_b200_whisper_mel(m, pcm, n_samples, n_utts, nullptr));
+    int st = oasr_internal_precheck(m->be);
+    if (st) return st;
+    StreamScope sc(m);
+    W_TRY(run_encoder(m, n_utts));
+    const int P = m->cfg.n_text_ctx;
+    std::vector<int32_t> tk(n_utts);
+    W_TRY(set_position(m, 0));
+    std::vector<int32_t> last(n_utts);
+    for (int i = 0; i < n_prompt + n_new - 1; ++i) {
+        if (m->be->abort_cb && m->be->abort_cb(m->be->abort_data)) return OASR_STATUS_ABORTED;  // step checkpoint
+        if (i < n_prompt) {
+            for (int b = 0; b < n_utts; ++b) tk[b] = prompt[i];
+            OASR_CUDA_TRY(m->be, cudaMemcpyAsync(m->tokens, tk.data(), n_utts * 4, cudaMemcpyHostToDevice, m->stream));
+            OASR_CUDA_TRY(m->be, cudaStreamSynchronize(m->stream));  // tk is reused on the next iteration
+        }
+        W_TRY(decode_step_graph(m, n_utts));
+        if (stop_at_eot && i >= n_prompt - 1) {
+            OASR_CUDA_TRY(m->be, cudaMemcpyAsync(last.data(), m->tokens, n_utts * 4, cudaMemcpyDeviceToHost, m->stream));
+            OASR_CUDA_TRY(m->be, cudaStreamSynchronize(m->stream));
+            bool all = true;
+            for (int b = 0; b < n_utts; ++b) all = all && last[b] == eot;
+            if (all) break;
+        }
+    }
+    std::vector<int32_t> hist((size_t)n_utts * P);
+    OASR_CUDA_TRY(m->be, cudaMemcpyAsync(hist.data(), m->history, hist.size() * 4, cudaMemcpyDeviceToHost, m->stream));
+    OASR_CUDA_TRY(m->be, cudaStreamSynchronize(m->stream));
+    for (int b = 0; b < n_utts; ++b)
+        for (int i = 0; i < n_new; ++i) tokens_out[(int64_t)b * n_new + i] = hist[(size_t)b * P + n_prompt + i];
+    return oasr_b200_synchronize(m->be);
+}
+
+}  // extern "C"

@@ -5,6 +5,7 @@
 #include <math.h>
 
 #include "kernels.cuh"
+#include "model.cuh"
 
 using namespace oasr;
 
@@ -78,6 +79,18 @@ __global__ void argmax_first_kernel(const char *x, int64_t nb1, int64_t n, int32
 
 }  // namespace
 
+namespace oasr {
+int launch_argmax_rows(oasr_backend *be, const float *x, int64_t ld, int64_t n, int rows, int32_t *out) {
+    argmax_first_kernel<<<(unsigned)rows, 1024, 0, be->stream>>>((const char *)x, ld * 4, n, out);
+    return oasr_internal_launch_check(be, "argmax_first");
+}
+
+int mul_mat_planes(oasr_backend *be, const oasr_weight *w, const ActPlanes &a, int64_t rows, float *y, int64_t y_ld) {
+    if (rows <= 8) return launch_mmv_quant(be, w, 0, a, (int)rows, (int)w->ne[0], y, y_ld);
+    return launch_mmq(be, w, 0, a, rows, (int)w->ne[0], y, y_ld);
+}
+}  // namespace oasr
+
 extern "C" {
 
 int oasr_b200_mul_mat(oasr_backend *be, const oasr_weight *w, const oasr_tensor *x, oasr_tensor *dst, int32_t prec) {
@@ -124,6 +137,27 @@ int oasr_b200_mul_mat(oasr_backend *be, const oasr_weight *w, const oasr_tensor 
     // F16 / F32 weights: ggml CPU converts f32 activations to f16 for F16
     // weights; GGML_PREC_F32 keeps the f32 range (cpu_graph.rs:157-165).
     const bool round16 = w->type == OASR_TYPE_F16 && x->type == OASR_TYPE_F32 && prec != OASR_PREC_F32;
+    if (w->type == OASR_TYPE_F16 && prec != OASR_PREC_F32 && M > 8 && K % 64 == 0) {
+        // fp16 operands (the vec_dot type of F16), f32 accumulation, on the tensor cores
+        __half *x16 = (__half *)oasr_internal_scratch(be, align256((size_t)M * K * 2), &st);
+        if (st) return st;
+        for (int64_t i3 = 0; i3 < ne3; ++i3)
+            for (int64_t i2 = 0; i2 < ne2; ++i2) {
+                const int64_t slice = (i2 / r2) + (i3 / r3) * w->ne[2];
+                const char *xp = (const char *)x->data + i2 * x->nb[2] + i3 * x->nb[3];
+                if (x->type == OASR_TYPE_F32) {
+                    st = launch_cast_f16(be, (const float *)xp, x->nb[1] / 4, nullptr, M, (int)K, x16, K);
+                    if (st) return st;
+                } else {
+                    OASR_CUDA_TRY(be, cudaMemcpy2DAsync(x16, K * 2, xp, x->nb[1], K * 2, M, cudaMemcpyDeviceToDevice, be->stream));
+                }
+                float *y = reinterpret_cast<float *>((char *)dst->data + i2 * dst->nb[2] + i3 * dst->nb[3]);
+                st = launch_gemm_f16(be, x16, K, (const __half *)(w->qs + slice * N * w->qs_row_bytes), K, (int)M, (int)N,
+                                     (int)K, y, dst->nb[1] / 4, nullptr, false);
+                if (st) return st;
+            }
+        return OASR_STATUS_SUCCESS;
+    }
     for (int64_t i3 = 0; i3 < ne3; ++i3)
         for (int64_t i2 = 0; i2 < ne2; ++i2) {
             const int64_t slice = (i2 / r2) + (i3 / r3) * w->ne[2];

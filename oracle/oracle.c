@@ -525,6 +525,64 @@ static inline float load_elem(const char *p, int type) {
     return type == OO_TYPE_F32 ? *(const float *)p : oo_f16_to_f32(*(const uint16_t *)p);
 }
 
+static float r16(float x) { return oo_f16_to_f32(oo_f32_to_f16(x)); }
+
+/* tensor-core arithmetic (see oracle.h, OO_FA_TC128); no mask */
+static int fa_tc128(const oo_tensor *q, const oo_tensor *k, const oo_tensor *v, float scale, oo_tensor *dst) {
+    const int64_t D = q->ne[0], NQ = q->ne[1], H = q->ne[2], S = q->ne[3];
+    const int64_t NKV = k->ne[1], HKV = k->ne[2];
+    const int64_t G = H / HKV;
+    const float sl2 = scale * 1.4426950408889634f;
+    int bad = 0;
+#pragma omp parallel for schedule(dynamic, 4) reduction(| : bad)
+    for (int64_t ir = 0; ir < NQ * H * S; ++ir) {
+        const int64_t s = ir / (H * NQ), h = (ir / NQ) % H, iq = ir % NQ, hk = h / G;
+        float *qv = (float *)malloc((size_t)D * 4 * 3 + 128 * 4);
+        if (!qv) { bad = 1; continue; }
+        float *o = qv + D, *ot = qv + 2 * D, *x = qv + 3 * D;
+        const char *pq = (const char *)q->data + iq * q->nb[1] + h * q->nb[2] + s * q->nb[3];
+        for (int64_t d = 0; d < D; ++d) { qv[d] = r16(*(const float *)(pq + d * q->nb[0])); o[d] = 0.0f; }
+        float m = -INFINITY, l = 0.0f;
+        for (int64_t j0 = 0; j0 < NKV; j0 += 128) {
+            const int64_t nv = NKV - j0 < 128 ? NKV - j0 : 128;
+            float tmax = -INFINITY;
+            for (int64_t i = 0; i < nv; ++i) {
+                const char *kr = (const char *)k->data + (j0 + i) * k->nb[1] + hk * k->nb[2] + s * k->nb[3];
+                double acc = 0.0;
+                for (int64_t d = 0; d < D; ++d) acc += (double)(qv[d] * r16(load_elem(kr + d * k->nb[0], k->type)));
+                x[i] = (float)acc * sl2;
+                tmax = tmax > x[i] ? tmax : x[i];
+            }
+            const float mnew = m > tmax ? m : tmax;
+            const float alpha = exp2f(m - mnew);
+            float tsum = 0.0f;
+            for (int64_t i = 0; i < 128; i += 2) {
+                const float p0 = i < nv ? exp2f(x[i] - mnew) : 0.0f;
+                const float p1 = i + 1 < nv ? exp2f(x[i + 1] - mnew) : 0.0f;
+                tsum += p0 + p1;
+                if (i < nv) x[i] = r16(p0);
+                if (i + 1 < nv) x[i + 1] = r16(p1);
+            }
+            for (int64_t d = 0; d < D; ++d) {
+                double acc = 0.0;
+                for (int64_t i = 0; i < nv; ++i) {
+                    const char *vr = (const char *)v->data + (j0 + i) * v->nb[1] + hk * v->nb[2] + s * v->nb[3];
+                    acc += (double)(x[i] * r16(load_elem(vr + d * v->nb[0], v->type)));
+                }
+                ot[d] = (float)acc;
+            }
+            for (int64_t d = 0; d < D; ++d) o[d] = fmaf(o[d], alpha, ot[d]);
+            l = l * alpha + tsum;
+            m = mnew;
+        }
+        const float inv = l == 0.0f ? 0.0f : 1.0f / l;
+        float *out = (float *)((char *)dst->data + h * dst->nb[1] + iq * dst->nb[2] + s * dst->nb[3]);
+        for (int64_t d = 0; d < D; ++d) out[d] = o[d] * inv;
+        free(qv);
+    }
+    return bad ? OO_STATUS_ALLOC_FAILED : 0;
+}
+
 int oo_flash_attn_ext(const oo_tensor *q, const oo_tensor *k, const oo_tensor *v,
                       const oo_tensor *mask, float scale, int mode, oo_tensor *dst) {
     const int64_t DK = q->ne[0], NQ = q->ne[1], H = q->ne[2], S = q->ne[3];
@@ -539,6 +597,10 @@ int oo_flash_attn_ext(const oo_tensor *q, const oo_tensor *k, const oo_tensor *v
     if (dst->type != OO_TYPE_F32 || dst->ne[0] != DV || dst->ne[1] != H || dst->ne[2] != NQ || dst->ne[3] != S)
         return OO_STATUS_FAILED;
     const int64_t rk2 = H / HKV;
+    if (mode == OO_FA_TC128) {
+        if (mask) return OO_STATUS_FAILED;
+        return fa_tc128(q, k, v, scale, dst);
+    }
     const int f16acc = (mode == OO_FA_GGML) && v->type == OO_TYPE_F16;
     int bad = 0;
 #pragma omp parallel for schedule(dynamic, 4) reduction(| : bad)

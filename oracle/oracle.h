@@ -93,7 +93,12 @@ int oo_mul_mat(const oo_tensor *w, const oo_tensor *x, oo_tensor *dst);
  * k, v f16|f32 [D, n_kv, H_kv, S]; optional mask f16 [n_kv, >=n_q, *, *];
  * dst f32 [D, H, n_q, S].  mode 0 = ggml CPU (f16 V accumulator when v is
  * f16), mode 1 = f32 V accumulator. */
-enum { OO_FA_GGML = 0, OO_FA_F32 = 1 };
+enum { OO_FA_GGML = 0, OO_FA_F32 = 1, OO_FA_TC128 = 2 };
+/* OO_FA_TC128: the arithmetic of a tensor-core flash attention -- q, k, v rounded
+ * to fp16, scores in 128-key blocks with a running max in the base-2 domain,
+ * probabilities rounded to fp16 for the P.V product, f32 rescaling.  Used to
+ * check the GPU encoder attention kernel (ggml's CUDA backend makes the same
+ * fp16 conversion of f32 K/V); the ggml CPU semantics are modes 0 and 1. */
 int oo_flash_attn_ext(const oo_tensor *q, const oo_tensor *k, const oo_tensor *v,
                       const oo_tensor *mask, float scale, int mode, oo_tensor *dst);
 

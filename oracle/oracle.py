@@ -19,7 +19,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liboasr_oracle.so")
 
 F32, F16, Q4_0, Q8_0, Q4_K, Q8_K, I32 = 0, 1, 2, 8, 12, 15, 26
-FA_GGML, FA_F32 = 0, 1
+FA_GGML, FA_F32, FA_TC128 = 0, 1, 2
 BLOCK = {F32: (1, 4), F16: (1, 2), Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q8_K: (256, 292)}
 
 
