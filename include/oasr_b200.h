@@ -237,6 +237,13 @@ int oasr_b200_whisper_encode(oasr_whisper *m, const float *mel_host, int32_t n_u
  * logits [n_utts][n_vocab] (host, optional) and first-max next tokens out. */
 int oasr_b200_whisper_decode_step(oasr_whisper *m, const int32_t *tokens, int32_t n_utts, int32_t pos, float *logits,
                                   int32_t *next);
+/* The frontend from device-resident PCM (concatenated clips, n_samples host). */
+int oasr_b200_whisper_mel_device(oasr_whisper *m, const float *pcm_dev, const int64_t *n_samples, int32_t n_utts);
+/* Encoder + greedy decode from the device mel of the last whisper_mel* call;
+ * tokens_out [n_utts][n_new] is a device pointer when tokens_on_device != 0
+ * (then the call returns without waiting), else host memory. */
+int oasr_b200_whisper_generate(oasr_whisper *m, int32_t n_utts, const int32_t *prompt, int32_t n_prompt, int32_t n_new,
+                               int32_t eot, int32_t stop_at_eot, int32_t *tokens_out, int32_t tokens_on_device);
 /* Whole greedy transcription (run_native_transcription, api/backend/
  * native_transcribe.rs:1005): mel -> encoder -> prompt -> n_new greedy tokens
  * (first-max argmax, seq2seq_greedy_decode.rs:418), decoder steps replayed from

@@ -159,6 +159,8 @@ SIGNATURES = {
     "oasr_b200_whisper_encode": ([_P, _P, _I32, _P], ctypes.c_int),
     "oasr_b200_whisper_decode_step": ([_P, _P, _I32, _I32, _P, _P], ctypes.c_int),
     "oasr_b200_whisper_transcribe": ([_P, _P, _P, _I32, _P, _I32, _I32, _I32, _I32, _P], ctypes.c_int),
+    "oasr_b200_whisper_mel_device": ([_P, _P, _P, _I32], ctypes.c_int),
+    "oasr_b200_whisper_generate": ([_P, _I32, _P, _I32, _I32, _I32, _I32, _P, _I32], ctypes.c_int),
     "oasr_b200_row_size": ([_I32, _I64], _I64),
     "oasr_b200_quantize_chunk": ([_I32, _P, _P, _I64, _I64, _I64], _I64),
     "oasr_b200_synth_normal": ([_U64, _U64, _P, _I64, _F, _F], ctypes.c_int),

@@ -82,11 +82,21 @@ struct oasr_whisper {
 
 namespace {
 
+// Work goes to the backend's current stream when the caller set a non-legacy one
+// (so callers can order and time it), else to the model's own stream; CUDA
+// graph capture needs a non-legacy stream.
 struct StreamScope {
     oasr_backend *be;
-    cudaStream_t saved;
-    StreamScope(oasr_whisper *m) : be(m->be), saved(m->be->stream) { be->stream = m->stream; }
-    ~StreamScope() { be->stream = saved; }
+    oasr_whisper *m;
+    cudaStream_t saved_be, saved_m;
+    StreamScope(oasr_whisper *mm) : be(mm->be), m(mm), saved_be(mm->be->stream), saved_m(mm->stream) {
+        if (be->stream) m->stream = be->stream;
+        be->stream = m->stream;
+    }
+    ~StreamScope() {
+        be->stream = saved_be;
+        m->stream = saved_m;
+    }
 };
 
 template <typename T>
@@ -278,6 +288,10 @@ int run_decode_step(oasr_whisper *m, int n) {
     W_TRY(mul_mat_planes(be, m->tok_emb, ql, n, m->logits, m->cfg.n_vocab));
     W_TRY(launch_argmax_rows(be, m->logits, m->cfg.n_vocab, m->cfg.n_vocab, n, m->tokens));
     return OASR_STATUS_SUCCESS;
+}
+
+__global__ void fill_tokens_kernel(int *tokens, int n, int value) {
+    if (threadIdx.x < n) tokens[threadIdx.x] = value;
 }
 
 __global__ void advance_kernel(const int *tokens, int *pos, int *nkv, int *history, int n, int P) {
@@ -595,26 +609,41 @@ int oasr_b200_whisper_decode_step(oasr_whisper *m, const int32_t *tokens, int32_
     return oasr_b200_synchronize(m->be);
 }
 
-int oasr_b200_whisper_transcribe(oasr_whisper *m, const float *pcm, const int64_t *n_samples, int32_t n_utts,
-                                 const int32_t *prompt, int32_t n_prompt, int32_t n_new, int32_t eot, int32_t stop_at_eot,
-                                 int32_t *tokens_out) {
-    if (!m || !prompt || n_prompt < 1 || n_new < 1 || n_prompt + n_new > m->cfg.n_text_ctx || !tokens_out)
+int oasr_b200_whisper_mel_device(oasr_whisper *m, const float *pcm_dev, const int64_t *n_samples, int32_t n_utts) {
+    if (!m || !pcm_dev || !n_samples || n_utts < 1 || n_utts > m->B) return OASR_STATUS_FAILED;
+    int st = oasr_internal_precheck(m->be);
+    if (st) return st;
+    StreamScope sc(m);
+    int64_t off = 0;
+    OASR_CUDA_TRY(m->be, cudaMemsetAsync(m->audio, 0, (size_t)n_utts * N_SAMPLES_30S * 4, m->stream));
+    for (int b = 0; b < n_utts; ++b) {
+        if (n_samples[b] < 1) return oasr_internal_fail(m->be, OASR_STATUS_FAILED, "whisper_mel: empty clip");
+        const int64_t take = std::min<int64_t>(n_samples[b], N_SAMPLES_30S);
+        OASR_CUDA_TRY(m->be, cudaMemcpyAsync(m->audio + (int64_t)b * N_SAMPLES_30S, pcm_dev + off, take * 4,
+                                             cudaMemcpyDeviceToDevice, m->stream));
+        off += n_samples[b];
+    }
+    return launch_mel(m->be, m->audio, n_utts, N_SAMPLES_30S, N_MEL_FRAMES, m->cfg.n_mels, m->window, m->twiddle,
+                      m->filters, m->power, m->mel, m->max_key);
+}
+
+int oasr_b200_whisper_generate(oasr_whisper *m, int32_t n_utts, const int32_t *prompt, int32_t n_prompt, int32_t n_new,
+                               int32_t eot, int32_t stop_at_eot, int32_t *tokens_out, int32_t tokens_on_device) {
+    if (!m || !prompt || n_utts < 1 || n_utts > m->B || n_prompt < 1 || n_new < 1 ||
+        n_prompt + n_new > m->cfg.n_text_ctx || !tokens_out)
         return OASR_STATUS_FAILED;
-    W_TRY(oasr_b200_whisper_mel(m, pcm, n_samples, n_utts, nullptr));
     int st = oasr_internal_precheck(m->be);
     if (st) return st;
     StreamScope sc(m);
     W_TRY(run_encoder(m, n_utts));
     const int P = m->cfg.n_text_ctx;
-    std::vector<int32_t> tk(n_utts);
     W_TRY(set_position(m, 0));
     std::vector<int32_t> last(n_utts);
     for (int i = 0; i < n_prompt + n_new - 1; ++i) {
         if (m->be->abort_cb && m->be->abort_cb(m->be->abort_data)) return OASR_STATUS_ABORTED;  // step checkpoint
         if (i < n_prompt) {
-            for (int b = 0; b < n_utts; ++b) tk[b] = prompt[i];
-            OASR_CUDA_TRY(m->be, cudaMemcpyAsync(m->tokens, tk.data(), n_utts * 4, cudaMemcpyHostToDevice, m->stream));
-            OASR_CUDA_TRY(m->be, cudaStreamSynchronize(m->stream));  // tk is reused on the next iteration
+            // prompt token i for every sequence: one device-side fill, no host buffer to keep alive
+            fill_tokens_kernel<<<1, 32, 0, m->stream>>>(m->tokens, n_utts, prompt[i]);
         }
         W_TRY(decode_step_graph(m, n_utts));
         if (stop_at_eot && i >= n_prompt - 1) {
@@ -625,12 +654,23 @@ int oasr_b200_whisper_transcribe(oasr_whisper *m, const float *pcm, const int64_
             if (all) break;
         }
     }
-    std::vector<int32_t> hist((size_t)n_utts * P);
-    OASR_CUDA_TRY(m->be, cudaMemcpyAsync(hist.data(), m->history, hist.size() * 4, cudaMemcpyDeviceToHost, m->stream));
-    OASR_CUDA_TRY(m->be, cudaStreamSynchronize(m->stream));
-    for (int b = 0; b < n_utts; ++b)
-        for (int i = 0; i < n_new; ++i) tokens_out[(int64_t)b * n_new + i] = hist[(size_t)b * P + n_prompt + i];
-    return oasr_b200_synchronize(m->be);
+    // tokens_out[b][i] = history[b][n_prompt + i]
+    OASR_CUDA_TRY(m->be, cudaMemcpy2DAsync(tokens_out, (size_t)n_new * 4, m->history + n_prompt, (size_t)P * 4,
+                                           (size_t)n_new * 4, n_utts,
+                                           tokens_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                                           m->stream));
+    if (!tokens_on_device) {
+        OASR_CUDA_TRY(m->be, cudaStreamSynchronize(m->stream));
+        return oasr_b200_synchronize(m->be);
+    }
+    return oasr_internal_launch_check(m->be, "whisper_generate");
+}
+
+int oasr_b200_whisper_transcribe(oasr_whisper *m, const float *pcm, const int64_t *n_samples, int32_t n_utts,
+                                 const int32_t *prompt, int32_t n_prompt, int32_t n_new, int32_t eot, int32_t stop_at_eot,
+                                 int32_t *tokens_out) {
+    W_TRY(oasr_b200_whisper_mel(m, pcm, n_samples, n_utts, nullptr));
+    return oasr_b200_whisper_generate(m, n_utts, prompt, n_prompt, n_new, eot, stop_at_eot, tokens_out, 0);
 }
 
 }  // extern "C"

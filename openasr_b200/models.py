@@ -186,6 +186,17 @@ class WhisperModel:
                                                                    logits.ctypes.data, nxt.ctypes.data))
         return logits, nxt
 
+    def mel_device(self, pcm_dev, n_samples) -> None:
+        """frontend from a device tensor of concatenated clips (torch, f32)"""
+        ns = np.ascontiguousarray(n_samples, np.int64)
+        self.backend._check(bk.lib().oasr_b200_whisper_mel_device(self.handle, pcm_dev.data_ptr(), ns.ctypes.data, len(ns)))
+
+    def generate_device(self, n_utts: int, tokens_dev, n_new: int = 224, prompt=None) -> None:
+        """encoder + greedy decode into a device int32 tensor [n_utts][n_new]; returns without waiting"""
+        self._prompt = np.ascontiguousarray(prompt if prompt is not None else PROMPT[self.cfg.n_vocab], np.int32)
+        self.backend._check(bk.lib().oasr_b200_whisper_generate(
+            self.handle, n_utts, self._prompt.ctypes.data, len(self._prompt), n_new, EOT, 0, tokens_dev.data_ptr(), 1))
+
     def transcribe(self, clips, n_new: int = 224, prompt=None, stop_at_eot: bool = False) -> np.ndarray:
         prompt = np.ascontiguousarray(prompt if prompt is not None else PROMPT[self.cfg.n_vocab], np.int32)
         pcm, ns = self._pcm(clips)
