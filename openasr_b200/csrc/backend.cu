@@ -133,6 +133,7 @@ int oasr_b200_init(int32_t ordinal, oasr_backend **out) {
     be->n_weights = 0;
     be->scratch = nullptr;
     be->scratch_bytes = 0;
+    be->pdl = false;
     int st = OASR_STATUS_SUCCESS;
     std::vector<uint16_t> gelu;
     build_gelu_table(gelu);

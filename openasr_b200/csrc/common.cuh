@@ -7,6 +7,7 @@
 
 #include <atomic>
 #include <string>
+#include <utility>
 
 #include "../../include/oasr_b200.h"
 
@@ -68,6 +69,7 @@ struct oasr_backend {
     uint64_t weight_bytes;
     int64_t n_weights;
     std::string last_error;
+    bool pdl;  // launch with programmatic stream serialization (dependent kernels overlap)
 };
 
 #define OASR_CUDA_TRY(be, expr)                                                          \
@@ -81,6 +83,33 @@ int oasr_internal_fail(oasr_backend *be, int status, const std::string &msg);
 int oasr_internal_precheck(oasr_backend *be);  // poison / abort check before enqueueing
 int oasr_internal_launch_check(oasr_backend *be, const char *what);
 void *oasr_internal_scratch(oasr_backend *be, size_t bytes, int *status);
+
+// ---- programmatic dependent launch ----------------------------------------------------
+// A kernel launched with PDL may start while its predecessor in the stream is
+// still running: it must call griddep_wait() before reading anything the
+// predecessor writes (and before writing anything the predecessor reads).
+// Work that touches neither (e.g. streaming constant weights into registers)
+// can precede the wait.  Both instructions are no-ops for a normal launch.
+static __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+static __device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_k(oasr_backend *be, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                            Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = be->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = be->pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ---- device helpers --------------------------------------------------------------
 static __device__ __forceinline__ float warp_sum(float v) {

@@ -113,6 +113,8 @@ __global__ void resid_norm_quant_kernel(float *x, const float *add, const float 
                                         int family) {
     extern __shared__ float srow[];
     __shared__ double sh_d[32];
+    griddep_launch_dependents();
+    griddep_wait();
     const int64_t r = blockIdx.x;
     float *xr = x + r * n;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -164,6 +166,8 @@ __global__ void resid_norm_quant_kernel(float *x, const float *add, const float 
 __global__ void bias_gelu_quant_kernel(const float *x, const float *bias, int n, const uint16_t *tab, float *out_f32,
                                        ActPlanes q, int family) {
     extern __shared__ float srow[];
+    griddep_launch_dependents();
+    griddep_wait();
     const int64_t r = blockIdx.x;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         float v = x[r * n + i];
@@ -179,6 +183,8 @@ __global__ void bias_gelu_quant_kernel(const float *x, const float *bias, int n,
 // y = silu(g) * u (Qwen SwiGLU: ggml_silu then ggml_mul) -> quantized planes
 __global__ void swiglu_quant_kernel(const float *gu, int n, int64_t gu_ld, float *out_f32, ActPlanes q, int family) {
     extern __shared__ float srow[];
+    griddep_launch_dependents();
+    griddep_wait();
     const int64_t r = blockIdx.x;
     const float *g = gu + r * gu_ld, *u = g + n;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -195,6 +201,8 @@ __global__ void swiglu_quant_kernel(const float *gu, int n, int64_t gu_ld, float
 __global__ void qkv_split_kv_write_kernel(const float *qkv, const float *bias3, int d, float *q_out, __half *kc,
                                           __half *vc, int64_t cache_seq_stride, const int *pos_dev, int *err,
                                           int max_pos) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int b = blockIdx.x;
     const int pos = *pos_dev;
     if (pos < 0 || pos >= max_pos) {
@@ -214,6 +222,8 @@ __global__ void qkv_split_kv_write_kernel(const float *qkv, const float *bias3, 
 // x[b] = dequant(tok_emb Q8_0 row tokens[b]) + pos_emb[*pos]  (ggml_get_rows + ggml_add)
 __global__ void embed_q8_0_kernel(const uint8_t *qs, const uint16_t *dsc, int d, int vocab, const int *tokens,
                                   const float *pos_emb, const int *pos_dev, int max_pos, float *x, int *err) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int b = blockIdx.x;
     const int tok = tokens[b], pos = pos_dev ? *pos_dev : 0;
     if (tok < 0 || tok >= vocab || pos < 0 || pos >= max_pos) {
@@ -228,6 +238,8 @@ __global__ void embed_q8_0_kernel(const uint8_t *qs, const uint16_t *dsc, int d,
 
 // x[r][i] += bias[i] (+ add[r][i])
 __global__ void add_rows_kernel(float *x, const float *bias, const float *add, int64_t rows, int n) {
+    griddep_launch_dependents();
+    griddep_wait();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * n; i += (int64_t)gridDim.x * blockDim.x) {
         float v = x[i];
         if (bias) v = __fadd_rn(v, bias[i % n]);
@@ -239,6 +251,8 @@ __global__ void add_rows_kernel(float *x, const float *bias, const float *add, i
 // dst[r][c] = fp16(src[r][c] (+ bias[c])), r < rows, c < cols; zero for c in [cols, dst_ld)
 __global__ void cast_f16_kernel(const float *src, int64_t src_ld, const float *bias, int64_t rows, int cols,
                                 __half *dst, int64_t dst_ld) {
+    griddep_launch_dependents();
+    griddep_wait();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * dst_ld; i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = i / dst_ld;
         const int c = (int)(i % dst_ld);
@@ -357,8 +371,9 @@ int launch_resid_norm_quant(oasr_backend *be, float *x, const float *add, const 
                             const ActPlanes *q, int family) {
     ActPlanes qq{};
     if (q) qq = *q;
-    resid_norm_quant_kernel<<<(unsigned)rows, 256, n * sizeof(float), be->stream>>>(x, add, add_bias, n, eps, rms ? 1 : 0,
-                                                                                     gamma, beta, out_f32, qq, family);
+    const cudaError_t e = launch_k(be, resid_norm_quant_kernel, dim3((unsigned)rows), dim3(256), n * sizeof(float), x, add,
+                                   add_bias, n, eps, rms ? 1 : 0, gamma, beta, out_f32, qq, family);
+    if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "resid_norm_quant launch", __LINE__);
     return oasr_internal_launch_check(be, "resid_norm_quant");
 }
 
@@ -366,8 +381,9 @@ int launch_bias_gelu_quant(oasr_backend *be, const float *x, const float *bias, 
                            const ActPlanes *q, int family) {
     ActPlanes qq{};
     if (q) qq = *q;
-    bias_gelu_quant_kernel<<<(unsigned)rows, 256, n * sizeof(float), be->stream>>>(x, bias, n, be->gelu_table, out_f32,
-                                                                                    qq, family);
+    const cudaError_t e = launch_k(be, bias_gelu_quant_kernel, dim3((unsigned)rows), dim3(256), n * sizeof(float), x, bias,
+                                   n, (const uint16_t *)be->gelu_table, out_f32, qq, family);
+    if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "bias_gelu_quant launch", __LINE__);
     return oasr_internal_launch_check(be, "bias_gelu_quant");
 }
 
@@ -375,21 +391,26 @@ int launch_swiglu_quant(oasr_backend *be, const float *gu, int64_t rows, int n, 
                         const ActPlanes *q, int family) {
     ActPlanes qq{};
     if (q) qq = *q;
-    swiglu_quant_kernel<<<(unsigned)rows, 256, n * sizeof(float), be->stream>>>(gu, n, gu_ld, out_f32, qq, family);
+    const cudaError_t e = launch_k(be, swiglu_quant_kernel, dim3((unsigned)rows), dim3(256), n * sizeof(float), gu, n,
+                                   gu_ld, out_f32, qq, family);
+    if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "swiglu_quant launch", __LINE__);
     return oasr_internal_launch_check(be, "swiglu_quant");
 }
 
 int launch_qkv_split_kv_write(oasr_backend *be, const float *qkv, const float *bias3, int B, int d, float *q_out,
                               __half *kc, __half *vc, int64_t cache_seq_stride, const int *pos_dev, int max_pos) {
-    qkv_split_kv_write_kernel<<<B, 256, 0, be->stream>>>(qkv, bias3, d, q_out, kc, vc, cache_seq_stride, pos_dev,
-                                                         be->err_word, max_pos);
+    const cudaError_t e = launch_k(be, qkv_split_kv_write_kernel, dim3(B), dim3(256), 0, qkv, bias3, d, q_out, kc, vc,
+                                   cache_seq_stride, pos_dev, be->err_word, max_pos);
+    if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "qkv_split launch", __LINE__);
     return oasr_internal_launch_check(be, "qkv_split_kv_write");
 }
 
 int launch_embed_q8_0(oasr_backend *be, const oasr_weight *emb, const int *tokens, int B, const float *pos_emb,
                       const int *pos_dev, int max_pos, float *x) {
-    embed_q8_0_kernel<<<B, 256, 0, be->stream>>>(emb->qs, emb->d, (int)emb->ne[0], (int)emb->ne[1], tokens, pos_emb,
-                                                 pos_dev, max_pos, x, be->err_word);
+    const cudaError_t e = launch_k(be, embed_q8_0_kernel, dim3(B), dim3(256), 0, (const uint8_t *)emb->qs,
+                                   (const uint16_t *)emb->d, (int)emb->ne[0], (int)emb->ne[1], tokens, pos_emb, pos_dev,
+                                   max_pos, x, be->err_word);
+    if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "embed launch", __LINE__);
     return oasr_internal_launch_check(be, "embed_q8_0");
 }
 

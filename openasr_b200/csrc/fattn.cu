@@ -66,6 +66,8 @@ static __device__ __forceinline__ void load8(const char *p, float (&out)[8]) {
 
 template <int D, int QT, bool F16>
 __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
+    griddep_launch_dependents();
+    griddep_wait();
     constexpr int LPP = D / 8;        // lanes per KV position
     constexpr int PPW = 32 / LPP;     // positions per warp step
     constexpr int ES = F16 ? 2 : 4;   // element size
@@ -270,12 +272,12 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
 }
 
 template <int D, bool F16>
-static void launch_fa_d(const FaArgs &a, int QT, dim3 grid, cudaStream_t st) {
+static cudaError_t launch_fa_d(oasr_backend *be, const FaArgs &a, int QT, dim3 grid) {
     switch (QT) {
-    case 1: fattn_split_kernel<D, 1, F16><<<grid, 128, 0, st>>>(a); break;
-    case 2: fattn_split_kernel<D, 2, F16><<<grid, 128, 0, st>>>(a); break;
-    case 4: fattn_split_kernel<D, 4, F16><<<grid, 128, 0, st>>>(a); break;
-    default: fattn_split_kernel<D, 8, F16><<<grid, 128, 0, st>>>(a); break;
+    case 1: return launch_k(be, fattn_split_kernel<D, 1, F16>, grid, dim3(128), 0, a);
+    case 2: return launch_k(be, fattn_split_kernel<D, 2, F16>, grid, dim3(128), 0, a);
+    case 4: return launch_k(be, fattn_split_kernel<D, 4, F16>, grid, dim3(128), 0, a);
+    default: return launch_k(be, fattn_split_kernel<D, 8, F16>, grid, dim3(128), 0, a);
     }
 }
 
@@ -337,13 +339,10 @@ int launch_flash_attn_ex(oasr_backend *be, const oasr_tensor *q, const oasr_tens
     if (groups > 0x7fffffffLL) return oasr_internal_fail(be, OASR_STATUS_FAILED, "flash_attn: grid too large");
     dim3 grid((unsigned)groups, n_splits);
     const bool f16 = k->type == OASR_TYPE_F16;
-    if (D == 64) {
-        if (f16) launch_fa_d<64, true>(a, QT, grid, be->stream);
-        else launch_fa_d<64, false>(a, QT, grid, be->stream);
-    } else {
-        if (f16) launch_fa_d<128, true>(a, QT, grid, be->stream);
-        else launch_fa_d<128, false>(a, QT, grid, be->stream);
-    }
+    cudaError_t e;
+    if (D == 64) e = f16 ? launch_fa_d<64, true>(be, a, QT, grid) : launch_fa_d<64, false>(be, a, QT, grid);
+    else e = f16 ? launch_fa_d<128, true>(be, a, QT, grid) : launch_fa_d<128, false>(be, a, QT, grid);
+    if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "flash_attn launch", __LINE__);
     return oasr_internal_launch_check(be, "flash_attn");
 }
 

@@ -49,10 +49,10 @@ __global__ void __launch_bounds__(128, 3)
     // every lane runs the same trip count (shuffles below use the full warp);
     // items past the end of the row contribute zero
     const int nit_pad = (nitems + lpr - 1) & ~(lpr - 1);
-    for (int it = j; it < nit_pad; it += lpr) {
+    int4 w0[RP], w1[RP];
+    float dw[RP];
+    auto load_w = [&](int it) {
         const bool itv = it < nitems;
-        int4 w0[RP], w1[RP];
-        float dw[RP];
 #pragma unroll
         for (int p = 0; p < RP; ++p) {
             const int64_t row = row0 + (int64_t)p * rpp;
@@ -66,6 +66,15 @@ __global__ void __launch_bounds__(128, 3)
                 dw[p] = 0.0f;
             }
         }
+    };
+    // the weights do not depend on the previous kernel: start streaming them before
+    // waiting for the activations (programmatic dependent launch)
+    griddep_launch_dependents();
+    load_w(j);
+    griddep_wait();
+    for (int it = j; it < nit_pad; it += lpr) {
+        const bool itv = it < nitems;
+        if (it != j) load_w(it);
 #pragma unroll
         for (int m = 0; m < M; ++m) {
             const int itc = itv ? it : 0;
@@ -145,6 +154,21 @@ __global__ void __launch_bounds__(128, 3)
     for (int i = 0; i < RP * M; ++i) acc[i] = 0.0f;
 
     const int nit_pad = (nitems + lpr - 1) & ~(lpr - 1);
+    // pull the first item's weight lines towards L2 before waiting for the
+    // activations (programmatic dependent launch); holding them in registers
+    // across the wait would spill at RP = 4
+    griddep_launch_dependents();
+    if (j < nitems) {
+#pragma unroll
+        for (int p = 0; p < RP; ++p) {
+            const int64_t row = row0 + (int64_t)p * rpp;
+            if (row < N) {
+                const uint8_t *wp = w + row * w_ld + (int64_t)(j >> 2) * 144 + 32 * (j & 3);
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(wp + 16));
+            }
+        }
+    }
+    griddep_wait();
     for (int it = j; it < nit_pad; it += lpr) {
         const bool itv = it < nitems;
         const int sb = itv ? it >> 2 : 0, c = it & 3;
@@ -281,50 +305,55 @@ static int pick_rp(int64_t N, int lg, int sm_count) {
 }
 
 template <int M, int RP>
-static void launch_q8_rp(const oasr_weight *w, int64_t slice, const ActPlanes &a, int K, float *y, int64_t y_ld,
+static void launch_q8_rp(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int K, float *y, int64_t y_ld,
                          cudaStream_t st, bool q4, int lg) {
     const int64_t N = w->ne[1];
     const int rows_per_cta = 4 * (32 >> lg) * RP;
     const unsigned grid = (unsigned)((N + rows_per_cta - 1) / rows_per_cta);
     const uint8_t *wqs = w->qs + slice * N * w->qs_row_bytes;
     const uint16_t *wd = w->d + slice * N * w->d_row_elems;
+    (void)st;
     if (q4)
-        mmv_q8_kernel<M, RP, true><<<grid, 128, 0, st>>>(wqs, wd, w->qs_row_bytes, w->d_row_elems, N, K / 32, lg,
-                                                         a.qs, a.d, K, y, y_ld);
+        launch_k(be, mmv_q8_kernel<M, RP, true>, dim3(grid), dim3(128), 0, (const uint8_t *)wqs, (const uint16_t *)wd,
+                 (int64_t)w->qs_row_bytes, (int64_t)w->d_row_elems, N, K / 32, lg, (const int8_t *)a.qs,
+                 (const float *)a.d, K, y, y_ld);
     else
-        mmv_q8_kernel<M, RP, false><<<grid, 128, 0, st>>>(wqs, wd, w->qs_row_bytes, w->d_row_elems, N, K / 32, lg,
-                                                          a.qs, a.d, K, y, y_ld);
+        launch_k(be, mmv_q8_kernel<M, RP, false>, dim3(grid), dim3(128), 0, (const uint8_t *)wqs, (const uint16_t *)wd,
+                 (int64_t)w->qs_row_bytes, (int64_t)w->d_row_elems, N, K / 32, lg, (const int8_t *)a.qs,
+                 (const float *)a.d, K, y, y_ld);
 }
 
 template <int M>
-static void launch_q8(const oasr_weight *w, int64_t slice, const ActPlanes &a, int K, float *y, int64_t y_ld,
+static void launch_q8(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int K, float *y, int64_t y_ld,
                       cudaStream_t st, bool q4, int sm_count) {
     const int lg = pick_lpr_log2(K / 32);
     switch (pick_rp(w->ne[1], lg, sm_count)) {
-    case 4: launch_q8_rp<M, 4>(w, slice, a, K, y, y_ld, st, q4, lg); break;
-    case 2: launch_q8_rp<M, 2>(w, slice, a, K, y, y_ld, st, q4, lg); break;
-    default: launch_q8_rp<M, 1>(w, slice, a, K, y, y_ld, st, q4, lg); break;
+    case 4: launch_q8_rp<M, 4>(be, w, slice, a, K, y, y_ld, st, q4, lg); break;
+    case 2: launch_q8_rp<M, 2>(be, w, slice, a, K, y, y_ld, st, q4, lg); break;
+    default: launch_q8_rp<M, 1>(be, w, slice, a, K, y, y_ld, st, q4, lg); break;
     }
 }
 
 template <int M, int RP>
-static void launch_q4k_rp(const oasr_weight *w, int64_t slice, const ActPlanes &a, int K, float *y, int64_t y_ld,
+static void launch_q4k_rp(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int K, float *y, int64_t y_ld,
                           cudaStream_t st, int lg) {
     const int64_t N = w->ne[1];
     const int rows_per_cta = 4 * (32 >> lg) * RP;
     const unsigned grid = (unsigned)((N + rows_per_cta - 1) / rows_per_cta);
-    mmv_q4k_kernel<M, RP><<<grid, 128, 0, st>>>(w->qs + slice * N * w->qs_row_bytes, w->qs_row_bytes, N, K / 64, lg,
-                                                a.qs, a.d, a.bs16, K, y, y_ld);
+    (void)st;
+    launch_k(be, mmv_q4k_kernel<M, RP>, dim3(grid), dim3(128), 0, (const uint8_t *)(w->qs + slice * N * w->qs_row_bytes),
+             (int64_t)w->qs_row_bytes, N, K / 64, lg, (const int8_t *)a.qs, (const float *)a.d, (const int16_t *)a.bs16,
+             K, y, y_ld);
 }
 
 template <int M>
-static void launch_q4k(const oasr_weight *w, int64_t slice, const ActPlanes &a, int K, float *y, int64_t y_ld,
+static void launch_q4k(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int K, float *y, int64_t y_ld,
                        cudaStream_t st, int sm_count) {
     const int lg = std::max(2, pick_lpr_log2(K / 64));  // the 4 items of a super-block share aligned lanes
     switch (pick_rp(w->ne[1], lg, sm_count)) {
-    case 4: launch_q4k_rp<M, 4>(w, slice, a, K, y, y_ld, st, lg); break;
-    case 2: launch_q4k_rp<M, 2>(w, slice, a, K, y, y_ld, st, lg); break;
-    default: launch_q4k_rp<M, 1>(w, slice, a, K, y, y_ld, st, lg); break;
+    case 4: launch_q4k_rp<M, 4>(be, w, slice, a, K, y, y_ld, st, lg); break;
+    case 2: launch_q4k_rp<M, 2>(be, w, slice, a, K, y, y_ld, st, lg); break;
+    default: launch_q4k_rp<M, 1>(be, w, slice, a, K, y, y_ld, st, lg); break;
     }
 }
 
@@ -333,26 +362,26 @@ int launch_mmv_quant(oasr_backend *be, const oasr_weight *w, int64_t slice, cons
     cudaStream_t st = be->stream;
     if (w->type == OASR_TYPE_Q4_K) {
         switch (M) {
-        case 1: launch_q4k<1>(w, slice, a, K, y, y_ld, st, be->sm_count); break;
-        case 2: launch_q4k<2>(w, slice, a, K, y, y_ld, st, be->sm_count); break;
-        case 3: launch_q4k<3>(w, slice, a, K, y, y_ld, st, be->sm_count); break;
-        case 4: launch_q4k<4>(w, slice, a, K, y, y_ld, st, be->sm_count); break;
-        case 5: launch_q4k<5>(w, slice, a, K, y, y_ld, st, be->sm_count); break;
-        case 6: launch_q4k<6>(w, slice, a, K, y, y_ld, st, be->sm_count); break;
-        case 7: launch_q4k<7>(w, slice, a, K, y, y_ld, st, be->sm_count); break;
-        default: launch_q4k<8>(w, slice, a, K, y, y_ld, st, be->sm_count); break;
+        case 1: launch_q4k<1>(be, w, slice, a, K, y, y_ld, st, be->sm_count); break;
+        case 2: launch_q4k<2>(be, w, slice, a, K, y, y_ld, st, be->sm_count); break;
+        case 3: launch_q4k<3>(be, w, slice, a, K, y, y_ld, st, be->sm_count); break;
+        case 4: launch_q4k<4>(be, w, slice, a, K, y, y_ld, st, be->sm_count); break;
+        case 5: launch_q4k<5>(be, w, slice, a, K, y, y_ld, st, be->sm_count); break;
+        case 6: launch_q4k<6>(be, w, slice, a, K, y, y_ld, st, be->sm_count); break;
+        case 7: launch_q4k<7>(be, w, slice, a, K, y, y_ld, st, be->sm_count); break;
+        default: launch_q4k<8>(be, w, slice, a, K, y, y_ld, st, be->sm_count); break;
         }
     } else {
         const bool q4 = w->type == OASR_TYPE_Q4_0;
         switch (M) {
-        case 1: launch_q8<1>(w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
-        case 2: launch_q8<2>(w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
-        case 3: launch_q8<3>(w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
-        case 4: launch_q8<4>(w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
-        case 5: launch_q8<5>(w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
-        case 6: launch_q8<6>(w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
-        case 7: launch_q8<7>(w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
-        default: launch_q8<8>(w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
+        case 1: launch_q8<1>(be, w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
+        case 2: launch_q8<2>(be, w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
+        case 3: launch_q8<3>(be, w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
+        case 4: launch_q8<4>(be, w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
+        case 5: launch_q8<5>(be, w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
+        case 6: launch_q8<6>(be, w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
+        case 7: launch_q8<7>(be, w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
+        default: launch_q8<8>(be, w, slice, a, K, y, y_ld, st, q4, be->sm_count); break;
         }
     }
     return oasr_internal_launch_check(be, "mmv_quant");

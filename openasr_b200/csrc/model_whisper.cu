@@ -291,10 +291,12 @@ int run_decode_step(oasr_whisper *m, int n) {
 }
 
 __global__ void fill_tokens_kernel(int *tokens, int n, int value) {
+    griddep_wait();
     if (threadIdx.x < n) tokens[threadIdx.x] = value;
 }
 
 __global__ void advance_kernel(const int *tokens, int *pos, int *nkv, int *history, int n, int P) {
+    griddep_wait();
     const int b = threadIdx.x;
     const int p = *pos;
     if (b < n && p + 1 < P) history[b * P + p + 1] = tokens[b];
@@ -314,8 +316,16 @@ int decode_step_graph(oasr_whisper *m, int n) {
     if (!m->graph) {
         cudaGraph_t g;
         OASR_CUDA_TRY(be, cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+        // inside the step graph every kernel waits on its predecessor with griddepcontrol,
+        // so successive launches overlap their prologues (programmatic dependent launch)
+        be->pdl = true;
         int st = run_decode_step(m, n);
-        if (st == OASR_STATUS_SUCCESS) advance_kernel<<<1, 32, 0, m->stream>>>(m->tokens, m->pos, m->nkv, m->history, n, m->cfg.n_text_ctx);
+        if (st == OASR_STATUS_SUCCESS) {
+            const cudaError_t le = launch_k(be, advance_kernel, dim3(1), dim3(32), 0, (const int *)m->tokens, m->pos,
+                                            m->nkv, m->history, n, (int)m->cfg.n_text_ctx);
+            if (le != cudaSuccess) st = oasr_internal_cuda_fail(be, le, "advance launch", __LINE__);
+        }
+        be->pdl = false;
         cudaError_t e = cudaStreamEndCapture(m->stream, &g);
         if (st) return st;
         if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "cudaStreamEndCapture", __LINE__);

@@ -46,6 +46,8 @@ __global__ void set_rows_kernel(char *dst, int64_t d_nb1, int64_t d_nb2, int64_t
 
 // ---- first-max argmax ---------------------------------------------------------------------
 __global__ void argmax_first_kernel(const char *x, int64_t nb1, int64_t n, int32_t *out) {
+    griddep_launch_dependents();
+    griddep_wait();
     const float *row = reinterpret_cast<const float *>(x + blockIdx.x * nb1);
     float best = -INFINITY;
     int64_t bi = -1;
@@ -81,7 +83,8 @@ __global__ void argmax_first_kernel(const char *x, int64_t nb1, int64_t n, int32
 
 namespace oasr {
 int launch_argmax_rows(oasr_backend *be, const float *x, int64_t ld, int64_t n, int rows, int32_t *out) {
-    argmax_first_kernel<<<(unsigned)rows, 1024, 0, be->stream>>>((const char *)x, ld * 4, n, out);
+    const cudaError_t e = launch_k(be, argmax_first_kernel, dim3((unsigned)rows), dim3(1024), 0, (const char *)x, ld * 4, n, out);
+    if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "argmax launch", __LINE__);
     return oasr_internal_launch_check(be, "argmax_first");
 }
 

@@ -35,6 +35,8 @@ __device__ __forceinline__ float load_act(const char *row, int k) {
 template <bool F16>
 __global__ void __launch_bounds__(256) quantize_q8_0_kernel(ActRows xr, int K, int64_t R, int8_t *__restrict__ qs,
                                                             float *__restrict__ dsc) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int64_t groups_per_row = K / 4;
     const int64_t total = R * groups_per_row;
     for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total; g += (int64_t)gridDim.x * blockDim.x) {
@@ -68,6 +70,8 @@ template <bool F16>
 __global__ void __launch_bounds__(256) quantize_q8_K_kernel(ActRows xr, int K, int64_t R, int8_t *__restrict__ qs,
                                                             float *__restrict__ dsc, int16_t *__restrict__ bs16,
                                                             __half *__restrict__ qs16, __half *__restrict__ bs16h) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int lane = threadIdx.x & 31;
     const int64_t nsb = K / 256;
     const int64_t total = R * nsb;
@@ -138,17 +142,16 @@ int launch_quantize_act(oasr_backend *be, const oasr_tensor *x, int family, cons
     if (family == FAMILY_Q8_0) {
         const int64_t work = R * (K / 4);
         const int blocks = (int)std::min<int64_t>((work + threads - 1) / threads, (int64_t)be->sm_count * 16);
-        if (f16)
-            quantize_q8_0_kernel<true><<<blocks, threads, 0, be->stream>>>(xr, K, R, p.qs, p.d);
-        else
-            quantize_q8_0_kernel<false><<<blocks, threads, 0, be->stream>>>(xr, K, R, p.qs, p.d);
+        const cudaError_t e = f16 ? launch_k(be, quantize_q8_0_kernel<true>, dim3(blocks), dim3(threads), 0, xr, K, R, p.qs, p.d)
+                                  : launch_k(be, quantize_q8_0_kernel<false>, dim3(blocks), dim3(threads), 0, xr, K, R, p.qs, p.d);
+        if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "quantize_q8_0 launch", __LINE__);
     } else {
         const int64_t work = R * (K / 256) * 32;
         const int blocks = (int)std::min<int64_t>((work + threads - 1) / threads, (int64_t)be->sm_count * 16);
-        if (f16)
-            quantize_q8_K_kernel<true><<<blocks, threads, 0, be->stream>>>(xr, K, R, p.qs, p.d, p.bs16, p.qs16, p.bs16h);
-        else
-            quantize_q8_K_kernel<false><<<blocks, threads, 0, be->stream>>>(xr, K, R, p.qs, p.d, p.bs16, p.qs16, p.bs16h);
+        const cudaError_t e =
+            f16 ? launch_k(be, quantize_q8_K_kernel<true>, dim3(blocks), dim3(threads), 0, xr, K, R, p.qs, p.d, p.bs16, p.qs16, p.bs16h)
+                : launch_k(be, quantize_q8_K_kernel<false>, dim3(blocks), dim3(threads), 0, xr, K, R, p.qs, p.d, p.bs16, p.qs16, p.bs16h);
+        if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "quantize_q8_K launch", __LINE__);
     }
     return oasr_internal_launch_check(be, "quantize_act");
 }
