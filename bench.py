@@ -309,6 +309,24 @@ N_NEW = 224
 UTT_SEED = 0x0A5A0005
 
 
+def reduce_over_ranks(dev_s: float, e2e_s: float, audio_s: float, device) -> tuple[float, float, float]:
+    """Whole-job figures from every rank's own: the slowest rank's device and
+    end-to-end times (max) and the audio seconds all ranks processed (sum).
+    Every rank must call it (two collectives, same order); a single process
+    returns its inputs."""
+    import torch
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return dev_s, e2e_s, audio_s
+    t = torch.tensor([dev_s, e2e_s, audio_s], dtype=torch.float64, device=device)
+    mx = t.clone()
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    tot = t.clone()
+    dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+    return float(mx[0]), float(mx[1]), float(tot[2])
+
+
 def utterance_lengths(step: int, rank: int, n: int = 8) -> list[int]:
     """utterance lengths uniform in 5-30 s (seeded), 16 kHz samples."""
     rng = np.random.default_rng([UTT_SEED, step, rank])
@@ -369,8 +387,6 @@ def run_reference(args) -> None:
         return
     # the reference's own ggml CPU path is unbuildable here (empty ggml submodule,
     # no Rust toolchain): its CPU restatement in oracle/ is timed instead
-    for _ in range(max(0, args.warmup - 3)):
-        pass
     cb = rtfx_cpu_baseline()
     v = cb["value"]
     print(json.dumps({
@@ -488,13 +504,7 @@ def run_b200(args) -> None:
         e2e_s = h0.elapsed_time(h1) / 1e3
         fa = _fa_roofline(be, torch, stream)
     timed_audio = sum(audio_s[args.warmup:])
-    t = torch.tensor([dev_s, e2e_s, timed_audio], device="cuda", dtype=torch.float64)
-    if world > 1:
-        mx = t.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        tot = t.clone()
-        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
-        dev_s, e2e_s, timed_audio = float(mx[0]), float(mx[1]), float(tot[2])
+    dev_s, e2e_s, timed_audio = reduce_over_ranks(dev_s, e2e_s, timed_audio, "cuda")
     if rank == 0:
         peak, peak_kind = measured_peak_hbm()
         achieved = fa["bytes"] / (fa["us"] * 1e-6) / 1e9
@@ -531,13 +541,131 @@ def run_b200(args) -> None:
 
 
 def ncu_traffic_fa() -> float | None:
-    p = os.path.join(ROOT, "profiles", "fattn_split_cross_b8.json")
-    if os.path.exists(p):
-        try:
-            return float(json.load(open(p))["dram_bytes_per_launch"])
-        except (KeyError, ValueError):
-            return None
+    """dram read + write bytes of one cross-attention launch, from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "fattn_split_cross_b8.md")
+    try:
+        for line in open(p):
+            if line.startswith("| dram_bytes_per_launch |"):
+                return float(line.split("|")[2])
+    except (OSError, ValueError):
+        return None
     return None
+
+
+def run_kernels(args) -> None:
+    """Per-kernel roofline table at the RTFx workload's own shapes (whisper-large-v3,
+    batch 8 per GPU), each op timed alone with CUDA events on the launching stream:
+    decode GEMVs (Q4_K, M = 8, rotated over 12 layers' weights = 155 MB > L2), the
+    Q8_0 logits head (two copies, 141 MB), cross- and self-attention flash-decode,
+    the encoder's Q4_K tensor-core GEMMs (M = 12000) and the encoder flash attention
+    (8 x 20 heads x 1500 x 1500).  Also the small, fixed command the committed ncu
+    captures use."""
+    import torch
+
+    import openasr_b200 as ob
+
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream()
+    be = ob.Backend(0)
+    be.set_stream(stream)
+    peak_hbm, hbm_kind = measured_peak_hbm()
+    peak_tc, tc_kind = measured_peak_tensor()
+    B, d, ffn, T, H = 8, 1280, 5120, 1500, 20
+    rows = []
+
+    def timed(fn, iters):
+        for i in range(3):
+            fn(i)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        stream.synchronize()
+        e0.record(stream)
+        for i in range(iters):
+            fn(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / iters * 1e3
+
+    def add(name, shape, us, amount, unit):
+        if unit == "GB/s":
+            ach, pk, kind = amount / (us * 1e-6) / 1e9, peak_hbm, hbm_kind
+        else:
+            ach, pk, kind = amount / (us * 1e-6) / 1e12, peak_tc, tc_kind
+        rows.append({"kernel": name, "shape": shape, "us": round(us, 2), "achieved": round(ach, 1), "unit": unit,
+                     "peak": pk, "peak_kind": kind, "frac": round(ach / pk, 4)})
+
+    with torch.cuda.stream(stream):
+        # decode GEMVs: one weight per role and layer, activations pre-quantized (q8_K)
+        n_rot = 12
+        roles = [("qkv", d, 3 * d), ("o", d, d), ("cross_q", d, d), ("cross_o", d, d), ("fc1", d, ffn),
+                 ("fc2", ffn, d)]
+        for role, K, N in roles:
+            ws = [be.upload_weight(ob.quantize(ob.Q4_K, ob.synth_normal(0xD0 + 97 * j + N + K, N * K, 0.0, 0.02)
+                                               .reshape(N, K)), ob.Q4_K, [K, N]) for j in range(n_rot)]
+            x = torch.randn(B, K, device="cuda")
+            qa = torch.empty(be.act_bytes(ob.Q4_K, K, B), dtype=torch.uint8, device="cuda")
+            be.quantize_act(ob.Q4_K, x, qa)
+            y = torch.empty(B, N, device="cuda")
+            us = timed(lambda i: be.mul_mat_qact(ws[i % n_rot], qa, B, y), 48)
+            add("mmv_q4k_kernel", f"{role} Q4_K N={N} K={K} M={B}", us, N * K * 144 / 256 + B * K + B * N * 4, "GB/s")
+            del ws
+        # logits head (Q8_0, tied token embedding)
+        V = 51866
+        lm = [be.upload_weight(ob.quantize(ob.Q8_0, ob.synth_normal(0xE0 + j, V * d, 0.0, 0.02).reshape(V, d)),
+                               ob.Q8_0, [d, V]) for j in range(2)]
+        x = torch.randn(B, d, device="cuda")
+        qa = torch.empty(be.act_bytes(ob.Q8_0, d, B), dtype=torch.uint8, device="cuda")
+        be.quantize_act(ob.Q8_0, x, qa)
+        y = torch.empty(B, V, device="cuda")
+        us = timed(lambda i: be.mul_mat_qact(lm[i % 2], qa, B, y), 20)
+        add("mmv_q8_kernel", f"logits Q8_0 N={V} K={d} M={B}", us, V * d * 34 / 32 + B * d + B * V * 4, "GB/s")
+        del lm
+        # cross-attention flash-decode (the dominant decode kernel)
+        fa = _fa_roofline(be, torch, stream)
+        add("fattn_split_kernel", f"cross S={B} H={H} n_kv={T} D=64 f16 K/V", fa["us"], fa["bytes"], "GB/s")
+        # self-attention flash-decode at position 128 of the 448-slot cache
+        P, nkv = 448, 128
+        kc = torch.randn(B, P, d, device="cuda").half()
+        vc = torch.randn(B, P, d, device="cuda").half()
+        kv = kc[:, :nkv].reshape(B, nkv, H, 64).permute(0, 2, 1, 3)
+        vv = vc[:, :nkv].reshape(B, nkv, H, 64).permute(0, 2, 1, 3)
+        q = torch.randn(B, 1, H, 64, device="cuda").permute(0, 2, 1, 3)
+        o = torch.empty(B, 1, H, 64, device="cuda")
+        us = timed(lambda i: be.flash_attn_ext(q, kv, vv, None, 0.125, o), 50)
+        add("fattn_split_kernel", f"self S={B} H={H} n_kv={nkv} D=64 f16 K/V", us, 2 * B * nkv * d * 2 + 2 * B * d * 4,
+            "GB/s")
+        del kc, vc
+        # encoder GEMMs: Q4_K weights x q8_K activations on the tensor cores, M = 8 x 1500
+        Menc = B * T
+        for role, K, N in [("qkv", d, 3 * d), ("o", d, d), ("fc1", d, ffn), ("fc2", ffn, d)]:
+            w = be.upload_weight(ob.quantize(ob.Q4_K, ob.synth_normal(0xF0 + N + K, N * K, 0.0, 0.02).reshape(N, K)),
+                                 ob.Q4_K, [K, N])
+            x = torch.randn(Menc, K, device="cuda")
+            qa = torch.empty(be.act_bytes(ob.Q4_K, K, Menc), dtype=torch.uint8, device="cuda")
+            be.quantize_act(ob.Q4_K, x, qa)
+            y = torch.empty(Menc, N, device="cuda")
+            us = timed(lambda i: be.mul_mat_qact(w, qa, Menc, y), 10)
+            add("mmq_q4k_tc_kernel", f"encoder {role} Q4_K N={N} K={K} M={Menc}", us, 2.0 * Menc * N * K, "TFLOP/s")
+            del w, x, qa, y
+        # encoder self-attention: f16 pre-pass + tcgen05 flash attention
+        qkv = torch.randn(B, T, 3 * d, device="cuda")
+        qe = qkv[:, :, :d].reshape(B, T, H, 64).permute(0, 2, 1, 3)
+        ke = qkv[:, :, d:2 * d].reshape(B, T, H, 64).permute(0, 2, 1, 3).half()
+        ve = qkv[:, :, 2 * d:].reshape(B, T, H, 64).permute(0, 2, 1, 3).half()
+        oe = torch.empty(B, T, H, 64, device="cuda")
+        us = timed(lambda i: be.flash_attn_ext(qe, ke, ve, None, 0.125, oe), 10)
+        add("fa_prep_kernel+fattn_tc_kernel", f"encoder S={B} H={H} {T}x{T} D=64", us, 4.0 * B * H * T * T * 64,
+            "TFLOP/s")
+    print(json.dumps({"workload": "kernels", "n_gpus": 1, "kernels": rows}), flush=True)
+    be.close()
+
+
+def measured_peak_tensor() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        j = json.load(open(p))
+        return float(j["bf16_tflops"]), "measured (bf16 burst)"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
 
 
 def main() -> None:
@@ -546,12 +674,14 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["rtfx", "mulmat"], default="rtfx")
+    ap.add_argument("--workload", choices=["rtfx", "mulmat", "kernels"], default="rtfx")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.steps is None:
         args.steps = 8 if args.workload == "rtfx" else 20
-    if args.workload == "rtfx":
+    if args.workload == "kernels":
+        run_kernels(args)
+    elif args.workload == "rtfx":
         (run_reference if args.impl == "reference" else run_b200)(args)
     elif args.impl == "reference":
         run_reference_mulmat(args)
