@@ -182,6 +182,27 @@ int oasr_b200_flash_attn_ext(oasr_backend *be, const oasr_tensor *q, const oasr_
                              const oasr_tensor *v, const oasr_tensor *mask, float scale, float max_bias,
                              float logit_softcap, int32_t prec, oasr_tensor *dst);
 
+/* Allocation-free GGML_OP_FLASH_ATTN_EXT.  No reference counterpart: the
+ * reference has no entry point that promises to allocate nothing.  Same
+ * arguments, checks and results as oasr_b200_flash_attn_ext for every shape
+ * that call runs through its split-KV kernel (decode and short prefill); it
+ * always uses that kernel, never the tensor-core encoder path (whose staging
+ * copies need backend scratch).  The split-KV partials and tickets live in a
+ * file-scope device array of 4 MiB of partials and 1024 tickets per device;
+ * a shape that needs more fails with OASR_STATUS_FAILED and a message naming
+ * both sizes, and nothing is launched.  Calls neither allocate nor free device
+ * or host memory.
+ *  - The tickets must be zero when a launch starts: they are zero when the
+ *    module loads and every launch leaves them at zero.
+ *  - Calls that overlap on one device (two streams, two backends, or two
+ *    host threads without ordering) share that array and race: serialise them.
+ *  - The first call on a device looks the array's address up (which may load
+ *    the module); make it outside stream capture.  A first call during capture
+ *    is refused.  Later calls may be captured into CUDA graphs. */
+int oasr_b200_flash_attn_ext_static(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k,
+                                    const oasr_tensor *v, const oasr_tensor *mask, float scale, float max_bias,
+                                    float logit_softcap, int32_t prec, oasr_tensor *dst);
+
 /* GGML_OP_SET_ROWS (ggml_set_rows ffi.rs:884; cpu_graph.rs:4882): write f32 rows
  * of src [D, n, ne2, ne3] into dst (f16|f32) rows rows[i] (I32 or I64 [n]). */
 int oasr_b200_set_rows(oasr_backend *be, oasr_tensor *dst, const oasr_tensor *src, const oasr_tensor *rows);

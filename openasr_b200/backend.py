@@ -150,6 +150,7 @@ SIGNATURES = {
     "oasr_b200_quantize_act": ([_P, _I32, _TP, _P, _SZ], ctypes.c_int),
     "oasr_b200_mul_mat_qact": ([_P, _P, _P, _I64, _TP], ctypes.c_int),
     "oasr_b200_flash_attn_ext": ([_P, _TP, _TP, _TP, _TP, _F, _F, _F, _I32, _TP], ctypes.c_int),
+    "oasr_b200_flash_attn_ext_static": ([_P, _TP, _TP, _TP, _TP, _F, _F, _F, _I32, _TP], ctypes.c_int),
     "oasr_b200_set_rows": ([_P, _TP, _TP, _TP], ctypes.c_int),
     "oasr_b200_argmax_first": ([_P, _TP, _TP], ctypes.c_int),
     "oasr_b200_whisper_load": ([_P, ctypes.POINTER(OasrWhisperConfig), ctypes.POINTER(OasrNamedTensor), _I32,
@@ -381,6 +382,15 @@ class Backend:
                        prec: int = PREC_DEFAULT) -> None:
         md = describe(mask) if mask is not None else None
         self._check(lib().oasr_b200_flash_attn_ext(
+            self.handle, ctypes.byref(describe(q)), ctypes.byref(describe(k)), ctypes.byref(describe(v)),
+            ctypes.byref(md) if md is not None else None, scale, max_bias, logit_softcap, prec, ctypes.byref(describe(out))))
+
+    def flash_attn_ext_static(self, q, k, v, mask, scale: float, out, max_bias: float = 0.0,
+                              logit_softcap: float = 0.0, prec: int = PREC_DEFAULT) -> None:
+        """flash_attn_ext over file-scope device scratch: allocates nothing; overlapping
+        calls on one device race (see the C header)."""
+        md = describe(mask) if mask is not None else None
+        self._check(lib().oasr_b200_flash_attn_ext_static(
             self.handle, ctypes.byref(describe(q)), ctypes.byref(describe(k)), ctypes.byref(describe(v)),
             ctypes.byref(md) if md is not None else None, scale, max_bias, logit_softcap, prec, ctypes.byref(describe(out))))
 

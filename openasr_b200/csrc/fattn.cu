@@ -19,6 +19,9 @@
 // waiting) merges the partials and resets the ticket.
 #include <float.h>
 
+#include <mutex>
+#include <string>
+
 #include "kernels.cuh"
 
 namespace oasr {
@@ -286,10 +289,69 @@ int launch_flash_attn(oasr_backend *be, const oasr_tensor *q, const oasr_tensor 
     return launch_flash_attn_ex(be, q, k, v, mask, scale, dst, nullptr, nullptr);
 }
 
+// Split-KV scratch: `partials` of `partial_bytes` and `tickets` of `n_tickets` zeroed
+// counters.  NULL partials = take them from the backend's (growable) scratch.
+struct FaScratch {
+    float *partials;
+    size_t partial_bytes;
+    unsigned int *tickets;
+    int64_t n_tickets;
+};
+
+static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
+                                   const oasr_tensor *mask, float scale, oasr_tensor *dst, const float *q_bias,
+                                   const int *nkv_dev, const FaScratch *fixed);
+
 // q_bias: optional [H*D] f32 added to q; nkv_dev: optional device KV length (k->ne[1] is the maximum)
 int launch_flash_attn_ex(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
                          const oasr_tensor *mask, float scale, oasr_tensor *dst, const float *q_bias,
                          const int *nkv_dev) {
+    return launch_flash_attn_split(be, q, k, v, mask, scale, dst, q_bias, nkv_dev, nullptr);
+}
+
+// ---- allocation-free variant ------------------------------------------------------------
+// File-scope device scratch for oasr_b200_flash_attn_ext_static: one copy per device,
+// zero-initialised when the module loads.  The tickets must be zero when a launch
+// starts; the last CTA of each split group resets its ticket, so they stay zero from
+// one call to the next.  The partials need no initial value (every split writes its
+// own slot before the merge reads it).
+static __device__ __align__(256) float g_fa_static_partials[FA_STATIC_PARTIAL_BYTES / sizeof(float)];
+static __device__ __align__(256) unsigned int g_fa_static_tickets[FA_STATIC_TICKETS];
+
+int launch_flash_attn_static(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
+                             const oasr_tensor *mask, float scale, oasr_tensor *dst) {
+    // symbol addresses, looked up once per device (the lookup may load the module,
+    // so the first call on a device must not be inside a stream capture)
+    static std::mutex mu;
+    static void *partials[FA_STATIC_MAX_DEVICES] = {};
+    static void *tickets[FA_STATIC_MAX_DEVICES] = {};
+    if (be->device < 0 || be->device >= FA_STATIC_MAX_DEVICES)
+        return oasr_internal_fail(be, OASR_STATUS_FAILED, "flash_attn_ext_static: device ordinal out of range");
+    FaScratch fs;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!partials[be->device]) {
+            cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+            if (cudaStreamIsCapturing(be->stream, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+                return oasr_internal_fail(be, OASR_STATUS_FAILED,
+                                          "flash_attn_ext_static: first call on a device must precede stream capture");
+            void *p = nullptr, *t = nullptr;
+            OASR_CUDA_TRY(be, cudaGetSymbolAddress(&p, g_fa_static_partials));
+            OASR_CUDA_TRY(be, cudaGetSymbolAddress(&t, g_fa_static_tickets));
+            tickets[be->device] = t;
+            partials[be->device] = p;
+        }
+        fs.partials = (float *)partials[be->device];
+        fs.tickets = (unsigned int *)tickets[be->device];
+    }
+    fs.partial_bytes = FA_STATIC_PARTIAL_BYTES;
+    fs.n_tickets = FA_STATIC_TICKETS;
+    return launch_flash_attn_split(be, q, k, v, mask, scale, dst, nullptr, nullptr, &fs);
+}
+
+static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
+                                   const oasr_tensor *mask, float scale, oasr_tensor *dst, const float *q_bias,
+                                   const int *nkv_dev, const FaScratch *fixed) {
     FaArgs a;
     a.q_bias = q_bias;
     a.nkv_dev = nkv_dev;
@@ -329,14 +391,25 @@ int launch_flash_attn_ex(oasr_backend *be, const oasr_tensor *q, const oasr_tens
     a.n_splits = n_splits;
     a.kv_per_split = (a.NKV + n_splits - 1) / n_splits;
     a.partials = nullptr;
-    a.counters = be->counters;
-    if (n_splits > 1) {
-        int st = 0;
-        const size_t bytes = (size_t)a.S * a.H * a.NQ * n_splits * (D + 2) * sizeof(float);
-        a.partials = (float *)oasr_internal_scratch(be, bytes, &st);
-        if (st) return st;
-    }
+    a.counters = fixed ? fixed->tickets : be->counters;
     if (groups > 0x7fffffffLL) return oasr_internal_fail(be, OASR_STATUS_FAILED, "flash_attn: grid too large");
+    if (n_splits > 1) {
+        const size_t bytes = (size_t)a.S * a.H * a.NQ * n_splits * (D + 2) * sizeof(float);
+        if (fixed) {
+            if (bytes > fixed->partial_bytes || groups > fixed->n_tickets)
+                return oasr_internal_fail(
+                    be, OASR_STATUS_FAILED,
+                    "flash_attn_ext_static: split-KV partials need " + std::to_string(bytes) + " bytes and " +
+                        std::to_string(groups) + " tickets; the static scratch holds " +
+                        std::to_string(fixed->partial_bytes) + " bytes and " + std::to_string(fixed->n_tickets) +
+                        " tickets (use oasr_b200_flash_attn_ext)");
+            a.partials = fixed->partials;
+        } else {
+            int st = 0;
+            a.partials = (float *)oasr_internal_scratch(be, bytes, &st);
+            if (st) return st;
+        }
+    }
     dim3 grid((unsigned)groups, n_splits);
     const bool f16 = k->type == OASR_TYPE_F16;
     cudaError_t e;

@@ -87,5 +87,11 @@ int launch_flash_attn(oasr_backend *be, const oasr_tensor *q, const oasr_tensor 
 int launch_flash_attn_ex(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
                          const oasr_tensor *mask, float scale, oasr_tensor *dst, const float *q_bias,
                          const int *nkv_dev);
+// allocation-free split-KV attention over file-scope device scratch (fattn.cu)
+constexpr size_t FA_STATIC_PARTIAL_BYTES = (size_t)4 << 20;  // 4 MiB of split partials
+constexpr int64_t FA_STATIC_TICKETS = 1024;                   // split groups (one ticket each)
+constexpr int FA_STATIC_MAX_DEVICES = 64;
+int launch_flash_attn_static(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
+                             const oasr_tensor *mask, float scale, oasr_tensor *dst);
 
 }  // namespace oasr

@@ -218,11 +218,12 @@ int oasr_b200_mul_mat_qact(oasr_backend *be, const oasr_weight *w, const void *q
     return launch_mmq(be, w, 0, a, rows, (int)K, y, dst->nb[1] / 4);
 }
 
-int oasr_b200_flash_attn_ext(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
-                             const oasr_tensor *mask, float scale, float max_bias, float logit_softcap, int32_t prec,
-                             oasr_tensor *dst) {
-    int st = oasr_internal_precheck(be);
-    if (st) return st;
+// Argument checks shared by both attention entry points: a status; *empty is set
+// when there is nothing to compute (no queries).
+static int fa_validate(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
+                       const oasr_tensor *mask, float max_bias, float logit_softcap, int32_t prec,
+                       oasr_tensor *dst, bool *empty) {
+    *empty = false;
     if (!q || !k || !v || !dst) return oasr_internal_fail(be, OASR_STATUS_FAILED, "flash_attn_ext: null argument");
     if (max_bias != 0.0f || logit_softcap != 0.0f)
         return oasr_internal_fail(be, OASR_STATUS_FAILED, "flash_attn_ext: max_bias/logit_softcap must be 0");
@@ -256,18 +257,43 @@ int oasr_b200_flash_attn_ext(oasr_backend *be, const oasr_tensor *q, const oasr_
     if (dst->type != OASR_TYPE_F32 || dst->ne[0] != D || dst->ne[1] != q->ne[2] || dst->ne[2] != q->ne[1] ||
         dst->ne[3] != q->ne[3] || dst->nb[0] != 4)
         return oasr_internal_fail(be, OASR_STATUS_FAILED, "flash_attn_ext: dst must be f32 [D, H, n_q, S]");
-    if (q->ne[1] == 0 || q->ne[2] == 0 || q->ne[3] == 0) return OASR_STATUS_SUCCESS;
-    if (k->ne[1] == 0) {
-        // no keys: ggml leaves S = 0 and writes zeros
-        for (int64_t s = 0; s < dst->ne[3]; ++s)
-            for (int64_t i = 0; i < dst->ne[2]; ++i)
-                for (int64_t h = 0; h < dst->ne[1]; ++h)
-                    OASR_CUDA_TRY(be, cudaMemsetAsync((char *)dst->data + h * dst->nb[1] + i * dst->nb[2] + s * dst->nb[3], 0,
-                                                      D * 4, be->stream));
-        return OASR_STATUS_SUCCESS;
-    }
+    *empty = q->ne[1] == 0 || q->ne[2] == 0 || q->ne[3] == 0;
+    return OASR_STATUS_SUCCESS;
+}
+
+// ggml leaves S = 0 with no keys and writes zeros
+static int fa_zero_fill(oasr_backend *be, const oasr_tensor *dst, int64_t D) {
+    for (int64_t s = 0; s < dst->ne[3]; ++s)
+        for (int64_t i = 0; i < dst->ne[2]; ++i)
+            for (int64_t h = 0; h < dst->ne[1]; ++h)
+                OASR_CUDA_TRY(be, cudaMemsetAsync((char *)dst->data + h * dst->nb[1] + i * dst->nb[2] + s * dst->nb[3], 0,
+                                                  D * 4, be->stream));
+    return OASR_STATUS_SUCCESS;
+}
+
+int oasr_b200_flash_attn_ext(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
+                             const oasr_tensor *mask, float scale, float max_bias, float logit_softcap, int32_t prec,
+                             oasr_tensor *dst) {
+    int st = oasr_internal_precheck(be);
+    if (st) return st;
+    bool empty;
+    st = fa_validate(be, q, k, v, mask, max_bias, logit_softcap, prec, dst, &empty);
+    if (st || empty) return st;
+    if (k->ne[1] == 0) return fa_zero_fill(be, dst, q->ne[0]);
     if (flash_attn_tc_eligible(q, k, mask, dst)) return launch_flash_attn_tc(be, q, k, v, scale, dst);
     return launch_flash_attn(be, q, k, v, mask, scale, dst);
+}
+
+int oasr_b200_flash_attn_ext_static(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k,
+                                    const oasr_tensor *v, const oasr_tensor *mask, float scale, float max_bias,
+                                    float logit_softcap, int32_t prec, oasr_tensor *dst) {
+    int st = oasr_internal_precheck(be);
+    if (st) return st;
+    bool empty;
+    st = fa_validate(be, q, k, v, mask, max_bias, logit_softcap, prec, dst, &empty);
+    if (st || empty) return st;
+    if (k->ne[1] == 0) return fa_zero_fill(be, dst, q->ne[0]);
+    return launch_flash_attn_static(be, q, k, v, mask, scale, dst);
 }
 
 int oasr_b200_set_rows(oasr_backend *be, oasr_tensor *dst, const oasr_tensor *src, const oasr_tensor *rows) {
