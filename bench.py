@@ -573,17 +573,32 @@ def run_kernels(args) -> None:
     B, d, ffn, T, H = 8, 1280, 5120, 1500, 20
     rows = []
 
+    def gemv_name(fam):
+        dp4a = os.environ.get("OASR_B200_DECODE_GEMV") == "dp4a"
+        if fam == "q4k":
+            return "mmv_q4k_kernel (dp4a)" if dp4a else "mmv_q4k_tc_kernel (mma.sync s8)"
+        return "mmv_q8_kernel (dp4a)" if dp4a else "mmv_q80_tc_kernel (mma.sync s8)"
+
     def timed(fn, iters):
+        """mean device time of one call: `iters` calls captured in a CUDA graph (no
+        host launch overhead between them), the graph replayed 3 times"""
         for i in range(3):
             fn(i)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(iters):
+                fn(i)
+        graph.replay()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         stream.synchronize()
         e0.record(stream)
-        for i in range(iters):
-            fn(i)
+        for _ in range(3):
+            graph.replay()
         e1.record(stream)
         torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / iters * 1e3
+        del graph
+        return e0.elapsed_time(e1) / (3 * iters) * 1e3
 
     def add(name, shape, us, amount, unit):
         if unit == "GB/s":
@@ -606,7 +621,7 @@ def run_kernels(args) -> None:
             be.quantize_act(ob.Q4_K, x, qa)
             y = torch.empty(B, N, device="cuda")
             us = timed(lambda i: be.mul_mat_qact(ws[i % n_rot], qa, B, y), 48)
-            add("mmv_q4k_kernel", f"{role} Q4_K N={N} K={K} M={B}", us, N * K * 144 / 256 + B * K + B * N * 4, "GB/s")
+            add(gemv_name("q4k"), f"{role} Q4_K N={N} K={K} M={B}", us, N * K * 144 / 256 + B * K + B * N * 4, "GB/s")
             del ws
         # logits head (Q8_0, tied token embedding)
         V = 51866
@@ -617,7 +632,7 @@ def run_kernels(args) -> None:
         be.quantize_act(ob.Q8_0, x, qa)
         y = torch.empty(B, V, device="cuda")
         us = timed(lambda i: be.mul_mat_qact(lm[i % 2], qa, B, y), 20)
-        add("mmv_q8_kernel", f"logits Q8_0 N={V} K={d} M={B}", us, V * d * 34 / 32 + B * d + B * V * 4, "GB/s")
+        add(gemv_name("q80"), f"logits Q8_0 N={V} K={d} M={B}", us, V * d * 34 / 32 + B * d + B * V * 4, "GB/s")
         del lm
         # cross-attention flash-decode (the dominant decode kernel)
         fa = _fa_roofline(be, torch, stream)

@@ -11,7 +11,7 @@
 #include <cstdlib>
 #include <vector>
 
-#include "common.cuh"
+#include "kernels.cuh"
 
 using namespace oasr;
 
@@ -134,6 +134,11 @@ int oasr_b200_init(int32_t ordinal, oasr_backend **out) {
     be->scratch = nullptr;
     be->scratch_bytes = 0;
     be->pdl = false;
+    {
+        // decode GEMV path: tensor-core tiles by default, the dp4a kernel on request
+        const char *env = getenv("OASR_B200_DECODE_GEMV");
+        be->decode_tiles = !(env && strcmp(env, "dp4a") == 0);
+    }
     int st = OASR_STATUS_SUCCESS;
     std::vector<uint16_t> gelu;
     build_gelu_table(gelu);
@@ -301,9 +306,19 @@ int oasr_b200_weight_upload(oasr_backend *be, const void *host, size_t bytes, in
         e = cudaMalloc(&w->qs, bytes);
         if (e == cudaSuccess) e = cudaMemcpy(w->qs, src, bytes, cudaMemcpyHostToDevice);
     }
+    w->tiles = nullptr;
+    if (e == cudaSuccess && be->decode_tiles && mmv_tiles_supported(type, ne[0])) {
+        // decode-tile copy for the tensor-core GEMV, built on the device from the planes above
+        const size_t tb = mmv_tiles_bytes(type, ne[1], ne[0], ne[2] * ne[3]);
+        e = cudaMalloc(&w->tiles, tb);
+        if (e == cudaSuccess) e = build_mmv_tiles(w, be->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(be->stream);
+        if (e == cudaSuccess) w->device_bytes += tb;
+    }
     if (e != cudaSuccess) {
         if (w->qs) cudaFree(w->qs);
         if (w->d) cudaFree(w->d);
+        if (w->tiles) cudaFree(w->tiles);
         delete w;
         return oasr_internal_cuda_fail(be, e, "weight_upload", __LINE__);
     }
@@ -323,6 +338,7 @@ int oasr_b200_weight_free(oasr_backend *be, oasr_weight *w) {
     }
     if (w->qs) cudaFree(w->qs);
     if (w->d) cudaFree(w->d);
+    if (w->tiles) cudaFree(w->tiles);
     delete w;
     return OASR_STATUS_SUCCESS;
 }

@@ -48,6 +48,7 @@ struct oasr_weight {
     uint16_t *d;
     int64_t qs_row_bytes;    // bytes per row in the qs plane
     int64_t d_row_elems;     // fp16 scales per row in the d plane
+    uint8_t *tiles;          // decode-tile copy for the tensor-core GEMV (Q4_K, Q8_0), or null
     uint64_t device_bytes;
 };
 
@@ -70,6 +71,7 @@ struct oasr_backend {
     int64_t n_weights;
     std::string last_error;
     bool pdl;  // launch with programmatic stream serialization (dependent kernels overlap)
+    bool decode_tiles;  // build decode tiles at upload (OASR_B200_DECODE_GEMV=dp4a turns it off)
 };
 
 #define OASR_CUDA_TRY(be, expr)                                                          \

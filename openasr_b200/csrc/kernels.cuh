@@ -70,6 +70,12 @@ int launch_quantize_act(oasr_backend *be, const oasr_tensor *x, int family, cons
 // decode GEMV (M <= 8 activation rows sharing one weight slice)
 int launch_mmv_quant(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int M, int K,
                      float *y, int64_t y_ld);
+// decode GEMV on the integer tensor-core path over the weight's decode tiles (mmv_tc.cu)
+bool mmv_tiles_supported(int type, int64_t K);
+size_t mmv_tiles_bytes(int type, int64_t N, int64_t K, int64_t slices);
+cudaError_t build_mmv_tiles(oasr_weight *w, cudaStream_t st);
+int launch_mmv_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int M, int K, float *y,
+                  int64_t y_ld);
 int launch_mmv_float(oasr_backend *be, const oasr_weight *w, int64_t slice, const char *x, int64_t x_ld_bytes,
                      bool x_f16, bool round_x_f16, int M, int K, float *y, int64_t y_ld);
 

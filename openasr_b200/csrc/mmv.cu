@@ -359,6 +359,7 @@ static void launch_q4k(oasr_backend *be, const oasr_weight *w, int64_t slice, co
 
 int launch_mmv_quant(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int M, int K,
                      float *y, int64_t y_ld) {
+    if (w->tiles) return launch_mmv_tc(be, w, slice, a, M, K, y, y_ld);
     cudaStream_t st = be->stream;
     if (w->type == OASR_TYPE_Q4_K) {
         switch (M) {

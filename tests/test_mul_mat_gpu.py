@@ -192,3 +192,60 @@ def test_q4k_tensor_core_gemm_is_bit_exact(gpu_backend, M, N, K):
     got = _run(gpu_backend, wq, ob.Q4_K, N, K, x)
     ref = oo.mul_mat(wq, ob.Q4_K, K, N, x)
     np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qt", [ob.Q8_0, ob.Q4_K])
+@pytest.mark.parametrize("N,K", [(17, 256), (100, 512), (51866, 1280), (40, 7680)])
+@pytest.mark.parametrize("M", [1, 5, 8])
+def test_decode_tiles_ragged_rows_and_depths(gpu_backend, qt, N, K, M):
+    """The tensor-core GEMV reads 16-row decode tiles: a last tile with padding
+    rows, one unit per row (K = 256), and rows longer than one unit per warp."""
+    seed = 0x0A5A000B + N + K + M
+    wq = _weights(N, K, qt, seed)
+    x = oo.synth_normal(seed ^ 0x5A5A, M * K).reshape(M, K)
+    got = _run(gpu_backend, wq, qt, N, K, x)
+    ref = oo.mul_mat(wq, qt, K, N, x)
+    err = max_abs_rel(got, ref)
+    assert err <= TOL and err <= TIGHT, (qt, N, K, M, err)
+
+
+_DP4A_CHILD = r"""
+import sys
+sys.path.insert(0, sys.argv[1])
+import numpy as np, torch
+import openasr_b200 as ob
+from oracle import oracle as oo
+from tests.conftest import max_abs_rel
+be = ob.Backend(0)
+worst = 0.0
+for qt in (ob.Q8_0, ob.Q4_K):
+    for (N, K, M) in ((1280, 1280, 8), (3840, 1280, 3), (1024, 3072, 1)):
+        w = oo.quantize(qt, oo.synth_normal(N + K + qt, N * K, 0.0, 0.02).reshape(N, K))
+        x = oo.synth_normal(M + K, M * K).reshape(M, K)
+        W = be.upload_weight(w, qt, [K, N])
+        out = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        be.mul_mat(W, torch.from_numpy(x).cuda(), out)
+        be.synchronize()
+        W.free()
+        worst = max(worst, max_abs_rel(out.cpu().numpy(), oo.mul_mat(w, qt, K, N, x)))
+print("WORST", worst)
+be.close()
+"""
+
+
+@pytest.mark.gpu
+def test_dp4a_decode_gemv_still_matches_oracle():
+    """OASR_B200_DECODE_GEMV=dp4a keeps the CUDA-core GEMV for Q8_0 / Q4_K
+    (the Q4_0 path always uses it)."""
+    import os
+    import subprocess
+    import sys
+
+    from tests.conftest import ROOT
+
+    env = dict(os.environ, OASR_B200_DECODE_GEMV="dp4a")
+    r = subprocess.run([sys.executable, "-c", _DP4A_CHILD, ROOT], capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0, r.stderr[-2000:]
+    worst = float(r.stdout.split("WORST")[1])
+    assert worst <= TIGHT, worst
