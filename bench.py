@@ -337,11 +337,11 @@ def launches_per_batch(n_enc: int, n_dec: int, n_prompt: int, n_new: int, batch:
     """Kernel launches of one generate() (counted from model_whisper.cu):
     mel 3; prelude 4 + batch positional adds; per encoder layer 10 + 4 attention
     (3 pre-pass + 1 tensor-core); final norm 1; 2 cross-K/V per decoder layer;
-    per decoder step 1 embed + 15 per layer + 3 head + 1 advance; 1 fill per
-    prompt token."""
+    per decoder step 1 embed + 8 per layer (6 fused GEMVs, 2 attentions) + 3 head
+    (LN + quantize, logits, argmax) + 1 advance; 1 fill per prompt token."""
     enc = 3 + 4 + batch + n_enc * 14 + 1 + 2 * n_dec
     steps = n_prompt + n_new - 1
-    return enc + steps * (1 + 15 * n_dec + 3 + 1) + n_prompt
+    return enc + steps * (1 + 8 * n_dec + 3 + 1) + n_prompt
 
 
 def rtfx_cpu_baseline(seconds_budget: float = 20.0) -> dict:

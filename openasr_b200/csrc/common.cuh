@@ -113,6 +113,30 @@ static cudaError_t launch_k(oasr_backend *be, void (*kernel)(KArgs...), dim3 gri
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// ---- last-CTA ticket ------------------------------------------------------------------
+// "The last CTA to finish does the rest": call with every thread of the CTA after its
+// global stores.  bar.sync orders those stores before thread 0's release-acquire
+// atomic (release is cumulative over the barrier), so the CTA that draws ticket
+// total-1 sees every other CTA's stores; it resets the ticket, so each launch leaves
+// it at zero.  Read other CTAs' data with L2 loads (ld.cg / __ldcg).
+static __device__ __forceinline__ unsigned int atom_add_acq_rel_gpu(unsigned int *p, unsigned int v) {
+    unsigned int old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+static __device__ __forceinline__ bool cta_last_arrival(unsigned int *ticket, unsigned int total) {
+    __shared__ unsigned int s_last_flag;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const bool last = atom_add_acq_rel_gpu(ticket, 1u) == total - 1;
+        if (last) atomicExch(ticket, 0u);  // every other CTA has drawn its ticket
+        s_last_flag = last;
+    }
+    __syncthreads();
+    return s_last_flag != 0;
+}
+
 // ---- device helpers --------------------------------------------------------------
 static __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -366,13 +366,201 @@ static int blocks_for(int64_t work, int threads, oasr_backend *be) {
     return (int)std::max<int64_t>(1, std::min<int64_t>((work + threads - 1) / threads, (int64_t)be->sm_count * 32));
 }
 
+// ---- chunk-parallel row kernels ---------------------------------------------------------------
+// One warp per chunk of 32*E elements (E = 8 for the q8_K family: one 256 super-block;
+// E = 4 for q8_0: four 32-blocks of 8 lanes), every operand loaded before any
+// arithmetic, so a row costs one memory round trip instead of one per element
+// group.  Arithmetic as resid_norm_quant / bias_gelu_quant above.
+
+template <int E>
+static __device__ __forceinline__ void ldE(const float *p, float (&v)[E]) {
+    if (E == 8) {
+        const float4 a = *reinterpret_cast<const float4 *>(p), b = *reinterpret_cast<const float4 *>(p + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[E > 4 ? 4 : 0] = b.x; v[E > 5 ? 5 : 0] = b.y; v[E > 6 ? 6 : 0] = b.z; v[E > 7 ? 7 : 0] = b.w;
+    } else {
+        const float4 a = *reinterpret_cast<const float4 *>(p);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    }
+}
+
+template <int E>
+static __device__ __forceinline__ void stE(float *p, const float (&v)[E]) {
+    *reinterpret_cast<float4 *>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    if (E == 8) *reinterpret_cast<float4 *>(p + 4) = make_float4(v[E > 4 ? 4 : 0], v[E > 5 ? 5 : 0], v[E > 6 ? 6 : 0], v[E > 7 ? 7 : 0]);
+}
+
+// quantize one warp chunk (lane holds E consecutive values at k0 = chunk*32*E + E*lane) of row r
+template <int E>
+static __device__ __forceinline__ void quant_chunk(const float (&v)[E], int64_t r, int n, int k0, int lane,
+                                                   const ActPlanes &a) {
+    if (E == 8) {
+        // q8_K: one super-block per warp, first-max
+        float amax = -1.0f, maxv = 0.0f;
+        int idx = 0;
+#pragma unroll
+        for (int i = 0; i < E; ++i)
+            if (fabsf(v[i]) > amax) { amax = fabsf(v[i]); maxv = v[i]; idx = k0 + i; }
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const float oa = __shfl_xor_sync(0xffffffffu, amax, o);
+            const float ov = __shfl_xor_sync(0xffffffffu, maxv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+            if (oa > amax || (oa == amax && oi < idx)) { amax = oa; maxv = ov; idx = oi; }
+        }
+        int q[E];
+        float d = 0.0f;
+        if (amax == 0.0f) {
+#pragma unroll
+            for (int i = 0; i < E; ++i) q[i] = 0;
+        } else {
+            const float iscale = __fdiv_rn(-127.0f, maxv);
+#pragma unroll
+            for (int i = 0; i < E; ++i) q[i] = min(127, __float2int_rn(__fmul_rn(iscale, v[i])));
+            d = __frcp_rn(iscale);
+        }
+        int sum = 0;
+#pragma unroll
+        for (int i = 0; i < E; ++i) sum += q[i];
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        uint2 pk;
+        pk.x = (uint32_t)(uint8_t)q[0] | (uint32_t)(uint8_t)q[1] << 8 | (uint32_t)(uint8_t)q[2] << 16 |
+               (uint32_t)(uint8_t)q[3] << 24;
+        pk.y = (uint32_t)(uint8_t)q[E > 4 ? 4 : 0] | (uint32_t)(uint8_t)q[E > 5 ? 5 : 0] << 8 |
+               (uint32_t)(uint8_t)q[E > 6 ? 6 : 0] << 16 | (uint32_t)(uint8_t)q[E > 7 ? 7 : 0] << 24;
+        *reinterpret_cast<uint2 *>(a.qs + r * n + k0) = pk;
+        if ((lane & 1) == 0) a.bs16[r * (n / 16) + k0 / 16] = (int16_t)sum;
+        if (lane == 0) a.d[r * (n / 256) + k0 / 256] = d;
+        if (a.qs16) {
+            __half2 h[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                h[i] = __halves2half2(__int2half_rn(q[(2 * i) % E]), __int2half_rn(q[(2 * i + 1) % E]));
+            *reinterpret_cast<int4 *>(a.qs16 + r * n + k0) = *reinterpret_cast<int4 *>(h);
+            if ((lane & 1) == 0) a.bs16h[r * (n / 16) + k0 / 16] = __int2half_rn(sum);
+        }
+    } else {
+        // q8_0: 8 lanes per 32-block
+        const unsigned gmask = 0xFFu << (lane & 24);
+        float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+        amax = fmaxf(amax, __shfl_xor_sync(gmask, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(gmask, amax, 2));
+        amax = fmaxf(amax, __shfl_xor_sync(gmask, amax, 4));
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
+        uint32_t packed = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) packed |= (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(v[i], id)) << (8 * i);
+        *reinterpret_cast<uint32_t *>(a.qs + r * n + k0) = packed;
+        if ((k0 & 31) == 0) a.d[r * (n / 32) + k0 / 32] = __half2float(__float2half_rn(d));
+    }
+}
+
+// CTA = one row, warp = one chunk: x (+)= add + bias; y = norm(x)(*gamma + beta) -> out_f32 / planes
+template <int E>
+__global__ void ln_quant_chunks_kernel(float *x, const float *add, const float *add_bias, int n, float eps, int rms,
+                                       const float *gamma, const float *beta, float *out_f32, ActPlanes q) {
+    __shared__ double sh[32];
+    griddep_launch_dependents();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int64_t r = blockIdx.x;
+    const int k0 = warp * 32 * E + E * lane;
+    float g[E], b[E], ad[E], ab[E];
+    // parameters do not depend on the previous kernel
+    if (gamma) ldE<E>(gamma + k0, g);
+    if (beta) ldE<E>(beta + k0, b);
+    if (add_bias) ldE<E>(add_bias + k0, ab);
+    griddep_wait();
+    float v[E];
+    ldE<E>(x + r * n + k0, v);
+    if (add) {
+        ldE<E>(add + r * n + k0, ad);
+#pragma unroll
+        for (int i = 0; i < E; ++i) v[i] = __fadd_rn(v[i], add_bias ? __fadd_rn(ad[i], ab[i]) : ad[i]);
+        stE<E>(x + r * n + k0, v);
+    }
+    auto block_sum_d = [&](double s) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) sh[warp] = s;
+        __syncthreads();
+        double t = 0.0;
+        for (int i = 0; i < nw; ++i) t += sh[i];
+        __syncthreads();
+        return t;
+    };
+    float scale;
+    if (rms) {
+        double s = 0.0;
+#pragma unroll
+        for (int i = 0; i < E; ++i) s += (double)__fmul_rn(v[i], v[i]);
+        s = block_sum_d(s);
+        scale = __frcp_rn(__fsqrt_rn(__fadd_rn((float)(s / (double)n), eps)));
+    } else {
+        double s = 0.0;
+#pragma unroll
+        for (int i = 0; i < E; ++i) s += (double)v[i];
+        const float mean = (float)(block_sum_d(s) / (double)n);
+        double s2 = 0.0;
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+            v[i] = __fsub_rn(v[i], mean);
+            s2 += (double)__fmul_rn(v[i], v[i]);
+        }
+        scale = __frcp_rn(__fsqrt_rn(__fadd_rn((float)(block_sum_d(s2) / (double)n), eps)));
+    }
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+        float u = __fmul_rn(v[i], scale);
+        if (gamma) u = __fmul_rn(u, g[i]);
+        if (beta) u = __fadd_rn(u, b[i]);
+        v[i] = u;
+    }
+    if (out_f32) stE<E>(out_f32 + r * n + k0, v);
+    if (q.qs) quant_chunk<E>(v, r, n, k0, lane, q);
+}
+
+// warp = one (row, chunk): y = gelu(x + bias) -> out_f32 / planes
+template <int E>
+__global__ void gelu_quant_chunks_kernel(const float *x, const float *bias, int n, int64_t n_chunks,
+                                         const uint16_t *tab, float *out_f32, ActPlanes q) {
+    griddep_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (w >= n_chunks) return;  // warp-uniform
+    const int per_row = n / (32 * E);
+    const int64_t r = w / per_row;
+    const int k0 = (int)(w - r * per_row) * 32 * E + E * lane;
+    float bb[E], v[E];
+    if (bias) ldE<E>(bias + k0, bb);
+    griddep_wait();
+    ldE<E>(x + r * n + k0, v);
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = gelu_tab(bias ? __fadd_rn(v[i], bb[i]) : v[i], tab);
+    if (out_f32) stE<E>(out_f32 + r * n + k0, v);
+    if (q.qs) quant_chunk<E>(v, r, n, k0, lane, q);
+}
+
 int launch_resid_norm_quant(oasr_backend *be, float *x, const float *add, const float *add_bias, int64_t rows, int n,
                             float eps, bool rms, const float *gamma, const float *beta, float *out_f32,
                             const ActPlanes *q, int family) {
     ActPlanes qq{};
     if (q) qq = *q;
-    const cudaError_t e = launch_k(be, resid_norm_quant_kernel, dim3((unsigned)rows), dim3(256), n * sizeof(float), x, add,
-                                   add_bias, n, eps, rms ? 1 : 0, gamma, beta, out_f32, qq, family);
+    cudaError_t e;
+    // chunk-parallel form when a row is whole warp chunks (<= 32 warps) of the planes' family
+    const int E = (!q || family == FAMILY_Q8_K) ? 8 : 4;
+    if (n % (32 * E) == 0 && n / (32 * E) <= 32 && (!q || family != FAMILY_Q8_K || n % 256 == 0)) {
+        const dim3 block(32 * (n / (32 * E)));
+        if (E == 8)
+            e = launch_k(be, ln_quant_chunks_kernel<8>, dim3((unsigned)rows), block, 0, x, add, add_bias, n, eps,
+                         rms ? 1 : 0, gamma, beta, out_f32, qq);
+        else
+            e = launch_k(be, ln_quant_chunks_kernel<4>, dim3((unsigned)rows), block, 0, x, add, add_bias, n, eps,
+                         rms ? 1 : 0, gamma, beta, out_f32, qq);
+    } else {
+        e = launch_k(be, resid_norm_quant_kernel, dim3((unsigned)rows), dim3(256), n * sizeof(float), x, add, add_bias,
+                     n, eps, rms ? 1 : 0, gamma, beta, out_f32, qq, family);
+    }
     if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "resid_norm_quant launch", __LINE__);
     return oasr_internal_launch_check(be, "resid_norm_quant");
 }
@@ -381,8 +569,21 @@ int launch_bias_gelu_quant(oasr_backend *be, const float *x, const float *bias, 
                            const ActPlanes *q, int family) {
     ActPlanes qq{};
     if (q) qq = *q;
-    const cudaError_t e = launch_k(be, bias_gelu_quant_kernel, dim3((unsigned)rows), dim3(256), n * sizeof(float), x, bias,
-                                   n, (const uint16_t *)be->gelu_table, out_f32, qq, family);
+    cudaError_t e;
+    const int E = (!q || family == FAMILY_Q8_K) ? 8 : 4;
+    if (n % (32 * E) == 0) {
+        const int64_t chunks = rows * (n / (32 * E));
+        const unsigned grid = (unsigned)((chunks + 7) / 8);
+        if (E == 8)
+            e = launch_k(be, gelu_quant_chunks_kernel<8>, dim3(grid), dim3(256), 0, x, bias, n, chunks,
+                         (const uint16_t *)be->gelu_table, out_f32, qq);
+        else
+            e = launch_k(be, gelu_quant_chunks_kernel<4>, dim3(grid), dim3(256), 0, x, bias, n, chunks,
+                         (const uint16_t *)be->gelu_table, out_f32, qq);
+    } else {
+        e = launch_k(be, bias_gelu_quant_kernel, dim3((unsigned)rows), dim3(256), n * sizeof(float), x, bias, n,
+                     (const uint16_t *)be->gelu_table, out_f32, qq, family);
+    }
     if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "bias_gelu_quant launch", __LINE__);
     return oasr_internal_launch_check(be, "bias_gelu_quant");
 }

@@ -241,18 +241,7 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
     if (a.n_splits == 1) return;
 
     // last CTA of this (kv head, seq, q tile) merges the split partials
-    __shared__ bool s_last;
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        unsigned int *ctr = a.counters + blockIdx.x;
-        const unsigned int ticket = atomicAdd(ctr, 1u);
-        s_last = ticket == (unsigned)(a.n_splits - 1);
-        if (s_last) *ctr = 0u;  // every launch leaves the tickets at zero
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
+    if (!cta_last_arrival(a.counters + blockIdx.x, (unsigned)a.n_splits)) return;
     for (int o = threadIdx.x; o < QT * D; o += 128) {
         const int t = o / D, e = o % D;
         const int r = qt * QT + t;

@@ -30,80 +30,20 @@
 // msum = sum_j m_j * bsum_j, the latter from one f16 MMA of the duplicated mins
 // against the 16-wide activation sums (|bsum16| <= 2032, products and sums are
 // integers below 2^24, so the f32 result is exact).
-#include "kernels.cuh"
+#include "mma_frag.cuh"
 
 namespace oasr {
 
-constexpr int TILE_ROWS = 16;
-constexpr int Q4K_UNIT = 2368;
-constexpr int Q80_UNIT = 1088;
-
-static __device__ __forceinline__ void mma_s8_16832(int (&d)[4], int a0, int a1, int a2, int a3, int b0, int b1) {
-    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%10,%10,%10};"
-        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
-}
-
-static __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                                     uint32_t a3, uint32_t b0, uint32_t b1) {
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%10,%10,%10};"
-        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.0f));
-}
-
-static __device__ __forceinline__ int ldg_nc_b32(const void *p) {
-    int r;
-    asm volatile("ld.global.nc.b32 %0, [%1];" : "=r"(r) : "l"(p));
-    return r;
-}
-
-static __device__ __forceinline__ int4 ldg_nc_v4(const void *p) {
-    int4 r;
-    asm volatile("ld.global.nc.v4.s32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
-    return r;
-}
-
-static __device__ __forceinline__ int byte_at(int w, int i) { return (w >> (8 * i)) & 0xFF; }
-
-// two equal f16 values from a small non-negative integer
-static __device__ __forceinline__ uint32_t dup_h2(int v) {
-    const __half h = __int2half_rn(v);
-    const uint16_t u = __half_as_ushort(h);
-    return (uint32_t)u | ((uint32_t)u << 16);
-}
-
-static __device__ __forceinline__ uint32_t i16x2_to_h2(int packed) {
-    const __half lo = __int2half_rn((int)(int16_t)(packed & 0xFFFF));
-    const __half hi = __int2half_rn((int)(int16_t)((unsigned)packed >> 16));
-    return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
-}
-
-struct Q4kUnit {
-    int4 q[4];
-    int4 sa, sb;   // rows g, g+8: sc[0..7] | m[0..7]
-    int dda, ddb;  // rows g, g+8: fp16 d | fp16 dmin << 16
-};
-
-static __device__ __forceinline__ void load_q4k_unit(Q4kUnit &u, const uint8_t *p, int lane, int g) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) u.q[i] = ldg_stream(p + i * 512 + lane * 16);
-    u.sa = ldg_nc_v4(p + 2048 + 16 * g);
-    u.sb = ldg_nc_v4(p + 2048 + 16 * (g + 8));
-    u.dda = ldg_nc_b32(p + 2304 + 4 * g);
-    u.ddb = ldg_nc_b32(p + 2304 + 4 * (g + 8));
-}
-
-// One CTA per 16-row tile; warp w handles super-blocks w, w + W, ...; the W
-// partial tiles are summed in shared memory in warp order.
+// One CTA per 16-row tile; warp w handles super-blocks w, w + W, ... with the next
+// unit's loads issued before the current one's MMAs; the W partial tiles are
+// summed in shared memory in warp order.
 template <int W>
 __global__ void __launch_bounds__(W * 32) mmv_q4k_tc_kernel(const uint8_t *__restrict__ tiles, int nsb, int64_t N,
                                                             int M, const int8_t *__restrict__ aqs,
                                                             const float *__restrict__ ad,
                                                             const int16_t *__restrict__ abs16, int K,
                                                             float *__restrict__ y, int64_t y_ld) {
-    __shared__ float red[W > 1 ? W : 1][32][4];
+    __shared__ float red[W * 32 * 4];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const uint8_t *tile = tiles + (int64_t)blockIdx.x * nsb * Q4K_UNIT;
@@ -116,69 +56,20 @@ __global__ void __launch_bounds__(W * 32) mmv_q4k_tc_kernel(const uint8_t *__res
     if (s < nsb) load_q4k_unit(cur, tile + (int64_t)s * Q4K_UNIT, lane, g);
     griddep_wait();
 
-    const bool gv = g < M;                 // B-fragment activation row
+    // B-fragment activation row g (rows past M read row 0 and are never stored)
+    const int gr = g < M ? g : 0;
+    const int8_t *arow = aqs + (int64_t)gr * K;
+    const int16_t *brow = abs16 + (int64_t)gr * (K / 16);
     const int m0 = 2 * t, m1 = 2 * t + 1;  // C-fragment activation rows
-    const int8_t *arow = aqs + (int64_t)(gv ? g : 0) * K;
-    const int16_t *brow = abs16 + (int64_t)(gv ? g : 0) * (K / 16);
     for (; s < nsb; s += W) {
         const bool more = s + W < nsb;
         if (more) load_q4k_unit(nxt, tile + (int64_t)(s + W) * Q4K_UNIT, lane, g);
-        int isum[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            int2 blo = make_int2(0, 0), bhi = make_int2(0, 0);
-            if (gv) {
-                blo = __ldg(reinterpret_cast<const int2 *>(arow + 256 * s + 64 * i + 8 * t));
-                bhi = __ldg(reinterpret_cast<const int2 *>(arow + 256 * s + 64 * i + 32 + 8 * t));
-            }
-            const int4 q = cur.q[i];
-            int dlo[4], dhi[4];
-            // a0 = row g quants 8t..8t+3, a1 = row g+8, a2 = row g quants 8t+4..8t+7, a3 = row g+8
-            mma_s8_16832(dlo, q.x & 0x0F0F0F0F, q.z & 0x0F0F0F0F, q.y & 0x0F0F0F0F, q.w & 0x0F0F0F0F, blo.x, blo.y);
-            mma_s8_16832(dhi, (q.x >> 4) & 0x0F0F0F0F, (q.z >> 4) & 0x0F0F0F0F, (q.y >> 4) & 0x0F0F0F0F,
-                         (q.w >> 4) & 0x0F0F0F0F, bhi.x, bhi.y);
-            // sub-blocks 2i (low nibbles) and 2i+1 (high nibbles)
-            const int wa = i < 2 ? cur.sa.x : cur.sa.y, wb = i < 2 ? cur.sb.x : cur.sb.y;
-            const int sh = 2 * (i & 1);
-            const int sca0 = byte_at(wa, sh), sca1 = byte_at(wa, sh + 1);
-            const int scb0 = byte_at(wb, sh), scb1 = byte_at(wb, sh + 1);
-            isum[0] += sca0 * dlo[0] + sca1 * dhi[0];
-            isum[1] += sca0 * dlo[1] + sca1 * dhi[1];
-            isum[2] += scb0 * dlo[2] + scb1 * dhi[2];
-            isum[3] += scb0 * dlo[3] + scb1 * dhi[3];
-        }
-        // min term: k slots 2t, 2t+1 <-> 16-sums 2t, 2t+1 (sub-block t); slots 8+2t, 9+2t <-> sub-block 4+t
-        uint32_t b0 = 0, b1 = 0;
-        if (gv) {
-            b0 = i16x2_to_h2(__ldg(reinterpret_cast<const int *>(brow + 16 * s + 2 * t)));
-            b1 = i16x2_to_h2(__ldg(reinterpret_cast<const int *>(brow + 16 * s + 8 + 2 * t)));
-        }
-        float msum[4];
-        mma_f16_16816(msum, dup_h2(byte_at(cur.sa.z, t)), dup_h2(byte_at(cur.sb.z, t)), dup_h2(byte_at(cur.sa.w, t)),
-                      dup_h2(byte_at(cur.sb.w, t)), b0, b1);
         const float da0 = m0 < M ? __ldg(ad + (int64_t)m0 * nsb + s) : 0.0f;
         const float da1 = m1 < M ? __ldg(ad + (int64_t)m1 * nsb + s) : 0.0f;
-        const float dwa = h2f((uint16_t)(cur.dda & 0xFFFF)), dma = h2f((uint16_t)((unsigned)cur.dda >> 16));
-        const float dwb = h2f((uint16_t)(cur.ddb & 0xFFFF)), dmb = h2f((uint16_t)((unsigned)cur.ddb >> 16));
-        acc[0] += __fsub_rn(__fmul_rn(__fmul_rn(dwa, da0), (float)isum[0]), __fmul_rn(__fmul_rn(dma, da0), msum[0]));
-        acc[1] += __fsub_rn(__fmul_rn(__fmul_rn(dwa, da1), (float)isum[1]), __fmul_rn(__fmul_rn(dma, da1), msum[1]));
-        acc[2] += __fsub_rn(__fmul_rn(__fmul_rn(dwb, da0), (float)isum[2]), __fmul_rn(__fmul_rn(dmb, da0), msum[2]));
-        acc[3] += __fsub_rn(__fmul_rn(__fmul_rn(dwb, da1), (float)isum[3]), __fmul_rn(__fmul_rn(dmb, da1), msum[3]));
+        q4k_unit_accumulate<false>(acc, cur, s, arow, brow, da0, da1, t);
         if (more) cur = nxt;
     }
-
-    if (W > 1) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) red[warp][lane][e] = acc[e];
-        __syncthreads();
-        if (warp != 0) return;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            float v = red[0][lane][e];
-            for (int w2 = 1; w2 < W; ++w2) v += red[w2][lane][e];
-            acc[e] = v;
-        }
-    }
+    if (!reduce_warps<W>(acc, red, warp, lane)) return;
     const int64_t ra = (int64_t)blockIdx.x * TILE_ROWS + g, rb = ra + 8;
     if (m0 < M) {
         if (ra < N) y[(int64_t)m0 * y_ld + ra] = acc[0];
@@ -190,24 +81,12 @@ __global__ void __launch_bounds__(W * 32) mmv_q4k_tc_kernel(const uint8_t *__res
     }
 }
 
-struct Q80Unit {
-    int4 q[2];
-    int dda, ddb;  // rows g, g+8: fp16 d of block 2p | block 2p+1 << 16
-};
-
-static __device__ __forceinline__ void load_q80_unit(Q80Unit &u, const uint8_t *p, int lane, int g) {
-    u.q[0] = ldg_stream(p + lane * 16);
-    u.q[1] = ldg_stream(p + 512 + lane * 16);
-    u.dda = ldg_nc_b32(p + 1024 + 4 * g);
-    u.ddb = ldg_nc_b32(p + 1024 + 4 * (g + 8));
-}
-
 template <int W>
 __global__ void __launch_bounds__(W * 32) mmv_q80_tc_kernel(const uint8_t *__restrict__ tiles, int npairs, int64_t N,
                                                             int M, const int8_t *__restrict__ aqs,
                                                             const float *__restrict__ ad, int K,
                                                             float *__restrict__ y, int64_t y_ld) {
-    __shared__ float red[W > 1 ? W : 1][32][4];
+    __shared__ float red[W * 32 * 4];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const uint8_t *tile = tiles + (int64_t)blockIdx.x * npairs * Q80_UNIT;
@@ -220,45 +99,17 @@ __global__ void __launch_bounds__(W * 32) mmv_q80_tc_kernel(const uint8_t *__res
     if (p < npairs) load_q80_unit(cur, tile + (int64_t)p * Q80_UNIT, lane, g);
     griddep_wait();
 
-    const bool gv = g < M;
+    const int8_t *arow = aqs + (int64_t)(g < M ? g : 0) * K;
     const int m0 = 2 * t, m1 = 2 * t + 1;
-    const int8_t *arow = aqs + (int64_t)(gv ? g : 0) * K;
-    const float *ad0 = ad + (int64_t)(m0 < M ? m0 : 0) * nb, *ad1 = ad + (int64_t)(m1 < M ? m1 : 0) * nb;
+    const float *ad0 = m0 < M ? ad + (int64_t)m0 * nb : nullptr;
+    const float *ad1 = m1 < M ? ad + (int64_t)m1 * nb : nullptr;
     for (; p < npairs; p += W) {
         const bool more = p + W < npairs;
         if (more) load_q80_unit(nxt, tile + (int64_t)(p + W) * Q80_UNIT, lane, g);
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const int b = 2 * p + i;
-            int2 bb = make_int2(0, 0);
-            if (gv) bb = __ldg(reinterpret_cast<const int2 *>(arow + 32 * b + 8 * t));
-            const int4 q = cur.q[i];
-            int d[4];
-            mma_s8_16832(d, q.x, q.z, q.y, q.w, bb.x, bb.y);
-            const float dwa = h2f((uint16_t)(i == 0 ? (cur.dda & 0xFFFF) : ((unsigned)cur.dda >> 16)));
-            const float dwb = h2f((uint16_t)(i == 0 ? (cur.ddb & 0xFFFF) : ((unsigned)cur.ddb >> 16)));
-            const float da0 = m0 < M ? __ldg(ad0 + b) : 0.0f;
-            const float da1 = m1 < M ? __ldg(ad1 + b) : 0.0f;
-            acc[0] += __fmul_rn((float)d[0], __fmul_rn(dwa, da0));
-            acc[1] += __fmul_rn((float)d[1], __fmul_rn(dwa, da1));
-            acc[2] += __fmul_rn((float)d[2], __fmul_rn(dwb, da0));
-            acc[3] += __fmul_rn((float)d[3], __fmul_rn(dwb, da1));
-        }
+        q80_unit_accumulate<false>(acc, cur, p, arow, ad0, ad1, t);
         if (more) cur = nxt;
     }
-
-    if (W > 1) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) red[warp][lane][e] = acc[e];
-        __syncthreads();
-        if (warp != 0) return;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            float v = red[0][lane][e];
-            for (int w2 = 1; w2 < W; ++w2) v += red[w2][lane][e];
-            acc[e] = v;
-        }
-    }
+    if (!reduce_warps<W>(acc, red, warp, lane)) return;
     const int64_t ra = (int64_t)blockIdx.x * TILE_ROWS + g, rb = ra + 8;
     if (m0 < M) {
         if (ra < N) y[(int64_t)m0 * y_ld + ra] = acc[0];

@@ -29,6 +29,15 @@ int launch_gemm_f16(oasr_backend *be, const __half *A, int64_t lda, const __half
                     float *y, int64_t y_ld, const float *bias, bool gelu);
 int launch_argmax_rows(oasr_backend *be, const float *x, int64_t ld, int64_t n, int rows, int32_t *out);
 
+// Fused decoder GEMVs (dgemv.cu): the weight's decode tiles against up to 8 activation
+// rows; quantize-in-prologue (attention output) and QKV / KV-write epilogue forms.
+int dgemv_configure(oasr_backend *be);
+bool dgemv_supported(const oasr_weight *w, bool quant_prologue);
+int launch_dgemv(oasr_backend *be, const oasr_weight *w, const ActPlanes &in, int M, float *y, int64_t y_ld);
+int launch_dgemv_quant(oasr_backend *be, const oasr_weight *w, const float *h, int M, float *y, int64_t y_ld);
+int launch_dgemv_qkv(oasr_backend *be, const oasr_weight *w, const ActPlanes &in, int M, const float *bias3, int d,
+                     float *q_out, __half *kc, __half *vc, int64_t cache_seq_stride, const int *pos_dev, int max_pos);
+
 // y[rows][N] = w . activation planes (rows <= 8: GEMV, else tensor-core / chunked GEMM)
 int mul_mat_planes(oasr_backend *be, const oasr_weight *w, const ActPlanes &a, int64_t rows, float *y, int64_t y_ld);
 

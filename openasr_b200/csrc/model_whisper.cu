@@ -19,6 +19,7 @@
 // and the KV length live in device memory, so the graph replays for every step
 // and the greedy argmax feeds the next step without a host round trip.
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <map>
@@ -71,6 +72,7 @@ struct oasr_whisper {
     void *qa_d, *qa_f;
     // decoder activations, B rows
     float *dx, *dqkv, *dq, *dattn, *dt, *df, *logits;
+    bool fused_dec;  // decoder GEMVs run as dgemv (prologue/epilogue fused), see run_decode_step
     void *dqa_d, *dqa_f, *dqa_lm;
     int *tokens, *pos, *nkv, *history;
     int enc_family, dec_family;
@@ -241,7 +243,60 @@ int run_encoder(oasr_whisper *m, int n) {
 }
 
 // ---- one decoder step for n sequences at device position *pos -------------------------------
+// The decoder step with fused GEMVs (dgemv.cu): 12 launches per layer.
+//   LN1 planes -> qkv (q, self-K/V row out) -> self-attention -> out-proj (quantizes
+//   the attention rows itself) -> residual + LN -> cross-q -> cross-attention (+b_cq)
+//   -> cross-out (same) -> residual + LN -> fc1 -> GELU + quantize -> fc2 ->
+//   residual + next LN1 (after the last layer: the final LN into the head's q8_0 planes).
+static int run_decode_step_fused(oasr_whisper *m, int n) {
+    oasr_backend *be = m->be;
+    const int d = m->d, H = m->H, T = m->T_enc, P = m->cfg.n_text_ctx;
+    const int df = m->dec_family;
+    const ActPlanes qd = act_planes_at(m->dqa_d, df, n, d);
+    const ActPlanes qf = act_planes_at(m->dqa_f, df, n, m->ffn);
+    const ActPlanes ql = act_planes_at(m->dqa_lm, FAMILY_Q8_0, n, d);
+    const float scale = 1.0f / sqrtf(64.0f);
+    W_TRY(launch_embed_q8_0(be, m->tok_emb, m->tokens, n, m->dec_pos, m->pos, P, m->dx));
+    W_TRY(launch_resid_norm_quant(be, m->dx, nullptr, nullptr, n, d, LN_EPS, false, m->dec[0].ln1_g, m->dec[0].ln1_b,
+                                  nullptr, &qd, df));
+    for (size_t l = 0; l < m->dec.size(); ++l) {
+        const DecLayer &L = m->dec[l];
+        const bool last = l + 1 == m->dec.size();
+        W_TRY(launch_dgemv_qkv(be, L.qkv, qd, n, L.b_qkv, d, m->dq, L.self_k, L.self_v, (int64_t)P * d, m->pos, P));
+        {
+            oasr_tensor q = make_tensor(OASR_TYPE_F32, m->dq, 64, 1, H, n, (int64_t)d * 4, 256, (int64_t)d * 4);
+            oasr_tensor k = make_tensor(OASR_TYPE_F16, L.self_k, 64, P, H, n, (int64_t)d * 2, 128, (int64_t)P * d * 2);
+            oasr_tensor v = make_tensor(OASR_TYPE_F16, L.self_v, 64, P, H, n, (int64_t)d * 2, 128, (int64_t)P * d * 2);
+            oasr_tensor o = make_tensor(OASR_TYPE_F32, m->dattn, 64, H, 1, n, 256, (int64_t)d * 4, (int64_t)d * 4);
+            W_TRY(launch_flash_attn_ex(be, &q, &k, &v, nullptr, scale, &o, nullptr, m->nkv));
+        }
+        W_TRY(launch_dgemv_quant(be, L.o, m->dattn, n, m->dt, d));
+        W_TRY(launch_resid_norm_quant(be, m->dx, m->dt, L.b_o, n, d, LN_EPS, false, L.lnc_g, L.lnc_b, nullptr, &qd, df));
+        W_TRY(launch_dgemv(be, L.cq, qd, n, m->dq, d));
+        {
+            oasr_tensor q = make_tensor(OASR_TYPE_F32, m->dq, 64, 1, H, n, (int64_t)d * 4, 256, (int64_t)d * 4);
+            oasr_tensor k = make_tensor(OASR_TYPE_F16, L.cross_kv, 64, T, H, n, (int64_t)d * 4, 128, (int64_t)T * d * 4);
+            oasr_tensor v = make_tensor(OASR_TYPE_F16, L.cross_kv + d, 64, T, H, n, (int64_t)d * 4, 128, (int64_t)T * d * 4);
+            oasr_tensor o = make_tensor(OASR_TYPE_F32, m->dattn, 64, H, 1, n, 256, (int64_t)d * 4, (int64_t)d * 4);
+            W_TRY(launch_flash_attn_ex(be, &q, &k, &v, nullptr, scale, &o, L.b_cq, nullptr));
+        }
+        W_TRY(launch_dgemv_quant(be, L.co, m->dattn, n, m->dt, d));
+        W_TRY(launch_resid_norm_quant(be, m->dx, m->dt, L.b_co, n, d, LN_EPS, false, L.ln2_g, L.ln2_b, nullptr, &qd, df));
+        W_TRY(launch_dgemv(be, L.fc1, qd, n, m->df, m->ffn));
+        W_TRY(launch_bias_gelu_quant(be, m->df, L.b_fc1, n, m->ffn, nullptr, &qf, df));
+        W_TRY(launch_dgemv(be, L.fc2, qf, n, m->dt, d));
+        const float *g_next = last ? m->lnd_g : m->dec[l + 1].ln1_g;
+        const float *b_next = last ? m->lnd_b : m->dec[l + 1].ln1_b;
+        W_TRY(launch_resid_norm_quant(be, m->dx, m->dt, L.b_fc2, n, d, LN_EPS, false, g_next, b_next, nullptr,
+                                      last ? &ql : &qd, last ? FAMILY_Q8_0 : df));
+    }
+    W_TRY(mul_mat_planes(be, m->tok_emb, ql, n, m->logits, m->cfg.n_vocab));
+    W_TRY(launch_argmax_rows(be, m->logits, m->cfg.n_vocab, m->cfg.n_vocab, n, m->tokens));
+    return OASR_STATUS_SUCCESS;
+}
+
 int run_decode_step(oasr_whisper *m, int n) {
+    if (m->fused_dec) return run_decode_step_fused(m, n);
     oasr_backend *be = m->be;
     const int d = m->d, H = m->H, T = m->T_enc, P = m->cfg.n_text_ctx;
     const int df = m->dec_family;
@@ -508,6 +563,17 @@ int oasr_b200_whisper_load(oasr_backend *be, const oasr_whisper_config *cfg, con
     m->dec_family = weight_family(m->dec[0].fc1);
     if (weight_family(m->dec[0].ckv) != m->dec_family)
         return fail(oasr_internal_fail(be, OASR_STATUS_FAILED, "whisper: decoder weights must share one type family"));
+    {
+        // fused decoder GEMVs need every decoder linear in decode tiles;
+        // OASR_B200_DECODE_FUSION=off keeps the unfused kernel sequence
+        const char *env = getenv("OASR_B200_DECODE_FUSION");
+        m->fused_dec = !(env && strcmp(env, "off") == 0) && B <= 8;
+        for (const DecLayer &L : m->dec)
+            m->fused_dec = m->fused_dec && dgemv_supported(L.qkv, false) && dgemv_supported(L.o, true) &&
+                           dgemv_supported(L.cq, false) && dgemv_supported(L.co, true) &&
+                           dgemv_supported(L.fc1, false) && dgemv_supported(L.fc2, false);
+        if (m->fused_dec) L_TRY(dgemv_configure(be));
+    }
     // frontend tables (host-computed like the reference's plan, whisper/mel.rs:64-96)
     {
         std::vector<float> win(N_FFT), filt((size_t)nm * (N_FFT / 2 + 1));
