@@ -67,6 +67,26 @@ static __device__ __forceinline__ void load8(const char *p, float (&out)[8]) {
     }
 }
 
+// Copy n floats that other CTAs wrote (read through L2) into shared memory, 128
+// threads, eight independent loads in flight per thread.
+static __device__ __forceinline__ void stage_l2(float *dst, const float *src, int n) {
+    for (int i0 = threadIdx.x; i0 < n; i0 += 8 * 128) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = i0 + j * 128;
+            v[j] = i < n ? __ldcg(src + i) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int i = i0 + j * 128;
+            if (i < n) dst[i] = v[j];
+        }
+    }
+}
+
+constexpr int FA_HEADS_MAX_SPLITS = 16;  // most KV splits of one query row (partials staged by the merging CTA)
+
 template <int D, int QT, bool F16>
 __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
     griddep_launch_dependents();
@@ -240,15 +260,184 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
     }
     if (a.n_splits == 1) return;
 
-    // last CTA of this (kv head, seq, q tile) merges the split partials
+    // last CTA of this (kv head, seq, q tile) merges the split partials, one query row at
+    // a time: the row's [split][D + 2] partials are staged in shared memory first
     if (!cta_last_arrival(a.counters + blockIdx.x, (unsigned)a.n_splits)) return;
-    for (int o = threadIdx.x; o < QT * D; o += 128) {
-        const int t = o / D, e = o % D;
+    __shared__ float s_part[FA_HEADS_MAX_SPLITS * (D + 2)];
+    for (int t = 0; t < QT; ++t) {
         const int r = qt * QT + t;
-        if (r >= a.QG) continue;
+        if (r >= a.QG) break;  // CTA-uniform
         const int h = hk * a.G + r / a.NQ, iq = r % a.NQ;
         const int64_t row = ((int64_t)s * a.H + h) * a.NQ + iq;
-        const volatile float *pp = a.partials + row * a.n_splits * (D + 2);
+        if (t > 0) __syncthreads();
+        stage_l2(s_part, a.partials + row * a.n_splits * (D + 2), a.n_splits * (D + 2));
+        __syncthreads();
+        for (int e = threadIdx.x; e < D; e += 128) {
+            float M = -INFINITY;
+            for (int sp = 0; sp < a.n_splits; ++sp) M = fmaxf(M, s_part[sp * (D + 2) + D]);
+            float L = 0.0f, A = 0.0f;
+            for (int sp = 0; sp < a.n_splits; ++sp) {
+                const float m = s_part[sp * (D + 2) + D];
+                const float f = m == -INFINITY ? 0.0f : expf(m - M);
+                L += s_part[sp * (D + 2) + D + 1] * f;
+                A += s_part[sp * (D + 2) + e] * f;
+            }
+            float *out = reinterpret_cast<float *>(a.dst + h * a.d_nb1 + iq * a.d_nb2 + s * a.d_nb3);
+            out[e] = L == 0.0f ? 0.0f : A / L;
+        }
+    }
+}
+
+// Decode attention with one query per (sequence, head) over f16 K/V whose heads lie
+// contiguously in a KV row (the Whisper decoder's self- and cross-attention caches):
+// a CTA takes 4 heads of one sequence and a range of KV positions, and every warp
+// reads, per position, the 4 heads' 512 contiguous bytes of K and of V (8 lanes per
+// head, 16 bytes per lane) with U positions of loads in flight, so the cache streams
+// in long sequential runs.  Arithmetic as fattn_split_kernel<64, 1, true>: q rounded
+// to f16, fmaf dot over 8 dims then the 8-lane shuffle tree, exp online softmax; the
+// splits merge in the last-arriving CTA of each (sequence, head group).
+template <int U>
+__global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
+    constexpr int D = 64;
+    griddep_launch_dependents();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int hl = lane >> 3, sl = lane & 7;
+    const int HG = a.H / 4;
+    const int hg = blockIdx.x % HG, s = blockIdx.x / HG, split = blockIdx.y;
+    const int h = 4 * hg + hl;
+    const char *kb = a.k + h * a.k_nb2 + s * a.k_nb3 + sl * 16;
+    const char *vb = a.v + h * a.v_nb2 + s * a.v_nb3 + sl * 16;
+    griddep_wait();
+
+    float qv[8];
+    {
+        const float *qp = reinterpret_cast<const float *>(a.q + h * a.q_nb2 + s * a.q_nb3) + sl * 8;
+        const float *qb = a.q_bias ? a.q_bias + h * D + sl * 8 : nullptr;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            float x = qp[e];
+            if (qb) x = __fadd_rn(x, qb[e]);
+            qv[e] = __half2float(__float2half_rn(x));
+        }
+    }
+    float mx = -INFINITY, sm = 0.0f, acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+
+    const int nkv = a.nkv_dev ? min(*a.nkv_dev, a.NKV) : a.NKV;
+    const int kv0 = split * a.kv_per_split;
+    const int kv1 = min(nkv, kv0 + a.kv_per_split);
+    // register double buffering: the loads of the next U positions are in flight while
+    // the current U are consumed
+    auto load = [&](int pb, int4 (&kr)[U], int4 (&vr)[U]) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int p = pb + 4 * u;
+            if (p < kv1) {
+                kr[u] = *reinterpret_cast<const int4 *>(kb + (int64_t)p * a.k_nb1);
+                vr[u] = *reinterpret_cast<const int4 *>(vb + (int64_t)p * a.v_nb1);
+            } else {
+                kr[u] = vr[u] = make_int4(0, 0, 0, 0);  // weight 0 below; keep 0 * v finite
+            }
+        }
+    };
+    // the U scores are independent: compute them all, then fold the block into the
+    // running softmax state with one rescale (a block-wise online softmax)
+    auto consume = [&](int pb, const int4 (&kr)[U], const int4 (&vr)[U]) {
+        float sc[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            float kf[8];
+            load8<true>(reinterpret_cast<const char *>(&kr[u]), kf);
+            float d = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) d = fmaf(qv[e], kf[e], d);
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+            sc[u] = pb + 4 * u < kv1 ? d * a.scale : -INFINITY;
+        }
+        float mb = sc[0];
+#pragma unroll
+        for (int u = 1; u < U; ++u) mb = fmaxf(mb, sc[u]);
+        const float mnew = fmaxf(mx, mb);    // finite: position pb is valid
+        const float corr = expf(mx - mnew);  // mx = -inf -> 0
+        sm *= corr;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] *= corr;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const float w = expf(sc[u] - mnew);  // invalid positions: exp(-inf) = 0
+            float vf[8];
+            load8<true>(reinterpret_cast<const char *>(&vr[u]), vf);
+            sm += w;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] = fmaf(w, vf[e], acc[e]);
+        }
+        mx = mnew;
+    };
+    int4 kA[U], vA[U], kB[U], vB[U];
+    int pb = kv0 + warp;
+    if (pb < kv1) load(pb, kA, vA);
+    while (pb < kv1) {
+        int pn = pb + 4 * U;
+        if (pn < kv1) load(pn, kB, vB);
+        consume(pb, kA, vA);
+        pb = pn;
+        if (pb >= kv1) break;
+        pn = pb + 4 * U;
+        if (pn < kv1) load(pn, kA, vA);
+        consume(pb, kB, vB);
+        pb = pn;
+    }
+
+    // merge the 4 warps (disjoint positions, same heads) through shared memory
+    __shared__ float s_m[4][4], s_s[4][4];
+    __shared__ float s_acc[4][4][D];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s_acc[warp][hl][sl * 8 + e] = acc[e];
+    if (sl == 0) {
+        s_m[warp][hl] = mx;
+        s_s[warp][hl] = sm;
+    }
+    __syncthreads();
+    for (int o = threadIdx.x; o < 4 * D; o += 128) {
+        const int t = o / D, e = o % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, s_m[w][t]);
+        float L = 0.0f, A = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const float f = s_m[w][t] == -INFINITY ? 0.0f : expf(s_m[w][t] - M);
+            L += s_s[w][t] * f;
+            A += s_acc[w][t][e] * f;
+        }
+        const int hh = 4 * hg + t;
+        if (a.n_splits == 1) {
+            float *out = reinterpret_cast<float *>(a.dst + hh * a.d_nb1 + s * a.d_nb3);
+            out[e] = L == 0.0f ? 0.0f : A / L;
+        } else {
+            const int64_t row = (int64_t)s * a.H + hh;
+            float *pp = a.partials + (row * a.n_splits + split) * (D + 2);
+            pp[e] = A;
+            if (e == 0) {
+                pp[D] = M;
+                pp[D + 1] = L;
+            }
+        }
+    }
+    if (a.n_splits == 1) return;
+    if (!cta_last_arrival(a.counters + blockIdx.x, (unsigned)a.n_splits)) return;
+    // the 4 heads' partials are contiguous ([head][split][D + 2]): stage them in shared
+    // memory with every load in flight, then merge in split order
+    __shared__ float s_part[4 * FA_HEADS_MAX_SPLITS * (D + 2)];
+    const int nP = 4 * a.n_splits * (D + 2);
+    const float *pbase = a.partials + ((int64_t)s * a.H + 4 * hg) * a.n_splits * (D + 2);
+    stage_l2(s_part, pbase, nP);
+    __syncthreads();
+    for (int o = threadIdx.x; o < 4 * D; o += 128) {
+        const int t = o / D, e = o % D;
+        const float *pp = s_part + t * a.n_splits * (D + 2);
         float M = -INFINITY;
         for (int sp = 0; sp < a.n_splits; ++sp) M = fmaxf(M, pp[sp * (D + 2) + D]);
         float L = 0.0f, A = 0.0f;
@@ -258,7 +447,7 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
             L += pp[sp * (D + 2) + D + 1] * f;
             A += pp[sp * (D + 2) + e] * f;
         }
-        float *out = reinterpret_cast<float *>(a.dst + h * a.d_nb1 + iq * a.d_nb2 + s * a.d_nb3);
+        float *out = reinterpret_cast<float *>(a.dst + (4 * hg + t) * a.d_nb1 + s * a.d_nb3);
         out[e] = L == 0.0f ? 0.0f : A / L;
     }
 }
@@ -371,11 +560,21 @@ static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const
     const int QT = a.QG >= 8 ? 8 : (a.QG >= 4 ? 4 : (a.QG >= 2 ? 2 : 1));
     a.n_qtiles = (a.QG + QT - 1) / QT;
     a.scale = scale;
-    const int64_t groups = (int64_t)a.HKV * a.S * a.n_qtiles;
+    // one query per (sequence, head), f16 heads contiguous in a KV row: the 4-head kernel
+    const bool heads = D == 64 && k->type == OASR_TYPE_F16 && a.NQ == 1 && a.G == 1 && !mask && a.H % 4 == 0 &&
+                       k->nb[2] == 2 * D && v->nb[2] == 2 * D && a.S * (int64_t)(a.H / 4) <= (1 << 16);
+    const int64_t groups = heads ? (int64_t)a.S * (a.H / 4) : (int64_t)a.HKV * a.S * a.n_qtiles;
     int n_splits = 1;
-    if (groups < 4LL * be->sm_count && groups <= (1 << 16)) {
+    if (heads) {
+        // one full wave of resident CTAs, at least 32 positions per split
+        static int occ = 0;  // resident CTAs per SM (same for every device of this build)
+        if (occ == 0 && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fattn_heads_kernel<8>, 128, 0) != cudaSuccess)
+            occ = 1;
+        n_splits = (int)(((int64_t)be->sm_count * std::max(occ, 1)) / groups);
+        n_splits = std::max(1, std::min(std::min(n_splits, a.NKV / 32), FA_HEADS_MAX_SPLITS));
+    } else if (groups < 4LL * be->sm_count && groups <= (1 << 16)) {
         n_splits = (int)((4LL * be->sm_count + groups - 1) / groups);
-        n_splits = std::min(n_splits, std::max(1, a.NKV / 64));
+        n_splits = std::min(std::min(n_splits, std::max(1, a.NKV / 64)), FA_HEADS_MAX_SPLITS);
     }
     a.n_splits = n_splits;
     a.kv_per_split = (a.NKV + n_splits - 1) / n_splits;
@@ -402,7 +601,8 @@ static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const
     dim3 grid((unsigned)groups, n_splits);
     const bool f16 = k->type == OASR_TYPE_F16;
     cudaError_t e;
-    if (D == 64) e = f16 ? launch_fa_d<64, true>(be, a, QT, grid) : launch_fa_d<64, false>(be, a, QT, grid);
+    if (heads) e = launch_k(be, fattn_heads_kernel<8>, grid, dim3(128), 0, a);
+    else if (D == 64) e = f16 ? launch_fa_d<64, true>(be, a, QT, grid) : launch_fa_d<64, false>(be, a, QT, grid);
     else e = f16 ? launch_fa_d<128, true>(be, a, QT, grid) : launch_fa_d<128, false>(be, a, QT, grid);
     if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "flash_attn launch", __LINE__);
     return oasr_internal_launch_check(be, "flash_attn");

@@ -159,3 +159,31 @@ def test_tensor_core_flash_attention_shapes(gpu_backend, S, H, HKV, NQ, NKV):
     ref = oo.flash_attn_ext(q, k, v, None, 0.125, oo.FA_F32)
     err = max_abs_rel(got, ref)
     assert err <= TOL, err
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("S,H,NKV", [(8, 20, 1500), (8, 20, 1), (1, 20, 33), (3, 8, 1500), (2, 4, 5), (8, 20, 447)])
+def test_head_contiguous_kv_rows(gpu_backend, S, H, NKV):
+    """Decoder caches whose heads are contiguous in a KV row: the cross cache
+    [seq][frame][K (H*64) | V (H*64)] and the self cache [seq][pos][H*64]
+    (the 4-head decode kernel's layout), one query per head."""
+    import torch
+
+    D = 64
+    rng = np.random.default_rng(400 + S * H + NKV)
+    kv = rng.normal(0, 1, (S, NKV, 2 * H * D)).astype(np.float16)
+    q = rng.normal(0, 1, (S, 1, H * D)).astype(np.float32)
+    kvt = torch.from_numpy(kv).cuda()
+    kt = kvt[:, :, : H * D].reshape(S, NKV, H, D).permute(0, 2, 1, 3)
+    vt = kvt[:, :, H * D:].reshape(S, NKV, H, D).permute(0, 2, 1, 3)
+    qt = torch.from_numpy(q).cuda().reshape(S, 1, H, D).permute(0, 2, 1, 3)
+    out = torch.full((S, 1, H, D), float("nan"), dtype=torch.float32, device="cuda")
+    gpu_backend.flash_attn_ext(qt, kt, vt, None, 0.125, out)
+    gpu_backend.synchronize()
+    qn = q.reshape(S, 1, H, D).transpose(0, 2, 1, 3)
+    kn = kv[:, :, : H * D].reshape(S, NKV, H, D).transpose(0, 2, 1, 3)
+    vn = kv[:, :, H * D:].reshape(S, NKV, H, D).transpose(0, 2, 1, 3)
+    ref = oo.flash_attn_ext(np.ascontiguousarray(qn), np.ascontiguousarray(kn), np.ascontiguousarray(vn), None, 0.125,
+                            oo.FA_F32)
+    err = max_abs_rel(out.cpu().numpy(), ref)
+    assert err <= TOL and err <= TIGHT, err
