@@ -73,6 +73,7 @@ struct oasr_whisper {
     // decoder activations, B rows
     float *dx, *dqkv, *dq, *dattn, *dt, *df, *logits;
     bool fused_dec;  // decoder GEMVs run as dgemv (prologue/epilogue fused), see run_decode_step
+    bool pdl;        // programmatic dependent launch inside the step graph (OASR_B200_PDL=0 turns it off)
     void *dqa_d, *dqa_f, *dqa_lm;
     int *tokens, *pos, *nkv, *history;
     int enc_family, dec_family;
@@ -373,7 +374,7 @@ int decode_step_graph(oasr_whisper *m, int n) {
         OASR_CUDA_TRY(be, cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
         // inside the step graph every kernel waits on its predecessor with griddepcontrol,
         // so successive launches overlap their prologues (programmatic dependent launch)
-        be->pdl = true;
+        be->pdl = m->pdl;
         int st = run_decode_step(m, n);
         if (st == OASR_STATUS_SUCCESS) {
             const cudaError_t le = launch_k(be, advance_kernel, dim3(1), dim3(32), 0, (const int *)m->tokens, m->pos,
@@ -566,6 +567,8 @@ int oasr_b200_whisper_load(oasr_backend *be, const oasr_whisper_config *cfg, con
     {
         // fused decoder GEMVs need every decoder linear in decode tiles;
         // OASR_B200_DECODE_FUSION=off keeps the unfused kernel sequence
+        const char *pdl_env = getenv("OASR_B200_PDL");
+        m->pdl = !(pdl_env && strcmp(pdl_env, "0") == 0);
         const char *env = getenv("OASR_B200_DECODE_FUSION");
         m->fused_dec = !(env && strcmp(env, "off") == 0) && B <= 8;
         for (const DecLayer &L : m->dec)
