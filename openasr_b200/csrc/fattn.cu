@@ -85,6 +85,7 @@ static __device__ __forceinline__ void stage_l2(float *dst, const float *src, in
     }
 }
 
+constexpr int FA_HEADS_U = 8;            // KV positions per warp load batch (double buffered)
 constexpr int FA_HEADS_MAX_SPLITS = 16;  // most KV splits of one query row (partials staged by the merging CTA)
 
 template <int D, int QT, bool F16>
@@ -568,7 +569,7 @@ static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const
     if (heads) {
         // one full wave of resident CTAs, at least 32 positions per split
         static int occ = 0;  // resident CTAs per SM (same for every device of this build)
-        if (occ == 0 && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fattn_heads_kernel<8>, 128, 0) != cudaSuccess)
+        if (occ == 0 && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fattn_heads_kernel<FA_HEADS_U>, 128, 0) != cudaSuccess)
             occ = 1;
         n_splits = (int)(((int64_t)be->sm_count * std::max(occ, 1)) / groups);
         n_splits = std::max(1, std::min(std::min(n_splits, a.NKV / 32), FA_HEADS_MAX_SPLITS));
@@ -601,7 +602,7 @@ static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const
     dim3 grid((unsigned)groups, n_splits);
     const bool f16 = k->type == OASR_TYPE_F16;
     cudaError_t e;
-    if (heads) e = launch_k(be, fattn_heads_kernel<8>, grid, dim3(128), 0, a);
+    if (heads) e = launch_k(be, fattn_heads_kernel<FA_HEADS_U>, grid, dim3(128), 0, a);
     else if (D == 64) e = f16 ? launch_fa_d<64, true>(be, a, QT, grid) : launch_fa_d<64, false>(be, a, QT, grid);
     else e = f16 ? launch_fa_d<128, true>(be, a, QT, grid) : launch_fa_d<128, false>(be, a, QT, grid);
     if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "flash_attn launch", __LINE__);

@@ -34,10 +34,11 @@
 
 namespace oasr {
 
-// One CTA per 16-row tile; warp w handles super-blocks w, w + W, ... with the next
-// unit's loads issued before the current one's MMAs; the W partial tiles are
-// summed in shared memory in warp order.
-template <int W>
+// One CTA per 16-row tile; warp w handles super-blocks w, w + W, ... (LOOP: with the
+// next unit's loads issued before the current one's MMAs; !LOOP: W >= super-blocks,
+// one unit per warp, all loads issued at once); the W partial tiles are summed in
+// shared memory in warp order.
+template <int W, bool LOOP>
 __global__ void __launch_bounds__(W * 32) mmv_q4k_tc_kernel(const uint8_t *__restrict__ tiles, int nsb, int64_t N,
                                                             int M, const int8_t *__restrict__ aqs,
                                                             const float *__restrict__ ad,
@@ -61,13 +62,19 @@ __global__ void __launch_bounds__(W * 32) mmv_q4k_tc_kernel(const uint8_t *__res
     const int8_t *arow = aqs + (int64_t)gr * K;
     const int16_t *brow = abs16 + (int64_t)gr * (K / 16);
     const int m0 = 2 * t, m1 = 2 * t + 1;  // C-fragment activation rows
-    for (; s < nsb; s += W) {
-        const bool more = s + W < nsb;
-        if (more) load_q4k_unit(nxt, tile + (int64_t)(s + W) * Q4K_UNIT, lane, g);
+    if (LOOP) {
+        for (; s < nsb; s += W) {
+            const bool more = s + W < nsb;
+            if (more) load_q4k_unit(nxt, tile + (int64_t)(s + W) * Q4K_UNIT, lane, g);
+            const float da0 = m0 < M ? __ldg(ad + (int64_t)m0 * nsb + s) : 0.0f;
+            const float da1 = m1 < M ? __ldg(ad + (int64_t)m1 * nsb + s) : 0.0f;
+            q4k_unit_accumulate<false>(acc, cur, s, arow, brow, da0, da1, t);
+            if (more) cur = nxt;
+        }
+    } else if (s < nsb) {
         const float da0 = m0 < M ? __ldg(ad + (int64_t)m0 * nsb + s) : 0.0f;
         const float da1 = m1 < M ? __ldg(ad + (int64_t)m1 * nsb + s) : 0.0f;
         q4k_unit_accumulate<false>(acc, cur, s, arow, brow, da0, da1, t);
-        if (more) cur = nxt;
     }
     if (!reduce_warps<W>(acc, red, warp, lane)) return;
     const int64_t ra = (int64_t)blockIdx.x * TILE_ROWS + g, rb = ra + 8;
@@ -239,12 +246,12 @@ cudaError_t build_mmv_tiles(oasr_weight *w, cudaStream_t st) {
 // ---- launcher -------------------------------------------------------------------------
 // Warps per CTA: one per unit of a tile up to 8 (Q4_K: K <= 2048 gives one super-block
 // per warp); larger K loops with the next unit's loads issued ahead.
-template <int W>
+template <int W, bool LOOP>
 static cudaError_t launch_q4k_w(oasr_backend *be, const uint8_t *tiles, int nsb, int64_t N, int M, const ActPlanes &a,
                                 int K, float *y, int64_t y_ld) {
     const unsigned grid = (unsigned)((N + TILE_ROWS - 1) / TILE_ROWS);
-    return launch_k(be, mmv_q4k_tc_kernel<W>, dim3(grid), dim3(W * 32), 0, tiles, nsb, N, M, (const int8_t *)a.qs,
-                    (const float *)a.d, (const int16_t *)a.bs16, K, y, y_ld);
+    return launch_k(be, mmv_q4k_tc_kernel<W, LOOP>, dim3(grid), dim3(W * 32), 0, tiles, nsb, N, M,
+                    (const int8_t *)a.qs, (const float *)a.d, (const int16_t *)a.bs16, K, y, y_ld);
 }
 
 template <int W>
@@ -262,11 +269,17 @@ int launch_mmv_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, const A
     cudaError_t e;
     if (w->type == OASR_TYPE_Q4_K) {
         const int nsb = K / 256;
-        if (nsb <= 1) e = launch_q4k_w<1>(be, tiles, nsb, N, M, a, K, y, y_ld);
-        else if (nsb <= 2) e = launch_q4k_w<2>(be, tiles, nsb, N, M, a, K, y, y_ld);
-        else if (nsb <= 4) e = launch_q4k_w<4>(be, tiles, nsb, N, M, a, K, y, y_ld);
-        else if (nsb <= 5) e = launch_q4k_w<5>(be, tiles, nsb, N, M, a, K, y, y_ld);
-        else e = launch_q4k_w<8>(be, tiles, nsb, N, M, a, K, y, y_ld);
+        // one super-block per warp up to 32 of them (K <= 8192), else 8 looping warps
+        if (nsb <= 1) e = launch_q4k_w<1, false>(be, tiles, nsb, N, M, a, K, y, y_ld);
+        else if (nsb <= 2) e = launch_q4k_w<2, false>(be, tiles, nsb, N, M, a, K, y, y_ld);
+        else if (nsb <= 4) e = launch_q4k_w<4, false>(be, tiles, nsb, N, M, a, K, y, y_ld);
+        else if (nsb <= 5) e = launch_q4k_w<5, false>(be, tiles, nsb, N, M, a, K, y, y_ld);
+        else if (nsb <= 8) e = launch_q4k_w<8, false>(be, tiles, nsb, N, M, a, K, y, y_ld);
+        else if (nsb <= 12) e = launch_q4k_w<12, false>(be, tiles, nsb, N, M, a, K, y, y_ld);
+        else if (nsb <= 16) e = launch_q4k_w<16, false>(be, tiles, nsb, N, M, a, K, y, y_ld);
+        else if (nsb <= 20) e = launch_q4k_w<20, false>(be, tiles, nsb, N, M, a, K, y, y_ld);
+        else if (nsb <= 32) e = launch_q4k_w<32, false>(be, tiles, nsb, N, M, a, K, y, y_ld);
+        else e = launch_q4k_w<8, true>(be, tiles, nsb, N, M, a, K, y, y_ld);
     } else {
         const int npairs = K / 64;
         // long rows (e.g. the logits head) keep 4 warps per tile, each looping over ~5 units

@@ -273,7 +273,7 @@ static int run_decode_step_fused(oasr_whisper *m, int n) {
         }
         W_TRY(launch_dgemv_quant(be, L.o, m->dattn, n, m->dt, d));
         W_TRY(launch_resid_norm_quant(be, m->dx, m->dt, L.b_o, n, d, LN_EPS, false, L.lnc_g, L.lnc_b, nullptr, &qd, df));
-        W_TRY(launch_dgemv(be, L.cq, qd, n, m->dq, d));
+        W_TRY(mul_mat_planes(be, L.cq, qd, n, m->dq, d));
         {
             oasr_tensor q = make_tensor(OASR_TYPE_F32, m->dq, 64, 1, H, n, (int64_t)d * 4, 256, (int64_t)d * 4);
             oasr_tensor k = make_tensor(OASR_TYPE_F16, L.cross_kv, 64, T, H, n, (int64_t)d * 4, 128, (int64_t)T * d * 4);
@@ -283,9 +283,9 @@ static int run_decode_step_fused(oasr_whisper *m, int n) {
         }
         W_TRY(launch_dgemv_quant(be, L.co, m->dattn, n, m->dt, d));
         W_TRY(launch_resid_norm_quant(be, m->dx, m->dt, L.b_co, n, d, LN_EPS, false, L.ln2_g, L.ln2_b, nullptr, &qd, df));
-        W_TRY(launch_dgemv(be, L.fc1, qd, n, m->df, m->ffn));
+        W_TRY(mul_mat_planes(be, L.fc1, qd, n, m->df, m->ffn));
         W_TRY(launch_bias_gelu_quant(be, m->df, L.b_fc1, n, m->ffn, nullptr, &qf, df));
-        W_TRY(launch_dgemv(be, L.fc2, qf, n, m->dt, d));
+        W_TRY(mul_mat_planes(be, L.fc2, qf, n, m->dt, d));
         const float *g_next = last ? m->lnd_g : m->dec[l + 1].ln1_g;
         const float *b_next = last ? m->lnd_b : m->dec[l + 1].ln1_b;
         W_TRY(launch_resid_norm_quant(be, m->dx, m->dt, L.b_fc2, n, d, LN_EPS, false, g_next, b_next, nullptr,
