@@ -182,23 +182,29 @@ int oasr_b200_flash_attn_ext(oasr_backend *be, const oasr_tensor *q, const oasr_
                              const oasr_tensor *v, const oasr_tensor *mask, float scale, float max_bias,
                              float logit_softcap, int32_t prec, oasr_tensor *dst);
 
-/* Allocation-free GGML_OP_FLASH_ATTN_EXT.  No reference counterpart: the
- * reference has no entry point that promises to allocate nothing.  Same
- * arguments, checks and results as oasr_b200_flash_attn_ext for every shape
- * that call runs through its split-KV kernel (decode and short prefill); it
- * always uses that kernel, never the tensor-core encoder path (whose staging
- * copies need backend scratch).  The split-KV partials and tickets live in a
- * file-scope device array of 4 MiB of partials and 1024 tickets per device;
- * a shape that needs more fails with OASR_STATUS_FAILED and a message naming
- * both sizes, and nothing is launched.  Calls neither allocate nor free device
- * or host memory.
+/* Allocation-free GGML_OP_FLASH_ATTN_EXT.  No reference counterpart.
+ * For callers that must not allocate device memory once they are running: a
+ * host whose memory planner reserves the GPU's budget up front and treats any
+ * later allocation as a failure, or a real-time decode loop where a
+ * cudaMalloc (which may synchronise the device) would stall the audio
+ * pipeline.  oasr_b200_flash_attn_ext may grow the backend's scratch; this
+ * call never allocates or frees device or host memory.
+ * Same arguments, checks and results as oasr_b200_flash_attn_ext for every
+ * shape that call runs through its split-KV kernels (decode and short
+ * prefill); it always uses those kernels, never the tensor-core encoder path
+ * (whose staging copies need backend scratch).  The split-KV partials and
+ * tickets live in a file-scope device array: 4 MiB of partials and 1024
+ * tickets, held on every GPU that loads the library until the process exits.
+ * A shape that needs more fails with OASR_STATUS_FAILED and a message naming
+ * both sizes, and nothing is launched.
  *  - The tickets must be zero when a launch starts: they are zero when the
- *    module loads and every launch leaves them at zero.
+ *    module loads and every launch leaves them at zero.  The partials need no
+ *    initial value (each split writes its slot before the merge reads it).
  *  - Calls that overlap on one device (two streams, two backends, or two
  *    host threads without ordering) share that array and race: serialise them.
- *  - The first call on a device looks the array's address up (which may load
- *    the module); make it outside stream capture.  A first call during capture
- *    is refused.  Later calls may be captured into CUDA graphs. */
+ *  - The first call on a device looks the array's address up
+ *    (cudaGetSymbolAddress, which may load the module); make that first call
+ *    before any stream capture.  A first call made during capture is refused. */
 int oasr_b200_flash_attn_ext_static(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k,
                                     const oasr_tensor *v, const oasr_tensor *mask, float scale, float max_bias,
                                     float logit_softcap, int32_t prec, oasr_tensor *dst);

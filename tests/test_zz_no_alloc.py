@@ -1,9 +1,11 @@
 """oasr_b200_flash_attn_ext_static: the allocation-free attention entry point.
 
-It runs the split-KV kernel over a file-scope device array instead of the
+Hosts that reserve all device memory up front (or cannot afford a
+synchronising cudaMalloc inside a real-time decode loop) call this variant: it
+runs the split-KV kernels over a file-scope device array instead of the
 backend's growable scratch.  Its results must equal oasr_b200_flash_attn_ext
 bit for bit on the shapes that entry point also runs through the split-KV
-kernel, on consecutive calls (the per-group tickets must be back at zero after
+kernels, on consecutive calls (the per-group tickets must be back at zero after
 each call), and it must leave the backend's scratch untouched.  This file is
 collected last so that it also runs after every other GPU test."""
 import os
