@@ -307,6 +307,14 @@ int oasr_b200_weight_upload(oasr_backend *be, const void *host, size_t bytes, in
         if (e == cudaSuccess) e = cudaMemcpy(w->qs, src, bytes, cudaMemcpyHostToDevice);
     }
     w->tiles = nullptr;
+    w->dT = nullptr;
+    if (e == cudaSuccess && mmq_q80_tc_supported(type, ne[1], ne[0])) {
+        const size_t db = (size_t)(ne[2] * ne[3] * (ne[0] / 32) * ne[1]) * sizeof(float);
+        e = cudaMalloc(&w->dT, db);
+        if (e == cudaSuccess) e = build_q80_scales_t(w, be->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(be->stream);
+        if (e == cudaSuccess) w->device_bytes += db;
+    }
     if (e == cudaSuccess && be->decode_tiles && mmv_tiles_supported(type, ne[0])) {
         // decode-tile copy for the tensor-core GEMV, built on the device from the planes above
         const size_t tb = mmv_tiles_bytes(type, ne[1], ne[0], ne[2] * ne[3]);
@@ -319,6 +327,7 @@ int oasr_b200_weight_upload(oasr_backend *be, const void *host, size_t bytes, in
         if (w->qs) cudaFree(w->qs);
         if (w->d) cudaFree(w->d);
         if (w->tiles) cudaFree(w->tiles);
+        if (w->dT) cudaFree(w->dT);
         delete w;
         return oasr_internal_cuda_fail(be, e, "weight_upload", __LINE__);
     }
@@ -339,6 +348,7 @@ int oasr_b200_weight_free(oasr_backend *be, oasr_weight *w) {
     if (w->qs) cudaFree(w->qs);
     if (w->d) cudaFree(w->d);
     if (w->tiles) cudaFree(w->tiles);
+    if (w->dT) cudaFree(w->dT);
     delete w;
     return OASR_STATUS_SUCCESS;
 }

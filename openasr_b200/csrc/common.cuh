@@ -49,6 +49,7 @@ struct oasr_weight {
     int64_t qs_row_bytes;    // bytes per row in the qs plane
     int64_t d_row_elems;     // fp16 scales per row in the d plane
     uint8_t *tiles;          // decode-tile copy for the tensor-core GEMV (Q4_K, Q8_0), or null
+    float *dT;               // Q8_0: block-major f32 scales [slices][K/32][N] for the tensor-core GEMM, or null
     uint64_t device_bytes;
 };
 

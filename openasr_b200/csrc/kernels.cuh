@@ -79,7 +79,9 @@ int launch_mmv_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, const A
 int launch_mmv_float(oasr_backend *be, const oasr_weight *w, int64_t slice, const char *x, int64_t x_ld_bytes,
                      bool x_f16, bool round_x_f16, int M, int K, float *y, int64_t y_ld);
 
-// prefill / encoder GEMM (M > 8)
+// prefill / encoder GEMM (M > 8); Q8_0 on tcgen05 needs the block-major scale copy
+bool mmq_q80_tc_supported(int type, int64_t N, int64_t K);
+cudaError_t build_q80_scales_t(oasr_weight *w, cudaStream_t st);
 int launch_mmq(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int64_t M, int K,
                float *y, int64_t y_ld);
 

@@ -23,8 +23,8 @@
 // TMEM: two accumulator sets (isum 128 cols + msum 128 cols) so the epilogue
 // of super-block s overlaps the MMAs of s+1.  Every mbarrier wait is bounded.
 //
-// Q8_0 / Q4_0 (per-32 scales) still use the K1 GEMV kernel over groups of 8
-// rows in this revision.
+// Q8_0 runs on tcgen05 kind::i8 (mmq_q80_tc_kernel below); Q4_0 still uses the
+// K1 GEMV kernel over groups of 8 rows.
 #include <cudaTypedefs.h>
 
 #include "kernels.cuh"
@@ -329,6 +329,211 @@ __global__ void __launch_bounds__(448, 1)
     }
 }
 
+// ---- Q8_0: tcgen05 kind::i8 -------------------------------------------------------------------
+// ggml CPU (vec_dot_q8_0_q8_0) forms, per 32-element block b, the integer dot isum_b
+// and adds (float)isum_b * (d_w,b * d_a,b) to an f32 sum in block order.  One
+// tcgen05.mma.kind::i8 (K = 32 bytes = one block) writes isum_b for a 128 x 128 tile
+// into its own TMEM buffer (four buffers rotate); sixteen epilogue warps read each
+// buffer as soon as its MMA commits and apply that block's term with ggml's roundings,
+// so the result equals the CPU oracle bit for bit.  Per stage TMA brings 128 K of
+// activations and of weights (int8, 128B swizzle) and the 4 blocks' weight scales
+// (f32, block-major copy made at upload).
+// Warps: 0 TMA producer, 1 TMEM allocator + MMA issuer, 2-17 epilogue (warp w reads
+// TMEM lane quarter w % 4, 32 of the 128 columns).
+namespace q80 {
+constexpr int BM = 128, BN = 128, BK = 128;  // BK bytes = 4 blocks per stage
+constexpr int STAGES = 4;
+constexpr int TILE = 128 * 128;
+constexpr int DWTILE = 4 * BN * 4;           // 4 blocks x 128 weight rows, f32
+constexpr int STAGE_BYTES = 2 * TILE + DWTILE;
+constexpr int NTHREADS = 576;
+constexpr int OFF_A = 0;
+constexpr int OFF_B = OFF_A + STAGES * TILE;
+constexpr int OFF_DW = OFF_B + STAGES * TILE;
+constexpr int OFF_BAR = OFF_DW + STAGES * DWTILE;
+constexpr int NBAR = 2 * STAGES + 8 + 1;
+constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+}  // namespace q80
+
+__global__ void __launch_bounds__(576, 1)
+    mmq_q80_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
+                      const __grid_constant__ CUtensorMap tmap_dw, int N, const float *__restrict__ ad, int M, int K,
+                      float *__restrict__ y, int64_t y_ld, int *err) {
+    using namespace q80;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = (uint64_t *)(smem + OFF_BAR);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + STAGES;
+    uint64_t *tmem_full = bars + 2 * STAGES;
+    uint64_t *tmem_empty = tmem_full + 4;
+    uint64_t *done = tmem_empty + 4;
+    uint32_t *tmem_slot = (uint32_t *)(smem + OFF_MISC);
+    volatile int *abort_flag = (volatile int *)(smem + OFF_MISC + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int nkc = K / BK, nb = K / 32;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1 + 16);  // MMA commit + every epilogue warp (weight scales read)
+        }
+        for (int i = 0; i < 4; ++i) {
+            mbar_init(&tmem_full[i], 1);
+            mbar_init(&tmem_empty[i], 16);
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int issued = 0;
+            for (int kc = 0; kc < nkc; ++kc) {
+                const int s = kc % STAGES;
+                if (!mbar_wait(&empty[s], ((kc / STAGES) & 1) ^ 1, abort_flag, err)) break;
+                mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+                tma_load_2d(smem + OFF_A + s * TILE, &tmap_a, &full[s], kc * BK, m0);
+                tma_load_2d(smem + OFF_B + s * TILE, &tmap_w, &full[s], kc * BK, n0);
+                tma_load_2d(smem + OFF_DW + s * DWTILE, &tmap_dw, &full[s], n0, kc * 4);
+                issued = kc + 1;
+            }
+            // no TMA write may still be in flight when the CTA exits
+            for (int kc = max(0, issued - STAGES); kc < issued; ++kc) {
+                const long long t0 = clock64();
+                while (!mbar_try_wait(&full[kc % STAGES], (kc / STAGES) & 1) && clock64() - t0 < (1LL << 31)) {
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_s8_s32(BM, BN);
+            bool ok = true;
+            for (int kc = 0; kc < nkc && ok; ++kc) {
+                const int s = kc % STAGES;
+                if (!mbar_wait(&full[s], (kc / STAGES) & 1, abort_flag, err)) break;
+                tc_fence_after();
+                const uint64_t da = sw128_desc(smem_u32(smem + OFF_A + s * TILE));
+                const uint64_t db = sw128_desc(smem_u32(smem + OFF_B + s * TILE));
+                for (int j = 0; j < 4; ++j) {  // block 4kc + j -> TMEM buffer j
+                    if (!mbar_wait(&tmem_empty[j], (kc & 1) ^ 1, abort_flag, err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    umma_i8(tmem + 128 * j, da + 2 * j, db + 2 * j, idesc, 0);
+                    umma_commit(&tmem_full[j]);
+                }
+                umma_commit(&empty[s]);
+            }
+            umma_commit(done);
+            const long long t0 = clock64();
+            while (!mbar_try_wait(done, 0) && clock64() - t0 < (1LL << 31)) {
+            }
+        }
+    } else {
+        // ---- epilogue: row m0 + 32q + lane, columns n0 + 32c .. +31 ----
+        const int q = warp & 3, c = (warp - 2) >> 2;
+        const int row = m0 + 32 * q + lane;
+        const bool rv = row < M;
+        float acc[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+        const float *adr = ad + (int64_t)(rv ? row : 0) * nb;
+        float4 da_next = rv ? *reinterpret_cast<const float4 *>(adr) : make_float4(0, 0, 0, 0);
+        for (int kc = 0; kc < nkc; ++kc) {
+            const int s = kc % STAGES;
+            const float4 da4 = da_next;
+            if (rv && kc + 1 < nkc) da_next = *reinterpret_cast<const float4 *>(adr + 4 * (kc + 1));
+            // observe the stage's TMA completion: makes the weight-scale tile visible here
+            if (!mbar_wait(&full[s], (kc / STAGES) & 1, abort_flag, err)) break;
+            bool ok = true;
+            for (int j = 0; j < 4; ++j) {
+                if (!mbar_wait(&tmem_full[j], kc & 1, abort_flag, err)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const float da = j == 0 ? da4.x : (j == 1 ? da4.y : (j == 2 ? da4.z : da4.w));
+                const float *dw = reinterpret_cast<const float *>(smem + OFF_DW + s * DWTILE) + j * BN + 32 * c;
+                const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(128 * j + 32 * c);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t r[16];
+                    tmem_ld16(tb + 16 * h, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 16; i += 4) {
+                        const float4 w4 = *reinterpret_cast<const float4 *>(dw + 16 * h + i);
+                        const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const float dd = __fmul_rn(wv[u], da);
+                            acc[16 * h + i + u] = __fadd_rn(acc[16 * h + i + u],
+                                                            __fmul_rn((float)(int)r[i + u], dd));
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tmem_empty[j]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            if (!ok) break;
+        }
+        if (rv) {
+            float *yr = y + (int64_t)row * y_ld + n0 + 32 * c;
+            if (n0 + 32 * c + 32 <= N && (((uintptr_t)yr) & 15) == 0) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4 *>(yr + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                    if (n0 + 32 * c + i < N) yr[i] = acc[i];
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// block-major f32 copy of the Q8_0 scale plane: dT[slice][b][n] = d[slice][n][b]
+__global__ void q80_scales_t_kernel(const uint16_t *__restrict__ d, int64_t N, int nb, int64_t total,
+                                    float *__restrict__ dT) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t n = i % N, t = i / N;
+        const int64_t b = t % nb, sl = t / nb;
+        dT[i] = h2f(d[(sl * N + n) * nb + b]);
+    }
+}
+
+cudaError_t build_q80_scales_t(oasr_weight *w, cudaStream_t st) {
+    const int64_t N = w->ne[1], nb = w->ne[0] / 32, slices = w->ne[2] * w->ne[3];
+    const int64_t total = slices * nb * N;
+    const unsigned grid = (unsigned)std::min<int64_t>((total + 255) / 256, 65535);
+    q80_scales_t_kernel<<<grid, 256, 0, st>>>(w->d, N, (int)nb, total, w->dT);
+    return cudaGetLastError();
+}
+
+bool mmq_q80_tc_supported(int type, int64_t N, int64_t K) {
+    return type == OASR_TYPE_Q8_0 && K % q80::BK == 0 && N % 4 == 0;
+}
+
 // ---- host side ----------------------------------------------------------------------------
 static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -379,10 +584,37 @@ static int launch_q4k_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, 
     return oasr_internal_launch_check(be, "mmq_q4k_tc");
 }
 
+static int launch_q80_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int64_t M, int K,
+                         float *y, int64_t y_ld) {
+    const int64_t N = w->ne[1];
+    CUtensorMap map_a, map_w, map_dw;
+    // activations and weights: int8 [rows][K], 128 rows x 128 bytes per box, 128B swizzle
+    int st = encode_2d(be, &map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.qs, K, M, (uint64_t)K, 128, 128,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    st = encode_2d(be, &map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->qs + slice * N * w->qs_row_bytes, K, N,
+                   (uint64_t)w->qs_row_bytes, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    // weight scales, block-major f32 [K/32][N]: 128 weight rows x 4 blocks per box
+    st = encode_2d(be, &map_dw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->dT + slice * (int64_t)(K / 32) * N, N, K / 32,
+                   (uint64_t)N * 4, 128, 4, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(mmq_q80_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, q80::SMEM_BYTES);
+        attr_set = true;
+    }
+    dim3 grid((unsigned)((N + q80::BN - 1) / q80::BN), (unsigned)((M + q80::BM - 1) / q80::BM));
+    mmq_q80_tc_kernel<<<grid, q80::NTHREADS, q80::SMEM_BYTES, be->stream>>>(map_a, map_w, map_dw, (int)N, a.d, (int)M,
+                                                                            K, y, y_ld, be->err_word);
+    return oasr_internal_launch_check(be, "mmq_q80_tc");
+}
+
 int launch_mmq(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int64_t M, int K,
                float *y, int64_t y_ld) {
     const bool k_family = w->type == OASR_TYPE_Q4_K;
     if (k_family && a.qs16 && a.bs16h) return launch_q4k_tc(be, w, slice, a, M, K, y, y_ld);
+    if (w->dT && (y_ld & 3) == 0) return launch_q80_tc(be, w, slice, a, M, K, y, y_ld);
     const int family = k_family ? FAMILY_Q8_K : FAMILY_Q8_0;
     for (int64_t m0 = 0; m0 < M; m0 += 8) {
         const int mc = (int)std::min<int64_t>(8, M - m0);

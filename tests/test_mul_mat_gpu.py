@@ -249,3 +249,17 @@ def test_dp4a_decode_gemv_still_matches_oracle():
     assert r.returncode == 0, r.stderr[-2000:]
     worst = float(r.stdout.split("WORST")[1])
     assert worst <= TIGHT, worst
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K", [(9, 128, 128), (128, 256, 384), (300, 1280, 1280), (1500, 1152, 384),
+                                   (200, 200, 1536), (77, 4096, 1024)])
+def test_q8_0_tensor_core_gemm_is_bit_exact(gpu_backend, M, N, K):
+    """The tcgen05 kind::i8 Q8_0 GEMM forms each 32-block's integer dot exactly and adds
+    the blocks' float terms in order with ggml's roundings, so it equals the oracle bit
+    for bit (ragged M and N, K a multiple of 128)."""
+    wq = _weights(N, K, ob.Q8_0, 0x0A5A000C + M)
+    x = oo.synth_normal(0x0A5A000D + N, M * K).reshape(M, K)
+    got = _run(gpu_backend, wq, ob.Q8_0, N, K, x)
+    ref = oo.mul_mat(wq, ob.Q8_0, K, N, x)
+    np.testing.assert_array_equal(got, ref)
