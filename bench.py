@@ -661,6 +661,18 @@ def run_kernels(args) -> None:
             us = timed(lambda i: be.mul_mat_qact(w, qa, Menc, y), 10)
             add("mmq_q4k_tc_kernel", f"encoder {role} Q4_K N={N} K={K} M={Menc}", us, 2.0 * Menc * N * K, "TFLOP/s")
             del w, x, qa, y
+        # Q8_0 prefill GEMMs on tcgen05 kind::i8 (configs[1] shapes at M = 1500)
+        for N, K in [(4096, 1024), (6144, 1024), (1024, 3072)]:
+            Mp = 1500
+            w = be.upload_weight(ob.quantize(ob.Q8_0, ob.synth_normal(0xF8 + N + K, N * K, 0.0, 0.02).reshape(N, K)),
+                                 ob.Q8_0, [K, N])
+            x = torch.randn(Mp, K, device="cuda")
+            qa = torch.empty(be.act_bytes(ob.Q8_0, K, Mp), dtype=torch.uint8, device="cuda")
+            be.quantize_act(ob.Q8_0, x, qa)
+            y = torch.empty(Mp, N, device="cuda")
+            us = timed(lambda i: be.mul_mat_qact(w, qa, Mp, y), 10)
+            add("mmq_q80_tc_kernel", f"prefill Q8_0 N={N} K={K} M={Mp}", us, 2.0 * Mp * N * K, "TFLOP/s")
+            del w, x, qa, y
         # encoder self-attention: f16 pre-pass + tcgen05 flash attention
         qkv = torch.randn(B, T, 3 * d, device="cuda")
         qe = qkv[:, :, :d].reshape(B, T, H, 64).permute(0, 2, 1, 3)
