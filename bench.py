@@ -524,7 +524,7 @@ def run_b200(args) -> None:
                     "h2d_bytes_per_step": int(np.mean([p.nbytes for p in pcm_host[args.warmup:]])),
                     "d2h_bytes_per_step": B * N_NEW * 4},
             "gpu_launches": args.steps * launches_per_batch(32, 32, 4, N_NEW, B),
-            "roofline": {"bound": "hbm", "kernel": "fattn_split_kernel (cross-attention decode, 8 x 20 heads x 1500 "
+            "roofline": {"bound": "hbm", "kernel": "fattn_heads_kernel (cross-attention decode, 8 x 20 heads x 1500 "
                                                    "f16 K/V)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": ncu_traffic_fa(), "algorithmic_bytes": fa["bytes"],
@@ -542,7 +542,7 @@ def run_b200(args) -> None:
 
 def ncu_traffic_fa() -> float | None:
     """dram read + write bytes of one cross-attention launch, from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "fattn_split_cross_b8.md")
+    p = os.path.join(ROOT, "profiles", "fattn_heads_cross_b8.md")
     try:
         for line in open(p):
             if line.startswith("| dram_bytes_per_launch |"):
@@ -636,7 +636,7 @@ def run_kernels(args) -> None:
         del lm
         # cross-attention flash-decode (the dominant decode kernel)
         fa = _fa_roofline(be, torch, stream)
-        add("fattn_split_kernel", f"cross S={B} H={H} n_kv={T} D=64 f16 K/V", fa["us"], fa["bytes"], "GB/s")
+        add("fattn_heads_kernel", f"cross S={B} H={H} n_kv={T} D=64 f16 K/V", fa["us"], fa["bytes"], "GB/s")
         # self-attention flash-decode at position 128 of the 448-slot cache
         P, nkv = 448, 128
         kc = torch.randn(B, P, d, device="cuda").half()
@@ -646,7 +646,7 @@ def run_kernels(args) -> None:
         q = torch.randn(B, 1, H, 64, device="cuda").permute(0, 2, 1, 3)
         o = torch.empty(B, 1, H, 64, device="cuda")
         us = timed(lambda i: be.flash_attn_ext(q, kv, vv, None, 0.125, o), 50)
-        add("fattn_split_kernel", f"self S={B} H={H} n_kv={nkv} D=64 f16 K/V", us, 2 * B * nkv * d * 2 + 2 * B * d * 4,
+        add("fattn_heads_kernel", f"self S={B} H={H} n_kv={nkv} D=64 f16 K/V", us, 2 * B * nkv * d * 2 + 2 * B * d * 4,
             "GB/s")
         del kc, vc
         # encoder GEMMs: Q4_K weights x q8_K activations on the tensor cores, M = 8 x 1500
