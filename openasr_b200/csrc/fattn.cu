@@ -138,9 +138,11 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
         for (int e = 0; e < 8; ++e) acc[t][e] = 0.0f;
     }
 
+    // with a device-side KV length the splits share the live positions evenly
     const int nkv = a.nkv_dev ? min(*a.nkv_dev, a.NKV) : a.NKV;
-    const int kv0 = split * a.kv_per_split;
-    const int kv1 = min(nkv, kv0 + a.kv_per_split);
+    const int per = a.nkv_dev ? (nkv + a.n_splits - 1) / a.n_splits : a.kv_per_split;
+    const int kv0 = split * per;
+    const int kv1 = min(nkv, kv0 + per);
     const char *kbase = a.k + hk * a.k_nb2 + s * a.k_nb3 + sl * 8 * ES;
     const char *vbase = a.v + hk * a.v_nb2 + s * a.v_nb3 + sl * 8 * ES;
     // U warp-steps of K/V rows are loaded before any is consumed so that each
@@ -325,9 +327,11 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
 
+    // with a device-side KV length the splits share the live positions evenly
     const int nkv = a.nkv_dev ? min(*a.nkv_dev, a.NKV) : a.NKV;
-    const int kv0 = split * a.kv_per_split;
-    const int kv1 = min(nkv, kv0 + a.kv_per_split);
+    const int per = a.nkv_dev ? (nkv + a.n_splits - 1) / a.n_splits : a.kv_per_split;
+    const int kv0 = split * per;
+    const int kv1 = min(nkv, kv0 + per);
     // register double buffering: the loads of the next U positions are in flight while
     // the current U are consumed
     auto load = [&](int pb, int4 (&kr)[U], int4 (&vr)[U]) {
