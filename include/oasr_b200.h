@@ -280,6 +280,69 @@ int oasr_b200_whisper_transcribe(oasr_whisper *m, const float *pcm, const int64_
                                  const int32_t *prompt, int32_t n_prompt, int32_t n_new, int32_t eot,
                                  int32_t stop_at_eot, int32_t *tokens_out);
 
+/* ---- Qwen3-ASR LLM decoder -------------------------------------------------------
+ * The decoder-only LLM stack of models/qwen (Qwen3AsrLlmWholeDecoderGraphExecutor,
+ * llm_transformer.rs; layer graph nn/decoder.rs:1850-2140): per layer RMSNorm ->
+ * q|k|v -> per-head q_norm / k_norm RMSNorm -> RoPE NEOX -> set_rows f16 K/V ->
+ * GQA flash_attn_ext -> attn_output -> residual -> RMSNorm -> silu(gate) * up ->
+ * down -> residual; then RMSNorm -> lm_head -> first-max argmax
+ * (build_fused_logits_top1, llm_transformer.rs:2096-2115).  Tensor names are the
+ * GGUF names of the reference's qwen3 contract (decoder_contract.rs):
+ * token_embd.weight (Q8_0), output_norm.weight, output.weight (optional: absent =
+ * tied to token_embd), blk.N.{attn_norm, attn_q, attn_k, attn_v, attn_q_norm,
+ * attn_k_norm, attn_output, ffn_norm, ffn_gate, ffn_up, ffn_down}.weight; linear
+ * weights Q8_0, Q4_0 or Q4_K, norms F32. */
+typedef struct oasr_qwen_config {
+    int32_t d_model;      /* 1024 */
+    int32_t n_layers;     /* 28 */
+    int32_t n_heads;      /* 16 query heads */
+    int32_t n_kv_heads;   /* 8 (GQA) */
+    int32_t head_dim;     /* 128 */
+    int32_t ffn;          /* 3072 */
+    int32_t n_vocab;      /* 151936 */
+    int32_t max_pos;      /* KV positions per sequence (2048) */
+    int32_t max_prefill;  /* prompt positions one prefill call may carry per sequence */
+    int32_t max_batch;    /* sequences decoded in lockstep, <= 8 (batched_decode.rs:49) */
+    float rope_theta;     /* 1e6 (llm_transformer.rs:489) */
+    float rms_eps;        /* 1e-6 (logits_head.rs:23) */
+} oasr_qwen_config;
+
+typedef struct oasr_qwen oasr_qwen;
+
+/* Resident decoder (replaces the resident arena + executor construction of
+ * Qwen3AsrLlmWholeDecoderGraphExecutor and its KV arena,
+ * allocate_zeroed_llm_resident_kv_arena, nn/decoder.rs:2339). */
+int oasr_b200_qwen_load(oasr_backend *be, const oasr_qwen_config *cfg, const oasr_named_tensor *tensors,
+                        int32_t n_tensors, oasr_qwen **out);
+int oasr_b200_qwen_free(oasr_qwen *m);
+/* The whole prompt as one causal pass (run_prefill, llm_transformer.rs:3859-3895):
+ * emb [n_seq][n_tok][d_model] f32 prompt embeddings (host, or device when
+ * emb_on_device) fill positions 0..n_tok-1 of each sequence's KV cache; the last
+ * position's logits [n_seq][n_vocab] (host, optional) and first-max tokens
+ * [n_seq] (host, optional) come back, and the decode state moves to position
+ * n_tok with those tokens as the next inputs. */
+int oasr_b200_qwen_prefill(oasr_qwen *m, const float *emb, int32_t emb_on_device, int32_t n_seq, int32_t n_tok,
+                           float *logits, int32_t *next);
+/* One batched decode step at position pos (run_step_reused_batched_top1,
+ * llm_transformer.rs:4983): tokens [n_seq] (host; NULL = the tokens the previous
+ * prefill or step selected) -> logits [n_seq][n_vocab] (host, optional) and
+ * first-max tokens (host, optional). */
+int oasr_b200_qwen_decode_step(oasr_qwen *m, const int32_t *tokens, int32_t n_seq, int32_t pos, float *logits,
+                               int32_t *next);
+/* Prefill + greedy decode of n_new tokens per sequence (the first from the
+ * prompt's last logits), decode steps replayed from one CUDA graph
+ * (decode_continuous_batch, batched_decode.rs:643).  tokens_out [n_seq][n_new]
+ * is a device pointer when tokens_on_device != 0 (the call then returns without
+ * waiting), else host memory.  With stop_at_eos the loop ends once every
+ * sequence emitted `eos` (later entries are then undefined). */
+int oasr_b200_qwen_generate(oasr_qwen *m, const float *emb, int32_t emb_on_device, int32_t n_seq, int32_t n_tok,
+                            int32_t n_new, int32_t eos, int32_t stop_at_eos, int32_t *tokens_out,
+                            int32_t tokens_on_device);
+/* Copy positions [0, n_pos) of one layer's f16 K and V cache rows of sequence seq
+ * to host [n_kv_heads][n_pos][head_dim] (either output may be NULL). */
+int oasr_b200_qwen_read_kv(oasr_qwen *m, int32_t layer, int32_t seq, int32_t n_pos, uint16_t *k_out,
+                           uint16_t *v_out);
+
 /* ---- host-side helpers (no device work) --------------------------------------- */
 /* ggml_row_size (ffi.rs:619) */
 int64_t oasr_b200_row_size(int32_t type, int64_t ne0);

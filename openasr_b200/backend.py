@@ -123,6 +123,12 @@ class OasrWhisperConfig(ctypes.Structure):
                  "n_text_ctx", "max_batch")]
 
 
+class OasrQwenConfig(ctypes.Structure):
+    _fields_ = [(f, ctypes.c_int32) for f in
+                ("d_model", "n_layers", "n_heads", "n_kv_heads", "head_dim", "ffn", "n_vocab", "max_pos",
+                 "max_prefill", "max_batch")] + [("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float)]
+
+
 ABORT_CB = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p)
 
 # every symbol include/oasr_b200.h declares, with (argtypes, restype)
@@ -162,6 +168,13 @@ SIGNATURES = {
     "oasr_b200_whisper_transcribe": ([_P, _P, _P, _I32, _P, _I32, _I32, _I32, _I32, _P], ctypes.c_int),
     "oasr_b200_whisper_mel_device": ([_P, _P, _P, _I32], ctypes.c_int),
     "oasr_b200_whisper_generate": ([_P, _I32, _P, _I32, _I32, _I32, _I32, _P, _I32], ctypes.c_int),
+    "oasr_b200_qwen_load": ([_P, ctypes.POINTER(OasrQwenConfig), ctypes.POINTER(OasrNamedTensor), _I32,
+                             ctypes.POINTER(_P)], ctypes.c_int),
+    "oasr_b200_qwen_free": ([_P], ctypes.c_int),
+    "oasr_b200_qwen_prefill": ([_P, _P, _I32, _I32, _I32, _P, _P], ctypes.c_int),
+    "oasr_b200_qwen_decode_step": ([_P, _P, _I32, _I32, _P, _P], ctypes.c_int),
+    "oasr_b200_qwen_generate": ([_P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I32], ctypes.c_int),
+    "oasr_b200_qwen_read_kv": ([_P, _I32, _I32, _I32, _P, _P], ctypes.c_int),
     "oasr_b200_row_size": ([_I32, _I64], _I64),
     "oasr_b200_quantize_chunk": ([_I32, _P, _P, _I64, _I64, _I64], _I64),
     "oasr_b200_synth_normal": ([_U64, _U64, _P, _I64, _F, _F], ctypes.c_int),

@@ -3,7 +3,8 @@
 //   residual add + LayerNorm / RMSNorm (+gamma, beta) + activation quantization
 //   bias + GELU (+ quantization), fused QKV split + f16 KV-cache write,
 //   token embedding (Q8_0 get_rows) + positional add, im2col (f16), casts,
-//   the Whisper log-mel frontend and RoPE.
+//   SiLU * up (+ quantization), the decode-step advance and the Whisper log-mel
+//   frontend.
 // Rounding follows ggml's CPU ops (nn/decoder.rs, whisper/ggml_executor.rs call
 // ggml_norm, ggml_rms_norm, ggml_mul, ggml_add, ggml_gelu, ggml_silu): norms sum
 // in double, every add/mul rounds separately (no FMA contraction), GELU reads
@@ -344,20 +345,17 @@ __global__ void mel_norm_kernel(float *mel, int64_t per_utt, const int *max_key)
     }
 }
 
-// ---- RoPE, NEOX mode (ggml_rope_ext with freq_scale 1, ext_factor 0, attn_factor 1) ----------
-// x [rows = T*H][D]; theta_i = pos * base^(-2i/D) built by repeated multiplication as ggml does
-__global__ void rope_neox_kernel(float *x, int D, int H, const int *pos, int pos_offset_rows, float theta_scale) {
-    const int r = blockIdx.x;  // t*H + h
-    const int t = r / H;
-    const int p = pos[t];
-    for (int i = threadIdx.x; i < D / 2; i += blockDim.x) {
-        float theta = (float)p;
-        for (int j = 0; j < i; ++j) theta = __fmul_rn(theta, theta_scale);
-        const float c = cosf(theta), s = sinf(theta);
-        float *row = x + (int64_t)r * D;
-        const float x0 = row[i], x1 = row[i + D / 2];
-        row[i] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-        row[i + D / 2] = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+// After a decode step the selected tokens become the inputs of position pos + 1
+// (history[b][pos + 1]) and the device position and KV length advance by one.
+__global__ void decode_advance_kernel(const int *tokens, int *pos, int *nkv, int *history, int n, int P) {
+    griddep_wait();
+    const int b = threadIdx.x;
+    const int p = *pos;
+    if (b < n && p + 1 < P) history[b * P + p + 1] = tokens[b];
+    __syncthreads();
+    if (b == 0) {
+        *pos = p + 1;
+        *nkv = p + 2;
     }
 }
 
@@ -615,6 +613,12 @@ int launch_embed_q8_0(oasr_backend *be, const oasr_weight *emb, const int *token
     return oasr_internal_launch_check(be, "embed_q8_0");
 }
 
+int launch_decode_advance(oasr_backend *be, const int *tokens, int *pos, int *nkv, int *history, int n, int P) {
+    const cudaError_t e = launch_k(be, decode_advance_kernel, dim3(1), dim3(32), 0, tokens, pos, nkv, history, n, P);
+    if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "decode_advance launch", __LINE__);
+    return oasr_internal_launch_check(be, "decode_advance");
+}
+
 int launch_add_rows(oasr_backend *be, float *x, const float *bias, const float *add, int64_t rows, int n) {
     add_rows_kernel<<<blocks_for(rows * n, 256, be), 256, 0, be->stream>>>(x, bias, add, rows, n);
     return oasr_internal_launch_check(be, "add_rows");
@@ -644,12 +648,6 @@ int launch_mel(oasr_backend *be, const float *audio, int B, int n_samples, int n
     const int64_t per = (int64_t)n_mels * n_frames;
     mel_norm_kernel<<<dim3(blocks_for(per, 256, be), B), 256, 0, be->stream>>>(mel, per, max_key);
     return oasr_internal_launch_check(be, "mel");
-}
-
-int launch_rope_neox(oasr_backend *be, float *x, int T, int H, int D, const int *pos, float freq_base) {
-    const float theta_scale = powf(freq_base, -2.0f / (float)D);
-    rope_neox_kernel<<<T * H, 64, 0, be->stream>>>(x, D, H, pos, 0, theta_scale);
-    return oasr_internal_launch_check(be, "rope_neox");
 }
 
 }  // namespace oasr

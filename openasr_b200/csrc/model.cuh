@@ -17,6 +17,8 @@ int launch_qkv_split_kv_write(oasr_backend *be, const float *qkv, const float *b
 int launch_embed_q8_0(oasr_backend *be, const oasr_weight *emb, const int *tokens, int B, const float *pos_emb,
                       const int *pos_dev, int max_pos, float *x);
 int launch_add_rows(oasr_backend *be, float *x, const float *bias, const float *add, int64_t rows, int n);
+// decode-step epilogue: history[b][*pos + 1] = tokens[b] (b < n), *pos += 1, *nkv = *pos + 1
+int launch_decode_advance(oasr_backend *be, const int *tokens, int *pos, int *nkv, int *history, int n, int P);
 int launch_cast_f16(oasr_backend *be, const float *src, int64_t src_ld, const float *bias, int64_t rows, int cols,
                     __half *dst, int64_t dst_ld);
 int launch_im2col_f16(oasr_backend *be, const float *src, int64_t s_b, int64_t s_ic, int64_t s_t, int B, int IC,
@@ -24,7 +26,6 @@ int launch_im2col_f16(oasr_backend *be, const float *src, int64_t s_b, int64_t s
 int launch_mel(oasr_backend *be, const float *audio, int B, int n_samples, int n_frames, int n_mels,
                const float *window, const float2 *twiddle, const float *filters, float *power, float *mel,
                int *max_key);
-int launch_rope_neox(oasr_backend *be, float *x, int T, int H, int D, const int *pos, float freq_base);
 int launch_gemm_f16(oasr_backend *be, const __half *A, int64_t lda, const __half *B, int64_t ldb, int M, int N, int K,
                     float *y, int64_t y_ld, const float *bias, bool gelu);
 int launch_argmax_rows(oasr_backend *be, const float *x, int64_t ld, int64_t n, int rows, int32_t *out);

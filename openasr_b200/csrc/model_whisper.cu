@@ -351,18 +351,6 @@ __global__ void fill_tokens_kernel(int *tokens, int n, int value) {
     if (threadIdx.x < n) tokens[threadIdx.x] = value;
 }
 
-__global__ void advance_kernel(const int *tokens, int *pos, int *nkv, int *history, int n, int P) {
-    griddep_wait();
-    const int b = threadIdx.x;
-    const int p = *pos;
-    if (b < n && p + 1 < P) history[b * P + p + 1] = tokens[b];
-    __syncthreads();
-    if (b == 0) {
-        *pos = p + 1;
-        *nkv = p + 2;
-    }
-}
-
 int decode_step_graph(oasr_whisper *m, int n) {
     oasr_backend *be = m->be;
     if (m->graph && m->graph_batch != n) {
@@ -376,11 +364,8 @@ int decode_step_graph(oasr_whisper *m, int n) {
         // so successive launches overlap their prologues (programmatic dependent launch)
         be->pdl = m->pdl;
         int st = run_decode_step(m, n);
-        if (st == OASR_STATUS_SUCCESS) {
-            const cudaError_t le = launch_k(be, advance_kernel, dim3(1), dim3(32), 0, (const int *)m->tokens, m->pos,
-                                            m->nkv, m->history, n, (int)m->cfg.n_text_ctx);
-            if (le != cudaSuccess) st = oasr_internal_cuda_fail(be, le, "advance launch", __LINE__);
-        }
+        if (st == OASR_STATUS_SUCCESS)
+            st = launch_decode_advance(be, m->tokens, m->pos, m->nkv, m->history, n, (int)m->cfg.n_text_ctx);
         be->pdl = false;
         cudaError_t e = cudaStreamEndCapture(m->stream, &g);
         if (st) return st;

@@ -1,5 +1,6 @@
-"""Model-level host API: Whisper-shaped configs, seeded synthetic packs and the
-resident model handle over the C ABI (oasr_b200_whisper_*).
+"""Model-level host API: Whisper- and Qwen3-ASR-shaped configs, seeded synthetic
+packs and the resident model handles over the C ABI (oasr_b200_whisper_*,
+oasr_b200_qwen_*).
 
 Synthetic packs follow BASELINE.json: linear weights N(0, 0.02) quantized to
 the named ggml type (Q8_0 for whisper-tiny, Q4_K for whisper-large-v3), token
@@ -124,6 +125,22 @@ def whisper_synthetic_pack(cfg: WhisperConfig, seed: int = 0x0A5A0001, synth=Non
     return T
 
 
+def _named_tensors(pack: dict):
+    """oasr_named_tensor array over a pack's host arrays (+ the objects to keep alive)"""
+    arr = (bk.OasrNamedTensor * len(pack))()
+    keep = []
+    for i, (name, (t, ne, data)) in enumerate(pack.items()):
+        data = np.ascontiguousarray(data)
+        nm = name.encode()
+        keep += [nm, data]
+        arr[i].name = nm
+        arr[i].type = t
+        arr[i].ne[:] = list(ne) + [1] * (4 - len(ne))
+        arr[i].data = data.ctypes.data
+        arr[i].bytes = data.nbytes
+    return arr, keep
+
+
 def synthetic_audio(seed: int, n_samples: int, rms: float = 0.1) -> np.ndarray:
     """16 kHz Gaussian noise at -20 dBFS RMS (sigma 0.1)."""
     return bk.synth_normal(seed, n_samples, 0.0, rms)
@@ -137,21 +154,11 @@ class WhisperModel:
         self.cfg = cfg
         c = bk.OasrWhisperConfig(cfg.n_mels, cfg.d_model, cfg.n_heads, cfg.n_enc_layers, cfg.n_dec_layers,
                                  cfg.n_vocab, cfg.n_audio_ctx, cfg.n_text_ctx, cfg.max_batch)
-        arr = (bk.OasrNamedTensor * len(pack))()
-        self._keep = []
-        for i, (name, (t, ne, data)) in enumerate(pack.items()):
-            data = np.ascontiguousarray(data)
-            nm = name.encode()
-            self._keep += [nm, data]
-            arr[i].name = nm
-            arr[i].type = t
-            arr[i].ne[:] = list(ne) + [1] * (4 - len(ne))
-            arr[i].data = data.ctypes.data
-            arr[i].bytes = data.nbytes
+        arr, keep = _named_tensors(pack)
         h = ctypes.c_void_p()
         backend._check(bk.lib().oasr_b200_whisper_load(backend.handle, ctypes.byref(c), arr, len(pack), ctypes.byref(h)))
         self.handle = h
-        self._keep = None  # weights are resident now
+        del keep  # weights are resident now
 
     def close(self) -> None:
         if self.handle:
@@ -205,3 +212,135 @@ class WhisperModel:
             self.handle, pcm.ctypes.data, ns.ctypes.data, len(clips), prompt.ctypes.data, len(prompt), n_new, EOT,
             1 if stop_at_eot else 0, out.ctypes.data))
         return out
+
+
+# ---- Qwen3-ASR LLM decoder --------------------------------------------------------------
+@dataclasses.dataclass(frozen=True)
+class QwenConfig:
+    d_model: int = 1024
+    n_layers: int = 28
+    n_heads: int = 16
+    n_kv_heads: int = 8
+    head_dim: int = 128
+    ffn: int = 3072
+    n_vocab: int = 151936
+    max_pos: int = 2048
+    max_prefill: int = 512
+    max_batch: int = 8
+    rope_theta: float = 1e6
+    rms_eps: float = 1e-6
+    weight_type: int = bk.Q8_0
+
+    def replace(self, **kw) -> "QwenConfig":
+        return dataclasses.replace(self, **kw)
+
+
+# Qwen3-ASR-0.6B-shaped decoder, seeded random Q8_0
+QWEN3_ASR_0_6B = QwenConfig()
+# The 390-frame prompt stands for 30 s of audio (13 audio embeddings per second).
+QWEN_PREFIX_FRAMES = 390
+QWEN_PREFIX_SECONDS = 30.0
+QWEN_EOS = 151645  # <|im_end|>
+
+
+def qwen_synthetic_pack(cfg: QwenConfig, seed: int = 0x0A5A0003, tied: bool = True, synth=None, quantize=None) -> dict:
+    """{name: (ggml_type, ne[4], ndarray)} for a seeded random Qwen3-shaped decoder in the
+    GGUF names of the reference's qwen3 contract.  Linear weights N(0, 0.02) quantized to
+    cfg.weight_type, token embedding Q8_0 (also the logits head when `tied`, as in
+    Qwen3-0.6B), RMSNorm gains N(1, 0.1) so that a missing or misplaced gain shows."""
+    synth = synth or bk.synth_normal
+    quantize = quantize or bk.quantize
+    d, D, qt = cfg.d_model, cfg.head_dim, cfg.weight_type
+    T: dict = {}
+
+    def lin(name, K, N, t):
+        w = synth(_seed(seed, name), N * K, 0.0, 0.02).reshape(N, K)
+        T[name] = (t, [K, N, 1, 1], quantize(t, w))
+
+    def gain(name, n):
+        T[name] = (bk.F32, [n, 1, 1, 1], synth(_seed(seed, name), n, 1.0, 0.1))
+
+    lin("token_embd.weight", d, cfg.n_vocab, bk.Q8_0)
+    if not tied:
+        lin("output.weight", d, cfg.n_vocab, bk.Q8_0)
+    gain("output_norm.weight", d)
+    for i in range(cfg.n_layers):
+        p = f"blk.{i}."
+        gain(p + "attn_norm.weight", d)
+        lin(p + "attn_q.weight", d, cfg.n_heads * D, qt)
+        lin(p + "attn_k.weight", d, cfg.n_kv_heads * D, qt)
+        lin(p + "attn_v.weight", d, cfg.n_kv_heads * D, qt)
+        gain(p + "attn_q_norm.weight", D)
+        gain(p + "attn_k_norm.weight", D)
+        lin(p + "attn_output.weight", cfg.n_heads * D, d, qt)
+        gain(p + "ffn_norm.weight", d)
+        lin(p + "ffn_gate.weight", d, cfg.ffn, qt)
+        lin(p + "ffn_up.weight", d, cfg.ffn, qt)
+        lin(p + "ffn_down.weight", cfg.ffn, d, qt)
+    return T
+
+
+def qwen_synthetic_prefix(seed: int, n_seq: int, n_tok: int, d: int) -> np.ndarray:
+    """[n_seq][n_tok][d] audio-embedding frames drawn N(0, 1), one stream per sequence"""
+    return np.stack([bk.synth_normal(_seed(seed, f"prefix.{s}"), n_tok * d).reshape(n_tok, d) for s in range(n_seq)])
+
+
+class QwenModel:
+    """A resident Qwen3-ASR LLM decoder on one backend (oasr_b200_qwen_*)."""
+
+    def __init__(self, backend: bk.Backend, cfg: QwenConfig, pack: dict):
+        self.backend = backend
+        self.cfg = cfg
+        c = bk.OasrQwenConfig(cfg.d_model, cfg.n_layers, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn,
+                              cfg.n_vocab, cfg.max_pos, cfg.max_prefill, cfg.max_batch, cfg.rope_theta, cfg.rms_eps)
+        arr, keep = _named_tensors(pack)
+        h = ctypes.c_void_p()
+        backend._check(bk.lib().oasr_b200_qwen_load(backend.handle, ctypes.byref(c), arr, len(pack), ctypes.byref(h)))
+        self.handle = h
+        del keep
+
+    def close(self) -> None:
+        if self.handle:
+            bk.lib().oasr_b200_qwen_free(self.handle)
+            self.handle = ctypes.c_void_p(0)
+
+    def prefill(self, emb: np.ndarray):
+        """emb [n_seq][n_tok][d] -> (logits [n_seq][n_vocab], first tokens [n_seq])"""
+        e = np.ascontiguousarray(emb, np.float32)
+        n, T = e.shape[0], e.shape[1]
+        logits = np.empty((n, self.cfg.n_vocab), np.float32)
+        nxt = np.empty(n, np.int32)
+        self.backend._check(bk.lib().oasr_b200_qwen_prefill(self.handle, e.ctypes.data, 0, n, T, logits.ctypes.data,
+                                                            nxt.ctypes.data))
+        return logits, nxt
+
+    def decode_step(self, tokens, pos: int):
+        tk = np.ascontiguousarray(tokens, np.int32)
+        logits = np.empty((len(tk), self.cfg.n_vocab), np.float32)
+        nxt = np.empty(len(tk), np.int32)
+        self.backend._check(bk.lib().oasr_b200_qwen_decode_step(self.handle, tk.ctypes.data, len(tk), pos,
+                                                                logits.ctypes.data, nxt.ctypes.data))
+        return logits, nxt
+
+    def generate(self, emb: np.ndarray, n_new: int = 256, eos: int = QWEN_EOS, stop_at_eos: bool = False) -> np.ndarray:
+        """prefill + n_new greedy tokens per sequence -> [n_seq][n_new]"""
+        e = np.ascontiguousarray(emb, np.float32)
+        n, T = e.shape[0], e.shape[1]
+        out = np.empty((n, n_new), np.int32)
+        self.backend._check(bk.lib().oasr_b200_qwen_generate(self.handle, e.ctypes.data, 0, n, T, n_new, eos,
+                                                             1 if stop_at_eos else 0, out.ctypes.data, 0))
+        return out
+
+    def generate_device(self, emb_dev, n_seq: int, n_tok: int, tokens_dev, n_new: int = 256) -> None:
+        """device embeddings (torch f32 [n_seq][n_tok][d]) -> device tokens; returns without waiting"""
+        self.backend._check(bk.lib().oasr_b200_qwen_generate(self.handle, emb_dev.data_ptr(), 1, n_seq, n_tok, n_new,
+                                                             QWEN_EOS, 0, tokens_dev.data_ptr(), 1))
+
+    def read_kv(self, layer: int, seq: int, n_pos: int):
+        """(K, V) f16 [n_kv_heads][n_pos][head_dim] of one layer and sequence"""
+        c = self.cfg
+        k = np.empty((c.n_kv_heads, n_pos, c.head_dim), np.float16)
+        v = np.empty_like(k)
+        self.backend._check(bk.lib().oasr_b200_qwen_read_kv(self.handle, layer, seq, n_pos, k.ctypes.data,
+                                                            v.ctypes.data))
+        return k, v
