@@ -98,6 +98,14 @@ static __device__ __forceinline__ void griddep_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Hint: start streaming [p, p + bytes) from HBM into L2 (p 16-byte aligned, bytes a
+// multiple of 16).  Nothing waits on it; a kernel issues it for data that does not
+// depend on its predecessor (weights) before griddep_wait(), so under programmatic
+// dependent launch the stream overlaps the predecessor's tail.
+static __device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 template <typename... KArgs, typename... Args>
 static cudaError_t launch_k(oasr_backend *be, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                             Args &&...args) {

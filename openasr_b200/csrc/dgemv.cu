@@ -187,7 +187,9 @@ static __device__ void pro_quant(const DgemvArgs &a, const DgSmem &sm, int warp,
 }
 
 // ---- the kernel -------------------------------------------------------------------------------
-template <int FAM, int PRO, int EPI>
+// UPW > 0: warp w takes units w, w + 8, ... (UPW of them), all loaded before the wait;
+// UPW = 0: looping form with one unit in flight ahead of the one in use.
+template <int FAM, int PRO, int EPI, int UPW>
 __global__ void __launch_bounds__(DG_WARPS * 32, 2) dgemv_kernel(DgemvArgs a) {
     extern __shared__ __align__(16) char dg_smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -199,12 +201,26 @@ __global__ void __launch_bounds__(DG_WARPS * 32, 2) dgemv_kernel(DgemvArgs a) {
 
     // weights first (they do not depend on the previous kernel)
     griddep_launch_dependents();
-    Q4kUnit ck, nk;
-    Q80Unit c8, n8;
+    constexpr int NU = UPW > 0 ? UPW : 1;
+    Q4kUnit ck[FAM == FAMILY_Q8_K ? NU : 1], nk;
+    Q80Unit c8[FAM == FAMILY_Q8_K ? 1 : NU], n8;
     int u = warp;
-    if (u < a.units) {
-        if (FAM == FAMILY_Q8_K) load_q4k_unit(ck, tile + (int64_t)u * UNIT, lane, g);
-        else load_q80_unit(c8, tile + (int64_t)u * UNIT, lane, g);
+    if (UPW > 0) {
+#pragma unroll
+        for (int j = 0; j < NU; ++j) {
+            const int uj = warp + j * DG_WARPS;
+            if (uj < a.units) {
+                if (FAM == FAMILY_Q8_K) load_q4k_unit(ck[j], tile + (int64_t)uj * UNIT, lane, g);
+                else load_q80_unit(c8[j], tile + (int64_t)uj * UNIT, lane, g);
+            }
+        }
+    } else {
+        // the whole tile streams toward L2 while the first units load into registers
+        if (threadIdx.x == 0) prefetch_l2_bulk(tile, (uint32_t)a.units * UNIT);
+        if (u < a.units) {
+            if (FAM == FAMILY_Q8_K) load_q4k_unit(ck[0], tile + (int64_t)u * UNIT, lane, g);
+            else load_q80_unit(c8[0], tile + (int64_t)u * UNIT, lane, g);
+        }
     }
     griddep_wait();
 
@@ -228,18 +244,33 @@ __global__ void __launch_bounds__(DG_WARPS * 32, 2) dgemv_kernel(DgemvArgs a) {
         adrow0 = m0 < a.M ? a.in.d + (int64_t)m0 * nd : nullptr;
         adrow1 = m1 < a.M ? a.in.d + (int64_t)m1 * nd : nullptr;
     }
-    for (; u < a.units; u += DG_WARPS) {
-        const bool more = u + DG_WARPS < a.units;
-        if (FAM == FAMILY_Q8_K) {
-            if (more) load_q4k_unit(nk, tile + (int64_t)(u + DG_WARPS) * UNIT, lane, g);
-            const float da0 = adrow0 ? (SM ? adrow0[u] : __ldg(adrow0 + u)) : 0.0f;
-            const float da1 = adrow1 ? (SM ? adrow1[u] : __ldg(adrow1 + u)) : 0.0f;
-            q4k_unit_accumulate<SM>(acc, ck, u, arow, brow, da0, da1, t);
-            if (more) ck = nk;
-        } else {
-            if (more) load_q80_unit(n8, tile + (int64_t)(u + DG_WARPS) * UNIT, lane, g);
-            q80_unit_accumulate<SM>(acc, c8, u, arow, adrow0, adrow1, t);
-            if (more) c8 = n8;
+    if (UPW > 0) {
+#pragma unroll
+        for (int j = 0; j < NU; ++j) {
+            const int uj = warp + j * DG_WARPS;
+            if (uj >= a.units) break;
+            if (FAM == FAMILY_Q8_K) {
+                const float da0 = adrow0 ? (SM ? adrow0[uj] : __ldg(adrow0 + uj)) : 0.0f;
+                const float da1 = adrow1 ? (SM ? adrow1[uj] : __ldg(adrow1 + uj)) : 0.0f;
+                q4k_unit_accumulate<SM>(acc, ck[j], uj, arow, brow, da0, da1, t);
+            } else {
+                q80_unit_accumulate<SM>(acc, c8[j], uj, arow, adrow0, adrow1, t);
+            }
+        }
+    } else {
+        for (; u < a.units; u += DG_WARPS) {
+            const bool more = u + DG_WARPS < a.units;
+            if (FAM == FAMILY_Q8_K) {
+                if (more) load_q4k_unit(nk, tile + (int64_t)(u + DG_WARPS) * UNIT, lane, g);
+                const float da0 = adrow0 ? (SM ? adrow0[u] : __ldg(adrow0 + u)) : 0.0f;
+                const float da1 = adrow1 ? (SM ? adrow1[u] : __ldg(adrow1 + u)) : 0.0f;
+                q4k_unit_accumulate<SM>(acc, ck[0], u, arow, brow, da0, da1, t);
+                if (more) ck[0] = nk;
+            } else {
+                if (more) load_q80_unit(n8, tile + (int64_t)(u + DG_WARPS) * UNIT, lane, g);
+                q80_unit_accumulate<SM>(acc, c8[0], u, arow, adrow0, adrow1, t);
+                if (more) c8[0] = n8;
+            }
         }
     }
     if (!reduce_warps<DG_WARPS>(acc, sm.red, warp, lane)) return;
@@ -273,7 +304,17 @@ __global__ void __launch_bounds__(DG_WARPS * 32, 2) dgemv_kernel(DgemvArgs a) {
 // ---- host side ----------------------------------------------------------------------------------
 template <int FAM, int PRO, int EPI>
 static cudaError_t dg_set_attr() {
-    return cudaFuncSetAttribute(dgemv_kernel<FAM, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, DG_SMEM_MAX);
+    cudaError_t e = cudaSuccess;
+    // the instantiations dg_launch can pick (Q4_K units hold 26 registers: one per warp at most)
+    if constexpr (FAM == FAMILY_Q8_K) {
+        for (auto fn : {dgemv_kernel<FAM, PRO, EPI, 0>, dgemv_kernel<FAM, PRO, EPI, 1>})
+            if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, DG_SMEM_MAX);
+    } else {
+        for (auto fn : {dgemv_kernel<FAM, PRO, EPI, 0>, dgemv_kernel<FAM, PRO, EPI, 1>, dgemv_kernel<FAM, PRO, EPI, 2>,
+                        dgemv_kernel<FAM, PRO, EPI, 4>})
+            if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, DG_SMEM_MAX);
+    }
+    return e;
 }
 
 template <int FAM>
@@ -303,7 +344,18 @@ static int dg_launch(oasr_backend *be, const DgemvArgs &a) {
         return oasr_internal_fail(be, OASR_STATUS_FAILED, "dgemv: dgemv_configure was not called on this device");
     const size_t smem = dg_smem_bytes(FAM, PRO, a.K);
     const unsigned grid = (unsigned)((a.N + TILE_ROWS - 1) / TILE_ROWS);
-    const cudaError_t e = launch_k(be, dgemv_kernel<FAM, PRO, EPI>, dim3(grid), dim3(DG_WARPS * 32), smem, a);
+    // all of a warp's units in flight at once, up to 4 (Q8_0) or 1 (Q4_K) per warp, else looping
+    const int upw = (a.units + DG_WARPS - 1) / DG_WARPS;
+    cudaError_t e;
+    if (upw <= 1) {
+        e = launch_k(be, dgemv_kernel<FAM, PRO, EPI, 1>, dim3(grid), dim3(DG_WARPS * 32), smem, a);
+    } else if constexpr (FAM == FAMILY_Q8_K) {
+        e = launch_k(be, dgemv_kernel<FAM, PRO, EPI, 0>, dim3(grid), dim3(DG_WARPS * 32), smem, a);
+    } else {
+        if (upw <= 2) e = launch_k(be, dgemv_kernel<FAM, PRO, EPI, 2>, dim3(grid), dim3(DG_WARPS * 32), smem, a);
+        else if (upw <= 4) e = launch_k(be, dgemv_kernel<FAM, PRO, EPI, 4>, dim3(grid), dim3(DG_WARPS * 32), smem, a);
+        else e = launch_k(be, dgemv_kernel<FAM, PRO, EPI, 0>, dim3(grid), dim3(DG_WARPS * 32), smem, a);
+    }
     if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "dgemv launch", __LINE__);
     return oasr_internal_launch_check(be, "dgemv");
 }

@@ -539,6 +539,28 @@ __global__ void gelu_quant_chunks_kernel(const float *x, const float *bias, int 
     if (q.qs) quant_chunk<E>(v, r, n, k0, lane, q);
 }
 
+// warp = one (row, chunk): y = silu(gate) * up -> out_f32 / planes (gate|up -> down boundary);
+// arithmetic as swiglu_quant_kernel
+template <int E>
+__global__ void swiglu_quant_chunks_kernel(const float *gu, int n, int64_t gu_ld, int64_t n_chunks, float *out_f32,
+                                           ActPlanes q) {
+    griddep_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (w >= n_chunks) return;  // warp-uniform
+    const int per_row = n / (32 * E);
+    const int64_t r = w / per_row;
+    const int k0 = (int)(w - r * per_row) * 32 * E + E * lane;
+    griddep_wait();
+    float g[E], u[E], v[E];
+    ldE<E>(gu + r * gu_ld + k0, g);
+    ldE<E>(gu + r * gu_ld + n + k0, u);
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = __fmul_rn(__fdiv_rn(g[i], __fadd_rn(1.0f, expf(-g[i]))), u[i]);
+    if (out_f32) stE<E>(out_f32 + r * n + k0, v);
+    if (q.qs) quant_chunk<E>(v, r, n, k0, lane, q);
+}
+
 int launch_resid_norm_quant(oasr_backend *be, float *x, const float *add, const float *add_bias, int64_t rows, int n,
                             float eps, bool rms, const float *gamma, const float *beta, float *out_f32,
                             const ActPlanes *q, int family) {
@@ -590,8 +612,19 @@ int launch_swiglu_quant(oasr_backend *be, const float *gu, int64_t rows, int n, 
                         const ActPlanes *q, int family) {
     ActPlanes qq{};
     if (q) qq = *q;
-    const cudaError_t e = launch_k(be, swiglu_quant_kernel, dim3((unsigned)rows), dim3(256), n * sizeof(float), gu, n,
-                                   gu_ld, out_f32, qq, family);
+    cudaError_t e;
+    const int E = (!q || family == FAMILY_Q8_K) ? 8 : 4;
+    if (n % (32 * E) == 0 && gu_ld % 4 == 0) {
+        const int64_t chunks = rows * (n / (32 * E));
+        const unsigned grid = (unsigned)((chunks + 7) / 8);
+        if (E == 8)
+            e = launch_k(be, swiglu_quant_chunks_kernel<8>, dim3(grid), dim3(256), 0, gu, n, gu_ld, chunks, out_f32, qq);
+        else
+            e = launch_k(be, swiglu_quant_chunks_kernel<4>, dim3(grid), dim3(256), 0, gu, n, gu_ld, chunks, out_f32, qq);
+    } else {
+        e = launch_k(be, swiglu_quant_kernel, dim3((unsigned)rows), dim3(256), n * sizeof(float), gu, n, gu_ld, out_f32,
+                     qq, family);
+    }
     if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "swiglu_quant launch", __LINE__);
     return oasr_internal_launch_check(be, "swiglu_quant");
 }

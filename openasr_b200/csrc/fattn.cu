@@ -91,6 +91,18 @@ constexpr int FA_HEADS_MAX_SPLITS = 16;  // most KV splits of one query row (par
 template <int D, int QT, bool F16>
 __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
     griddep_launch_dependents();
+    if (threadIdx.x == 0 && a.nkv_dev && a.k_nb1 == D * (F16 ? 2 : 4) && a.v_nb1 == a.k_nb1) {
+        // decode over a cache whose rows of one head are contiguous: stream this CTA's K/V
+        // rows toward L2 before the wait.  Only a hint (the range is recomputed below); the
+        // KV length is set between steps, not by the predecessor kernel.
+        const int g = blockIdx.x / a.n_qtiles, hk0 = g % a.HKV, s0 = g / a.HKV;
+        const int nkv = min(*a.nkv_dev, a.NKV), per = (nkv + a.n_splits - 1) / a.n_splits;
+        const int p0 = blockIdx.y * per, p1 = min(nkv, p0 + per);
+        if (p1 > p0) {
+            prefetch_l2_bulk(a.k + hk0 * a.k_nb2 + s0 * a.k_nb3 + (int64_t)p0 * a.k_nb1, (uint32_t)((p1 - p0) * a.k_nb1));
+            prefetch_l2_bulk(a.v + hk0 * a.v_nb2 + s0 * a.v_nb3 + (int64_t)p0 * a.v_nb1, (uint32_t)((p1 - p0) * a.v_nb1));
+        }
+    }
     griddep_wait();
     constexpr int LPP = D / 8;        // lanes per KV position
     constexpr int PPW = 32 / LPP;     // positions per warp step
@@ -485,6 +497,25 @@ static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const
                                    const oasr_tensor *mask, float scale, oasr_tensor *dst, const float *q_bias,
                                    const int *nkv_dev, const FaScratch *fixed);
 
+// resident CTAs per SM of one fattn_split_kernel instantiation (same for every device of this build)
+static int split_kernel_occupancy(int D, int QT, bool f16) {
+    static int cache[2][4][2];
+    const int qi = QT == 1 ? 0 : QT == 2 ? 1 : QT == 4 ? 2 : 3;
+    int &occ = cache[D == 128][qi][f16];
+    if (occ) return occ;
+    const void *fn = nullptr;
+#define FA_OCC_FN(DD, F)                                                                         \
+    fn = qi == 0 ? (const void *)fattn_split_kernel<DD, 1, F> : qi == 1 ? (const void *)fattn_split_kernel<DD, 2, F> \
+       : qi == 2 ? (const void *)fattn_split_kernel<DD, 4, F> : (const void *)fattn_split_kernel<DD, 8, F>
+    if (D == 128) { if (f16) FA_OCC_FN(128, true); else FA_OCC_FN(128, false); }
+    else { if (f16) FA_OCC_FN(64, true); else FA_OCC_FN(64, false); }
+#undef FA_OCC_FN
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, 128, 0) != cudaSuccess || n < 1) n = 1;
+    occ = n;
+    return occ;
+}
+
 // q_bias: optional [H*D] f32 added to q; nkv_dev: optional device KV length (k->ne[1] is the maximum)
 int launch_flash_attn_ex(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
                          const oasr_tensor *mask, float scale, oasr_tensor *dst, const float *q_bias,
@@ -577,6 +608,14 @@ static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const
             occ = 1;
         n_splits = (int)(((int64_t)be->sm_count * std::max(occ, 1)) / groups);
         n_splits = std::max(1, std::min(std::min(n_splits, a.NKV / 32), FA_HEADS_MAX_SPLITS));
+    } else if (nkv_dev && groups <= (1 << 16)) {
+        // model decode steps (device KV length): as many splits as fit one wave of
+        // resident CTAs -- a partial second wave would double the latency
+        const int resident = be->sm_count * split_kernel_occupancy(D, QT, k->type == OASR_TYPE_F16);
+        if (groups < resident) {
+            n_splits = (int)(resident / groups);
+            n_splits = std::min(std::min(n_splits, std::max(1, a.NKV / 64)), FA_HEADS_MAX_SPLITS);
+        }
     } else if (groups < 4LL * be->sm_count && groups <= (1 << 16)) {
         n_splits = (int)((4LL * be->sm_count + groups - 1) / groups);
         n_splits = std::min(std::min(n_splits, std::max(1, a.NKV / 64)), FA_HEADS_MAX_SPLITS);

@@ -88,7 +88,11 @@ __global__ void __launch_bounds__(W * 32) mmv_q4k_tc_kernel(const uint8_t *__res
     }
 }
 
-template <int W>
+// Q8_0: warp w takes units w, w + W, ... (UPW of them) and issues every one of its loads
+// before the wait, so a tile's weights are one round trip in flight (they do not
+// depend on the predecessor).  UPW = 0 is the looping form for K past 8 units per warp:
+// one unit per warp in flight ahead of the one in use.
+template <int W, int UPW>
 __global__ void __launch_bounds__(W * 32) mmv_q80_tc_kernel(const uint8_t *__restrict__ tiles, int npairs, int64_t N,
                                                             int M, const int8_t *__restrict__ aqs,
                                                             const float *__restrict__ ad, int K,
@@ -101,20 +105,33 @@ __global__ void __launch_bounds__(W * 32) mmv_q80_tc_kernel(const uint8_t *__res
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 
     griddep_launch_dependents();
-    Q80Unit cur, nxt;
-    int p = warp;
-    if (p < npairs) load_q80_unit(cur, tile + (int64_t)p * Q80_UNIT, lane, g);
+    constexpr int NU = UPW > 0 ? UPW : 2;
+    Q80Unit u[NU];
+    if (UPW > 0) {
+#pragma unroll
+        for (int j = 0; j < NU; ++j)
+            if (warp + j * W < npairs) load_q80_unit(u[j], tile + (int64_t)(warp + j * W) * Q80_UNIT, lane, g);
+    } else {
+        if (threadIdx.x == 0) prefetch_l2_bulk(tile, (uint32_t)npairs * Q80_UNIT);
+        if (warp < npairs) load_q80_unit(u[0], tile + (int64_t)warp * Q80_UNIT, lane, g);
+    }
     griddep_wait();
 
     const int8_t *arow = aqs + (int64_t)(g < M ? g : 0) * K;
     const int m0 = 2 * t, m1 = 2 * t + 1;
     const float *ad0 = m0 < M ? ad + (int64_t)m0 * nb : nullptr;
     const float *ad1 = m1 < M ? ad + (int64_t)m1 * nb : nullptr;
-    for (; p < npairs; p += W) {
-        const bool more = p + W < npairs;
-        if (more) load_q80_unit(nxt, tile + (int64_t)(p + W) * Q80_UNIT, lane, g);
-        q80_unit_accumulate<false>(acc, cur, p, arow, ad0, ad1, t);
-        if (more) cur = nxt;
+    if (UPW > 0) {
+#pragma unroll
+        for (int j = 0; j < NU; ++j)
+            if (warp + j * W < npairs) q80_unit_accumulate<false>(acc, u[j], warp + j * W, arow, ad0, ad1, t);
+    } else {
+        for (int p = warp; p < npairs; p += W) {
+            const bool more = p + W < npairs;
+            if (more) load_q80_unit(u[1], tile + (int64_t)(p + W) * Q80_UNIT, lane, g);
+            q80_unit_accumulate<false>(acc, u[0], p, arow, ad0, ad1, t);
+            if (more) u[0] = u[1];
+        }
     }
     if (!reduce_warps<W>(acc, red, warp, lane)) return;
     const int64_t ra = (int64_t)blockIdx.x * TILE_ROWS + g, rb = ra + 8;
@@ -254,12 +271,12 @@ static cudaError_t launch_q4k_w(oasr_backend *be, const uint8_t *tiles, int nsb,
                     (const int8_t *)a.qs, (const float *)a.d, (const int16_t *)a.bs16, K, y, y_ld);
 }
 
-template <int W>
+template <int W, int UPW>
 static cudaError_t launch_q80_w(oasr_backend *be, const uint8_t *tiles, int npairs, int64_t N, int M,
                                 const ActPlanes &a, int K, float *y, int64_t y_ld) {
     const unsigned grid = (unsigned)((N + TILE_ROWS - 1) / TILE_ROWS);
-    return launch_k(be, mmv_q80_tc_kernel<W>, dim3(grid), dim3(W * 32), 0, tiles, npairs, N, M, (const int8_t *)a.qs,
-                    (const float *)a.d, K, y, y_ld);
+    return launch_k(be, mmv_q80_tc_kernel<W, UPW>, dim3(grid), dim3(W * 32), 0, tiles, npairs, N, M,
+                    (const int8_t *)a.qs, (const float *)a.d, K, y, y_ld);
 }
 
 int launch_mmv_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int M, int K, float *y,
@@ -282,9 +299,19 @@ int launch_mmv_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, const A
         else e = launch_q4k_w<8, true>(be, tiles, nsb, N, M, a, K, y, y_ld);
     } else {
         const int npairs = K / 64;
-        // long rows (e.g. the logits head) keep 4 warps per tile, each looping over ~5 units
-        if (npairs <= 4) e = launch_q80_w<2>(be, tiles, npairs, N, M, a, K, y, y_ld);
-        else e = launch_q80_w<4>(be, tiles, npairs, N, M, a, K, y, y_ld);
+        // Few tiles (N up to 4 x 16 rows per SM): every unit of a tile in flight at once --
+        // 8 warps up to 8 units, 16 warps with up to 8 units each up to K = 8192.  Many
+        // tiles (logits heads) or longer rows: 4 looping warps per tile behind a bulk L2
+        // prefetch of the tile, the CTA count supplying the parallelism.
+        const int64_t ntiles = (N + TILE_ROWS - 1) / TILE_ROWS;
+        if (ntiles > 4LL * be->sm_count) e = launch_q80_w<4, 0>(be, tiles, npairs, N, M, a, K, y, y_ld);
+        else if (npairs <= 8) e = launch_q80_w<8, 1>(be, tiles, npairs, N, M, a, K, y, y_ld);
+        else if (npairs <= 16) e = launch_q80_w<16, 1>(be, tiles, npairs, N, M, a, K, y, y_ld);
+        else if (npairs <= 32) e = launch_q80_w<16, 2>(be, tiles, npairs, N, M, a, K, y, y_ld);
+        else if (npairs <= 48) e = launch_q80_w<16, 3>(be, tiles, npairs, N, M, a, K, y, y_ld);
+        else if (npairs <= 64) e = launch_q80_w<16, 4>(be, tiles, npairs, N, M, a, K, y, y_ld);
+        else if (npairs <= 128) e = launch_q80_w<16, 8>(be, tiles, npairs, N, M, a, K, y, y_ld);
+        else e = launch_q80_w<4, 0>(be, tiles, npairs, N, M, a, K, y, y_ld);
     }
     if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "mmv_tc launch", __LINE__);
     return oasr_internal_launch_check(be, "mmv_tc");
