@@ -99,6 +99,7 @@ void *oasr_internal_scratch(oasr_backend *be, size_t bytes, int *status) {
         return nullptr;
     }
     be->scratch_bytes = nb;
+    ++be->scratch_epoch;
     return be->scratch;
 }
 

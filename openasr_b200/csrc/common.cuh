@@ -62,6 +62,7 @@ struct oasr_backend {
     // activation scratch: quantized activations, flash-decode partials, counters
     uint8_t *scratch;
     size_t scratch_bytes;
+    uint64_t scratch_epoch;   // bumped whenever the scratch is reallocated (captured graphs hold its address)
     unsigned int *counters;   // zero-initialised; kernels leave them at zero
     int *err_word;            // device error word (oasr::ERR_*)
     uint16_t *gelu_table;     // 65536-entry fp16 GELU table (ggml CPU semantics)

@@ -67,6 +67,7 @@ struct oasr_qwen {
     bool pdl;
     cudaGraphExec_t graph;
     int graph_batch;
+    uint64_t graph_epoch;  // backend scratch epoch at capture
     std::vector<void *> allocs;
     std::vector<oasr_weight *> weights;
 };
@@ -345,7 +346,9 @@ int run_decode_step(oasr_qwen *m, int n) {
 
 int decode_step_graph(oasr_qwen *m, int n) {
     oasr_backend *be = m->be;
-    if (m->graph && m->graph_batch != n) {
+    // re-capture when the batch changes or the backend's scratch (which the graph's
+    // attention partials and argmax records live in) was reallocated since the capture
+    if (m->graph && (m->graph_batch != n || m->graph_epoch != be->scratch_epoch)) {
         cudaGraphExecDestroy(m->graph);
         m->graph = nullptr;
     }
@@ -363,6 +366,7 @@ int decode_step_graph(oasr_qwen *m, int n) {
         cudaGraphDestroy(g);
         if (ie != cudaSuccess) return oasr_internal_cuda_fail(be, ie, "cudaGraphInstantiate", __LINE__);
         m->graph_batch = n;
+        m->graph_epoch = be->scratch_epoch;
     }
     OASR_CUDA_TRY(be, cudaGraphLaunch(m->graph, m->stream));
     return OASR_STATUS_SUCCESS;

@@ -79,6 +79,7 @@ struct oasr_whisper {
     int enc_family, dec_family;
     cudaGraphExec_t graph;
     int graph_batch;
+    uint64_t graph_epoch;  // backend scratch epoch at capture
     std::vector<void *> allocs;
     std::vector<oasr_weight *> weights;
 };
@@ -353,7 +354,9 @@ __global__ void fill_tokens_kernel(int *tokens, int n, int value) {
 
 int decode_step_graph(oasr_whisper *m, int n) {
     oasr_backend *be = m->be;
-    if (m->graph && m->graph_batch != n) {
+    // re-capture when the batch changes or the backend's scratch (which the graph's
+    // attention partials and argmax records live in) was reallocated since the capture
+    if (m->graph && (m->graph_batch != n || m->graph_epoch != be->scratch_epoch)) {
         cudaGraphExecDestroy(m->graph);
         m->graph = nullptr;
     }
@@ -374,6 +377,7 @@ int decode_step_graph(oasr_whisper *m, int n) {
         cudaGraphDestroy(g);
         if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "cudaGraphInstantiate", __LINE__);
         m->graph_batch = n;
+        m->graph_epoch = be->scratch_epoch;
     }
     OASR_CUDA_TRY(be, cudaGraphLaunch(m->graph, m->stream));
     return OASR_STATUS_SUCCESS;

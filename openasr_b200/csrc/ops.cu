@@ -79,11 +79,76 @@ __global__ void argmax_first_kernel(const char *x, int64_t nb1, int64_t n, int32
     }
 }
 
+// larger value wins; ties (and "no finite value", bi < 0) resolve to the lower index
+static __device__ __forceinline__ void argmax_merge(float &best, int64_t &bi, float ov, int64_t oi) {
+    if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi < bi))) { best = ov; bi = oi; }
+}
+
+static __device__ __forceinline__ void argmax_block(float &best, int64_t &bi) {
+    __shared__ float sv[32];
+    __shared__ int64_t si[32];
+    for (int o = 16; o > 0; o >>= 1)
+        argmax_merge(best, bi, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, bi, o));
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+    __syncthreads();
+    best = lane < nw ? sv[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : -1;
+    for (int o = 16; o > 0; o >>= 1)
+        argmax_merge(best, bi, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, bi, o));
+}
+
+// Long rows (logits heads): CTA (chunk c, row) takes ARGMAX_CHUNK consecutive entries and
+// records its first max; the last CTA of the row to finish merges the chunks' records.
+constexpr int ARGMAX_CHUNK = 4096;
+
+__global__ void __launch_bounds__(256) argmax_chunks_kernel(const float *x, int64_t ld, int64_t n, int nchunks,
+                                                            float *pv, long long *pi, unsigned int *tickets,
+                                                            int32_t *out) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const int row = blockIdx.y, c = blockIdx.x;
+    const float *xr = x + (int64_t)row * ld;
+    const int64_t lo = (int64_t)c * ARGMAX_CHUNK, hi = min(n, lo + ARGMAX_CHUNK);
+    float best = -INFINITY;
+    int64_t bi = -1;
+    for (int64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const float v = xr[i];
+        if (isfinite(v) && (bi < 0 || v > best)) { best = v; bi = i; }
+    }
+    argmax_block(best, bi);
+    if (threadIdx.x == 0) {
+        pv[(int64_t)row * nchunks + c] = best;
+        pi[(int64_t)row * nchunks + c] = bi;
+    }
+    if (!cta_last_arrival(tickets + row, (unsigned)nchunks)) return;
+    best = -INFINITY;
+    bi = -1;
+    for (int k = threadIdx.x; k < nchunks; k += blockDim.x)
+        argmax_merge(best, bi, __ldcg(pv + (int64_t)row * nchunks + k), __ldcg(pi + (int64_t)row * nchunks + k));
+    __syncthreads();  // argmax_block reuses its shared records
+    argmax_block(best, bi);
+    if (threadIdx.x == 0) out[row] = (int32_t)(bi < 0 ? 0 : bi);
+}
+
 }  // namespace
 
 namespace oasr {
 int launch_argmax_rows(oasr_backend *be, const float *x, int64_t ld, int64_t n, int rows, int32_t *out) {
-    const cudaError_t e = launch_k(be, argmax_first_kernel, dim3((unsigned)rows), dim3(1024), 0, (const char *)x, ld * 4, n, out);
+    cudaError_t e;
+    const int64_t nchunks = (n + ARGMAX_CHUNK - 1) / ARGMAX_CHUNK;
+    if (nchunks > 1 && nchunks <= 65535 && rows <= 65535) {
+        // chunk records from the scratch, one row ticket each (left at zero by the merging CTA)
+        int st = 0;
+        char *scr = (char *)oasr_internal_scratch(be, (size_t)rows * nchunks * (sizeof(float) + sizeof(long long)), &st);
+        if (st) return st;
+        long long *pi = reinterpret_cast<long long *>(scr);
+        float *pv = reinterpret_cast<float *>(scr + (size_t)rows * nchunks * sizeof(long long));
+        e = launch_k(be, argmax_chunks_kernel, dim3((unsigned)nchunks, (unsigned)rows), dim3(256), 0, x, ld, n,
+                     (int)nchunks, pv, pi, be->counters, out);
+    } else {
+        e = launch_k(be, argmax_first_kernel, dim3((unsigned)rows), dim3(1024), 0, (const char *)x, ld * 4, n, out);
+    }
     if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "argmax launch", __LINE__);
     return oasr_internal_launch_check(be, "argmax_first");
 }
@@ -338,6 +403,9 @@ int oasr_b200_argmax_first(oasr_backend *be, const oasr_tensor *logits, oasr_ten
     if (out->type != OASR_TYPE_I32 || out->ne[0] != logits->ne[1])
         return oasr_internal_fail(be, OASR_STATUS_FAILED, "argmax_first: out must be I32 [rows]");
     if (logits->ne[1] == 0) return OASR_STATUS_SUCCESS;
+    if (logits->nb[1] % 4 == 0 && logits->ne[1] <= INT32_MAX)
+        return launch_argmax_rows(be, (const float *)logits->data, logits->nb[1] / 4, logits->ne[0], (int)logits->ne[1],
+                                  (int32_t *)out->data);
     argmax_first_kernel<<<(unsigned)logits->ne[1], 1024, 0, be->stream>>>((const char *)logits->data, logits->nb[1],
                                                                           logits->ne[0], (int32_t *)out->data);
     return oasr_internal_launch_check(be, "argmax_first");

@@ -47,7 +47,26 @@ def test_argmax_first_matches_oracle(gpu_backend):
     x[1, [7, 9000, 151935]] = 50.0          # ties -> lowest index
     x[2, :] = -np.inf; x[2, 77] = np.nan    # no finite value -> 0
     x[3, 10] = np.inf; x[3, 11] = 40.0      # non-finite ignored
+    x[4, [4095, 4096]] = 60.0               # tie across a 4096-entry chunk edge
+    x[5, [300, 301, 4000]] = 61.0           # ties inside one chunk
+    x[6, 151935] = 62.0                     # max in the ragged last chunk
+    x[7, :] = 1.0                           # all equal -> 0
     out = torch.empty(8, dtype=torch.int32, device="cuda")
+    gpu_backend.argmax_first(torch.from_numpy(x).cuda(), out)
+    gpu_backend.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), oo.argmax_first(x))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape", [(3, 100), (2, 4096), (5, 4097), (1, 8191), (9, 51866), (2, 300000)])
+def test_argmax_first_row_lengths(gpu_backend, shape):
+    """Row lengths on both sides of the one-CTA / chunked boundary (4096 entries)."""
+    import torch
+
+    rng = np.random.default_rng(shape[1])
+    x = rng.normal(0, 1, shape).astype(np.float32)
+    x[:, rng.integers(0, shape[1], 4)] = 9.0  # shared ties in every row
+    out = torch.empty(shape[0], dtype=torch.int32, device="cuda")
     gpu_backend.argmax_first(torch.from_numpy(x).cuda(), out)
     gpu_backend.synchronize()
     np.testing.assert_array_equal(out.cpu().numpy(), oo.argmax_first(x))

@@ -30,6 +30,7 @@ What is exact and what is not follows from ggml's arithmetic:
 import numpy as np
 import pytest
 
+import openasr_b200 as ob
 from openasr_b200 import models as om
 from oracle import oracle as oo
 from oracle import qwen_ref as qr
@@ -175,13 +176,24 @@ def test_batched_generate_equals_serial(mid_model):
 
 
 @pytest.mark.gpu
+def test_generate_after_scratch_growth_recaptures(mid_model, gpu_backend):
+    """The step graph holds the backend scratch's address: growing the scratch after a
+    capture must lead to a fresh capture, with unchanged tokens."""
+    emb = prefix(2, 17, seed=0x0A5A3350)
+    before = mid_model.generate(emb, 6)
+    grown = gpu_backend.mem_stats()["scratch_bytes"] + (64 << 20)
+    gpu_backend.reserve_scratch(grown)
+    assert gpu_backend.mem_stats()["scratch_bytes"] >= grown
+    np.testing.assert_array_equal(mid_model.generate(emb, 6), before)
+
+
+@pytest.mark.gpu
 def test_single_position_prompt_and_bounds(mid_model, mid):
     cfg, pack = mid
     emb = prefix(1, 1, seed=0x0A5A3400)
     logits, nxt = mid_model.prefill(emb)
     lr = qr.QwenRef(cfg, pack).prefill(emb[0], qr.QwenRef(cfg, pack).new_cache(1))
     assert max_abs_rel(logits[0], lr) < FLIP
-    import openasr_b200 as ob
     with pytest.raises(ob.GgmlBackendError):
         mid_model.prefill(prefix(1, cfg.max_prefill + 1))
     with pytest.raises(ob.GgmlBackendError):
