@@ -5,6 +5,11 @@ configs[3]/[4] Whisper-large-v3-shaped Q4_K model, batch 8 per GPU: every
 rank runs mel + encoder + 224 greedy decoder steps on its own batch of 8
 utterances per step (independent replicas, weak scaling).
 
+Qwen workload (--workload qwen [--batch 1|4|8]): the
+Qwen3-ASR-0.6B-shaped Q8_0 decoder; one step = one oasr_b200_qwen_generate of
+`batch` sequences per GPU (390-frame prompt standing for 30 s of audio, causal
+prefill, 256 greedy tokens); metric RTFx = 30 s x sequences / device time.
+
 Secondary workload (--workload mulmat, BASELINE.json configs[1], decode part): the op-level quantized
 mul_mat sweep at batch-8 decode.  One step = one GGML_OP_MUL_MAT per weight of
 the Qwen3-0.6B-shaped set {4096x1024, 1024x2048, 6144x1024, 1024x3072,
@@ -686,6 +691,204 @@ def run_kernels(args) -> None:
     be.close()
 
 
+# ==================================================================================
+# Qwen workload (--workload qwen)
+# ==================================================================================
+QWEN_METRIC = "RTFx (audio-s/s), Qwen3-ASR-0.6B-shaped Q8_0 decoder, 390-frame prompt, greedy 256 tokens"
+QWEN_NEW = 256
+QWEN_SEED = 0x0A5A0003
+
+
+def qwen_launches_per_batch(n_layers: int, n_new: int) -> int:
+    """Kernel launches of one oasr_b200_qwen_generate (counted from model_qwen.cu):
+    prefill = first RMSNorm + 10 per layer (3 GEMMs + o GEMM, q/k-norm+RoPE+KV write,
+    attention, quantize, RMSNorm, SwiGLU) less the last layer's trailing RMSNorm + head
+    (RMSNorm, logits, argmax) + 1 advance; decode step = embed + RMSNorm + 9 per layer +
+    logits + argmax + advance; the causal mask is built once per prompt length."""
+    prefill = 1 + 10 * n_layers - 1 + 3 + 1
+    step = 2 + 9 * n_layers + 3
+    return prefill + (n_new - 1) * step
+
+
+def qwen_cpu_baseline() -> dict:
+    """The oracle (CPU restatement) on a bounded sample: the full-width decoder at 1 and
+    2 layers, the 390-frame prefill and 2 decode steps of one sequence, extrapolated
+    linearly in layers to 28 and in steps to 255."""
+    from oracle import oracle as oo
+    from oracle import qwen_ref as qr
+    from openasr_b200 import models as om
+
+    cores = os.cpu_count() or 1
+    emb = om.qwen_synthetic_prefix(0x0A5A3700, 1, om.QWEN_PREFIX_FRAMES, 1024)[0]
+    times = {}
+    for L in (1, 2):
+        cfg = om.QWEN3_ASR_0_6B.replace(n_layers=L, max_batch=1, max_prefill=om.QWEN_PREFIX_FRAMES)
+        ref = qr.QwenRef(cfg, om.qwen_synthetic_pack(cfg, seed=QWEN_SEED, synth=oo.synth_normal, quantize=oo.quantize))
+        cache = ref.new_cache(1)
+        t0 = time.perf_counter()
+        tok = int(oo.argmax_first(ref.prefill(emb, cache))[0])
+        t1 = time.perf_counter()
+        for i in range(2):
+            tok = int(oo.argmax_first(ref.step([tok], om.QWEN_PREFIX_FRAMES + i, cache)[0])[0])
+        t2 = time.perf_counter()
+        times[L] = (t1 - t0, (t2 - t1) / 2)
+    pre_layer = times[2][0] - times[1][0]
+    step_layer = times[2][1] - times[1][1]
+    pre = times[1][0] - pre_layer + 28 * pre_layer
+    step = times[1][1] - step_layer + 28 * step_layer
+    per_seq = pre + (QWEN_NEW - 1) * step
+    return {"value": om.QWEN_PREFIX_SECONDS / per_seq, "unit": "audio-s/s", "cores": cores, "kind": "port",
+            "sample": (f"oracle (CPU restatement of ggml semantics, OpenMP {cores} threads) on the full-width decoder "
+                       f"at 1 and 2 layers: 390-frame prefill {times[1][0]:.2f}/{times[2][0]:.2f} s, decode step "
+                       f"{times[1][1]:.3f}/{times[2][1]:.3f} s; extrapolated to 28 layers and 255 steps = "
+                       f"{per_seq:.1f} s per sequence (30 s of audio)")}
+
+
+def run_reference_qwen(args) -> None:
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    cb = qwen_cpu_baseline()
+    v = cb["value"]
+    print(json.dumps({
+        "impl": "reference", "metric": QWEN_METRIC, "value": v, "unit": "audio-s/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": args.batch * 30.0 / v * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "q8_0 x q8_0 int dot, f32 accumulate; f16 KV",
+        "data": "synthetic (seeded N(0,0.02) Q8_0 weights, N(0,1) 390-frame prompt embeddings)",
+        "config": {"workload": f"configs[2]: qwen3-asr-0.6b-shaped decoder, batch {args.batch}, 390-frame prompt, "
+                               f"greedy {QWEN_NEW} tokens", "l2": "inputs larger than L2"},
+        "cpu_baseline": cb,
+        "e2e": {"value": v, "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def _qwen_fa_roofline(be, torch, stream, S: int, n_kv: int, n_rot: int = 8, iters: int = 40) -> dict:
+    """The decode step's attention (fattn_split_kernel<128, 2, f16>: GQA 16 q / 8 kv heads,
+    D 128) over the mid-generation KV length, through the public flash_attn_ext entry point
+    on views of the model's cache layout [seq][kv head][max_pos][128], timed alone on the
+    bench stream and rotating over 8 layers' caches (> L2)."""
+    P, HKV, H, D = 2048, 8, 16, 128
+    caches = [(torch.randn(S, HKV, P, D, device="cuda").half(), torch.randn(S, HKV, P, D, device="cuda").half())
+              for _ in range(n_rot)]
+    q = torch.randn(S, H, 1, D, device="cuda")
+    out = torch.empty(S, 1, H, D, device="cuda")
+    scale = 1.0 / float(np.sqrt(np.float32(D)))
+
+    def launch(i):
+        k, v = caches[i % n_rot]
+        be.flash_attn_ext(q, k[:, :, :n_kv], v[:, :, :n_kv], None, scale, out)
+
+    for i in range(5):
+        launch(i)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream.synchronize()
+    e0.record(stream)
+    for i in range(iters):
+        launch(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / iters * 1e3
+    return {"us": us, "bytes": S * HKV * n_kv * D * 2 * 2 + 2 * S * H * D * 4, "n_kv": n_kv}
+
+
+def run_b200_qwen(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import openasr_b200 as ob
+    from openasr_b200 import models as om
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    B, T = args.batch, om.QWEN_PREFIX_FRAMES
+    cfg = om.QWEN3_ASR_0_6B.replace(max_batch=B, max_prefill=T)
+    t_setup = time.perf_counter()
+    stream = torch.cuda.Stream()
+    be = ob.Backend(local)
+    be.set_stream(stream)
+    model = om.QwenModel(be, cfg, om.qwen_synthetic_pack(cfg, seed=QWEN_SEED))
+    t_setup = time.perf_counter() - t_setup
+    n_steps = args.warmup + args.steps
+    emb_host = [om.qwen_synthetic_prefix(0x0A5A3700 + 1000 * rank + i, B, T, cfg.d_model) for i in range(n_steps)]
+    with torch.cuda.stream(stream):
+        emb_dev = [torch.from_numpy(e).cuda() for e in emb_host]
+        emb_pin = [torch.from_numpy(e).pin_memory() for e in emb_host]
+        toks_dev = torch.empty((B, QWEN_NEW), dtype=torch.int32, device="cuda")
+        for i in range(args.warmup):
+            model.generate_device(emb_dev[i], B, T, toks_dev, QWEN_NEW)
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        sampler = ClockSampler(local)
+        sampler.start()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(args.warmup, n_steps):
+            model.generate_device(emb_dev[i], B, T, toks_dev, QWEN_NEW)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        be.synchronize()
+        clocks = sampler.stop()
+        dev_s = e0.elapsed_time(e1) / 1e3
+        # e2e: the public generate call from pinned host embeddings to host tokens
+        if world > 1:
+            dist.barrier()
+        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        h0.record(stream)
+        for i in range(args.warmup, n_steps):
+            out = np.empty((B, QWEN_NEW), np.int32)
+            be._check(ob.lib().oasr_b200_qwen_generate(model.handle, emb_pin[i].data_ptr(), 0, B, T, QWEN_NEW,
+                                                       om.QWEN_EOS, 0, out.ctypes.data, 0))
+        h1.record(stream)
+        torch.cuda.synchronize()
+        e2e_s = h0.elapsed_time(h1) / 1e3
+        fa = _qwen_fa_roofline(be, torch, stream, B, T + QWEN_NEW // 2)
+    audio = om.QWEN_PREFIX_SECONDS * B * args.steps
+    dev_s, e2e_s, audio = reduce_over_ranks(dev_s, e2e_s, audio, "cuda")
+    if rank == 0:
+        peak, peak_kind = measured_peak_hbm()
+        achieved = fa["bytes"] / (fa["us"] * 1e-6) / 1e9
+        tokens = B * QWEN_NEW * args.steps * world
+        line = {
+            "metric": QWEN_METRIC, "value": audio / dev_s, "unit": "audio-s/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_s / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "q8_0 x q8_0 int dot (f32 accumulate), f16 KV",
+            "data": "synthetic (seeded N(0,0.02) Q8_0 weights, N(0,1) 390-frame prompt embeddings)",
+            "config": {"workload": f"configs[2]: qwen3-asr-0.6b-shaped decoder (28 layers, d 1024, 16/8 heads of 128, "
+                                   f"ffn 3072, vocab 151936), batch {B} per GPU, 390-frame prompt (30 s of audio), "
+                                   f"greedy {QWEN_NEW} tokens, prefill + decode on device",
+                       "batch_per_gpu": B, "sequences_per_step": B * world, "new_tokens": QWEN_NEW,
+                       "tokens_per_s": tokens / dev_s,
+                       "l2": "inputs larger than L2 (633 MB of Q8_0 weights per decode step)",
+                       "parallelism": f"independent replicas x{world} (sequences sharded per GPU)",
+                       "setup_s": round(t_setup, 1)},
+            "e2e": {"value": audio / e2e_s, "unit": "audio-s/s", "h2d_bytes_per_step": int(emb_host[0].nbytes),
+                    "d2h_bytes_per_step": B * QWEN_NEW * 4},
+            "gpu_launches": args.steps * qwen_launches_per_batch(cfg.n_layers, QWEN_NEW),
+            "roofline": {"bound": "hbm", "kernel": f"fattn_split_kernel<128,2,f16> (GQA decode attention, {B} x 8 kv "
+                                                   f"heads x {fa['n_kv']} f16 K/V positions)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes": fa["bytes"],
+                         "avg_launch_us": fa["us"], "how": "same kernel and shapes through flash_attn_ext, timed alone "
+                                                           "on the bench stream, caches rotated over 8 layers"},
+            "clocks": clocks,
+        }
+        line["cpu_baseline"] = qwen_cpu_baseline()
+        print(json.dumps(line), flush=True)
+    model.close()
+    be.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def measured_peak_tensor() -> tuple[float, str]:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -701,15 +904,18 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["rtfx", "mulmat", "kernels"], default="rtfx")
+    ap.add_argument("--workload", choices=["rtfx", "qwen", "mulmat", "kernels"], default="rtfx")
+    ap.add_argument("--batch", type=int, default=8, help="sequences per GPU (qwen workload: 1, 4 or 8)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.steps is None:
-        args.steps = 8 if args.workload == "rtfx" else 20
+        args.steps = 8 if args.workload in ("rtfx", "qwen") else 20
     if args.workload == "kernels":
         run_kernels(args)
     elif args.workload == "rtfx":
         (run_reference if args.impl == "reference" else run_b200)(args)
+    elif args.workload == "qwen":
+        (run_reference_qwen if args.impl == "reference" else run_b200_qwen)(args)
     elif args.impl == "reference":
         run_reference_mulmat(args)
     else:
