@@ -182,6 +182,19 @@ int oasr_b200_flash_attn_ext(oasr_backend *be, const oasr_tensor *q, const oasr_
                              const oasr_tensor *v, const oasr_tensor *mask, float scale, float max_bias,
                              float logit_softcap, int32_t prec, oasr_tensor *dst);
 
+/* GGML_OP_FLASH_ATTN_EXT under the causal mask, with no mask tensor read.  No
+ * reference counterpart: the reference passes the mask of
+ * build_causal_mask_f16_bits (nn/decoder.rs:766-790; the Qwen prompt pass,
+ * llm_transformer.rs:3859-3895), under which key j is visible to query i when
+ * j <= i + n_kv - n_q; a host that knows its mask is that one can call this
+ * instead and skip the n_q x n_kv mask.  Runs on the tcgen05 tensor cores with
+ * fp16 operands and fp16 probabilities (the arithmetic ggml's CUDA backend
+ * uses): head_dim 64 or 128, n_q >= 64, n_kv >= n_q; other shapes fail with
+ * OASR_STATUS_FAILED (use oasr_b200_flash_attn_ext with the mask).  Arguments
+ * otherwise as oasr_b200_flash_attn_ext (no mask argument). */
+int oasr_b200_flash_attn_causal(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
+                                float scale, int32_t prec, oasr_tensor *dst);
+
 /* Allocation-free GGML_OP_FLASH_ATTN_EXT.  No reference counterpart.
  * For callers that must not allocate device memory once they are running: a
  * host whose memory planner reserves the GPU's budget up front and treats any

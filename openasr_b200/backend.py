@@ -157,6 +157,7 @@ SIGNATURES = {
     "oasr_b200_mul_mat_qact": ([_P, _P, _P, _I64, _TP], ctypes.c_int),
     "oasr_b200_flash_attn_ext": ([_P, _TP, _TP, _TP, _TP, _F, _F, _F, _I32, _TP], ctypes.c_int),
     "oasr_b200_flash_attn_ext_static": ([_P, _TP, _TP, _TP, _TP, _F, _F, _F, _I32, _TP], ctypes.c_int),
+    "oasr_b200_flash_attn_causal": ([_P, _TP, _TP, _TP, _F, _I32, _TP], ctypes.c_int),
     "oasr_b200_set_rows": ([_P, _TP, _TP, _TP], ctypes.c_int),
     "oasr_b200_argmax_first": ([_P, _TP, _TP], ctypes.c_int),
     "oasr_b200_whisper_load": ([_P, ctypes.POINTER(OasrWhisperConfig), ctypes.POINTER(OasrNamedTensor), _I32,
@@ -406,6 +407,13 @@ class Backend:
         self._check(lib().oasr_b200_flash_attn_ext_static(
             self.handle, ctypes.byref(describe(q)), ctypes.byref(describe(k)), ctypes.byref(describe(v)),
             ctypes.byref(md) if md is not None else None, scale, max_bias, logit_softcap, prec, ctypes.byref(describe(out))))
+
+    def flash_attn_causal(self, q, k, v, scale: float, out, prec: int = PREC_DEFAULT) -> None:
+        """flash_attn_ext under the causal mask (key j visible to query i when
+        j <= i + n_kv - n_q) on the tensor cores; no mask tensor."""
+        self._check(lib().oasr_b200_flash_attn_causal(
+            self.handle, ctypes.byref(describe(q)), ctypes.byref(describe(k)), ctypes.byref(describe(v)), scale, prec,
+            ctypes.byref(describe(out))))
 
     def set_rows(self, dst, src, rows) -> None:
         self._check(lib().oasr_b200_set_rows(self.handle, ctypes.byref(describe(dst)), ctypes.byref(describe(src)),

@@ -1,24 +1,29 @@
-// fattn_tc.cu -- K4: tiled flash attention on the tcgen05 tensor cores for the
-// encoder's self-attention (n_q = n_kv = 1500, head_dim 64, no mask).
+// fattn_tc.cu -- K4: tiled flash attention on the tcgen05 tensor cores for long
+// query blocks: the Whisper encoder's self-attention (n_q = n_kv = 1500, head_dim
+// 64, no mask) and the Qwen decoder's causal prompt pass (head_dim 128, GQA).
 //
-// Semantics (cpu_graph.rs:4144-4220; encoder call site ggml_executor.rs:1650-1695):
-//   O[:, h, i, s] = softmax(scale * Q[:, i, h, s] . K[:, :, h/G, s]) V
+// Semantics (cpu_graph.rs:4144-4220; call sites ggml_executor.rs:1650-1695 and
+// nn/decoder.rs:2040-2064):
+//   O[:, h, i, s] = softmax(scale * Q[:, i, h, s] . K[:, :, h/G, s] + mask) V
+// where the only mask taken here is the causal one (key j visible to query i when
+// j <= i + n_kv - n_q, build_causal_mask_f16_bits, nn/decoder.rs:766-790).
 // Q, K and V are rounded to fp16 (the operand type of the tensor-core MMA;
 // ggml's CUDA backend makes the same conversion for f32 K/V), S = Q K^T and
 // O = P V accumulate in f32 in TMEM, P is rounded to fp16, and the softmax runs
 // in f32 with online rescaling.
 //
-// A pre-pass writes Q and K as fp16 [S*H][n][64] rows and V transposed as
-// fp16 [S*H_kv][64][n_pad] so that every MMA operand is a K-major tile in the
-// 128-byte swizzle layout fetched by TMA:
-//   MMA1  S(128 q x 128 keys)  = Q tile (128 x 64)      . K tile (128 keys x 64)^T
-//   MMA2  Ot(128 q x 64 dims)  = P tile (128 x 128 keys) . Vt tile (64 dims x 128 keys)^T
+// A pre-pass writes Q and K as fp16 [S*H][n][D] rows and V transposed as
+// fp16 [S*H_kv][D][n_pad] so that every MMA operand is a K-major tile of 64-element
+// (128-byte) rows in the 128-byte swizzle layout fetched by TMA:
+//   MMA1  S(128 q x 128 keys) = Q tile (128 x D) . K tile (128 keys x D)^T
+//   MMA2  Ot(128 q x D dims)  = P tile (128 x 128 keys) . Vt tile (D dims x 128 keys)^T
 // CTA = one 128-query tile of one head, 6 warps:
 //   warps 0-3  softmax (one query row per thread) + output accumulation in registers
 //   warp 4     TMA producer (Q once, then K / Vt tiles through a 2-slot ring)
 //   warp 5     TMEM allocator (256 columns) + single-thread MMA issuer
-// Two CTAs share an SM (112 KB shared memory, 256 TMEM columns each), so one
-// CTA's softmax overlaps the other's MMAs.  Every mbarrier wait is bounded.
+// D = 64: two CTAs share an SM (112 KB shared memory each), so one CTA's softmax
+// overlaps the other's MMAs; D = 128: one CTA per SM (192 KB).  Causal tiles wholly
+// above the diagonal are skipped.  Every mbarrier wait is bounded.
 #include <cudaTypedefs.h>
 
 #include "kernels.cuh"
@@ -26,38 +31,44 @@
 
 namespace oasr {
 
-namespace fa4 {
-constexpr int BQ = 128, BKV = 128, D = 64;
-constexpr int QTILE = BQ * 128;              // 16 KB
-constexpr int KTILE = BKV * 128;             // 16 KB
-constexpr int VTILE = 64 * 128;              // 8 KB: 64 dims x 64 keys
-constexpr int SLOT = KTILE + 2 * VTILE;      // K tile + two Vt half-tiles
-constexpr int PTILE = BQ * 128;              // 16 KB: 128 q x 64 keys
-constexpr int OFF_Q = 0;
-constexpr int OFF_KV = OFF_Q + QTILE;
-constexpr int OFF_P = OFF_KV + 2 * SLOT;
-constexpr int OFF_BAR = OFF_P + 2 * PTILE;
-constexpr int NBAR = 10;
-constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-constexpr int SMEM_BYTES = OFF_MISC + 16;  // two CTAs per SM: <= (228 KB - 2 x 1 KB reserved) / 2
-static_assert(SMEM_BYTES <= 115712, "two CTAs per SM");
-constexpr int NTHREADS = 192;
-}  // namespace fa4
+template <int D_>
+struct FaTc {
+    static constexpr int D = D_;
+    static constexpr int BQ = 128, BKV = 128;
+    static constexpr int SUB = 128 * 128;                // one 64-element-wide swizzled sub-tile of 128 rows
+    static constexpr int QTILE = (D / 64) * SUB;        // 128 q x D
+    static constexpr int KTILE = (D / 64) * SUB;        // 128 keys x D
+    static constexpr int VTILE = D * 128;               // D dims x 64 keys
+    static constexpr int SLOT = KTILE + 2 * VTILE;      // K tile + two Vt half-tiles
+    static constexpr int PTILE = BQ * 128;              // 128 q x 64 keys
+    static constexpr int OFF_Q = 0;
+    static constexpr int OFF_KV = OFF_Q + QTILE;
+    static constexpr int OFF_P = OFF_KV + 2 * SLOT;
+    static constexpr int OFF_BAR = OFF_P + 2 * PTILE;
+    static constexpr int NBAR = 10;
+    static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+    static constexpr int SMEM_BYTES = OFF_MISC + 16;
+    static constexpr int CTAS_PER_SM = D == 64 ? 2 : 1;
+    static constexpr int NTHREADS = 192;
+    // D = 64: two CTAs per SM, <= (228 KB - 2 x 1 KB reserved) / 2; D = 128: one CTA, <= 227 KB
+    static_assert(SMEM_BYTES <= (D == 64 ? 115712 : 232448), "shared memory per CTA");
+    static_assert(D == 64 || D == 128, "head_dim 64 or 128");
+};
 
 // ---- pre-pass: q,k -> fp16 rows [S*H][n][64]; v -> fp16 [S*Hkv][64][n_pad] -------------
 template <bool F16IN>
-__global__ void fa_prep_kernel(const char *src, int64_t nb1, int64_t nb2, int64_t nb3, int n, int H, int S,
+__global__ void fa_prep_kernel(const char *src, int64_t nb1, int64_t nb2, int64_t nb3, int n, int H, int S, int D,
                                __half *dst, bool transpose, int n_pad) {
-    const int64_t total = (int64_t)S * H * n * 64;
+    const int64_t total = (int64_t)S * H * n * D;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int d = (int)(i & 63);
-        const int64_t r = i >> 6;
+        const int d = (int)(i % D);
+        const int64_t r = i / D;
         const int p = (int)(r % n);
         const int64_t hs = r / n;
         const int h = (int)(hs % H), s = (int)(hs / H);
         const char *e = src + p * nb1 + h * nb2 + s * nb3;
         const float v = F16IN ? __half2float(reinterpret_cast<const __half *>(e)[d]) : reinterpret_cast<const float *>(e)[d];
-        if (transpose) dst[(hs * 64 + d) * n_pad + p] = __float2half_rn(v);
+        if (transpose) dst[(hs * D + d) * n_pad + p] = __float2half_rn(v);
         else dst[i] = __float2half_rn(v);
     }
 }
@@ -68,11 +79,13 @@ __global__ void fa_zero_pad_kernel(__half *vt, int64_t rows, int n, int n_pad) {
         vt[(i / w) * n_pad + n + (i % w)] = __float2half_rn(0.0f);
 }
 
-__global__ void __launch_bounds__(192, 2)
+template <int D, bool CAUSAL>
+__global__ void __launch_bounds__(192, FaTc<D>::CTAS_PER_SM)
     fattn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_vt, int NQ, int NKV, int H, int HKV, float scale_log2,
                     char *dst, int64_t d_nb1, int64_t d_nb2, int64_t d_nb3, int *err) {
-    using namespace fa4;
+    using C = FaTc<D>;
+    constexpr int BQ = C::BQ, BKV = C::BKV, NSUB = D / 64;
     extern __shared__ __align__(1024) uint8_t smem_fa[];
     uint8_t *smem = smem_fa;
     // the 128-byte swizzle tiles need a 1024-byte aligned base; refuse (no waits, no TMEM) otherwise
@@ -80,7 +93,7 @@ __global__ void __launch_bounds__(192, 2)
         if (threadIdx.x == 0) atomicOr(err, ERR_BAD_SHAPE);
         return;
     }
-    uint64_t *bars = (uint64_t *)(smem + OFF_BAR);
+    uint64_t *bars = (uint64_t *)(smem + C::OFF_BAR);
     uint64_t *q_full = bars + 0;
     uint64_t *kv_full = bars + 1;   // [2]
     uint64_t *kv_empty = bars + 3;  // [2]
@@ -88,8 +101,8 @@ __global__ void __launch_bounds__(192, 2)
     uint64_t *p_full = bars + 6;
     uint64_t *o_full = bars + 7;
     uint64_t *done = bars + 8;
-    uint32_t *tmem_slot = (uint32_t *)(smem + OFF_MISC);
-    volatile int *abort_flag = (volatile int *)(smem + OFF_MISC + 4);
+    uint32_t *tmem_slot = (uint32_t *)(smem + C::OFF_MISC);
+    volatile int *abort_flag = (volatile int *)(smem + C::OFF_MISC + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int qt = blockIdx.x;       // query tile
@@ -98,7 +111,9 @@ __global__ void __launch_bounds__(192, 2)
     const int G = H / HKV;
     const int hks = s * HKV + h / G;  // kv row block
     const int q0 = qt * BQ;
-    const int ntiles = (NKV + BKV - 1) / BKV;
+    const int qoff = NKV - NQ;        // causal: query i sits at key position i + qoff
+    int ntiles = (NKV + BKV - 1) / BKV;
+    if (CAUSAL) ntiles = min(ntiles, (q0 + BQ - 1 + qoff) / BKV + 1);  // later tiles are wholly masked
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
@@ -117,21 +132,24 @@ __global__ void __launch_bounds__(192, 2)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_slot;  // S: cols [0,128), Ot: cols [128,192)
+    const uint32_t tmem = *tmem_slot;  // S: cols [0,128), Ot: cols [128,128+D)
 
     if (warp == 4) {
         if (lane == 0) {
-            mbar_arrive_expect_tx(q_full, QTILE);
-            tma_load_2d(smem + OFF_Q, &tm_q, q_full, 0, hs * NQ + q0);
+            mbar_arrive_expect_tx(q_full, C::QTILE);
+#pragma unroll
+            for (int u = 0; u < NSUB; ++u) tma_load_2d(smem + C::OFF_Q + u * C::SUB, &tm_q, q_full, 64 * u, hs * NQ + q0);
             int issued = 0;
             for (int j = 0; j < ntiles; ++j) {
                 const int b = j & 1;
                 if (!mbar_wait(&kv_empty[b], ((j >> 1) & 1) ^ 1, abort_flag, err)) break;
-                uint8_t *slot = smem + OFF_KV + b * SLOT;
-                mbar_arrive_expect_tx(&kv_full[b], SLOT);
-                tma_load_2d(slot, &tm_k, &kv_full[b], 0, hks * NKV + j * BKV);
-                tma_load_2d(slot + KTILE, &tm_vt, &kv_full[b], j * BKV, hks * 64);
-                tma_load_2d(slot + KTILE + VTILE, &tm_vt, &kv_full[b], j * BKV + 64, hks * 64);
+                uint8_t *slot = smem + C::OFF_KV + b * C::SLOT;
+                mbar_arrive_expect_tx(&kv_full[b], C::SLOT);
+#pragma unroll
+                for (int u = 0; u < NSUB; ++u)
+                    tma_load_2d(slot + u * C::SUB, &tm_k, &kv_full[b], 64 * u, hks * NKV + j * BKV);
+                tma_load_2d(slot + C::KTILE, &tm_vt, &kv_full[b], j * BKV, hks * D);
+                tma_load_2d(slot + C::KTILE + C::VTILE, &tm_vt, &kv_full[b], j * BKV + 64, hks * D);
                 issued = j + 1;
             }
             for (int j = max(0, issued - 2); j < issued; ++j) {
@@ -149,25 +167,28 @@ __global__ void __launch_bounds__(192, 2)
             constexpr uint32_t id2 = idesc_f16_f32(BQ, D);
             const uint32_t t_s = tmem, t_o = tmem + 128;
             bool ok = mbar_wait(q_full, 0, abort_flag, err);
-            const uint64_t dq = sw128_desc(smem_u32(smem + OFF_Q));
             for (int j = 0; j < ntiles && ok; ++j) {
                 const int b = j & 1;
-                uint8_t *slot = smem + OFF_KV + b * SLOT;
+                uint8_t *slot = smem + C::OFF_KV + b * C::SLOT;
                 if (!mbar_wait(&kv_full[b], (j >> 1) & 1, abort_flag, err)) break;
                 // S may be overwritten once the softmax of tile j-1 has read it (p_full of j-1)
                 if (j > 0 && !mbar_wait(p_full, (j - 1) & 1, abort_flag, err)) break;
                 tc_fence_after();
-                const uint64_t dk = sw128_desc(smem_u32(slot));
+                // 16 dims per MMA: 4 steps inside each 64-dim swizzled sub-tile
 #pragma unroll
-                for (int k = 0; k < 4; ++k) umma_f16(t_s, dq + 2 * k, dk + 2 * k, id1, k != 0);
+                for (int k = 0; k < D / 16; ++k) {
+                    const uint64_t dq = sw128_desc(smem_u32(smem + C::OFF_Q + (k >> 2) * C::SUB)) + 2 * (k & 3);
+                    const uint64_t dk = sw128_desc(smem_u32(slot + (k >> 2) * C::SUB)) + 2 * (k & 3);
+                    umma_f16(t_s, dq, dk, id1, k != 0);
+                }
                 umma_commit(s_full);
                 // O_tile = P . Vt^T once the softmax has written P for this tile
                 if (!mbar_wait(p_full, j & 1, abort_flag, err)) break;
                 tc_fence_after();
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
-                    const uint64_t dp = sw128_desc(smem_u32(smem + OFF_P + (k >> 2) * PTILE)) + 2 * (k & 3);
-                    const uint64_t dv = sw128_desc(smem_u32(slot + KTILE + (k >> 2) * VTILE)) + 2 * (k & 3);
+                    const uint64_t dp = sw128_desc(smem_u32(smem + C::OFF_P + (k >> 2) * C::PTILE)) + 2 * (k & 3);
+                    const uint64_t dv = sw128_desc(smem_u32(slot + C::KTILE + (k >> 2) * C::VTILE)) + 2 * (k & 3);
                     umma_f16(t_o, dp, dv, id2, k != 0);
                 }
                 umma_commit(&kv_empty[b]);
@@ -181,15 +202,18 @@ __global__ void __launch_bounds__(192, 2)
     } else {
         // ---- softmax warpgroup: thread = query row q0 + 32*warp + lane ----
         const int r = 32 * warp + lane;
+        const int qpos = q0 + r + qoff;  // last key position this row may see (causal)
         const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
         float m = -INFINITY, l = 0.0f;
-        float o[64];
+        float o[D];
 #pragma unroll
-        for (int i = 0; i < 64; ++i) o[i] = 0.0f;
+        for (int i = 0; i < D; ++i) o[i] = 0.0f;
         for (int j = 0; j < ntiles; ++j) {
             if (!mbar_wait(s_full, j & 1, abort_flag, err)) break;
             tc_fence_after();
-            const int nvalid = min(BKV, NKV - j * BKV);
+            // keys j*BKV + c visible to this row: c < lim
+            int lim = min(BKV, NKV - j * BKV);
+            if (CAUSAL) lim = min(lim, qpos - j * BKV + 1);
             // pass 1: row max of this tile
             float tmax = -INFINITY;
 #pragma unroll
@@ -199,10 +223,11 @@ __global__ void __launch_bounds__(192, 2)
                 tmem_ld_wait();
 #pragma unroll
                 for (int i = 0; i < 16; ++i)
-                    if (16 * c + i < nvalid) tmax = fmaxf(tmax, __uint_as_float(v[i]) * scale_log2);
+                    if (16 * c + i < lim) tmax = fmaxf(tmax, __uint_as_float(v[i]) * scale_log2);
             }
             const float mnew = fmaxf(m, tmax);
-            const float alpha = exp2f(m - mnew);  // m = -inf on the first tile -> 0
+            // m = -inf on the first tile -> 0; a row with nothing visible yet keeps o = 0
+            const float alpha = mnew == -INFINITY ? 1.0f : exp2f(m - mnew);
             // pass 2: p = 2^(s*scale*log2e - mnew), row sum, P (fp16) into the swizzled A tiles
             float tsum = 0.0f;
 #pragma unroll
@@ -213,14 +238,14 @@ __global__ void __launch_bounds__(192, 2)
                 uint32_t pk[8];
 #pragma unroll
                 for (int i = 0; i < 16; i += 2) {
-                    const float p0 = 16 * c + i < nvalid ? exp2f(__uint_as_float(v[i]) * scale_log2 - mnew) : 0.0f;
-                    const float p1 = 16 * c + i + 1 < nvalid ? exp2f(__uint_as_float(v[i + 1]) * scale_log2 - mnew) : 0.0f;
+                    const float p0 = 16 * c + i < lim ? exp2f(__uint_as_float(v[i]) * scale_log2 - mnew) : 0.0f;
+                    const float p1 = 16 * c + i + 1 < lim ? exp2f(__uint_as_float(v[i + 1]) * scale_log2 - mnew) : 0.0f;
                     tsum += p0 + p1;
                     const __half2 hp = __floats2half2_rn(p0, p1);
                     pk[i / 2] = *reinterpret_cast<const uint32_t *>(&hp);
                 }
                 // keys 16c..16c+15 = two 16-byte chunks of the 64-key tile c/4
-                uint8_t *pt = smem + OFF_P + (c >> 2) * PTILE;
+                uint8_t *pt = smem + C::OFF_P + (c >> 2) * C::PTILE;
                 const int ch = (c & 3) * 2;
                 *reinterpret_cast<int4 *>(pt + sw128_off(r, ch)) = make_int4(pk[0], pk[1], pk[2], pk[3]);
                 *reinterpret_cast<int4 *>(pt + sw128_off(r, ch + 1)) = make_int4(pk[4], pk[5], pk[6], pk[7]);
@@ -234,7 +259,7 @@ __global__ void __launch_bounds__(192, 2)
             if (!mbar_wait(o_full, j & 1, abort_flag, err)) break;
             tc_fence_after();
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < D / 16; ++c) {
                 uint32_t v[16];
                 tmem_ld16(trow + 128 + 16 * c, v);
                 tmem_ld_wait();
@@ -248,7 +273,7 @@ __global__ void __launch_bounds__(192, 2)
             const float inv = l == 0.0f ? 0.0f : 1.0f / l;
             float *out = reinterpret_cast<float *>(dst + h * d_nb1 + qi * d_nb2 + s * d_nb3);
 #pragma unroll
-            for (int i = 0; i < 64; i += 4)
+            for (int i = 0; i < D; i += 4)
                 *reinterpret_cast<float4 *>(out + i) = make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
         }
     }
@@ -287,18 +312,40 @@ static bool encode_f16_2d(CUtensorMap *map, const void *base, uint64_t inner, ui
 
 bool flash_attn_tc_eligible(const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *mask,
                             const oasr_tensor *dst) {
-    return q->ne[0] == 64 && q->ne[1] >= 64 && k->ne[1] >= 64 && mask == nullptr && dst->nb[1] % 16 == 0 &&
-           dst->nb[2] % 16 == 0 && dst->nb[3] % 16 == 0 && ((uintptr_t)dst->data & 15) == 0;
+    // the public entry point routes the encoder shape here (head_dim 64, no mask); the causal
+    // head_dim-128 form is taken by the Qwen prompt pass directly
+    return q->ne[0] == 64 && k->ne[0] == 64 && q->ne[1] >= 64 && k->ne[1] >= 64 && mask == nullptr &&
+           dst->nb[1] % 16 == 0 && dst->nb[2] % 16 == 0 && dst->nb[3] % 16 == 0 && ((uintptr_t)dst->data & 15) == 0;
+}
+
+template <int D, bool CAUSAL>
+static cudaError_t launch_fa_tc(oasr_backend *be, dim3 grid, const CUtensorMap &mq, const CUtensorMap &mk,
+                                const CUtensorMap &mv, int NQ, int NKV, int H, int HKV, float scale_log2,
+                                const oasr_tensor *dst) {
+    using C = FaTc<D>;
+    static bool attr_set = false;  // per instantiation, same for every device of this build
+    if (!attr_set) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(fattn_tc_kernel<D, CAUSAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    fattn_tc_kernel<D, CAUSAL><<<grid, C::NTHREADS, C::SMEM_BYTES, be->stream>>>(
+        mq, mk, mv, NQ, NKV, H, HKV, scale_log2, (char *)dst->data, dst->nb[1], dst->nb[2], dst->nb[3], be->err_word);
+    return cudaGetLastError();
 }
 
 int launch_flash_attn_tc(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
-                         float scale, oasr_tensor *dst) {
+                         float scale, oasr_tensor *dst, bool causal) {
+    const int D = (int)q->ne[0];
     const int NQ = (int)q->ne[1], H = (int)q->ne[2], S = (int)q->ne[3];
     const int NKV = (int)k->ne[1], HKV = (int)k->ne[2];
+    if ((D != 64 && D != 128) || (causal && NKV < NQ))
+        return oasr_internal_fail(be, OASR_STATUS_FAILED, "flash_attn_tc: head_dim 64 or 128; causal needs n_kv >= n_q");
     const int n_pad = (NKV + 7) & ~7;
-    const size_t q_bytes = align256((size_t)S * H * NQ * 64 * 2);
-    const size_t k_bytes = align256((size_t)S * HKV * NKV * 64 * 2);
-    const size_t v_bytes = align256((size_t)S * HKV * 64 * n_pad * 2);
+    const size_t q_bytes = align256((size_t)S * H * NQ * D * 2);
+    const size_t k_bytes = align256((size_t)S * HKV * NKV * D * 2);
+    const size_t v_bytes = align256((size_t)S * HKV * D * n_pad * 2);
     int st = 0;
     uint8_t *scr = (uint8_t *)oasr_internal_scratch(be, q_bytes + k_bytes + v_bytes, &st);
     if (st) return st;
@@ -306,36 +353,35 @@ int launch_flash_attn_tc(oasr_backend *be, const oasr_tensor *q, const oasr_tens
     const bool f16k = k->type == OASR_TYPE_F16;
     const int blocks = be->sm_count * 8;
     fa_prep_kernel<false><<<blocks, 256, 0, be->stream>>>((const char *)q->data, q->nb[1], q->nb[2], q->nb[3], NQ, H, S,
-                                                          q16, false, 0);
+                                                          D, q16, false, 0);
     if (f16k) {
         fa_prep_kernel<true><<<blocks, 256, 0, be->stream>>>((const char *)k->data, k->nb[1], k->nb[2], k->nb[3], NKV,
-                                                             HKV, S, k16, false, 0);
+                                                             HKV, S, D, k16, false, 0);
         fa_prep_kernel<true><<<blocks, 256, 0, be->stream>>>((const char *)v->data, v->nb[1], v->nb[2], v->nb[3], NKV,
-                                                             HKV, S, vt16, true, n_pad);
+                                                             HKV, S, D, vt16, true, n_pad);
     } else {
         fa_prep_kernel<false><<<blocks, 256, 0, be->stream>>>((const char *)k->data, k->nb[1], k->nb[2], k->nb[3], NKV,
-                                                              HKV, S, k16, false, 0);
+                                                              HKV, S, D, k16, false, 0);
         fa_prep_kernel<false><<<blocks, 256, 0, be->stream>>>((const char *)v->data, v->nb[1], v->nb[2], v->nb[3], NKV,
-                                                              HKV, S, vt16, true, n_pad);
+                                                              HKV, S, D, vt16, true, n_pad);
     }
-    if (n_pad > NKV) fa_zero_pad_kernel<<<64, 256, 0, be->stream>>>(vt16, (int64_t)S * HKV * 64, NKV, n_pad);
+    if (n_pad > NKV) fa_zero_pad_kernel<<<64, 256, 0, be->stream>>>(vt16, (int64_t)S * HKV * D, NKV, n_pad);
     st = oasr_internal_launch_check(be, "fa_prep");
     if (st) return st;
+    // 64-element (128-byte) boxes: Q / K tiles of 128 rows, Vt half-tiles of D rows x 64 keys
     CUtensorMap mq, mk, mv;
-    if (!encode_f16_2d(&mq, q16, 64, (uint64_t)S * H * NQ, 64, 128) ||
-        !encode_f16_2d(&mk, k16, 64, (uint64_t)S * HKV * NKV, 64, 128) ||
-        !encode_f16_2d(&mv, vt16, (uint64_t)n_pad, (uint64_t)S * HKV * 64, 64, 64))
+    if (!encode_f16_2d(&mq, q16, (uint64_t)D, (uint64_t)S * H * NQ, 64, 128) ||
+        !encode_f16_2d(&mk, k16, (uint64_t)D, (uint64_t)S * HKV * NKV, 64, 128) ||
+        !encode_f16_2d(&mv, vt16, (uint64_t)n_pad, (uint64_t)S * HKV * D, 64, (uint32_t)D))
         return oasr_internal_fail(be, OASR_STATUS_FAILED, "flash_attn_tc: tensor map encoding failed");
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(fattn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa4::SMEM_BYTES);
-        attr_set = true;
-    }
-    dim3 grid((unsigned)((NQ + fa4::BQ - 1) / fa4::BQ), (unsigned)(S * H));
+    dim3 grid((unsigned)((NQ + 127) / 128), (unsigned)(S * H));
     const float scale_log2 = scale * 1.4426950408889634f;
-    fattn_tc_kernel<<<grid, fa4::NTHREADS, fa4::SMEM_BYTES, be->stream>>>(mq, mk, mv, NQ, NKV, H, HKV, scale_log2,
-                                                                         (char *)dst->data, dst->nb[1], dst->nb[2],
-                                                                         dst->nb[3], be->err_word);
+    cudaError_t e;
+    if (D == 64) e = causal ? launch_fa_tc<64, true>(be, grid, mq, mk, mv, NQ, NKV, H, HKV, scale_log2, dst)
+                            : launch_fa_tc<64, false>(be, grid, mq, mk, mv, NQ, NKV, H, HKV, scale_log2, dst);
+    else e = causal ? launch_fa_tc<128, true>(be, grid, mq, mk, mv, NQ, NKV, H, HKV, scale_log2, dst)
+                    : launch_fa_tc<128, false>(be, grid, mq, mk, mv, NQ, NKV, H, HKV, scale_log2, dst);
+    if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "fattn_tc launch", __LINE__);
     return oasr_internal_launch_check(be, "fattn_tc");
 }
 

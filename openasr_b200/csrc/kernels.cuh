@@ -88,8 +88,10 @@ int launch_mmq(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActP
 // attention
 bool flash_attn_tc_eligible(const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *mask,
                             const oasr_tensor *dst);
+// tcgen05 flash attention for long query blocks (fattn_tc.cu): head_dim 64 or 128,
+// no mask or (causal) key j visible to query i when j <= i + n_kv - n_q
 int launch_flash_attn_tc(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
-                         float scale, oasr_tensor *dst);
+                         float scale, oasr_tensor *dst, bool causal);
 int launch_flash_attn(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
                       const oasr_tensor *mask, float scale, oasr_tensor *dst);
 int launch_flash_attn_ex(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,

@@ -35,6 +35,7 @@ using namespace oasr;
 namespace {
 
 constexpr int QWEN_HEAD_DIM = 128;  // head width the per-head kernels are written for
+constexpr int QWEN_TC_MIN_ROWS = 64;  // prompt length from which attention runs on the tensor cores
 
 struct QLayer {
     oasr_weight *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
@@ -253,6 +254,8 @@ int attend(oasr_qwen *m, const QLayer &L, const float *q, int nq, int n, int nkv
                          (int64_t)nkv_max * nq * 2);
     }
     const float scale = 1.0f / sqrtf((float)D);
+    // prompt passes of at least one 64-row tile: causal flash attention on the tcgen05 tensor cores
+    if (mask && nq >= QWEN_TC_MIN_ROWS && nq == nkv_max) return launch_flash_attn_tc(m->be, &tq, &tk, &tv, scale, &to, true);
     return launch_flash_attn_ex(m->be, &tq, &tk, &tv, mask ? &tm : nullptr, scale, &to, nullptr, nkv_dev);
 }
 

@@ -345,8 +345,24 @@ int oasr_b200_flash_attn_ext(oasr_backend *be, const oasr_tensor *q, const oasr_
     st = fa_validate(be, q, k, v, mask, max_bias, logit_softcap, prec, dst, &empty);
     if (st || empty) return st;
     if (k->ne[1] == 0) return fa_zero_fill(be, dst, q->ne[0]);
-    if (flash_attn_tc_eligible(q, k, mask, dst)) return launch_flash_attn_tc(be, q, k, v, scale, dst);
+    if (flash_attn_tc_eligible(q, k, mask, dst)) return launch_flash_attn_tc(be, q, k, v, scale, dst, false);
     return launch_flash_attn(be, q, k, v, mask, scale, dst);
+}
+
+int oasr_b200_flash_attn_causal(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
+                                float scale, int32_t prec, oasr_tensor *dst) {
+    int st = oasr_internal_precheck(be);
+    if (st) return st;
+    bool empty;
+    st = fa_validate(be, q, k, v, nullptr, 0.0f, 0.0f, prec, dst, &empty);
+    if (st || empty) return st;
+    const int64_t D = q->ne[0];
+    if ((D != 64 && D != 128) || q->ne[1] < 64 || k->ne[1] < q->ne[1] || dst->nb[1] % 16 || dst->nb[2] % 16 ||
+        dst->nb[3] % 16 || ((uintptr_t)dst->data & 15))
+        return oasr_internal_fail(be, OASR_STATUS_FAILED,
+                                  "flash_attn_causal: needs head_dim 64|128, n_q >= 64, n_kv >= n_q and 16-byte "
+                                  "aligned dst rows (use flash_attn_ext with the mask)");
+    return launch_flash_attn_tc(be, q, k, v, scale, dst, true);
 }
 
 int oasr_b200_flash_attn_ext_static(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k,

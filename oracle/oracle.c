@@ -527,8 +527,9 @@ static inline float load_elem(const char *p, int type) {
 
 static float r16(float x) { return oo_f16_to_f32(oo_f32_to_f16(x)); }
 
-/* tensor-core arithmetic (see oracle.h, OO_FA_TC128); no mask */
-static int fa_tc128(const oo_tensor *q, const oo_tensor *k, const oo_tensor *v, float scale, oo_tensor *dst) {
+/* tensor-core arithmetic (see oracle.h, OO_FA_TC128); mask entries 0 (visible) or -inf (hidden) */
+static int fa_tc128(const oo_tensor *q, const oo_tensor *k, const oo_tensor *v, const oo_tensor *mask, float scale,
+                    oo_tensor *dst) {
     const int64_t D = q->ne[0], NQ = q->ne[1], H = q->ne[2], S = q->ne[3];
     const int64_t NKV = k->ne[1], HKV = k->ne[2];
     const int64_t G = H / HKV;
@@ -542,11 +543,19 @@ static int fa_tc128(const oo_tensor *q, const oo_tensor *k, const oo_tensor *v, 
         float *o = qv + D, *ot = qv + 2 * D, *x = qv + 3 * D;
         const char *pq = (const char *)q->data + iq * q->nb[1] + h * q->nb[2] + s * q->nb[3];
         for (int64_t d = 0; d < D; ++d) { qv[d] = r16(*(const float *)(pq + d * q->nb[0])); o[d] = 0.0f; }
+        const char *mp = mask ? (const char *)mask->data + iq * mask->nb[1] + (h % mask->ne[2]) * mask->nb[2] +
+                                    (s % mask->ne[3]) * mask->nb[3]
+                              : NULL;
         float m = -INFINITY, l = 0.0f;
         for (int64_t j0 = 0; j0 < NKV; j0 += 128) {
             const int64_t nv = NKV - j0 < 128 ? NKV - j0 : 128;
             float tmax = -INFINITY;
             for (int64_t i = 0; i < nv; ++i) {
+                /* mask: 0 = visible, -inf = hidden (the kernel takes no other values) */
+                if (mp && oo_f16_to_f32(*(const uint16_t *)(mp + (j0 + i) * mask->nb[0])) == -INFINITY) {
+                    x[i] = -INFINITY;
+                    continue;
+                }
                 const char *kr = (const char *)k->data + (j0 + i) * k->nb[1] + hk * k->nb[2] + s * k->nb[3];
                 double acc = 0.0;
                 for (int64_t d = 0; d < D; ++d) acc += (double)(qv[d] * r16(load_elem(kr + d * k->nb[0], k->type)));
@@ -554,11 +563,11 @@ static int fa_tc128(const oo_tensor *q, const oo_tensor *k, const oo_tensor *v, 
                 tmax = tmax > x[i] ? tmax : x[i];
             }
             const float mnew = m > tmax ? m : tmax;
-            const float alpha = exp2f(m - mnew);
+            const float alpha = mnew == -INFINITY ? 1.0f : exp2f(m - mnew);
             float tsum = 0.0f;
             for (int64_t i = 0; i < 128; i += 2) {
-                const float p0 = i < nv ? exp2f(x[i] - mnew) : 0.0f;
-                const float p1 = i + 1 < nv ? exp2f(x[i + 1] - mnew) : 0.0f;
+                const float p0 = i < nv && x[i] != -INFINITY ? exp2f(x[i] - mnew) : 0.0f;
+                const float p1 = i + 1 < nv && x[i + 1] != -INFINITY ? exp2f(x[i + 1] - mnew) : 0.0f;
                 tsum += p0 + p1;
                 if (i < nv) x[i] = r16(p0);
                 if (i + 1 < nv) x[i + 1] = r16(p1);
@@ -598,8 +607,17 @@ int oo_flash_attn_ext(const oo_tensor *q, const oo_tensor *k, const oo_tensor *v
         return OO_STATUS_FAILED;
     const int64_t rk2 = H / HKV;
     if (mode == OO_FA_TC128) {
-        if (mask) return OO_STATUS_FAILED;
-        return fa_tc128(q, k, v, scale, dst);
+        if (mask) /* visible / hidden masks only */
+            for (int64_t i3 = 0; i3 < mask->ne[3]; ++i3)
+                for (int64_t i2 = 0; i2 < mask->ne[2]; ++i2)
+                    for (int64_t i1 = 0; i1 < NQ; ++i1)
+                        for (int64_t i0 = 0; i0 < NKV; ++i0) {
+                            const float mv = oo_f16_to_f32(*(const uint16_t *)((const char *)mask->data + i0 * mask->nb[0] +
+                                                                               i1 * mask->nb[1] + i2 * mask->nb[2] +
+                                                                               i3 * mask->nb[3]));
+                            if (mv != 0.0f && mv != -INFINITY) return OO_STATUS_FAILED;
+                        }
+        return fa_tc128(q, k, v, mask, scale, dst);
     }
     const int f16acc = (mode == OO_FA_GGML) && v->type == OO_TYPE_F16;
     int bad = 0;

@@ -96,9 +96,10 @@ int oo_mul_mat(const oo_tensor *w, const oo_tensor *x, oo_tensor *dst);
 enum { OO_FA_GGML = 0, OO_FA_F32 = 1, OO_FA_TC128 = 2 };
 /* OO_FA_TC128: the arithmetic of a tensor-core flash attention -- q, k, v rounded
  * to fp16, scores in 128-key blocks with a running max in the base-2 domain,
- * probabilities rounded to fp16 for the P.V product, f32 rescaling.  Used to
- * check the GPU encoder attention kernel (ggml's CUDA backend makes the same
- * fp16 conversion of f32 K/V); the ggml CPU semantics are modes 0 and 1. */
+ * probabilities rounded to fp16 for the P.V product, f32 rescaling; a mask may
+ * only hide keys (entries 0 or -inf).  Used to check the GPU tensor-core
+ * attention (encoder; the Qwen causal prompt pass) -- ggml's CUDA backend makes
+ * the same fp16 conversion of f32 K/V; the ggml CPU semantics are modes 0 and 1. */
 int oo_flash_attn_ext(const oo_tensor *q, const oo_tensor *k, const oo_tensor *v,
                       const oo_tensor *mask, float scale, int mode, oo_tensor *dst);
 

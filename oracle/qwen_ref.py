@@ -13,6 +13,11 @@ with eps 1e-6 (logits_head.rs:23) and theta 1e6 (llm_transformer.rs:489).
 The prompt runs as one causal pass (run_prefill, llm_transformer.rs:3859-3895,
 causal f16 mask as build_causal_mask_f16_bits, nn/decoder.rs:766-790); each
 decode step attends over the live prefix (run_step, llm_transformer.rs:3203).
+Prompt attention of `tc_min_rows` or more positions is evaluated in the
+oracle's tensor-core arithmetic mode (fp16 operands and probabilities, 128-key
+blocks), the arithmetic the device's prompt pass is specified to use (ggml's
+CUDA backend makes the same fp16 conversion); shorter prompts and decode steps
+use f32 accumulation.
 Every elementwise op rounds to float32 separately, as ggml's f32 ops do.
 """
 from __future__ import annotations
@@ -39,9 +44,10 @@ class QwenRef:
     rope_theta, rms_eps, max_pos; `pack` is {name: (type, ne, data)} in the GGUF
     tensor names of the reference's qwen3 contract (decoder_contract.rs)."""
 
-    def __init__(self, cfg, pack: dict):
+    def __init__(self, cfg, pack: dict, tc_min_rows: int = 64):
         self.cfg = cfg
         self.T = pack
+        self.tc_min_rows = tc_min_rows
         self.out_name = "output.weight" if "output.weight" in pack else "token_embd.weight"
 
     def vec(self, name):
@@ -83,9 +89,10 @@ class QwenRef:
         vc[s, :, pos0:pos0 + T] = _f16(v.transpose(1, 0, 2))
         n_kv = pos0 + T
         mask = causal_mask(T, n_kv, pos0) if T > 1 else None
+        mode = oo.FA_TC128 if T >= self.tc_min_rows and pos0 == 0 else oo.FA_F32
         a = oo.flash_attn_ext(np.ascontiguousarray(q.transpose(1, 0, 2))[None],
                               np.ascontiguousarray(kc[s:s + 1, :, :n_kv]), np.ascontiguousarray(vc[s:s + 1, :, :n_kv]),
-                              mask, float(np.float32(1.0) / np.sqrt(np.float32(D))), oo.FA_F32)  # (1, T, H, D)
+                              mask, float(np.float32(1.0) / np.sqrt(np.float32(D))), mode)  # (1, T, H, D)
         x = (x + self.lin(p + "attn_output.weight", a.reshape(T, H * D))).astype(np.float32)
         h = self.rms(x, self.vec(p + "ffn_norm.weight"))
         g = self.lin(p + "ffn_gate.weight", h)

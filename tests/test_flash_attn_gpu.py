@@ -187,3 +187,51 @@ def test_head_contiguous_kv_rows(gpu_backend, S, H, NKV):
                             oo.FA_F32)
     err = max_abs_rel(out.cpu().numpy(), ref)
     assert err <= TOL and err <= TIGHT, err
+
+
+def _causal_offset_mask(NQ, NKV):
+    """key j visible to query i when j <= i + NKV - NQ (build_causal_mask_f16_bits for
+    NQ = NKV, nn/decoder.rs:766-790)"""
+    m = np.zeros((NQ, NKV), np.float16)
+    for i in range(NQ):
+        m[i, i + NKV - NQ + 1:] = -np.inf
+    return m
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("S,H,HKV,NQ,NKV,D", [(1, 16, 8, 64, 64, 128), (2, 16, 8, 390, 390, 128),
+                                               (1, 16, 8, 200, 457, 128), (2, 4, 4, 130, 130, 64),
+                                               (1, 8, 2, 129, 300, 64)])
+def test_causal_tensor_core_attention(gpu_backend, S, H, HKV, NQ, NKV, D):
+    """oasr_b200_flash_attn_causal against the oracle's tensor-core arithmetic under the
+    causal mask: query tiles on the diagonal, key tiles past it skipped, an offset
+    between query and key positions (n_kv > n_q), GQA and both head widths."""
+    import torch
+
+    q, k, v = _case(900 + NQ + NKV + D, S, H, HKV, NQ, NKV, D)
+    out = torch.empty((S, NQ, H, D), dtype=torch.float32, device="cuda")
+    gpu_backend.flash_attn_causal(torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda(),
+                                  torch.from_numpy(v).cuda(), 1.0 / np.sqrt(D), out)
+    gpu_backend.synchronize()
+    got = out.cpu().numpy()
+    mask = _causal_offset_mask(NQ, NKV)
+    ref = oo.flash_attn_ext(q, k, v, mask, 1.0 / np.sqrt(D), oo.FA_TC128)
+    err = max_abs_rel(got, ref)
+    assert err <= TOL, err
+    # a causal boundary one key off (the classic mistake) is far outside that bound
+    off = oo.flash_attn_ext(q, k, v, _causal_offset_mask(NQ, NKV + 1)[:, :NKV], 1.0 / np.sqrt(D), oo.FA_TC128)
+    assert max_abs_rel(got, off) > 20 * TOL
+    # and the exact-arithmetic result is within the north-star tolerance
+    assert max_abs_rel(got, oo.flash_attn_ext(q, k, v, mask, 1.0 / np.sqrt(D), oo.FA_F32)) <= TOL
+
+
+@pytest.mark.gpu
+def test_causal_attention_rejects_short_blocks(gpu_backend):
+    import torch
+
+    q, k, v = _case(5, 1, 16, 8, 32, 32, 128)
+    out = torch.empty((1, 32, 16, 128), dtype=torch.float32, device="cuda")
+    with pytest.raises(ob.GgmlBackendError):
+        gpu_backend.flash_attn_causal(torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda(),
+                                      torch.from_numpy(v).cuda(), 0.088, out)
+    gpu_backend.synchronize()

@@ -66,6 +66,15 @@ def check_token(got, ref_logits, where, noise=FLIP):
         assert got == oo.argmax_first(ref_logits)[0], where
 
 
+def assert_mostly_exact(errs, exact=1e-5):
+    """Steps agree to f32 noise unless one value landed on a q8_0 rounding boundary
+    (measured: a single flip moves a one-layer decode row's logits by ~1.2e-2 of the
+    largest logit); flips are a minority and stay within FLIP."""
+    errs = np.asarray(errs)
+    assert errs.max() < FLIP, errs
+    assert (errs < exact).sum() * 2 > len(errs), errs
+
+
 def rel_stats(got, ref):
     d = np.abs(np.asarray(got, np.float64) - ref) / np.abs(ref).max()
     return float(d.max()), float(np.median(d))
@@ -87,15 +96,49 @@ def test_one_layer_matches_reference_to_f32_noise(gpu_backend):
             k, v = m.read_kv(0, s, 30)
             np.testing.assert_array_equal(k.view(np.uint16), cache[0][0][0, :, :30].view(np.uint16))
             np.testing.assert_array_equal(v.view(np.uint16), cache[0][1][0, :, :30].view(np.uint16))
-        for i, tok in enumerate([5, 4095, 17, 2048, 3000]):
+        errs = []
+        for i, tok in enumerate([5, 4095, 17, 2048, 3000, 1, 999, 123]):
             g, n1 = m.decode_step([tok], 30 + i)
             rr = ref.step([tok], 30 + i, cache)[0]
-            assert max_abs_rel(g[0], rr) < 1e-5, i
-            check_token(n1[0], rr, f"step {i}", noise=1e-5)
+            errs.append(max_abs_rel(g[0], rr))
+            check_token(n1[0], rr, f"step {i}")
+        assert_mostly_exact(errs)
         # decode-step K/V rows: the GEMV sums blocks in another order, so f16 rows agree to one ulp
         k, v = m.read_kv(0, 0, 35)
         assert np.abs(k.astype(np.float32) - cache[0][0][0, :, :35]).max() <= 2e-3 * np.abs(k.astype(np.float32)).max()
         assert np.abs(v.astype(np.float32) - cache[0][1][0, :, :35]).max() <= 2e-3 * np.abs(v.astype(np.float32)).max()
+    finally:
+        m.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T", [64, 150, 257])
+def test_one_layer_tensor_core_prompt_pass(gpu_backend, T):
+    """Prompts of 64+ positions take the causal tcgen05 attention (fp16 operands and
+    probabilities, 128-key tiles, the diagonal tile masked in the softmax); the oracle
+    evaluates the same arithmetic (FA_TC128 with the causal mask)."""
+    cfg = ONE.replace(max_prefill=T, max_pos=512)
+    pack = om.qwen_synthetic_pack(cfg, seed=0x0A5A0003)
+    m = om.QwenModel(gpu_backend, cfg, pack)
+    try:
+        ref = qr.QwenRef(cfg, pack)
+        emb = prefix(2, T, seed=0x0A5A3060 + T)
+        logits, nxt = m.prefill(emb)
+        g, _ = m.decode_step([11, 22], T)  # decode steps continue from the tensor-core prompt pass
+        for s, tok in ((0, 11), (1, 22)):
+            cache = ref.new_cache(1)
+            lr = ref.prefill(emb[s], cache)
+            # the prompt's last row carries an N(0, 1) embedding: flips move it less than a
+            # decode row (measured <= 3e-3); the attention itself is pinned op-level in
+            # test_flash_attn_gpu.py::test_causal_tensor_core_attention
+            mx, med = rel_stats(logits[s], lr)
+            assert mx < 1e-2 and med < 2e-3, (T, s, mx, med)
+            check_token(nxt[s], lr, f"T={T} seq {s}", noise=1e-2)
+            k, v = m.read_kv(0, s, T)
+            np.testing.assert_array_equal(k.view(np.uint16), cache[0][0][0, :, :T].view(np.uint16))
+            np.testing.assert_array_equal(v.view(np.uint16), cache[0][1][0, :, :T].view(np.uint16))
+            # one step: f32 noise, or a single rounding-boundary flip
+            assert max_abs_rel(g[s], ref.step([tok], T, cache)[0]) < FLIP
     finally:
         m.close()
 
