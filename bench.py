@@ -806,7 +806,7 @@ def run_b200_qwen(args) -> None:
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
-    B, T = args.batch, om.QWEN_PREFIX_FRAMES
+    B, T, NEW = args.batch, om.QWEN_PREFIX_FRAMES, args.new_tokens
     cfg = om.QWEN3_ASR_0_6B.replace(max_batch=B, max_prefill=T)
     t_setup = time.perf_counter()
     stream = torch.cuda.Stream()
@@ -819,9 +819,9 @@ def run_b200_qwen(args) -> None:
     with torch.cuda.stream(stream):
         emb_dev = [torch.from_numpy(e).cuda() for e in emb_host]
         emb_pin = [torch.from_numpy(e).pin_memory() for e in emb_host]
-        toks_dev = torch.empty((B, QWEN_NEW), dtype=torch.int32, device="cuda")
+        toks_dev = torch.empty((B, NEW), dtype=torch.int32, device="cuda")
         for i in range(args.warmup):
-            model.generate_device(emb_dev[i], B, T, toks_dev, QWEN_NEW)
+            model.generate_device(emb_dev[i], B, T, toks_dev, NEW)
         stream.synchronize()
         if world > 1:
             dist.barrier()
@@ -831,7 +831,7 @@ def run_b200_qwen(args) -> None:
         torch.cuda.synchronize()
         e0.record(stream)
         for i in range(args.warmup, n_steps):
-            model.generate_device(emb_dev[i], B, T, toks_dev, QWEN_NEW)
+            model.generate_device(emb_dev[i], B, T, toks_dev, NEW)
         e1.record(stream)
         torch.cuda.synchronize()
         be.synchronize()
@@ -843,8 +843,8 @@ def run_b200_qwen(args) -> None:
         h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         h0.record(stream)
         for i in range(args.warmup, n_steps):
-            out = np.empty((B, QWEN_NEW), np.int32)
-            be._check(ob.lib().oasr_b200_qwen_generate(model.handle, emb_pin[i].data_ptr(), 0, B, T, QWEN_NEW,
+            out = np.empty((B, NEW), np.int32)
+            be._check(ob.lib().oasr_b200_qwen_generate(model.handle, emb_pin[i].data_ptr(), 0, B, T, NEW,
                                                        om.QWEN_EOS, 0, out.ctypes.data, 0))
         h1.record(stream)
         torch.cuda.synchronize()
@@ -855,24 +855,25 @@ def run_b200_qwen(args) -> None:
     if rank == 0:
         peak, peak_kind = measured_peak_hbm()
         achieved = fa["bytes"] / (fa["us"] * 1e-6) / 1e9
-        tokens = B * QWEN_NEW * args.steps * world
+        tokens = B * NEW * args.steps * world
         line = {
-            "metric": QWEN_METRIC, "value": audio / dev_s, "unit": "audio-s/s", "n_gpus": world,
+            "metric": QWEN_METRIC.replace(f"greedy {QWEN_NEW}", f"greedy {NEW}"), "value": audio / dev_s,
+            "unit": "audio-s/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_s / args.steps * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "q8_0 x q8_0 int dot (f32 accumulate), f16 KV",
             "data": "synthetic (seeded N(0,0.02) Q8_0 weights, N(0,1) 390-frame prompt embeddings)",
             "config": {"workload": f"configs[2]: qwen3-asr-0.6b-shaped decoder (28 layers, d 1024, 16/8 heads of 128, "
                                    f"ffn 3072, vocab 151936), batch {B} per GPU, 390-frame prompt (30 s of audio), "
-                                   f"greedy {QWEN_NEW} tokens, prefill + decode on device",
-                       "batch_per_gpu": B, "sequences_per_step": B * world, "new_tokens": QWEN_NEW,
+                                   f"greedy {NEW} tokens, prefill + decode on device",
+                       "batch_per_gpu": B, "sequences_per_step": B * world, "new_tokens": NEW,
                        "tokens_per_s": tokens / dev_s,
                        "l2": "inputs larger than L2 (633 MB of Q8_0 weights per decode step)",
                        "parallelism": f"independent replicas x{world} (sequences sharded per GPU)",
                        "setup_s": round(t_setup, 1)},
             "e2e": {"value": audio / e2e_s, "unit": "audio-s/s", "h2d_bytes_per_step": int(emb_host[0].nbytes),
-                    "d2h_bytes_per_step": B * QWEN_NEW * 4},
-            "gpu_launches": args.steps * qwen_launches_per_batch(cfg.n_layers, QWEN_NEW),
+                    "d2h_bytes_per_step": B * NEW * 4},
+            "gpu_launches": args.steps * qwen_launches_per_batch(cfg.n_layers, NEW),
             "roofline": {"bound": "hbm", "kernel": f"fattn_split_kernel<128,2,f16> (GQA decode attention, {B} x 8 kv "
                                                    f"heads x {fa['n_kv']} f16 K/V positions)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
@@ -906,6 +907,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=["rtfx", "qwen", "mulmat", "kernels"], default="rtfx")
     ap.add_argument("--batch", type=int, default=8, help="sequences per GPU (qwen workload: 1, 4 or 8)")
+    ap.add_argument("--new-tokens", type=int, default=256,
+                    help="qwen workload: greedy tokens per sequence (256 = configs[2]; fewer only to profile)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.steps is None:
