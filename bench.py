@@ -314,6 +314,29 @@ N_NEW = 224
 UTT_SEED = 0x0A5A0005
 
 
+def graph_timed(torch, stream, fn, iters: int, replays: int = 3) -> float:
+    """Mean device time (us) of one fn(i) call: `iters` calls captured into a CUDA graph
+    (no host launch overhead between them), the graph replayed `replays` times between
+    CUDA events on `stream`."""
+    for i in range(3):
+        fn(i)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(iters):
+            fn(i)
+    graph.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream.synchronize()
+    e0.record(stream)
+    for _ in range(replays):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    del graph
+    return e0.elapsed_time(e1) / (replays * iters) * 1e3
+
+
 def reduce_over_ranks(dev_s: float, e2e_s: float, audio_s: float, device) -> tuple[float, float, float]:
     """Whole-job figures from every rank's own: the slowest rank's device and
     end-to-end times (max) and the audio seconds all ranks processed (sum).
@@ -408,8 +431,9 @@ def run_reference(args) -> None:
 
 def _fa_roofline(be, torch, stream, n_layers_rot: int = 4, iters: int = 20) -> dict:
     """The dominant kernel of the decode step -- cross-attention flash-decode over the
-    f16 cross-K/V of 8 utterances (fattn_split_kernel, D 64, 20 heads, n_kv 1500) --
-    timed alone on the benchmark stream, rotating over 4 layers' K/V (246 MB > L2)."""
+    f16 cross-K/V of 8 utterances (fattn_heads_kernel, D 64, 20 heads, n_kv 1500) --
+    timed alone on the benchmark stream from a CUDA graph of `iters` launches,
+    rotating over 4 layers' K/V (246 MB > L2)."""
     S, H, N, D = 8, 20, 1500, 64
     kv = [torch.randn(S, N, 2 * H * D, device="cuda").half() for _ in range(n_layers_rot)]
     q = torch.randn(S, 1, H * D, device="cuda")
@@ -421,16 +445,11 @@ def _fa_roofline(be, torch, stream, n_layers_rot: int = 4, iters: int = 20) -> d
         views.append((k, v))
     qv = q.reshape(S, 1, H, D).permute(0, 2, 1, 3)
     ov = out.reshape(S, 1, H, D)
-    for i in range(5):
+
+    def launch(i):
         be.flash_attn_ext(qv, views[i % n_layers_rot][0], views[i % n_layers_rot][1], None, 0.125, ov)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    stream.synchronize()
-    e0.record(stream)
-    for i in range(iters):
-        be.flash_attn_ext(qv, views[i % n_layers_rot][0], views[i % n_layers_rot][1], None, 0.125, ov)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    us = e0.elapsed_time(e1) / iters * 1e3
+
+    us = graph_timed(torch, stream, launch, iters)
     nbytes = S * N * 2 * H * D * 2 + 2 * S * H * D * 4
     return {"us": us, "bytes": nbytes}
 
@@ -534,7 +553,8 @@ def run_b200(args) -> None:
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": ncu_traffic_fa(), "algorithmic_bytes": fa["bytes"],
                          "avg_launch_us": fa["us"], "how": "same kernel and shapes timed alone on the bench stream "
-                                                           "after the timed region, K/V rotated over 246 MB"},
+                                                           "after the timed region from a CUDA graph of 20 launches, "
+                                                           "K/V rotated over 246 MB"},
             "clocks": clocks,
         }
         line["cpu_baseline"] = rtfx_cpu_baseline()
@@ -563,8 +583,9 @@ def run_kernels(args) -> None:
     decode GEMVs (Q4_K, M = 8, rotated over 12 layers' weights = 155 MB > L2), the
     Q8_0 logits head (two copies, 141 MB), cross- and self-attention flash-decode,
     the encoder's Q4_K tensor-core GEMMs (M = 12000) and the encoder flash attention
-    (8 x 20 heads x 1500 x 1500).  Also the small, fixed command the committed ncu
-    captures use."""
+    (8 x 20 heads x 1500 x 1500); then the Qwen decode GEMVs, GQA decode
+    attention and causal prompt attention at batch 8.  Also the small, fixed command the
+    committed ncu captures use."""
     import torch
 
     import openasr_b200 as ob
@@ -585,25 +606,7 @@ def run_kernels(args) -> None:
         return "mmv_q8_kernel (dp4a)" if dp4a else "mmv_q80_tc_kernel (mma.sync s8)"
 
     def timed(fn, iters):
-        """mean device time of one call: `iters` calls captured in a CUDA graph (no
-        host launch overhead between them), the graph replayed 3 times"""
-        for i in range(3):
-            fn(i)
-        stream.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            for i in range(iters):
-                fn(i)
-        graph.replay()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        stream.synchronize()
-        e0.record(stream)
-        for _ in range(3):
-            graph.replay()
-        e1.record(stream)
-        torch.cuda.synchronize()
-        del graph
-        return e0.elapsed_time(e1) / (3 * iters) * 1e3
+        return graph_timed(torch, stream, fn, iters)
 
     def add(name, shape, us, amount, unit):
         if unit == "GB/s":
@@ -687,6 +690,33 @@ def run_kernels(args) -> None:
         us = timed(lambda i: be.flash_attn_ext(qe, ke, ve, None, 0.125, oe), 10)
         add("fa_prep_kernel+fattn_tc_kernel", f"encoder S={B} H={H} {T}x{T} D=64", us, 4.0 * B * H * T * T * 64,
             "TFLOP/s")
+        del qkv
+        # Qwen3-ASR-0.6B decode (configs[2], batch 8): Q8_0 GEMVs rotated over 4 layers' weights
+        for role, N, K in [("qwen qkv", 4096, 1024), ("qwen gate|up", 6144, 1024), ("qwen down", 1024, 3072),
+                           ("qwen o", 1024, 2048), ("qwen lm_head", 151936, 1024)]:
+            n_rot = 2 if N > 100000 else 4
+            ws = [be.upload_weight(ob.quantize(ob.Q8_0, ob.synth_normal(0x100 + 16 * j + N + K, N * K, 0.0, 0.02)
+                                               .reshape(N, K)), ob.Q8_0, [K, N]) for j in range(n_rot)]
+            x = torch.randn(B, K, device="cuda")
+            qa = torch.empty(be.act_bytes(ob.Q8_0, K, B), dtype=torch.uint8, device="cuda")
+            be.quantize_act(ob.Q8_0, x, qa)
+            y = torch.empty(B, N, device="cuda")
+            us = timed(lambda i: be.mul_mat_qact(ws[i % n_rot], qa, B, y), 20 if N > 100000 else 48)
+            add(gemv_name("q80"), f"{role} Q8_0 N={N} K={K} M={B}", us, N * K * 34 / 32 + B * K + B * N * 4, "GB/s")
+            del ws
+        # Qwen GQA decode attention at the mid-generation KV length
+        fq = _qwen_fa_roofline(be, torch, stream, B, 390 + 128)
+        add("fattn_gqa_kernel<2>", f"qwen decode S={B} H=16 HKV=8 n_kv={fq['n_kv']} D=128", fq["us"], fq["bytes"],
+            "GB/s")
+        # Qwen causal prompt attention on the tensor cores (8 x 390 rows, GQA, D 128)
+        Tq = 390
+        qq = torch.randn(B, 16, Tq, 128, device="cuda")
+        kq = torch.randn(B, 8, Tq, 128, device="cuda").half()
+        vq = torch.randn(B, 8, Tq, 128, device="cuda").half()
+        oq = torch.empty(B, Tq, 16, 128, device="cuda")
+        us = timed(lambda i: be.flash_attn_causal(qq, kq, vq, 1.0 / float(np.sqrt(128.0)), oq), 10)
+        add("fa_prep_kernel+fattn_tc_kernel<128,causal>", f"qwen prompt S={B} H=16 HKV=8 {Tq}x{Tq} D=128", us,
+            2.0 * B * 16 * Tq * (Tq + 1) * 128, "TFLOP/s")
     print(json.dumps({"workload": "kernels", "n_gpus": 1, "kernels": rows}), flush=True)
     be.close()
 
@@ -699,13 +729,16 @@ QWEN_NEW = 256
 QWEN_SEED = 0x0A5A0003
 
 
-def qwen_launches_per_batch(n_layers: int, n_new: int) -> int:
+def qwen_launches_per_batch(n_layers: int, n_new: int, n_tok: int = 390) -> int:
     """Kernel launches of one oasr_b200_qwen_generate (counted from model_qwen.cu):
-    prefill = first RMSNorm + 10 per layer (3 GEMMs + o GEMM, q/k-norm+RoPE+KV write,
-    attention, quantize, RMSNorm, SwiGLU) less the last layer's trailing RMSNorm + head
-    (RMSNorm, logits, argmax) + 1 advance; decode step = embed + RMSNorm + 9 per layer +
-    logits + argmax + advance; the causal mask is built once per prompt length."""
-    prefill = 1 + 10 * n_layers - 1 + 3 + 1
+    prefill = first RMSNorm + per layer (q|k|v, o, gate|up and down GEMMs, q/k-norm +
+    RoPE + KV write, attention, quantize, RMSNorm, SwiGLU = 10; the tensor-core attention
+    of 64+ rows adds 3 f16 staging kernels and, when n_tok % 8, a pad kernel) less the last
+    layer's trailing RMSNorm + head (RMSNorm, logits, argmax) + 1 advance; decode step =
+    embed + RMSNorm + 9 per layer + logits + argmax + advance; the causal mask is built
+    once per prompt length."""
+    attn_extra = (3 + (1 if n_tok % 8 else 0)) if n_tok >= 64 else 0
+    prefill = 1 + (10 + attn_extra) * n_layers - 1 + 3 + 1
     step = 2 + 9 * n_layers + 3
     return prefill + (n_new - 1) * step
 
@@ -763,10 +796,10 @@ def run_reference_qwen(args) -> None:
 
 
 def _qwen_fa_roofline(be, torch, stream, S: int, n_kv: int, n_rot: int = 8, iters: int = 40) -> dict:
-    """The decode step's attention (fattn_split_kernel<128, 2, f16>: GQA 16 q / 8 kv heads,
-    D 128) over the mid-generation KV length, through the public flash_attn_ext entry point
-    on views of the model's cache layout [seq][kv head][max_pos][128], timed alone on the
-    bench stream and rotating over 8 layers' caches (> L2)."""
+    """The decode step's attention (fattn_gqa_kernel<2>: GQA 16 q / 8 kv heads, D 128) over
+    the mid-generation KV length, through the public flash_attn_ext entry point on views
+    of the model's cache layout [seq][kv head][max_pos][128], timed alone on the bench
+    stream from a CUDA graph of `iters` launches, rotating over 8 layers' caches (> L2)."""
     P, HKV, H, D = 2048, 8, 16, 128
     caches = [(torch.randn(S, HKV, P, D, device="cuda").half(), torch.randn(S, HKV, P, D, device="cuda").half())
               for _ in range(n_rot)]
@@ -778,16 +811,7 @@ def _qwen_fa_roofline(be, torch, stream, S: int, n_kv: int, n_rot: int = 8, iter
         k, v = caches[i % n_rot]
         be.flash_attn_ext(q, k[:, :, :n_kv], v[:, :, :n_kv], None, scale, out)
 
-    for i in range(5):
-        launch(i)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    stream.synchronize()
-    e0.record(stream)
-    for i in range(iters):
-        launch(i)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    us = e0.elapsed_time(e1) / iters * 1e3
+    us = graph_timed(torch, stream, launch, iters)
     return {"us": us, "bytes": S * HKV * n_kv * D * 2 * 2 + 2 * S * H * D * 4, "n_kv": n_kv}
 
 
@@ -873,13 +897,14 @@ def run_b200_qwen(args) -> None:
                        "setup_s": round(t_setup, 1)},
             "e2e": {"value": audio / e2e_s, "unit": "audio-s/s", "h2d_bytes_per_step": int(emb_host[0].nbytes),
                     "d2h_bytes_per_step": B * NEW * 4},
-            "gpu_launches": args.steps * qwen_launches_per_batch(cfg.n_layers, NEW),
-            "roofline": {"bound": "hbm", "kernel": f"fattn_split_kernel<128,2,f16> (GQA decode attention, {B} x 8 kv "
+            "gpu_launches": args.steps * qwen_launches_per_batch(cfg.n_layers, NEW, T),
+            "roofline": {"bound": "hbm", "kernel": f"fattn_gqa_kernel<2> (GQA decode attention, {B} x 8 kv "
                                                    f"heads x {fa['n_kv']} f16 K/V positions)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes": fa["bytes"],
                          "avg_launch_us": fa["us"], "how": "same kernel and shapes through flash_attn_ext, timed alone "
-                                                           "on the bench stream, caches rotated over 8 layers"},
+                                                           "on the bench stream from a CUDA graph of 40 launches, "
+                                                           "caches rotated over 8 layers"},
             "clocks": clocks,
         }
         line["cpu_baseline"] = qwen_cpu_baseline()

@@ -87,6 +87,7 @@ static __device__ __forceinline__ void stage_l2(float *dst, const float *src, in
 
 constexpr int FA_HEADS_U = 8;            // KV positions per warp load batch (double buffered)
 constexpr int FA_HEADS_MAX_SPLITS = 16;  // most KV splits of one query row (partials staged by the merging CTA)
+constexpr int FA_GQA_U = 2;              // KV positions per lane group and load batch (double buffered)
 
 template <int D, int QT, bool F16>
 __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
@@ -469,6 +470,230 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
     }
 }
 
+// Decode attention with grouped queries over head-major f16 caches (the Qwen decoder:
+// [seq][kv head][pos][128], one kv head's positions in contiguous 256-byte rows): a CTA
+// takes one (sequence, kv head), its G query heads and a range of positions.  Eight lanes
+// share a position (16 dims = two 16-byte loads of K and of V per lane), so a warp covers
+// four positions per step and all G heads reuse every K/V load; two batches of U
+// positions per lane group are in flight in registers, and each batch is folded into the
+// running softmax with one rescale per head.  Arithmetic as fattn_split_kernel<128, G,
+// true>: q rounded to f16, fmaf dot over 16 dims then the 8-lane shuffle tree, exp online
+// softmax; the splits merge in order in the last-arriving CTA of each (sequence, kv head).
+template <int G, int U>
+__global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
+    constexpr int D = 128;
+    griddep_launch_dependents();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int grp = lane >> 3, sl = lane & 7;  // position group in the warp, lane in the group
+    const int hk = blockIdx.x % a.HKV, s = blockIdx.x / a.HKV, split = blockIdx.y;
+    const char *kb = a.k + hk * a.k_nb2 + s * a.k_nb3 + sl * 32;
+    const char *vb = a.v + hk * a.v_nb2 + s * a.v_nb3 + sl * 32;
+    if (threadIdx.x == 0 && a.nkv_dev) {
+        // stream this CTA's K/V rows toward L2 before the wait (a hint; the range is
+        // recomputed below, and the KV length is set between steps)
+        const int nk = min(*a.nkv_dev, a.NKV), pp = (nk + a.n_splits - 1) / a.n_splits;
+        const int p0 = split * pp, p1 = min(nk, p0 + pp);
+        if (p1 > p0) {
+            prefetch_l2_bulk(a.k + hk * a.k_nb2 + s * a.k_nb3 + (int64_t)p0 * a.k_nb1, (uint32_t)((p1 - p0) * a.k_nb1));
+            prefetch_l2_bulk(a.v + hk * a.v_nb2 + s * a.v_nb3 + (int64_t)p0 * a.v_nb1, (uint32_t)((p1 - p0) * a.v_nb1));
+        }
+    }
+    griddep_wait();
+
+    float qv[G][16];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const float *qp = reinterpret_cast<const float *>(a.q + (hk * G + g) * a.q_nb2 + s * a.q_nb3) + sl * 16;
+#pragma unroll
+        for (int e = 0; e < 16; e += 4) {
+            const float4 x = *reinterpret_cast<const float4 *>(qp + e);
+            qv[g][e] = __half2float(__float2half_rn(x.x));
+            qv[g][e + 1] = __half2float(__float2half_rn(x.y));
+            qv[g][e + 2] = __half2float(__float2half_rn(x.z));
+            qv[g][e + 3] = __half2float(__float2half_rn(x.w));
+        }
+    }
+    float mx[G], sm[G], acc[G][16];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        mx[g] = -INFINITY;
+        sm[g] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) acc[g][e] = 0.0f;
+    }
+
+    const int nkv = a.nkv_dev ? min(*a.nkv_dev, a.NKV) : a.NKV;
+    const int per = a.nkv_dev ? (nkv + a.n_splits - 1) / a.n_splits : a.kv_per_split;
+    const int kv0 = split * per;
+    const int kv1 = min(nkv, kv0 + per);
+    // positions of lane group (warp, grp) in a batch: pb + 16 u (pb = first position of
+    // the batch for this group); a CTA batch covers 16 U positions
+    constexpr int STEP = 16 * U;
+    auto load = [&](int pb, int4 (&kr)[U][2], int4 (&vr)[U][2]) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int p = pb + 16 * u;
+            if (p < kv1) {
+                const int4 *kp = reinterpret_cast<const int4 *>(kb + (int64_t)p * a.k_nb1);
+                const int4 *vp = reinterpret_cast<const int4 *>(vb + (int64_t)p * a.v_nb1);
+                kr[u][0] = kp[0];
+                kr[u][1] = kp[1];
+                vr[u][0] = vp[0];
+                vr[u][1] = vp[1];
+            } else {
+                kr[u][0] = kr[u][1] = vr[u][0] = vr[u][1] = make_int4(0, 0, 0, 0);  // weight 0 below
+            }
+        }
+    };
+    auto consume = [&](int pb, const int4 (&kr)[U][2], const int4 (&vr)[U][2]) {
+        float sc[G][U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            float kf[16];
+            load8<true>(reinterpret_cast<const char *>(&kr[u][0]), *reinterpret_cast<float(*)[8]>(&kf[0]));
+            load8<true>(reinterpret_cast<const char *>(&kr[u][1]), *reinterpret_cast<float(*)[8]>(&kf[8]));
+            const bool valid = pb + 16 * u < kv1;
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                float d = 0.0f;
+#pragma unroll
+                for (int e = 0; e < 16; ++e) d = fmaf(qv[g][e], kf[e], d);
+#pragma unroll
+                for (int o = 4; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                sc[g][u] = valid ? d * a.scale : -INFINITY;
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            float mb = sc[g][0];
+#pragma unroll
+            for (int u = 1; u < U; ++u) mb = fmaxf(mb, sc[g][u]);
+            const float mnew = fmaxf(mx[g], mb);
+            if (mnew == -INFINITY) continue;      // nothing visible to this group yet
+            const float corr = expf(mx[g] - mnew);  // mx = -inf -> 0
+            sm[g] *= corr;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) acc[g][e] *= corr;
+            mx[g] = mnew;
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            float vf[16];
+            load8<true>(reinterpret_cast<const char *>(&vr[u][0]), *reinterpret_cast<float(*)[8]>(&vf[0]));
+            load8<true>(reinterpret_cast<const char *>(&vr[u][1]), *reinterpret_cast<float(*)[8]>(&vf[8]));
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                if (sc[g][u] == -INFINITY) continue;
+                const float w = expf(sc[g][u] - mx[g]);
+                sm[g] += w;
+#pragma unroll
+                for (int e = 0; e < 16; ++e) acc[g][e] = fmaf(w, vf[e], acc[g][e]);
+            }
+        }
+    };
+    int4 kA[U][2], vA[U][2], kB[U][2], vB[U][2];
+    // warp-uniform loop bounds: every lane runs the same iterations (the shuffles need
+    // all 32); positions past kv1 carry weight 0
+    const int wbase = kv0 + 4 * warp;  // the warp's first position of a batch (group 0)
+    int pb = wbase;
+    if (pb < kv1) load(pb + grp, kA, vA);
+    while (pb < kv1) {
+        int pn = pb + STEP;
+        if (pn < kv1) load(pn + grp, kB, vB);
+        consume(pb + grp, kA, vA);
+        pb = pn;
+        if (pb >= kv1) break;
+        pn = pb + STEP;
+        if (pn < kv1) load(pn + grp, kA, vA);
+        consume(pb + grp, kB, vB);
+        pb = pn;
+    }
+
+    // merge the warp's 4 position groups (same dims, different positions)
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+#pragma unroll
+        for (int o = 8; o < 32; o <<= 1) {
+            const float om = __shfl_xor_sync(0xffffffffu, mx[g], o);
+            const float os = __shfl_xor_sync(0xffffffffu, sm[g], o);
+            const float nm = fmaxf(mx[g], om);
+            const float f0 = mx[g] == -INFINITY ? 0.0f : expf(mx[g] - nm);
+            const float f1 = om == -INFINITY ? 0.0f : expf(om - nm);
+            sm[g] = sm[g] * f0 + os * f1;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const float oa = __shfl_xor_sync(0xffffffffu, acc[g][e], o);
+                acc[g][e] = acc[g][e] * f0 + oa * f1;
+            }
+            mx[g] = nm;
+        }
+    }
+    // merge the 4 warps through shared memory
+    __shared__ float s_m[4][G], s_s[4][G];
+    __shared__ float s_acc[4][G][D];
+    if (grp == 0) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) s_acc[warp][g][sl * 16 + e] = acc[g][e];
+            if (sl == 0) {
+                s_m[warp][g] = mx[g];
+                s_s[warp][g] = sm[g];
+            }
+        }
+    }
+    __syncthreads();
+    for (int o = threadIdx.x; o < G * D; o += 128) {
+        const int g = o / D, e = o % D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, s_m[w][g]);
+        float L = 0.0f, A = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const float f = s_m[w][g] == -INFINITY ? 0.0f : expf(s_m[w][g] - M);
+            L += s_s[w][g] * f;
+            A += s_acc[w][g][e] * f;
+        }
+        const int h = hk * G + g;
+        if (a.n_splits == 1) {
+            float *out = reinterpret_cast<float *>(a.dst + h * a.d_nb1 + s * a.d_nb3);
+            out[e] = L == 0.0f ? 0.0f : A / L;
+        } else {
+            const int64_t row = (int64_t)s * a.H + h;
+            float *pp = a.partials + (row * a.n_splits + split) * (D + 2);
+            pp[e] = A;
+            if (e == 0) {
+                pp[D] = M;
+                pp[D + 1] = L;
+            }
+        }
+    }
+    if (a.n_splits == 1) return;
+    if (!cta_last_arrival(a.counters + blockIdx.x, (unsigned)a.n_splits)) return;
+    // the G heads' partials are contiguous ([head][split][D + 2]): stage them in shared
+    // memory with every load in flight, then merge in split order
+    __shared__ float s_part[G * FA_HEADS_MAX_SPLITS * (D + 2)];
+    const float *pbase = a.partials + ((int64_t)s * a.H + hk * G) * a.n_splits * (D + 2);
+    stage_l2(s_part, pbase, G * a.n_splits * (D + 2));
+    __syncthreads();
+    for (int o = threadIdx.x; o < G * D; o += 128) {
+        const int g = o / D, e = o % D;
+        const float *pp = s_part + g * a.n_splits * (D + 2);
+        float M = -INFINITY;
+        for (int sp = 0; sp < a.n_splits; ++sp) M = fmaxf(M, pp[sp * (D + 2) + D]);
+        float L = 0.0f, A = 0.0f;
+        for (int sp = 0; sp < a.n_splits; ++sp) {
+            const float m = pp[sp * (D + 2) + D];
+            const float f = m == -INFINITY ? 0.0f : expf(m - M);
+            L += pp[sp * (D + 2) + D + 1] * f;
+            A += pp[sp * (D + 2) + e] * f;
+        }
+        float *out = reinterpret_cast<float *>(a.dst + (hk * G + g) * a.d_nb1 + s * a.d_nb3);
+        out[e] = L == 0.0f ? 0.0f : A / L;
+    }
+}
+
 template <int D, bool F16>
 static cudaError_t launch_fa_d(oasr_backend *be, const FaArgs &a, int QT, dim3 grid) {
     switch (QT) {
@@ -510,6 +735,19 @@ static int split_kernel_occupancy(int D, int QT, bool f16) {
     if (D == 128) { if (f16) FA_OCC_FN(128, true); else FA_OCC_FN(128, false); }
     else { if (f16) FA_OCC_FN(64, true); else FA_OCC_FN(64, false); }
 #undef FA_OCC_FN
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, 128, 0) != cudaSuccess || n < 1) n = 1;
+    occ = n;
+    return occ;
+}
+
+// resident CTAs per SM of the GQA decode kernel for G query heads per kv head
+static int gqa_kernel_occupancy(int G) {
+    static int cache[5];
+    int &occ = cache[G];
+    if (occ) return occ;
+    const void *fn = G == 1 ? (const void *)fattn_gqa_kernel<1, FA_GQA_U>
+                   : G == 2 ? (const void *)fattn_gqa_kernel<2, FA_GQA_U> : (const void *)fattn_gqa_kernel<4, FA_GQA_U>;
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, 128, 0) != cudaSuccess || n < 1) n = 1;
     occ = n;
@@ -599,9 +837,21 @@ static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const
     // one query per (sequence, head), f16 heads contiguous in a KV row: the 4-head kernel
     const bool heads = D == 64 && k->type == OASR_TYPE_F16 && a.NQ == 1 && a.G == 1 && !mask && a.H % 4 == 0 &&
                        k->nb[2] == 2 * D && v->nb[2] == 2 * D && a.S * (int64_t)(a.H / 4) <= (1 << 16);
-    const int64_t groups = heads ? (int64_t)a.S * (a.H / 4) : (int64_t)a.HKV * a.S * a.n_qtiles;
+    // one query per (sequence, head) over head-major f16 caches with 256-byte rows: the GQA kernel
+    const bool gqa = !heads && D == 128 && k->type == OASR_TYPE_F16 && v->type == OASR_TYPE_F16 && a.NQ == 1 &&
+                     !mask && !q_bias && (a.G == 1 || a.G == 2 || a.G == 4) && k->nb[1] == 256 && v->nb[1] == 256 &&
+                     k->nb[2] % 16 == 0 && k->nb[3] % 16 == 0 && v->nb[2] % 16 == 0 && v->nb[3] % 16 == 0 &&
+                     q->nb[2] % 16 == 0 && q->nb[3] % 16 == 0 && ((uintptr_t)q->data & 15) == 0 &&
+                     ((uintptr_t)k->data & 15) == 0 && ((uintptr_t)v->data & 15) == 0 &&
+                     (int64_t)a.S * a.HKV <= 0x7fffffffLL;
+    const int64_t groups = heads ? (int64_t)a.S * (a.H / 4) : gqa ? (int64_t)a.S * a.HKV : (int64_t)a.HKV * a.S * a.n_qtiles;
     int n_splits = 1;
-    if (heads) {
+    if (gqa) {
+        // one full wave of resident CTAs, at least 32 positions per split
+        const int resident = be->sm_count * gqa_kernel_occupancy(a.G);
+        n_splits = (int)std::max<int64_t>(1, resident / groups);
+        n_splits = std::max(1, std::min(std::min(n_splits, a.NKV / 32), FA_HEADS_MAX_SPLITS));
+    } else if (heads) {
         // one full wave of resident CTAs, at least 32 positions per split
         static int occ = 0;  // resident CTAs per SM (same for every device of this build)
         if (occ == 0 && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fattn_heads_kernel<FA_HEADS_U>, 128, 0) != cudaSuccess)
@@ -646,6 +896,9 @@ static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const
     const bool f16 = k->type == OASR_TYPE_F16;
     cudaError_t e;
     if (heads) e = launch_k(be, fattn_heads_kernel<FA_HEADS_U>, grid, dim3(128), 0, a);
+    else if (gqa) e = a.G == 1 ? launch_k(be, fattn_gqa_kernel<1, FA_GQA_U>, grid, dim3(128), 0, a)
+                    : a.G == 2 ? launch_k(be, fattn_gqa_kernel<2, FA_GQA_U>, grid, dim3(128), 0, a)
+                               : launch_k(be, fattn_gqa_kernel<4, FA_GQA_U>, grid, dim3(128), 0, a);
     else if (D == 64) e = f16 ? launch_fa_d<64, true>(be, a, QT, grid) : launch_fa_d<64, false>(be, a, QT, grid);
     else e = f16 ? launch_fa_d<128, true>(be, a, QT, grid) : launch_fa_d<128, false>(be, a, QT, grid);
     if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "flash_attn launch", __LINE__);

@@ -235,3 +235,17 @@ def test_causal_attention_rejects_short_blocks(gpu_backend):
         gpu_backend.flash_attn_causal(torch.from_numpy(q).cuda(), torch.from_numpy(k).cuda(),
                                       torch.from_numpy(v).cuda(), 0.088, out)
     gpu_backend.synchronize()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("S,H,HKV", [(1, 16, 8), (8, 16, 8), (3, 8, 8), (2, 16, 4)])
+@pytest.mark.parametrize("NKV", [1, 17, 391, 2048])
+def test_gqa_decode_head_major_cache(gpu_backend, S, H, HKV, NKV):
+    """One query per head over head-major f16 caches [seq][kv head][pos][128] (the Qwen
+    decoder's layout) takes the grouped-query decode kernel (G = 1, 2, 4 query heads per
+    kv head); same arithmetic as the split kernel, checked against the exact-f32 oracle."""
+    q, k, v = _case(700 + S * NKV + H + HKV, S, H, HKV, 1, NKV, 128)
+    got = _fa(gpu_backend, q, k, v, None, 1.0 / np.sqrt(128))
+    ref = oo.flash_attn_ext(q, k, v, None, 1.0 / np.sqrt(128), oo.FA_F32)
+    err = max_abs_rel(got, ref)
+    assert err <= TOL and err <= TIGHT, err
