@@ -46,7 +46,23 @@ struct FaArgs {
     unsigned int *counters;   // one ticket per (kv head, seq, q tile)
     const float *q_bias;      // optional [H*D] added to q before the fp16 rounding
     const int *nkv_dev;       // optional device-side KV length (<= NKV), for graph-captured decode
+    // optional (GQA kernel): the output rows [S][H * D] quantized to q8_0 planes (quants oq,
+    // f16-rounded scales od [S][H * D / 32]) instead of written as f32 -- the next mul_mat's input
+    int8_t *oq;
+    float *od;
 };
+
+// One output element per thread of a full warp, 32 consecutive dims of one head per warp:
+// quantize_row_q8_0 of the warp's block (d = amax / 127, q = round(v / d), d stored f16)
+static __device__ __forceinline__ void store_q8_0_warp(float v, int8_t *q, float *d_slot, int lane) {
+    float amax = fabsf(v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __frcp_rn(d) : 0.0f;
+    *q = (int8_t)(int)roundf(__fmul_rn(v, id));
+    if (lane == 0) *d_slot = __half2float(__float2half_rn(d));
+}
 
 template <bool F16>
 static __device__ __forceinline__ void load8(const char *p, float (&out)[8]) {
@@ -657,8 +673,13 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
         }
         const int h = hk * G + g;
         if (a.n_splits == 1) {
-            float *out = reinterpret_cast<float *>(a.dst + h * a.d_nb1 + s * a.d_nb3);
-            out[e] = L == 0.0f ? 0.0f : A / L;
+            const float val = L == 0.0f ? 0.0f : A / L;
+            if (a.oq) {
+                const int64_t idx = ((int64_t)s * a.H + h) * D + e;
+                store_q8_0_warp(val, a.oq + idx, a.od + idx / 32, lane);
+            } else {
+                reinterpret_cast<float *>(a.dst + h * a.d_nb1 + s * a.d_nb3)[e] = val;
+            }
         } else {
             const int64_t row = (int64_t)s * a.H + h;
             float *pp = a.partials + (row * a.n_splits + split) * (D + 2);
@@ -689,8 +710,13 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
             L += pp[sp * (D + 2) + D + 1] * f;
             A += pp[sp * (D + 2) + e] * f;
         }
-        float *out = reinterpret_cast<float *>(a.dst + (hk * G + g) * a.d_nb1 + s * a.d_nb3);
-        out[e] = L == 0.0f ? 0.0f : A / L;
+        const float val = L == 0.0f ? 0.0f : A / L;
+        if (a.oq) {
+            const int64_t idx = ((int64_t)s * a.H + hk * G + g) * D + e;
+            store_q8_0_warp(val, a.oq + idx, a.od + idx / 32, lane);
+        } else {
+            reinterpret_cast<float *>(a.dst + (hk * G + g) * a.d_nb1 + s * a.d_nb3)[e] = val;
+        }
     }
 }
 
@@ -720,7 +746,7 @@ struct FaScratch {
 
 static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
                                    const oasr_tensor *mask, float scale, oasr_tensor *dst, const float *q_bias,
-                                   const int *nkv_dev, const FaScratch *fixed);
+                                   const int *nkv_dev, const FaScratch *fixed, const ActPlanes *out_q8 = nullptr);
 
 // resident CTAs per SM of one fattn_split_kernel instantiation (same for every device of this build)
 static int split_kernel_occupancy(int D, int QT, bool f16) {
@@ -759,6 +785,11 @@ int launch_flash_attn_ex(oasr_backend *be, const oasr_tensor *q, const oasr_tens
                          const oasr_tensor *mask, float scale, oasr_tensor *dst, const float *q_bias,
                          const int *nkv_dev) {
     return launch_flash_attn_split(be, q, k, v, mask, scale, dst, q_bias, nkv_dev, nullptr);
+}
+
+int launch_flash_attn_decode_q8(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
+                                float scale, oasr_tensor *dst, const int *nkv_dev, const ActPlanes &out_q8) {
+    return launch_flash_attn_split(be, q, k, v, nullptr, scale, dst, nullptr, nkv_dev, nullptr, &out_q8);
 }
 
 // ---- allocation-free variant ------------------------------------------------------------
@@ -803,8 +834,8 @@ int launch_flash_attn_static(oasr_backend *be, const oasr_tensor *q, const oasr_
 
 static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
                                    const oasr_tensor *mask, float scale, oasr_tensor *dst, const float *q_bias,
-                                   const int *nkv_dev, const FaScratch *fixed) {
-    FaArgs a;
+                                   const int *nkv_dev, const FaScratch *fixed, const ActPlanes *out_q8) {
+    FaArgs a = {};
     a.q_bias = q_bias;
     a.nkv_dev = nkv_dev;
     const int D = (int)q->ne[0];
@@ -844,6 +875,11 @@ static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const
                      q->nb[2] % 16 == 0 && q->nb[3] % 16 == 0 && ((uintptr_t)q->data & 15) == 0 &&
                      ((uintptr_t)k->data & 15) == 0 && ((uintptr_t)v->data & 15) == 0 &&
                      (int64_t)a.S * a.HKV <= 0x7fffffffLL;
+    if (out_q8) {
+        if (!gqa) return oasr_internal_fail(be, OASR_STATUS_FAILED, "flash_attn: q8_0 output needs the GQA decode kernel");
+        a.oq = out_q8->qs;
+        a.od = out_q8->d;
+    }
     const int64_t groups = heads ? (int64_t)a.S * (a.H / 4) : gqa ? (int64_t)a.S * a.HKV : (int64_t)a.HKV * a.S * a.n_qtiles;
     int n_splits = 1;
     if (gqa) {

@@ -64,7 +64,7 @@ struct oasr_qwen {
     void *dqa;
     int *tokens, *pos, *nkv, *history;
     int family;
-    bool fused_o;  // attention output quantized inside the o_proj GEMV (dgemv)
+    bool attn_q8;  // decode attention writes its output as the o_proj's q8_0 planes
     bool pdl;
     cudaGraphExec_t graph;
     int graph_batch;
@@ -239,7 +239,7 @@ int launch_qkv_post(oasr_qwen *m, const float *qkv, int64_t rows, int T, const i
 
 // attention of `nq` query rows per sequence over the sequence's cache rows
 int attend(oasr_qwen *m, const QLayer &L, const float *q, int nq, int n, int nkv_max, const __half *mask,
-           const int *nkv_dev, float *out) {
+           const int *nkv_dev, float *out, const ActPlanes *out_q8 = nullptr) {
     const int D = m->D, H = m->H, HKV = m->HKV, P = m->P;
     const int64_t qrow = (int64_t)m->qw * 4;
     oasr_tensor tq = make_tensor(OASR_TYPE_F32, q, D, nq, H, n, qrow, (int64_t)D * 4, qrow * nq);
@@ -254,6 +254,7 @@ int attend(oasr_qwen *m, const QLayer &L, const float *q, int nq, int n, int nkv
                          (int64_t)nkv_max * nq * 2);
     }
     const float scale = 1.0f / sqrtf((float)D);
+    if (out_q8) return launch_flash_attn_decode_q8(m->be, &tq, &tk, &tv, scale, &to, nkv_dev, *out_q8);
     // prompt passes of at least one 64-row tile: causal flash attention on the tcgen05 tensor cores
     if (mask && nq >= QWEN_TC_MIN_ROWS && nq == nkv_max) return launch_flash_attn_tc(m->be, &tq, &tk, &tv, scale, &to, true);
     return launch_flash_attn_ex(m->be, &tq, &tk, &tv, mask ? &tm : nullptr, scale, &to, nullptr, nkv_dev);
@@ -306,9 +307,9 @@ int run_prefill(oasr_qwen *m, int n, int T) {
 
 // ---- one decode step: token of each of n sequences at device position *pos ----------------
 // 9 launches per layer: RMSNorm+quantize -> q|k|v GEMV -> norms + RoPE + cache
-// write -> attention -> o_proj (quantizes the attention rows itself) -> residual
-// + RMSNorm + quantize -> gate|up GEMV -> SiLU * up + quantize -> down GEMV (its
-// residual is added by the next layer's first kernel).
+// write -> attention (writes its output rows as q8_0 planes) -> o_proj GEMV ->
+// residual + RMSNorm + quantize -> gate|up GEMV -> SiLU * up + quantize -> down GEMV
+// (its residual is added by the next layer's first kernel).
 int run_decode_step(oasr_qwen *m, int n) {
     oasr_backend *be = m->be;
     const int d = m->d, fam = m->family;
@@ -325,15 +326,16 @@ int run_decode_step(oasr_qwen *m, int n) {
         const bool last = l + 1 == m->layers.size();
         Q_TRY(mul_mat_planes(be, L.qkv, qd, n, m->dqkv, m->qw + 2 * m->kvw));
         Q_TRY(launch_qkv_post(m, m->dqkv, n, 1, m->pos, 0, L, m->dq));
-        Q_TRY(attend(m, L, m->dq, 1, n, m->P, nullptr, m->nkv, m->dattn));
-        if (m->fused_o) {
-            Q_TRY(launch_dgemv_quant(be, L.o, m->dattn, n, m->dt, d));
+        if (m->attn_q8) {
+            // the attention writes its output rows as the o_proj's q8_0 input planes
+            Q_TRY(attend(m, L, m->dq, 1, n, m->P, nullptr, m->nkv, m->dattn, &qq));
         } else {
+            Q_TRY(attend(m, L, m->dq, 1, n, m->P, nullptr, m->nkv, m->dattn));
             oasr_tensor at = make_tensor(OASR_TYPE_F32, m->dattn, m->qw, n, 1, 1, (int64_t)m->qw * 4,
                                          (int64_t)m->qw * 4 * n, (int64_t)m->qw * 4 * n);
             Q_TRY(launch_quantize_act(be, &at, fam, qq));
-            Q_TRY(mul_mat_planes(be, L.o, qq, n, m->dt, d));
         }
+        Q_TRY(mul_mat_planes(be, L.o, qq, n, m->dt, d));
         Q_TRY(launch_resid_norm_quant(be, m->dx, m->dt, nullptr, n, d, m->cfg.rms_eps, true, L.ffn_norm, nullptr,
                                       nullptr, &qd, fam));
         Q_TRY(mul_mat_planes(be, L.gu, qd, n, m->dgu, 2 * m->ffn));
@@ -507,9 +509,11 @@ int oasr_b200_qwen_load(oasr_backend *be, const oasr_qwen_config *cfg, const oas
     {
         const char *pdl_env = getenv("OASR_B200_PDL");
         m->pdl = !(pdl_env && strcmp(pdl_env, "0") == 0);
-        m->fused_o = true;
-        for (const QLayer &L : m->layers) m->fused_o = m->fused_o && dgemv_supported(L.o, true);
-        if (m->fused_o) L_TRY(dgemv_configure(be));
+        // q8_0 activations (Q8_0 / Q4_0 weights) and 1, 2 or 4 query heads per kv head: the GQA
+        // decode kernel quantizes the attention rows itself (measured faster than quantizing
+        // them in the o_proj GEMV's prologue, 7.1 us per layer, or in a separate launch)
+        const int G = m->H / m->HKV;
+        m->attn_q8 = m->family == FAMILY_Q8_0 && (G == 1 || G == 2 || G == 4);
     }
     // rotation table: theta_i = p * theta_scale^i accumulated by repeated multiplication
     // (ggml_rope_cache_init), cos / sin from the host's libm like the CPU op
