@@ -23,6 +23,7 @@
 #include <string>
 
 #include "kernels.cuh"
+#include "quant_warp.cuh"
 
 namespace oasr {
 
@@ -46,10 +47,14 @@ struct FaArgs {
     unsigned int *counters;   // one ticket per (kv head, seq, q tile)
     const float *q_bias;      // optional [H*D] added to q before the fp16 rounding
     const int *nkv_dev;       // optional device-side KV length (<= NKV), for graph-captured decode
-    // optional (GQA kernel): the output rows [S][H * D] quantized to q8_0 planes (quants oq,
-    // f16-rounded scales od [S][H * D / 32]) instead of written as f32 -- the next mul_mat's input
+    // optional (GQA and 4-head decode kernels): the output rows [S][H * D] quantized to
+    // activation planes instead of written as f32 -- the next mul_mat's input: quants oq
+    // [S][H * D], scales od ([S][H * D / 32] q8_0, [S][H * D / 256] q8_K) and, for q8_K,
+    // 16-wide sums obs [S][H * D / 16]
     int8_t *oq;
     float *od;
+    int16_t *obs;
+    int oq_family;
 };
 
 // One output element per thread of a full warp, 32 consecutive dims of one head per warp:
@@ -320,6 +325,21 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
     }
 }
 
+// The 4 heads' 256 outputs of a 4-head decode CTA (staged in s_out) are one 256-element
+// chunk of the output row: warp 0 quantizes it into the next mul_mat's activation planes
+// (q8_K: one super-block; q8_0: eight blocks).
+static __device__ void heads_quantize_out(const FaArgs &a, const float *s_out, int s, int hg, int warp, int lane) {
+    __syncthreads();
+    if (warp != 0) return;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = s_out[8 * lane + i];
+    const int64_t K = (int64_t)a.H * 64;
+    int8_t *q = a.oq + s * K + 256 * hg;
+    if (a.oq_family == FAMILY_Q8_K) q8k_chunk(v, q, a.od + s * (K / 256) + hg, a.obs + s * (K / 16) + 16 * hg, lane);
+    else q80_chunk(v, q, a.od + s * (K / 32) + 8 * hg, lane);
+}
+
 // Decode attention with one query per (sequence, head) over f16 K/V whose heads lie
 // contiguously in a KV row (the Whisper decoder's self- and cross-attention caches):
 // a CTA takes 4 heads of one sequence and a range of KV positions, and every warp
@@ -425,6 +445,7 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
     }
 
     // merge the 4 warps (disjoint positions, same heads) through shared memory
+    __shared__ float s_out[4 * D];  // the 4 heads' outputs when they leave as activation planes
     __shared__ float s_m[4][4], s_s[4][4];
     __shared__ float s_acc[4][4][D];
 #pragma unroll
@@ -448,8 +469,9 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
         }
         const int hh = 4 * hg + t;
         if (a.n_splits == 1) {
-            float *out = reinterpret_cast<float *>(a.dst + hh * a.d_nb1 + s * a.d_nb3);
-            out[e] = L == 0.0f ? 0.0f : A / L;
+            const float val = L == 0.0f ? 0.0f : A / L;
+            if (a.oq) s_out[t * D + e] = val;
+            else reinterpret_cast<float *>(a.dst + hh * a.d_nb1 + s * a.d_nb3)[e] = val;
         } else {
             const int64_t row = (int64_t)s * a.H + hh;
             float *pp = a.partials + (row * a.n_splits + split) * (D + 2);
@@ -460,7 +482,10 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
             }
         }
     }
-    if (a.n_splits == 1) return;
+    if (a.n_splits == 1) {
+        if (a.oq) heads_quantize_out(a, s_out, s, hg, warp, lane);
+        return;
+    }
     if (!cta_last_arrival(a.counters + blockIdx.x, (unsigned)a.n_splits)) return;
     // the 4 heads' partials are contiguous ([head][split][D + 2]): stage them in shared
     // memory with every load in flight, then merge in split order
@@ -481,9 +506,11 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
             L += pp[sp * (D + 2) + D + 1] * f;
             A += pp[sp * (D + 2) + e] * f;
         }
-        float *out = reinterpret_cast<float *>(a.dst + (4 * hg + t) * a.d_nb1 + s * a.d_nb3);
-        out[e] = L == 0.0f ? 0.0f : A / L;
+        const float val = L == 0.0f ? 0.0f : A / L;
+        if (a.oq) s_out[t * D + e] = val;
+        else reinterpret_cast<float *>(a.dst + (4 * hg + t) * a.d_nb1 + s * a.d_nb3)[e] = val;
     }
+    if (a.oq) heads_quantize_out(a, s_out, s, hg, warp, lane);
 }
 
 // Decode attention with grouped queries over head-major f16 caches (the Qwen decoder:
@@ -746,7 +773,8 @@ struct FaScratch {
 
 static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
                                    const oasr_tensor *mask, float scale, oasr_tensor *dst, const float *q_bias,
-                                   const int *nkv_dev, const FaScratch *fixed, const ActPlanes *out_q8 = nullptr);
+                                   const int *nkv_dev, const FaScratch *fixed, const ActPlanes *out_q8 = nullptr,
+                                   int out_family = FAMILY_Q8_0);
 
 // resident CTAs per SM of one fattn_split_kernel instantiation (same for every device of this build)
 static int split_kernel_occupancy(int D, int QT, bool f16) {
@@ -788,8 +816,15 @@ int launch_flash_attn_ex(oasr_backend *be, const oasr_tensor *q, const oasr_tens
 }
 
 int launch_flash_attn_decode_q8(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
-                                float scale, oasr_tensor *dst, const int *nkv_dev, const ActPlanes &out_q8) {
-    return launch_flash_attn_split(be, q, k, v, nullptr, scale, dst, nullptr, nkv_dev, nullptr, &out_q8);
+                                float scale, oasr_tensor *dst, const float *q_bias, const int *nkv_dev,
+                                const ActPlanes &out_q8, int family) {
+    return launch_flash_attn_split(be, q, k, v, nullptr, scale, dst, q_bias, nkv_dev, nullptr, &out_q8, family);
+}
+
+bool flash_attn_decode_q8_supported(int H, int HKV, int D, int family) {
+    const int G = HKV > 0 ? H / HKV : 0;
+    if (D == 128) return family == FAMILY_Q8_0 && H % HKV == 0 && (G == 1 || G == 2 || G == 4);
+    return D == 64 && H == HKV && H % 4 == 0;  // the 4-head kernel (one 256-value chunk per CTA)
 }
 
 // ---- allocation-free variant ------------------------------------------------------------
@@ -834,7 +869,8 @@ int launch_flash_attn_static(oasr_backend *be, const oasr_tensor *q, const oasr_
 
 static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
                                    const oasr_tensor *mask, float scale, oasr_tensor *dst, const float *q_bias,
-                                   const int *nkv_dev, const FaScratch *fixed, const ActPlanes *out_q8) {
+                                   const int *nkv_dev, const FaScratch *fixed, const ActPlanes *out_q8,
+                                   int out_family) {
     FaArgs a = {};
     a.q_bias = q_bias;
     a.nkv_dev = nkv_dev;
@@ -876,9 +912,13 @@ static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const
                      ((uintptr_t)k->data & 15) == 0 && ((uintptr_t)v->data & 15) == 0 &&
                      (int64_t)a.S * a.HKV <= 0x7fffffffLL;
     if (out_q8) {
-        if (!gqa) return oasr_internal_fail(be, OASR_STATUS_FAILED, "flash_attn: q8_0 output needs the GQA decode kernel");
+        if (!((gqa && out_family == FAMILY_Q8_0) || (heads && D == 64)))
+            return oasr_internal_fail(be, OASR_STATUS_FAILED,
+                                      "flash_attn: activation-plane output needs the GQA (q8_0) or 4-head decode kernel");
         a.oq = out_q8->qs;
         a.od = out_q8->d;
+        a.obs = out_q8->bs16;
+        a.oq_family = out_family;
     }
     const int64_t groups = heads ? (int64_t)a.S * (a.H / 4) : gqa ? (int64_t)a.S * a.HKV : (int64_t)a.HKV * a.S * a.n_qtiles;
     int n_splits = 1;

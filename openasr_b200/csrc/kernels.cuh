@@ -97,12 +97,15 @@ int launch_flash_attn(oasr_backend *be, const oasr_tensor *q, const oasr_tensor 
 int launch_flash_attn_ex(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
                          const oasr_tensor *mask, float scale, oasr_tensor *dst, const float *q_bias,
                          const int *nkv_dev);
-// Decode attention (one query per head over head-major f16 caches: the GQA kernel) whose
-// output rows [S][H * D] are written as q8_0 planes (FAMILY_Q8_0 layout of act_planes_at
-// for S rows of H * D) -- the input of the next Q8_0 / Q4_0 mul_mat -- instead of f32.
-// Fails if the shapes do not take the GQA kernel.  `dst` describes the output shape only.
+// Decode attention (one query per head) whose output rows [S][H * D] leave as the next
+// mul_mat's activation planes (act_planes_at layout of `family` for S rows of H * D)
+// instead of f32: the GQA kernel (head-major f16 caches, D 128, q8_0) or the 4-head kernel
+// (heads contiguous per KV row, D 64, q8_0 or q8_K).  Fails for shapes that take neither;
+// flash_attn_decode_q8_supported tells in advance.  `dst` describes the output shape only.
 int launch_flash_attn_decode_q8(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
-                                float scale, oasr_tensor *dst, const int *nkv_dev, const ActPlanes &out_q8);
+                                float scale, oasr_tensor *dst, const float *q_bias, const int *nkv_dev,
+                                const ActPlanes &out_q8, int family);
+bool flash_attn_decode_q8_supported(int H, int HKV, int D, int family);
 // allocation-free split-KV attention over file-scope device scratch (fattn.cu)
 constexpr size_t FA_STATIC_PARTIAL_BYTES = (size_t)4 << 20;  // 4 MiB of split partials
 constexpr int64_t FA_STATIC_TICKETS = 1024;                   // split groups (one ticket each)

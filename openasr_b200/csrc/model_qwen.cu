@@ -254,7 +254,7 @@ int attend(oasr_qwen *m, const QLayer &L, const float *q, int nq, int n, int nkv
                          (int64_t)nkv_max * nq * 2);
     }
     const float scale = 1.0f / sqrtf((float)D);
-    if (out_q8) return launch_flash_attn_decode_q8(m->be, &tq, &tk, &tv, scale, &to, nkv_dev, *out_q8);
+    if (out_q8) return launch_flash_attn_decode_q8(m->be, &tq, &tk, &tv, scale, &to, nullptr, nkv_dev, *out_q8, FAMILY_Q8_0);
     // prompt passes of at least one 64-row tile: causal flash attention on the tcgen05 tensor cores
     if (mask && nq >= QWEN_TC_MIN_ROWS && nq == nkv_max) return launch_flash_attn_tc(m->be, &tq, &tk, &tv, scale, &to, true);
     return launch_flash_attn_ex(m->be, &tq, &tk, &tv, mask ? &tm : nullptr, scale, &to, nullptr, nkv_dev);
@@ -512,8 +512,7 @@ int oasr_b200_qwen_load(oasr_backend *be, const oasr_qwen_config *cfg, const oas
         // q8_0 activations (Q8_0 / Q4_0 weights) and 1, 2 or 4 query heads per kv head: the GQA
         // decode kernel quantizes the attention rows itself (measured faster than quantizing
         // them in the o_proj GEMV's prologue, 7.1 us per layer, or in a separate launch)
-        const int G = m->H / m->HKV;
-        m->attn_q8 = m->family == FAMILY_Q8_0 && (G == 1 || G == 2 || G == 4);
+        m->attn_q8 = flash_attn_decode_q8_supported(m->H, m->HKV, m->D, m->family);
     }
     // rotation table: theta_i = p * theta_scale^i accumulated by repeated multiplication
     // (ggml_rope_cache_init), cos / sin from the host's libm like the CPU op

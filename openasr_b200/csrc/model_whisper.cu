@@ -73,6 +73,7 @@ struct oasr_whisper {
     // decoder activations, B rows
     float *dx, *dqkv, *dq, *dattn, *dt, *df, *logits;
     bool fused_dec;  // decoder GEMVs run as dgemv (prologue/epilogue fused), see run_decode_step
+    bool attn_planes;  // the fused step's attentions emit the out-projections' activation planes
     bool pdl;        // programmatic dependent launch inside the step graph (OASR_B200_PDL=0 turns it off)
     void *dqa_d, *dqa_f, *dqa_lm;
     int *tokens, *pos, *nkv, *history;
@@ -246,10 +247,12 @@ int run_encoder(oasr_whisper *m, int n) {
 
 // ---- one decoder step for n sequences at device position *pos -------------------------------
 // The decoder step with fused GEMVs (dgemv.cu): 12 launches per layer.
-//   LN1 planes -> qkv (q, self-K/V row out) -> self-attention -> out-proj (quantizes
-//   the attention rows itself) -> residual + LN -> cross-q -> cross-attention (+b_cq)
-//   -> cross-out (same) -> residual + LN -> fc1 -> GELU + quantize -> fc2 ->
-//   residual + next LN1 (after the last layer: the final LN into the head's q8_0 planes).
+//   LN1 planes -> qkv (q, self-K/V row out) -> self-attention (writes its output as the
+//   out-projection's activation planes; with heads not a multiple of 4 the out-projection
+//   quantizes them in its prologue instead) -> out-proj -> residual + LN -> cross-q ->
+//   cross-attention (+b_cq, same output planes) -> cross-out -> residual + LN -> fc1 ->
+//   GELU + quantize -> fc2 -> residual + next LN1 (after the last layer: the final LN
+//   into the head's q8_0 planes).
 static int run_decode_step_fused(oasr_whisper *m, int n) {
     oasr_backend *be = m->be;
     const int d = m->d, H = m->H, T = m->T_enc, P = m->cfg.n_text_ctx;
@@ -270,9 +273,11 @@ static int run_decode_step_fused(oasr_whisper *m, int n) {
             oasr_tensor k = make_tensor(OASR_TYPE_F16, L.self_k, 64, P, H, n, (int64_t)d * 2, 128, (int64_t)P * d * 2);
             oasr_tensor v = make_tensor(OASR_TYPE_F16, L.self_v, 64, P, H, n, (int64_t)d * 2, 128, (int64_t)P * d * 2);
             oasr_tensor o = make_tensor(OASR_TYPE_F32, m->dattn, 64, H, 1, n, 256, (int64_t)d * 4, (int64_t)d * 4);
-            W_TRY(launch_flash_attn_ex(be, &q, &k, &v, nullptr, scale, &o, nullptr, m->nkv));
+            if (m->attn_planes) W_TRY(launch_flash_attn_decode_q8(be, &q, &k, &v, scale, &o, nullptr, m->nkv, qd, df));
+            else W_TRY(launch_flash_attn_ex(be, &q, &k, &v, nullptr, scale, &o, nullptr, m->nkv));
         }
-        W_TRY(launch_dgemv_quant(be, L.o, m->dattn, n, m->dt, d));
+        if (m->attn_planes) W_TRY(mul_mat_planes(be, L.o, qd, n, m->dt, d));
+        else W_TRY(launch_dgemv_quant(be, L.o, m->dattn, n, m->dt, d));
         W_TRY(launch_resid_norm_quant(be, m->dx, m->dt, L.b_o, n, d, LN_EPS, false, L.lnc_g, L.lnc_b, nullptr, &qd, df));
         W_TRY(mul_mat_planes(be, L.cq, qd, n, m->dq, d));
         {
@@ -280,9 +285,11 @@ static int run_decode_step_fused(oasr_whisper *m, int n) {
             oasr_tensor k = make_tensor(OASR_TYPE_F16, L.cross_kv, 64, T, H, n, (int64_t)d * 4, 128, (int64_t)T * d * 4);
             oasr_tensor v = make_tensor(OASR_TYPE_F16, L.cross_kv + d, 64, T, H, n, (int64_t)d * 4, 128, (int64_t)T * d * 4);
             oasr_tensor o = make_tensor(OASR_TYPE_F32, m->dattn, 64, H, 1, n, 256, (int64_t)d * 4, (int64_t)d * 4);
-            W_TRY(launch_flash_attn_ex(be, &q, &k, &v, nullptr, scale, &o, L.b_cq, nullptr));
+            if (m->attn_planes) W_TRY(launch_flash_attn_decode_q8(be, &q, &k, &v, scale, &o, L.b_cq, nullptr, qd, df));
+            else W_TRY(launch_flash_attn_ex(be, &q, &k, &v, nullptr, scale, &o, L.b_cq, nullptr));
         }
-        W_TRY(launch_dgemv_quant(be, L.co, m->dattn, n, m->dt, d));
+        if (m->attn_planes) W_TRY(mul_mat_planes(be, L.co, qd, n, m->dt, d));
+        else W_TRY(launch_dgemv_quant(be, L.co, m->dattn, n, m->dt, d));
         W_TRY(launch_resid_norm_quant(be, m->dx, m->dt, L.b_co, n, d, LN_EPS, false, L.ln2_g, L.ln2_b, nullptr, &qd, df));
         W_TRY(mul_mat_planes(be, L.fc1, qd, n, m->df, m->ffn));
         W_TRY(launch_bias_gelu_quant(be, m->df, L.b_fc1, n, m->ffn, nullptr, &qf, df));
@@ -565,6 +572,10 @@ int oasr_b200_whisper_load(oasr_backend *be, const oasr_whisper_config *cfg, con
                            dgemv_supported(L.cq, false) && dgemv_supported(L.co, true) &&
                            dgemv_supported(L.fc1, false) && dgemv_supported(L.fc2, false);
         if (m->fused_dec) L_TRY(dgemv_configure(be));
+        // the 4-head decode attention (heads a multiple of 4) quantizes its 256-value output
+        // chunks itself, so the out-projections run as plain GEMVs (measured faster than
+        // quantizing the attention rows in every GEMV CTA's prologue)
+        m->attn_planes = m->fused_dec && flash_attn_decode_q8_supported(m->H, m->H, 64, m->dec_family);
     }
     // frontend tables (host-computed like the reference's plan, whisper/mel.rs:64-96)
     {
