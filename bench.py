@@ -565,9 +565,10 @@ def run_b200(args) -> None:
         dist.destroy_process_group()
 
 
-def ncu_traffic_fa() -> float | None:
-    """dram read + write bytes of one cross-attention launch, from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "fattn_heads_cross_b8.md")
+def ncu_traffic_fa(summary: str = "fattn_heads_cross_b8.md") -> float | None:
+    """dram read + write bytes of one attention launch, from a committed ncu summary
+    (the cross-attention's by default)."""
+    p = os.path.join(ROOT, "profiles", summary)
     try:
         for line in open(p):
             if line.startswith("| dram_bytes_per_launch |"):
@@ -901,7 +902,11 @@ def run_b200_qwen(args) -> None:
             "roofline": {"bound": "hbm", "kernel": f"fattn_gqa_kernel<2> (GQA decode attention, {B} x 8 kv "
                                                    f"heads x {fa['n_kv']} f16 K/V positions)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes": fa["bytes"],
+                         "peak_kind": peak_kind,
+                         # the committed capture is of this exact shape (8 sequences, 518 positions)
+                         "traffic": ncu_traffic_fa("fattn_gqa_decode_qwen_b8.md")
+                         if (B, fa["n_kv"]) == (8, 518) else None,
+                         "algorithmic_bytes": fa["bytes"],
                          "avg_launch_us": fa["us"], "how": "same kernel and shapes through flash_attn_ext, timed alone "
                                                            "on the bench stream from a CUDA graph of 40 launches, "
                                                            "caches rotated over 8 layers"},
