@@ -55,6 +55,12 @@ struct FaArgs {
     float *od;
     int16_t *obs;
     int oq_family;
+    // 4-head kernel, K/V rows that no launch this one can overlap under programmatic
+    // dependent launch writes are loaded before the wait on the predecessor:
+    // KV_STATIC_ALL every row (the cross-attention's encoder K/V); KV_STATIC_OLD every
+    // row but the newest live one (self-attention: the predecessor writes row *nkv_dev - 1;
+    // *nkv_dev itself must not be written by an overlapping launch)
+    int kv_static;
 };
 
 // One output element per thread of a full warp, 32 consecutive dims of one head per warp:
@@ -359,28 +365,19 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
     const int h = 4 * hg + hl;
     const char *kb = a.k + h * a.k_nb2 + s * a.k_nb3 + sl * 16;
     const char *vb = a.v + h * a.v_nb2 + s * a.v_nb3 + sl * 16;
-    griddep_wait();
 
     float qv[8];
-    {
-        const float *qp = reinterpret_cast<const float *>(a.q + h * a.q_nb2 + s * a.q_nb3) + sl * 8;
-        const float *qb = a.q_bias ? a.q_bias + h * D + sl * 8 : nullptr;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            float x = qp[e];
-            if (qb) x = __fadd_rn(x, qb[e]);
-            qv[e] = __half2float(__float2half_rn(x));
-        }
-    }
     float mx = -INFINITY, sm = 0.0f, acc[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
-
     // with a device-side KV length the splits share the live positions evenly
-    const int nkv = a.nkv_dev ? min(*a.nkv_dev, a.NKV) : a.NKV;
-    const int per = a.nkv_dev ? (nkv + a.n_splits - 1) / a.n_splits : a.kv_per_split;
-    const int kv0 = split * per;
-    const int kv1 = min(nkv, kv0 + per);
+    int kv0 = 0, kv1 = 0;
+    auto range = [&]() {
+        const int nkv = a.nkv_dev ? min(*a.nkv_dev, a.NKV) : a.NKV;
+        const int per = a.nkv_dev ? (nkv + a.n_splits - 1) / a.n_splits : a.kv_per_split;
+        kv0 = split * per;
+        kv1 = min(nkv, kv0 + per);
+    };
     // register double buffering: the loads of the next U positions are in flight while
     // the current U are consumed
     auto load = [&](int pb, int4 (&kr)[U], int4 (&vr)[U]) {
@@ -429,12 +426,42 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
         }
         mx = mnew;
     };
+
     int4 kA[U], vA[U], kB[U], vB[U];
+    bool a_loaded = false, b_loaded = false;  // the first / second batch is already in flight
+    const bool early = a.kv_static != KV_STATIC_NONE;
+    if (early) {
+        range();
+        // rows below `lim` are final before the predecessor runs
+        const int lim = a.kv_static == KV_STATIC_ALL ? kv1 : min(kv1, (a.nkv_dev ? *a.nkv_dev : a.NKV) - 1);
+        const int p0 = kv0 + warp, p1 = p0 + 4 * U;
+        if (p0 < kv1 && min(p0 + 4 * (U - 1), kv1 - 1) < lim) {
+            load(p0, kA, vA);
+            a_loaded = true;
+            if (p1 < kv1 && min(p1 + 4 * (U - 1), kv1 - 1) < lim) {
+                load(p1, kB, vB);
+                b_loaded = true;
+            }
+        }
+    }
+    griddep_wait();
+    {
+        const float *qp = reinterpret_cast<const float *>(a.q + h * a.q_nb2 + s * a.q_nb3) + sl * 8;
+        const float *qb = a.q_bias ? a.q_bias + h * D + sl * 8 : nullptr;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            float x = qp[e];
+            if (qb) x = __fadd_rn(x, qb[e]);
+            qv[e] = __half2float(__float2half_rn(x));
+        }
+    }
+    if (!early) range();
     int pb = kv0 + warp;
-    if (pb < kv1) load(pb, kA, vA);
+    if (!a_loaded && pb < kv1) load(pb, kA, vA);
     while (pb < kv1) {
         int pn = pb + 4 * U;
-        if (pn < kv1) load(pn, kB, vB);
+        if (pn < kv1 && !b_loaded) load(pn, kB, vB);
+        b_loaded = false;
         consume(pb, kA, vA);
         pb = pn;
         if (pb >= kv1) break;
@@ -774,7 +801,7 @@ struct FaScratch {
 static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
                                    const oasr_tensor *mask, float scale, oasr_tensor *dst, const float *q_bias,
                                    const int *nkv_dev, const FaScratch *fixed, const ActPlanes *out_q8 = nullptr,
-                                   int out_family = FAMILY_Q8_0);
+                                   int out_family = FAMILY_Q8_0, int kv_static = 0);
 
 // resident CTAs per SM of one fattn_split_kernel instantiation (same for every device of this build)
 static int split_kernel_occupancy(int D, int QT, bool f16) {
@@ -817,8 +844,9 @@ int launch_flash_attn_ex(oasr_backend *be, const oasr_tensor *q, const oasr_tens
 
 int launch_flash_attn_decode_q8(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
                                 float scale, oasr_tensor *dst, const float *q_bias, const int *nkv_dev,
-                                const ActPlanes &out_q8, int family) {
-    return launch_flash_attn_split(be, q, k, v, nullptr, scale, dst, q_bias, nkv_dev, nullptr, &out_q8, family);
+                                const ActPlanes &out_q8, int family, int kv_static) {
+    return launch_flash_attn_split(be, q, k, v, nullptr, scale, dst, q_bias, nkv_dev, nullptr, &out_q8, family,
+                                   kv_static);
 }
 
 bool flash_attn_decode_q8_supported(int H, int HKV, int D, int family) {
@@ -870,7 +898,7 @@ int launch_flash_attn_static(oasr_backend *be, const oasr_tensor *q, const oasr_
 static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
                                    const oasr_tensor *mask, float scale, oasr_tensor *dst, const float *q_bias,
                                    const int *nkv_dev, const FaScratch *fixed, const ActPlanes *out_q8,
-                                   int out_family) {
+                                   int out_family, int kv_static) {
     FaArgs a = {};
     a.q_bias = q_bias;
     a.nkv_dev = nkv_dev;
@@ -911,6 +939,7 @@ static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const
                      q->nb[2] % 16 == 0 && q->nb[3] % 16 == 0 && ((uintptr_t)q->data & 15) == 0 &&
                      ((uintptr_t)k->data & 15) == 0 && ((uintptr_t)v->data & 15) == 0 &&
                      (int64_t)a.S * a.HKV <= 0x7fffffffLL;
+    if (heads) a.kv_static = kv_static;
     if (out_q8) {
         if (!((gqa && out_family == FAMILY_Q8_0) || (heads && D == 64)))
             return oasr_internal_fail(be, OASR_STATUS_FAILED,

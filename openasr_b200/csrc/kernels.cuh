@@ -102,9 +102,14 @@ int launch_flash_attn_ex(oasr_backend *be, const oasr_tensor *q, const oasr_tens
 // instead of f32: the GQA kernel (head-major f16 caches, D 128, q8_0) or the 4-head kernel
 // (heads contiguous per KV row, D 64, q8_0 or q8_K).  Fails for shapes that take neither;
 // flash_attn_decode_q8_supported tells in advance.  `dst` describes the output shape only.
+// kv_static (4-head kernel only): which K/V rows no launch this one can overlap under
+// programmatic dependent launch writes, so that its first loads go before the wait on
+// the predecessor: none, all, or all but the newest live row (*nkv_dev - 1, which the
+// predecessor writes; *nkv_dev itself is then final before the launch).
+enum : int { KV_STATIC_NONE = 0, KV_STATIC_ALL = 1, KV_STATIC_OLD = 2 };
 int launch_flash_attn_decode_q8(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
                                 float scale, oasr_tensor *dst, const float *q_bias, const int *nkv_dev,
-                                const ActPlanes &out_q8, int family);
+                                const ActPlanes &out_q8, int family, int kv_static = 0);
 bool flash_attn_decode_q8_supported(int H, int HKV, int D, int family);
 // allocation-free split-KV attention over file-scope device scratch (fattn.cu)
 constexpr size_t FA_STATIC_PARTIAL_BYTES = (size_t)4 << 20;  // 4 MiB of split partials

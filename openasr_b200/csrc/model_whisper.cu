@@ -253,6 +253,10 @@ int run_encoder(oasr_whisper *m, int n) {
 //   cross-attention (+b_cq, same output planes) -> cross-out -> residual + LN -> fc1 ->
 //   GELU + quantize -> fc2 -> residual + next LN1 (after the last layer: the final LN
 //   into the head's q8_0 planes).
+// Both attentions issue their first K/V loads before waiting on their predecessor: the
+// cross K/V were written before the step graph started, and of the self K/V only the
+// newest row (*nkv - 1) comes from the qkv GEMV in front; *nkv itself only changes in the
+// position advance that closes the step (or in a host copy between steps).
 static int run_decode_step_fused(oasr_whisper *m, int n) {
     oasr_backend *be = m->be;
     const int d = m->d, H = m->H, T = m->T_enc, P = m->cfg.n_text_ctx;
@@ -273,7 +277,8 @@ static int run_decode_step_fused(oasr_whisper *m, int n) {
             oasr_tensor k = make_tensor(OASR_TYPE_F16, L.self_k, 64, P, H, n, (int64_t)d * 2, 128, (int64_t)P * d * 2);
             oasr_tensor v = make_tensor(OASR_TYPE_F16, L.self_v, 64, P, H, n, (int64_t)d * 2, 128, (int64_t)P * d * 2);
             oasr_tensor o = make_tensor(OASR_TYPE_F32, m->dattn, 64, H, 1, n, 256, (int64_t)d * 4, (int64_t)d * 4);
-            if (m->attn_planes) W_TRY(launch_flash_attn_decode_q8(be, &q, &k, &v, scale, &o, nullptr, m->nkv, qd, df));
+            if (m->attn_planes)
+                W_TRY(launch_flash_attn_decode_q8(be, &q, &k, &v, scale, &o, nullptr, m->nkv, qd, df, KV_STATIC_OLD));
             else W_TRY(launch_flash_attn_ex(be, &q, &k, &v, nullptr, scale, &o, nullptr, m->nkv));
         }
         if (m->attn_planes) W_TRY(mul_mat_planes(be, L.o, qd, n, m->dt, d));
@@ -285,7 +290,8 @@ static int run_decode_step_fused(oasr_whisper *m, int n) {
             oasr_tensor k = make_tensor(OASR_TYPE_F16, L.cross_kv, 64, T, H, n, (int64_t)d * 4, 128, (int64_t)T * d * 4);
             oasr_tensor v = make_tensor(OASR_TYPE_F16, L.cross_kv + d, 64, T, H, n, (int64_t)d * 4, 128, (int64_t)T * d * 4);
             oasr_tensor o = make_tensor(OASR_TYPE_F32, m->dattn, 64, H, 1, n, 256, (int64_t)d * 4, (int64_t)d * 4);
-            if (m->attn_planes) W_TRY(launch_flash_attn_decode_q8(be, &q, &k, &v, scale, &o, L.b_cq, nullptr, qd, df));
+            if (m->attn_planes)
+                W_TRY(launch_flash_attn_decode_q8(be, &q, &k, &v, scale, &o, L.b_cq, nullptr, qd, df, KV_STATIC_ALL));
             else W_TRY(launch_flash_attn_ex(be, &q, &k, &v, nullptr, scale, &o, L.b_cq, nullptr));
         }
         if (m->attn_planes) W_TRY(mul_mat_planes(be, L.co, qd, n, m->dt, d));
