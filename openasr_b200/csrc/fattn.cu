@@ -46,7 +46,9 @@ struct FaArgs {
     float *partials;          // [rows][n_splits][D + 2]
     unsigned int *counters;   // one ticket per (kv head, seq, q tile)
     const float *q_bias;      // optional [H*D] added to q before the fp16 rounding
-    const int *nkv_dev;       // optional device-side KV length (<= NKV), for graph-captured decode
+    const int *nkv_dev;       // optional device-side KV length (<= NKV), for graph-captured decode; the
+                              // decode kernels may read it before their PDL wait, so no launch they can
+                              // overlap writes it (the model drivers advance it between steps)
     // optional (GQA and 4-head decode kernels): the output rows [S][H * D] quantized to
     // activation planes instead of written as f32 -- the next mul_mat's input: quants oq
     // [S][H * D], scales od ([S][H * D / 32] q8_0, [S][H * D / 256] q8_K) and, for q8_K,
@@ -55,7 +57,7 @@ struct FaArgs {
     float *od;
     int16_t *obs;
     int oq_family;
-    // 4-head kernel, K/V rows that no launch this one can overlap under programmatic
+    // 4-head and GQA kernels, K/V rows that no launch this one can overlap under programmatic
     // dependent launch writes are loaded before the wait on the predecessor:
     // KV_STATIC_ALL every row (the cross-attention's encoder K/V); KV_STATIC_OLD every
     // row but the newest live one (self-attention: the predecessor writes row *nkv_dev - 1;
@@ -568,21 +570,8 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
             prefetch_l2_bulk(a.v + hk * a.v_nb2 + s * a.v_nb3 + (int64_t)p0 * a.v_nb1, (uint32_t)((p1 - p0) * a.v_nb1));
         }
     }
-    griddep_wait();
 
     float qv[G][16];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-        const float *qp = reinterpret_cast<const float *>(a.q + (hk * G + g) * a.q_nb2 + s * a.q_nb3) + sl * 16;
-#pragma unroll
-        for (int e = 0; e < 16; e += 4) {
-            const float4 x = *reinterpret_cast<const float4 *>(qp + e);
-            qv[g][e] = __half2float(__float2half_rn(x.x));
-            qv[g][e + 1] = __half2float(__float2half_rn(x.y));
-            qv[g][e + 2] = __half2float(__float2half_rn(x.z));
-            qv[g][e + 3] = __half2float(__float2half_rn(x.w));
-        }
-    }
     float mx[G], sm[G], acc[G][16];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -592,6 +581,7 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
         for (int e = 0; e < 16; ++e) acc[g][e] = 0.0f;
     }
 
+    // the KV length is final before the launch (set between steps)
     const int nkv = a.nkv_dev ? min(*a.nkv_dev, a.NKV) : a.NKV;
     const int per = a.nkv_dev ? (nkv + a.n_splits - 1) / a.n_splits : a.kv_per_split;
     const int kv0 = split * per;
@@ -665,11 +655,40 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
     // warp-uniform loop bounds: every lane runs the same iterations (the shuffles need
     // all 32); positions past kv1 carry weight 0
     const int wbase = kv0 + 4 * warp;  // the warp's first position of a batch (group 0)
+    // rows that no overlapping launch writes: the warp's first two batches load before the
+    // wait on the predecessor when every live row of the batch is below `lim`
+    bool a_loaded = false, b_loaded = false;
+    if (a.kv_static != KV_STATIC_NONE) {
+        const int lim = a.kv_static == KV_STATIC_ALL ? kv1 : min(kv1, nkv - 1);
+        auto batch_static = [&](int p) { return p < kv1 && min(p + 3 + 16 * (U - 1), kv1 - 1) < lim; };
+        if (batch_static(wbase)) {
+            load(wbase + grp, kA, vA);
+            a_loaded = true;
+            if (batch_static(wbase + STEP)) {
+                load(wbase + STEP + grp, kB, vB);
+                b_loaded = true;
+            }
+        }
+    }
+    griddep_wait();
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const float *qp = reinterpret_cast<const float *>(a.q + (hk * G + g) * a.q_nb2 + s * a.q_nb3) + sl * 16;
+#pragma unroll
+        for (int e = 0; e < 16; e += 4) {
+            const float4 x = *reinterpret_cast<const float4 *>(qp + e);
+            qv[g][e] = __half2float(__float2half_rn(x.x));
+            qv[g][e + 1] = __half2float(__float2half_rn(x.y));
+            qv[g][e + 2] = __half2float(__float2half_rn(x.z));
+            qv[g][e + 3] = __half2float(__float2half_rn(x.w));
+        }
+    }
     int pb = wbase;
-    if (pb < kv1) load(pb + grp, kA, vA);
+    if (!a_loaded && pb < kv1) load(pb + grp, kA, vA);
     while (pb < kv1) {
         int pn = pb + STEP;
-        if (pn < kv1) load(pn + grp, kB, vB);
+        if (pn < kv1 && !b_loaded) load(pn + grp, kB, vB);
+        b_loaded = false;
         consume(pb + grp, kA, vA);
         pb = pn;
         if (pb >= kv1) break;
@@ -939,7 +958,7 @@ static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const
                      q->nb[2] % 16 == 0 && q->nb[3] % 16 == 0 && ((uintptr_t)q->data & 15) == 0 &&
                      ((uintptr_t)k->data & 15) == 0 && ((uintptr_t)v->data & 15) == 0 &&
                      (int64_t)a.S * a.HKV <= 0x7fffffffLL;
-    if (heads) a.kv_static = kv_static;
+    if (heads || gqa) a.kv_static = kv_static;
     if (out_q8) {
         if (!((gqa && out_family == FAMILY_Q8_0) || (heads && D == 64)))
             return oasr_internal_fail(be, OASR_STATUS_FAILED,

@@ -254,7 +254,11 @@ int attend(oasr_qwen *m, const QLayer &L, const float *q, int nq, int n, int nkv
                          (int64_t)nkv_max * nq * 2);
     }
     const float scale = 1.0f / sqrtf((float)D);
-    if (out_q8) return launch_flash_attn_decode_q8(m->be, &tq, &tk, &tv, scale, &to, nullptr, nkv_dev, *out_q8, FAMILY_Q8_0);
+    // decode: the rows below *nkv_dev - 1 were written by earlier steps, so the attention loads
+    // them before waiting on qkv_post (which writes the newest row)
+    if (out_q8)
+        return launch_flash_attn_decode_q8(m->be, &tq, &tk, &tv, scale, &to, nullptr, nkv_dev, *out_q8, FAMILY_Q8_0,
+                                           KV_STATIC_OLD);
     // prompt passes of at least one 64-row tile: causal flash attention on the tcgen05 tensor cores
     if (mask && nq >= QWEN_TC_MIN_ROWS && nq == nkv_max) return launch_flash_attn_tc(m->be, &tq, &tk, &tv, scale, &to, true);
     return launch_flash_attn_ex(m->be, &tq, &tk, &tv, mask ? &tm : nullptr, scale, &to, nullptr, nkv_dev);
