@@ -395,7 +395,12 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
         }
     };
     // the U scores are independent: compute them all, then fold the block into the
-    // running softmax state with one rescale (a block-wise online softmax)
+    // running softmax state with one rescale (a block-wise online softmax).  With U = 8
+    // the 8 lanes of a head finish the 8 dot products as a transpose-reduce: at each
+    // butterfly level a lane keeps half of its partial sums and adds the partner's half,
+    // so lane sl ends with the whole dot of position sl (the same pairs added in the same
+    // order as a per-position butterfly: bit-identical scores), takes one exp instead of
+    // 8, and the weights are gathered back by shuffles.
     auto consume = [&](int pb, const int4 (&kr)[U], const int4 (&vr)[U]) {
         float sc[U];
 #pragma unroll
@@ -405,26 +410,59 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
             float d = 0.0f;
 #pragma unroll
             for (int e = 0; e < 8; ++e) d = fmaf(qv[e], kf[e], d);
-#pragma unroll
-            for (int o = 4; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-            sc[u] = pb + 4 * u < kv1 ? d * a.scale : -INFINITY;
+            sc[u] = d;
         }
-        float mb = sc[0];
+        float wv[U];
+        float mnew;
+        if constexpr (U == 8) {
+            const bool b4 = sl & 4, b2 = sl & 2, b1 = sl & 1;
+            float r4[4], r2[2];
 #pragma unroll
-        for (int u = 1; u < U; ++u) mb = fmaxf(mb, sc[u]);
-        const float mnew = fmaxf(mx, mb);    // finite: position pb is valid
+            for (int j = 0; j < 4; ++j) {
+                const float keep = b4 ? sc[j + 4] : sc[j], send = b4 ? sc[j] : sc[j + 4];
+                r4[j] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+            }
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const float keep = b2 ? r4[j + 2] : r4[j], send = b2 ? r4[j] : r4[j + 2];
+                r2[j] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+            }
+            const float keep = b1 ? r2[1] : r2[0], send = b1 ? r2[0] : r2[1];
+            const float dot = keep + __shfl_xor_sync(0xffffffffu, send, 1);  // position pb + 4 sl
+            const float s1 = pb + 4 * sl < kv1 ? dot * a.scale : -INFINITY;
+            float mb = s1;
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+            mnew = fmaxf(mx, mb);                    // finite: position pb is valid
+            const float w1 = expf(s1 - mnew);        // invalid positions: exp(-inf) = 0
+#pragma unroll
+            for (int u = 0; u < U; ++u) wv[u] = __shfl_sync(0xffffffffu, w1, (lane & ~7) | u);
+        } else {
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                float d = sc[u];
+#pragma unroll
+                for (int o = 4; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                sc[u] = pb + 4 * u < kv1 ? d * a.scale : -INFINITY;
+            }
+            float mb = sc[0];
+#pragma unroll
+            for (int u = 1; u < U; ++u) mb = fmaxf(mb, sc[u]);
+            mnew = fmaxf(mx, mb);
+#pragma unroll
+            for (int u = 0; u < U; ++u) wv[u] = expf(sc[u] - mnew);
+        }
         const float corr = expf(mx - mnew);  // mx = -inf -> 0
         sm *= corr;
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[e] *= corr;
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            const float w = expf(sc[u] - mnew);  // invalid positions: exp(-inf) = 0
             float vf[8];
             load8<true>(reinterpret_cast<const char *>(&vr[u]), vf);
-            sm += w;
+            sm += wv[u];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) acc[e] = fmaf(w, vf[e], acc[e]);
+            for (int e = 0; e < 8; ++e) acc[e] = fmaf(wv[u], vf[e], acc[e]);
         }
         mx = mnew;
     };
