@@ -55,28 +55,80 @@ struct FaTc {
     static_assert(D == 64 || D == 128, "head_dim 64 or 128");
 };
 
-// ---- pre-pass: q,k -> fp16 rows [S*H][n][64]; v -> fp16 [S*Hkv][64][n_pad] -------------
-template <bool F16IN>
-__global__ void fa_prep_kernel(const char *src, int64_t nb1, int64_t nb2, int64_t nb3, int n, int H, int S, int D,
-                               __half *dst, bool transpose, int n_pad) {
-    const int64_t total = (int64_t)S * H * n * D;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int d = (int)(i % D);
-        const int64_t r = i / D;
-        const int p = (int)(r % n);
-        const int64_t hs = r / n;
-        const int h = (int)(hs % H), s = (int)(hs / H);
-        const char *e = src + p * nb1 + h * nb2 + s * nb3;
-        const float v = F16IN ? __half2float(reinterpret_cast<const __half *>(e)[d]) : reinterpret_cast<const float *>(e)[d];
-        if (transpose) dst[(hs * D + d) * n_pad + p] = __float2half_rn(v);
-        else dst[i] = __float2half_rn(v);
+// ---- pre-pass: q, k -> fp16 rows [S*H][n][D]; v -> fp16 [S*Hkv][D][n_pad] ------------
+// CTA = 64 positions of one row block hs =
+// s * H + h; each thread moves 16-byte chunks (4 f32 or 8 f16 values).  Rows go out as
+// f16 [hs][n][D]; with TR they are transposed through shared memory into
+// [hs][D][n_pad] (128-byte row pieces per store) and positions n..n_pad-1 are written
+// as zeros.  Values round to fp16 with round-to-nearest-even (f16 inputs pass unchanged).
+template <bool F16IN, int D, bool TR>
+__global__ void __launch_bounds__(256) fa_prep_tile_kernel(const char *src, int64_t nb1, int64_t nb2, int64_t nb3, int n,
+                                                           int H, __half *dst, int n_pad) {
+    constexpr int TP = 64;               // positions per tile
+    constexpr int EPC = F16IN ? 8 : 4;   // values per 16-byte chunk
+    constexpr int CPR = D / EPC;         // chunks per row
+    constexpr int LD = TP + 8;           // shared row pitch in halves (144 bytes: 16-byte aligned)
+    __shared__ __align__(16) __half tile[TR ? D : 1][LD];
+    const int p0 = blockIdx.x * TP;
+    const int hs = blockIdx.y;
+    const int h = hs % H, s = hs / H;
+    const char *base = src + (int64_t)h * nb2 + (int64_t)s * nb3;
+    for (int c = threadIdx.x; c < TP * CPR; c += 256) {
+        const int pr = c / CPR, ch = c % CPR;
+        const int p = p0 + pr;
+        uint4 raw = make_uint4(0, 0, 0, 0);
+        if (p < n) raw = *reinterpret_cast<const uint4 *>(base + (int64_t)p * nb1 + ch * 16);
+        if (F16IN) {
+            if (TR) {
+                const __half *hv = reinterpret_cast<const __half *>(&raw);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) tile[ch * 8 + j][pr] = hv[j];
+            } else if (p < n) {
+                *reinterpret_cast<uint4 *>(dst + ((int64_t)hs * n + p) * D + ch * 8) = raw;
+            }
+        } else {
+            const float *fv = reinterpret_cast<const float *>(&raw);
+            const __half2 h01 = __halves2half2(__float2half_rn(fv[0]), __float2half_rn(fv[1]));
+            const __half2 h23 = __halves2half2(__float2half_rn(fv[2]), __float2half_rn(fv[3]));
+            if (TR) {
+                tile[ch * 4 + 0][pr] = __low2half(h01);
+                tile[ch * 4 + 1][pr] = __high2half(h01);
+                tile[ch * 4 + 2][pr] = __low2half(h23);
+                tile[ch * 4 + 3][pr] = __high2half(h23);
+            } else if (p < n) {
+                uint2 pk;
+                pk.x = *reinterpret_cast<const uint32_t *>(&h01);
+                pk.y = *reinterpret_cast<const uint32_t *>(&h23);
+                *reinterpret_cast<uint2 *>(dst + ((int64_t)hs * n + p) * D + ch * 4) = pk;
+            }
+        }
+    }
+    if (TR) {
+        __syncthreads();
+        for (int c = threadIdx.x; c < D * (TP / 8); c += 256) {
+            const int d = c / (TP / 8), pc = c % (TP / 8);
+            const int p = p0 + pc * 8;
+            if (p >= n_pad) continue;  // n_pad is a multiple of 8: chunks are wholly in or out
+            *reinterpret_cast<uint4 *>(dst + ((int64_t)hs * D + d) * n_pad + p) =
+                *reinterpret_cast<const uint4 *>(&tile[d][pc * 8]);
+        }
     }
 }
 
-__global__ void fa_zero_pad_kernel(__half *vt, int64_t rows, int n, int n_pad) {
-    const int w = n_pad - n;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * w; i += (int64_t)gridDim.x * blockDim.x)
-        vt[(i / w) * n_pad + n + (i % w)] = __float2half_rn(0.0f);
+// one pre-pass operand through the tiled kernel (D 64 or 128; data and byte strides
+// multiples of 16; S * H <= 65535)
+template <bool F16IN>
+static void fa_prep_tiled(oasr_backend *be, const oasr_tensor *t, int n, int H, int S, int D, __half *dst, bool tr,
+                          int n_pad) {
+    const int rows = tr ? n_pad : n;
+    const dim3 grid((unsigned)((rows + 63) / 64), (unsigned)(S * H));
+    const char *src = (const char *)t->data;
+#define FA_PREP_TILE(DD, TRV)                                                                                       \
+    fa_prep_tile_kernel<F16IN, DD, TRV><<<grid, 256, 0, be->stream>>>(src, t->nb[1], t->nb[2], t->nb[3], n, H, dst, \
+                                                                      n_pad)
+    if (D == 64) { if (tr) FA_PREP_TILE(64, true); else FA_PREP_TILE(64, false); }
+    else { if (tr) FA_PREP_TILE(128, true); else FA_PREP_TILE(128, false); }
+#undef FA_PREP_TILE
 }
 
 template <int D, bool CAUSAL>
@@ -351,21 +403,23 @@ int launch_flash_attn_tc(oasr_backend *be, const oasr_tensor *q, const oasr_tens
     if (st) return st;
     __half *q16 = (__half *)scr, *k16 = (__half *)(scr + q_bytes), *vt16 = (__half *)(scr + q_bytes + k_bytes);
     const bool f16k = k->type == OASR_TYPE_F16;
-    const int blocks = be->sm_count * 8;
-    fa_prep_kernel<false><<<blocks, 256, 0, be->stream>>>((const char *)q->data, q->nb[1], q->nb[2], q->nb[3], NQ, H, S,
-                                                          D, q16, false, 0);
+    // the pre-pass moves 16-byte chunks: every caller's views (flash_attn_ext's and
+    // flash_attn_causal's validated inputs, the model drivers' buffers) are 16-byte aligned
+    const bool aligned = ((uintptr_t)q->data & 15) == 0 && q->nb[1] % 16 == 0 && q->nb[2] % 16 == 0 &&
+                         q->nb[3] % 16 == 0 && ((uintptr_t)k->data & 15) == 0 && k->nb[1] % 16 == 0 &&
+                         k->nb[2] % 16 == 0 && k->nb[3] % 16 == 0 && ((uintptr_t)v->data & 15) == 0 &&
+                         v->nb[1] % 16 == 0 && v->nb[2] % 16 == 0 && v->nb[3] % 16 == 0;
+    if (!aligned || (int64_t)S * H > 65535)
+        return oasr_internal_fail(be, OASR_STATUS_FAILED,
+                                  "flash_attn_tc: q/k/v rows must be 16-byte aligned and S * H <= 65535");
+    fa_prep_tiled<false>(be, q, NQ, H, S, D, q16, false, 0);
     if (f16k) {
-        fa_prep_kernel<true><<<blocks, 256, 0, be->stream>>>((const char *)k->data, k->nb[1], k->nb[2], k->nb[3], NKV,
-                                                             HKV, S, D, k16, false, 0);
-        fa_prep_kernel<true><<<blocks, 256, 0, be->stream>>>((const char *)v->data, v->nb[1], v->nb[2], v->nb[3], NKV,
-                                                             HKV, S, D, vt16, true, n_pad);
+        fa_prep_tiled<true>(be, k, NKV, HKV, S, D, k16, false, 0);
+        fa_prep_tiled<true>(be, v, NKV, HKV, S, D, vt16, true, n_pad);
     } else {
-        fa_prep_kernel<false><<<blocks, 256, 0, be->stream>>>((const char *)k->data, k->nb[1], k->nb[2], k->nb[3], NKV,
-                                                              HKV, S, D, k16, false, 0);
-        fa_prep_kernel<false><<<blocks, 256, 0, be->stream>>>((const char *)v->data, v->nb[1], v->nb[2], v->nb[3], NKV,
-                                                              HKV, S, D, vt16, true, n_pad);
+        fa_prep_tiled<false>(be, k, NKV, HKV, S, D, k16, false, 0);
+        fa_prep_tiled<false>(be, v, NKV, HKV, S, D, vt16, true, n_pad);
     }
-    if (n_pad > NKV) fa_zero_pad_kernel<<<64, 256, 0, be->stream>>>(vt16, (int64_t)S * HKV * D, NKV, n_pad);
     st = oasr_internal_launch_check(be, "fa_prep");
     if (st) return st;
     // 64-element (128-byte) boxes: Q / K tiles of 128 rows, Vt half-tiles of D rows x 64 keys

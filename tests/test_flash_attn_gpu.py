@@ -162,6 +162,42 @@ def test_tensor_core_flash_attention_shapes(gpu_backend, S, H, HKV, NQ, NKV):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("kv_dtype", [np.float16, np.float32])
+@pytest.mark.parametrize("aligned", [True, False])
+def test_tensor_core_attention_strided_views(gpu_backend, kv_dtype, aligned):
+    """The tensor-core path's fp16 pre-pass on strided views with rows of 16-byte
+    multiples (Vt written through shared memory, padding keys zeroed; n_kv = 203 leaves
+    5 padding keys in the last 8-key group); views whose data or row strides are not
+    16-byte multiples are refused."""
+    import torch
+
+    S, H, HKV, NQ, NKV, D = 2, 4, 2, 130, 203, 64
+    q, k, v = _case(77 + aligned, S, H, HKV, NQ, NKV, D, kv_dtype)
+    extra = 8 if aligned else 1  # elements of row padding (and offset) around each row
+
+    def view(a):
+        s_, h_, n_, d_ = a.shape
+        buf = torch.zeros((s_, h_, n_, d_ + extra), dtype=torch.float16 if a.dtype == np.float16 else torch.float32,
+                          device="cuda")
+        buf[..., extra:extra + d_] = torch.from_numpy(a).cuda()
+        return buf[..., extra:extra + d_]
+
+    qt, kt, vt = view(q), view(k), view(v)
+    assert (qt.data_ptr() % 16 == 0) == aligned
+    out = torch.empty((S, NQ, H, D), dtype=torch.float32, device="cuda")
+    if not aligned:
+        # rows that are not 16-byte aligned are refused up front (no kernel runs)
+        with pytest.raises(ob.backend.UnsupportedInputs, match="16-byte aligned"):
+            gpu_backend.flash_attn_ext(qt, kt, vt, None, 0.125, out)
+        return
+    gpu_backend.flash_attn_ext(qt, kt, vt, None, 0.125, out)
+    gpu_backend.synchronize()
+    ref = oo.flash_attn_ext(q, k, v, None, 0.125, oo.FA_F32)
+    err = max_abs_rel(out.cpu().numpy(), ref)
+    assert err <= TOL, err
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("S,H,NKV", [(8, 20, 1500), (8, 20, 1), (1, 20, 33), (3, 8, 1500), (2, 4, 5), (8, 20, 447)])
 def test_head_contiguous_kv_rows(gpu_backend, S, H, NKV):
     """Decoder caches whose heads are contiguous in a KV row: the cross cache
