@@ -689,7 +689,7 @@ def run_kernels(args) -> None:
         ve = qkv[:, :, 2 * d:].reshape(B, T, H, 64).permute(0, 2, 1, 3).half()
         oe = torch.empty(B, T, H, 64, device="cuda")
         us = timed(lambda i: be.flash_attn_ext(qe, ke, ve, None, 0.125, oe), 10)
-        add("fa_prep_kernel+fattn_tc_kernel", f"encoder S={B} H={H} {T}x{T} D=64", us, 4.0 * B * H * T * T * 64,
+        add("fa_prep_tile_kernel+fattn_tc_kernel", f"encoder S={B} H={H} {T}x{T} D=64", us, 4.0 * B * H * T * T * 64,
             "TFLOP/s")
         del qkv
         # Qwen3-ASR-0.6B decode (configs[2], batch 8): Q8_0 GEMVs rotated over 4 layers' weights
@@ -716,8 +716,23 @@ def run_kernels(args) -> None:
         vq = torch.randn(B, 8, Tq, 128, device="cuda").half()
         oq = torch.empty(B, Tq, 16, 128, device="cuda")
         us = timed(lambda i: be.flash_attn_causal(qq, kq, vq, 1.0 / float(np.sqrt(128.0)), oq), 10)
-        add("fa_prep_kernel+fattn_tc_kernel<128,causal>", f"qwen prompt S={B} H=16 HKV=8 {Tq}x{Tq} D=128", us,
+        add("fa_prep_tile_kernel+fattn_tc_kernel<128,causal>", f"qwen prompt S={B} H=16 HKV=8 {Tq}x{Tq} D=128", us,
             2.0 * B * 16 * Tq * (Tq + 1) * 128, "TFLOP/s")
+    # resident weight upload (raw pack bytes from pageable host memory through the pinned
+    # staging ring, plane split, decode tiles and scale copies built on the device): the
+    # Qwen lm_head shape, 165 MB of Q8_0 blocks; wall time of the synchronous call
+    import time
+    raw = np.random.default_rng(5).integers(0, 256, (151936, 1024 // 32 * 34), dtype=np.uint8)
+    best = float("inf")
+    for _ in range(3):
+        t0 = time.perf_counter()
+        w = be.upload_weight(raw, ob.Q8_0, [1024, 151936])
+        best = min(best, time.perf_counter() - t0)
+        w.free()
+    rows.append({"kernel": "oasr_b200_weight_upload (staged H2D + split_blocks_kernel + tile build)",
+                 "shape": "Q8_0 151936x1024 (165.3 MB raw)", "us": round(best * 1e6, 1),
+                 "achieved": round(raw.nbytes / best / 1e9, 2), "unit": "GB/s host->device (raw bytes / wall time)",
+                 "peak": None, "peak_kind": None, "frac": None})
     print(json.dumps({"workload": "kernels", "n_gpus": 1, "kernels": rows}), flush=True)
     be.close()
 

@@ -8,7 +8,9 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <cstdlib>
+#include <thread>
 #include <vector>
 
 #include "kernels.cuh"
@@ -31,6 +33,67 @@ void build_gelu_table(std::vector<uint16_t> &t) {
         const float x = host_f16_to_f32((uint16_t)i);
         const float inner = S * x * (1.0f + A * x * x);
         t[i] = host_f32_to_f16(0.5f * x * (1.0f + tanhf(inner)));
+    }
+}
+// ---- weight upload: raw blocks through pinned staging, planes split on the device --------
+constexpr size_t kStageBytes = 16ull << 20;  // one staging buffer
+
+// host copy into a staging buffer, spread over up to 8 threads for large chunks (a single
+// core's memcpy is slower than the host-to-device link)
+void par_memcpy(void *dst, const void *src, size_t n) {
+    const int nt = n >= (4u << 20) ? 8 : n >= (1u << 20) ? 2 : 1;
+    if (nt == 1) {
+        memcpy(dst, src, n);
+        return;
+    }
+    const size_t per = (n / nt + 63) & ~(size_t)63;
+    std::vector<std::thread> th;
+    for (int t = 1; t < nt; ++t) {
+        const size_t o = std::min(n, per * t), e = std::min(n, o + per);
+        if (e > o) th.emplace_back([=] { memcpy((char *)dst + o, (const char *)src + o, e - o); });
+    }
+    memcpy(dst, src, std::min(n, per));
+    for (auto &x : th) x.join();
+}
+
+cudaError_t ensure_stage(oasr_backend *be) {
+    for (int i = 0; i < 2; ++i) {
+        if (be->stage[i]) continue;
+        cudaError_t e = cudaHostAlloc(&be->stage[i], kStageBytes, cudaHostAllocDefault);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&be->stage_done[i], cudaEventDisableTiming);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+// bytes at `src` (any host memory) -> device `dst`: chunk i is copied into staging buffer
+// i % 2 while the asynchronous copy of chunk i - 1 runs
+cudaError_t upload_staged(oasr_backend *be, void *dst, const void *src, size_t bytes) {
+    cudaError_t e = ensure_stage(be);
+    for (size_t off = 0, i = 0; e == cudaSuccess && off < bytes; ++i) {
+        const size_t n = std::min(kStageBytes, bytes - off);
+        const int b = (int)(i & 1);
+        e = cudaEventSynchronize(be->stage_done[b]);
+        if (e != cudaSuccess) break;
+        par_memcpy(be->stage[b], (const char *)src + off, n);
+        e = cudaMemcpyAsync((char *)dst + off, be->stage[b], n, cudaMemcpyHostToDevice, be->stream);
+        if (e == cudaSuccess) e = cudaEventRecord(be->stage_done[b], be->stream);
+        off += n;
+    }
+    return e;
+}
+
+// raw Q8_0 / Q4_0 blocks [rows][nb][bb] -> quant plane [rows][nb * qb] + fp16 scale plane
+// [rows][nb] (one thread per block; the scale is the block's first two bytes)
+__global__ void split_blocks_kernel(const uint8_t *raw, int64_t nblocks, int64_t nb, int bb, int64_t qs_row, uint8_t *qs,
+                                    uint16_t *d) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nblocks; i += (int64_t)gridDim.x * blockDim.x) {
+        const uint8_t *blk = raw + i * bb;
+        const int64_t r = i / nb, b = i - r * nb;
+        d[i] = (uint16_t)(blk[0] | (blk[1] << 8));
+        const int qb = bb - 2;
+        uint8_t *q = qs + r * qs_row + b * qb;
+        for (int j = 0; j < qb; ++j) q[j] = blk[2 + j];
     }
 }
 }  // namespace
@@ -172,6 +235,10 @@ int oasr_b200_free(oasr_backend *be) {
     if (be->counters) cudaFree(be->counters);
     if (be->err_word) cudaFree(be->err_word);
     if (be->gelu_table) cudaFree(be->gelu_table);
+    for (int i = 0; i < 2; ++i) {
+        if (be->stage[i]) cudaFreeHost(be->stage[i]);
+        if (be->stage_done[i]) cudaEventDestroy(be->stage_done[i]);
+    }
     if (be->own_stream) cudaStreamDestroy(be->own_stream);
     delete be;
     return OASR_STATUS_SUCCESS;
@@ -279,7 +346,8 @@ int oasr_b200_weight_upload(oasr_backend *be, const void *host, size_t bytes, in
     for (int i = 0; i < 4; ++i) w->ne[i] = ne[i];
     w->qs = nullptr;
     w->d = nullptr;
-    const uint8_t *src = (const uint8_t *)host;
+    // the pack's raw blocks cross to the device once, through the pinned staging ring
+    // (bulk host-to-device copies); Q8_0 / Q4_0 blocks are split into planes there
     cudaError_t e;
     if (type == OASR_TYPE_Q8_0 || type == OASR_TYPE_Q4_0) {
         const int bb = type == OASR_TYPE_Q8_0 ? BYTES_Q8_0 : BYTES_Q4_0;
@@ -287,25 +355,29 @@ int oasr_b200_weight_upload(oasr_backend *be, const void *host, size_t bytes, in
         const int64_t nb = ne[0] / 32;
         w->qs_row_bytes = nb * qb;
         w->d_row_elems = nb;
-        std::vector<uint8_t> qs((size_t)(rows * w->qs_row_bytes));
-        std::vector<uint16_t> d((size_t)(rows * nb));
-        for (int64_t r = 0; r < rows; ++r)
-            for (int64_t b = 0; b < nb; ++b) {
-                const uint8_t *blk = src + r * rs + b * bb;
-                memcpy(&d[(size_t)(r * nb + b)], blk, 2);
-                memcpy(&qs[(size_t)(r * w->qs_row_bytes + b * qb)], blk + 2, qb);
-            }
-        w->device_bytes = qs.size() + d.size() * 2;
-        e = cudaMalloc(&w->qs, qs.size());
-        if (e == cudaSuccess) e = cudaMalloc(&w->d, d.size() * 2);
-        if (e == cudaSuccess) e = cudaMemcpy(w->qs, qs.data(), qs.size(), cudaMemcpyHostToDevice);
-        if (e == cudaSuccess) e = cudaMemcpy(w->d, d.data(), d.size() * 2, cudaMemcpyHostToDevice);
+        const size_t qs_bytes = (size_t)(rows * w->qs_row_bytes), d_bytes = (size_t)(rows * nb) * 2;
+        w->device_bytes = qs_bytes + d_bytes;
+        void *raw = nullptr;
+        e = cudaMalloc(&w->qs, qs_bytes);
+        if (e == cudaSuccess) e = cudaMalloc(&w->d, d_bytes);
+        if (e == cudaSuccess) e = cudaMalloc(&raw, bytes);
+        if (e == cudaSuccess) e = upload_staged(be, raw, host, bytes);
+        if (e == cudaSuccess) {
+            const int64_t nblocks = rows * nb;
+            const unsigned grid = (unsigned)std::min<int64_t>((nblocks + 255) / 256, (int64_t)be->sm_count * 16);
+            split_blocks_kernel<<<grid, 256, 0, be->stream>>>((const uint8_t *)raw, nblocks, nb, bb, w->qs_row_bytes,
+                                                              (uint8_t *)w->qs, (uint16_t *)w->d);
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = cudaStreamSynchronize(be->stream);
+        if (raw) cudaFree(raw);
     } else {
         w->qs_row_bytes = rs;
         w->d_row_elems = 0;
         w->device_bytes = bytes;
         e = cudaMalloc(&w->qs, bytes);
-        if (e == cudaSuccess) e = cudaMemcpy(w->qs, src, bytes, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = upload_staged(be, w->qs, host, bytes);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(be->stream);
     }
     w->tiles = nullptr;
     w->dT = nullptr;

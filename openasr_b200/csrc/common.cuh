@@ -74,6 +74,10 @@ struct oasr_backend {
     std::string last_error;
     bool pdl;  // launch with programmatic stream serialization (dependent kernels overlap)
     bool decode_tiles;  // build decode tiles at upload (OASR_B200_DECODE_GEMV=dp4a turns it off)
+    // weight upload staging: two pinned host buffers, each reused once the copy that last
+    // read it has completed (its event), allocated at the first upload
+    void *stage[2];
+    cudaEvent_t stage_done[2];
 };
 
 #define OASR_CUDA_TRY(be, expr)                                                          \
