@@ -291,7 +291,8 @@ def run_b200_mulmat(args) -> None:
             "e2e": {"value": world * STEP_BYTES / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": launches_per_step * args.steps,
-            "roofline": {"bound": "hbm", "kernel": "mmv_q8_kernel (lm_head 151936x1024 Q8_0, M=8)",
+            "roofline": {"bound": "hbm", "kernel": "oasr_b200_mul_mat: quantize_q8_0_kernel + mmv_q80_tc_kernel "
+                                                   "(lm_head 151936x1024 Q8_0, M=8)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": ncu_traffic(), "algorithmic_bytes": lm_bytes,
                          "avg_launch_us": lm_ms * 1e3},
@@ -422,7 +423,7 @@ def run_reference(args) -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 8 * 17.5 / v * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "q4_K x q8_K int dot, f32 accumulate; f16 KV",
         "data": "synthetic (seeded N(0,0.02) Q4_K weights, -20 dBFS Gaussian-noise audio, lengths U[5,30] s)",
-        "config": {"workload": "configs[4]: whisper-large-v3-shaped Q4_K, batch 8 per GPU, greedy 224 tokens",
+        "config": {"workload": "configs[3] (whisper-large-v3-shaped Q4_K, batch 8 per GPU, greedy 224 tokens) with configs[4] lengths",
                    "l2": "inputs larger than L2"},
         "cpu_baseline": cb,
         "e2e": {"value": v, "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -538,7 +539,7 @@ def run_b200(args) -> None:
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "q4_K x q8_K int dot (f32 accumulate), fp16 tensor-core conv/attention, f16 KV",
             "data": "synthetic (seeded N(0,0.02) Q4_K weights, -20 dBFS Gaussian-noise audio, lengths U[5,30] s)",
-            "config": {"workload": "configs[4]/[4-box]: whisper-large-v3-shaped Q4_K (32+32 layers, d 1280, vocab "
+            "config": {"workload": "configs[3] with configs[4] utterance lengths: whisper-large-v3-shaped Q4_K (32+32 layers, d 1280, vocab "
                                    "51866), batch 8 per GPU, greedy 224 tokens, mel+encoder+decoder on device",
                        "batch_per_gpu": B, "utterances_per_step": B * world, "new_tokens": N_NEW,
                        "l2": "inputs larger than L2 (1.97 GB cross-K/V + 0.48 GB weights per decode step)",

@@ -231,6 +231,153 @@ int oasr_b200_set_rows(oasr_backend *be, oasr_tensor *dst, const oasr_tensor *sr
  * maximal; out I32 [rows]. */
 int oasr_b200_argmax_first(oasr_backend *be, const oasr_tensor *logits, oasr_tensor *out);
 
+/* ---- memory API v1 (the optional table the plugin loader resolves through
+ * ggml_backend_reg_get_proc_address("ggml_backend_memory_get_api_v1"); layouts and
+ * constants of ffi.rs:144-333, fixed widths checked by backend_memory.rs:697-704:
+ * domain id 24 B, request 88 B, claim 96 B, quote 48 B, stats 152 B, table 64 B).
+ * Every `dev` / `backend` handle here is an oasr_backend (one device + one stream).
+ * Count protocol (backend_memory.rs:193-356): a call with a null array returns the
+ * item count in *count; a call with an array of *count items fills at most that many
+ * and sets *count to the number written, failing (OASR_STATUS_FAILED, *count = the
+ * number needed) when the array is too small.  Domains: 1 device-local HBM (heap 0,
+ * the backend's weights, activation scratch and tables), 2 host-pinned (heap 1, the
+ * weight-upload staging buffers).  Request kinds: BUFFER (an engine-owned device
+ * buffer, claimed, committed by the engine), HOST_IMPORT (a host weight payload
+ * copied to HBM by oasr_b200_weight_upload: device claim plus staging), GRAPH_PRIVATE
+ * (the backend's activation scratch; reserve_private grows it), TRANSFER (the
+ * pinned staging buffers; reserve_private allocates them).  A quote carries the
+ * stats generation and a token; reserve_private refuses a quote whose token,
+ * request fingerprint or generation no longer matches (any allocation, free, trim
+ * or quarantine bumps the generation).  reserve_private with a null claim array is
+ * the sizing query and changes nothing.  trim (flags ignored) synchronises the
+ * stream and releases the activation scratch and the staging buffers (graphs
+ * captured before must be re-captured: the model drivers do so themselves).
+ * quarantine poisons the backend (later calls: OASR_STATUS_BACKEND_POISONED) and
+ * records the reason; stats then report health QUARANTINED. */
+#define OASR_MEMORY_ABI_V1 1u
+enum {
+    OASR_MEMORY_DOMAIN_DEVICE_LOCAL = 1, OASR_MEMORY_DOMAIN_HOST_PAGEABLE = 2, OASR_MEMORY_DOMAIN_HOST_PINNED = 3,
+    OASR_MEMORY_DOMAIN_UNIFIED = 4, OASR_MEMORY_DOMAIN_FILE_BACKED = 5
+};
+enum {
+    OASR_MEMORY_REQUEST_BUFFER = 1, OASR_MEMORY_REQUEST_HOST_IMPORT = 2, OASR_MEMORY_REQUEST_GRAPH_PRIVATE = 3,
+    OASR_MEMORY_REQUEST_TRANSFER = 4
+};
+enum {
+    OASR_MEMORY_QUOTE_PROVISIONAL = 1u << 0, OASR_MEMORY_QUOTE_HAS_RESIDUAL_UNCERTAINTY = 1u << 1,
+    OASR_MEMORY_QUOTE_OPAQUE_DRIVER_COSTS_REQUIRE_DOMAIN_HEADROOM = 1u << 2
+};
+enum { OASR_MEMORY_STATS_BUDGET_UNAVAILABLE = 1u << 0 };
+enum {
+    OASR_MEMORY_CLAIM_EXACT = 1u << 0, OASR_MEMORY_CLAIM_CONSERVATIVE_UPPER = 1u << 1,
+    OASR_MEMORY_CLAIM_DRIVER_ESTIMATE = 1u << 2, OASR_MEMORY_CLAIM_PROVISIONAL = 1u << 6
+};
+enum {
+    OASR_MEMORY_HEALTHY = 0, OASR_MEMORY_DEGRADED = 1, OASR_MEMORY_QUARANTINED = 2, OASR_MEMORY_DEVICE_LOST = 3
+};
+
+typedef struct oasr_memory_domain_id_v1 {
+    uint8_t physical_device_uuid[16];
+    uint32_t heap_index;
+    uint32_t kind;
+} oasr_memory_domain_id_v1;
+
+typedef struct oasr_memory_domain_v1 {
+    uint32_t struct_size;
+    uint32_t flags;
+    oasr_memory_domain_id_v1 id;
+    char name[48];
+} oasr_memory_domain_v1;
+
+typedef struct oasr_memory_request_v1 {
+    uint32_t struct_size;
+    uint32_t kind;
+    uint32_t flags;
+    uint32_t usage; /* ggml buffer usage: 1 WEIGHTS, 2 COMPUTE (ffi.rs:141-142) */
+    uint64_t request_id;
+    void *backend;
+    void *peer_backend;
+    void *buft;
+    void *graph;
+    const void *host_ptr;
+    uint64_t requested_bytes;
+    uint64_t currently_allocated_bytes;
+    uint64_t max_tensor_bytes;
+} oasr_memory_request_v1;
+
+typedef struct oasr_memory_claim_v1 {
+    uint32_t struct_size;
+    uint32_t flags;
+    uint64_t request_id;
+    oasr_memory_domain_id_v1 domain;
+    uint64_t payload_requested_bytes;
+    uint64_t committed_before_bytes;
+    uint64_t committed_after_upper_bytes;
+    uint64_t commit_peak_extra_upper_bytes;
+    uint64_t resident_after_upper_bytes;
+    uint64_t retained_after_use_upper_bytes;
+    uint64_t releasable_after_use_upper_bytes;
+} oasr_memory_claim_v1;
+
+typedef struct oasr_memory_quote_v1 {
+    uint32_t struct_size;
+    uint32_t flags;
+    uint32_t residual_flags;
+    uint32_t residual_request_count;
+    uint64_t provisional_requested_upper_bytes;
+    uint64_t stats_generation;
+    uint64_t quote_token;
+    uint64_t request_fingerprint;
+} oasr_memory_quote_v1;
+
+typedef struct oasr_memory_stats_v1 {
+    uint32_t struct_size;
+    uint32_t flags;
+    oasr_memory_domain_id_v1 domain;
+    uint64_t generation;
+    uint64_t timestamp_monotonic_ns;
+    uint64_t total_bytes;
+    uint64_t budget_bytes;
+    uint64_t device_used_bytes;
+    uint64_t device_free_bytes;
+    uint64_t backend_owned_live_bytes;
+    uint64_t backend_owned_cached_bytes;
+    uint64_t backend_owned_workspace_bytes;
+    uint64_t backend_owned_high_water_bytes;
+    uint64_t allocation_count;
+    uint64_t allocation_failure_count;
+    uint32_t health;
+    int32_t last_ggml_status;
+    int64_t last_native_error;
+    uint64_t quarantine_generation;
+} oasr_memory_stats_v1;
+
+typedef struct oasr_memory_quarantine_v1 {
+    uint32_t struct_size;
+    uint32_t flags;
+    uint32_t reason;
+    int32_t ggml_status;
+    int64_t native_error;
+    char message[96];
+} oasr_memory_quarantine_v1;
+
+typedef struct oasr_memory_api_v1 {
+    uint32_t struct_size;
+    uint32_t abi_version;
+    uint64_t capabilities;
+    int (*get_domains)(void *dev, oasr_memory_domain_v1 *domains, uint32_t *count);
+    int (*quote)(const oasr_memory_request_v1 *requests, uint32_t n, oasr_memory_quote_v1 *quote,
+                 oasr_memory_claim_v1 *claims, uint32_t *n_claims);
+    int (*reserve_private)(const oasr_memory_request_v1 *requests, uint32_t n, const oasr_memory_quote_v1 *quote,
+                           oasr_memory_claim_v1 *claims, uint32_t *n_claims);
+    int (*get_stats)(void *dev, void *backend, oasr_memory_stats_v1 *stats, uint32_t *count);
+    int (*trim)(void *backend, uint64_t flags);
+    int (*quarantine)(void *backend, const oasr_memory_quarantine_v1 *info);
+} oasr_memory_api_v1;
+
+/* ggml_backend_memory_get_api_v1 (GgmlBackendMemoryGetApiV1Fn, ffi.rs:331-332) */
+const oasr_memory_api_v1 *oasr_b200_memory_get_api_v1(void);
+
 /* ---- model drivers ------------------------------------------------------------------
  * The graphs openasr-core builds around the hot ops (layer map L2/L3), restated
  * natively so a whole encoder pass or decoder step runs on this device without

@@ -131,6 +131,100 @@ class OasrQwenConfig(ctypes.Structure):
 
 ABORT_CB = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p)
 
+
+# ---- memory API v1 (ffi.rs:144-333; fixed widths of backend_memory.rs:697-704) ----------
+MEMORY_ABI_V1 = 1
+DOMAIN_DEVICE_LOCAL, DOMAIN_HOST_PAGEABLE, DOMAIN_HOST_PINNED, DOMAIN_UNIFIED, DOMAIN_FILE_BACKED = 1, 2, 3, 4, 5
+REQUEST_BUFFER, REQUEST_HOST_IMPORT, REQUEST_GRAPH_PRIVATE, REQUEST_TRANSFER = 1, 2, 3, 4
+STATS_BUDGET_UNAVAILABLE = 1
+CLAIM_EXACT, CLAIM_CONSERVATIVE_UPPER = 1, 2
+MEMORY_HEALTHY, MEMORY_DEGRADED, MEMORY_QUARANTINED, MEMORY_DEVICE_LOST = 0, 1, 2, 3
+
+
+class MemDomainId(ctypes.Structure):
+    _fields_ = [("physical_device_uuid", ctypes.c_uint8 * 16), ("heap_index", ctypes.c_uint32),
+                ("kind", ctypes.c_uint32)]
+
+
+class MemDomain(ctypes.Structure):
+    _fields_ = [("struct_size", ctypes.c_uint32), ("flags", ctypes.c_uint32), ("id", MemDomainId),
+                ("name", ctypes.c_char * 48)]
+
+
+class MemRequest(ctypes.Structure):
+    _fields_ = [("struct_size", ctypes.c_uint32), ("kind", ctypes.c_uint32), ("flags", ctypes.c_uint32),
+                ("usage", ctypes.c_uint32), ("request_id", ctypes.c_uint64), ("backend", ctypes.c_void_p),
+                ("peer_backend", ctypes.c_void_p), ("buft", ctypes.c_void_p), ("graph", ctypes.c_void_p),
+                ("host_ptr", ctypes.c_void_p), ("requested_bytes", ctypes.c_uint64),
+                ("currently_allocated_bytes", ctypes.c_uint64), ("max_tensor_bytes", ctypes.c_uint64)]
+
+
+class MemClaim(ctypes.Structure):
+    _fields_ = [("struct_size", ctypes.c_uint32), ("flags", ctypes.c_uint32), ("request_id", ctypes.c_uint64),
+                ("domain", MemDomainId)] + [(f, ctypes.c_uint64) for f in (
+                    "payload_requested_bytes", "committed_before_bytes", "committed_after_upper_bytes",
+                    "commit_peak_extra_upper_bytes", "resident_after_upper_bytes", "retained_after_use_upper_bytes",
+                    "releasable_after_use_upper_bytes")]
+
+
+class MemQuote(ctypes.Structure):
+    _fields_ = [("struct_size", ctypes.c_uint32), ("flags", ctypes.c_uint32), ("residual_flags", ctypes.c_uint32),
+                ("residual_request_count", ctypes.c_uint32), ("provisional_requested_upper_bytes", ctypes.c_uint64),
+                ("stats_generation", ctypes.c_uint64), ("quote_token", ctypes.c_uint64),
+                ("request_fingerprint", ctypes.c_uint64)]
+
+
+class MemStats(ctypes.Structure):
+    _fields_ = [("struct_size", ctypes.c_uint32), ("flags", ctypes.c_uint32), ("domain", MemDomainId)] + [
+        (f, ctypes.c_uint64) for f in (
+            "generation", "timestamp_monotonic_ns", "total_bytes", "budget_bytes", "device_used_bytes",
+            "device_free_bytes", "backend_owned_live_bytes", "backend_owned_cached_bytes",
+            "backend_owned_workspace_bytes", "backend_owned_high_water_bytes", "allocation_count",
+            "allocation_failure_count")] + [
+        ("health", ctypes.c_uint32), ("last_ggml_status", ctypes.c_int32), ("last_native_error", ctypes.c_int64),
+        ("quarantine_generation", ctypes.c_uint64)]
+
+
+class MemQuarantine(ctypes.Structure):
+    _fields_ = [("struct_size", ctypes.c_uint32), ("flags", ctypes.c_uint32), ("reason", ctypes.c_uint32),
+                ("ggml_status", ctypes.c_int32), ("native_error", ctypes.c_int64), ("message", ctypes.c_char * 96)]
+
+
+_U32P = ctypes.POINTER(ctypes.c_uint32)
+MEM_GET_DOMAINS = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(MemDomain), _U32P)
+MEM_QUOTE = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.POINTER(MemRequest), ctypes.c_uint32, ctypes.POINTER(MemQuote),
+                             ctypes.POINTER(MemClaim), _U32P)
+MEM_RESERVE_PRIVATE = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.POINTER(MemRequest), ctypes.c_uint32,
+                                       ctypes.POINTER(MemQuote), ctypes.POINTER(MemClaim), _U32P)
+MEM_GET_STATS = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(MemStats), _U32P)
+MEM_TRIM = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64)
+MEM_QUARANTINE = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(MemQuarantine))
+
+
+class MemoryApiV1(ctypes.Structure):
+    _fields_ = [("struct_size", ctypes.c_uint32), ("abi_version", ctypes.c_uint32), ("capabilities", ctypes.c_uint64),
+                ("get_domains", MEM_GET_DOMAINS), ("quote", MEM_QUOTE), ("reserve_private", MEM_RESERVE_PRIVATE),
+                ("get_stats", MEM_GET_STATS), ("trim", MEM_TRIM), ("quarantine", MEM_QUARANTINE)]
+
+
+def memory_api() -> MemoryApiV1:
+    """The table ggml_backend_memory_get_api_v1 returns (static for the process)."""
+    return lib().oasr_b200_memory_get_api_v1().contents
+
+
+def _counted(call, item_type):
+    """The v1 count protocol: size with a null array, then fill (backend_memory.rs:193-356)."""
+    n = ctypes.c_uint32(0)
+    rc = call(None, ctypes.byref(n))
+    if rc != 0:
+        return rc, []
+    items = (item_type * max(n.value, 1))()
+    for it in items:
+        it.struct_size = ctypes.sizeof(item_type)
+    cap = ctypes.c_uint32(n.value)
+    rc = call(items, ctypes.byref(cap))
+    return rc, list(items)[: cap.value] if rc == 0 else []
+
 # every symbol include/oasr_b200.h declares, with (argtypes, restype)
 _P, _I32, _I64, _U64, _F, _SZ = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_uint64, ctypes.c_float, ctypes.c_size_t
 _TP = ctypes.POINTER(OasrTensor)
@@ -179,6 +273,7 @@ SIGNATURES = {
     "oasr_b200_row_size": ([_I32, _I64], _I64),
     "oasr_b200_quantize_chunk": ([_I32, _P, _P, _I64, _I64, _I64], _I64),
     "oasr_b200_synth_normal": ([_U64, _U64, _P, _I64, _F, _F], ctypes.c_int),
+    "oasr_b200_memory_get_api_v1": ([], ctypes.POINTER(MemoryApiV1)),
 }
 
 _lib = None
@@ -338,6 +433,62 @@ class Backend:
 
     def synchronize(self) -> None:
         self._check(lib().oasr_b200_synchronize(self.handle))
+
+    # -- memory API v1 (the table a plugin loader resolves by proc address) --
+    def memory_domains(self) -> list:
+        api = memory_api()
+        rc, items = _counted(lambda arr, n: api.get_domains(self.handle, arr, n), MemDomain)
+        self._check(rc)
+        return items
+
+    def memory_stats(self) -> list:
+        api = memory_api()
+        rc, items = _counted(lambda arr, n: api.get_stats(self.handle, self.handle, arr, n), MemStats)
+        self._check(rc)
+        return items
+
+    def memory_request(self, kind: int, nbytes: int, request_id: int = 0, usage: int = 0) -> MemRequest:
+        r = MemRequest()
+        r.struct_size = ctypes.sizeof(MemRequest)
+        r.kind, r.usage, r.request_id, r.requested_bytes = kind, usage, request_id, nbytes
+        r.backend = self.handle
+        return r
+
+    def memory_quote(self, requests) -> tuple:
+        """(quote, claims) for a list of MemRequest."""
+        api = memory_api()
+        arr = (MemRequest * max(len(requests), 1))(*requests)
+        q = MemQuote()
+        q.struct_size = ctypes.sizeof(MemQuote)
+        rc, claims = _counted(lambda c, n: api.quote(arr, len(requests), ctypes.byref(q), c, n), MemClaim)
+        self._check(rc)
+        return q, claims
+
+    def memory_reserve_private(self, requests, quote: MemQuote, sizing_only: bool = False):
+        """Commit the backend-private requests of `quote`; returns the actual claims (or,
+        with sizing_only, just their count)."""
+        api = memory_api()
+        arr = (MemRequest * max(len(requests), 1))(*requests)
+        n = ctypes.c_uint32(0)
+        self._check(api.reserve_private(arr, len(requests), ctypes.byref(quote), None, ctypes.byref(n)))
+        if sizing_only:
+            return n.value
+        claims = (MemClaim * max(n.value, 1))()
+        for c in claims:
+            c.struct_size = ctypes.sizeof(MemClaim)
+        cap = ctypes.c_uint32(n.value)
+        self._check(api.reserve_private(arr, len(requests), ctypes.byref(quote), claims, ctypes.byref(cap)))
+        return list(claims)[: cap.value]
+
+    def memory_trim(self, flags: int = 0) -> None:
+        self._check(memory_api().trim(self.handle, flags))
+
+    def memory_quarantine(self, status: int, message: str, native_error: int = 0) -> None:
+        q = MemQuarantine()
+        q.struct_size = ctypes.sizeof(MemQuarantine)
+        q.ggml_status, q.native_error = status, native_error
+        q.message = message.encode()[:95]
+        self._check(memory_api().quarantine(self.handle, ctypes.byref(q)))
 
     def reserve_scratch(self, nbytes: int) -> None:
         self._check(lib().oasr_b200_reserve_scratch(self.handle, nbytes))

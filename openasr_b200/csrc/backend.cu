@@ -19,6 +19,7 @@ using namespace oasr;
 
 namespace {
 constexpr size_t kCounterSlots = 1 << 16;  // flash-decode split counters
+static_assert(kBackendFixedBytes == kCounterSlots * 4 + 4 + 65536 * 2, "fixed backend bytes");
 constexpr size_t kDefaultScratch = 64ull << 20;
 
 uint16_t host_f32_to_f16(float f) { return __half_as_ushort(__float2half_rn(f)); }
@@ -36,7 +37,7 @@ void build_gelu_table(std::vector<uint16_t> &t) {
     }
 }
 // ---- weight upload: raw blocks through pinned staging, planes split on the device --------
-constexpr size_t kStageBytes = 16ull << 20;  // one staging buffer
+constexpr size_t kStageBytes = kUploadStageBytes;
 
 // host copy into a staging buffer, spread over up to 8 threads for large chunks (a single
 // core's memcpy is slower than the host-to-device link)
@@ -56,20 +57,45 @@ void par_memcpy(void *dst, const void *src, size_t n) {
     for (auto &x : th) x.join();
 }
 
-cudaError_t ensure_stage(oasr_backend *be) {
+}  // namespace
+
+cudaError_t oasr_internal_stage_alloc(oasr_backend *be) {
     for (int i = 0; i < 2; ++i) {
         if (be->stage[i]) continue;
         cudaError_t e = cudaHostAlloc(&be->stage[i], kStageBytes, cudaHostAllocDefault);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&be->stage_done[i], cudaEventDisableTiming);
+        oasr_internal_mem_event(be, e == cudaSuccess);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
 }
 
+void oasr_internal_stage_release(oasr_backend *be) {
+    for (int i = 0; i < 2; ++i) {
+        if (be->stage_done[i]) cudaEventSynchronize(be->stage_done[i]);
+        if (be->stage[i]) cudaFreeHost(be->stage[i]);
+        if (be->stage_done[i]) cudaEventDestroy(be->stage_done[i]);
+        be->stage[i] = nullptr;
+        be->stage_done[i] = nullptr;
+    }
+    be->mem_generation.fetch_add(1);
+}
+
+void oasr_internal_scratch_release(oasr_backend *be) {
+    cudaStreamSynchronize(be->stream);
+    if (be->scratch) cudaFree(be->scratch);
+    be->scratch = nullptr;
+    be->scratch_bytes = 0;
+    ++be->scratch_epoch;
+    be->mem_generation.fetch_add(1);
+}
+
+namespace {
+
 // bytes at `src` (any host memory) -> device `dst`: chunk i is copied into staging buffer
 // i % 2 while the asynchronous copy of chunk i - 1 runs
 cudaError_t upload_staged(oasr_backend *be, void *dst, const void *src, size_t bytes) {
-    cudaError_t e = ensure_stage(be);
+    cudaError_t e = oasr_internal_stage_alloc(be);
     for (size_t off = 0, i = 0; e == cudaSuccess && off < bytes; ++i) {
         const size_t n = std::min(kStageBytes, bytes - off);
         const int b = (int)(i & 1);
@@ -98,8 +124,18 @@ __global__ void split_blocks_kernel(const uint8_t *raw, int64_t nblocks, int64_t
 }
 }  // namespace
 
+void oasr_internal_mem_event(oasr_backend *be, bool ok) {
+    if (ok) ++be->mem_alloc_count;
+    else ++be->mem_alloc_failures;
+    be->mem_generation.fetch_add(1);
+    be->mem_high_water = std::max(be->mem_high_water, oasr_internal_owned_device_bytes(be));
+}
+
 int oasr_internal_fail(oasr_backend *be, int status, const std::string &msg) {
-    if (be) be->last_error = msg;
+    if (be) {
+        be->last_error = msg;
+        if (status != OASR_STATUS_SUCCESS) be->last_status = status;
+    }
     return status;
 }
 
@@ -107,6 +143,7 @@ int oasr_internal_cuda_fail(oasr_backend *be, cudaError_t e, const char *what, i
     char buf[512];
     snprintf(buf, sizeof buf, "%s failed at backend.cu:%d: %s", what, line, cudaGetErrorString(e));
     int st = e == cudaErrorMemoryAllocation ? OASR_STATUS_ALLOC_FAILED : OASR_STATUS_EXECUTION_FAILED;
+    if (be) be->last_native_error = (int64_t)e;
     if (e == cudaErrorIllegalAddress || e == cudaErrorLaunchFailure || e == cudaErrorIllegalInstruction ||
         e == cudaErrorMisalignedAddress || e == cudaErrorHardwareStackError || e == cudaErrorECCUncorrectable ||
         e == cudaErrorNoDevice || e == cudaErrorDevicesUnavailable)
@@ -158,11 +195,13 @@ void *oasr_internal_scratch(oasr_backend *be, size_t bytes, int *status) {
     be->scratch_bytes = 0;
     e = cudaMalloc(&be->scratch, nb);
     if (e != cudaSuccess) {
+        oasr_internal_mem_event(be, false);
         *status = oasr_internal_cuda_fail(be, e, "cudaMalloc(scratch)", __LINE__);
         return nullptr;
     }
     be->scratch_bytes = nb;
     ++be->scratch_epoch;
+    oasr_internal_mem_event(be, true);
     return be->scratch;
 }
 
@@ -402,10 +441,12 @@ int oasr_b200_weight_upload(oasr_backend *be, const void *host, size_t bytes, in
         if (w->tiles) cudaFree(w->tiles);
         if (w->dT) cudaFree(w->dT);
         delete w;
+        oasr_internal_mem_event(be, false);
         return oasr_internal_cuda_fail(be, e, "weight_upload", __LINE__);
     }
     be->weight_bytes += w->device_bytes;
     be->n_weights += 1;
+    oasr_internal_mem_event(be, true);
     *out = w;
     return OASR_STATUS_SUCCESS;
 }
@@ -417,6 +458,7 @@ int oasr_b200_weight_free(oasr_backend *be, oasr_weight *w) {
         cudaStreamSynchronize(be->stream);
         be->weight_bytes -= w->device_bytes;
         be->n_weights -= 1;
+        be->mem_generation.fetch_add(1);
     }
     if (w->qs) cudaFree(w->qs);
     if (w->d) cudaFree(w->d);

@@ -78,7 +78,33 @@ struct oasr_backend {
     // read it has completed (its event), allocated at the first upload
     void *stage[2];
     cudaEvent_t stage_done[2];
+    // memory API v1 bookkeeping (memory_api.cu): a generation that every change of the
+    // backend's allocations bumps, allocation counters, the owned-bytes high water, the
+    // quarantine state, the last failure, and the last quote issued
+    std::atomic<uint64_t> mem_generation;
+    uint64_t mem_alloc_count, mem_alloc_failures, mem_high_water;
+    uint64_t quarantine_generation;
+    int quarantined;
+    int last_status;
+    int64_t last_native_error;
+    uint64_t quote_token, quote_fingerprint, quote_generation;
 };
+
+// fixed device bytes every backend holds besides weights and scratch (split-KV tickets,
+// error word, GELU table)
+constexpr uint64_t kBackendFixedBytes = (uint64_t)(1 << 16) * 4 + 4 + 65536 * 2;
+inline uint64_t oasr_internal_owned_device_bytes(const oasr_backend *be) {
+    return be->weight_bytes + be->scratch_bytes + kBackendFixedBytes;
+}
+// record an allocation (ok) or a failed allocation, and bump the memory generation
+void oasr_internal_mem_event(oasr_backend *be, bool ok);
+// weight-upload staging: two pinned buffers of kUploadStageBytes (allocated on demand)
+constexpr size_t kUploadStageBytes = 16ull << 20;
+cudaError_t oasr_internal_stage_alloc(oasr_backend *be);
+void oasr_internal_stage_release(oasr_backend *be);
+// free the activation scratch after the stream drains (the next use reallocates it and
+// bumps scratch_epoch, so captured step graphs are re-captured)
+void oasr_internal_scratch_release(oasr_backend *be);
 
 #define OASR_CUDA_TRY(be, expr)                                                          \
     do {                                                                                 \
