@@ -285,3 +285,33 @@ def test_gqa_decode_head_major_cache(gpu_backend, S, H, HKV, NKV):
     ref = oo.flash_attn_ext(q, k, v, None, 1.0 / np.sqrt(128), oo.FA_F32)
     err = max_abs_rel(got, ref)
     assert err <= TOL and err <= TIGHT, err
+
+
+@pytest.mark.gpu
+def test_q8_0_kv_is_refused_like_the_reference_gpu_surface(gpu_backend):
+    """The reference accepts Q8_0 K/V only on its CPU and Metal backends
+    (kv_element.rs:113-121; its own test asserts the GPU backend refuses it,
+    kv_element.rs:290-292), so this GPU backend refuses it too: the capability
+    probe answers no, and flash_attn_ext / set_rows fail with UnsupportedInputs
+    before any kernel runs."""
+    import torch
+
+    import ctypes
+
+    q = torch.zeros((1, 2, 1, 32), device="cuda")
+    kq = torch.zeros((1, 1, 2, 34), dtype=torch.uint8, device="cuda")  # two Q8_0 rows of 32 values
+    kt = ob.backend.describe(kq, ob.Q8_0)
+    kt.ne[0], kt.nb[0] = 32, 34
+    qt = ob.backend.describe(q)
+    out = torch.full((1, 1, 2, 32), 7.0, device="cuda")
+    ot = ob.backend.describe(out)
+    L = ob.lib()
+    assert L.oasr_b200_supports_op(gpu_backend.handle, ob.OP_FLASH_ATTN_EXT, ctypes.byref(qt), ctypes.byref(kt)) == 0
+    assert L.oasr_b200_supports_op(gpu_backend.handle, ob.OP_SET_ROWS, ctypes.byref(kt), None) == 0
+    rc = L.oasr_b200_flash_attn_ext(gpu_backend.handle, ctypes.byref(qt), ctypes.byref(kt), ctypes.byref(kt), None,
+                                    1.0, 0.0, 0.0, 0, ctypes.byref(ot))
+    assert rc == ob.backend.STATUS_FAILED
+    assert b"F16 or F32" in L.oasr_b200_last_error(gpu_backend.handle)
+    gpu_backend.synchronize()
+    assert torch.all(out == 7.0)  # nothing was written
+
