@@ -363,14 +363,18 @@ def utterance_lengths(step: int, rank: int, n: int = 8) -> list[int]:
 
 
 def launches_per_batch(n_enc: int, n_dec: int, n_prompt: int, n_new: int, batch: int) -> int:
-    """Kernel launches of one generate() (counted from model_whisper.cu):
-    mel 3; prelude 4 + batch positional adds; per encoder layer 10 + 4 attention
-    (3 pre-pass + 1 tensor-core); final norm 1; 2 cross-K/V per decoder layer;
-    per decoder step 1 embed + 8 per layer (6 fused GEMVs, 2 attentions) + 3 head
-    (LN + quantize, logits, argmax) + 1 advance; 1 fill per prompt token."""
-    enc = 3 + 4 + batch + n_enc * 14 + 1 + 2 * n_dec
+    """Kernel launches of one generate() (counted from model_whisper.cu, and equal to
+    the committed launch list): mel 3; prelude 4 (2 im2col + 2 conv GEMMs) + batch
+    positional adds; per encoder layer 13 (2 LayerNorm + quantize, 4 tensor-core GEMMs,
+    3 f16 pre-pass + 1 tensor-core attention, attention-output quantize, GELU +
+    quantize, residual add); final norm 1; 2 cross-K/V per decoder layer (GEMM + f16
+    cast); per decoder step 1 embed + 1 first LayerNorm + 12 per layer (qkv GEMV, self
+    attention, o GEMV, LayerNorm, cross-q GEMV, cross attention, cross-o GEMV,
+    LayerNorm, fc1 GEMV, GELU + quantize, fc2 GEMV, LayerNorm) + logits + argmax +
+    position advance; 1 token fill per prompt step."""
+    enc = 3 + 4 + batch + n_enc * 13 + 1 + 2 * n_dec
     steps = n_prompt + n_new - 1
-    return enc + steps * (1 + 8 * n_dec + 3 + 1) + n_prompt
+    return enc + steps * (1 + 1 + 12 * n_dec + 2 + 1) + n_prompt
 
 
 def rtfx_cpu_baseline(seconds_budget: float = 20.0) -> dict:
@@ -750,11 +754,11 @@ def qwen_launches_per_batch(n_layers: int, n_new: int, n_tok: int = 390) -> int:
     """Kernel launches of one oasr_b200_qwen_generate (counted from model_qwen.cu):
     prefill = first RMSNorm + per layer (q|k|v, o, gate|up and down GEMMs, q/k-norm +
     RoPE + KV write, attention, quantize, RMSNorm, SwiGLU = 10; the tensor-core attention
-    of 64+ rows adds 3 f16 staging kernels and, when n_tok % 8, a pad kernel) less the last
-    layer's trailing RMSNorm + head (RMSNorm, logits, argmax) + 1 advance; decode step =
-    embed + RMSNorm + 9 per layer + logits + argmax + advance; the causal mask is built
-    once per prompt length."""
-    attn_extra = (3 + (1 if n_tok % 8 else 0)) if n_tok >= 64 else 0
+    of 64+ rows adds its 3 f16 staging kernels) less the last layer's trailing RMSNorm +
+    head (RMSNorm, logits, argmax) + 1 advance; decode step = embed + RMSNorm + 9 per
+    layer + logits + argmax + advance (equal to the committed launch list); the causal
+    mask is built once per prompt length."""
+    attn_extra = 3 if n_tok >= 64 else 0
     prefill = 1 + (10 + attn_extra) * n_layers - 1 + 3 + 1
     step = 2 + 9 * n_layers + 3
     return prefill + (n_new - 1) * step
