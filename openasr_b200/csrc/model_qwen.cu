@@ -47,6 +47,9 @@ struct QLayer {
 
 struct oasr_qwen {
     oasr_backend *be;
+    // scratch the captured decode step needs (reserved at load, and again before a
+    // capture if the memory API's trim released it: scratch cannot grow during capture)
+    size_t step_scratch;
     oasr_qwen_config cfg;
     cudaStream_t stream;
     int d, H, HKV, D, ffn, qw, kvw, P, B, Tmax;
@@ -355,6 +358,11 @@ int run_decode_step(oasr_qwen *m, int n) {
 
 int decode_step_graph(oasr_qwen *m, int n) {
     oasr_backend *be = m->be;
+    if (be->scratch_bytes < m->step_scratch) {
+        int st = 0;
+        oasr_internal_scratch(be, m->step_scratch, &st);
+        if (st) return st;
+    }
     // re-capture when the batch changes or the backend's scratch (which the graph's
     // attention partials and argmax records live in) was reallocated since the capture
     if (m->graph && (m->graph_batch != n || m->graph_epoch != be->scratch_epoch)) {
@@ -559,7 +567,8 @@ int oasr_b200_qwen_load(oasr_backend *be, const oasr_qwen_config *cfg, const oas
     L_TRY(qalloc(m, &m->history, (size_t)B * P * 4));
     // flash-decode partials for the largest split configuration of a decode step,
     // reserved now so that no step (and no graph capture) has to grow the scratch
-    L_TRY(oasr_b200_reserve_scratch(be, (size_t)std::max<int64_t>(64ll << 20, (int64_t)B * m->H * 16 * (D + 2) * 4)));
+    m->step_scratch = (size_t)std::max<int64_t>(64ll << 20, (int64_t)B * m->H * 16 * (D + 2) * 4);
+    L_TRY(oasr_b200_reserve_scratch(be, m->step_scratch));
 #undef L_TRY
     *out = m;
     return OASR_STATUS_SUCCESS;

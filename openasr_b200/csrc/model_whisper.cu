@@ -51,6 +51,9 @@ struct DecLayer {
 
 struct oasr_whisper {
     oasr_backend *be;
+    // scratch the captured decode step needs (reserved at load, and again before a
+    // capture if the memory API's trim released it: scratch cannot grow during capture)
+    size_t step_scratch;
     oasr_whisper_config cfg;
     cudaStream_t stream;
     int d, H, ffn, K1p, K2p, T_enc, B;
@@ -367,6 +370,11 @@ __global__ void fill_tokens_kernel(int *tokens, int n, int value) {
 
 int decode_step_graph(oasr_whisper *m, int n) {
     oasr_backend *be = m->be;
+    if (be->scratch_bytes < m->step_scratch) {
+        int st = 0;
+        oasr_internal_scratch(be, m->step_scratch, &st);
+        if (st) return st;
+    }
     // re-capture when the batch changes or the backend's scratch (which the graph's
     // attention partials and argmax records live in) was reallocated since the capture
     if (m->graph && (m->graph_batch != n || m->graph_epoch != be->scratch_epoch)) {
@@ -629,7 +637,8 @@ int oasr_b200_whisper_load(oasr_backend *be, const oasr_whisper_config *cfg, con
     L_TRY(dalloc(m, &m->nkv, 4));
     L_TRY(dalloc(m, &m->history, (size_t)B * P * 4));
     // flash-decode partials for the largest split configuration seen by a decoder step
-    L_TRY(oasr_b200_reserve_scratch(be, (size_t)std::max<int64_t>(64ll << 20, (int64_t)B * m->H * 1024 * 66 * 4)));
+    m->step_scratch = (size_t)std::max<int64_t>(64ll << 20, (int64_t)B * m->H * 1024 * 66 * 4);
+    L_TRY(oasr_b200_reserve_scratch(be, m->step_scratch));
 #undef L_TRY
     *out = m;
     return OASR_STATUS_SUCCESS;

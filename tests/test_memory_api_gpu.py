@@ -138,3 +138,30 @@ def test_quarantine_poisons_the_backend(fresh_backend):
     assert W is None
     # trim still releases memory on a quarantined backend
     be.memory_trim()
+
+
+@pytest.mark.gpu
+def test_model_drivers_recover_after_trim(fresh_backend):
+    """trim releases the scratch that the drivers' captured decode steps point into:
+    the next generation reserves it again before re-capturing (scratch cannot grow
+    during a capture) and gives the same tokens."""
+    from openasr_b200 import models as om
+
+    be = fresh_backend
+    wcfg = om.WHISPER_TINY.replace(max_batch=2)
+    wm = om.WhisperModel(be, wcfg, om.whisper_synthetic_pack(wcfg, seed=0x0A5A0001))
+    qcfg = om.QWEN3_ASR_0_6B.replace(n_layers=1, n_vocab=4096, max_pos=256, max_prefill=64, max_batch=2)
+    qm = om.QwenModel(be, qcfg, om.qwen_synthetic_pack(qcfg, seed=0x0A5A0003))
+    try:
+        clip = [om.synthetic_audio(0x0A5A1000, 16000 * 8)]
+        emb = om.qwen_synthetic_prefix(0x0A5A3000, 2, 40, qcfg.d_model)
+        w_before, q_before = wm.transcribe(clip, n_new=12), qm.generate(emb, n_new=12)
+        be.memory_trim()
+        assert _stats(be)[0].backend_owned_workspace_bytes == 0
+        w_after, q_after = wm.transcribe(clip, n_new=12), qm.generate(emb, n_new=12)
+        np.testing.assert_array_equal(w_before, w_after)
+        np.testing.assert_array_equal(q_before, q_after)
+    finally:
+        qm.close()
+        wm.close()
+
