@@ -48,8 +48,14 @@ def test_stats_follow_uploads_and_frees(fresh_backend):
     assert dev0.device_used_bytes + dev0.device_free_bytes == dev0.total_bytes
     assert pin0.flags & bk.STATS_BUDGET_UNAVAILABLE
     wq = oo.quantize(ob.Q8_0, oo.synth_normal(3, 512 * 1024, 0.0, 0.02).reshape(512, 1024))
+    # the quote of this import bounds what the upload then adds to the device
+    _, (dclaim, hclaim) = be.memory_quote([be.memory_request(bk.REQUEST_HOST_IMPORT, wq.nbytes, usage=1)])
+    assert dclaim.domain.kind == bk.DOMAIN_DEVICE_LOCAL and hclaim.domain.kind == bk.DOMAIN_HOST_PINNED
     W = be.upload_weight(wq, ob.Q8_0, [1024, 512])
     dev1, pin1 = _stats(be)
+    grown = dev1.backend_owned_live_bytes - dev0.backend_owned_live_bytes
+    assert grown <= dclaim.retained_after_use_upper_bytes <= dclaim.commit_peak_extra_upper_bytes
+    assert hclaim.committed_after_upper_bytes == pin1.backend_owned_live_bytes
     assert dev1.generation > dev0.generation
     assert dev1.allocation_count > dev0.allocation_count
     assert dev1.backend_owned_live_bytes - dev0.backend_owned_live_bytes == be.mem_stats()["weight_bytes"]
