@@ -687,6 +687,17 @@ def run_kernels(args) -> None:
             us = timed(lambda i: be.mul_mat_qact(w, qa, Mp, y), 10)
             add("mmq_q80_tc_kernel", f"prefill Q8_0 N={N} K={K} M={Mp}", us, 2.0 * Mp * N * K, "TFLOP/s")
             del w, x, qa, y
+        # Q4_0 on the same kernel (its nibbles expanded to int8 at upload), one configs[1] shape
+        N, K, Mp = 4096, 1024, 1500
+        w = be.upload_weight(ob.quantize(ob.Q4_0, ob.synth_normal(0xF4 + N + K, N * K, 0.0, 0.02).reshape(N, K)),
+                             ob.Q4_0, [K, N])
+        x = torch.randn(Mp, K, device="cuda")
+        qa = torch.empty(be.act_bytes(ob.Q4_0, K, Mp), dtype=torch.uint8, device="cuda")
+        be.quantize_act(ob.Q4_0, x, qa)
+        y = torch.empty(Mp, N, device="cuda")
+        us = timed(lambda i: be.mul_mat_qact(w, qa, Mp, y), 10)
+        add("mmq_q80_tc_kernel (Q4_0 expanded)", f"prefill Q4_0 N={N} K={K} M={Mp}", us, 2.0 * Mp * N * K, "TFLOP/s")
+        del w, x, qa, y
         # encoder self-attention: f16 pre-pass + tcgen05 flash attention
         qkv = torch.randn(B, T, 3 * d, device="cuda")
         qe = qkv[:, :, :d].reshape(B, T, H, 64).permute(0, 2, 1, 3)

@@ -420,12 +420,18 @@ int oasr_b200_weight_upload(oasr_backend *be, const void *host, size_t bytes, in
     }
     w->tiles = nullptr;
     w->dT = nullptr;
+    w->qs8 = nullptr;
     if (e == cudaSuccess && mmq_q80_tc_supported(type, ne[1], ne[0])) {
+        // the tensor-core GEMM's operands: block-major f32 scales, and for Q4_0 the quants
+        // expanded to int8 (the GEMM then runs as Q8_0 on them, bit for bit the Q4_0 dot)
         const size_t db = (size_t)(ne[2] * ne[3] * (ne[0] / 32) * ne[1]) * sizeof(float);
+        const size_t qb = type == OASR_TYPE_Q4_0 ? (size_t)(rows * ne[0]) : 0;
         e = cudaMalloc(&w->dT, db);
         if (e == cudaSuccess) e = build_q80_scales_t(w, be->stream);
+        if (e == cudaSuccess && qb) e = cudaMalloc(&w->qs8, qb);
+        if (e == cudaSuccess && qb) e = build_q40_expanded(w, be->stream);
         if (e == cudaSuccess) e = cudaStreamSynchronize(be->stream);
-        if (e == cudaSuccess) w->device_bytes += db;
+        if (e == cudaSuccess) w->device_bytes += db + qb;
     }
     if (e == cudaSuccess && be->decode_tiles && mmv_tiles_supported(type, ne[0])) {
         // decode-tile copy for the tensor-core GEMV, built on the device from the planes above
@@ -440,6 +446,7 @@ int oasr_b200_weight_upload(oasr_backend *be, const void *host, size_t bytes, in
         if (w->d) cudaFree(w->d);
         if (w->tiles) cudaFree(w->tiles);
         if (w->dT) cudaFree(w->dT);
+        if (w->qs8) cudaFree(w->qs8);
         delete w;
         oasr_internal_mem_event(be, false);
         return oasr_internal_cuda_fail(be, e, "weight_upload", __LINE__);
@@ -464,6 +471,7 @@ int oasr_b200_weight_free(oasr_backend *be, oasr_weight *w) {
     if (w->d) cudaFree(w->d);
     if (w->tiles) cudaFree(w->tiles);
     if (w->dT) cudaFree(w->dT);
+    if (w->qs8) cudaFree(w->qs8);
     delete w;
     return OASR_STATUS_SUCCESS;
 }

@@ -49,7 +49,8 @@ struct oasr_weight {
     int64_t qs_row_bytes;    // bytes per row in the qs plane
     int64_t d_row_elems;     // fp16 scales per row in the d plane
     uint8_t *tiles;          // decode-tile copy for the tensor-core GEMV (Q4_K, Q8_0), or null
-    float *dT;               // Q8_0: block-major f32 scales [slices][K/32][N] for the tensor-core GEMM, or null
+    float *dT;               // Q8_0 / Q4_0: block-major f32 scales [slices][K/32][N] for the tensor-core GEMM, or null
+    int8_t *qs8;             // Q4_0: the quants expanded to int8 (q - 8) [slices][N][K] for that GEMM, or null
     uint64_t device_bytes;
 };
 

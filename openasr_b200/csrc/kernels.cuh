@@ -82,6 +82,7 @@ int launch_mmv_float(oasr_backend *be, const oasr_weight *w, int64_t slice, cons
 // prefill / encoder GEMM (M > 8); Q8_0 on tcgen05 needs the block-major scale copy
 bool mmq_q80_tc_supported(int type, int64_t N, int64_t K);
 cudaError_t build_q80_scales_t(oasr_weight *w, cudaStream_t st);
+cudaError_t build_q40_expanded(oasr_weight *w, cudaStream_t st);  // w->qs8 from a Q4_0 weight's nibble plane
 int launch_mmq(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int64_t M, int K,
                float *y, int64_t y_ld);
 

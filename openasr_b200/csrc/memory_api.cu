@@ -122,12 +122,13 @@ uint32_t price(const oasr_backend *be, const oasr_memory_request_v1 *req, uint32
         const oasr_memory_request_v1 &r = req[i];
         const uint64_t b = r.requested_bytes;
         if (r.kind == OASR_MEMORY_REQUEST_BUFFER || r.kind == OASR_MEMORY_REQUEST_HOST_IMPORT) {
-            // an engine buffer: one allocation; an imported weight: its planes, decode
-            // tiles and (Q8_0) transposed f32 scales -- 2.12 x the raw bytes for Q8_0
-            // (1 + 1 + 4/34), 2.03 x for Q4_K -- bounded by 2.5 x, plus the raw copy
-            // the plane split reads while it runs
+            // an engine buffer: one allocation; an imported weight: its planes and the
+            // copies the kernels read -- decode tiles and transposed f32 scales for Q8_0
+            // (2.12 x the raw bytes), decode tiles for Q4_K (2.03 x), the int8 expansion
+            // and transposed scales for Q4_0 (1 + 32/18 + 4/18 = 3.0 x) -- bounded by 3 x,
+            // plus the raw copy the plane split reads while it runs
             const uint64_t resident = r.kind == OASR_MEMORY_REQUEST_BUFFER ? round_up(b, kDeviceGranularity)
-                                                                            : round_up(b * 5 / 2, kDeviceGranularity);
+                                                                            : round_up(3 * b, kDeviceGranularity);
             const uint64_t temp = r.kind == OASR_MEMORY_REQUEST_HOST_IMPORT ? round_up(b, kDeviceGranularity) : 0;
             oasr_memory_claim_v1 &c = out[k++];
             init_claim(c, be, r, OASR_MEMORY_DOMAIN_DEVICE_LOCAL);

@@ -530,8 +530,33 @@ cudaError_t build_q80_scales_t(oasr_weight *w, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+// Q4_0 runs on the same kernel: ggml's Q4_0 x q8_0 block dot is the integer dot of the
+// nibbles minus 8 with the q8_0 quants, scaled like Q8_0's ((float)isum * (d_w * d_a)), so
+// the nibbles expanded to int8 at upload are a Q8_0 quant plane with the same scales
 bool mmq_q80_tc_supported(int type, int64_t N, int64_t K) {
-    return type == OASR_TYPE_Q8_0 && K % q80::BK == 0 && N % 4 == 0;
+    return (type == OASR_TYPE_Q8_0 || type == OASR_TYPE_Q4_0) && K % q80::BK == 0 && N % 4 == 0;
+}
+
+// Q4_0 nibble plane [rows][K/2] (ggml order: byte j of a block holds elements j and j + 16
+// in its low and high nibble) -> int8 (q - 8) [rows][K]; one thread per block
+__global__ void q40_expand_kernel(const uint8_t *qs, int64_t nblocks, int64_t nb, int64_t qs_row, int8_t *q8) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nblocks; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / nb, b = i - r * nb;
+        const uint8_t *src = qs + r * qs_row + b * 16;
+        int8_t *dst = q8 + (r * nb + b) * 32;
+        for (int j = 0; j < 16; ++j) {
+            const int v = src[j];
+            dst[j] = (int8_t)((v & 0xF) - 8);
+            dst[j + 16] = (int8_t)((v >> 4) - 8);
+        }
+    }
+}
+
+cudaError_t build_q40_expanded(oasr_weight *w, cudaStream_t st) {
+    const int64_t nb = w->ne[0] / 32, rows = w->ne[1] * w->ne[2] * w->ne[3], nblocks = rows * nb;
+    const unsigned grid = (unsigned)std::min<int64_t>((nblocks + 255) / 256, 65535);
+    q40_expand_kernel<<<grid, 256, 0, st>>>(w->qs, nblocks, nb, w->qs_row_bytes, w->qs8);
+    return cudaGetLastError();
 }
 
 // ---- host side ----------------------------------------------------------------------------
@@ -592,8 +617,12 @@ static int launch_q80_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, 
     int st = encode_2d(be, &map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.qs, K, M, (uint64_t)K, 128, 128,
                        CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
-    st = encode_2d(be, &map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->qs + slice * N * w->qs_row_bytes, K, N,
-                   (uint64_t)w->qs_row_bytes, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    // Q8_0: the quant plane; Q4_0: its int8 expansion (rows of K bytes)
+    const bool q40 = w->type == OASR_TYPE_Q4_0;
+    const uint8_t *wq = q40 ? (const uint8_t *)w->qs8 : w->qs;
+    const int64_t wrow = q40 ? (int64_t)K : w->qs_row_bytes;
+    st = encode_2d(be, &map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, wq + slice * N * wrow, K, N, (uint64_t)wrow, 128, 128,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
     // weight scales, block-major f32 [K/32][N]: 128 weight rows x 4 blocks per box
     st = encode_2d(be, &map_dw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->dT + slice * (int64_t)(K / 32) * N, N, K / 32,
@@ -614,7 +643,8 @@ int launch_mmq(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActP
                float *y, int64_t y_ld) {
     const bool k_family = w->type == OASR_TYPE_Q4_K;
     if (k_family && a.qs16 && a.bs16h) return launch_q4k_tc(be, w, slice, a, M, K, y, y_ld);
-    if (w->dT && (y_ld & 3) == 0) return launch_q80_tc(be, w, slice, a, M, K, y, y_ld);
+    if (w->dT && (w->type == OASR_TYPE_Q8_0 || w->qs8) && (y_ld & 3) == 0)
+        return launch_q80_tc(be, w, slice, a, M, K, y, y_ld);
     const int family = k_family ? FAMILY_Q8_K : FAMILY_Q8_0;
     for (int64_t m0 = 0; m0 < M; m0 += 8) {
         const int mc = (int)std::min<int64_t>(8, M - m0);

@@ -281,6 +281,19 @@ def test_dp4a_decode_gemv_still_matches_oracle():
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K", [(9, 128, 128), (300, 1280, 1280), (1500, 1024, 3072), (77, 4096, 1024)])
+def test_q4_0_tensor_core_gemm_is_bit_exact(gpu_backend, M, N, K):
+    """Q4_0 at M > 8 runs the tcgen05 kind::i8 GEMM on its nibbles expanded to int8 at
+    upload (q - 8, ggml's element order) with its own scales: ggml's Q4_0 x q8_0 block dot
+    is that integer dot scaled like Q8_0's, so the result equals the oracle bit for bit."""
+    wq = _weights(N, K, ob.Q4_0, 0x0A5A001C + M)
+    x = oo.synth_normal(0x0A5A001D + N, M * K).reshape(M, K)
+    got = _run(gpu_backend, wq, ob.Q4_0, N, K, x)
+    ref = oo.mul_mat(wq, ob.Q4_0, K, N, x)
+    np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("M,N,K", [(9, 128, 128), (128, 256, 384), (300, 1280, 1280), (1500, 1152, 384),
                                    (200, 200, 1536), (77, 4096, 1024)])
 def test_q8_0_tensor_core_gemm_is_bit_exact(gpu_backend, M, N, K):
