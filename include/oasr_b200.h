@@ -253,7 +253,9 @@ int oasr_b200_argmax_first(oasr_backend *be, const oasr_tensor *logits, oasr_ten
  * stream and releases the activation scratch and the staging buffers (graphs
  * captured before must be re-captured: the model drivers do so themselves).
  * quarantine poisons the backend (later calls: OASR_STATUS_BACKEND_POISONED) and
- * records the reason; stats then report health QUARANTINED. */
+ * records the reason; stats then report health QUARANTINED.  Like every other call on
+ * a backend, these come from one thread at a time per backend (the last quote issued
+ * and the generation are per-backend state). */
 #define OASR_MEMORY_ABI_V1 1u
 enum {
     OASR_MEMORY_DOMAIN_DEVICE_LOCAL = 1, OASR_MEMORY_DOMAIN_HOST_PAGEABLE = 2, OASR_MEMORY_DOMAIN_HOST_PINNED = 3,
