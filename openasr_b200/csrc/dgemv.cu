@@ -30,6 +30,7 @@ constexpr int DG_SMEM_MAX = 200 << 10;
 struct DgemvArgs {
     const uint8_t *tiles;
     int units;  // super-blocks (Q4_K) or block pairs (Q8_0) per row
+    int terms_bytes;  // shared memory of one segment of block terms
     int64_t N;
     int K, M;
     // PRO_PLANES: quantized activations (family of the weight)
@@ -58,17 +59,29 @@ static __device__ __forceinline__ void ld8(const float *p, float (&v)[8]) {
 
 // ---- PRO_QUANT: f32 rows -> shared q8 planes ----------------------------------------------------
 struct DgSmem {
-    int8_t *aq;   // [8][K + 32]
-    float *ad;    // [8][nd]
-    int16_t *ab;  // [8][K / 16] (q8_K)
-    float *red;   // [8][32][4]
+    int8_t *aq;     // [8][K + 32]
+    float *ad;      // [8][nd]
+    int16_t *ab;    // [8][K / 16] (q8_K)
+    float *terms;   // one segment of block terms (mma_frag.cuh)
     int aq_ld, nd;
 };
 
+// block terms per unit (Q4_K: one super-block; Q8_0: a block pair) and rounds per segment
+template <int FAM>
+struct DgTerms {
+    static constexpr int BPU = FAM == FAMILY_Q8_K ? 1 : 2;
+    static constexpr int SEGJ = TERM_SEG_BLOCKS / (DG_WARPS * BPU);
+};
+
+static inline size_t dg_terms_bytes(int fam, int units) {
+    return fam == FAMILY_Q8_K ? term_smem_bytes<DG_WARPS, 1, DgTerms<FAMILY_Q8_K>::SEGJ>(units)
+                              : term_smem_bytes<DG_WARPS, 2, DgTerms<FAMILY_Q8_0>::SEGJ>(units);
+}
+
 static __host__ __device__ inline size_t dg_align16(size_t x) { return (x + 15) & ~(size_t)15; }
 
-static __host__ __device__ inline size_t dg_smem_bytes(int fam, int pro, int K) {
-    size_t b = (size_t)DG_WARPS * 32 * 4 * 4;  // reduction
+static inline size_t dg_smem_bytes(int fam, int pro, int K) {
+    size_t b = dg_align16(dg_terms_bytes(fam, fam == FAMILY_Q8_K ? K / 256 : K / 64));
     if (pro == PRO_QUANT) {
         const int nd = fam == FAMILY_Q8_K ? K / 256 : K / 32;
         b += dg_align16((size_t)DG_ROWS * (K + 32)) + dg_align16((size_t)DG_ROWS * nd * 4);
@@ -77,10 +90,11 @@ static __host__ __device__ inline size_t dg_smem_bytes(int fam, int pro, int K) 
     return b;
 }
 
-static __device__ inline DgSmem dg_carve(char *base, int fam, int pro, int K) {
+// terms first (their size is the launch's: rounds of the segment), the planes after them
+static __device__ inline DgSmem dg_carve(char *base, int fam, int pro, int K, size_t terms_bytes) {
     DgSmem s;
-    s.red = (float *)base;
-    size_t off = (size_t)DG_WARPS * 32 * 4 * 4;
+    s.terms = (float *)base;
+    size_t off = terms_bytes;
     s.aq_ld = K + 32;
     s.nd = fam == FAMILY_Q8_K ? K / 256 : K / 32;
     s.aq = nullptr;
@@ -132,9 +146,10 @@ static __device__ void pro_quant(const DgemvArgs &a, const DgSmem &sm, int warp,
 template <int FAM, int PRO, int EPI, int UPW>
 __global__ void __launch_bounds__(DG_WARPS * 32, 2) dgemv_kernel(DgemvArgs a) {
     extern __shared__ __align__(16) char dg_smem[];
+    constexpr int BPU = DgTerms<FAM>::BPU, SEGJ = DgTerms<FAM>::SEGJ;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const DgSmem sm = dg_carve(dg_smem, FAM, PRO, a.K);
+    const DgSmem sm = dg_carve(dg_smem, FAM, PRO, a.K, a.terms_bytes);
     constexpr int UNIT = FAM == FAMILY_Q8_K ? Q4K_UNIT : Q80_UNIT;
     const uint8_t *tile = a.tiles + (int64_t)blockIdx.x * a.units * UNIT;
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -144,7 +159,6 @@ __global__ void __launch_bounds__(DG_WARPS * 32, 2) dgemv_kernel(DgemvArgs a) {
     constexpr int NU = UPW > 0 ? UPW : 1;
     Q4kUnit ck[FAM == FAMILY_Q8_K ? NU : 1], nk;
     Q80Unit c8[FAM == FAMILY_Q8_K ? 1 : NU], n8;
-    int u = warp;
     if (UPW > 0) {
 #pragma unroll
         for (int j = 0; j < NU; ++j) {
@@ -157,9 +171,9 @@ __global__ void __launch_bounds__(DG_WARPS * 32, 2) dgemv_kernel(DgemvArgs a) {
     } else {
         // the whole tile streams toward L2 while the first units load into registers
         if (threadIdx.x == 0) prefetch_l2_bulk(tile, (uint32_t)a.units * UNIT);
-        if (u < a.units) {
-            if (FAM == FAMILY_Q8_K) load_q4k_unit(ck[0], tile + (int64_t)u * UNIT, lane, g);
-            else load_q80_unit(c8[0], tile + (int64_t)u * UNIT, lane, g);
+        if (warp < a.units) {
+            if (FAM == FAMILY_Q8_K) load_q4k_unit(ck[0], tile + (int64_t)warp * UNIT, lane, g);
+            else load_q80_unit(c8[0], tile + (int64_t)warp * UNIT, lane, g);
         }
     }
     griddep_wait();
@@ -184,36 +198,45 @@ __global__ void __launch_bounds__(DG_WARPS * 32, 2) dgemv_kernel(DgemvArgs a) {
         adrow0 = m0 < a.M ? a.in.d + (int64_t)m0 * nd : nullptr;
         adrow1 = m1 < a.M ? a.in.d + (int64_t)m1 * nd : nullptr;
     }
+    // one unit's block terms into its segment slot
+    auto terms_of = [&](int j, int uj, const Q4kUnit &qk, const Q80Unit &q8) {
+        float *slot = term_slot<DG_WARPS, BPU, SEGJ>(sm.terms, j, warp);
+        if (FAM == FAMILY_Q8_K) {
+            const float da0 = adrow0 ? (SM ? adrow0[uj] : __ldg(adrow0 + uj)) : 0.0f;
+            const float da1 = adrow1 ? (SM ? adrow1[uj] : __ldg(adrow1 + uj)) : 0.0f;
+            q4k_unit_terms<SM>(slot, qk, uj, arow, brow, da0, da1, lane, t);
+        } else {
+            q80_unit_terms<SM>(slot, q8, uj, arow, adrow0, adrow1, lane, t);
+        }
+    };
+    const int nrounds = (a.units + DG_WARPS - 1) / DG_WARPS;
     if (UPW > 0) {
 #pragma unroll
         for (int j = 0; j < NU; ++j) {
+            if (j >= nrounds) break;  // CTA-uniform
             const int uj = warp + j * DG_WARPS;
-            if (uj >= a.units) break;
-            if (FAM == FAMILY_Q8_K) {
-                const float da0 = adrow0 ? (SM ? adrow0[uj] : __ldg(adrow0 + uj)) : 0.0f;
-                const float da1 = adrow1 ? (SM ? adrow1[uj] : __ldg(adrow1 + uj)) : 0.0f;
-                q4k_unit_accumulate<SM>(acc, ck[j], uj, arow, brow, da0, da1, t);
-            } else {
-                q80_unit_accumulate<SM>(acc, c8[j], uj, arow, adrow0, adrow1, t);
-            }
+            if (uj < a.units) terms_of(j, uj, ck[FAM == FAMILY_Q8_K ? j : 0], c8[FAM == FAMILY_Q8_K ? 0 : j]);
+            segment_end<DG_WARPS, BPU, SEGJ>(acc, sm.terms, j, nrounds, a.units, warp, lane);
         }
     } else {
-        for (; u < a.units; u += DG_WARPS) {
-            const bool more = u + DG_WARPS < a.units;
-            if (FAM == FAMILY_Q8_K) {
-                if (more) load_q4k_unit(nk, tile + (int64_t)(u + DG_WARPS) * UNIT, lane, g);
-                const float da0 = adrow0 ? (SM ? adrow0[u] : __ldg(adrow0 + u)) : 0.0f;
-                const float da1 = adrow1 ? (SM ? adrow1[u] : __ldg(adrow1 + u)) : 0.0f;
-                q4k_unit_accumulate<SM>(acc, ck[0], u, arow, brow, da0, da1, t);
-                if (more) ck[0] = nk;
-            } else {
-                if (more) load_q80_unit(n8, tile + (int64_t)(u + DG_WARPS) * UNIT, lane, g);
-                q80_unit_accumulate<SM>(acc, c8[0], u, arow, adrow0, adrow1, t);
-                if (more) c8[0] = n8;
+        for (int j = 0; j < nrounds; ++j) {
+            const int u = j * DG_WARPS + warp;
+            if (u < a.units) {
+                const bool more = u + DG_WARPS < a.units;
+                if (FAM == FAMILY_Q8_K) {
+                    if (more) load_q4k_unit(nk, tile + (int64_t)(u + DG_WARPS) * UNIT, lane, g);
+                    terms_of(j, u, ck[0], c8[0]);
+                    if (more) ck[0] = nk;
+                } else {
+                    if (more) load_q80_unit(n8, tile + (int64_t)(u + DG_WARPS) * UNIT, lane, g);
+                    terms_of(j, u, ck[0], c8[0]);
+                    if (more) c8[0] = n8;
+                }
             }
+            segment_end<DG_WARPS, BPU, SEGJ>(acc, sm.terms, j, nrounds, a.units, warp, lane);
         }
     }
-    if (!reduce_warps<DG_WARPS>(acc, sm.red, warp, lane)) return;
+    if (warp != 0) return;
 
     const int64_t ra = (int64_t)blockIdx.x * TILE_ROWS + g, rb = ra + 8;
     {
@@ -279,9 +302,11 @@ int dgemv_configure(oasr_backend *be) {
 }
 
 template <int FAM, int PRO, int EPI>
-static int dg_launch(oasr_backend *be, const DgemvArgs &a) {
+static int dg_launch(oasr_backend *be, const DgemvArgs &a0) {
     if (be->device < 0 || be->device >= 64 || !g_dg_configured[be->device])
         return oasr_internal_fail(be, OASR_STATUS_FAILED, "dgemv: dgemv_configure was not called on this device");
+    DgemvArgs a = a0;
+    a.terms_bytes = (int)dg_align16(dg_terms_bytes(FAM, a.units));
     const size_t smem = dg_smem_bytes(FAM, PRO, a.K);
     const unsigned grid = (unsigned)((a.N + TILE_ROWS - 1) / TILE_ROWS);
     // all of a warp's units in flight at once, up to 4 (Q8_0) or 1 (Q4_K) per warp, else looping

@@ -8,9 +8,11 @@
 // Rounding follows ggml's CPU ops (nn/decoder.rs, whisper/ggml_executor.rs call
 // ggml_norm, ggml_rms_norm, ggml_mul, ggml_add, ggml_gelu, ggml_silu): norms sum
 // in double, every add/mul rounds separately (no FMA contraction), GELU reads
-// the same fp16 table ggml builds, and quantization matches quant_act.cu.
+// the same fp16 table ggml builds, SiLU's e^x is the decode path's exp_f32
+// (fmath.cuh), and quantization matches quant_act.cu.
 #include <math.h>
 
+#include "fmath.cuh"
 #include "kernels.cuh"
 #include "model.cuh"
 
@@ -189,7 +191,7 @@ __global__ void swiglu_quant_kernel(const float *gu, int n, int64_t gu_ld, float
     const int64_t r = blockIdx.x;
     const float *g = gu + r * gu_ld, *u = g + n;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float s = __fdiv_rn(g[i], __fadd_rn(1.0f, expf(-g[i])));
+        const float s = __fdiv_rn(g[i], __fadd_rn(1.0f, exp_f32(-g[i])));
         const float v = __fmul_rn(s, u[i]);
         srow[i] = v;
         if (out_f32) out_f32[r * n + i] = v;
@@ -556,7 +558,7 @@ __global__ void swiglu_quant_chunks_kernel(const float *gu, int n, int64_t gu_ld
     ldE<E>(gu + r * gu_ld + k0, g);
     ldE<E>(gu + r * gu_ld + n + k0, u);
 #pragma unroll
-    for (int i = 0; i < E; ++i) v[i] = __fmul_rn(__fdiv_rn(g[i], __fadd_rn(1.0f, expf(-g[i]))), u[i]);
+    for (int i = 0; i < E; ++i) v[i] = __fmul_rn(__fdiv_rn(g[i], __fadd_rn(1.0f, exp_f32(-g[i]))), u[i]);
     if (out_f32) stE<E>(out_f32 + r * n + k0, v);
     if (q.qs) quant_chunk<E>(v, r, n, k0, lane, q);
 }

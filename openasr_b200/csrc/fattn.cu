@@ -23,6 +23,7 @@
 #include <string>
 
 #include "kernels.cuh"
+#include "fmath.cuh"
 #include "quant_warp.cuh"
 
 namespace oasr {
@@ -117,6 +118,8 @@ static __device__ __forceinline__ void stage_l2(float *dst, const float *src, in
 constexpr int FA_HEADS_U = 8;            // KV positions per warp load batch (double buffered)
 constexpr int FA_HEADS_MAX_SPLITS = 16;  // most KV splits of one query row (partials staged by the merging CTA)
 constexpr int FA_GQA_U = 2;              // KV positions per lane group and load batch (double buffered)
+constexpr int FA_SPLITS_HEADS = 7;       // KV splits of the 4-head decode kernel
+constexpr int FA_SPLITS_GQA = 4;         // KV splits of the GQA decode kernel
 
 template <int D, int QT, bool F16>
 __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
@@ -218,23 +221,23 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
             float d = 0.0f;
             if (pv) {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) d = fmaf(qv[t][e], kf[e], d);
+                for (int e = 0; e < 8; ++e) d = __fmaf_rn(qv[t][e], kf[e], d);
             }
 #pragma unroll
-            for (int o = LPP / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+            for (int o = LPP / 2; o > 0; o >>= 1) d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, o));
             if (!pv || !qvalid[t]) continue;
-            float sc = d * a.scale;
+            float sc = __fmul_rn(d, a.scale);
             if (mrow[t]) {
                 const float mv = __half2float(*reinterpret_cast<const __half *>(mrow[t] + (int64_t)p * a.m_nb0));
                 if (mv == -INFINITY) continue;
-                sc += mv;
+                sc = __fadd_rn(sc, mv);
             }
             const float mnew = fmaxf(mx[t], sc);
-            const float corr = expf(mx[t] - mnew);  // mx = -inf -> 0
-            const float w = expf(sc - mnew);
-            sm[t] = sm[t] * corr + w;
+            const float corr = exp_f32(__fsub_rn(mx[t], mnew));  // mx = -inf -> 0
+            const float w = exp_f32(__fsub_rn(sc, mnew));
+            sm[t] = __fmaf_rn(sm[t], corr, w);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) acc[t][e] = fmaf(w, vf[e], acc[t][e] * corr);
+            for (int e = 0; e < 8; ++e) acc[t][e] = __fmaf_rn(w, vf[e], __fmul_rn(acc[t][e], corr));
             mx[t] = mnew;
         }
         }
@@ -248,13 +251,13 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
             const float om = __shfl_xor_sync(0xffffffffu, mx[t], o);
             const float os = __shfl_xor_sync(0xffffffffu, sm[t], o);
             const float nm = fmaxf(mx[t], om);
-            const float f0 = mx[t] == -INFINITY ? 0.0f : expf(mx[t] - nm);
-            const float f1 = om == -INFINITY ? 0.0f : expf(om - nm);
-            sm[t] = sm[t] * f0 + os * f1;
+            const float f0 = mx[t] == -INFINITY ? 0.0f : exp_f32(__fsub_rn(mx[t], nm));
+            const float f1 = om == -INFINITY ? 0.0f : exp_f32(__fsub_rn(om, nm));
+            sm[t] = __fmaf_rn(os, f1, __fmul_rn(sm[t], f0));
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
                 const float oa = __shfl_xor_sync(0xffffffffu, acc[t][e], o);
-                acc[t][e] = acc[t][e] * f0 + oa * f1;
+                acc[t][e] = __fmaf_rn(oa, f1, __fmul_rn(acc[t][e], f0));
             }
             mx[t] = nm;
         }
@@ -283,16 +286,16 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
         float L = 0.0f, A = 0.0f;
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
-            const float f = s_m[w][t] == -INFINITY ? 0.0f : expf(s_m[w][t] - M);
-            L += s_s[w][t] * f;
-            A += s_acc[w][t][e] * f;
+            const float f = s_m[w][t] == -INFINITY ? 0.0f : exp_f32(__fsub_rn(s_m[w][t], M));
+            L = __fmaf_rn(s_s[w][t], f, L);
+            A = __fmaf_rn(s_acc[w][t][e], f, A);
         }
         const int r = qt * QT + t;
         if (r >= a.QG) continue;
         const int h = hk * a.G + r / a.NQ, iq = r % a.NQ;
         if (a.n_splits == 1) {
             float *out = reinterpret_cast<float *>(a.dst + h * a.d_nb1 + iq * a.d_nb2 + s * a.d_nb3);
-            out[e] = L == 0.0f ? 0.0f : A / L;
+            out[e] = L == 0.0f ? 0.0f : __fdiv_rn(A, L);
         } else {
             const int64_t row = ((int64_t)s * a.H + h) * a.NQ + iq;
             float *pp = a.partials + (row * a.n_splits + split) * (D + 2);
@@ -323,12 +326,12 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
             float L = 0.0f, A = 0.0f;
             for (int sp = 0; sp < a.n_splits; ++sp) {
                 const float m = s_part[sp * (D + 2) + D];
-                const float f = m == -INFINITY ? 0.0f : expf(m - M);
-                L += s_part[sp * (D + 2) + D + 1] * f;
-                A += s_part[sp * (D + 2) + e] * f;
+                const float f = m == -INFINITY ? 0.0f : exp_f32(__fsub_rn(m, M));
+                L = __fmaf_rn(s_part[sp * (D + 2) + D + 1], f, L);
+                A = __fmaf_rn(s_part[sp * (D + 2) + e], f, A);
             }
             float *out = reinterpret_cast<float *>(a.dst + h * a.d_nb1 + iq * a.d_nb2 + s * a.d_nb3);
-            out[e] = L == 0.0f ? 0.0f : A / L;
+            out[e] = L == 0.0f ? 0.0f : __fdiv_rn(A, L);
         }
     }
 }
@@ -409,7 +412,7 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
             load8<true>(reinterpret_cast<const char *>(&kr[u]), kf);
             float d = 0.0f;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) d = fmaf(qv[e], kf[e], d);
+            for (int e = 0; e < 8; ++e) d = __fmaf_rn(qv[e], kf[e], d);
             sc[u] = d;
         }
         float wv[U];
@@ -420,21 +423,21 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const float keep = b4 ? sc[j + 4] : sc[j], send = b4 ? sc[j] : sc[j + 4];
-                r4[j] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+                r4[j] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 4));
             }
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
                 const float keep = b2 ? r4[j + 2] : r4[j], send = b2 ? r4[j] : r4[j + 2];
-                r2[j] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+                r2[j] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 2));
             }
             const float keep = b1 ? r2[1] : r2[0], send = b1 ? r2[0] : r2[1];
-            const float dot = keep + __shfl_xor_sync(0xffffffffu, send, 1);  // position pb + 4 sl
-            const float s1 = pb + 4 * sl < kv1 ? dot * a.scale : -INFINITY;
+            const float dot = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 1));  // position pb + 4 sl
+            const float s1 = pb + 4 * sl < kv1 ? __fmul_rn(dot, a.scale) : -INFINITY;
             float mb = s1;
 #pragma unroll
             for (int o = 4; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
             mnew = fmaxf(mx, mb);                    // finite: position pb is valid
-            const float w1 = expf(s1 - mnew);        // invalid positions: exp(-inf) = 0
+            const float w1 = exp_f32(__fsub_rn(s1, mnew));  // invalid positions: exp(-inf) = 0
 #pragma unroll
             for (int u = 0; u < U; ++u) wv[u] = __shfl_sync(0xffffffffu, w1, (lane & ~7) | u);
         } else {
@@ -442,27 +445,27 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
             for (int u = 0; u < U; ++u) {
                 float d = sc[u];
 #pragma unroll
-                for (int o = 4; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-                sc[u] = pb + 4 * u < kv1 ? d * a.scale : -INFINITY;
+                for (int o = 4; o > 0; o >>= 1) d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, o));
+                sc[u] = pb + 4 * u < kv1 ? __fmul_rn(d, a.scale) : -INFINITY;
             }
             float mb = sc[0];
 #pragma unroll
             for (int u = 1; u < U; ++u) mb = fmaxf(mb, sc[u]);
             mnew = fmaxf(mx, mb);
 #pragma unroll
-            for (int u = 0; u < U; ++u) wv[u] = expf(sc[u] - mnew);
+            for (int u = 0; u < U; ++u) wv[u] = exp_f32(__fsub_rn(sc[u], mnew));
         }
-        const float corr = expf(mx - mnew);  // mx = -inf -> 0
-        sm *= corr;
+        const float corr = exp_f32(__fsub_rn(mx, mnew));  // mx = -inf -> 0
+        sm = __fmul_rn(sm, corr);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] *= corr;
+        for (int e = 0; e < 8; ++e) acc[e] = __fmul_rn(acc[e], corr);
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             float vf[8];
             load8<true>(reinterpret_cast<const char *>(&vr[u]), vf);
-            sm += wv[u];
+            sm = __fadd_rn(sm, wv[u]);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) acc[e] = fmaf(wv[u], vf[e], acc[e]);
+            for (int e = 0; e < 8; ++e) acc[e] = __fmaf_rn(wv[u], vf[e], acc[e]);
         }
         mx = mnew;
     };
@@ -530,13 +533,13 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
         float L = 0.0f, A = 0.0f;
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
-            const float f = s_m[w][t] == -INFINITY ? 0.0f : expf(s_m[w][t] - M);
-            L += s_s[w][t] * f;
-            A += s_acc[w][t][e] * f;
+            const float f = s_m[w][t] == -INFINITY ? 0.0f : exp_f32(__fsub_rn(s_m[w][t], M));
+            L = __fmaf_rn(s_s[w][t], f, L);
+            A = __fmaf_rn(s_acc[w][t][e], f, A);
         }
         const int hh = 4 * hg + t;
         if (a.n_splits == 1) {
-            const float val = L == 0.0f ? 0.0f : A / L;
+            const float val = L == 0.0f ? 0.0f : __fdiv_rn(A, L);
             if (a.oq) s_out[t * D + e] = val;
             else reinterpret_cast<float *>(a.dst + hh * a.d_nb1 + s * a.d_nb3)[e] = val;
         } else {
@@ -569,11 +572,11 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
         float L = 0.0f, A = 0.0f;
         for (int sp = 0; sp < a.n_splits; ++sp) {
             const float m = pp[sp * (D + 2) + D];
-            const float f = m == -INFINITY ? 0.0f : expf(m - M);
-            L += pp[sp * (D + 2) + D + 1] * f;
-            A += pp[sp * (D + 2) + e] * f;
+            const float f = m == -INFINITY ? 0.0f : exp_f32(__fsub_rn(m, M));
+            L = __fmaf_rn(pp[sp * (D + 2) + D + 1], f, L);
+            A = __fmaf_rn(pp[sp * (D + 2) + e], f, A);
         }
-        const float val = L == 0.0f ? 0.0f : A / L;
+        const float val = L == 0.0f ? 0.0f : __fdiv_rn(A, L);
         if (a.oq) s_out[t * D + e] = val;
         else reinterpret_cast<float *>(a.dst + (4 * hg + t) * a.d_nb1 + s * a.d_nb3)[e] = val;
     }
@@ -655,10 +658,10 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
             for (int g = 0; g < G; ++g) {
                 float d = 0.0f;
 #pragma unroll
-                for (int e = 0; e < 16; ++e) d = fmaf(qv[g][e], kf[e], d);
+                for (int e = 0; e < 16; ++e) d = __fmaf_rn(qv[g][e], kf[e], d);
 #pragma unroll
-                for (int o = 4; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-                sc[g][u] = valid ? d * a.scale : -INFINITY;
+                for (int o = 4; o > 0; o >>= 1) d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, o));
+                sc[g][u] = valid ? __fmul_rn(d, a.scale) : -INFINITY;
             }
         }
 #pragma unroll
@@ -668,10 +671,10 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
             for (int u = 1; u < U; ++u) mb = fmaxf(mb, sc[g][u]);
             const float mnew = fmaxf(mx[g], mb);
             if (mnew == -INFINITY) continue;      // nothing visible to this group yet
-            const float corr = expf(mx[g] - mnew);  // mx = -inf -> 0
-            sm[g] *= corr;
+            const float corr = exp_f32(__fsub_rn(mx[g], mnew));  // mx = -inf -> 0
+            sm[g] = __fmul_rn(sm[g], corr);
 #pragma unroll
-            for (int e = 0; e < 16; ++e) acc[g][e] *= corr;
+            for (int e = 0; e < 16; ++e) acc[g][e] = __fmul_rn(acc[g][e], corr);
             mx[g] = mnew;
         }
 #pragma unroll
@@ -682,10 +685,10 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
 #pragma unroll
             for (int g = 0; g < G; ++g) {
                 if (sc[g][u] == -INFINITY) continue;
-                const float w = expf(sc[g][u] - mx[g]);
-                sm[g] += w;
+                const float w = exp_f32(__fsub_rn(sc[g][u], mx[g]));
+                sm[g] = __fadd_rn(sm[g], w);
 #pragma unroll
-                for (int e = 0; e < 16; ++e) acc[g][e] = fmaf(w, vf[e], acc[g][e]);
+                for (int e = 0; e < 16; ++e) acc[g][e] = __fmaf_rn(w, vf[e], acc[g][e]);
             }
         }
     };
@@ -744,13 +747,13 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
             const float om = __shfl_xor_sync(0xffffffffu, mx[g], o);
             const float os = __shfl_xor_sync(0xffffffffu, sm[g], o);
             const float nm = fmaxf(mx[g], om);
-            const float f0 = mx[g] == -INFINITY ? 0.0f : expf(mx[g] - nm);
-            const float f1 = om == -INFINITY ? 0.0f : expf(om - nm);
-            sm[g] = sm[g] * f0 + os * f1;
+            const float f0 = mx[g] == -INFINITY ? 0.0f : exp_f32(__fsub_rn(mx[g], nm));
+            const float f1 = om == -INFINITY ? 0.0f : exp_f32(__fsub_rn(om, nm));
+            sm[g] = __fmaf_rn(os, f1, __fmul_rn(sm[g], f0));
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
                 const float oa = __shfl_xor_sync(0xffffffffu, acc[g][e], o);
-                acc[g][e] = acc[g][e] * f0 + oa * f1;
+                acc[g][e] = __fmaf_rn(oa, f1, __fmul_rn(acc[g][e], f0));
             }
             mx[g] = nm;
         }
@@ -778,13 +781,13 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
         float L = 0.0f, A = 0.0f;
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
-            const float f = s_m[w][g] == -INFINITY ? 0.0f : expf(s_m[w][g] - M);
-            L += s_s[w][g] * f;
-            A += s_acc[w][g][e] * f;
+            const float f = s_m[w][g] == -INFINITY ? 0.0f : exp_f32(__fsub_rn(s_m[w][g], M));
+            L = __fmaf_rn(s_s[w][g], f, L);
+            A = __fmaf_rn(s_acc[w][g][e], f, A);
         }
         const int h = hk * G + g;
         if (a.n_splits == 1) {
-            const float val = L == 0.0f ? 0.0f : A / L;
+            const float val = L == 0.0f ? 0.0f : __fdiv_rn(A, L);
             if (a.oq) {
                 const int64_t idx = ((int64_t)s * a.H + h) * D + e;
                 store_q8_0_warp(val, a.oq + idx, a.od + idx / 32, lane);
@@ -817,11 +820,11 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
         float L = 0.0f, A = 0.0f;
         for (int sp = 0; sp < a.n_splits; ++sp) {
             const float m = pp[sp * (D + 2) + D];
-            const float f = m == -INFINITY ? 0.0f : expf(m - M);
-            L += pp[sp * (D + 2) + D + 1] * f;
-            A += pp[sp * (D + 2) + e] * f;
+            const float f = m == -INFINITY ? 0.0f : exp_f32(__fsub_rn(m, M));
+            L = __fmaf_rn(pp[sp * (D + 2) + D + 1], f, L);
+            A = __fmaf_rn(pp[sp * (D + 2) + e], f, A);
         }
-        const float val = L == 0.0f ? 0.0f : A / L;
+        const float val = L == 0.0f ? 0.0f : __fdiv_rn(A, L);
         if (a.oq) {
             const int64_t idx = ((int64_t)s * a.H + hk * G + g) * D + e;
             store_q8_0_warp(val, a.oq + idx, a.od + idx / 32, lane);
@@ -859,38 +862,6 @@ static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const
                                    const oasr_tensor *mask, float scale, oasr_tensor *dst, const float *q_bias,
                                    const int *nkv_dev, const FaScratch *fixed, const ActPlanes *out_q8 = nullptr,
                                    int out_family = FAMILY_Q8_0, int kv_static = 0);
-
-// resident CTAs per SM of one fattn_split_kernel instantiation (same for every device of this build)
-static int split_kernel_occupancy(int D, int QT, bool f16) {
-    static int cache[2][4][2];
-    const int qi = QT == 1 ? 0 : QT == 2 ? 1 : QT == 4 ? 2 : 3;
-    int &occ = cache[D == 128][qi][f16];
-    if (occ) return occ;
-    const void *fn = nullptr;
-#define FA_OCC_FN(DD, F)                                                                         \
-    fn = qi == 0 ? (const void *)fattn_split_kernel<DD, 1, F> : qi == 1 ? (const void *)fattn_split_kernel<DD, 2, F> \
-       : qi == 2 ? (const void *)fattn_split_kernel<DD, 4, F> : (const void *)fattn_split_kernel<DD, 8, F>
-    if (D == 128) { if (f16) FA_OCC_FN(128, true); else FA_OCC_FN(128, false); }
-    else { if (f16) FA_OCC_FN(64, true); else FA_OCC_FN(64, false); }
-#undef FA_OCC_FN
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, 128, 0) != cudaSuccess || n < 1) n = 1;
-    occ = n;
-    return occ;
-}
-
-// resident CTAs per SM of the GQA decode kernel for G query heads per kv head
-static int gqa_kernel_occupancy(int G) {
-    static int cache[5];
-    int &occ = cache[G];
-    if (occ) return occ;
-    const void *fn = G == 1 ? (const void *)fattn_gqa_kernel<1, FA_GQA_U>
-                   : G == 2 ? (const void *)fattn_gqa_kernel<2, FA_GQA_U> : (const void *)fattn_gqa_kernel<4, FA_GQA_U>;
-    int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, 128, 0) != cudaSuccess || n < 1) n = 1;
-    occ = n;
-    return occ;
-}
 
 // q_bias: optional [H*D] f32 added to q; nkv_dev: optional device KV length (k->ne[1] is the maximum)
 int launch_flash_attn_ex(oasr_backend *be, const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *v,
@@ -1007,30 +978,19 @@ static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const
         a.oq_family = out_family;
     }
     const int64_t groups = heads ? (int64_t)a.S * (a.H / 4) : gqa ? (int64_t)a.S * a.HKV : (int64_t)a.HKV * a.S * a.n_qtiles;
+    // The split plan depends on the kernel and the cache length only -- never on the
+    // batch width, the other groups or the device -- so a sequence's output has the same
+    // bits whatever batch it runs in and on whichever GPU (the reference's batched ==
+    // serial property, and what lets a serving scheduler regroup sequences freely).
+    // The counts are the one-wave plans of a 148-SM B200 at 8 sequences (Whisper-large
+    // heads: 40 groups x 7 at 2 CTAs/SM; Qwen GQA: 64 groups x 4), at least 32 (64)
+    // positions per split.  Tickets exist for 2^16 groups.
     int n_splits = 1;
-    if (gqa) {
-        // one full wave of resident CTAs, at least 32 positions per split
-        const int resident = be->sm_count * gqa_kernel_occupancy(a.G);
-        n_splits = (int)std::max<int64_t>(1, resident / groups);
-        n_splits = std::max(1, std::min(std::min(n_splits, a.NKV / 32), FA_HEADS_MAX_SPLITS));
-    } else if (heads) {
-        // one full wave of resident CTAs, at least 32 positions per split
-        static int occ = 0;  // resident CTAs per SM (same for every device of this build)
-        if (occ == 0 && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, fattn_heads_kernel<FA_HEADS_U>, 128, 0) != cudaSuccess)
-            occ = 1;
-        n_splits = (int)(((int64_t)be->sm_count * std::max(occ, 1)) / groups);
-        n_splits = std::max(1, std::min(std::min(n_splits, a.NKV / 32), FA_HEADS_MAX_SPLITS));
-    } else if (nkv_dev && groups <= (1 << 16)) {
-        // model decode steps (device KV length): as many splits as fit one wave of
-        // resident CTAs -- a partial second wave would double the latency
-        const int resident = be->sm_count * split_kernel_occupancy(D, QT, k->type == OASR_TYPE_F16);
-        if (groups < resident) {
-            n_splits = (int)(resident / groups);
-            n_splits = std::min(std::min(n_splits, std::max(1, a.NKV / 64)), FA_HEADS_MAX_SPLITS);
-        }
-    } else if (groups < 4LL * be->sm_count && groups <= (1 << 16)) {
-        n_splits = (int)((4LL * be->sm_count + groups - 1) / groups);
-        n_splits = std::min(std::min(n_splits, std::max(1, a.NKV / 64)), FA_HEADS_MAX_SPLITS);
+    if (groups <= (1 << 16)) {
+        if (heads) n_splits = std::min(FA_SPLITS_HEADS, a.NKV / 32);
+        else if (gqa) n_splits = std::min(FA_SPLITS_GQA, a.NKV / 32);
+        else n_splits = std::min(FA_HEADS_MAX_SPLITS, a.NKV / 64);
+        n_splits = std::max(1, n_splits);
     }
     a.n_splits = n_splits;
     a.kv_per_split = (a.NKV + n_splits - 1) / n_splits;

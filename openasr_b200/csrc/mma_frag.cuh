@@ -92,14 +92,25 @@ static __device__ __forceinline__ int act_ld4(const int16_t *p) {
     return __ldg(reinterpret_cast<const int *>(p));
 }
 
+// ---- canonical summation order ---------------------------------------------------------
+// Every quantized mul_mat output is the sum of its per-block float terms in block order,
+// starting from zero:  y = ((0 + t_0) + t_1) + ... + t_{nb-1}.  That is ggml's vec_dot
+// loop order and the CPU restatement's, and the tensor-core GEMMs add their per-block
+// tiles in the same order, so a result does not depend on the kernel, the warp count or
+// the device.  The MMA cores below write each block's terms of a 16-row x 8-column tile to
+// shared memory (TERM_FLOATS per block: [lane][4], one float4 per lane) and one warp then
+// folds them in block order (fold_terms).  Terms of activation columns >= M are never read.
+constexpr int TERM_FLOATS = 32 * 4;
+constexpr int TERM_SEG_BLOCKS = 96;  // blocks of terms one segment holds (48 KB)
+
 // One Q4_K unit (16 rows x super-block s) against the 8 activation rows:
 //   arow = q8_K quants of activation row g (row base), brow = its 16-wide sums (row base),
 //   da0 / da1 = the q8_K scales of activation rows 2t, 2t+1 for super-block s (0 past M).
-// C layout: acc[0] (row g, act 2t), acc[1] (row g, act 2t+1), acc[2] (row g+8, 2t), acc[3] (row g+8, 2t+1).
+// C layout: c[0] (row g, act 2t), c[1] (row g, act 2t+1), c[2] (row g+8, 2t), c[3] (row g+8, 2t+1).
+// Writes the super-block's term (d_w*d_a)*isum - (dmin_w*d_a)*msum to tb[4 lane + e].
 template <bool SMEM>
-static __device__ __forceinline__ void q4k_unit_accumulate(float (&acc)[4], const Q4kUnit &u, int s,
-                                                           const int8_t *arow, const int16_t *brow, float da0,
-                                                           float da1, int t) {
+static __device__ __forceinline__ void q4k_unit_terms(float *tb, const Q4kUnit &u, int s, const int8_t *arow,
+                                                      const int16_t *brow, float da0, float da1, int lane, int t) {
     int isum[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -129,18 +140,20 @@ static __device__ __forceinline__ void q4k_unit_accumulate(float (&acc)[4], cons
                   dup_h2(byte_at(u.sb.w, t)), b0, b1);
     const float dwa = h2f((uint16_t)(u.dda & 0xFFFF)), dma = h2f((uint16_t)((unsigned)u.dda >> 16));
     const float dwb = h2f((uint16_t)(u.ddb & 0xFFFF)), dmb = h2f((uint16_t)((unsigned)u.ddb >> 16));
-    acc[0] += __fsub_rn(__fmul_rn(__fmul_rn(dwa, da0), (float)isum[0]), __fmul_rn(__fmul_rn(dma, da0), msum[0]));
-    acc[1] += __fsub_rn(__fmul_rn(__fmul_rn(dwa, da1), (float)isum[1]), __fmul_rn(__fmul_rn(dma, da1), msum[1]));
-    acc[2] += __fsub_rn(__fmul_rn(__fmul_rn(dwb, da0), (float)isum[2]), __fmul_rn(__fmul_rn(dmb, da0), msum[2]));
-    acc[3] += __fsub_rn(__fmul_rn(__fmul_rn(dwb, da1), (float)isum[3]), __fmul_rn(__fmul_rn(dmb, da1), msum[3]));
+    float4 v;
+    v.x = __fsub_rn(__fmul_rn(__fmul_rn(dwa, da0), (float)isum[0]), __fmul_rn(__fmul_rn(dma, da0), msum[0]));
+    v.y = __fsub_rn(__fmul_rn(__fmul_rn(dwa, da1), (float)isum[1]), __fmul_rn(__fmul_rn(dma, da1), msum[1]));
+    v.z = __fsub_rn(__fmul_rn(__fmul_rn(dwb, da0), (float)isum[2]), __fmul_rn(__fmul_rn(dmb, da0), msum[2]));
+    v.w = __fsub_rn(__fmul_rn(__fmul_rn(dwb, da1), (float)isum[3]), __fmul_rn(__fmul_rn(dmb, da1), msum[3]));
+    *reinterpret_cast<float4 *>(tb + 4 * lane) = v;
 }
 
 // One Q8_0 unit (16 rows x blocks 2p, 2p+1); ad0 / ad1 = q8_0 scale rows of activations 2t, 2t+1
-// (null past M).
+// (null past M).  Writes block 2p's terms (float)isum * (d_w * d_a) to tb[4 lane + e] and block
+// 2p+1's to tb[TERM_FLOATS + 4 lane + e].
 template <bool SMEM>
-static __device__ __forceinline__ void q80_unit_accumulate(float (&acc)[4], const Q80Unit &u, int p,
-                                                           const int8_t *arow, const float *ad0, const float *ad1,
-                                                           int t) {
+static __device__ __forceinline__ void q80_unit_terms(float *tb, const Q80Unit &u, int p, const int8_t *arow,
+                                                      const float *ad0, const float *ad1, int lane, int t) {
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
         const int b = 2 * p + i;
@@ -152,29 +165,52 @@ static __device__ __forceinline__ void q80_unit_accumulate(float (&acc)[4], cons
         const float dwb = h2f((uint16_t)(i == 0 ? (u.ddb & 0xFFFF) : ((unsigned)u.ddb >> 16)));
         const float da0 = ad0 ? (SMEM ? ad0[b] : __ldg(ad0 + b)) : 0.0f;
         const float da1 = ad1 ? (SMEM ? ad1[b] : __ldg(ad1 + b)) : 0.0f;
-        acc[0] += __fmul_rn((float)d[0], __fmul_rn(dwa, da0));
-        acc[1] += __fmul_rn((float)d[1], __fmul_rn(dwa, da1));
-        acc[2] += __fmul_rn((float)d[2], __fmul_rn(dwb, da0));
-        acc[3] += __fmul_rn((float)d[3], __fmul_rn(dwb, da1));
+        float4 v;
+        v.x = __fmul_rn((float)d[0], __fmul_rn(dwa, da0));
+        v.y = __fmul_rn((float)d[1], __fmul_rn(dwa, da1));
+        v.z = __fmul_rn((float)d[2], __fmul_rn(dwb, da0));
+        v.w = __fmul_rn((float)d[3], __fmul_rn(dwb, da1));
+        *reinterpret_cast<float4 *>(tb + i * TERM_FLOATS + 4 * lane) = v;
     }
 }
 
-// Sum the W warps' C fragments in warp order through shared memory `red` ([W][32][4]);
-// returns true in warp 0, whose acc then holds the tile's totals.
-template <int W>
-static __device__ __forceinline__ bool reduce_warps(float (&acc)[4], float *red, int warp, int lane) {
-    if (W == 1) return true;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) red[(warp * 32 + lane) * 4 + e] = acc[e];
-    __syncthreads();
-    if (warp != 0) return false;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        float v = red[lane * 4 + e];
-        for (int w2 = 1; w2 < W; ++w2) v += red[(w2 * 32 + lane) * 4 + e];
-        acc[e] = v;
+// acc[e] += t_b[4 lane + e] for b = 0 .. nblk-1, in that order
+static __device__ __forceinline__ void fold_terms(float (&acc)[4], const float *terms, int nblk, int lane) {
+#pragma unroll 4
+    for (int b = 0; b < nblk; ++b) {
+        const float4 v = *reinterpret_cast<const float4 *>(terms + b * TERM_FLOATS + 4 * lane);
+        acc[0] = __fadd_rn(acc[0], v.x);
+        acc[1] = __fadd_rn(acc[1], v.y);
+        acc[2] = __fadd_rn(acc[2], v.z);
+        acc[3] = __fadd_rn(acc[3], v.w);
     }
-    return true;
+}
+
+// Rounds of W units (round j holds units j W .. j W + W - 1, unit j W + w in warp w) are
+// written to shared memory SEGJ rounds at a time; after the last round of a segment the CTA
+// syncs and warp 0 folds the segment's blocks (units [u0, u1), BPU blocks each) into acc.
+// Every warp must call it for the same rounds.
+template <int W, int BPU, int SEGJ>
+static __device__ __forceinline__ void segment_end(float (&acc)[4], const float *terms, int j, int nrounds,
+                                                   int nunits, int warp, int lane) {
+    if (j % SEGJ != SEGJ - 1 && j != nrounds - 1) return;
+    const int u0 = (j - j % SEGJ) * W, u1 = min(nunits, (j + 1) * W);
+    __syncthreads();
+    if (warp == 0) fold_terms(acc, terms, (u1 - u0) * BPU, lane);
+    __syncthreads();
+}
+
+// term slot of unit (round j, warp w) within its segment
+template <int W, int BPU, int SEGJ>
+static __device__ __forceinline__ float *term_slot(float *terms, int j, int warp) {
+    return terms + ((j % SEGJ) * W + warp) * BPU * TERM_FLOATS;
+}
+
+// dynamic shared memory of one segment for `nunits` units
+template <int W, int BPU, int SEGJ>
+static inline size_t term_smem_bytes(int nunits) {
+    const int rounds = (nunits + W - 1) / W;
+    return (size_t)(rounds < SEGJ ? rounds : SEGJ) * W * BPU * TERM_FLOATS * sizeof(float);
 }
 
 }  // namespace oasr

@@ -22,11 +22,26 @@ namespace oasr {
 static __device__ __forceinline__ int nib_lo(int v) { return v & 0x0F0F0F0F; }
 static __device__ __forceinline__ int nib_hi(int v) { return (v >> 4) & 0x0F0F0F0F; }
 
-template <int N>
-static __device__ __forceinline__ void reduce_lanes(float (&v)[N], int lpr) {
-    for (int o = lpr >> 1; o > 0; o >>= 1) {
+// Canonical summation order (as mma_frag.cuh: every output is the sum of its per-block
+// terms in block order).  A pass of the item loop gives each of the warp's lanes one item
+// (block) of its row; the lanes stage their terms ([p][m][lane], rows of 33 floats so
+// that neither the stores nor the folding reads collide in a bank) in the warp's shared
+// slice, and lane L then adds, for the outputs it owns (o = L, L + 32, ...: sub-row, pass
+// row p, activation m), the pass's items of that row in item order.
+template <int RPM, int IPL>
+static __device__ __forceinline__ void fold_pass(float (&out)[RPM], const float *stage, int lane, int lpr_log2,
+                                                 int first_item, int nitems) {
+    const int lpr = 1 << lpr_log2, rpp = 32 >> lpr_log2;
+    const int outs = rpp * RPM;
 #pragma unroll
-        for (int i = 0; i < N; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], o);
+    for (int k = 0; k < RPM; ++k) {
+        const int o = lane + 32 * k;
+        if (o >= outs) break;
+        const int sub = o / RPM, pm = o - sub * RPM;
+        for (int jj = 0; jj < lpr / IPL; ++jj) {
+            if (first_item + jj * IPL >= nitems) break;
+            out[k] = __fadd_rn(out[k], stage[pm * 33 + sub * (lpr / IPL) + jj]);
+        }
     }
 }
 
@@ -37,17 +52,20 @@ __global__ void __launch_bounds__(128, 3)
                   int64_t N, int nitems, int lpr_log2, const int8_t *__restrict__ aqs, const float *__restrict__ ad,
                   int K, float *__restrict__ y, int64_t y_ld) {
     constexpr int QB = Q4 ? 16 : 32;
+    __shared__ float stage_all[4][33 * RP * M];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int lpr = 1 << lpr_log2, rpp = 32 >> lpr_log2;
     const int sub = lane >> lpr_log2, j = lane & (lpr - 1);
-    const int64_t row0 = ((int64_t)blockIdx.x * 4 + warp) * (int64_t)(rpp * RP) + sub;
+    const int64_t wrow0 = ((int64_t)blockIdx.x * 4 + warp) * (int64_t)(rpp * RP);  // the warp's first row
+    const int64_t row0 = wrow0 + sub;
     const int nb = K / 32;
-    float acc[RP * M];
+    float *stage = stage_all[warp];
+    float out[RP * M];  // outputs this lane folds (o = lane + 32 k)
 #pragma unroll
-    for (int i = 0; i < RP * M; ++i) acc[i] = 0.0f;
+    for (int i = 0; i < RP * M; ++i) out[i] = 0.0f;
 
-    // every lane runs the same trip count (shuffles below use the full warp);
-    // items past the end of the row contribute zero
+    // every lane runs the same trip count (the warp folds each pass together);
+    // items past the end of the row are never folded
     const int nit_pad = (nitems + lpr - 1) & ~(lpr - 1);
     int4 w0[RP], w1[RP];
     float dw[RP];
@@ -75,6 +93,7 @@ __global__ void __launch_bounds__(128, 3)
     for (int it = j; it < nit_pad; it += lpr) {
         const bool itv = it < nitems;
         if (it != j) load_w(it);
+        float term[RP * M];
 #pragma unroll
         for (int m = 0; m < M; ++m) {
             const int itc = itv ? it : 0;
@@ -105,20 +124,23 @@ __global__ void __launch_bounds__(128, 3)
                     s = __dp4a(w1[p].z, a1.z, s);
                     s = __dp4a(w1[p].w, a1.w, s);
                 }
-                acc[p * M + m] += __fmul_rn((float)s, __fmul_rn(dw[p], da));
+                term[p * M + m] = __fmul_rn((float)s, __fmul_rn(dw[p], da));
             }
         }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < RP * M; ++i) stage[i * 33 + lane] = term[i];
+        __syncwarp();
+        fold_pass<RP * M, 1>(out, stage, lane, lpr_log2, it - j, nitems);
     }
-    reduce_lanes(acc, lpr);
-    if (j == 0) {
+    const int outs = rpp * RP * M;
 #pragma unroll
-        for (int p = 0; p < RP; ++p) {
-            const int64_t row = row0 + (int64_t)p * rpp;
-            if (row < N) {
-#pragma unroll
-                for (int m = 0; m < M; ++m) y[(int64_t)m * y_ld + row] = acc[p * M + m];
-            }
-        }
+    for (int k = 0; k < RP * M; ++k) {
+        const int o = lane + 32 * k;
+        if (o >= outs) break;
+        const int s2 = o / (RP * M), pm = o - s2 * (RP * M), p = pm / M, m = pm - p * M;
+        const int64_t row = wrow0 + s2 + (int64_t)p * rpp;
+        if (row < N) y[(int64_t)m * y_ld + row] = out[k];
     }
 }
 
@@ -144,14 +166,18 @@ __global__ void __launch_bounds__(128, 3)
     mmv_q4k_kernel(const uint8_t *__restrict__ w, int64_t w_ld, int64_t N, int nitems, int lpr_log2,
                    const int8_t *__restrict__ aqs, const float *__restrict__ ad, const int16_t *__restrict__ abs16,
                    int K, float *__restrict__ y, int64_t y_ld) {
+    __shared__ float stage_all[4][33 * RP * M];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int lpr = 1 << lpr_log2, rpp = 32 >> lpr_log2;
     const int sub = lane >> lpr_log2, j = lane & (lpr - 1);
-    const int64_t row0 = ((int64_t)blockIdx.x * 4 + warp) * (int64_t)(rpp * RP) + sub;
+    const int64_t wrow0 = ((int64_t)blockIdx.x * 4 + warp) * (int64_t)(rpp * RP);
+    const int64_t row0 = wrow0 + sub;
     const int nsb = K / 256;
-    float acc[RP * M];
+    float *stage = stage_all[warp];
+    float out[RP * M];  // outputs this lane folds (o = lane + 32 k)
 #pragma unroll
-    for (int i = 0; i < RP * M; ++i) acc[i] = 0.0f;
+    for (int i = 0; i < RP * M; ++i) out[i] = 0.0f;
+    float term[RP * M];
 
     const int nit_pad = (nitems + lpr - 1) & ~(lpr - 1);
     // pull the first item's weight lines towards L2 before waiting for the
@@ -228,24 +254,29 @@ __global__ void __launch_bounds__(128, 3)
                 msum += __shfl_xor_sync(0xffffffffu, msum, 1);
                 isum += __shfl_xor_sync(0xffffffffu, isum, 2);
                 msum += __shfl_xor_sync(0xffffffffu, msum, 2);
-                if ((j & 3) == 0) {
-                    const float d = __fmul_rn(h2f((uint16_t)(hdr[p].x & 0xFFFF)), da);
-                    const float dm = __fmul_rn(h2f((uint16_t)((unsigned)hdr[p].x >> 16)), da);
-                    acc[p * M + m] += __fsub_rn(__fmul_rn(d, (float)isum), __fmul_rn(dm, (float)msum));
-                }
+                const float d = __fmul_rn(h2f((uint16_t)(hdr[p].x & 0xFFFF)), da);
+                const float dm = __fmul_rn(h2f((uint16_t)((unsigned)hdr[p].x >> 16)), da);
+                term[p * M + m] = __fsub_rn(__fmul_rn(d, (float)isum), __fmul_rn(dm, (float)msum));
             }
         }
+        // lane j % 4 == 0 holds its super-block's terms: stage them, fold this pass's
+        // super-blocks of each row in order
+        __syncwarp();
+        if ((j & 3) == 0) {
+#pragma unroll
+            for (int i = 0; i < RP * M; ++i) stage[i * 33 + (lane >> 2)] = term[i];
+        }
+        __syncwarp();
+        fold_pass<RP * M, 4>(out, stage, lane, lpr_log2, it - j, nitems);
     }
-    reduce_lanes(acc, lpr);
-    if (j == 0) {
+    const int outs = rpp * RP * M;
 #pragma unroll
-        for (int p = 0; p < RP; ++p) {
-            const int64_t row = row0 + (int64_t)p * rpp;
-            if (row < N) {
-#pragma unroll
-                for (int m = 0; m < M; ++m) y[(int64_t)m * y_ld + row] = acc[p * M + m];
-            }
-        }
+    for (int k = 0; k < RP * M; ++k) {
+        const int o = lane + 32 * k;
+        if (o >= outs) break;
+        const int s2 = o / (RP * M), pm = o - s2 * (RP * M), p = pm / M, m = pm - p * M;
+        const int64_t row = wrow0 + s2 + (int64_t)p * rpp;
+        if (row < N) y[(int64_t)m * y_ld + row] = out[k];
     }
 }
 

@@ -36,15 +36,16 @@ namespace oasr {
 
 // One CTA per 16-row tile; warp w handles super-blocks w, w + W, ... (LOOP: with the
 // next unit's loads issued before the current one's MMAs; !LOOP: W >= super-blocks,
-// one unit per warp, all loads issued at once); the W partial tiles are summed in
-// shared memory in warp order.
+// one unit per warp, all loads issued at once).  Each super-block's terms go to shared
+// memory and warp 0 adds them in super-block order (mma_frag.cuh: fold_terms).
 template <int W, bool LOOP>
 __global__ void __launch_bounds__(W * 32) mmv_q4k_tc_kernel(const uint8_t *__restrict__ tiles, int nsb, int64_t N,
                                                             int M, const int8_t *__restrict__ aqs,
                                                             const float *__restrict__ ad,
                                                             const int16_t *__restrict__ abs16, int K,
                                                             float *__restrict__ y, int64_t y_ld) {
-    __shared__ float red[W * 32 * 4];
+    constexpr int SEGJ = TERM_SEG_BLOCKS / W;
+    extern __shared__ __align__(16) float terms[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const uint8_t *tile = tiles + (int64_t)blockIdx.x * nsb * Q4K_UNIT;
@@ -53,8 +54,7 @@ __global__ void __launch_bounds__(W * 32) mmv_q4k_tc_kernel(const uint8_t *__res
     // weights do not depend on the previous kernel: issue them before the wait
     griddep_launch_dependents();
     Q4kUnit cur, nxt;
-    int s = warp;
-    if (s < nsb) load_q4k_unit(cur, tile + (int64_t)s * Q4K_UNIT, lane, g);
+    if (warp < nsb) load_q4k_unit(cur, tile + (int64_t)warp * Q4K_UNIT, lane, g);
     griddep_wait();
 
     // B-fragment activation row g (rows past M read row 0 and are never stored)
@@ -62,21 +62,19 @@ __global__ void __launch_bounds__(W * 32) mmv_q4k_tc_kernel(const uint8_t *__res
     const int8_t *arow = aqs + (int64_t)gr * K;
     const int16_t *brow = abs16 + (int64_t)gr * (K / 16);
     const int m0 = 2 * t, m1 = 2 * t + 1;  // C-fragment activation rows
-    if (LOOP) {
-        for (; s < nsb; s += W) {
-            const bool more = s + W < nsb;
-            if (more) load_q4k_unit(nxt, tile + (int64_t)(s + W) * Q4K_UNIT, lane, g);
+    const int nrounds = LOOP ? (nsb + W - 1) / W : 1;
+    for (int j = 0; j < nrounds; ++j) {
+        const int s = j * W + warp;
+        if (s < nsb) {
+            if (LOOP && s + W < nsb) load_q4k_unit(nxt, tile + (int64_t)(s + W) * Q4K_UNIT, lane, g);
             const float da0 = m0 < M ? __ldg(ad + (int64_t)m0 * nsb + s) : 0.0f;
             const float da1 = m1 < M ? __ldg(ad + (int64_t)m1 * nsb + s) : 0.0f;
-            q4k_unit_accumulate<false>(acc, cur, s, arow, brow, da0, da1, t);
-            if (more) cur = nxt;
+            q4k_unit_terms<false>(term_slot<W, 1, SEGJ>(terms, j, warp), cur, s, arow, brow, da0, da1, lane, t);
+            if (LOOP && s + W < nsb) cur = nxt;
         }
-    } else if (s < nsb) {
-        const float da0 = m0 < M ? __ldg(ad + (int64_t)m0 * nsb + s) : 0.0f;
-        const float da1 = m1 < M ? __ldg(ad + (int64_t)m1 * nsb + s) : 0.0f;
-        q4k_unit_accumulate<false>(acc, cur, s, arow, brow, da0, da1, t);
+        segment_end<W, 1, SEGJ>(acc, terms, j, nrounds, nsb, warp, lane);
     }
-    if (!reduce_warps<W>(acc, red, warp, lane)) return;
+    if (warp != 0) return;
     const int64_t ra = (int64_t)blockIdx.x * TILE_ROWS + g, rb = ra + 8;
     if (m0 < M) {
         if (ra < N) y[(int64_t)m0 * y_ld + ra] = acc[0];
@@ -91,13 +89,15 @@ __global__ void __launch_bounds__(W * 32) mmv_q4k_tc_kernel(const uint8_t *__res
 // Q8_0: warp w takes units w, w + W, ... (UPW of them) and issues every one of its loads
 // before the wait, so a tile's weights are one round trip in flight (they do not
 // depend on the predecessor).  UPW = 0 is the looping form for K past 8 units per warp:
-// one unit per warp in flight ahead of the one in use.
+// one unit per warp in flight ahead of the one in use.  Block terms are folded in block
+// order by warp 0 as in mmv_q4k_tc_kernel.
 template <int W, int UPW>
 __global__ void __launch_bounds__(W * 32) mmv_q80_tc_kernel(const uint8_t *__restrict__ tiles, int npairs, int64_t N,
                                                             int M, const int8_t *__restrict__ aqs,
                                                             const float *__restrict__ ad, int K,
                                                             float *__restrict__ y, int64_t y_ld) {
-    __shared__ float red[W * 32 * 4];
+    constexpr int SEGJ = TERM_SEG_BLOCKS / (2 * W);
+    extern __shared__ __align__(16) float terms[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const uint8_t *tile = tiles + (int64_t)blockIdx.x * npairs * Q80_UNIT;
@@ -121,19 +121,28 @@ __global__ void __launch_bounds__(W * 32) mmv_q80_tc_kernel(const uint8_t *__res
     const int m0 = 2 * t, m1 = 2 * t + 1;
     const float *ad0 = m0 < M ? ad + (int64_t)m0 * nb : nullptr;
     const float *ad1 = m1 < M ? ad + (int64_t)m1 * nb : nullptr;
+    const int nrounds = (npairs + W - 1) / W;
     if (UPW > 0) {
 #pragma unroll
-        for (int j = 0; j < NU; ++j)
-            if (warp + j * W < npairs) q80_unit_accumulate<false>(acc, u[j], warp + j * W, arow, ad0, ad1, t);
+        for (int j = 0; j < NU; ++j) {
+            if (j >= nrounds) break;  // CTA-uniform
+            const int p = warp + j * W;
+            if (p < npairs) q80_unit_terms<false>(term_slot<W, 2, SEGJ>(terms, j, warp), u[j], p, arow, ad0, ad1, lane, t);
+            segment_end<W, 2, SEGJ>(acc, terms, j, nrounds, npairs, warp, lane);
+        }
     } else {
-        for (int p = warp; p < npairs; p += W) {
-            const bool more = p + W < npairs;
-            if (more) load_q80_unit(u[1], tile + (int64_t)(p + W) * Q80_UNIT, lane, g);
-            q80_unit_accumulate<false>(acc, u[0], p, arow, ad0, ad1, t);
-            if (more) u[0] = u[1];
+        for (int j = 0; j < nrounds; ++j) {
+            const int p = j * W + warp;
+            if (p < npairs) {
+                const bool more = p + W < npairs;
+                if (more) load_q80_unit(u[1], tile + (int64_t)(p + W) * Q80_UNIT, lane, g);
+                q80_unit_terms<false>(term_slot<W, 2, SEGJ>(terms, j, warp), u[0], p, arow, ad0, ad1, lane, t);
+                if (more) u[0] = u[1];
+            }
+            segment_end<W, 2, SEGJ>(acc, terms, j, nrounds, npairs, warp, lane);
         }
     }
-    if (!reduce_warps<W>(acc, red, warp, lane)) return;
+    if (warp != 0) return;
     const int64_t ra = (int64_t)blockIdx.x * TILE_ROWS + g, rb = ra + 8;
     if (m0 < M) {
         if (ra < N) y[(int64_t)m0 * y_ld + ra] = acc[0];
@@ -267,7 +276,8 @@ template <int W, bool LOOP>
 static cudaError_t launch_q4k_w(oasr_backend *be, const uint8_t *tiles, int nsb, int64_t N, int M, const ActPlanes &a,
                                 int K, float *y, int64_t y_ld) {
     const unsigned grid = (unsigned)((N + TILE_ROWS - 1) / TILE_ROWS);
-    return launch_k(be, mmv_q4k_tc_kernel<W, LOOP>, dim3(grid), dim3(W * 32), 0, tiles, nsb, N, M,
+    const size_t smem = term_smem_bytes<W, 1, TERM_SEG_BLOCKS / W>(nsb);
+    return launch_k(be, mmv_q4k_tc_kernel<W, LOOP>, dim3(grid), dim3(W * 32), smem, tiles, nsb, N, M,
                     (const int8_t *)a.qs, (const float *)a.d, (const int16_t *)a.bs16, K, y, y_ld);
 }
 
@@ -275,7 +285,8 @@ template <int W, int UPW>
 static cudaError_t launch_q80_w(oasr_backend *be, const uint8_t *tiles, int npairs, int64_t N, int M,
                                 const ActPlanes &a, int K, float *y, int64_t y_ld) {
     const unsigned grid = (unsigned)((N + TILE_ROWS - 1) / TILE_ROWS);
-    return launch_k(be, mmv_q80_tc_kernel<W, UPW>, dim3(grid), dim3(W * 32), 0, tiles, npairs, N, M,
+    const size_t smem = term_smem_bytes<W, 2, TERM_SEG_BLOCKS / (2 * W)>(npairs);
+    return launch_k(be, mmv_q80_tc_kernel<W, UPW>, dim3(grid), dim3(W * 32), smem, tiles, npairs, N, M,
                     (const int8_t *)a.qs, (const float *)a.d, K, y, y_ld);
 }
 

@@ -782,7 +782,7 @@ void oo_gelu(const float *x, float *y, int64_t n) {
 
 void oo_silu(const float *x, float *y, int64_t n) {
 #pragma omp parallel for schedule(static)
-    for (int64_t i = 0; i < n; ++i) y[i] = x[i] / (1.0f + expf(-x[i]));
+    for (int64_t i = 0; i < n; ++i) y[i] = x[i] / (1.0f + oo_expf(-x[i]));
 }
 
 void oo_rope_neox(float *x, int64_t D, int64_t H, int64_t T, const int32_t *pos, float freq_base) {
@@ -801,4 +801,402 @@ void oo_rope_neox(float *x, int64_t D, int64_t H, int64_t T, const int32_t *pos,
             theta *= theta_scale;
         }
     }
+}
+
+/* ------------------------------------------------------------------------ */
+/* the decode path's canonical arithmetic (see oracle.h)                     */
+/* ------------------------------------------------------------------------ */
+static float pow2i(int k) { /* 2^k, -126 <= k <= 127 */
+    uint32_t b = (uint32_t)(k + 127) << 23;
+    float f;
+    memcpy(&f, &b, 4);
+    return f;
+}
+
+float oo_expf(float x) {
+    if (!(x == x)) return x;
+    if (x > 88.72283935546875f) return INFINITY;
+    if (x < -103.97208404541015625f) return 0.0f;
+    const float t = rintf(x * 1.44269502162933349609375f);
+    float r = fmaf(-t, 0.693145751953125f, x);
+    r = fmaf(-t, 1.428606765330187045e-06f, r);
+    float p = 1.9841270113e-04f;
+    p = fmaf(p, r, 1.3888889225e-03f);
+    p = fmaf(p, r, 8.3333337680e-03f);
+    p = fmaf(p, r, 4.1666667908e-02f);
+    p = fmaf(p, r, 1.6666667163e-01f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const int n = (int)t;
+    if (n > 127) return (p * pow2i(127)) * 2.0f;
+    if (n < -126) return (p * pow2i(n + 64)) * pow2i(-64);
+    return p * pow2i(n);
+}
+
+/* xor butterfly over `n` (power of two) lanes: after level o every lane holds
+ * v[l] + v[l ^ o]; returns lane 0's final value (all lanes agree: + commutes) */
+static double butterfly_d(double *v, int n) {
+    for (int o = n / 2; o > 0; o >>= 1)
+        for (int l = 0; l < n; ++l)
+            if (l < (l ^ o)) {
+                const double s = v[l] + v[l ^ o];
+                v[l] = s;
+                v[l ^ o] = s;
+            }
+    return v[0];
+}
+
+static float butterfly_f(float *v, int n) {
+    for (int o = n / 2; o > 0; o >>= 1)
+        for (int l = 0; l < n; ++l)
+            if (l < (l ^ o)) {
+                const float s = v[l] + v[l ^ o];
+                v[l] = s;
+                v[l ^ o] = s;
+            }
+    return v[0];
+}
+
+/* the device's double reduction of per-element values x[i] (squared when sq) over a
+ * row of n: E > 0 chunk kernel, E == 0 256-thread kernel (elementwise.cu) */
+static double dev_row_sum(const float *x, int64_t n, int E, int sq) {
+    double lanes[32];
+    double t = 0.0;
+    if (E > 0) {
+        const int64_t nw = n / (32 * E);
+        for (int64_t w = 0; w < nw; ++w) {
+            for (int l = 0; l < 32; ++l) {
+                double s = 0.0;
+                for (int i = 0; i < E; ++i) {
+                    const float v = x[w * 32 * E + (int64_t)E * l + i];
+                    s += (double)(sq ? v * v : v);
+                }
+                lanes[l] = s;
+            }
+            t += butterfly_d(lanes, 32);
+        }
+    } else {
+        for (int w = 0; w < 8; ++w) {
+            for (int l = 0; l < 32; ++l) {
+                double s = 0.0;
+                for (int64_t i = 32 * w + l; i < n; i += 256) {
+                    const float v = x[i];
+                    s += (double)(sq ? v * v : v);
+                }
+                lanes[l] = s;
+            }
+            t += butterfly_d(lanes, 32);
+        }
+    }
+    return t;
+}
+
+void oo_norm_dev(const float *x, float *y, int64_t n, int64_t rows, float eps, int rms, int E) {
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+        const float *xr = x + r * n;
+        float *yr = y + r * n;
+        if (rms) {
+            const float mean = (float)(dev_row_sum(xr, n, E, 1) / (double)n);
+            const float scale = 1.0f / sqrtf(mean + eps);
+            for (int64_t i = 0; i < n; ++i) yr[i] = xr[i] * scale;
+        } else {
+            const float mean = (float)(dev_row_sum(xr, n, E, 0) / (double)n);
+            for (int64_t i = 0; i < n; ++i) yr[i] = xr[i] - mean;
+            const float var = (float)(dev_row_sum(yr, n, E, 1) / (double)n);
+            const float scale = 1.0f / sqrtf(var + eps);
+            for (int64_t i = 0; i < n; ++i) yr[i] = yr[i] * scale;
+        }
+    }
+}
+
+/* ---- decode attention, device order ------------------------------------------------- */
+#define FA_SPLITS_HEADS 7
+#define FA_SPLITS_GQA 4
+#define FA_SPLITS_MAX 16
+
+int oo_fa_device_splits(int kind, int64_t nkv_max, int64_t groups) {
+    if (groups > (1 << 16)) return 1;
+    int64_t n = kind == OO_FAK_HEADS ? (nkv_max / 32 < FA_SPLITS_HEADS ? nkv_max / 32 : FA_SPLITS_HEADS)
+              : kind == OO_FAK_GQA   ? (nkv_max / 32 < FA_SPLITS_GQA ? nkv_max / 32 : FA_SPLITS_GQA)
+                                     : (nkv_max / 64 < FA_SPLITS_MAX ? nkv_max / 64 : FA_SPLITS_MAX);
+    return n < 1 ? 1 : (int)n;
+}
+
+/* online-softmax state of one lane group: running max, sum, D accumulators */
+typedef struct { float m, l; float a[128]; } fa_state;
+
+static void fa_state_init(fa_state *s, int D) {
+    s->m = -INFINITY;
+    s->l = 0.0f;
+    for (int e = 0; e < D; ++e) s->a[e] = 0.0f;
+}
+
+/* a absorbs its shuffle partner b: a = a * f(a) + b * f(b), b's product fused */
+static void fa_combine(fa_state *a, const fa_state *b, int D) {
+    const float nm = fmaxf(a->m, b->m);
+    const float f0 = a->m == -INFINITY ? 0.0f : oo_expf(a->m - nm);
+    const float f1 = b->m == -INFINITY ? 0.0f : oo_expf(b->m - nm);
+    a->l = fmaf(b->l, f1, a->l * f0);
+    for (int e = 0; e < D; ++e) a->a[e] = fmaf(b->a[e], f1, a->a[e] * f0);
+    a->m = nm;
+}
+
+/* merge of parts in order (the 4 warps of a CTA, or the splits of a row):
+ * M = max m, L = sum l f, A = sum a f (f = e^(m - M)), each product fused into its sum */
+static void fa_merge(const fa_state *parts, int n, int D, fa_state *out) {
+    float M = -INFINITY;
+    for (int i = 0; i < n; ++i) M = fmaxf(M, parts[i].m);
+    float L = 0.0f;
+    for (int e = 0; e < D; ++e) out->a[e] = 0.0f;
+    for (int i = 0; i < n; ++i) {
+        const float f = parts[i].m == -INFINITY ? 0.0f : oo_expf(parts[i].m - M);
+        L = fmaf(parts[i].l, f, L);
+        for (int e = 0; e < D; ++e) out->a[e] = fmaf(parts[i].a[e], f, out->a[e]);
+    }
+    out->m = M;
+    out->l = L;
+}
+
+/* dot of q and a K row as a lane group computes it: lane sl of `lanes` takes dims
+ * per*sl .. per*sl + per - 1 in an fmaf chain, then the xor butterfly of the group */
+static float fa_dot(const float *q, const float *kr, int lanes, int per) {
+    float d[16];
+    for (int sl = 0; sl < lanes; ++sl) {
+        float s = 0.0f;
+        for (int e = 0; e < per; ++e) s = fmaf(q[per * sl + e], kr[per * sl + e], s);
+        d[sl] = s;
+    }
+    return butterfly_f(d, lanes);
+}
+
+/* rows of one (sequence, kv head): K/V rows [nkv][D] as f32 (converted from f16 exactly) */
+typedef struct {
+    const float *k, *v;  /* [nkv][D] */
+    const float *mask;   /* [nkv] or NULL (one query row) */
+    int64_t nkv;
+} fa_rows;
+
+/* fattn_split_kernel: one query row, positions [kv0, kv1) */
+static void fa_split_part(const float *q, const fa_rows *r, int D, float scale, int64_t kv0, int64_t kv1,
+                          fa_state *out, fa_state *scratch /* [16] */) {
+    const int LPP = D / 8, PPW = 32 / LPP, U = 4;
+    fa_state *grp = scratch;
+    fa_state warps[4];
+    for (int w = 0; w < 4; ++w) {
+        for (int g = 0; g < PPW; ++g) fa_state_init(&grp[g], D);
+        for (int64_t pb = kv0 + (int64_t)w * PPW; pb < kv1; pb += 4 * PPW * U)
+            for (int u = 0; u < U; ++u)
+                for (int g = 0; g < PPW; ++g) {
+                    const int64_t p = pb + (int64_t)u * 4 * PPW + g;
+                    if (p >= kv1) continue;
+                    float sc = fa_dot(q, r->k + p * D, LPP, 8) * scale;
+                    if (r->mask) {
+                        const float mv = r->mask[p];
+                        if (mv == -INFINITY) continue;
+                        sc = sc + mv;
+                    }
+                    fa_state *s = &grp[g];
+                    const float mnew = fmaxf(s->m, sc);
+                    const float corr = oo_expf(s->m - mnew);
+                    const float wgt = oo_expf(sc - mnew);
+                    s->l = fmaf(s->l, corr, wgt);
+                    const float *vr = r->v + p * D;
+                    for (int e = 0; e < D; ++e) s->a[e] = fmaf(wgt, vr[e], s->a[e] * corr);
+                    s->m = mnew;
+                }
+        /* position groups: level o = LPP, 2 LPP, ... pairs group g with g ^ (o / LPP) */
+        for (int lvl = 1; lvl < PPW; lvl <<= 1) {
+            fa_state nxt[4];
+            for (int g = 0; g < PPW; ++g) {
+                nxt[g] = grp[g];
+                fa_combine(&nxt[g], &grp[g ^ lvl], D);
+            }
+            for (int g = 0; g < PPW; ++g) grp[g] = nxt[g];
+        }
+        warps[w] = grp[0];
+    }
+    fa_merge(warps, 4, D, out);
+}
+
+/* fattn_heads_kernel<8>: one (sequence, head), D 64, positions [kv0, kv1) */
+static void fa_heads_part(const float *q, const fa_rows *r, float scale, int64_t kv0, int64_t kv1, fa_state *out) {
+    const int D = 64, U = 8;
+    fa_state warps[4];
+    for (int w = 0; w < 4; ++w) {
+        fa_state *s = &warps[w];
+        fa_state_init(s, D);
+        for (int64_t pb = kv0 + w; pb < kv1; pb += 4 * U) {
+            float sc[8], wv[8];
+            float mb = -INFINITY;
+            for (int u = 0; u < U; ++u) {
+                const int64_t p = pb + 4 * u;
+                sc[u] = p < kv1 ? fa_dot(q, r->k + p * D, 8, 8) * scale : -INFINITY;
+                mb = fmaxf(mb, sc[u]);
+            }
+            const float mnew = fmaxf(s->m, mb);
+            for (int u = 0; u < U; ++u) wv[u] = oo_expf(sc[u] - mnew);
+            const float corr = oo_expf(s->m - mnew);
+            s->l = s->l * corr;
+            for (int e = 0; e < D; ++e) s->a[e] = s->a[e] * corr;
+            for (int u = 0; u < U; ++u) {
+                const int64_t p = pb + 4 * u;
+                s->l = s->l + wv[u];
+                for (int e = 0; e < D; ++e) s->a[e] = fmaf(wv[u], p < kv1 ? r->v[p * D + e] : 0.0f, s->a[e]);
+            }
+            s->m = mnew;
+        }
+    }
+    fa_merge(warps, 4, D, out);
+}
+
+/* fattn_gqa_kernel<G, 2>: one (sequence, kv head) and its G query heads, D 128,
+ * positions [kv0, kv1); q = G rows of 128, out = G states */
+static void fa_gqa_part(const float *q, int G, const fa_rows *r, float scale, int64_t kv0, int64_t kv1,
+                        fa_state *out, fa_state *scratch /* [4 warps][4 groups][G] */) {
+    const int D = 128, U = 2;
+    for (int w = 0; w < 4; ++w)
+        for (int grp = 0; grp < 4; ++grp) {
+            fa_state *st = scratch + (w * 4 + grp) * G;
+            for (int g = 0; g < G; ++g) fa_state_init(&st[g], D);
+            for (int64_t pb = kv0 + 4 * w; pb < kv1; pb += 16 * U) {
+                float sc[4][2];
+                for (int u = 0; u < U; ++u) {
+                    const int64_t p = pb + grp + 16 * u;
+                    for (int g = 0; g < G; ++g)
+                        sc[g][u] = p < kv1 ? fa_dot(q + g * D, r->k + p * D, 8, 16) * scale : -INFINITY;
+                }
+                for (int g = 0; g < G; ++g) {
+                    float mb = sc[g][0];
+                    for (int u = 1; u < U; ++u) mb = fmaxf(mb, sc[g][u]);
+                    const float mnew = fmaxf(st[g].m, mb);
+                    if (mnew == -INFINITY) continue;
+                    const float corr = oo_expf(st[g].m - mnew);
+                    st[g].l = st[g].l * corr;
+                    for (int e = 0; e < D; ++e) st[g].a[e] = st[g].a[e] * corr;
+                    st[g].m = mnew;
+                }
+                for (int u = 0; u < U; ++u) {
+                    const int64_t p = pb + grp + 16 * u;
+                    for (int g = 0; g < G; ++g) {
+                        if (sc[g][u] == -INFINITY) continue;
+                        const float wgt = oo_expf(sc[g][u] - st[g].m);
+                        st[g].l = st[g].l + wgt;
+                        for (int e = 0; e < D; ++e) st[g].a[e] = fmaf(wgt, r->v[p * D + e], st[g].a[e]);
+                    }
+                }
+            }
+        }
+    for (int g = 0; g < G; ++g) {
+        fa_state warps[4];
+        for (int w = 0; w < 4; ++w) {
+            fa_state grp4[4];
+            for (int grp = 0; grp < 4; ++grp) grp4[grp] = scratch[(w * 4 + grp) * G + g];
+            for (int lvl = 1; lvl < 4; lvl <<= 1) {
+                fa_state nxt[4];
+                for (int x = 0; x < 4; ++x) {
+                    nxt[x] = grp4[x];
+                    fa_combine(&nxt[x], &grp4[x ^ lvl], D);
+                }
+                for (int x = 0; x < 4; ++x) grp4[x] = nxt[x];
+            }
+            warps[w] = grp4[0];
+        }
+        fa_merge(warps, 4, D, &out[g]);
+    }
+}
+
+static float elem_f(const char *p, int type) {
+    return type == OO_TYPE_F32 ? *(const float *)p : oo_f16_to_f32(*(const uint16_t *)p);
+}
+
+int oo_fa_device(const oo_tensor *q, const oo_tensor *k, const oo_tensor *v, const oo_tensor *mask, float scale,
+                 int kind, int64_t nkv_max, oo_tensor *dst) {
+    pthread_once(&f16_once, f16_table_init);
+    const int64_t D = q->ne[0], NQ = q->ne[1], H = q->ne[2], S = q->ne[3];
+    const int64_t NKV = k->ne[1], HKV = k->ne[2];
+    if (q->type != OO_TYPE_F32 || k->ne[0] != D || v->ne[0] != D || k->type != v->type) return OO_STATUS_FAILED;
+    if (k->type != OO_TYPE_F16 && k->type != OO_TYPE_F32) return OO_STATUS_FAILED;
+    if (v->ne[1] != NKV || v->ne[2] != HKV || k->ne[3] != S || v->ne[3] != S || HKV == 0 || H % HKV) return OO_STATUS_FAILED;
+    if (nkv_max < NKV) return OO_STATUS_FAILED;
+    if (dst->type != OO_TYPE_F32 || dst->ne[0] != D || dst->ne[1] != H || dst->ne[2] != NQ || dst->ne[3] != S)
+        return OO_STATUS_FAILED;
+    const int64_t G = H / HKV;
+    if (kind == OO_FAK_HEADS && !(D == 64 && k->type == OO_TYPE_F16 && NQ == 1 && G == 1 && !mask && H % 4 == 0))
+        return OO_STATUS_FAILED;
+    if (kind == OO_FAK_GQA && !(D == 128 && k->type == OO_TYPE_F16 && NQ == 1 && !mask && (G == 1 || G == 2 || G == 4)))
+        return OO_STATUS_FAILED;
+    if (kind == OO_FAK_SPLIT && !(D == 64 || D == 128)) return OO_STATUS_FAILED;
+    const int f16 = k->type == OO_TYPE_F16;
+    const int64_t QG = G * NQ, QT = QG >= 8 ? 8 : QG >= 4 ? 4 : QG >= 2 ? 2 : 1;
+    const int64_t groups = kind == OO_FAK_HEADS ? S * (H / 4) : kind == OO_FAK_GQA ? S * HKV : HKV * S * ((QG + QT - 1) / QT);
+    const int ns = oo_fa_device_splits(kind, nkv_max, groups);
+    const int64_t per = (NKV + ns - 1) / ns;
+    int bad = 0;
+#pragma omp parallel for schedule(dynamic, 1) collapse(2) reduction(| : bad)
+    for (int64_t s = 0; s < S; ++s)
+        for (int64_t hk = 0; hk < HKV; ++hk) {
+            fa_rows r;
+            float *kv = (float *)malloc((size_t)(2 * NKV * D + NKV + 4 * D) * sizeof(float));
+            fa_state *st = (fa_state *)malloc(sizeof(fa_state) * (size_t)(16 * 4 + 2 * FA_SPLITS_MAX * 4 + 4));
+            if (!kv || !st) { free(kv); free(st); bad = 1; continue; }
+            float *kf = kv, *vf = kv + NKV * D, *mrow = kv + 2 * NKV * D, *qv = mrow + NKV;
+            for (int64_t p = 0; p < NKV; ++p)
+                for (int64_t d = 0; d < D; ++d) {
+                    kf[p * D + d] = elem_f((const char *)k->data + d * k->nb[0] + p * k->nb[1] + hk * k->nb[2] + s * k->nb[3], k->type);
+                    vf[p * D + d] = elem_f((const char *)v->data + d * v->nb[0] + p * v->nb[1] + hk * v->nb[2] + s * v->nb[3], v->type);
+                }
+            r.k = kf;
+            r.v = vf;
+            r.nkv = NKV;
+            fa_state *parts = st + 64;       /* [splits][G] */
+            fa_state *res = parts + FA_SPLITS_MAX * 4;
+            for (int64_t g = 0; g < G; ++g)
+                for (int64_t iq = 0; iq < NQ; ++iq) {
+                    const int64_t h = hk * G + g;
+                    if (kind == OO_FAK_GQA && iq > 0) break;
+                    /* the query as the kernel holds it: rounded to f16 over f16 K/V */
+                    const int64_t gq = kind == OO_FAK_GQA ? G : 1;
+                    for (int64_t gg = 0; gg < gq; ++gg) {
+                        const int64_t hh = kind == OO_FAK_GQA ? hk * G + gg : h;
+                        for (int64_t d = 0; d < D; ++d) {
+                            const float x = *(const float *)((const char *)q->data + d * q->nb[0] + iq * q->nb[1] + hh * q->nb[2] + s * q->nb[3]);
+                            qv[gg * D + d] = f16 ? oo_f16_to_f32(oo_f32_to_f16(x)) : x;
+                        }
+                    }
+                    if (kind == OO_FAK_GQA && g > 0) break;  /* all G heads at once */
+                    r.mask = NULL;
+                    if (mask) {
+                        for (int64_t p = 0; p < NKV; ++p)
+                            mrow[p] = oo_f16_to_f32(*(const uint16_t *)((const char *)mask->data + p * mask->nb[0] + iq * mask->nb[1] +
+                                                                       (h % mask->ne[2]) * mask->nb[2] + (s % mask->ne[3]) * mask->nb[3]));
+                        r.mask = mrow;
+                    }
+                    for (int sp = 0; sp < ns; ++sp) {
+                        const int64_t kv0 = sp * per, kv1 = kv0 + per < NKV ? kv0 + per : NKV;
+                        if (kind == OO_FAK_HEADS) fa_heads_part(qv, &r, scale, kv0, kv1, &parts[sp]);
+                        else if (kind == OO_FAK_GQA) {
+                            fa_state tmp[4];
+                            fa_gqa_part(qv, (int)G, &r, scale, kv0, kv1, tmp, st);
+                            for (int64_t gg = 0; gg < G; ++gg) parts[gg * FA_SPLITS_MAX + sp] = tmp[gg];
+                        } else fa_split_part(qv, &r, (int)D, scale, kv0, kv1, &parts[sp], st);
+                    }
+                    const int64_t nout = kind == OO_FAK_GQA ? G : 1;
+                    for (int64_t gg = 0; gg < nout; ++gg) {
+                        const fa_state *pp = kind == OO_FAK_GQA ? parts + gg * FA_SPLITS_MAX : parts;
+                        const fa_state *fin = pp;
+                        if (ns > 1) {
+                            fa_merge(pp, ns, (int)D, res);
+                            fin = res;
+                        }
+                        const int64_t hh = kind == OO_FAK_GQA ? hk * G + gg : h;
+                        float *out = (float *)((char *)dst->data + hh * dst->nb[1] + iq * dst->nb[2] + s * dst->nb[3]);
+                        for (int64_t d = 0; d < D; ++d) out[d] = fin->l == 0.0f ? 0.0f : fin->a[d] / fin->l;
+                    }
+                }
+            free(kv);
+            free(st);
+        }
+    return bad ? OO_STATUS_ALLOC_FAILED : 0;
 }

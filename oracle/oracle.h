@@ -113,9 +113,42 @@ void oo_argmax_first(const float *x, int64_t n, int64_t rows, int32_t *out);
 void oo_norm(const float *x, float *y, int64_t n, int64_t rows, float eps);      /* ggml_norm */
 void oo_rms_norm(const float *x, float *y, int64_t n, int64_t rows, float eps);  /* ggml_rms_norm */
 void oo_gelu(const float *x, float *y, int64_t n);                                 /* ggml_gelu (fp16 table) */
-void oo_silu(const float *x, float *y, int64_t n);                                 /* ggml_silu */
+void oo_silu(const float *x, float *y, int64_t n);                                 /* ggml_silu, e^x as oo_expf */
 /* ggml_rope_ext NEOX mode on [D, H, T] rows: positions[t]; n_dims = D */
 void oo_rope_neox(float *x, int64_t D, int64_t H, int64_t T, const int32_t *pos, float freq_base);
+
+/* ---- the decode path's canonical arithmetic -------------------------------------------
+ * ggml's CPU ops leave the f32 summation order to the ISA (AVX2 and AVX-512 builds of
+ * ggml differ in the last bits); this restatement fixes one order per op -- the order the
+ * B200 kernels use -- so that greedy transcripts can be compared bit for bit.  The
+ * quantized mul_mat above already sums its per-block terms in block order (ggml's
+ * vec_dot loop order), which every device mul_mat path follows.  The functions below
+ * restate the other reductions of a decode step. */
+
+/* e^x: Cody-Waite reduction (ln2 split as fdlibm's float split), degree-7 Taylor
+ * polynomial in Horner form with fmaf, scaling by 2^n (two steps below 2^-126).  Used by
+ * the SiLU and by the decode attentions' softmax. */
+float oo_expf(float x);
+
+/* LayerNorm (rms = 0) / RMSNorm (rms = 1) of rows of n, without gain or bias, with the
+ * device's reduction tree: layout E > 0 = one warp per 32E-element chunk (lane l of warp
+ * w sums elements 32Ew + El .. +E-1 in double, the warp adds lanes by an xor butterfly,
+ * the warps' sums are added in warp order); E = 0 = the 256-thread row kernel (thread i
+ * sums elements i, i + 256, ...).  Means and variances are sums / n rounded to float. */
+void oo_norm_dev(const float *x, float *y, int64_t n, int64_t rows, float eps, int rms, int E);
+
+/* Decode attention as the device kernels compute it (flash_attn_ext with one query
+ * tile).  kind: OO_FAK_SPLIT (generic split-KV kernel: D 64 / 128, masks, f16 or f32
+ * K/V), OO_FAK_HEADS (4-head kernel: D 64, f16, one query, no mask, H % 4 == 0),
+ * OO_FAK_GQA (GQA kernel: D 128, f16, one query, no mask, G in {1, 2, 4}).  The KV
+ * range [0, k->ne[1]) is the live prefix; nkv_max is the cache length the split plan
+ * is taken from (>= k->ne[1]).  Shapes and dst as oo_flash_attn_ext. */
+enum { OO_FAK_SPLIT = 0, OO_FAK_HEADS = 1, OO_FAK_GQA = 2 };
+int oo_fa_device(const oo_tensor *q, const oo_tensor *k, const oo_tensor *v, const oo_tensor *mask, float scale,
+                 int kind, int64_t nkv_max, oo_tensor *dst);
+/* the split count the device plans for `kind` over a cache of nkv_max positions with
+ * `groups` CTA groups (fattn.cu) */
+int oo_fa_device_splits(int kind, int64_t nkv_max, int64_t groups);
 
 #ifdef __cplusplus
 }

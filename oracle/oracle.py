@@ -20,6 +20,10 @@ LIB_PATH = os.path.join(HERE, "liboasr_oracle.so")
 
 F32, F16, Q4_0, Q8_0, Q4_K, Q8_K, I32 = 0, 1, 2, 8, 12, 15, 26
 FA_GGML, FA_F32, FA_TC128 = 0, 1, 2
+# decode-attention kernels whose arithmetic oo_fa_device restates (fattn.cu)
+FAK_SPLIT, FAK_HEADS, FAK_GQA = 0, 1, 2
+# norm reduction layouts (elementwise.cu): one warp per 32E-element chunk, or the 256-thread row kernel
+NORM_E8, NORM_E4, NORM_ROW = 8, 4, 0
 BLOCK = {F32: (1, 4), F16: (1, 2), Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q8_K: (256, 292)}
 
 
@@ -45,7 +49,8 @@ _lib = None
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(os.path.join(HERE, "oracle.c")):
+        src_mtime = max(os.path.getmtime(os.path.join(HERE, f)) for f in ("oracle.c", "oracle.h"))
+        if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < src_mtime:
             build()
         L = ctypes.CDLL(LIB_PATH)
         P, I64, F, I = ctypes.c_void_p, ctypes.c_int64, ctypes.c_float, ctypes.c_int
@@ -65,6 +70,10 @@ def lib():
         for name in ("oo_gelu", "oo_silu"):
             getattr(L, name).argtypes, getattr(L, name).restype = [P, P, I64], None
         L.oo_rope_neox.argtypes, L.oo_rope_neox.restype = [P, I64, I64, I64, P, F], None
+        L.oo_expf.argtypes, L.oo_expf.restype = [F], F
+        L.oo_norm_dev.argtypes, L.oo_norm_dev.restype = [P, P, I64, I64, F, I, I], None
+        L.oo_fa_device.argtypes, L.oo_fa_device.restype = [TP, TP, TP, TP, F, I, I64, TP], I
+        L.oo_fa_device_splits.argtypes, L.oo_fa_device_splits.restype = [I, I64, I64], I
         _lib = L
     return _lib
 
@@ -238,3 +247,61 @@ def rope_neox(x: np.ndarray, pos: np.ndarray, freq_base: float) -> np.ndarray:
     p = np.ascontiguousarray(pos, np.int32)
     lib().oo_rope_neox(_ptr(y), D, H, T, _ptr(p), freq_base)
     return y
+
+
+# ---- the decode path's canonical arithmetic (oracle.h) ------------------------------------
+def expf(x) -> np.ndarray:
+    """the decode path's e^x (oo_expf) elementwise"""
+    x = np.asarray(x, np.float32)
+    f = lib().oo_expf
+    return np.array([f(float(v)) for v in x.ravel()], np.float32).reshape(x.shape)
+
+
+def norm_dev(x: np.ndarray, eps: float, rms: bool, layout: int) -> np.ndarray:
+    """LayerNorm / RMSNorm of the last axis with the device's reduction tree (oo_norm_dev)"""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty_like(x)
+    lib().oo_norm_dev(_ptr(x), _ptr(y), x.shape[-1], x.size // x.shape[-1], eps, 1 if rms else 0, layout)
+    return y
+
+
+def norm_layout(n: int, family: int | None) -> int:
+    """the reduction layout the device's residual + norm (+ quantize) kernel uses for rows of n
+    whose output feeds a mul_mat of activation family `family` (Q8_0 -> q8_0 planes, Q4_K ->
+    q8_K planes, None -> f32 only): elementwise.cu launch_resid_norm_quant"""
+    E = 4 if family == Q8_0 else 8
+    if n % (32 * E) == 0 and n // (32 * E) <= 32 and (family != Q8_K or n % 256 == 0):
+        return E
+    return NORM_ROW
+
+
+def fa_device(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask: np.ndarray | None, scale: float,
+              kind: int, nkv_max: int | None = None) -> np.ndarray:
+    """Decode attention with the device kernels' arithmetic (oo_fa_device).  Shapes as
+    flash_attn_ext; k / v hold the live prefix, nkv_max the cache length (split plan)."""
+    q = np.ascontiguousarray(q, np.float32)
+    k = np.ascontiguousarray(k)
+    v = np.ascontiguousarray(v)
+    kt = F16 if k.dtype == np.float16 else F32
+    S, H, NQ, D = q.shape
+    tq = tensor(q, F32)
+    tk = tensor(k.view(np.uint16) if kt == F16 else k, kt)
+    tv = tensor(v.view(np.uint16) if kt == F16 else v, kt)
+    tm = None
+    if mask is not None:
+        mask = np.ascontiguousarray(mask.view(np.uint16) if mask.dtype == np.float16 else mask)
+        tm = tensor(mask, F16)
+        tm.nb[:] = [2, mask.shape[-1] * 2, mask.shape[-1] * 2 * mask.shape[-2],
+                    mask.shape[-1] * 2 * mask.shape[-2] * (mask.shape[-3] if mask.ndim >= 3 else 1)]
+    out = np.zeros((S, NQ, H, D), np.float32)
+    to = tensor(out, F32)
+    nkv_max = k.shape[-2] if nkv_max is None else nkv_max
+    rc = lib().oo_fa_device(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv),
+                            ctypes.byref(tm) if tm is not None else None, scale, kind, nkv_max, ctypes.byref(to))
+    if rc != 0:
+        raise RuntimeError(f"oo_fa_device failed ({rc})")
+    return out
+
+
+def fa_device_splits(kind: int, nkv_max: int, groups: int = 1) -> int:
+    return int(lib().oo_fa_device_splits(kind, nkv_max, groups))

@@ -16,8 +16,11 @@ decode step attends over the live prefix (run_step, llm_transformer.rs:3203).
 Prompt attention of `tc_min_rows` or more positions is evaluated in the
 oracle's tensor-core arithmetic mode (fp16 operands and probabilities, 128-key
 blocks), the arithmetic the device's prompt pass is specified to use (ggml's
-CUDA backend makes the same fp16 conversion); shorter prompts and decode steps
-use f32 accumulation.
+CUDA backend makes the same fp16 conversion); its accumulation inside the MMA
+unit is the hardware's, so that op is checked against a bound.  Shorter prompts
+and every decode step use the canonical summation orders of oracle.h (RMSNorm
+trees, the split / GQA decode attention, the SiLU's e^x, block-order mul_mat):
+a decode step from the same cache is the device's bit for bit.
 Every elementwise op rounds to float32 separately, as ggml's f32 ops do.
 """
 from __future__ import annotations
@@ -58,20 +61,26 @@ class QwenRef:
         return oo.mul_mat(data, t, ne[0], ne[1], np.ascontiguousarray(x, np.float32))
 
     def rms(self, x, w):
-        return (oo.rms_norm(x, self.cfg.rms_eps) * w).astype(np.float32)
+        """RMSNorm * w with the device's reduction tree: rows of d feed a Q8_0 mul_mat
+        (q8_0 planes); per-head rows of 128 are one warp (qkv_post in model_qwen.cu)"""
+        x = np.asarray(x, np.float32)
+        n = x.shape[-1]
+        layout = oo.norm_layout(n, oo.Q8_0) if n != self.cfg.head_dim else oo.NORM_E4
+        return (oo.norm_dev(x, self.cfg.rms_eps, True, layout) * w).astype(np.float32)
 
-    def new_cache(self, n_seq: int = 1):
-        """per layer (K, V) f16 [n_seq][n_kv_heads][max_pos][head_dim]"""
+    def new_cache(self, n_seq: int = 1, n_pos: int | None = None):
+        """per layer (K, V) f16 [n_seq][n_kv_heads][n_pos (default max_pos)][head_dim]"""
         c = self.cfg
-        shape = (n_seq, c.n_kv_heads, c.max_pos, c.head_dim)
+        shape = (n_seq, c.n_kv_heads, n_pos or c.max_pos, c.head_dim)
         return [(np.zeros(shape, np.float16), np.zeros(shape, np.float16)) for _ in range(c.n_layers)]
 
     def embed(self, tokens) -> np.ndarray:
         t, ne, data = self.T["token_embd.weight"]
         return np.stack([oo.dequantize(t, data[int(k):int(k) + 1], ne[0])[0] for k in tokens]).astype(np.float32)
 
-    def layer(self, x: np.ndarray, l: int, cache, s: int, pos0: int):
-        """x [T][d] = tokens at positions pos0..pos0+T-1 of sequence s; updates cache[l][:, s]."""
+    def layer(self, x: np.ndarray, l: int, cache, s: int, pos0: int, decode: bool = False):
+        """x [T][d] = tokens at positions pos0..pos0+T-1 of sequence s; updates cache[l][:, s].
+        decode: a decode step (one row attending over a cache of max_pos positions)."""
         c = self.cfg
         T, D, H, HKV = x.shape[0], c.head_dim, c.n_heads, c.n_kv_heads
         p = f"blk.{l}."
@@ -89,10 +98,17 @@ class QwenRef:
         vc[s, :, pos0:pos0 + T] = _f16(v.transpose(1, 0, 2))
         n_kv = pos0 + T
         mask = causal_mask(T, n_kv, pos0) if T > 1 else None
-        mode = oo.FA_TC128 if T >= self.tc_min_rows and pos0 == 0 else oo.FA_F32
-        a = oo.flash_attn_ext(np.ascontiguousarray(q.transpose(1, 0, 2))[None],
-                              np.ascontiguousarray(kc[s:s + 1, :, :n_kv]), np.ascontiguousarray(vc[s:s + 1, :, :n_kv]),
-                              mask, float(np.float32(1.0) / np.sqrt(np.float32(D))), mode)  # (1, T, H, D)
+        qh = np.ascontiguousarray(q.transpose(1, 0, 2))[None]
+        kk, vv = np.ascontiguousarray(kc[s:s + 1, :, :n_kv]), np.ascontiguousarray(vc[s:s + 1, :, :n_kv])
+        scale = float(np.float32(1.0) / np.sqrt(np.float32(D)))
+        if T >= self.tc_min_rows and pos0 == 0:
+            a = oo.flash_attn_ext(qh, kk, vv, mask, scale, oo.FA_TC128)  # (1, T, H, D)
+        elif T == 1:
+            # one query row over head-major f16 rows of 256 bytes: the GQA decode kernel, its
+            # split plan taken from the cache length (decode) or the prompt length (prefill)
+            a = oo.fa_device(qh, kk, vv, None, scale, oo.FAK_GQA, c.max_pos if decode else n_kv)
+        else:
+            a = oo.fa_device(qh, kk, vv, mask, scale, oo.FAK_SPLIT, n_kv)
         x = (x + self.lin(p + "attn_output.weight", a.reshape(T, H * D))).astype(np.float32)
         h = self.rms(x, self.vec(p + "ffn_norm.weight"))
         g = self.lin(p + "ffn_gate.weight", h)
@@ -118,7 +134,7 @@ class QwenRef:
         for s, tok in enumerate(tokens):
             x = self.embed([tok])
             for l in range(self.cfg.n_layers):
-                x = self.layer(x, l, cache, s, pos)
+                x = self.layer(x, l, cache, s, pos, decode=True)
             out.append(self.head(x)[0])
         return np.array(out)
 

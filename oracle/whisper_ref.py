@@ -10,6 +10,13 @@ reference's per-utterance graphs with float32 numpy for the elementwise glue
   decoder    whisper/ggml_decoder_graph.rs:2840-3010
 The DFT is evaluated in float64 (the reference uses rustfft; both round to
 f32 power spectra).
+The norms, the decode attentions and the matrix products follow the canonical
+summation orders of oracle.h (the device's orders), so a decoder step given the
+same encoder output is reproduced bit for bit.  The encoder's tensor-core ops
+(the fp16 conv GEMM and the 1500-frame attention) accumulate inside the MMA
+unit, whose f32 addition order is the hardware's; the encoder is therefore
+checked against bounds, and decoding is compared from the device's encoder
+output.
 """
 from __future__ import annotations
 
@@ -82,8 +89,16 @@ def _f16(x):
     return np.asarray(x, np.float32).astype(np.float16)
 
 
-def layer_norm(x, g, b):
-    return (oo.norm(x, float(LN_EPS)) * g + b).astype(np.float32)
+def layer_norm(x, g, b, family=None):
+    """LayerNorm with the device's reduction tree for rows feeding a mul_mat of `family`"""
+    x = np.asarray(x, np.float32)
+    y = oo.norm_dev(x, float(LN_EPS), False, oo.norm_layout(x.shape[-1], family))
+    return (y * g + b).astype(np.float32)
+
+
+def act_family(wtype: int) -> int:
+    """activation family (vec_dot type) of a weight type"""
+    return oo.Q8_K if wtype == oo.Q4_K else oo.Q8_0
 
 
 def conv1d(x_ct: np.ndarray, w_f16_bits: np.ndarray, ic: int, oc: int, stride: int, bias: np.ndarray):
@@ -104,6 +119,10 @@ class WhisperRef:
         self.cfg = cfg
         self.T = pack
         self.enc_fa_mode = enc_fa_mode
+        self.ef = act_family(pack["encoder.blocks.0.attn.query.weight"][0])
+        self.df = act_family(pack["decoder.blocks.0.attn.query.weight"][0])
+        # decode attention kernel: 4 heads per CTA when the head count allows it (fattn.cu)
+        self.fak = oo.FAK_HEADS if cfg.n_heads % 4 == 0 else oo.FAK_SPLIT
 
     def w(self, name):
         return self.T[name]
@@ -129,15 +148,15 @@ class WhisperRef:
         T = x.shape[0]
         for i in range(c.n_enc_layers):
             p = f"encoder.blocks.{i}."
-            h = layer_norm(x, self.vec(p + "attn_ln.weight"), self.vec(p + "attn_ln.bias"))
+            h = layer_norm(x, self.vec(p + "attn_ln.weight"), self.vec(p + "attn_ln.bias"), self.ef)
             q, k, v = self.lin(p + "attn.query", h), self.lin(p + "attn.key", h), self.lin(p + "attn.value", h)
             heads = lambda a: np.ascontiguousarray(a.reshape(T, H, 64).transpose(1, 0, 2))[None]
             a = oo.flash_attn_ext(heads(q), heads(k), heads(v), None, 0.125, self.enc_fa_mode)  # (1, T, H, 64)
             x = (x + self.lin(p + "attn.out", a.reshape(T, d))).astype(np.float32)
-            h = layer_norm(x, self.vec(p + "mlp_ln.weight"), self.vec(p + "mlp_ln.bias"))
+            h = layer_norm(x, self.vec(p + "mlp_ln.weight"), self.vec(p + "mlp_ln.bias"), self.ef)
             f = oo.gelu(self.lin(p + "mlp.0", h))
             x = (x + self.lin(p + "mlp.2", f)).astype(np.float32)
-        return layer_norm(x, self.vec("encoder.ln_post.weight"), self.vec("encoder.ln_post.bias"))
+        return layer_norm(x, self.vec("encoder.ln_post.weight"), self.vec("encoder.ln_post.bias"), self.df)
 
     def cross_kv(self, enc: np.ndarray):
         """per decoder layer (K f16 [T][d], V f16 [T][d])"""
@@ -161,25 +180,25 @@ class WhisperRef:
         x = (emb + self.vec("decoder.positional_embedding").reshape(-1, d)[pos]).astype(np.float32)[None]
         for i in range(c.n_dec_layers):
             p = f"decoder.blocks.{i}."
-            h = layer_norm(x, self.vec(p + "attn_ln.weight"), self.vec(p + "attn_ln.bias"))
+            h = layer_norm(x, self.vec(p + "attn_ln.weight"), self.vec(p + "attn_ln.bias"), self.df)
             q, k, v = self.lin(p + "attn.query", h), self.lin(p + "attn.key", h), self.lin(p + "attn.value", h)
             kc, vc = self_kv[i]
             kc[pos], vc[pos] = _f16(k[0]), _f16(v[0])
             kk = np.ascontiguousarray(kc[:pos + 1].reshape(pos + 1, H, 64).transpose(1, 0, 2))[None]
             vv = np.ascontiguousarray(vc[:pos + 1].reshape(pos + 1, H, 64).transpose(1, 0, 2))[None]
-            a = oo.flash_attn_ext(q.reshape(1, H, 1, 64).copy(), kk, vv, None, 0.125, oo.FA_F32)
+            a = oo.fa_device(q.reshape(1, H, 1, 64).copy(), kk, vv, None, 0.125, self.fak, c.n_text_ctx)
             x = (x + self.lin(p + "attn.out", a.reshape(1, d))).astype(np.float32)
-            h = layer_norm(x, self.vec(p + "cross_attn_ln.weight"), self.vec(p + "cross_attn_ln.bias"))
+            h = layer_norm(x, self.vec(p + "cross_attn_ln.weight"), self.vec(p + "cross_attn_ln.bias"), self.df)
             q = self.lin(p + "cross_attn.query", h)
             ck, cv = cross[i]
             Tn = ck.shape[0]
             kk = np.ascontiguousarray(ck.reshape(Tn, H, 64).transpose(1, 0, 2))[None]
             vv = np.ascontiguousarray(cv.reshape(Tn, H, 64).transpose(1, 0, 2))[None]
-            a = oo.flash_attn_ext(q.reshape(1, H, 1, 64).copy(), kk, vv, None, 0.125, oo.FA_F32)
+            a = oo.fa_device(q.reshape(1, H, 1, 64).copy(), kk, vv, None, 0.125, self.fak, Tn)
             x = (x + self.lin(p + "cross_attn.out", a.reshape(1, d))).astype(np.float32)
-            h = layer_norm(x, self.vec(p + "mlp_ln.weight"), self.vec(p + "mlp_ln.bias"))
+            h = layer_norm(x, self.vec(p + "mlp_ln.weight"), self.vec(p + "mlp_ln.bias"), self.df)
             x = (x + self.lin(p + "mlp.2", oo.gelu(self.lin(p + "mlp.0", h)))).astype(np.float32)
-        h = layer_norm(x, self.vec("decoder.ln.weight"), self.vec("decoder.ln.bias"))
+        h = layer_norm(x, self.vec("decoder.ln.weight"), self.vec("decoder.ln.bias"), oo.Q8_0)
         logits = oo.mul_mat(data, t, ne[0], ne[1], h)[0]
         return logits
 

@@ -315,3 +315,89 @@ def test_q8_0_kv_is_refused_like_the_reference_gpu_surface(gpu_backend):
     gpu_backend.synchronize()
     assert torch.all(out == 7.0)  # nothing was written
 
+
+
+# ---- decode attention: bit-exact against the oracle's restatement of the kernels ----------
+# The decode kernels fix their summation order (fmaf dot chains per lane, xor butterflies,
+# block-wise or per-position online softmax with the decode path's e^x, warp and split
+# merges with fused products) and their split plans depend on the cache length only, so
+# oo_fa_device reproduces them bit for bit.
+
+def _fa_views(be, q, kview, vview, mask, scale):
+    import torch
+
+    S, H, NQ, D = q.shape
+    out = torch.empty((S, NQ, H, D), dtype=torch.float32, device="cuda")
+    mt = torch.from_numpy(np.ascontiguousarray(mask)).cuda() if mask is not None else None
+    be.flash_attn_ext(torch.from_numpy(np.ascontiguousarray(q)).cuda(), kview, vview, mt, scale, out)
+    be.synchronize()
+    return out.cpu().numpy()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("S", [1, 3, 8])
+@pytest.mark.parametrize("n_kv", [1, 5, 33, 448, 1500])
+def test_heads_decode_kernel_is_bit_exact(gpu_backend, S, n_kv):
+    """Whisper-large decoder layout (20 heads of 64, heads contiguous in a cache row):
+    the 4-head kernel, self-attention cache [seq][pos][d] and the cross cache whose row
+    holds K then V ([seq][frame][K d | V d])."""
+    import torch
+
+    H, D = 20, 64
+    rng = np.random.default_rng(400 + S + n_kv)
+    q = rng.normal(0, 1, (S, H, 1, D)).astype(np.float32)
+    kv = torch.from_numpy(rng.normal(0, 1, (S, n_kv, 2, H, D)).astype(np.float16)).cuda()
+    k = kv[:, :, 0].permute(0, 2, 1, 3)
+    v = kv[:, :, 1].permute(0, 2, 1, 3)
+    got = _fa_views(gpu_backend, q, k, v, None, 0.125)
+    ref = oo.fa_device(q, k.cpu().numpy(), v.cpu().numpy(), None, 0.125, oo.FAK_HEADS)
+    np.testing.assert_array_equal(got, ref)
+    # a sequence's output does not depend on the batch it runs in
+    if S > 1:
+        np.testing.assert_array_equal(_fa_views(gpu_backend, q[1:2], k[1:2], v[1:2], None, 0.125), got[1:2])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("G", [1, 2, 4])
+@pytest.mark.parametrize("S", [1, 4, 8])
+@pytest.mark.parametrize("n_kv", [1, 40, 391, 2048])
+def test_gqa_decode_kernel_is_bit_exact(gpu_backend, G, S, n_kv):
+    """Qwen decoder layout: head-major f16 caches [seq][kv head][pos][128] (256-byte rows),
+    G query heads per kv head, one query row: the GQA kernel."""
+    import torch
+
+    HKV, D, P = 8, 128, 2048
+    H = HKV * G
+    rng = np.random.default_rng(500 + G * 100 + S + n_kv)
+    q = rng.normal(0, 1, (S, H, 1, D)).astype(np.float32)
+    kc = torch.from_numpy(rng.normal(0, 1, (S, HKV, P, D)).astype(np.float16)).cuda()
+    vc = torch.from_numpy(rng.normal(0, 1, (S, HKV, P, D)).astype(np.float16)).cuda()
+    k, v = kc[:, :, :n_kv], vc[:, :, :n_kv]
+    scale = float(np.float32(1 / np.sqrt(128)))
+    got = _fa_views(gpu_backend, q, k, v, None, scale)
+    ref = oo.fa_device(q, k.cpu().numpy(), v.cpu().numpy(), None, scale, oo.FAK_GQA)
+    np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("D,H,HKV,NQ,n_kv,masked,kv_dtype", [
+    (64, 6, 6, 1, 37, False, np.float16),      # whisper-tiny self-attention (6 heads)
+    (64, 6, 6, 1, 1500, False, np.float16),    # whisper-tiny cross-attention
+    (64, 4, 2, 3, 200, False, np.float32),     # f32 K/V, GQA, a query tile
+    (128, 16, 8, 5, 5, True, np.float16),      # Qwen prompt of 5 rows (causal mask)
+    (128, 16, 8, 63, 63, True, np.float16),    # Qwen prompt of 63 rows
+    (128, 16, 8, 1, 700, True, np.float16),    # masked decode row
+])
+def test_split_decode_kernel_is_bit_exact(gpu_backend, D, H, HKV, NQ, n_kv, masked, kv_dtype):
+    S = 2
+    q, k, v = _case(600 + D + NQ + n_kv, S, H, HKV, NQ, n_kv, D, kv_dtype)
+    mask = None
+    if masked:
+        mask = np.zeros((S, 1, NQ, n_kv), np.float16)
+        for s in range(S):
+            for t in range(NQ):
+                mask[s, 0, t, n_kv - NQ + t + 1 - s:] = -np.inf
+    scale = float(np.float32(1 / np.sqrt(D)))
+    got = _fa(gpu_backend, q, k, v, mask, scale)
+    ref = oo.fa_device(q, k, v, mask, scale, oo.FAK_SPLIT)
+    np.testing.assert_array_equal(got, ref)

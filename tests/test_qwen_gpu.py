@@ -1,31 +1,24 @@
-"""Model-level parity of the Qwen3-ASR decoder driver (oasr_b200_qwen_*) against
-the CPU restatement in oracle/qwen_ref.py, on seeded synthetic packs
-(Qwen3-ASR-0.6B widths, at reduced depth and vocab
-for the step-by-step checks and at full size for the prefill / smoke checks).
+"""Model-level parity of the Qwen3-ASR decoder driver (oasr_b200_qwen_*) against the
+CPU restatement in oracle/qwen_ref.py, on seeded synthetic packs (BASELINE.json
+Qwen3-ASR-0.6B widths; reduced depth and vocab for the fast checks, the
+full 28-layer model for greedy decoding at batch 1, 4 and 8).
 
-What is exact and what is not follows from ggml's arithmetic:
-  * Layer 0's K/V cache rows of a prompt depend only on the embeddings, RMSNorm,
-    the Q8_0 projections (integer block dots, in-order epilogue: bit-exact on
-    the tensor cores), the per-head norms and RoPE (rotation table from the
-    host's libm, like the CPU op): they equal the oracle's bit for bit.  A
-    one-layer model agrees with the oracle to f32 noise (measured ~2e-7 of the
-    largest logit) in prefill and in every decode step.
-  * Past the first attention the f32 summation order differs (split-KV merges
-    vs the oracle's sequential online softmax), so a value sitting on a q8_0
-    rounding boundary flips one quantization step now and then, and the flips
-    propagate through the layers (the same happens between ggml's own CPU
-    builds).  Decode rows carry small N(0, 0.02) token embeddings, so their
-    hidden state is mostly attention output and shows the noise most.  Measured
-    on the seeded packs (max / median of |diff| / max |logit|): 2 layers,
-    prefill 5e-3 / 1e-3, decode 1.1e-2 / 2e-3; 28 layers, prefill 2e-2 / 3e-3,
-    decode 4e-2 / 6e-3.  The bounds below sit about 2x above those, and the
-    greedy token must match wherever the oracle's top-2 margin exceeds the
-    noise bound.
-  * Same kernels on the same inputs give the same bits: the CUDA-graph greedy
-    loop equals host-driven steps, and a batch equals its sequences run alone
-    (the reference's batched == serial checks, batched_decode.rs); a decode
-    step equals a prefill whose last row is that token's embedding up to the
-    attention's split order.
+The criterion is bit equality.  Every op of a decode step follows one summation
+order on the device and in the oracle (block-order mul_mat, the RMSNorm reduction
+trees, the GQA / split decode attentions with the decode path's e^x, SiLU with the
+same e^x), so:
+  * a prompt shorter than 64 rows (split-KV attention under the causal mask) gives
+    the oracle's caches and logits exactly;
+  * a decode step from the same caches gives the oracle's logits exactly, hence the
+    same greedy token, for every one of the 256 steps of configs[2];
+  * a sequence's tokens do not depend on its batch (batched == serial, the
+    reference's batched_decode.rs property) because the attention split plans
+    depend on the cache length only.
+The one op that is not reproduced bit for bit is the tensor-core causal attention of
+prompts of 64+ rows: its QK^T and PV products accumulate inside the MMA unit in the
+hardware's order.  It is pinned op-level (test_flash_attn_gpu.py::
+test_causal_tensor_core_attention) and, here, by a bound on the prompt's logits; the
+decode that follows starts from the device's own caches and is then bit-exact.
 """
 import numpy as np
 import pytest
@@ -34,12 +27,10 @@ import openasr_b200 as ob
 from openasr_b200 import models as om
 from oracle import oracle as oo
 from oracle import qwen_ref as qr
-from tests.conftest import max_abs_rel
 
-FLIP = 2e-2       # 2 layers: bound on quantization-flip noise in logits (relative to max |logit|)
-FLIP_DEEP = 8e-2  # 28 layers
 MID = om.QWEN3_ASR_0_6B.replace(n_layers=2, n_vocab=4096, max_pos=256, max_prefill=64, max_batch=4)
 ONE = MID.replace(n_layers=1)
+TC_BOUND = 2e-2  # tensor-core prompt pass: max |logit diff| / max |logit|
 
 
 @pytest.fixture(scope="module")
@@ -59,64 +50,96 @@ def prefix(n, T, seed=0x0A5A3000, d=1024):
     return om.qwen_synthetic_prefix(seed, n, T, d)
 
 
-def check_token(got, ref_logits, where, noise=FLIP):
-    """greedy token: must match the oracle unless its top-2 margin is within the noise"""
-    top2 = np.sort(ref_logits)[-2:]
-    if top2[1] - top2[0] > noise * np.abs(ref_logits).max():
-        assert got == oo.argmax_first(ref_logits)[0], where
-
-
-def assert_mostly_exact(errs, exact=1e-5):
-    """Steps agree to f32 noise unless one value landed on a q8_0 rounding boundary
-    (measured: a single flip moves a one-layer decode row's logits by ~1.2e-2 of the
-    largest logit); flips are a minority and stay within FLIP."""
-    errs = np.asarray(errs)
-    assert errs.max() < FLIP, errs
-    assert (errs < exact).sum() * 2 > len(errs), errs
-
-
 def rel_stats(got, ref):
     d = np.abs(np.asarray(got, np.float64) - ref) / np.abs(ref).max()
     return float(d.max()), float(np.median(d))
 
 
+def device_cache(m, ref, n_seq, n_pos, cap=None):
+    """the oracle's cache layout (cap positions) filled with the device's first n_pos K/V
+    rows of every layer"""
+    cache = ref.new_cache(n_seq, cap or ref.cfg.max_pos)
+    for layer in range(ref.cfg.n_layers):
+        for s in range(n_seq):
+            k, v = m.read_kv(layer, s, n_pos)
+            cache[layer][0][s, :, :n_pos] = k
+            cache[layer][1][s, :, :n_pos] = v
+    return cache
+
+
+def assert_cache_equal(m, cache, n_seq, n_pos, layers):
+    for layer in layers:
+        for s in range(n_seq):
+            k, v = m.read_kv(layer, s, n_pos)
+            np.testing.assert_array_equal(k.view(np.uint16), cache[layer][0][s, :, :n_pos].view(np.uint16),
+                                          err_msg=f"K layer {layer} seq {s}")
+            np.testing.assert_array_equal(v.view(np.uint16), cache[layer][1][s, :, :n_pos].view(np.uint16),
+                                          err_msg=f"V layer {layer} seq {s}")
+
+
 @pytest.mark.gpu
-def test_one_layer_matches_reference_to_f32_noise(gpu_backend):
+def test_one_layer_prefill_and_decode_are_bit_exact(gpu_backend):
     pack = om.qwen_synthetic_pack(ONE, seed=0x0A5A0003)
     m = om.QwenModel(gpu_backend, ONE, pack)
     try:
         ref = qr.QwenRef(ONE, pack)
         emb = prefix(2, 30, seed=0x0A5A3050)
         logits, nxt = m.prefill(emb)
-        for s in (1, 0):  # sequence 0 last: the decode steps below continue it
-            cache = ref.new_cache(1)
-            lr = ref.prefill(emb[s], cache)
-            assert max_abs_rel(logits[s], lr) < 1e-5
-            check_token(nxt[s], lr, f"prefill {s}", noise=1e-5)
-            k, v = m.read_kv(0, s, 30)
-            np.testing.assert_array_equal(k.view(np.uint16), cache[0][0][0, :, :30].view(np.uint16))
-            np.testing.assert_array_equal(v.view(np.uint16), cache[0][1][0, :, :30].view(np.uint16))
-        errs = []
-        for i, tok in enumerate([5, 4095, 17, 2048, 3000, 1, 999, 123]):
-            g, n1 = m.decode_step([tok], 30 + i)
-            rr = ref.step([tok], 30 + i, cache)[0]
-            errs.append(max_abs_rel(g[0], rr))
-            check_token(n1[0], rr, f"step {i}")
-        assert_mostly_exact(errs)
-        # decode-step K/V rows: the GEMV sums blocks in another order, so f16 rows agree to one ulp
-        k, v = m.read_kv(0, 0, 35)
-        assert np.abs(k.astype(np.float32) - cache[0][0][0, :, :35]).max() <= 2e-3 * np.abs(k.astype(np.float32)).max()
-        assert np.abs(v.astype(np.float32) - cache[0][1][0, :, :35]).max() <= 2e-3 * np.abs(v.astype(np.float32)).max()
+        cache = ref.new_cache(2)
+        for s in range(2):
+            lr = ref.prefill(emb[s], cache, s)
+            np.testing.assert_array_equal(logits[s], lr, err_msg=f"prefill seq {s}")
+            assert nxt[s] == oo.argmax_first(lr)[0]
+        assert_cache_equal(m, cache, 2, 30, [0])
+        for i, toks in enumerate([[5, 4095], [17, 2048], [3000, 1], [999, 123]]):
+            g, n1 = m.decode_step(toks, 30 + i)
+            rr = ref.step(toks, 30 + i, cache)
+            np.testing.assert_array_equal(g, rr, err_msg=f"step {i}")
+            np.testing.assert_array_equal(n1, oo.argmax_first(rr))
+        assert_cache_equal(m, cache, 2, 34, [0])
     finally:
         m.close()
 
 
 @pytest.mark.gpu
+def test_prefill_below_64_rows_is_bit_exact(mid_model, mid):
+    """2 layers: split-KV attention under the causal mask, every cache row and the
+    last-row logits equal to the oracle's."""
+    cfg, pack = mid
+    emb = prefix(3, 40)
+    logits, nxt = mid_model.prefill(emb)
+    ref = qr.QwenRef(cfg, pack)
+    cache = ref.new_cache(3)
+    for s in range(3):
+        lr = ref.prefill(emb[s], cache, s)
+        np.testing.assert_array_equal(logits[s], lr, err_msg=f"prefill seq {s}")
+        assert nxt[s] == oo.argmax_first(lr)[0]
+    assert_cache_equal(mid_model, cache, 3, 40, range(cfg.n_layers))
+
+
+@pytest.mark.gpu
+def test_decode_steps_are_bit_exact_teacher_forced(mid_model, mid):
+    cfg, pack = mid
+    emb = prefix(1, 24, seed=0x0A5A3100)
+    mid_model.prefill(emb)
+    ref = qr.QwenRef(cfg, pack)
+    cache = ref.new_cache(1)
+    ref.prefill(emb[0], cache)
+    for i, tok in enumerate([5, 4095, 17, 2048, 3000, 1, 0, 999, 123, 4000, 7, 77]):
+        pos = 24 + i
+        logits, nxt = mid_model.decode_step([tok], pos)
+        lr = ref.step([tok], pos, cache)[0]
+        np.testing.assert_array_equal(logits[0], lr, err_msg=f"step at {pos}")
+        assert nxt[0] == oo.argmax_first(lr)[0]
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("T", [64, 150, 257])
-def test_one_layer_tensor_core_prompt_pass(gpu_backend, T):
-    """Prompts of 64+ positions take the causal tcgen05 attention (fp16 operands and
-    probabilities, 128-key tiles, the diagonal tile masked in the softmax); the oracle
-    evaluates the same arithmetic (FA_TC128 with the causal mask)."""
+def test_tensor_core_prompt_pass_then_exact_decode(gpu_backend, T):
+    """Prompts of 64+ rows take the causal tcgen05 attention (fp16 operands and
+    probabilities, 128-key tiles).  Layer 0's cache (before any attention) is exact,
+    the prompt's logits are within TC_BOUND, and decoding from the device's caches is
+    bit-exact."""
     cfg = ONE.replace(max_prefill=T, max_pos=512)
     pack = om.qwen_synthetic_pack(cfg, seed=0x0A5A0003)
     m = om.QwenModel(gpu_backend, cfg, pack)
@@ -124,77 +147,18 @@ def test_one_layer_tensor_core_prompt_pass(gpu_backend, T):
         ref = qr.QwenRef(cfg, pack)
         emb = prefix(2, T, seed=0x0A5A3060 + T)
         logits, nxt = m.prefill(emb)
-        g, _ = m.decode_step([11, 22], T)  # decode steps continue from the tensor-core prompt pass
-        for s, tok in ((0, 11), (1, 22)):
-            cache = ref.new_cache(1)
-            lr = ref.prefill(emb[s], cache)
-            # the prompt's last row carries an N(0, 1) embedding: flips move it less than a
-            # decode row (measured <= 3e-3); the attention itself is pinned op-level in
-            # test_flash_attn_gpu.py::test_causal_tensor_core_attention
+        cache = ref.new_cache(2)
+        for s in range(2):
+            lr = ref.prefill(emb[s], cache, s)
             mx, med = rel_stats(logits[s], lr)
-            assert mx < 1e-2 and med < 2e-3, (T, s, mx, med)
-            check_token(nxt[s], lr, f"T={T} seq {s}", noise=1e-2)
-            k, v = m.read_kv(0, s, T)
-            np.testing.assert_array_equal(k.view(np.uint16), cache[0][0][0, :, :T].view(np.uint16))
-            np.testing.assert_array_equal(v.view(np.uint16), cache[0][1][0, :, :T].view(np.uint16))
-            # one step: f32 noise, or a single rounding-boundary flip
-            assert max_abs_rel(g[s], ref.step([tok], T, cache)[0]) < FLIP
+            assert mx < TC_BOUND and med < 2e-3, (T, s, mx, med)
+        assert_cache_equal(m, cache, 2, T, [0])
+        dev = device_cache(m, ref, 2, T)
+        for i in range(3):
+            g, _ = m.decode_step([11 + i, 22 + i], T + i)
+            np.testing.assert_array_equal(g, ref.step([11 + i, 22 + i], T + i, dev), err_msg=f"T={T} step {i}")
     finally:
         m.close()
-
-
-@pytest.mark.gpu
-def test_prefill_layer0_kv_bit_exact_and_logits_match(mid_model, mid):
-    cfg, pack = mid
-    emb = prefix(2, 40)
-    logits, nxt = mid_model.prefill(emb)
-    ref = qr.QwenRef(cfg, pack)
-    for s in range(2):
-        cache = ref.new_cache(1)
-        lr = ref.prefill(emb[s], cache)
-        k0, v0 = mid_model.read_kv(0, s, 40)
-        np.testing.assert_array_equal(k0.view(np.uint16), cache[0][0][0, :, :40].view(np.uint16))
-        np.testing.assert_array_equal(v0.view(np.uint16), cache[0][1][0, :, :40].view(np.uint16))
-        k1, v1 = mid_model.read_kv(1, s, 40)
-        assert max_abs_rel(k1, cache[1][0][0, :, :40]) < FLIP
-        assert max_abs_rel(v1, cache[1][1][0, :, :40]) < FLIP
-        mx, med = rel_stats(logits[s], lr)
-        assert mx < FLIP and med < 3e-3, (mx, med)
-        check_token(nxt[s], lr, f"prefill seq {s}")
-
-
-@pytest.mark.gpu
-def test_decode_steps_match_reference_teacher_forced(mid_model, mid):
-    cfg, pack = mid
-    emb = prefix(1, 24, seed=0x0A5A3100)
-    mid_model.prefill(emb)
-    ref = qr.QwenRef(cfg, pack)
-    cache = ref.new_cache(1)
-    ref.prefill(emb[0], cache)
-    errs = []
-    for i, tok in enumerate([5, 4095, 17, 2048, 3000, 1, 0, 999, 123, 4000, 7, 77]):
-        pos = 24 + i
-        logits, nxt = mid_model.decode_step([tok], pos)
-        lr = ref.step([tok], pos, cache)[0]
-        errs.append(max_abs_rel(logits[0], lr))
-        check_token(nxt[0], lr, f"step at {pos}")
-    assert max(errs) < 2 * FLIP, errs
-    assert np.median(errs) < FLIP, errs
-
-
-@pytest.mark.gpu
-def test_decode_step_equals_prefill_of_appended_row(mid_model, mid):
-    cfg, pack = mid
-    emb = prefix(1, 27, seed=0x0A5A3150)
-    tok = 3210
-    row = qr.QwenRef(cfg, pack).embed([tok])
-    whole, _ = mid_model.prefill(np.concatenate([emb[0], row], 0)[None])
-    mid_model.prefill(emb)
-    step, _ = mid_model.decode_step([tok], 27)
-    # the GEMV and the tensor-core GEMM give the same bits; the attention splits its KV
-    # range differently (f32 noise), which q8_0 quantization absorbs unless a value sits
-    # on a rounding boundary (measured: identical)
-    assert max_abs_rel(step[0], whole[0]) < FLIP
 
 
 @pytest.mark.gpu
@@ -235,8 +199,8 @@ def test_single_position_prompt_and_bounds(mid_model, mid):
     cfg, pack = mid
     emb = prefix(1, 1, seed=0x0A5A3400)
     logits, nxt = mid_model.prefill(emb)
-    lr = qr.QwenRef(cfg, pack).prefill(emb[0], qr.QwenRef(cfg, pack).new_cache(1))
-    assert max_abs_rel(logits[0], lr) < FLIP
+    ref = qr.QwenRef(cfg, pack)
+    np.testing.assert_array_equal(logits[0], ref.prefill(emb[0], ref.new_cache(1)))
     with pytest.raises(ob.GgmlBackendError):
         mid_model.prefill(prefix(1, cfg.max_prefill + 1))
     with pytest.raises(ob.GgmlBackendError):
@@ -246,9 +210,10 @@ def test_single_position_prompt_and_bounds(mid_model, mid):
     np.testing.assert_array_equal(again, logits)
 
 
+# ---- configs[2] at full size: 28 layers, vocab 151936, 390-frame prompts, 256 tokens ------------
 @pytest.fixture(scope="module")
 def full(gpu_backend):
-    cfg = om.QWEN3_ASR_0_6B.replace(max_batch=2, max_prefill=om.QWEN_PREFIX_FRAMES)
+    cfg = om.QWEN3_ASR_0_6B.replace(max_prefill=om.QWEN_PREFIX_FRAMES)
     pack = om.qwen_synthetic_pack(cfg)
     m = om.QwenModel(gpu_backend, cfg, pack)
     yield cfg, pack, m
@@ -256,36 +221,31 @@ def full(gpu_backend):
 
 
 @pytest.mark.gpu
-def test_full_size_prefill_matches_reference(full):
-    """configs[2] shape: 28 layers, vocab 151936, the 390-frame prompt."""
+def test_full_size_greedy_256_is_bit_exact_at_batch_8_4_1(full):
+    """8 sequences of 390 audio-embedding frames, greedy 256 tokens.  The
+    prompt pass runs on the tensor cores (bounded against the oracle's prompt pass);
+    from its caches every one of the 255 decode steps equals the oracle's logits bit
+    for bit, and the CUDA-graph greedy loop gives the same 256 tokens at batch 8, at
+    batch 4 and at batch 1."""
     cfg, pack, m = full
-    emb = prefix(1, om.QWEN_PREFIX_FRAMES, seed=0x0A5A3500)
-    logits, nxt = m.prefill(emb)
+    T, n_new, B = om.QWEN_PREFIX_FRAMES, 256, 8
+    emb = prefix(B, T, seed=0x0A5A3600)
+    logits, first = m.prefill(emb)
     ref = qr.QwenRef(cfg, pack)
-    cache = ref.new_cache(1)
-    lr = ref.prefill(emb[0], cache)
-    k0, v0 = m.read_kv(0, 0, om.QWEN_PREFIX_FRAMES)
-    np.testing.assert_array_equal(k0.view(np.uint16), cache[0][0][0, :, :om.QWEN_PREFIX_FRAMES].view(np.uint16))
-    np.testing.assert_array_equal(v0.view(np.uint16), cache[0][1][0, :, :om.QWEN_PREFIX_FRAMES].view(np.uint16))
+    # the prompt pass against the oracle's own (tensor-core emulation) prompt pass, one sequence
+    lr = ref.prefill(emb[0], ref.new_cache(1, T))
     mx, med = rel_stats(logits[0], lr)
-    assert mx < FLIP_DEEP / 2 and med < 8e-3, (mx, med)
-    check_token(nxt[0], lr, "full-size prefill", noise=FLIP_DEEP)
-    # greedy decode steps on the oracle's tokens
-    tok = int(oo.argmax_first(lr)[0])
-    for i in range(3):
-        l1, n1 = m.decode_step([tok], om.QWEN_PREFIX_FRAMES + i)
-        r1 = ref.step([tok], om.QWEN_PREFIX_FRAMES + i, cache)[0]
-        mx, med = rel_stats(l1[0], r1)
-        assert mx < FLIP_DEEP and med < 1.5e-2, (i, mx, med)
-        check_token(n1[0], r1, f"full-size step {i}", noise=FLIP_DEEP)
-        tok = int(oo.argmax_first(r1)[0])
-
-
-@pytest.mark.gpu
-def test_full_size_batched_generate_equals_serial(full):
-    cfg, pack, m = full
-    emb = prefix(2, om.QWEN_PREFIX_FRAMES, seed=0x0A5A3600)
-    batched = m.generate(emb, 16)
-    assert ((batched >= 0) & (batched < cfg.n_vocab)).all()
-    for s in range(2):
-        np.testing.assert_array_equal(m.generate(emb[s:s + 1], 16)[0], batched[s])
+    assert mx < 2 * TC_BOUND and med < 8e-3, (mx, med)
+    # decode from the device's caches: bit-exact logits and tokens at every step
+    cache = device_cache(m, ref, B, T, T + n_new)
+    toks = [first.copy()]
+    for i in range(n_new - 1):
+        g, nxt = m.decode_step(toks[-1], T + i)
+        r = ref.step(toks[-1], T + i, cache)
+        np.testing.assert_array_equal(g, r, err_msg=f"step {i}")
+        np.testing.assert_array_equal(nxt, oo.argmax_first(r))
+        toks.append(nxt)
+    host = np.stack(toks, axis=1)
+    np.testing.assert_array_equal(m.generate(emb, n_new), host)
+    np.testing.assert_array_equal(m.generate(emb[:4], n_new), host[:4])
+    np.testing.assert_array_equal(m.generate(emb[:1], n_new), host[:1])

@@ -1,23 +1,26 @@
 """Model-level parity of the Whisper driver (oasr_b200_whisper_*) against the
 CPU reference graphs in oracle/whisper_ref.py, on seeded synthetic packs
-(BASELINE.json configs[0] whisper-tiny shape, and the whisper-large-v3 shape at
-reduced depth).
+(BASELINE.json configs[0] whisper-tiny, and configs[3] whisper-large-v3 at full
+depth: 32 encoder + 32 decoder layers, Q4_K linears).
 
-How the criteria follow from ggml's arithmetic: every mul_mat quantizes its
-activations to q8_0 / q8_K first, so an element whose value lands within an
-f32 ulp of a rounding boundary moves by a whole quantization step when the
-f32 summation order differs (GPU reduction trees vs the oracle's sequential
-sums; likewise between ggml's own AVX2 and AVX-512 builds).  Hence:
-  * decoder steps fed the same encoder output must agree to 1e-5 (measured
-    ~1e-7) and pick the same tokens;
-  * the encoder agrees element-wise to 1e-6 in the median after one layer with
-    isolated flip outliers <= 2e-3 (the op-level bar), and the flip noise
-    grows with depth (bounded here at 2e-2 for 4 layers);
-  * greedy transcripts are identical when both sides decode from the same
-    encoder output, and end to end up to the first step whose reference top-2
-    margin is below the encoder flip noise.
-The encoder attention is compared with the oracle's tensor-core arithmetic
-mode (fp16 operands), the rest with ggml CPU semantics."""
+The decoder is compared bit for bit.  Every op of a decode step follows one
+summation order on the device and in the oracle (block-order mul_mat, the
+LayerNorm reduction trees, the 4-head / split decode attentions with the decode
+path's e^x, GELU's fp16 table), so from the same encoder output the device's
+logits equal the oracle's at every step and the greedy transcripts are identical
+-- for all 224 tokens of configs[0] and of configs[3] (two utterances decoded as
+one batch).
+
+The encoder is compared against bounds, and only two of its ops are why: the
+conv stem's fp16 GEMM and the 1500-frame self-attention run on the tensor cores,
+whose MMA unit adds its products in the hardware's order (the oracle evaluates
+the same operand roundings: fp16 inputs, fp16 probabilities, 128-key tiles).
+Their last-bit differences flip a q8 activation now and then (an element within
+one f32 ulp of a rounding boundary moves one quantization step), so the encoder
+output agrees to ~1e-6 in the median and within ENC_BOUND at worst.  Decoding
+from the oracle's own encoder output is therefore reported, not gated, as the
+number of leading tokens that match.
+"""
 import numpy as np
 import pytest
 
@@ -80,82 +83,85 @@ def test_tiny_encoder_flip_noise_is_bounded(tiny_model, tiny):
     assert mx < 2e-2 and med < 1e-3, (mx, med)
 
 
-FLIP = 2e-2  # bound on one quantization flip's effect on a step's logits (relative to max |logit|)
+ENC_BOUND = 2e-2  # encoder output: max |diff| / max |value| (4 layers; flip noise)
+
+
+def greedy_from_device_encoder(model, ref, clips, n_new):
+    """device encoder output of each clip (from the device's log-mel) -> oracle greedy"""
+    out = []
+    for c in clips:
+        enc = model.encode(model.mel([c]), 1)[0]
+        out.append(ref.greedy(ref.cross_kv(enc), om.PROMPT[ref.cfg.n_vocab], n_new))
+    return out
+
+
+def matched_prefix(a, b):
+    a, b = np.asarray(a), np.asarray(b)
+    return len(a) if np.array_equal(a, b) else int(np.argmax(a != b))
 
 
 @pytest.mark.gpu
-def test_tiny_decoder_steps_match_reference_teacher_forced(tiny_model, tiny):
+def test_tiny_decoder_steps_bit_exact_teacher_forced(tiny_model, tiny):
     cfg, pack = tiny
     mel = wr.log_mel(clips(1)[0], 80)
     enc = tiny_model.encode(mel[None], 1)[0]
     ref = wr.WhisperRef(cfg, pack)
     cross, state = ref.cross_kv(enc), ref.new_state()
-    errs = []
     for pos, tok in enumerate(om.PROMPT[cfg.n_vocab] + [11, 2000, 51000, 7] + list(range(100, 2100, 100))):
         logits, nxt = tiny_model.decode_step([tok], pos)
         lr = ref.decode_step(tok, pos, cross, state)
-        errs.append(max_abs_rel(logits[0], lr))
-        top2 = np.sort(lr)[-2:]
-        if top2[1] - top2[0] > FLIP * np.abs(lr).max():
-            assert nxt[0] == oo.argmax_first(lr)[0], pos
-    errs = np.array(errs)
-    # steps agree to f32 noise until a quantization flip lands in the self-KV cache;
-    # from then on the difference persists but stays within FLIP (where the first
-    # flip lands depends on the f32 summation order; see the next test for rates)
-    assert errs.max() < FLIP, errs
+        np.testing.assert_array_equal(logits[0], lr, err_msg=f"position {pos}")
+        assert nxt[0] == oo.argmax_first(lr)[0]
 
 
 @pytest.mark.gpu
-def test_tiny_decoder_first_step_is_exact_except_rare_flips(tiny_model, tiny):
-    """30 fresh first steps (different prompt tokens) from the same encoder output:
-    without a quantization flip a step agrees to f32 noise (~1e-7); flips are
-    a minority (measured 1-7 in 30 on this 4-layer model, depending on the
-    summation order) and bounded by FLIP.  A wrong kernel moves every step, so
-    the median pins the arithmetic."""
+def test_tiny_first_steps_bit_exact_for_30_prompt_tokens(tiny_model, tiny):
+    """30 fresh first steps (different start tokens) from one encoder output."""
     cfg, pack = tiny
     enc = tiny_model.encode(wr.log_mel(clips(1)[0], 80)[None], 1)[0]
     ref = wr.WhisperRef(cfg, pack)
     cross = ref.cross_kv(enc)
-    errs = []
     for tok in range(50258, 50288):
         logits, _ = tiny_model.decode_step([tok], 0)
-        errs.append(max_abs_rel(logits[0], ref.decode_step(tok, 0, cross, ref.new_state())))
-    errs = np.array(errs)
-    assert np.median(errs) < 1e-6, errs
-    assert (errs < 1e-5).sum() >= 15 and errs.max() < FLIP, errs
-
-
-def _agree_until_near_tie(got, toks, logits):
-    """identical, or first divergence at a step whose reference top-2 margin is within the flip bound"""
-    if np.array_equal(got, toks):
-        return len(got)
-    i = int(np.argmax(got != toks))
-    top2 = np.sort(logits[i])[-2:]
-    assert top2[1] - top2[0] <= FLIP * np.abs(logits[i]).max(), (i, got[i], toks[i], top2[1] - top2[0])
-    return i
+        np.testing.assert_array_equal(logits[0], ref.decode_step(tok, 0, cross, ref.new_state()), err_msg=str(tok))
 
 
 @pytest.mark.gpu
-def test_tiny_greedy_224_matches_reference_from_same_encoder(tiny_model, tiny):
-    """30 s of -20 dBFS noise, greedy 224 tokens, batch 1; both sides
-    decode from the GPU encoder output."""
+def test_tiny_greedy_224_bit_exact_from_device_encoder(tiny_model, tiny):
+    """30 s of -20 dBFS noise, greedy 224 tokens, batch 1: the transcript
+    (CUDA-graph decode from PCM) equals the oracle's greedy decode of the device's
+    encoder output, and so do the logits of every step (host-driven steps)."""
     cfg, pack = tiny
     c = clips(1)[0]
     got = tiny_model.transcribe([c], n_new=224)[0]
-    enc = tiny_model.encode(wr.log_mel(c, 80)[None], 1)[0]
     ref = wr.WhisperRef(cfg, pack)
-    toks, logits = ref.greedy(ref.cross_kv(enc), om.PROMPT[cfg.n_vocab], 224)
-    _agree_until_near_tie(got, toks, logits)
+    (toks, logits), = greedy_from_device_encoder(tiny_model, ref, [c], 224)
+    np.testing.assert_array_equal(got, toks)
+    prompt = om.PROMPT[cfg.n_vocab]
+    seq = list(prompt) + list(toks)
+    for pos in range(len(prompt) + 224 - 1):
+        lg, _ = tiny_model.decode_step([seq[pos]], pos)
+        if pos >= len(prompt) - 1:
+            np.testing.assert_array_equal(lg[0], logits[pos - len(prompt) + 1], err_msg=f"position {pos}")
 
 
 @pytest.mark.gpu
-def test_tiny_greedy_end_to_end_agrees_until_a_near_tie(tiny_model, tiny):
+def test_tiny_greedy_end_to_end_from_pcm(tiny_model, tiny, record_property):
+    """The oracle's own log-mel and encoder (tensor-core ops emulated in arithmetic, not
+    in the hardware's addition order) against the device from PCM: the encoder output
+    is within ENC_BOUND and the matched transcript prefix is reported."""
     cfg, pack = tiny
     c = clips(1)[0]
-    got = tiny_model.transcribe([c], n_new=64)[0]
+    got = tiny_model.transcribe([c], n_new=224)[0]
     ref = wr.WhisperRef(cfg, pack)
-    toks, logits = ref.greedy(ref.cross_kv(ref.encode(wr.log_mel(c, 80))), om.PROMPT[cfg.n_vocab], 64)
-    _agree_until_near_tie(got, toks, logits)
+    enc_ref = ref.encode(wr.log_mel(c, 80))
+    enc_dev = tiny_model.encode(tiny_model.mel([c]), 1)[0]
+    mx, med = rel_stats(enc_dev, enc_ref)
+    assert mx < ENC_BOUND and med < 1e-3, (mx, med)
+    toks, _ = ref.greedy(ref.cross_kv(enc_ref), om.PROMPT[cfg.n_vocab], 224)
+    n = matched_prefix(got, toks)
+    record_property("end_to_end_matched_tokens", n)
+    print(f"configs[0] end to end from PCM: {n} of 224 tokens match the oracle's own encoder path")
 
 
 @pytest.mark.gpu
@@ -170,7 +176,8 @@ def test_batched_transcripts_equal_serial(tiny_model):
 def test_large_v3_shape_q4k_reduced_depth(gpu_backend):
     """configs[3] shape (d 1280, 20 heads, 128 mels, Q4_K linears) at 1+2 layers:
     the tensor-core Q4_K GEMM, the fp16 conv GEMM and the tensor-core attention
-    in the encoder; Q4_K GEMV, self- and cross-attention in the decoder."""
+    in the encoder (bounded); the fused decoder GEMVs, the 4-head self- and
+    cross-attention with their q8_K output planes in the decoder (bit-exact)."""
     cfg = om.WHISPER_LARGE_V3.replace(n_enc_layers=1, n_dec_layers=2, max_batch=2)
     pack = om.whisper_synthetic_pack(cfg, seed=0x0A5A0004)
     m = om.WhisperModel(gpu_backend, cfg, pack)
@@ -180,16 +187,33 @@ def test_large_v3_shape_q4k_reduced_depth(gpu_backend):
         enc = m.encode(mel[None], 1)[0]
         ref = wr.WhisperRef(cfg, pack)
         mx, med = rel_stats(enc, ref.encode(mel))
-        # 1280-wide projections: tensor-core attention residuals (~1e-5) flip q8_K
-        # activations in a large share of rows; bounded like the 4-layer tiny encoder
-        assert mx < 2e-2 and med < 1e-3, (mx, med)
+        assert mx < ENC_BOUND and med < 1e-3, (mx, med)
         cross, state = ref.cross_kv(enc), ref.new_state()
-        errs = []
         for pos, tok in enumerate(om.PROMPT[cfg.n_vocab] + [440, 9, 123, 4567]):
             logits, nxt = m.decode_step([tok], pos)
-            errs.append(max_abs_rel(logits[0], ref.decode_step(tok, pos, cross, state)))
-        assert max(errs) < FLIP and np.median(errs) < 1e-5, errs
+            np.testing.assert_array_equal(logits[0], ref.decode_step(tok, pos, cross, state), err_msg=f"position {pos}")
         toks = m.transcribe([c, clips(2)[1]], n_new=8)
         assert toks.shape == (2, 8) and np.all((toks >= 0) & (toks < cfg.n_vocab))
+    finally:
+        m.close()
+
+
+@pytest.mark.gpu
+def test_large_v3_full_depth_greedy_224_bit_exact(gpu_backend, record_property):
+    """configs[3] at full depth (32 encoder + 32 decoder layers, Q4_K linears, Q8_0
+    embeddings / logits head): two utterances decoded as one batch for 224 greedy
+    tokens; each transcript equals the oracle's greedy decode of the device's encoder
+    output for that utterance."""
+    cfg = om.WHISPER_LARGE_V3.replace(max_batch=2)
+    pack = om.whisper_synthetic_pack(cfg, seed=0x0A5A0004)
+    m = om.WhisperModel(gpu_backend, cfg, pack)
+    try:
+        cs = [om.synthetic_audio(0x0A5A2000 + i, int(16000 * s)) for i, s in enumerate((30.0, 12.5))]
+        got = m.transcribe(cs, n_new=224)
+        ref = wr.WhisperRef(cfg, pack)
+        outs = greedy_from_device_encoder(m, ref, cs, 224)
+        for i, (toks, _) in enumerate(outs):
+            np.testing.assert_array_equal(got[i], toks, err_msg=f"utterance {i}")
+        record_property("tokens_compared", 2 * 224)
     finally:
         m.close()
