@@ -158,3 +158,40 @@ def test_quantized_mul_mat_close_to_dequantized_f32():
         exact = x.astype(np.float64) @ wd.T.astype(np.float64)
         rel = np.abs(got - exact).max() / np.abs(exact).max()
         assert rel < 1.5e-2, (qt, rel)  # activation quantization error only
+
+
+# ---- activation quantizers and block dots against an independent numpy restatement ----------
+# tests/golden/gen_vecdot_golden.py restates ggml's q8_K quantizer and the Q4_K x q8_K,
+# Q4_0 x q8_0 and Q8_0 x q8_0 block dots (with the canonical block-order f32 sum) in
+# vectorised numpy, and takes the q8_0 activations from gguf's own quantizer.
+VD = np.load(os.path.join(os.path.dirname(__file__), "golden", "vecdot_numpy.npz"))
+
+
+def test_q8_k_quantizer_matches_independent_restatement():
+    x = VD["q8k_x"]
+    q = oo.quantize(oo.Q8_K, x).reshape(x.shape[0], -1, 292)
+    d = q[..., 0:4].copy().view(np.float32)[..., 0]
+    qs = q[..., 4:260].copy().view(np.int8).reshape(x.shape[0], -1)
+    bs = q[..., 260:292].copy().view(np.int16).reshape(x.shape[0], -1)
+    np.testing.assert_array_equal(d.view(np.uint32), VD["q8k_d"].view(np.uint32))
+    np.testing.assert_array_equal(qs, VD["q8k_qs"])
+    np.testing.assert_array_equal(bs, VD["q8k_bsums"])
+
+
+@pytest.mark.parametrize("name,qt", [("q4k", oo.Q4_K), ("q8_0", oo.Q8_0), ("q4_0", oo.Q4_0)])
+def test_block_dots_match_independent_restatement(name, qt):
+    w, x, y = VD[f"{name}_w"], VD[f"{name}_x"], VD[f"{name}_y"]
+    N, K = w.shape[0], x.shape[1]
+    got = oo.mul_mat(np.ascontiguousarray(w), qt, K, N, x)
+    np.testing.assert_array_equal(got.view(np.uint32), y.view(np.uint32))
+
+
+def test_decode_exp_is_within_one_ulp():
+    """oo_expf, the decode path's e^x (shared algorithm with the device's exp_f32)."""
+    rng = np.random.default_rng(3)
+    x = np.concatenate([rng.uniform(-87, 88, 20000), rng.normal(0, 1, 5000)]).astype(np.float32)
+    got = oo.expf(x).astype(np.float64)
+    ref = np.exp(x.astype(np.float64))
+    ulp = np.spacing(ref.astype(np.float32)).astype(np.float64)
+    assert (np.abs(got - ref) / ulp).max() <= 1.0
+    assert oo.expf(np.array([-np.inf, np.inf, -200.0, 0.0], np.float32)).tolist() == [0.0, np.inf, 0.0, 1.0]
