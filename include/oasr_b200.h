@@ -13,7 +13,8 @@
  *
  * Conventions (identical to ggml's):
  *   - a tensor is {type, data, ne[4], nb[4]}: ne0 is the fastest dimension,
- *     nb are byte strides (ffi.rs:24-30, GgmlTensorLayoutPrefix);
+ *     nb are byte strides -- ggml's tensor geometry as GgmlTensorLayoutPrefix
+ *     reads it (ffi.rs:24-30), see oasr_tensor for how it differs;
  *   - every function returns a ggml_status value (ffi.rs:102-117) and never
  *     aborts the process;
  *   - device tensors live in this device's memory; ops are enqueued on the
@@ -28,6 +29,7 @@
 #ifndef OASR_B200_H
 #define OASR_B200_H
 
+#include <stdbool.h>
 #include <stddef.h>
 #include <stdint.h>
 
@@ -73,17 +75,36 @@ enum oasr_op {
     OASR_OP_ARGMAX_FIRST = 4,
 };
 
-/* GGML_BACKEND_GRAPH_CANCEL_* -- ffi.rs:118-124 */
-enum oasr_cancel {
+/* GGML_BACKEND_GRAPH_CANCEL_* mechanisms and observation granularities -- ffi.rs:118-124 */
+enum oasr_cancel_mechanism {
+    OASR_CANCEL_DISABLED = 0,
     OASR_CANCEL_NATIVE = 1,
+    OASR_CANCEL_SEGMENTED = 2,
+};
+enum oasr_cancel_observation {
+    OASR_CANCEL_OBSERVATION_NONE = 0,
     OASR_CANCEL_OBSERVATION_SUBMISSION_CHECKPOINT = 1,
     OASR_CANCEL_OBSERVATION_GRAPH_COMPLETION = 2,
 };
 
-/* Prefix of struct ggml_tensor the reference reads (ffi.rs:24-30). */
+/* struct ggml_backend_graph_cancel_capability (GgmlBackendGraphCancelCapability,
+ * ffi.rs:125-131): how a compute call honours the abort callback, reported with its
+ * terminal status (ggml_backend_graph_compute_with_abort's out parameter, ffi.rs:453-459).
+ * The host accepts the pairs validate_graph_cancel_capability lists (cpu_graph.rs:7974-8002). */
+typedef struct oasr_cancel_capability {
+    int32_t mechanism;               /* enum oasr_cancel_mechanism */
+    int32_t observation_granularity; /* enum oasr_cancel_observation */
+} oasr_cancel_capability;
+
+/* A tensor: ggml's geometry (type, ne, nb with ne[0] fastest and nb byte strides),
+ * laid out like GgmlTensorLayoutPrefix (ffi.rs:24-30: c_int type, a pointer, i64 ne[4],
+ * usize nb[4]) -- but the pointer is the tensor's data (ggml_tensor.data), where that
+ * prefix has the buffer handle.  It is not a view of struct ggml_tensor: a host fills
+ * it from a ggml_tensor's type / data / ne / nb fields (INTEGRATION.md shows the
+ * conversion). */
 typedef struct oasr_tensor {
     int32_t type;  /* enum oasr_type */
-    int32_t flags; /* reserved, 0 */
+    int32_t flags; /* reserved, 0 (the padding GgmlTensorLayoutPrefix leaves after type) */
     void *data;    /* device pointer (host pointer only where a function says so) */
     int64_t ne[4]; /* elements per dimension, ne[0] fastest */
     int64_t nb[4]; /* byte strides */
@@ -108,8 +129,9 @@ typedef struct oasr_mem_stats {
     int64_t n_weights;
 } oasr_mem_stats;
 
-/* ggml_abort_callback (ffi.rs:334-336): return nonzero to abort. Lock-free. */
-typedef int (*oasr_abort_callback)(void *data);
+/* ggml_abort_callback (ffi.rs:334-336, GgmlAbortCallback: extern "C" fn(*mut c_void) -> bool):
+ * return true to abort.  Called on the thread that enqueues work; must be lock-free. */
+typedef bool (*oasr_abort_callback)(void *data);
 
 typedef struct oasr_backend oasr_backend; /* one device + one stream */
 typedef struct oasr_weight oasr_weight;   /* a resident quantized weight */
@@ -127,6 +149,19 @@ int oasr_b200_supports_op(oasr_backend *be, int32_t op, const oasr_tensor *src0,
 int oasr_b200_set_stream(oasr_backend *be, void *stream);
 void *oasr_b200_get_stream(oasr_backend *be);
 int oasr_b200_synchronize(oasr_backend *be);                   /* merged completion status */
+/* The merged completion status together with the cancel capability of the work it
+ * completes (ggml_backend_graph_compute_with_abort's status + *cancel_capability,
+ * ffi.rs:453-459): the abort callback is polled before every enqueue and between the
+ * steps of the model drivers' decode loops, so a live backend reports
+ * {OASR_CANCEL_NATIVE, OASR_CANCEL_OBSERVATION_SUBMISSION_CHECKPOINT}; a NULL backend
+ * returns OASR_STATUS_FAILED with {OASR_CANCEL_DISABLED, OASR_CANCEL_OBSERVATION_NONE}.
+ * `cancel_capability` may be NULL. */
+int oasr_b200_synchronize_ex(oasr_backend *be, oasr_cancel_capability *cancel_capability);
+/* Entry point lookup by name, as ggml_backend_reg_get_proc_address (ffi.rs:599;
+ * backend.rs:1290) answers a loader: "ggml_backend_memory_get_api_v1" ->
+ * oasr_b200_memory_get_api_v1, and every oasr_b200_* function of this header by its
+ * own name; NULL for any other name.  Host-only (no device needed). */
+void *oasr_b200_get_proc_address(const char *name);
 int oasr_b200_set_abort_callback(oasr_backend *be, oasr_abort_callback cb, void *data);
 int oasr_b200_mem_stats(oasr_backend *be, oasr_mem_stats *out);
 const char *oasr_b200_last_error(oasr_backend *be);
@@ -505,12 +540,25 @@ int oasr_b200_qwen_generate(oasr_qwen *m, const float *emb, int32_t emb_on_devic
 int oasr_b200_qwen_read_kv(oasr_qwen *m, int32_t layer, int32_t seq, int32_t n_pos, uint16_t *k_out,
                            uint16_t *v_out);
 
+/* ---- diagnostics (no reference counterpart) --------------------------------------
+ * Runs the failure path of the bounded pipeline waits that every tensor-core kernel
+ * uses: one CTA waits on an mbarrier that nobody arrives at, gives up after
+ * limit_cycles (1 .. 2^31) SM clocks, records the timeout in the device error word and
+ * returns.  The call returns what oasr_b200_synchronize then reports:
+ * OASR_STATUS_EXECUTION_FAILED with a timeout message; the backend stays usable (a
+ * timeout is not a device fault and does not poison it). */
+int oasr_b200_selftest_bounded_wait(oasr_backend *be, int64_t limit_cycles);
+
 /* ---- host-side helpers (no device work) --------------------------------------- */
 /* ggml_row_size (ffi.rs:619) */
 int64_t oasr_b200_row_size(int32_t type, int64_t ne0);
 /* ggml_quantize_chunk (ffi.rs:623): quantize nrows rows of n_per_row floats
  * starting at row start_row into ggml blocks (Q8_0, Q4_0, Q4_K, F16). Returns
- * bytes written or a negative status. */
+ * bytes written or a negative status.  Q8_0, Q4_0 and F16 are ggml's encoders
+ * (quantize_row_*_ref, bit-exact against gguf-py); Q4_K is NOT ggml's
+ * make_qkx2_quants search but a simple per-32 min/max encoder that writes valid
+ * Q4_K blocks (for synthetic weights) -- decoding follows the format exactly, but
+ * its bytes differ from ggml's Q4_K encoder for the same floats. */
 int64_t oasr_b200_quantize_chunk(int32_t type, const float *src, void *dst, int64_t start_row, int64_t nrows,
                                  int64_t n_per_row);
 /* Deterministic synthetic data: x[i] = mean + std * N(0,1) from SplitMix64

@@ -129,7 +129,27 @@ class OasrQwenConfig(ctypes.Structure):
                  "max_prefill", "max_batch")] + [("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float)]
 
 
-ABORT_CB = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p)
+# ggml_abort_callback: extern "C" fn(*mut c_void) -> bool (ffi.rs:334-336)
+ABORT_CB = ctypes.CFUNCTYPE(ctypes.c_bool, ctypes.c_void_p)
+
+# GGML_BACKEND_GRAPH_CANCEL_* (ffi.rs:118-124)
+CANCEL_DISABLED, CANCEL_NATIVE, CANCEL_SEGMENTED = 0, 1, 2
+CANCEL_OBSERVATION_NONE, CANCEL_OBSERVATION_SUBMISSION_CHECKPOINT, CANCEL_OBSERVATION_GRAPH_COMPLETION = 0, 1, 2
+
+
+class CancelCapability(ctypes.Structure):
+    """struct ggml_backend_graph_cancel_capability (ffi.rs:125-131)"""
+    _fields_ = [("mechanism", ctypes.c_int32), ("observation_granularity", ctypes.c_int32)]
+
+
+def valid_cancel_capability(status: int, cap: CancelCapability) -> bool:
+    """the pairs the reference host accepts with a terminal status
+    (validate_graph_cancel_capability, cpu_graph.rs:7974-8002)"""
+    m, o = cap.mechanism, cap.observation_granularity
+    pair = ((m, o) == (CANCEL_DISABLED, CANCEL_OBSERVATION_NONE)
+            or (m in (CANCEL_SEGMENTED, CANCEL_NATIVE)
+                and o in (CANCEL_OBSERVATION_SUBMISSION_CHECKPOINT, CANCEL_OBSERVATION_GRAPH_COMPLETION)))
+    return pair and not (status == 0 and m == CANCEL_DISABLED)
 
 
 # ---- memory API v1 (ffi.rs:144-333; fixed widths of backend_memory.rs:697-704) ----------
@@ -237,6 +257,9 @@ SIGNATURES = {
     "oasr_b200_set_stream": ([_P, _P], ctypes.c_int),
     "oasr_b200_get_stream": ([_P], _P),
     "oasr_b200_synchronize": ([_P], ctypes.c_int),
+    "oasr_b200_synchronize_ex": ([_P, ctypes.POINTER(CancelCapability)], ctypes.c_int),
+    "oasr_b200_get_proc_address": ([ctypes.c_char_p], _P),
+    "oasr_b200_selftest_bounded_wait": ([_P, _I64], ctypes.c_int),
     "oasr_b200_set_abort_callback": ([_P, ABORT_CB, _P], ctypes.c_int),
     "oasr_b200_mem_stats": ([_P, ctypes.POINTER(OasrMemStats)], ctypes.c_int),
     "oasr_b200_last_error": ([_P], ctypes.c_char_p),
@@ -434,6 +457,13 @@ class Backend:
     def synchronize(self) -> None:
         self._check(lib().oasr_b200_synchronize(self.handle))
 
+    def synchronize_ex(self) -> tuple[int, CancelCapability]:
+        """(merged status, cancel capability) as ggml_backend_graph_compute_with_abort
+        reports them; the status is returned, not raised"""
+        cap = CancelCapability()
+        rc = lib().oasr_b200_synchronize_ex(self.handle, ctypes.byref(cap))
+        return rc, cap
+
     # -- memory API v1 (the table a plugin loader resolves by proc address) --
     def memory_domains(self) -> list:
         api = memory_api()
@@ -499,7 +529,7 @@ class Backend:
             self._abort_cb = None
             self._check(lib().oasr_b200_set_abort_callback(self.handle, ABORT_CB(0), None))
             return
-        self._abort_cb = ABORT_CB(lambda _data: 1 if fn() else 0)
+        self._abort_cb = ABORT_CB(lambda _data: bool(fn()))
         self._check(lib().oasr_b200_set_abort_callback(self.handle, self._abort_cb, None))
 
     def supports_op(self, op: int, src0: OasrTensor, src1: OasrTensor | None = None) -> bool:

@@ -327,10 +327,19 @@ int oasr_b200_synchronize(oasr_backend *be) {
     if (err) {
         cudaMemset(be->err_word, 0, sizeof(int));
         return oasr_internal_fail(be, OASR_STATUS_EXECUTION_FAILED,
-                                  err & ERR_BAD_INDEX ? "kernel rejected an out-of-range row index"
-                                                      : "kernel rejected inconsistent launch geometry");
+                                  err & ERR_BAD_INDEX   ? "kernel rejected an out-of-range row index"
+                                  : err & ERR_BAD_SHAPE ? "kernel rejected inconsistent launch geometry"
+                                                        : "a kernel's bounded wait on its pipeline timed out");
     }
     return OASR_STATUS_SUCCESS;
+}
+
+int oasr_b200_synchronize_ex(oasr_backend *be, oasr_cancel_capability *cap) {
+    if (cap) {
+        cap->mechanism = be ? OASR_CANCEL_NATIVE : OASR_CANCEL_DISABLED;
+        cap->observation_granularity = be ? OASR_CANCEL_OBSERVATION_SUBMISSION_CHECKPOINT : OASR_CANCEL_OBSERVATION_NONE;
+    }
+    return oasr_b200_synchronize(be);
 }
 
 int oasr_b200_set_abort_callback(oasr_backend *be, oasr_abort_callback cb, void *data) {

@@ -34,6 +34,7 @@ enum : int {
     ERR_NONE = 0,
     ERR_BAD_INDEX = 1,   // set_rows / get_rows index out of range
     ERR_BAD_SHAPE = 2,   // launch geometry inconsistent with the descriptors
+    ERR_TIMEOUT = 4,     // a bounded wait (mbarrier, pipeline hand-off) gave up
 };
 
 }  // namespace oasr

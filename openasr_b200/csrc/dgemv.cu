@@ -288,22 +288,22 @@ static cudaError_t dg_set_attr_fam() {
     return e;
 }
 
-static bool g_dg_configured[64];
+static std::atomic<bool> g_dg_configured[64];  // per device: attributes raised (first call may race)
 
 // Raise the dynamic shared memory limit of every instantiation once per device
 // (model load calls this, outside any stream capture).
 int dgemv_configure(oasr_backend *be) {
     if (be->device < 0 || be->device >= 64) return oasr_internal_fail(be, OASR_STATUS_FAILED, "dgemv: device ordinal");
-    if (g_dg_configured[be->device]) return OASR_STATUS_SUCCESS;
+    if (g_dg_configured[be->device].load(std::memory_order_acquire)) return OASR_STATUS_SUCCESS;
     OASR_CUDA_TRY(be, dg_set_attr_fam<FAMILY_Q8_K>());
     OASR_CUDA_TRY(be, dg_set_attr_fam<FAMILY_Q8_0>());
-    g_dg_configured[be->device] = true;
+    g_dg_configured[be->device].store(true, std::memory_order_release);  // idempotent: racing callers set the same attributes
     return OASR_STATUS_SUCCESS;
 }
 
 template <int FAM, int PRO, int EPI>
 static int dg_launch(oasr_backend *be, const DgemvArgs &a0) {
-    if (be->device < 0 || be->device >= 64 || !g_dg_configured[be->device])
+    if (be->device < 0 || be->device >= 64 || !g_dg_configured[be->device].load(std::memory_order_acquire))
         return oasr_internal_fail(be, OASR_STATUS_FAILED, "dgemv: dgemv_configure was not called on this device");
     DgemvArgs a = a0;
     a.terms_bytes = (int)dg_align16(dg_terms_bytes(FAM, a.units));

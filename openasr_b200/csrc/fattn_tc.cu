@@ -375,7 +375,7 @@ static cudaError_t launch_fa_tc(oasr_backend *be, dim3 grid, const CUtensorMap &
                                 const CUtensorMap &mv, int NQ, int NKV, int H, int HKV, float scale_log2,
                                 const oasr_tensor *dst) {
     using C = FaTc<D>;
-    static bool attr_set = false;  // per instantiation, same for every device of this build
+    static std::atomic<bool> attr_set{false};  // per instantiation, same for every device of this build
     if (!attr_set) {
         const cudaError_t e =
             cudaFuncSetAttribute(fattn_tc_kernel<D, CAUSAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);

@@ -164,7 +164,7 @@ int launch_gemm_f16(oasr_backend *be, const __half *A, int64_t lda, const __half
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return oasr_internal_fail(be, OASR_STATUS_FAILED, "gemm_f16: tensor map encoding failed");
-    static bool attr_set = false;
+    static std::atomic<bool> attr_set{false};  // idempotent set-up; concurrent first calls set the same attribute
     if (!attr_set) {
         cudaFuncSetAttribute(gemm_f16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, gf16::SMEM_BYTES);
         attr_set = true;

@@ -331,7 +331,14 @@ int mem_trim(void *backend, uint64_t flags) {
     (void)flags;
     oasr_backend *be = (oasr_backend *)backend;
     if (!be) return OASR_STATUS_FAILED;
-    cudaSetDevice(be->device);
+    // nothing is released on a device that cannot be made current or while the
+    // backend's stream is being captured (the stream synchronize a release needs would
+    // invalidate the host's capture): the call fails and changes nothing.  A quarantined
+    // backend still releases (the host is taking its memory back).
+    if (cudaSetDevice(be->device) != cudaSuccess) return OASR_STATUS_FAILED;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(be->stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+        return OASR_STATUS_FAILED;
     oasr_internal_scratch_release(be);
     oasr_internal_stage_release(be);
     return OASR_STATUS_SUCCESS;

@@ -598,7 +598,7 @@ static int launch_q4k_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, 
     st = encode_2d(be, &map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->qs + slice * N * w->qs_row_bytes, w->qs_row_bytes, N,
                    w->qs_row_bytes, 144, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st) return st;
-    static bool attr_set = false;
+    static std::atomic<bool> attr_set{false};  // idempotent set-up; concurrent first calls set the same attribute
     if (!attr_set) {
         cudaFuncSetAttribute(mmq_q4k_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, q4k::SMEM_BYTES);
         attr_set = true;
@@ -628,7 +628,7 @@ static int launch_q80_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, 
     st = encode_2d(be, &map_dw, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w->dT + slice * (int64_t)(K / 32) * N, N, K / 32,
                    (uint64_t)N * 4, 128, 4, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st) return st;
-    static bool attr_set = false;
+    static std::atomic<bool> attr_set{false};  // idempotent set-up; concurrent first calls set the same attribute
     if (!attr_set) {
         cudaFuncSetAttribute(mmq_q80_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, q80::SMEM_BYTES);
         attr_set = true;

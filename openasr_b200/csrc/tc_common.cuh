@@ -8,8 +8,6 @@
 
 namespace oasr {
 
-enum : int { ERR_TIMEOUT = 4 };
-
 static __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return (uint32_t)__cvta_generic_to_shared(p);
 }
@@ -40,16 +38,17 @@ static __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t par
     return ok != 0;
 }
 
-// Bounded wait: gives up after ~2^31 cycles (about a second) or as soon as
-// another role has given up (shared abort flag), records ERR_TIMEOUT and
+// Bounded wait: gives up after `limit` cycles (default 2^31, about a second) or as
+// soon as another role has given up (shared abort flag), records ERR_TIMEOUT and
 // returns false so the caller can unwind without touching the pipeline.
+constexpr long long kMbarWaitLimit = 1LL << 31;
 static __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
-                                                 int *err) {
+                                                 int *err, long long limit = kMbarWaitLimit) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
         if (*abort_flag) return false;
-        if (clock64() - t0 > (1LL << 31)) {
+        if (clock64() - t0 > limit) {
             *abort_flag = 1;
             atomicOr(err, ERR_TIMEOUT);
             return false;

@@ -527,7 +527,9 @@ static inline float load_elem(const char *p, int type) {
 
 static float r16(float x) { return oo_f16_to_f32(oo_f32_to_f16(x)); }
 
-/* tensor-core arithmetic (see oracle.h, OO_FA_TC128); mask entries 0 (visible) or -inf (hidden) */
+/* tensor-core arithmetic (see oracle.h, OO_FA_TC128); mask entries 0 (visible) or -inf (hidden).
+ * K and V of each (sequence, kv head) are rounded to fp16 once into contiguous rows; the
+ * per-query arithmetic below is unchanged by that (same values, same summation order). */
 static int fa_tc128(const oo_tensor *q, const oo_tensor *k, const oo_tensor *v, const oo_tensor *mask, float scale,
                     oo_tensor *dst) {
     const int64_t D = q->ne[0], NQ = q->ne[1], H = q->ne[2], S = q->ne[3];
@@ -535,60 +537,70 @@ static int fa_tc128(const oo_tensor *q, const oo_tensor *k, const oo_tensor *v, 
     const int64_t G = H / HKV;
     const float sl2 = scale * 1.4426950408889634f;
     int bad = 0;
+    for (int64_t s = 0; s < S; ++s)
+        for (int64_t hk = 0; hk < HKV; ++hk) {
+            float *kr16 = (float *)malloc((size_t)(2 * NKV * D) * sizeof(float));
+            if (!kr16) return OO_STATUS_ALLOC_FAILED;
+            float *vr16 = kr16 + NKV * D;
+#pragma omp parallel for schedule(static)
+            for (int64_t j = 0; j < NKV; ++j)
+                for (int64_t d = 0; d < D; ++d) {
+                    kr16[j * D + d] = r16(load_elem((const char *)k->data + d * k->nb[0] + j * k->nb[1] + hk * k->nb[2] + s * k->nb[3], k->type));
+                    vr16[j * D + d] = r16(load_elem((const char *)v->data + d * v->nb[0] + j * v->nb[1] + hk * v->nb[2] + s * v->nb[3], v->type));
+                }
 #pragma omp parallel for schedule(dynamic, 4) reduction(| : bad)
-    for (int64_t ir = 0; ir < NQ * H * S; ++ir) {
-        const int64_t s = ir / (H * NQ), h = (ir / NQ) % H, iq = ir % NQ, hk = h / G;
-        float *qv = (float *)malloc((size_t)D * 4 * 3 + 128 * 4);
-        if (!qv) { bad = 1; continue; }
-        float *o = qv + D, *ot = qv + 2 * D, *x = qv + 3 * D;
-        const char *pq = (const char *)q->data + iq * q->nb[1] + h * q->nb[2] + s * q->nb[3];
-        for (int64_t d = 0; d < D; ++d) { qv[d] = r16(*(const float *)(pq + d * q->nb[0])); o[d] = 0.0f; }
-        const char *mp = mask ? (const char *)mask->data + iq * mask->nb[1] + (h % mask->ne[2]) * mask->nb[2] +
-                                    (s % mask->ne[3]) * mask->nb[3]
-                              : NULL;
-        float m = -INFINITY, l = 0.0f;
-        for (int64_t j0 = 0; j0 < NKV; j0 += 128) {
-            const int64_t nv = NKV - j0 < 128 ? NKV - j0 : 128;
-            float tmax = -INFINITY;
-            for (int64_t i = 0; i < nv; ++i) {
-                /* mask: 0 = visible, -inf = hidden (the kernel takes no other values) */
-                if (mp && oo_f16_to_f32(*(const uint16_t *)(mp + (j0 + i) * mask->nb[0])) == -INFINITY) {
-                    x[i] = -INFINITY;
-                    continue;
+            for (int64_t ir = 0; ir < NQ * G; ++ir) {
+                const int64_t h = hk * G + ir / NQ, iq = ir % NQ;
+                float *qv = (float *)malloc((size_t)D * 4 * 3 + 128 * 4);
+                if (!qv) { bad = 1; continue; }
+                float *o = qv + D, *ot = qv + 2 * D, *x = qv + 3 * D;
+                const char *pq = (const char *)q->data + iq * q->nb[1] + h * q->nb[2] + s * q->nb[3];
+                for (int64_t d = 0; d < D; ++d) { qv[d] = r16(*(const float *)(pq + d * q->nb[0])); o[d] = 0.0f; }
+                const char *mp = mask ? (const char *)mask->data + iq * mask->nb[1] + (h % mask->ne[2]) * mask->nb[2] +
+                                            (s % mask->ne[3]) * mask->nb[3]
+                                      : NULL;
+                float m = -INFINITY, l = 0.0f;
+                for (int64_t j0 = 0; j0 < NKV; j0 += 128) {
+                    const int64_t nv = NKV - j0 < 128 ? NKV - j0 : 128;
+                    float tmax = -INFINITY;
+                    for (int64_t i = 0; i < nv; ++i) {
+                        /* mask: 0 = visible, -inf = hidden (the kernel takes no other values) */
+                        if (mp && oo_f16_to_f32(*(const uint16_t *)(mp + (j0 + i) * mask->nb[0])) == -INFINITY) {
+                            x[i] = -INFINITY;
+                            continue;
+                        }
+                        const float *kr = kr16 + (j0 + i) * D;
+                        double acc = 0.0;
+                        for (int64_t d = 0; d < D; ++d) acc += (double)(qv[d] * kr[d]);
+                        x[i] = (float)acc * sl2;
+                        tmax = tmax > x[i] ? tmax : x[i];
+                    }
+                    const float mnew = m > tmax ? m : tmax;
+                    const float alpha = mnew == -INFINITY ? 1.0f : exp2f(m - mnew);
+                    float tsum = 0.0f;
+                    for (int64_t i = 0; i < 128; i += 2) {
+                        const float p0 = i < nv && x[i] != -INFINITY ? exp2f(x[i] - mnew) : 0.0f;
+                        const float p1 = i + 1 < nv && x[i + 1] != -INFINITY ? exp2f(x[i + 1] - mnew) : 0.0f;
+                        tsum += p0 + p1;
+                        if (i < nv) x[i] = r16(p0);
+                        if (i + 1 < nv) x[i + 1] = r16(p1);
+                    }
+                    for (int64_t d = 0; d < D; ++d) {
+                        double acc = 0.0;
+                        for (int64_t i = 0; i < nv; ++i) acc += (double)(x[i] * vr16[(j0 + i) * D + d]);
+                        ot[d] = (float)acc;
+                    }
+                    for (int64_t d = 0; d < D; ++d) o[d] = fmaf(o[d], alpha, ot[d]);
+                    l = l * alpha + tsum;
+                    m = mnew;
                 }
-                const char *kr = (const char *)k->data + (j0 + i) * k->nb[1] + hk * k->nb[2] + s * k->nb[3];
-                double acc = 0.0;
-                for (int64_t d = 0; d < D; ++d) acc += (double)(qv[d] * r16(load_elem(kr + d * k->nb[0], k->type)));
-                x[i] = (float)acc * sl2;
-                tmax = tmax > x[i] ? tmax : x[i];
+                const float inv = l == 0.0f ? 0.0f : 1.0f / l;
+                float *out = (float *)((char *)dst->data + h * dst->nb[1] + iq * dst->nb[2] + s * dst->nb[3]);
+                for (int64_t d = 0; d < D; ++d) out[d] = o[d] * inv;
+                free(qv);
             }
-            const float mnew = m > tmax ? m : tmax;
-            const float alpha = mnew == -INFINITY ? 1.0f : exp2f(m - mnew);
-            float tsum = 0.0f;
-            for (int64_t i = 0; i < 128; i += 2) {
-                const float p0 = i < nv && x[i] != -INFINITY ? exp2f(x[i] - mnew) : 0.0f;
-                const float p1 = i + 1 < nv && x[i + 1] != -INFINITY ? exp2f(x[i + 1] - mnew) : 0.0f;
-                tsum += p0 + p1;
-                if (i < nv) x[i] = r16(p0);
-                if (i + 1 < nv) x[i + 1] = r16(p1);
-            }
-            for (int64_t d = 0; d < D; ++d) {
-                double acc = 0.0;
-                for (int64_t i = 0; i < nv; ++i) {
-                    const char *vr = (const char *)v->data + (j0 + i) * v->nb[1] + hk * v->nb[2] + s * v->nb[3];
-                    acc += (double)(x[i] * r16(load_elem(vr + d * v->nb[0], v->type)));
-                }
-                ot[d] = (float)acc;
-            }
-            for (int64_t d = 0; d < D; ++d) o[d] = fmaf(o[d], alpha, ot[d]);
-            l = l * alpha + tsum;
-            m = mnew;
+            free(kr16);
         }
-        const float inv = l == 0.0f ? 0.0f : 1.0f / l;
-        float *out = (float *)((char *)dst->data + h * dst->nb[1] + iq * dst->nb[2] + s * dst->nb[3]);
-        for (int64_t d = 0; d < D; ++d) out[d] = o[d] * inv;
-        free(qv);
-    }
     return bad ? OO_STATUS_ALLOC_FAILED : 0;
 }
 

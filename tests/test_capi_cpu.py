@@ -68,3 +68,43 @@ def test_synth_normal_matches_oracle_stream():
     np.testing.assert_array_equal(ob.synth_normal(0x0A5A0001, 12345, 0.0, 0.02),
                                   oo.synth_normal(0x0A5A0001, 12345, 0.0, 0.02))
     np.testing.assert_array_equal(ob.synth_normal(3, 100, offset=77), oo.synth_normal(3, 177)[77:])
+
+
+def test_proc_address_resolves_every_entry_point():
+    """ggml_backend_reg_get_proc_address-style lookup (ffi.rs:599): each header function
+    under its own name, the memory API under its ggml name, NULL otherwise."""
+    import ctypes
+
+    L = ob.lib()
+    for s in header_symbols():
+        addr = L.oasr_b200_get_proc_address(s.encode())
+        assert addr and addr == ctypes.cast(getattr(L, s), ctypes.c_void_p).value, s
+    assert L.oasr_b200_get_proc_address(b"ggml_backend_memory_get_api_v1") == \
+        ctypes.cast(L.oasr_b200_memory_get_api_v1, ctypes.c_void_p).value
+    assert not L.oasr_b200_get_proc_address(b"ggml_backend_no_such_entry")
+    assert not L.oasr_b200_get_proc_address(None)
+
+
+def test_abort_callback_has_the_references_bool_type():
+    """ggml_abort_callback returns bool (ffi.rs:334-336); the binding passes exactly that type."""
+    import ctypes
+
+    text = open(os.path.join(ROOT, "include", "oasr_b200.h")).read()
+    assert re.search(r"typedef\s+bool\s*\(\*oasr_abort_callback\)\(void \*data\);", text)
+    assert bk.ABORT_CB._restype_ is ctypes.c_bool and bk.ABORT_CB._argtypes_ == (ctypes.c_void_p,)
+
+
+def test_synchronize_ex_without_a_backend():
+    """A NULL backend fails, reporting the DISABLED / NONE cancel pair, which the
+    reference host accepts with a failure status (cpu_graph.rs:7974-8002)."""
+    import ctypes
+
+    cap = bk.CancelCapability(99, 99)
+    rc = ob.lib().oasr_b200_synchronize_ex(None, ctypes.byref(cap))
+    assert rc == bk.STATUS_FAILED
+    assert (cap.mechanism, cap.observation_granularity) == (bk.CANCEL_DISABLED, bk.CANCEL_OBSERVATION_NONE)
+    assert bk.valid_cancel_capability(rc, cap)
+    # the validator itself follows the reference's table
+    assert not bk.valid_cancel_capability(0, bk.CancelCapability(bk.CANCEL_DISABLED, bk.CANCEL_OBSERVATION_NONE))
+    assert not bk.valid_cancel_capability(0, bk.CancelCapability(bk.CANCEL_NATIVE, bk.CANCEL_OBSERVATION_NONE))
+    assert bk.valid_cancel_capability(0, bk.CancelCapability(bk.CANCEL_SEGMENTED, bk.CANCEL_OBSERVATION_GRAPH_COMPLETION))

@@ -103,6 +103,62 @@ def test_abort_callback_returns_aborted(gpu_backend):
 
 
 @pytest.mark.gpu
+def test_abort_predicate_is_the_references_bool_callback(gpu_backend):
+    """ggml_abort_callback is extern "C" fn(*mut c_void) -> bool (ffi.rs:334-336): a
+    callback of exactly that C type, passed straight to the C ABI, aborts the next
+    enqueue while it returns true and lets it through once it returns false."""
+    import ctypes
+
+    import torch
+
+    state = ctypes.c_bool(True)
+    cb = ctypes.CFUNCTYPE(ctypes.c_bool, ctypes.c_void_p)(lambda data: ctypes.c_bool.from_address(data).value)
+    L = ob.lib()
+    assert L.oasr_b200_set_abort_callback(gpu_backend.handle, cb, ctypes.addressof(state)) == 0
+    x = torch.zeros((4, 4), device="cuda")
+    out = torch.zeros(4, dtype=torch.int32, device="cuda")
+    tx, to = ob.describe(x), ob.describe(out)
+    assert L.oasr_b200_argmax_first(gpu_backend.handle, ctypes.byref(tx), ctypes.byref(to)) == ob.backend.STATUS_ABORTED
+    state.value = False
+    assert L.oasr_b200_argmax_first(gpu_backend.handle, ctypes.byref(tx), ctypes.byref(to)) == 0
+    assert L.oasr_b200_set_abort_callback(gpu_backend.handle, ob.backend.ABORT_CB(0), None) == 0
+    gpu_backend.synchronize()
+
+
+@pytest.mark.gpu
+def test_synchronize_ex_reports_a_valid_cancel_capability(gpu_backend):
+    """The merged status comes with the cancel-capability pair the reference host
+    validates (cpu_graph.rs:7974-8002): native cancellation observed at submission
+    checkpoints."""
+    rc, cap = gpu_backend.synchronize_ex()
+    assert rc == 0
+    assert (cap.mechanism, cap.observation_granularity) == (ob.backend.CANCEL_NATIVE,
+                                                           ob.backend.CANCEL_OBSERVATION_SUBMISSION_CHECKPOINT)
+    assert ob.backend.valid_cancel_capability(rc, cap)
+
+
+@pytest.mark.gpu
+def test_bounded_pipeline_wait_times_out_cleanly(gpu_backend):
+    """A kernel whose mbarrier never completes gives up after its bound, records the
+    timeout in the device error word and returns: the call reports EXECUTION_FAILED
+    with a timeout message, and the backend keeps working (no device fault, no poison)."""
+    import torch
+
+    L = ob.lib()
+    rc = L.oasr_b200_selftest_bounded_wait(gpu_backend.handle, 1 << 22)
+    assert rc == ob.backend.STATUS_EXECUTION_FAILED
+    assert "timed out" in L.oasr_b200_last_error(gpu_backend.handle).decode()
+    rc, cap = gpu_backend.synchronize_ex()
+    assert rc == 0 and ob.backend.valid_cancel_capability(rc, cap)
+    x = torch.tensor([[1.0, 3.0, 3.0, 2.0]], device="cuda")
+    out = torch.zeros(1, dtype=torch.int32, device="cuda")
+    gpu_backend.argmax_first(x, out)
+    gpu_backend.synchronize()
+    assert out.item() == 1
+    assert L.oasr_b200_selftest_bounded_wait(gpu_backend.handle, 0) == ob.backend.STATUS_FAILED  # bound out of range
+
+
+@pytest.mark.gpu
 def test_props_and_mem_stats(gpu_backend):
     p = gpu_backend.props()
     assert p["name"] == "CUDA0" and p["device_type"] == 1 and p["cc_major"] == 10

@@ -171,3 +171,27 @@ def test_model_drivers_recover_after_trim(fresh_backend):
         qm.close()
         wm.close()
 
+
+
+@pytest.mark.gpu
+def test_trim_during_stream_capture_is_refused(fresh_backend):
+    """A trim while the backend's stream is being captured would synchronize inside the
+    capture and invalidate it: it fails, releases nothing, and the capture completes."""
+    import torch
+
+    be = fresh_backend
+    be.reserve_scratch(32 << 20)
+    s = torch.cuda.Stream()
+    be.set_stream(s)
+    before = _stats(be)[0].backend_owned_workspace_bytes
+    x = torch.zeros(16, device="cuda")
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        x.add_(1.0)
+        rc = bk.memory_api().trim(be.handle, 0)
+    assert rc == bk.STATUS_FAILED
+    g.replay()
+    torch.cuda.synchronize()
+    assert x[0].item() == 1.0
+    assert _stats(be)[0].backend_owned_workspace_bytes == before
+    be.set_stream(torch.cuda.current_stream())

@@ -18,9 +18,6 @@ import pytest
 import openasr_b200 as ob
 from tests.conftest import ROOT
 
-STATIC_PARTIAL_BYTES = 4 << 20
-
-
 def _inputs(seed, S, H, HKV, NQ, NKV, D, masked):
     import torch
 
@@ -37,30 +34,68 @@ def _inputs(seed, S, H, HKV, NQ, NKV, D, masked):
     return q, k, v, mask
 
 
+def _heads_inputs(seed, S, H, NKV):
+    """Whisper decoder layout: one query per head, heads contiguous in a KV row ([seq][pos][H][64])
+    -- the 4-head decode kernel"""
+    import torch
+
+    rng = np.random.default_rng(seed)
+    q = torch.from_numpy(rng.normal(0, 1, (S, H, 1, 64)).astype(np.float32)).cuda()
+    kv = torch.from_numpy(rng.normal(0, 1, (S, NKV, 2, H, 64)).astype(np.float16)).cuda()
+    return q, kv[:, :, 0].permute(0, 2, 1, 3), kv[:, :, 1].permute(0, 2, 1, 3), None
+
+
+def _gqa_inputs(seed, S, H, HKV, NKV):
+    """Qwen decoder layout: head-major f16 caches [seq][kv head][pos][128] viewed to the live
+    prefix, one query row, no mask -- the GQA decode kernel"""
+    import torch
+
+    rng = np.random.default_rng(seed)
+    q = torch.from_numpy(rng.normal(0, 1, (S, H, 1, 128)).astype(np.float32)).cuda()
+    kc = torch.from_numpy(rng.normal(0, 1, (S, HKV, 2048, 128)).astype(np.float16)).cuda()
+    vc = torch.from_numpy(rng.normal(0, 1, (S, HKV, 2048, 128)).astype(np.float16)).cuda()
+    return q, kc[:, :, :NKV], vc[:, :, :NKV], None
+
+
 def _out(S, H, NQ, D):
     import torch
 
     return torch.full((S, NQ, H, D), float("nan"), dtype=torch.float32, device="cuda")
 
 
-# whisper decode self/cross attention, GQA decode with a causal mask, D = 128
+# (layout, S, H, HKV, NQ, NKV, D, masked): the generic split-KV kernel (contiguous K/V,
+# masks, query tiles), the 4-head kernel (Whisper self / cross caches) and the GQA kernel
+# (Qwen caches, G = 1, 2, 4)
 SHAPES = [
-    (8, 20, 20, 1, 1500, 64, False),
-    (1, 20, 20, 1, 37, 64, False),
-    (4, 16, 8, 1, 391, 128, True),
-    (2, 16, 8, 3, 2048, 128, True),
+    ("split", 8, 20, 20, 1, 1500, 64, False),
+    ("split", 1, 20, 20, 1, 37, 64, False),
+    ("split", 4, 16, 8, 1, 391, 128, True),
+    ("split", 2, 16, 8, 3, 2048, 128, True),
+    ("heads", 8, 20, 20, 1, 1500, 64, False),
+    ("heads", 3, 20, 20, 1, 448, 64, False),
+    ("gqa", 8, 8, 8, 1, 646, 128, False),
+    ("gqa", 4, 16, 8, 1, 391, 128, False),
+    ("gqa", 2, 32, 8, 1, 2048, 128, False),
 ]
 
 
+def _make(layout, seed, S, H, HKV, NQ, NKV, D, masked):
+    if layout == "heads":
+        return _heads_inputs(seed, S, H, NKV)
+    if layout == "gqa":
+        return _gqa_inputs(seed, S, H, HKV, NKV)
+    return _inputs(seed, S, H, HKV, NQ, NKV, D, masked)
+
+
 @pytest.mark.gpu
-@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "-".join(map(str, s)))
 def test_static_equals_ext_on_consecutive_calls(gpu_backend, shape):
-    S, H, HKV, NQ, NKV, D, masked = shape
+    layout, S, H, HKV, NQ, NKV, D, masked = shape
     be = gpu_backend
     scale = 1.0 / np.sqrt(D)
     before = be.mem_stats()["scratch_bytes"]
     for call in range(2):
-        q, k, v, mask = _inputs(7000 + 31 * call + NKV, S, H, HKV, NQ, NKV, D, masked)
+        q, k, v, mask = _make(layout, 7000 + 31 * call + NKV, S, H, HKV, NQ, NKV, D, masked)
         ref, got = _out(S, H, NQ, D), _out(S, H, NQ, D)
         be.flash_attn_ext(q, k, v, mask, scale, ref)
         be.flash_attn_ext_static(q, k, v, mask, scale, got)
@@ -92,29 +127,36 @@ def test_static_fresh_backend_never_grows_scratch():
 
 
 @pytest.mark.gpu
-def test_static_rejects_oversize_split():
-    """Largest split grid on this device: groups = 4 * SMs - 1 split in two at D = 128
-    needs more partials than the static array holds; the call must fail cleanly and
-    the backend must keep working."""
+@pytest.mark.parametrize("case", ["partials", "tickets"])
+def test_static_rejects_oversize_split(case):
+    """Split plans depend on the shapes only, so both limits are reached on any device:
+    300 query rows of 8 heads at D = 128 over 256 keys split 4 ways need ~5 MB of
+    partials (the array holds 4 MiB); 256 sequences of 20 heads in the 4-head layout are
+    1280 split groups (1024 tickets).  Each call must fail with the sizes named, launch
+    nothing, and leave the backend working."""
     import torch
 
     be = ob.Backend(0)
     try:
         be.set_stream(torch.cuda.current_stream())
-        sms = torch.cuda.get_device_properties(0).multi_processor_count
-        groups = 4 * sms - 1
-        H, D, NKV = 8, 128, 256
-        NQ = groups  # one kv head, one sequence, 8 query rows per tile -> groups tiles
-        need = 1 * H * NQ * 2 * (D + 2) * 4
-        q, k, v, _ = _inputs(12, 1, H, 1, NQ, NKV, D, False)
-        out = _out(1, H, NQ, D)
-        if need > STATIC_PARTIAL_BYTES:
-            with pytest.raises(ob.GgmlBackendError) as ei:
-                be.flash_attn_ext_static(q, k, v, None, 0.088, out)
-            assert "static scratch holds" in str(ei.value)
-            assert torch.isnan(out).all()  # nothing was launched
-        # the same backend still serves a shape that fits
-        q2, k2, v2, _ = _inputs(13, 8, 20, 20, 1, 1500, 64, False)
+        if case == "partials":
+            H, NQ, D = 8, 300, 128
+            q, k, v, _ = _inputs(12, 1, H, 1, NQ, 256, D, False)
+            out = _out(1, H, NQ, D)
+        else:
+            H, NQ, D = 20, 1, 64
+            q, k, v, _ = _heads_inputs(14, 256, H, 64)
+            out = _out(256, H, NQ, D)
+        with pytest.raises(ob.GgmlBackendError) as ei:
+            be.flash_attn_ext_static(q, k, v, None, 1.0 / np.sqrt(D), out)
+        assert "static scratch holds" in str(ei.value)
+        assert torch.isnan(out).all()  # nothing was launched
+        # the regular entry point runs the same shape (growing its scratch)
+        be.flash_attn_ext(q, k, v, None, 1.0 / np.sqrt(D), out)
+        be.synchronize()
+        assert torch.isfinite(out).all()
+        # and the static entry still serves a shape that fits, bit-equal to the regular one
+        q2, k2, v2, _ = _heads_inputs(13, 8, 20, 1500)
         ref, got = _out(8, 20, 1, 64), _out(8, 20, 1, 64)
         be.flash_attn_ext(q2, k2, v2, None, 0.125, ref)
         be.flash_attn_ext_static(q2, k2, v2, None, 0.125, got)
