@@ -598,15 +598,17 @@ def run_b200(args) -> None:
         dev_s = e0.elapsed_time(e1) / 1e3
         # ---- the configs[4] job: this rank's whole shard, once ----
         barrier()
-        j0, j1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        j0.record(stream)
-        for j in range(nb):
-            step_device(j)
-        j1.record(stream)
-        torch.cuda.synchronize()
-        be.synchronize()
+        job_s = float("nan")
+        if not args.no_job:
+            j0, j1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            j0.record(stream)
+            for j in range(nb):
+                step_device(j)
+            j1.record(stream)
+            torch.cuda.synchronize()
+            be.synchronize()
+            job_s = j0.elapsed_time(j1) / 1e3
         clocks = sampler.stop()
-        job_s = j0.elapsed_time(j1) / 1e3
         # ---- e2e: the public transcribe call on pinned host PCM -> host tokens, copies included ----
         barrier()
         h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -642,11 +644,12 @@ def run_b200(args) -> None:
                        "l2": "inputs larger than L2 (1.97 GB cross-K/V + 0.48 GB weights per decode step)",
                        "parallelism": f"independent replicas x{world} (utterances sharded round-robin per GPU)",
                        "setup_s": round(t_setup, 1)},
-            "job": {"utterances": JOB_UTTS, "audio_s": job_audio, "batches_per_gpu": nb,
-                    "wall_s": max(job_times), "value": job_audio / max(job_times), "unit": "audio-s/s",
-                    "per_gpu_s": job_times, "imbalance": max(job_times) / min(job_times),
-                    "how": "every rank runs its whole round-robin shard once on the device (CUDA events); "
-                           "RTFx = the job's audio / the slowest rank's time"},
+            "job": None if args.no_job else {
+                "utterances": JOB_UTTS, "audio_s": job_audio, "batches_per_gpu": nb,
+                "wall_s": max(job_times), "value": job_audio / max(job_times), "unit": "audio-s/s",
+                "per_gpu_s": job_times, "imbalance": max(job_times) / min(job_times),
+                "how": "every rank runs its whole round-robin shard once on the device (CUDA events); "
+                       "RTFx = the job's audio / the slowest rank's time"},
             "e2e": {"value": timed_audio / e2e_s, "unit": "audio-s/s",
                     "h2d_bytes_per_step": int(np.mean([pcm_host[i % nb].nbytes
                                                        for i in range(args.warmup, args.warmup + args.steps)])),
@@ -661,7 +664,7 @@ def run_b200(args) -> None:
                                                            "K/V rotated over 246 MB"},
             "clocks": clocks,
         }
-        if world == 1:
+        if world == 1 and not args.no_job:
             cb = rtfx_cpu_sample()
             line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
         print(json.dumps(line), flush=True)
@@ -1067,6 +1070,8 @@ def main() -> None:
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--workload", choices=["rtfx", "qwen", "mulmat", "kernels"], default="rtfx")
     ap.add_argument("--batch", type=int, default=8, help="sequences per GPU (qwen workload: 1, 4 or 8)")
+    ap.add_argument("--no-job", action="store_true",
+                    help="rtfx workload: skip the 512-utterance job leg and the CPU sample (profiling runs)")
     ap.add_argument("--new-tokens", type=int, default=256,
                     help="qwen workload: greedy tokens per sequence (256 = configs[2]; fewer only to profile)")
     args = ap.parse_args()

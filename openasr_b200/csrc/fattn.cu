@@ -115,6 +115,41 @@ static __device__ __forceinline__ void stage_l2(float *dst, const float *src, in
     }
 }
 
+// Merge factors of the 4 warps of a CTA for row t (called by one thread per row):
+// M = max_w m_w, f_w = m_w == -inf ? 0 : e^(m_w - M), L = sum_w l_w f_w (products fused, in
+// warp order).  Each output element then adds its warps' accumulators with the same f_w, in
+// the same order -- one set of exps per row instead of one per element.
+template <int R>
+static __device__ __forceinline__ void warp_merge_factors(const float (&m)[4][R], const float (&l)[4][R], int t,
+                                                          float (&f)[4][R], float (&L)[R], float (&M)[R]) {
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) mx = fmaxf(mx, m[w][t]);
+    float sum = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        const float fw = m[w][t] == -INFINITY ? 0.0f : exp_f32(__fsub_rn(m[w][t], mx));
+        f[w][t] = fw;
+        sum = __fmaf_rn(l[w][t], fw, sum);
+    }
+    L[t] = sum;
+    M[t] = mx;
+}
+
+// The same for the n split partials of one row (pp = [split][D + 2]: acc[D], m, l), in split order.
+static __device__ __forceinline__ void split_merge_factors(const float *pp, int n, int D, float *f, float *L) {
+    float mx = -INFINITY;
+    for (int sp = 0; sp < n; ++sp) mx = fmaxf(mx, pp[sp * (D + 2) + D]);
+    float sum = 0.0f;
+    for (int sp = 0; sp < n; ++sp) {
+        const float m = pp[sp * (D + 2) + D];
+        const float fs = m == -INFINITY ? 0.0f : exp_f32(__fsub_rn(m, mx));
+        f[sp] = fs;
+        sum = __fmaf_rn(pp[sp * (D + 2) + D + 1], fs, sum);
+    }
+    *L = sum;
+}
+
 constexpr int FA_HEADS_U = 8;            // KV positions per warp load batch (double buffered)
 constexpr int FA_HEADS_MAX_SPLITS = 16;  // most KV splits of one query row (partials staged by the merging CTA)
 constexpr int FA_GQA_U = 2;              // KV positions per lane group and load batch (double buffered)
@@ -277,19 +312,17 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
         }
     }
     __syncthreads();
+    // the 4 warps' merge factors of each query row, once per row (warp_merge_factors)
+    __shared__ float s_f[4][QT], s_L[QT], s_M[QT];
+    if (threadIdx.x < QT) warp_merge_factors<QT>(s_m, s_s, threadIdx.x, s_f, s_L, s_M);
+    __syncthreads();
     // thread layout for the epilogue: QT*D outputs over 128 threads
     for (int o = threadIdx.x; o < QT * D; o += 128) {
         const int t = o / D, e = o % D;
-        float M = -INFINITY;
+        const float M = s_M[t], L = s_L[t];
+        float A = 0.0f;
 #pragma unroll
-        for (int w = 0; w < 4; ++w) M = fmaxf(M, s_m[w][t]);
-        float L = 0.0f, A = 0.0f;
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-            const float f = s_m[w][t] == -INFINITY ? 0.0f : exp_f32(__fsub_rn(s_m[w][t], M));
-            L = __fmaf_rn(s_s[w][t], f, L);
-            A = __fmaf_rn(s_acc[w][t][e], f, A);
-        }
+        for (int w = 0; w < 4; ++w) A = __fmaf_rn(s_acc[w][t][e], s_f[w][t], A);
         const int r = qt * QT + t;
         if (r >= a.QG) continue;
         const int h = hk * a.G + r / a.NQ, iq = r % a.NQ;
@@ -320,16 +353,13 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
         if (t > 0) __syncthreads();
         stage_l2(s_part, a.partials + row * a.n_splits * (D + 2), a.n_splits * (D + 2));
         __syncthreads();
+        __shared__ float s_fs[FA_HEADS_MAX_SPLITS], s_Ls;
+        if (threadIdx.x == 0) split_merge_factors(s_part, a.n_splits, D, s_fs, &s_Ls);
+        __syncthreads();
         for (int e = threadIdx.x; e < D; e += 128) {
-            float M = -INFINITY;
-            for (int sp = 0; sp < a.n_splits; ++sp) M = fmaxf(M, s_part[sp * (D + 2) + D]);
-            float L = 0.0f, A = 0.0f;
-            for (int sp = 0; sp < a.n_splits; ++sp) {
-                const float m = s_part[sp * (D + 2) + D];
-                const float f = m == -INFINITY ? 0.0f : exp_f32(__fsub_rn(m, M));
-                L = __fmaf_rn(s_part[sp * (D + 2) + D + 1], f, L);
-                A = __fmaf_rn(s_part[sp * (D + 2) + e], f, A);
-            }
+            const float L = s_Ls;
+            float A = 0.0f;
+            for (int sp = 0; sp < a.n_splits; ++sp) A = __fmaf_rn(s_part[sp * (D + 2) + e], s_fs[sp], A);
             float *out = reinterpret_cast<float *>(a.dst + h * a.d_nb1 + iq * a.d_nb2 + s * a.d_nb3);
             out[e] = L == 0.0f ? 0.0f : __fdiv_rn(A, L);
         }
@@ -524,19 +554,16 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
         s_m[warp][hl] = mx;
         s_s[warp][hl] = sm;
     }
+    __shared__ float s_f[4][4], s_L[4], s_M[4];
+    __syncthreads();
+    if (threadIdx.x < 4) warp_merge_factors<4>(s_m, s_s, threadIdx.x, s_f, s_L, s_M);
     __syncthreads();
     for (int o = threadIdx.x; o < 4 * D; o += 128) {
         const int t = o / D, e = o % D;
-        float M = -INFINITY;
+        const float M = s_M[t], L = s_L[t];
+        float A = 0.0f;
 #pragma unroll
-        for (int w = 0; w < 4; ++w) M = fmaxf(M, s_m[w][t]);
-        float L = 0.0f, A = 0.0f;
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-            const float f = s_m[w][t] == -INFINITY ? 0.0f : exp_f32(__fsub_rn(s_m[w][t], M));
-            L = __fmaf_rn(s_s[w][t], f, L);
-            A = __fmaf_rn(s_acc[w][t][e], f, A);
-        }
+        for (int w = 0; w < 4; ++w) A = __fmaf_rn(s_acc[w][t][e], s_f[w][t], A);
         const int hh = 4 * hg + t;
         if (a.n_splits == 1) {
             const float val = L == 0.0f ? 0.0f : __fdiv_rn(A, L);
@@ -564,18 +591,17 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
     const float *pbase = a.partials + ((int64_t)s * a.H + 4 * hg) * a.n_splits * (D + 2);
     stage_l2(s_part, pbase, nP);
     __syncthreads();
+    __shared__ float s_fs[4][FA_HEADS_MAX_SPLITS], s_Ls[4];
+    if (threadIdx.x < 4)
+        split_merge_factors(s_part + threadIdx.x * a.n_splits * (D + 2), a.n_splits, D, s_fs[threadIdx.x],
+                            &s_Ls[threadIdx.x]);
+    __syncthreads();
     for (int o = threadIdx.x; o < 4 * D; o += 128) {
         const int t = o / D, e = o % D;
         const float *pp = s_part + t * a.n_splits * (D + 2);
-        float M = -INFINITY;
-        for (int sp = 0; sp < a.n_splits; ++sp) M = fmaxf(M, pp[sp * (D + 2) + D]);
-        float L = 0.0f, A = 0.0f;
-        for (int sp = 0; sp < a.n_splits; ++sp) {
-            const float m = pp[sp * (D + 2) + D];
-            const float f = m == -INFINITY ? 0.0f : exp_f32(__fsub_rn(m, M));
-            L = __fmaf_rn(pp[sp * (D + 2) + D + 1], f, L);
-            A = __fmaf_rn(pp[sp * (D + 2) + e], f, A);
-        }
+        const float L = s_Ls[t];
+        float A = 0.0f;
+        for (int sp = 0; sp < a.n_splits; ++sp) A = __fmaf_rn(pp[sp * (D + 2) + e], s_fs[t][sp], A);
         const float val = L == 0.0f ? 0.0f : __fdiv_rn(A, L);
         if (a.oq) s_out[t * D + e] = val;
         else reinterpret_cast<float *>(a.dst + (4 * hg + t) * a.d_nb1 + s * a.d_nb3)[e] = val;
@@ -772,19 +798,16 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
             }
         }
     }
+    __shared__ float s_f[4][G], s_L[G], s_M[G];
+    __syncthreads();
+    if (threadIdx.x < G) warp_merge_factors<G>(s_m, s_s, threadIdx.x, s_f, s_L, s_M);
     __syncthreads();
     for (int o = threadIdx.x; o < G * D; o += 128) {
         const int g = o / D, e = o % D;
-        float M = -INFINITY;
+        const float M = s_M[g], L = s_L[g];
+        float A = 0.0f;
 #pragma unroll
-        for (int w = 0; w < 4; ++w) M = fmaxf(M, s_m[w][g]);
-        float L = 0.0f, A = 0.0f;
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-            const float f = s_m[w][g] == -INFINITY ? 0.0f : exp_f32(__fsub_rn(s_m[w][g], M));
-            L = __fmaf_rn(s_s[w][g], f, L);
-            A = __fmaf_rn(s_acc[w][g][e], f, A);
-        }
+        for (int w = 0; w < 4; ++w) A = __fmaf_rn(s_acc[w][g][e], s_f[w][g], A);
         const int h = hk * G + g;
         if (a.n_splits == 1) {
             const float val = L == 0.0f ? 0.0f : __fdiv_rn(A, L);
@@ -812,18 +835,17 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
     const float *pbase = a.partials + ((int64_t)s * a.H + hk * G) * a.n_splits * (D + 2);
     stage_l2(s_part, pbase, G * a.n_splits * (D + 2));
     __syncthreads();
+    __shared__ float s_fs[G][FA_HEADS_MAX_SPLITS], s_Ls[G];
+    if (threadIdx.x < G)
+        split_merge_factors(s_part + threadIdx.x * a.n_splits * (D + 2), a.n_splits, D, s_fs[threadIdx.x],
+                            &s_Ls[threadIdx.x]);
+    __syncthreads();
     for (int o = threadIdx.x; o < G * D; o += 128) {
         const int g = o / D, e = o % D;
         const float *pp = s_part + g * a.n_splits * (D + 2);
-        float M = -INFINITY;
-        for (int sp = 0; sp < a.n_splits; ++sp) M = fmaxf(M, pp[sp * (D + 2) + D]);
-        float L = 0.0f, A = 0.0f;
-        for (int sp = 0; sp < a.n_splits; ++sp) {
-            const float m = pp[sp * (D + 2) + D];
-            const float f = m == -INFINITY ? 0.0f : exp_f32(__fsub_rn(m, M));
-            L = __fmaf_rn(pp[sp * (D + 2) + D + 1], f, L);
-            A = __fmaf_rn(pp[sp * (D + 2) + e], f, A);
-        }
+        const float L = s_Ls[g];
+        float A = 0.0f;
+        for (int sp = 0; sp < a.n_splits; ++sp) A = __fmaf_rn(pp[sp * (D + 2) + e], s_fs[g][sp], A);
         const float val = L == 0.0f ? 0.0f : __fdiv_rn(A, L);
         if (a.oq) {
             const int64_t idx = ((int64_t)s * a.H + hk * G + g) * D + e;
