@@ -477,6 +477,48 @@ int oasr_b200_whisper_transcribe(oasr_whisper *m, const float *pcm, const int64_
                                  const int32_t *prompt, int32_t n_prompt, int32_t n_new, int32_t eot,
                                  int32_t stop_at_eot, int32_t *tokens_out);
 
+/* ---- serving: continuous batching (models/seq2seq_serve_batch.rs) ----------------
+ * The serve-batch engine decodes a queue of requests in up to max_batch slots: a
+ * finished slot is released and refilled from the queue (refill_free_slots,
+ * seq2seq_serve_batch.rs:775), the running width follows the bucket rule below, and
+ * it narrows with the active slots compacted to the front (try_shrink_active_slots,
+ * :634) or widens while requests wait (try_rebucket_active_slots, :528).
+ *
+ * Bucket width (serve_batch_bucket_width, serve_batch_env.rs:317): `active` rounded
+ * up to a power of two, capped at max_batch, never below `active`; 0 and 1 stay. */
+int32_t oasr_b200_serve_batch_width(int32_t active, int32_t max_batch);
+/* VRAM cap (serve_batch_vram_cap_decision_for_memory, serve_batch_env.rs:501):
+ * requested > 1 becomes min(requested, (free - reserve) / slot_bytes), at least 1;
+ * slot_bytes == 0 keeps the request.  oasr_b200_whisper_load applies it to
+ * max_batch > 2 with the device's free memory after the weights and a reserve of
+ * OASR_B200_SERVE_VRAM_RESERVE_MB (default 1024) MiB. */
+int32_t oasr_b200_serve_batch_vram_cap(int32_t requested, uint64_t slot_bytes, uint64_t free_bytes,
+                                       uint64_t reserve_bytes);
+/* Slots a loaded Whisper model decodes at most (max_batch after the VRAM cap). */
+int32_t oasr_b200_whisper_max_batch(oasr_whisper *m);
+
+typedef struct oasr_serve_stats {
+    int32_t steps;          /* decoder steps run (every slot of the width) */
+    int32_t admissions;     /* admission groups (mel + encoder of the refilled slots) */
+    int32_t width_changes;  /* re-bucketings: widen while requests wait, narrow with compaction */
+    int32_t max_width;      /* widest batch run */
+} oasr_serve_stats;
+
+/* Serve n_utts utterances (host PCM, concatenated, n_samples[i] each) through the
+ * continuous-batching loop: each slot is teacher-forced through `prompt`, then
+ * decodes greedily until it emits `eot` (when stop_at_eot), its budget (budgets[i],
+ * or max_new when budgets is NULL) or the context end.  tokens_out
+ * [n_utts][max_new] gets each request's generated tokens (the `eot` included),
+ * lengths_out[n_utts] their count.  max_width 0 = the model's max batch; the host
+ * looks for finished slots every check_every steps (steps of a finished slot
+ * are idle).  A slot's tokens do not depend on the batch it ran in: they equal a
+ * serial oasr_b200_whisper_transcribe of the same utterance.  The abort callback is
+ * polled before each group of steps. */
+int oasr_b200_whisper_serve(oasr_whisper *m, const float *pcm, const int64_t *n_samples, int32_t n_utts,
+                            const int32_t *prompt, int32_t n_prompt, const int32_t *budgets, int32_t max_new,
+                            int32_t eot, int32_t stop_at_eot, int32_t max_width, int32_t check_every,
+                            int32_t *tokens_out, int32_t *lengths_out, oasr_serve_stats *stats);
+
 /* ---- Qwen3-ASR LLM decoder -------------------------------------------------------
  * The decoder-only LLM stack of models/qwen (Qwen3AsrLlmWholeDecoderGraphExecutor,
  * llm_transformer.rs; layer graph nn/decoder.rs:1850-2140): per layer RMSNorm ->

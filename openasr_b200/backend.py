@@ -137,6 +137,11 @@ CANCEL_DISABLED, CANCEL_NATIVE, CANCEL_SEGMENTED = 0, 1, 2
 CANCEL_OBSERVATION_NONE, CANCEL_OBSERVATION_SUBMISSION_CHECKPOINT, CANCEL_OBSERVATION_GRAPH_COMPLETION = 0, 1, 2
 
 
+class ServeStats(ctypes.Structure):
+    """struct oasr_serve_stats"""
+    _fields_ = [(f, ctypes.c_int32) for f in ("steps", "admissions", "width_changes", "max_width")]
+
+
 class CancelCapability(ctypes.Structure):
     """struct ggml_backend_graph_cancel_capability (ffi.rs:125-131)"""
     _fields_ = [("mechanism", ctypes.c_int32), ("observation_granularity", ctypes.c_int32)]
@@ -285,6 +290,11 @@ SIGNATURES = {
     "oasr_b200_whisper_decode_step": ([_P, _P, _I32, _I32, _P, _P], ctypes.c_int),
     "oasr_b200_whisper_transcribe": ([_P, _P, _P, _I32, _P, _I32, _I32, _I32, _I32, _P], ctypes.c_int),
     "oasr_b200_whisper_mel_device": ([_P, _P, _P, _I32], ctypes.c_int),
+    "oasr_b200_whisper_max_batch": ([_P], ctypes.c_int32),
+    "oasr_b200_whisper_serve": ([_P, _P, _P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, _I32, _P, _P,
+                                 ctypes.POINTER(ServeStats)], ctypes.c_int),
+    "oasr_b200_serve_batch_width": ([_I32, _I32], ctypes.c_int32),
+    "oasr_b200_serve_batch_vram_cap": ([_I32, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64], ctypes.c_int32),
     "oasr_b200_whisper_generate": ([_P, _I32, _P, _I32, _I32, _I32, _I32, _P, _I32], ctypes.c_int),
     "oasr_b200_qwen_load": ([_P, ctypes.POINTER(OasrQwenConfig), ctypes.POINTER(OasrNamedTensor), _I32,
                              ctypes.POINTER(_P)], ctypes.c_int),

@@ -45,7 +45,7 @@ struct DgemvArgs {
     float *q_out;
     __half *kc, *vc;
     int64_t cache_seq_stride;
-    const int *pos;
+    const int *pos;  // EPI_QKV: cache row of each activation row [M]
     int max_pos, d;
     int *err;
 };
@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(DG_WARPS * 32, 2) dgemv_kernel(DgemvArgs a) {
             const int m = (e & 1) ? m1 : m0;
             if (n >= a.N || m >= a.M) continue;
             if (EPI == EPI_QKV) {
-                const int pos = *a.pos;
+                const int pos = a.pos[m];
                 const float v = a.bias3 ? __fadd_rn(acc[e], a.bias3[n]) : acc[e];
                 if (n < a.d) {
                     a.q_out[(int64_t)m * a.d + n] = v;

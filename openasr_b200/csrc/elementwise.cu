@@ -207,7 +207,7 @@ __global__ void qkv_split_kv_write_kernel(const float *qkv, const float *bias3, 
     griddep_launch_dependents();
     griddep_wait();
     const int b = blockIdx.x;
-    const int pos = *pos_dev;
+    const int pos = pos_dev[b];
     if (pos < 0 || pos >= max_pos) {
         if (threadIdx.x == 0) atomicOr(err, ERR_BAD_INDEX);
         return;
@@ -222,13 +222,13 @@ __global__ void qkv_split_kv_write_kernel(const float *qkv, const float *bias3, 
     }
 }
 
-// x[b] = dequant(tok_emb Q8_0 row tokens[b]) + pos_emb[*pos]  (ggml_get_rows + ggml_add)
+// x[b] = dequant(tok_emb Q8_0 row tokens[b]) + pos_emb[pos[b]]  (ggml_get_rows + ggml_add)
 __global__ void embed_q8_0_kernel(const uint8_t *qs, const uint16_t *dsc, int d, int vocab, const int *tokens,
                                   const float *pos_emb, const int *pos_dev, int max_pos, float *x, int *err) {
     griddep_launch_dependents();
     griddep_wait();
     const int b = blockIdx.x;
-    const int tok = tokens[b], pos = pos_dev ? *pos_dev : 0;
+    const int tok = tokens[b], pos = pos_dev ? pos_dev[b] : 0;
     if (tok < 0 || tok >= vocab || pos < 0 || pos >= max_pos) {
         if (threadIdx.x == 0) atomicOr(err, ERR_BAD_INDEX);
         return;
@@ -349,15 +349,41 @@ __global__ void mel_norm_kernel(float *mel, int64_t per_utt, const int *max_key)
 
 // After a decode step the selected tokens become the inputs of position pos + 1
 // (history[b][pos + 1]) and the device position and KV length advance by one.
-__global__ void decode_advance_kernel(const int *tokens, int *pos, int *nkv, int *history, int n, int P) {
+// The end of a decode step, per sequence b < n (position pos[b], KV length nkv[b] = pos[b] + 1):
+// record the step's selected token tokens[b] as history[b][pos + 1] and advance the position.
+// With a serving control block (sc.prompt != null) every slot also feeds its own next input:
+// the prompt token while pos + 1 is inside the prompt (teacher forcing, so slots at different
+// positions share one step), else the selected token; a slot whose token is `eot` (when
+// stop_at_eot), whose generated count reached its budget or whose context is full is marked
+// done and parks (its position, input and history stay until the host refills the slot).
+__global__ void decode_advance_kernel(int *tokens, int *pos, int *nkv, int *history, int n, int P, ServeCtl sc) {
     griddep_wait();
     const int b = threadIdx.x;
-    const int p = *pos;
-    if (b < n && p + 1 < P) history[b * P + p + 1] = tokens[b];
-    __syncthreads();
-    if (b == 0) {
-        *pos = p + 1;
-        *nkv = p + 2;
+    if (b >= n) return;
+    const int p = pos[b];
+    if (!sc.prompt) {
+        if (p + 1 < P) history[b * P + p + 1] = tokens[b];
+        pos[b] = p + 1;
+        nkv[b] = p + 2;
+        return;
+    }
+    if (sc.done[b]) return;
+    const int q = p + 1;
+    int tok = tokens[b];
+    bool fin = false;
+    if (q < sc.n_prompt) {
+        tok = sc.prompt[q];
+    } else {
+        history[b * P + q] = tok;
+        const int generated = q - sc.n_prompt + 1;
+        fin = (sc.stop_at_eot && tok == sc.eot) || generated >= sc.budget[b] || q + 1 >= P;
+    }
+    tokens[b] = tok;
+    if (fin) {
+        sc.done[b] = 1;
+    } else {
+        pos[b] = q;
+        nkv[b] = q + 1;
     }
 }
 
@@ -648,8 +674,9 @@ int launch_embed_q8_0(oasr_backend *be, const oasr_weight *emb, const int *token
     return oasr_internal_launch_check(be, "embed_q8_0");
 }
 
-int launch_decode_advance(oasr_backend *be, const int *tokens, int *pos, int *nkv, int *history, int n, int P) {
-    const cudaError_t e = launch_k(be, decode_advance_kernel, dim3(1), dim3(32), 0, tokens, pos, nkv, history, n, P);
+int launch_decode_advance(oasr_backend *be, int *tokens, int *pos, int *nkv, int *history, int n, int P,
+                          const ServeCtl &sc) {
+    const cudaError_t e = launch_k(be, decode_advance_kernel, dim3(1), dim3(32), 0, tokens, pos, nkv, history, n, P, sc);
     if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "decode_advance launch", __LINE__);
     return oasr_internal_launch_check(be, "decode_advance");
 }

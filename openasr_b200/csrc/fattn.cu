@@ -47,9 +47,10 @@ struct FaArgs {
     float *partials;          // [rows][n_splits][D + 2]
     unsigned int *counters;   // one ticket per (kv head, seq, q tile)
     const float *q_bias;      // optional [H*D] added to q before the fp16 rounding
-    const int *nkv_dev;       // optional device-side KV length (<= NKV), for graph-captured decode; the
-                              // decode kernels may read it before their PDL wait, so no launch they can
-                              // overlap writes it (the model drivers advance it between steps)
+    const int *nkv_dev;       // optional device-side KV length of each sequence ([S], <= NKV), for
+                              // graph-captured decode; the decode kernels may read it before their PDL
+                              // wait, so no launch they can overlap writes it (the model drivers
+                              // advance it between steps)
     // optional (GQA and 4-head decode kernels): the output rows [S][H * D] quantized to
     // activation planes instead of written as f32 -- the next mul_mat's input: quants oq
     // [S][H * D], scales od ([S][H * D / 32] q8_0, [S][H * D / 256] q8_K) and, for q8_K,
@@ -61,8 +62,8 @@ struct FaArgs {
     // 4-head and GQA kernels, K/V rows that no launch this one can overlap under programmatic
     // dependent launch writes are loaded before the wait on the predecessor:
     // KV_STATIC_ALL every row (the cross-attention's encoder K/V); KV_STATIC_OLD every
-    // row but the newest live one (self-attention: the predecessor writes row *nkv_dev - 1;
-    // *nkv_dev itself must not be written by an overlapping launch)
+    // row but the newest live one (self-attention: the predecessor writes row nkv_dev[s] - 1;
+    // nkv_dev itself must not be written by an overlapping launch)
     int kv_static;
 };
 
@@ -164,7 +165,7 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
         // rows toward L2 before the wait.  Only a hint (the range is recomputed below); the
         // KV length is set between steps, not by the predecessor kernel.
         const int g = blockIdx.x / a.n_qtiles, hk0 = g % a.HKV, s0 = g / a.HKV;
-        const int nkv = min(*a.nkv_dev, a.NKV), per = (nkv + a.n_splits - 1) / a.n_splits;
+        const int nkv = min(a.nkv_dev[s0], a.NKV), per = (nkv + a.n_splits - 1) / a.n_splits;
         const int p0 = blockIdx.y * per, p1 = min(nkv, p0 + per);
         if (p1 > p0) {
             prefetch_l2_bulk(a.k + hk0 * a.k_nb2 + s0 * a.k_nb3 + (int64_t)p0 * a.k_nb1, (uint32_t)((p1 - p0) * a.k_nb1));
@@ -219,7 +220,7 @@ __global__ void __launch_bounds__(128) fattn_split_kernel(FaArgs a) {
     }
 
     // with a device-side KV length the splits share the live positions evenly
-    const int nkv = a.nkv_dev ? min(*a.nkv_dev, a.NKV) : a.NKV;
+    const int nkv = a.nkv_dev ? min(a.nkv_dev[s], a.NKV) : a.NKV;
     const int per = a.nkv_dev ? (nkv + a.n_splits - 1) / a.n_splits : a.kv_per_split;
     const int kv0 = split * per;
     const int kv1 = min(nkv, kv0 + per);
@@ -408,7 +409,7 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
     // with a device-side KV length the splits share the live positions evenly
     int kv0 = 0, kv1 = 0;
     auto range = [&]() {
-        const int nkv = a.nkv_dev ? min(*a.nkv_dev, a.NKV) : a.NKV;
+        const int nkv = a.nkv_dev ? min(a.nkv_dev[s], a.NKV) : a.NKV;
         const int per = a.nkv_dev ? (nkv + a.n_splits - 1) / a.n_splits : a.kv_per_split;
         kv0 = split * per;
         kv1 = min(nkv, kv0 + per);
@@ -506,7 +507,7 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
     if (early) {
         range();
         // rows below `lim` are final before the predecessor runs
-        const int lim = a.kv_static == KV_STATIC_ALL ? kv1 : min(kv1, (a.nkv_dev ? *a.nkv_dev : a.NKV) - 1);
+        const int lim = a.kv_static == KV_STATIC_ALL ? kv1 : min(kv1, (a.nkv_dev ? a.nkv_dev[s] : a.NKV) - 1);
         const int p0 = kv0 + warp, p1 = p0 + 4 * U;
         if (p0 < kv1 && min(p0 + 4 * (U - 1), kv1 - 1) < lim) {
             load(p0, kA, vA);
@@ -630,7 +631,7 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
     if (threadIdx.x == 0 && a.nkv_dev) {
         // stream this CTA's K/V rows toward L2 before the wait (a hint; the range is
         // recomputed below, and the KV length is set between steps)
-        const int nk = min(*a.nkv_dev, a.NKV), pp = (nk + a.n_splits - 1) / a.n_splits;
+        const int nk = min(a.nkv_dev[s], a.NKV), pp = (nk + a.n_splits - 1) / a.n_splits;
         const int p0 = split * pp, p1 = min(nk, p0 + pp);
         if (p1 > p0) {
             prefetch_l2_bulk(a.k + hk * a.k_nb2 + s * a.k_nb3 + (int64_t)p0 * a.k_nb1, (uint32_t)((p1 - p0) * a.k_nb1));
@@ -649,7 +650,7 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
     }
 
     // the KV length is final before the launch (set between steps)
-    const int nkv = a.nkv_dev ? min(*a.nkv_dev, a.NKV) : a.NKV;
+    const int nkv = a.nkv_dev ? min(a.nkv_dev[s], a.NKV) : a.NKV;
     const int per = a.nkv_dev ? (nkv + a.n_splits - 1) / a.n_splits : a.kv_per_split;
     const int kv0 = split * per;
     const int kv1 = min(nkv, kv0 + per);

@@ -12,13 +12,30 @@ int launch_bias_gelu_quant(oasr_backend *be, const float *x, const float *bias, 
                            const ActPlanes *q, int family);
 int launch_swiglu_quant(oasr_backend *be, const float *gu, int64_t rows, int n, int64_t gu_ld, float *out_f32,
                         const ActPlanes *q, int family);
+// Decode-step state is per sequence (slot): pos_dev[b] is the cache row sequence b writes in
+// this step, nkv[b] = pos_dev[b] + 1 its attention length, so sequences at different positions
+// share one step (the serving scheduler refills a slot while the others continue).
 int launch_qkv_split_kv_write(oasr_backend *be, const float *qkv, const float *bias3, int B, int d, float *q_out,
                               __half *kc, __half *vc, int64_t cache_seq_stride, const int *pos_dev, int max_pos);
 int launch_embed_q8_0(oasr_backend *be, const oasr_weight *emb, const int *tokens, int B, const float *pos_emb,
                       const int *pos_dev, int max_pos, float *x);
 int launch_add_rows(oasr_backend *be, float *x, const float *bias, const float *add, int64_t rows, int n);
-// decode-step epilogue: history[b][*pos + 1] = tokens[b] (b < n), *pos += 1, *nkv = *pos + 1
-int launch_decode_advance(oasr_backend *be, const int *tokens, int *pos, int *nkv, int *history, int n, int P);
+// Serving control of the decode-step epilogue: the prompt every slot starts with (device,
+// n_prompt tokens), per-slot done flags and generated-token budgets, the end token.
+// prompt == nullptr is the lockstep mode (every slot advances; the host feeds the prompt).
+struct ServeCtl {
+    const int *prompt;
+    int n_prompt;
+    int *done;
+    const int *budget;
+    int eot;
+    int stop_at_eot;
+};
+// decode-step epilogue per slot b < n: history[b][pos[b] + 1] = tokens[b], pos[b] += 1,
+// nkv[b] = pos[b] + 1; with a ServeCtl, teacher-forced prompt inputs and done detection
+// (elementwise.cu decode_advance_kernel)
+int launch_decode_advance(oasr_backend *be, int *tokens, int *pos, int *nkv, int *history, int n, int P,
+                          const ServeCtl &sc = ServeCtl{});
 int launch_cast_f16(oasr_backend *be, const float *src, int64_t src_ld, const float *bias, int64_t rows, int cols,
                     __half *dst, int64_t dst_ld);
 int launch_im2col_f16(oasr_backend *be, const float *src, int64_t s_b, int64_t s_ic, int64_t s_t, int B, int IC,
@@ -56,6 +73,11 @@ inline oasr_tensor make_tensor(int type, const void *data, int64_t ne0, int64_t 
     t.nb[1] = nb1; t.nb[2] = nb2; t.nb[3] = nb3;
     return t;
 }
+
+// serving width rules (serve_policy.cpp): the device bytes of one Whisper serving slot and the
+// VRAM reserve the width cap keeps free
+uint64_t whisper_slot_bytes(const oasr_whisper_config *c);
+uint64_t serve_vram_reserve_bytes();
 
 // Host-side helpers shared with the CPU oracle's frontend definition (whisper/mel.rs):
 // periodic Hann window (scale first), Slaney mel filterbank (ratio-first edges).

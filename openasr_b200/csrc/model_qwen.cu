@@ -155,7 +155,7 @@ int upload_linear(oasr_qwen *m, const std::vector<const oasr_named_tensor *> &pa
 // RoPE NEOX on the pairs (i, i + 64) with (cos, sin) of the row's position from
 // `rope`; queries go to q_out [rows][H * 128] f32, keys and values to the f16
 // caches [seq][kv head][max_pos][128].  Row r is token r % T of sequence r / T at
-// position (*pos_dev or pos0) + r % T.
+// position (pos_dev[sequence] or pos0) + r % T.
 __global__ void __launch_bounds__(1024) qwen_qkv_post_kernel(const float *qkv, int64_t qkv_ld, int H, int HKV, int T,
                                                              const int *pos_dev, int pos0, const float *q_norm,
                                                              const float *k_norm, float eps, const float2 *rope,
@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(1024) qwen_qkv_post_kernel(const float *qkv, i
     griddep_wait();
     const int64_t r = blockIdx.x;
     const int s = (int)(r / T), t = (int)(r % T);
-    const int p = (pos_dev ? *pos_dev : pos0) + t;
+    const int p = (pos_dev ? pos_dev[s] : pos0) + t;
     if (p < 0 || p >= P) {
         if (threadIdx.x == 0) atomicOr(err, ERR_BAD_INDEX);
         return;
@@ -389,10 +389,15 @@ int decode_step_graph(oasr_qwen *m, int n) {
     return OASR_STATUS_SUCCESS;
 }
 
+// every slot at position pos (its KV length pos + 1)
 int set_position(oasr_qwen *m, int pos) {
-    int v[2] = {pos, pos + 1};
-    OASR_CUDA_TRY(m->be, cudaMemcpyAsync(m->pos, &v[0], sizeof(int), cudaMemcpyHostToDevice, m->stream));
-    OASR_CUDA_TRY(m->be, cudaMemcpyAsync(m->nkv, &v[1], sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    std::vector<int> v(2 * (size_t)m->B);
+    for (int b = 0; b < m->B; ++b) {
+        v[b] = pos;
+        v[m->B + b] = pos + 1;
+    }
+    OASR_CUDA_TRY(m->be, cudaMemcpyAsync(m->pos, v.data(), (size_t)m->B * 4, cudaMemcpyHostToDevice, m->stream));
+    OASR_CUDA_TRY(m->be, cudaMemcpyAsync(m->nkv, v.data() + m->B, (size_t)m->B * 4, cudaMemcpyHostToDevice, m->stream));
     return OASR_STATUS_SUCCESS;
 }
 
@@ -562,8 +567,8 @@ int oasr_b200_qwen_load(oasr_backend *be, const oasr_qwen_config *cfg, const oas
     L_TRY(qalloc(m, &m->logits, (size_t)B * cfg->n_vocab * 4));
     L_TRY(qalloc(m, (uint8_t **)&m->dqa, act_planes_bytes(FAMILY_Q8_K, B, kmax)));
     L_TRY(qalloc(m, &m->tokens, (size_t)B * 4));
-    L_TRY(qalloc(m, &m->pos, 4));
-    L_TRY(qalloc(m, &m->nkv, 4));
+    L_TRY(qalloc(m, &m->pos, (size_t)B * 4));  // per slot
+    L_TRY(qalloc(m, &m->nkv, (size_t)B * 4));
     L_TRY(qalloc(m, &m->history, (size_t)B * P * 4));
     // flash-decode partials for the largest split configuration of a decode step,
     // reserved now so that no step (and no graph capture) has to grow the scratch

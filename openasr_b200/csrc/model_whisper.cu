@@ -80,10 +80,16 @@ struct oasr_whisper {
     bool pdl;        // programmatic dependent launch inside the step graph (OASR_B200_PDL=0 turns it off)
     void *dqa_d, *dqa_f, *dqa_lm;
     int *tokens, *pos, *nkv, *history;
+    // serving: per-slot done flags and token budgets, the prompt on the device, admission lists
+    int *done, *budget, *prompt_dev, *serve_io;
     int enc_family, dec_family;
     cudaGraphExec_t graph;
     int graph_batch;
     uint64_t graph_epoch;  // backend scratch epoch at capture
+    // serve step graphs per power-of-two width (1, 2, 4, 8) and the serving parameters they hold
+    cudaGraphExec_t serve_graph[4];
+    uint64_t serve_epoch[4];
+    int serve_key[3];  // n_prompt, eot, stop_at_eot of the captured serve graphs
     std::vector<void *> allocs;
     std::vector<oasr_weight *> weights;
 };
@@ -195,7 +201,8 @@ int alloc_planes(oasr_whisper *m, void **p, int family, int64_t R, int64_t K) {
 }
 
 // ---- encoder ----------------------------------------------------------------------------------
-int run_encoder(oasr_whisper *m, int n) {
+// utterance i of the batch writes its cross-attention K|V into slot slot_of[i] (identity when null)
+int run_encoder(oasr_whisper *m, int n, const int *slot_of = nullptr) {
     oasr_backend *be = m->be;
     const int d = m->d, H = m->H, T = m->T_enc, nm = m->cfg.n_mels;
     const int64_t M = (int64_t)n * T;
@@ -243,7 +250,13 @@ int run_encoder(oasr_whisper *m, int n) {
     for (size_t l = 0; l < m->dec.size(); ++l) {
         const DecLayer &L = m->dec[l];
         W_TRY(mul_mat_planes(be, L.ckv, qx, M, m->qkv, 2 * d));
-        W_TRY(launch_cast_f16(be, m->qkv, 2 * d, L.b_ckv, M, 2 * d, L.cross_kv, 2 * d));
+        if (!slot_of) {
+            W_TRY(launch_cast_f16(be, m->qkv, 2 * d, L.b_ckv, M, 2 * d, L.cross_kv, 2 * d));
+        } else {
+            for (int i = 0; i < n; ++i)
+                W_TRY(launch_cast_f16(be, m->qkv + (int64_t)i * T * 2 * d, 2 * d, L.b_ckv, T, 2 * d,
+                                      L.cross_kv + (int64_t)slot_of[i] * T * 2 * d, 2 * d));
+        }
     }
     return OASR_STATUS_SUCCESS;
 }
@@ -404,10 +417,100 @@ int decode_step_graph(oasr_whisper *m, int n) {
     return OASR_STATUS_SUCCESS;
 }
 
+// every slot at position pos (its KV length pos + 1)
 int set_position(oasr_whisper *m, int pos) {
-    int v[2] = {pos, pos + 1};
-    OASR_CUDA_TRY(m->be, cudaMemcpyAsync(m->pos, &v[0], sizeof(int), cudaMemcpyHostToDevice, m->stream));
-    OASR_CUDA_TRY(m->be, cudaMemcpyAsync(m->nkv, &v[1], sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    std::vector<int> v(2 * (size_t)m->B);
+    for (int b = 0; b < m->B; ++b) {
+        v[b] = pos;
+        v[m->B + b] = pos + 1;
+    }
+    OASR_CUDA_TRY(m->be, cudaMemcpyAsync(m->pos, v.data(), (size_t)m->B * 4, cudaMemcpyHostToDevice, m->stream));
+    OASR_CUDA_TRY(m->be, cudaMemcpyAsync(m->nkv, v.data() + m->B, (size_t)m->B * 4, cudaMemcpyHostToDevice, m->stream));
+    return OASR_STATUS_SUCCESS;
+}
+
+// ---- serving: continuous batching over a queue of utterances --------------------------------
+// (seq2seq_serve_batch.rs:224-640 run_batch / decode_continuous_batch)
+
+// admission: slot slots[i] starts utterance i of the group -- position 0, the first prompt
+// token as its input, its generated-token budget
+__global__ void serve_admit_kernel(const int *io, int n, const int *prompt, int *tokens, int *pos, int *nkv,
+                                   int *done, int *budget) {
+    const int i = threadIdx.x;
+    if (i >= n) return;
+    const int b = io[i];
+    tokens[b] = prompt[0];
+    pos[b] = 0;
+    nkv[b] = 1;
+    done[b] = 0;
+    budget[b] = io[n + i];
+}
+
+// every slot parked (done) at position 0: slots outside the active set compute harmlessly
+__global__ void serve_park_kernel(int n, const int *prompt, int *tokens, int *pos, int *nkv, int *done, int *budget) {
+    const int b = threadIdx.x;
+    if (b >= n) return;
+    tokens[b] = prompt[0];
+    pos[b] = 0;
+    nkv[b] = 1;
+    done[b] = 1;
+    budget[b] = 1;
+}
+
+int width_index(int w) { return w <= 1 ? 0 : w <= 2 ? 1 : w <= 4 ? 2 : 3; }
+
+// one serve step of `w` slots: the decode step, then the per-slot advance with teacher-forced
+// prompts and done detection; one CUDA graph per power-of-two width
+int serve_step_graph(oasr_whisper *m, int w, const ServeCtl &sc) {
+    oasr_backend *be = m->be;
+    if (be->scratch_bytes < m->step_scratch) {
+        int st = 0;
+        oasr_internal_scratch(be, m->step_scratch, &st);
+        if (st) return st;
+    }
+    const int gi = width_index(w);
+    cudaGraphExec_t &g = m->serve_graph[gi];
+    if (g && m->serve_epoch[gi] != be->scratch_epoch) {
+        cudaGraphExecDestroy(g);
+        g = nullptr;
+    }
+    if (!g) {
+        cudaGraph_t graph;
+        OASR_CUDA_TRY(be, cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+        be->pdl = m->pdl;
+        int st = run_decode_step(m, w);
+        if (st == OASR_STATUS_SUCCESS)
+            st = launch_decode_advance(be, m->tokens, m->pos, m->nkv, m->history, w, (int)m->cfg.n_text_ctx, sc);
+        be->pdl = false;
+        const cudaError_t e = cudaStreamEndCapture(m->stream, &graph);
+        if (st) return st;
+        if (e != cudaSuccess) return oasr_internal_cuda_fail(be, e, "cudaStreamEndCapture", __LINE__);
+        const cudaError_t ie = cudaGraphInstantiate(&g, graph, 0);
+        cudaGraphDestroy(graph);
+        if (ie != cudaSuccess) return oasr_internal_cuda_fail(be, ie, "cudaGraphInstantiate", __LINE__);
+        m->serve_epoch[gi] = be->scratch_epoch;
+    }
+    OASR_CUDA_TRY(be, cudaGraphLaunch(g, m->stream));
+    return OASR_STATUS_SUCCESS;
+}
+
+// move slot `src`'s whole state to slot `dst` (compaction before a narrower width): its
+// cross-attention K|V, self-attention K/V rows, position, input, flags and history
+int serve_move_slot(oasr_whisper *m, int src, int dst) {
+    oasr_backend *be = m->be;
+    const int64_t d = m->d, T = m->T_enc, P = m->cfg.n_text_ctx;
+    for (const DecLayer &L : m->dec) {
+        OASR_CUDA_TRY(be, cudaMemcpyAsync(L.cross_kv + dst * T * 2 * d, L.cross_kv + src * T * 2 * d,
+                                          (size_t)(T * 2 * d * 2), cudaMemcpyDeviceToDevice, m->stream));
+        OASR_CUDA_TRY(be, cudaMemcpyAsync(L.self_k + dst * P * d, L.self_k + src * P * d, (size_t)(P * d * 2),
+                                          cudaMemcpyDeviceToDevice, m->stream));
+        OASR_CUDA_TRY(be, cudaMemcpyAsync(L.self_v + dst * P * d, L.self_v + src * P * d, (size_t)(P * d * 2),
+                                          cudaMemcpyDeviceToDevice, m->stream));
+    }
+    for (int *a : {m->tokens, m->pos, m->nkv, m->done, m->budget})
+        OASR_CUDA_TRY(be, cudaMemcpyAsync(a + dst, a + src, 4, cudaMemcpyDeviceToDevice, m->stream));
+    OASR_CUDA_TRY(be, cudaMemcpyAsync(m->history + dst * P, m->history + src * P, (size_t)P * 4,
+                                      cudaMemcpyDeviceToDevice, m->stream));
     return OASR_STATUS_SUCCESS;
 }
 
@@ -464,6 +567,8 @@ int oasr_b200_whisper_free(oasr_whisper *m) {
     cudaSetDevice(m->be->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->graph) cudaGraphExecDestroy(m->graph);
+    for (cudaGraphExec_t g : m->serve_graph)
+        if (g) cudaGraphExecDestroy(g);
     for (auto *w : m->weights) oasr_b200_weight_free(m->be, w);
     for (void *p : m->allocs) cudaFree(p);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -490,11 +595,29 @@ int oasr_b200_whisper_load(oasr_backend *be, const oasr_whisper_config *cfg, con
     m->ffn = 4 * cfg->d_model;
     m->T_enc = cfg->n_audio_ctx;
     m->B = cfg->max_batch;
+    {
+        // serving width capped by the device memory left for per-slot state once the
+        // weights are resident (serve_batch_vram_capped_max_batch, serve_batch_env.rs:295-315)
+        uint64_t weights = 0;
+        for (int i = 0; i < n_tensors; ++i) weights += tensors[i].bytes;
+        size_t free_b = 0, total_b = 0;
+        if (cfg->max_batch > 2 && cudaMemGetInfo(&free_b, &total_b) == cudaSuccess) {
+            const uint64_t used = 2 * weights;  // raw blocks + decode tiles / planes
+            const uint64_t avail = free_b > used ? free_b - used : 0;
+            m->B = oasr_b200_serve_batch_vram_cap(cfg->max_batch, oasr::whisper_slot_bytes(cfg), avail,
+                                                  oasr::serve_vram_reserve_bytes());
+        }
+    }
     m->K1p = (3 * cfg->n_mels + 63) / 64 * 64;
     m->K2p = (3 * cfg->d_model + 63) / 64 * 64;
     m->graph = nullptr;
     m->graph_batch = 0;
     m->stream = nullptr;
+    for (int i = 0; i < 4; ++i) {
+        m->serve_graph[i] = nullptr;
+        m->serve_epoch[i] = 0;
+    }
+    m->serve_key[0] = m->serve_key[1] = m->serve_key[2] = -1;
     auto fail = [&](int s) {
         oasr_b200_whisper_free(m);
         return s;
@@ -566,6 +689,9 @@ int oasr_b200_whisper_load(oasr_backend *be, const oasr_whisper_config *cfg, con
         L_TRY(dalloc(m, &L.self_k, (size_t)B * P * d * 2));
         L_TRY(dalloc(m, &L.self_v, (size_t)B * P * d * 2));
         L_TRY(dalloc(m, &L.cross_kv, (size_t)B * T * 2 * d * 2));
+        // slots that never held an utterance read zeros, not stale memory
+        if (cudaMemset(L.cross_kv, 0, (size_t)B * T * 2 * d * 2) != cudaSuccess)
+            return fail(oasr_internal_fail(be, OASR_STATUS_FAILED, "whisper: cross-K/V clear failed"));
         m->dec.push_back(L);
     }
     L_TRY(upload_f32(m, T_("decoder.ln.weight"), d, &m->lnd_g, "decoder.ln.weight"));
@@ -633,9 +759,13 @@ int oasr_b200_whisper_load(oasr_backend *be, const oasr_whisper_config *cfg, con
     L_TRY(alloc_planes(m, &m->dqa_f, FAMILY_Q8_K, B, m->ffn));
     L_TRY(alloc_planes(m, &m->dqa_lm, FAMILY_Q8_0, B, d));
     L_TRY(dalloc(m, &m->tokens, (size_t)B * 4));
-    L_TRY(dalloc(m, &m->pos, 4));
-    L_TRY(dalloc(m, &m->nkv, 4));
+    L_TRY(dalloc(m, &m->pos, (size_t)B * 4));  // per slot
+    L_TRY(dalloc(m, &m->nkv, (size_t)B * 4));
     L_TRY(dalloc(m, &m->history, (size_t)B * P * 4));
+    L_TRY(dalloc(m, &m->done, (size_t)B * 4));
+    L_TRY(dalloc(m, &m->budget, (size_t)B * 4));
+    L_TRY(dalloc(m, &m->prompt_dev, (size_t)P * 4));
+    L_TRY(dalloc(m, &m->serve_io, (size_t)4 * B * 4));
     // flash-decode partials for the largest split configuration seen by a decoder step
     m->step_scratch = (size_t)std::max<int64_t>(64ll << 20, (int64_t)B * m->H * 1024 * 66 * 4);
     L_TRY(oasr_b200_reserve_scratch(be, m->step_scratch));
@@ -758,6 +888,136 @@ int oasr_b200_whisper_generate(oasr_whisper *m, int32_t n_utts, const int32_t *p
         return oasr_b200_synchronize(m->be);
     }
     return oasr_internal_launch_check(m->be, "whisper_generate");
+}
+
+
+int oasr_b200_whisper_max_batch(oasr_whisper *m) { return m ? m->B : 0; }
+
+int oasr_b200_whisper_serve(oasr_whisper *m, const float *pcm, const int64_t *n_samples, int32_t n_utts,
+                            const int32_t *prompt, int32_t n_prompt, const int32_t *budgets, int32_t max_new,
+                            int32_t eot, int32_t stop_at_eot, int32_t max_width, int32_t check_every,
+                            int32_t *tokens_out, int32_t *lengths_out, oasr_serve_stats *stats) {
+    const int P = m ? (int)m->cfg.n_text_ctx : 0;
+    if (!m || !pcm || !n_samples || n_utts < 1 || !prompt || n_prompt < 1 || max_new < 1 ||
+        n_prompt + max_new > P || !tokens_out || !lengths_out || max_width < 0 || check_every < 1)
+        return m ? oasr_internal_fail(m->be, OASR_STATUS_FAILED, "whisper_serve: bad arguments") : OASR_STATUS_FAILED;
+    for (int r = 0; r < n_utts; ++r)
+        if (n_samples[r] < 1 || (budgets && (budgets[r] < 1 || budgets[r] > max_new)))
+            return oasr_internal_fail(m->be, OASR_STATUS_FAILED, "whisper_serve: empty clip or budget out of range");
+    int st = oasr_internal_precheck(m->be);
+    if (st) return st;
+    StreamScope sc(m);
+    oasr_backend *be = m->be;
+    const int W = max_width > 0 ? std::min(max_width, m->B) : m->B;
+    std::vector<int64_t> off(n_utts + 1, 0);
+    for (int r = 0; r < n_utts; ++r) off[r + 1] = off[r] + n_samples[r];
+    OASR_CUDA_TRY(be, cudaMemcpyAsync(m->prompt_dev, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, m->stream));
+    // the captured step graphs hold the serving parameters: re-capture when they change
+    if (m->serve_key[0] != n_prompt || m->serve_key[1] != eot || m->serve_key[2] != (stop_at_eot != 0)) {
+        for (cudaGraphExec_t &g : m->serve_graph)
+            if (g) {
+                cudaGraphExecDestroy(g);
+                g = nullptr;
+            }
+        m->serve_key[0] = n_prompt;
+        m->serve_key[1] = eot;
+        m->serve_key[2] = stop_at_eot != 0;
+    }
+    const ServeCtl ctl{m->prompt_dev, n_prompt, m->done, m->budget, eot, stop_at_eot != 0};
+    serve_park_kernel<<<1, 32, 0, m->stream>>>(m->B, m->prompt_dev, m->tokens, m->pos, m->nkv, m->done, m->budget);
+    W_TRY(oasr_internal_launch_check(be, "serve_park"));
+
+    std::vector<int> slot_req(m->B, -1);  // request held by each slot, -1 = free
+    int next = 0, active = 0, width = 0;
+    oasr_serve_stats stt = {};
+    // admit queued requests into the free slots below `width`: log-mel and encoder of the
+    // group (cross-attention K|V straight into the slots), then the slots' start state
+    auto admit = [&]() -> int {
+        std::vector<int> slots, reqs;
+        for (int b = 0; b < width && next < n_utts; ++b)
+            if (slot_req[b] < 0) {
+                slots.push_back(b);
+                reqs.push_back(next++);
+            }
+        if (slots.empty()) return OASR_STATUS_SUCCESS;
+        const int k = (int)slots.size();
+        OASR_CUDA_TRY(be, cudaMemsetAsync(m->audio, 0, (size_t)k * N_SAMPLES_30S * 4, m->stream));
+        for (int i = 0; i < k; ++i) {
+            const int64_t take = std::min<int64_t>(n_samples[reqs[i]], N_SAMPLES_30S);
+            OASR_CUDA_TRY(be, cudaMemcpyAsync(m->audio + (int64_t)i * N_SAMPLES_30S, pcm + off[reqs[i]], take * 4,
+                                              cudaMemcpyHostToDevice, m->stream));
+        }
+        W_TRY(launch_mel(be, m->audio, k, N_SAMPLES_30S, N_MEL_FRAMES, m->cfg.n_mels, m->window, m->twiddle,
+                         m->filters, m->power, m->mel, m->max_key));
+        W_TRY(run_encoder(m, k, slots.data()));
+        std::vector<int> io(2 * k);
+        for (int i = 0; i < k; ++i) {
+            io[i] = slots[i];
+            io[k + i] = budgets ? budgets[reqs[i]] : max_new;
+            slot_req[slots[i]] = reqs[i];
+        }
+        OASR_CUDA_TRY(be, cudaMemcpyAsync(m->serve_io, io.data(), io.size() * 4, cudaMemcpyHostToDevice, m->stream));
+        serve_admit_kernel<<<1, 32, 0, m->stream>>>(m->serve_io, k, m->prompt_dev, m->tokens, m->pos, m->nkv,
+                                                    m->done, m->budget);
+        W_TRY(oasr_internal_launch_check(be, "serve_admit"));
+        active += k;
+        ++stt.admissions;
+        return OASR_STATUS_SUCCESS;
+    };
+    width = oasr_b200_serve_batch_width(std::min(n_utts, W), W);
+    stt.max_width = width;
+    W_TRY(admit());
+    std::vector<int> done(m->B), pos(m->B);
+    while (active > 0) {
+        if (be->abort_cb && be->abort_cb(be->abort_data)) return OASR_STATUS_ABORTED;  // step checkpoint
+        for (int i = 0; i < check_every; ++i) W_TRY(serve_step_graph(m, width, ctl));
+        stt.steps += check_every;
+        OASR_CUDA_TRY(be, cudaMemcpyAsync(done.data(), m->done, (size_t)width * 4, cudaMemcpyDeviceToHost, m->stream));
+        OASR_CUDA_TRY(be, cudaMemcpyAsync(pos.data(), m->pos, (size_t)width * 4, cudaMemcpyDeviceToHost, m->stream));
+        OASR_CUDA_TRY(be, cudaStreamSynchronize(m->stream));
+        // harvest: a finished slot's generated tokens are history[n_prompt .. pos + 1]
+        for (int b = 0; b < width; ++b) {
+            const int r = slot_req[b];
+            if (r < 0 || !done[b]) continue;
+            const int count = pos[b] + 2 - n_prompt;
+            lengths_out[r] = count;
+            OASR_CUDA_TRY(be, cudaMemcpyAsync(tokens_out + (int64_t)r * max_new, m->history + (int64_t)b * P + n_prompt,
+                                              (size_t)count * 4, cudaMemcpyDeviceToHost, m->stream));
+            slot_req[b] = -1;
+            --active;
+        }
+        // refill the free slots; widen when more requests wait than the width holds
+        // (try_rebucket_active_slots), else narrow to the bucket of the active count
+        // (try_shrink_active_slots), compacting the active slots to the front
+        const int pending = n_utts - next;
+        const int want = oasr_b200_serve_batch_width(std::min(active + pending, W), W);
+        if (want > width) {
+            width = want;
+            ++stt.width_changes;
+        }
+        if (pending > 0) W_TRY(admit());
+        if (next >= n_utts && active > 0) {
+            const int narrow = oasr_b200_serve_batch_width(active, W);
+            if (narrow < width) {
+                int dst = 0;
+                for (int src = 0; src < width; ++src) {
+                    if (slot_req[src] < 0) continue;
+                    while (slot_req[dst] >= 0 && dst < src) ++dst;
+                    if (dst < src) {
+                        W_TRY(serve_move_slot(m, src, dst));
+                        slot_req[dst] = slot_req[src];
+                        slot_req[src] = -1;
+                    }
+                }
+                width = narrow;
+                ++stt.width_changes;
+            }
+        }
+        stt.max_width = std::max(stt.max_width, width);
+    }
+    OASR_CUDA_TRY(be, cudaStreamSynchronize(m->stream));
+    if (stats) *stats = stt;
+    return oasr_b200_synchronize(be);
 }
 
 int oasr_b200_whisper_transcribe(oasr_whisper *m, const float *pcm, const int64_t *n_samples, int32_t n_utts,

@@ -47,6 +47,8 @@ const Entry kEntries[] = {
     OASR_ENTRY(oasr_b200_qwen_read_kv),
     OASR_ENTRY(oasr_b200_reserve_scratch),
     OASR_ENTRY(oasr_b200_row_size),
+    OASR_ENTRY(oasr_b200_serve_batch_vram_cap),
+    OASR_ENTRY(oasr_b200_serve_batch_width),
     OASR_ENTRY(oasr_b200_set_abort_callback),
     OASR_ENTRY(oasr_b200_selftest_bounded_wait),
     OASR_ENTRY(oasr_b200_set_rows),
@@ -65,7 +67,9 @@ const Entry kEntries[] = {
     OASR_ENTRY(oasr_b200_whisper_generate),
     OASR_ENTRY(oasr_b200_whisper_load),
     OASR_ENTRY(oasr_b200_whisper_mel),
+    OASR_ENTRY(oasr_b200_whisper_max_batch),
     OASR_ENTRY(oasr_b200_whisper_mel_device),
+    OASR_ENTRY(oasr_b200_whisper_serve),
     OASR_ENTRY(oasr_b200_whisper_transcribe),
 };
 

@@ -213,6 +213,29 @@ class WhisperModel:
             1 if stop_at_eot else 0, out.ctypes.data))
         return out
 
+    @property
+    def max_batch(self) -> int:
+        """serving slots after the load-time VRAM cap"""
+        return int(bk.lib().oasr_b200_whisper_max_batch(self.handle))
+
+    def serve(self, clips, max_new: int = 224, budgets=None, prompt=None, stop_at_eot: bool = True,
+              max_width: int = 0, check_every: int = 8, eot: int = EOT):
+        """Continuous-batching transcription of a queue of clips (models/seq2seq_serve_batch.rs
+        decode_continuous_batch): finished slots are refilled from the queue and the batch
+        re-bucketed to powers of two.  Returns ([generated tokens per clip], ServeStats)."""
+        prompt = np.ascontiguousarray(prompt if prompt is not None else PROMPT[self.cfg.n_vocab], np.int32)
+        pcm, ns = self._pcm(clips)
+        n = len(clips)
+        out = np.empty((n, max_new), np.int32)
+        lens = np.zeros(n, np.int32)
+        bud = None if budgets is None else np.ascontiguousarray(budgets, np.int32)
+        st = bk.ServeStats()
+        self.backend._check(bk.lib().oasr_b200_whisper_serve(
+            self.handle, pcm.ctypes.data, ns.ctypes.data, n, prompt.ctypes.data, len(prompt),
+            None if bud is None else bud.ctypes.data, max_new, eot, 1 if stop_at_eot else 0, max_width, check_every,
+            out.ctypes.data, lens.ctypes.data, ctypes.byref(st)))
+        return [out[i, :lens[i]].copy() for i in range(n)], st
+
 
 # ---- Qwen3-ASR LLM decoder --------------------------------------------------------------
 @dataclasses.dataclass(frozen=True)
