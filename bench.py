@@ -138,13 +138,9 @@ def measured_peak_hbm() -> tuple[float, str]:
 
 
 def ncu_traffic() -> float | None:
-    p = os.path.join(ROOT, "profiles", "mmv_q8_0_lm_head_151936x1024_m8.json")
-    if os.path.exists(p):
-        try:
-            return float(json.load(open(p))["dram_bytes_per_launch"])
-        except (KeyError, ValueError):
-            return None
-    return None
+    """dram read + write bytes of one Qwen logits-head GEMV launch (Q8_0 151936 x 1024,
+    M = 8), from its committed ncu summary."""
+    return ncu_traffic_fa("mmv_q80_tc_lm_head_151936x1024_m8.md")
 
 
 # ---------------------------------------------------------------------------------------
@@ -706,6 +702,46 @@ def ncu_traffic_fa(summary: str = "fattn_heads_cross_b8.md") -> float | None:
     return None
 
 
+def run_profile_case(args) -> None:
+    """The small fixed cases the committed ncu captures of the model-internal kernels use:
+    each kernel at the RTFx / configs[2] workloads' own per-layer shapes, depth cut to 2
+    layers so the device holds about 1 GB.
+      --case whisper    whisper-large-v3-shaped Q4_K (2 + 2 layers, batch 8, 30 s clips)
+                        transcribing 8 tokens: conv stem gemm_f16_tc, encoder,
+                        ln_quant_chunks / gelu_quant_chunks, the fused decoder GEMVs
+                        (dgemv_kernel), cross- and self-attention, the Q8_0 logits head
+                        (mmv_q80_tc, the first launch of that kernel) and argmax_chunks
+      --case qwen_q8_0  Qwen3-ASR-0.6B-shaped (2 layers, batch 8, 390-frame prompt)
+                        generating 8 tokens: qwen_qkv_post, swiglu_quant_chunks, the
+                        151936-row logits head (mmv_q80_tc, first launch: the prefill's
+                        last-row logits)
+      --case qwen_q4_0  the same with Q4_0 linears: mmv_q8_kernel (the Q4_0 decode GEMV)"""
+    import torch
+
+    import openasr_b200 as ob
+    from openasr_b200 import models as om
+
+    torch.cuda.set_device(0)
+    be = ob.Backend(0)
+    out = {}
+    if args.case == "whisper":
+        cfg = om.WHISPER_LARGE_V3.replace(n_enc_layers=2, n_dec_layers=2, max_batch=8)
+        m = om.WhisperModel(be, cfg, om.whisper_synthetic_pack(cfg, seed=0x0A5A0004))
+        clips = [om.synthetic_audio(0x0A5A3000 + i, 16000 * 30) for i in range(8)]
+        out["tokens"] = m.transcribe(clips, n_new=8)[:, :4].tolist()
+        m.close()
+    else:
+        qc = om.QWEN3_ASR_0_6B.replace(n_layers=2, weight_type=ob.Q8_0 if args.case == "qwen_q8_0" else ob.Q4_0)
+        q = om.QwenModel(be, qc, om.qwen_synthetic_pack(qc))
+        emb = ob.synth_normal(0x0A5A3100, 8 * om.QWEN_PREFIX_FRAMES * qc.d_model, 0.0, 0.02).reshape(
+            8, om.QWEN_PREFIX_FRAMES, qc.d_model)
+        out["tokens"] = q.generate(emb, n_new=8)[:, :4].tolist()
+        q.close()
+    be.synchronize()
+    be.close()
+    print(json.dumps({"workload": "profile", "case": args.case, **out}), flush=True)
+
+
 def run_kernels(args) -> None:
     """Per-kernel roofline table at the RTFx workload's own shapes (whisper-large-v3,
     batch 8 per GPU), each op timed alone with CUDA events on the launching stream:
@@ -1086,8 +1122,10 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["rtfx", "qwen", "mulmat", "kernels"], default="rtfx")
+    ap.add_argument("--workload", choices=["rtfx", "qwen", "mulmat", "kernels", "profile"], default="rtfx")
     ap.add_argument("--batch", type=int, default=8, help="sequences per GPU (qwen workload: 1, 4 or 8)")
+    ap.add_argument("--case", choices=["whisper", "qwen_q8_0", "qwen_q4_0"], default="whisper",
+                    help="profile workload: which small model case to run")
     ap.add_argument("--no-job", action="store_true",
                     help="rtfx workload: skip the 512-utterance job leg and the CPU sample (profiling runs)")
     ap.add_argument("--new-tokens", type=int, default=256,
@@ -1096,7 +1134,9 @@ def main() -> None:
     args.warmup = max(args.warmup, 3)
     if args.steps is None:
         args.steps = 8 if args.workload in ("rtfx", "qwen") else 20
-    if args.workload == "kernels":
+    if args.workload == "profile":
+        run_profile_case(args)
+    elif args.workload == "kernels":
         run_kernels(args)
     elif args.workload == "rtfx":
         (run_reference if args.impl == "reference" else run_b200)(args)

@@ -510,8 +510,8 @@ typedef struct oasr_serve_stats {
  * or max_new when budgets is NULL) or the context end.  tokens_out
  * [n_utts][max_new] gets each request's generated tokens (the `eot` included),
  * lengths_out[n_utts] their count.  max_width 0 = the model's max batch; the host
- * looks for finished slots every check_every steps (steps of a finished slot
- * are idle).  A slot's tokens do not depend on the batch it ran in: they equal a
+ * looks for finished slots every check_every steps, and at the step the earliest
+ * budget ends (a slot that emits eot idles until the next look).  A slot's tokens do not depend on the batch it ran in: they equal a
  * serial oasr_b200_whisper_transcribe of the same utterance.  The abort callback is
  * polled before each group of steps. */
 int oasr_b200_whisper_serve(oasr_whisper *m, const float *pcm, const int64_t *n_samples, int32_t n_utts,

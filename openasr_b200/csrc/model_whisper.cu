@@ -598,11 +598,13 @@ int oasr_b200_whisper_load(oasr_backend *be, const oasr_whisper_config *cfg, con
     {
         // serving width capped by the device memory left for per-slot state once the
         // weights are resident (serve_batch_vram_capped_max_batch, serve_batch_env.rs:295-315)
-        uint64_t weights = 0;
-        for (int i = 0; i < n_tensors; ++i) weights += tensors[i].bytes;
+        // device bytes of the resident weights: raw blocks + decode tiles, and for Q4_K the
+        // tensor-core GEMM's fp16 operand (2 B per element = 3.6x the 4.5-bit blocks)
+        uint64_t used = 0;
+        for (int i = 0; i < n_tensors; ++i)
+            used += tensors[i].bytes * (tensors[i].type == OASR_TYPE_Q4_K ? 6 : 3);
         size_t free_b = 0, total_b = 0;
         if (cfg->max_batch > 2 && cudaMemGetInfo(&free_b, &total_b) == cudaSuccess) {
-            const uint64_t used = 2 * weights;  // raw blocks + decode tiles / planes
             const uint64_t avail = free_b > used ? free_b - used : 0;
             m->B = oasr_b200_serve_batch_vram_cap(cfg->max_batch, oasr::whisper_slot_bytes(cfg), avail,
                                                   oasr::serve_vram_reserve_bytes());
@@ -928,6 +930,7 @@ int oasr_b200_whisper_serve(oasr_whisper *m, const float *pcm, const int64_t *n_
     W_TRY(oasr_internal_launch_check(be, "serve_park"));
 
     std::vector<int> slot_req(m->B, -1);  // request held by each slot, -1 = free
+    std::vector<int> slot_age(m->B, 0);   // steps a slot has run since its admission
     int next = 0, active = 0, width = 0;
     oasr_serve_stats stt = {};
     // admit queued requests into the free slots below `width`: log-mel and encoder of the
@@ -955,6 +958,7 @@ int oasr_b200_whisper_serve(oasr_whisper *m, const float *pcm, const int64_t *n_
             io[i] = slots[i];
             io[k + i] = budgets ? budgets[reqs[i]] : max_new;
             slot_req[slots[i]] = reqs[i];
+            slot_age[slots[i]] = 0;
         }
         OASR_CUDA_TRY(be, cudaMemcpyAsync(m->serve_io, io.data(), io.size() * 4, cudaMemcpyHostToDevice, m->stream));
         serve_admit_kernel<<<1, 32, 0, m->stream>>>(m->serve_io, k, m->prompt_dev, m->tokens, m->pos, m->nkv,
@@ -970,8 +974,19 @@ int oasr_b200_whisper_serve(oasr_whisper *m, const float *pcm, const int64_t *n_
     std::vector<int> done(m->B), pos(m->B);
     while (active > 0) {
         if (be->abort_cb && be->abort_cb(be->abort_data)) return OASR_STATUS_ABORTED;  // step checkpoint
-        for (int i = 0; i < check_every; ++i) W_TRY(serve_step_graph(m, width, ctl));
-        stt.steps += check_every;
+        // steps to the next harvest: check_every, cut at the earliest step a slot reaches
+        // its budget (a slot with budget b finishes after n_prompt - 1 + b steps; one
+        // that meets eot earlier idles at most check_every - 1 steps)
+        int chunk = check_every;
+        for (int b = 0; b < width; ++b) {
+            const int r = slot_req[b];
+            if (r < 0) continue;
+            const int left = n_prompt - 1 + (budgets ? budgets[r] : max_new) - slot_age[b];
+            chunk = std::min(chunk, std::max(1, left));
+        }
+        for (int i = 0; i < chunk; ++i) W_TRY(serve_step_graph(m, width, ctl));
+        for (int b = 0; b < width; ++b) slot_age[b] += chunk;
+        stt.steps += chunk;
         OASR_CUDA_TRY(be, cudaMemcpyAsync(done.data(), m->done, (size_t)width * 4, cudaMemcpyDeviceToHost, m->stream));
         OASR_CUDA_TRY(be, cudaMemcpyAsync(pos.data(), m->pos, (size_t)width * 4, cudaMemcpyDeviceToHost, m->stream));
         OASR_CUDA_TRY(be, cudaStreamSynchronize(m->stream));
@@ -1006,6 +1021,7 @@ int oasr_b200_whisper_serve(oasr_whisper *m, const float *pcm, const int64_t *n_
                     if (dst < src) {
                         W_TRY(serve_move_slot(m, src, dst));
                         slot_req[dst] = slot_req[src];
+                        slot_age[dst] = slot_age[src];
                         slot_req[src] = -1;
                     }
                 }
