@@ -430,6 +430,8 @@ int oasr_b200_weight_upload(oasr_backend *be, const void *host, size_t bytes, in
     w->tiles = nullptr;
     w->dT = nullptr;
     w->qs8 = nullptr;
+    w->h16 = nullptr;
+    w->k_meta = nullptr;
     if (e == cudaSuccess && mmq_q80_tc_supported(type, ne[1], ne[0])) {
         // the tensor-core GEMM's operands: block-major f32 scales, and for Q4_0 the quants
         // expanded to int8 (the GEMM then runs as Q8_0 on them, bit for bit the Q4_0 dot)
@@ -441,6 +443,17 @@ int oasr_b200_weight_upload(oasr_backend *be, const void *host, size_t bytes, in
         if (e == cudaSuccess && qb) e = build_q40_expanded(w, be->stream);
         if (e == cudaSuccess) e = cudaStreamSynchronize(be->stream);
         if (e == cudaSuccess) w->device_bytes += db + qb;
+    }
+    if (e == cudaSuccess && mmq_q4k_tc_supported(type, ne[0])) {
+        // the tensor-core GEMM's operands: fp16 sub-scale x quant rows and per super-block
+        // metadata, built once on the device from the raw blocks
+        size_t mb = 0;
+        const size_t hb = q4k_operand_bytes(ne[1], ne[0], ne[2] * ne[3], &mb);
+        e = cudaMalloc(&w->h16, hb);
+        if (e == cudaSuccess) e = cudaMalloc(&w->k_meta, mb);
+        if (e == cudaSuccess) e = build_q4k_operand(w, be->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(be->stream);
+        if (e == cudaSuccess) w->device_bytes += hb + mb;
     }
     if (e == cudaSuccess && be->decode_tiles && mmv_tiles_supported(type, ne[0])) {
         // decode-tile copy for the tensor-core GEMV, built on the device from the planes above
@@ -456,6 +469,8 @@ int oasr_b200_weight_upload(oasr_backend *be, const void *host, size_t bytes, in
         if (w->tiles) cudaFree(w->tiles);
         if (w->dT) cudaFree(w->dT);
         if (w->qs8) cudaFree(w->qs8);
+        if (w->h16) cudaFree(w->h16);
+        if (w->k_meta) cudaFree(w->k_meta);
         delete w;
         oasr_internal_mem_event(be, false);
         return oasr_internal_cuda_fail(be, e, "weight_upload", __LINE__);
@@ -481,6 +496,8 @@ int oasr_b200_weight_free(oasr_backend *be, oasr_weight *w) {
     if (w->tiles) cudaFree(w->tiles);
     if (w->dT) cudaFree(w->dT);
     if (w->qs8) cudaFree(w->qs8);
+    if (w->h16) cudaFree(w->h16);
+    if (w->k_meta) cudaFree(w->k_meta);
     delete w;
     return OASR_STATUS_SUCCESS;
 }

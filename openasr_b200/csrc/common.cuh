@@ -52,6 +52,8 @@ struct oasr_weight {
     uint8_t *tiles;          // decode-tile copy for the tensor-core GEMV (Q4_K, Q8_0), or null
     float *dT;               // Q8_0 / Q4_0: block-major f32 scales [slices][K/32][N] for the tensor-core GEMM, or null
     int8_t *qs8;             // Q4_0: the quants expanded to int8 (q - 8) [slices][N][K] for that GEMM, or null
+    __half *h16;             // Q4_K: sub-scale x quant as fp16 [slices][N][K] for the tensor-core GEMM, or null
+    float *k_meta;           // Q4_K: per super-block d, dmin, mins of weight-row pairs for that GEMM, or null
     uint64_t device_bytes;
 };
 

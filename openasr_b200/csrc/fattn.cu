@@ -382,6 +382,163 @@ static __device__ void heads_quantize_out(const FaArgs &a, const float *s_out, i
     else q80_chunk(v, q, a.od + s * (K / 32) + 8 * hg, lane);
 }
 
+// One batch of a 4-head decode warp: U positions pb + 4u (u < U) of this lane group's
+// head, K / V as 16-byte pieces (8 dims) per lane; positions >= kv1 carry zero rows and
+// weight 0.  The U scores are independent: compute them all, then fold the block into the
+// running softmax state with one rescale (a block-wise online softmax).  With U = 8 the
+// 8 lanes of a head finish the 8 dot products as a transpose-reduce: at each butterfly
+// level a lane keeps half of its partial sums and adds the partner's half, so lane sl
+// ends with the whole dot of position sl (the same pairs added in the same order as a
+// per-position butterfly: bit-identical scores), takes one exp instead of 8, and the
+// weights are gathered back by shuffles.
+template <int U>
+static __device__ __forceinline__ void heads_consume(int pb, int kv1, float scale, int lane, int sl,
+                                                     const int4 (&kr)[U], const int4 (&vr)[U], const float (&qv)[8],
+                                                     float &mx, float &sm, float (&acc)[8]) {
+    float sc[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        float kf[8];
+        load8<true>(reinterpret_cast<const char *>(&kr[u]), kf);
+        float d = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) d = __fmaf_rn(qv[e], kf[e], d);
+        sc[u] = d;
+    }
+    float wv[U];
+    float mnew;
+    if constexpr (U == 8) {
+        const bool b4 = sl & 4, b2 = sl & 2, b1 = sl & 1;
+        float r4[4], r2[2];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float keep = b4 ? sc[j + 4] : sc[j], send = b4 ? sc[j] : sc[j + 4];
+            r4[j] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const float keep = b2 ? r4[j + 2] : r4[j], send = b2 ? r4[j] : r4[j + 2];
+            r2[j] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 2));
+        }
+        const float keep = b1 ? r2[1] : r2[0], send = b1 ? r2[0] : r2[1];
+        const float dot = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 1));  // position pb + 4 sl
+        const float s1 = pb + 4 * sl < kv1 ? __fmul_rn(dot, scale) : -INFINITY;
+        float mb = s1;
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+        mnew = fmaxf(mx, mb);                           // finite: position pb is valid
+        const float w1 = exp_f32(__fsub_rn(s1, mnew));  // invalid positions: exp(-inf) = 0
+#pragma unroll
+        for (int u = 0; u < U; ++u) wv[u] = __shfl_sync(0xffffffffu, w1, (lane & ~7) | u);
+    } else {
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            float d = sc[u];
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1) d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, o));
+            sc[u] = pb + 4 * u < kv1 ? __fmul_rn(d, scale) : -INFINITY;
+        }
+        float mb = sc[0];
+#pragma unroll
+        for (int u = 1; u < U; ++u) mb = fmaxf(mb, sc[u]);
+        mnew = fmaxf(mx, mb);
+#pragma unroll
+        for (int u = 0; u < U; ++u) wv[u] = exp_f32(__fsub_rn(sc[u], mnew));
+    }
+    const float corr = exp_f32(__fsub_rn(mx, mnew));  // mx = -inf -> 0
+    sm = __fmul_rn(sm, corr);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = __fmul_rn(acc[e], corr);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        float vf[8];
+        load8<true>(reinterpret_cast<const char *>(&vr[u]), vf);
+        sm = __fadd_rn(sm, wv[u]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = __fmaf_rn(wv[u], vf[e], acc[e]);
+    }
+    mx = mnew;
+}
+
+// The end of a 4-head decode CTA (warps 0-3 hold the online-softmax state of their
+// positions; any further warps of the CTA take part in the barriers only): merge the 4
+// warps through shared memory in warp order, then either write the outputs (one split) or
+// the (acc, m, l) partial, and in the last-arriving CTA of the (sequence, head group) merge
+// the splits in split order.  `scratch` holds 4 * FA_HEADS_MAX_SPLITS * 66 floats.
+static __device__ __forceinline__ void heads_finish(const FaArgs &a, const float (&acc)[8], float mx, float sm, int s,
+                                                    int hg, int split, int warp, int hl, int sl, int lane,
+                                                    float *scratch) {
+    constexpr int D = 64;
+    const bool worker = threadIdx.x < 128;
+    __shared__ float s_out[4 * D];  // the 4 heads' outputs when they leave as activation planes
+    __shared__ float s_m[4][4], s_s[4][4];
+    float(*s_acc)[4][D] = reinterpret_cast<float(*)[4][D]>(scratch);  // [warp][head][D]
+    if (worker) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s_acc[warp][hl][sl * 8 + e] = acc[e];
+        if (sl == 0) {
+            s_m[warp][hl] = mx;
+            s_s[warp][hl] = sm;
+        }
+    }
+    __shared__ float s_f[4][4], s_L[4], s_M[4];
+    __syncthreads();
+    if (threadIdx.x < 4) warp_merge_factors<4>(s_m, s_s, threadIdx.x, s_f, s_L, s_M);
+    __syncthreads();
+    if (worker)
+        for (int o = threadIdx.x; o < 4 * D; o += 128) {
+            const int t = o / D, e = o % D;
+            const float M = s_M[t], L = s_L[t];
+            float A = 0.0f;
+#pragma unroll
+            for (int w = 0; w < 4; ++w) A = __fmaf_rn(s_acc[w][t][e], s_f[w][t], A);
+            const int hh = 4 * hg + t;
+            if (a.n_splits == 1) {
+                const float val = L == 0.0f ? 0.0f : __fdiv_rn(A, L);
+                if (a.oq) s_out[t * D + e] = val;
+                else reinterpret_cast<float *>(a.dst + hh * a.d_nb1 + s * a.d_nb3)[e] = val;
+            } else {
+                const int64_t row = (int64_t)s * a.H + hh;
+                float *pp = a.partials + (row * a.n_splits + split) * (D + 2);
+                pp[e] = A;
+                if (e == 0) {
+                    pp[D] = M;
+                    pp[D + 1] = L;
+                }
+            }
+        }
+    if (a.n_splits == 1) {
+        if (a.oq) heads_quantize_out(a, s_out, s, hg, warp, lane);
+        return;
+    }
+    if (!cta_last_arrival(a.counters + blockIdx.x, (unsigned)a.n_splits)) return;
+    // the 4 heads' partials are contiguous ([head][split][D + 2]): stage them in shared
+    // memory with every load in flight, then merge in split order
+    float *s_part = scratch;  // the warps' accumulators are merged already
+    const int nP = 4 * a.n_splits * (D + 2);
+    const float *pbase = a.partials + ((int64_t)s * a.H + 4 * hg) * a.n_splits * (D + 2);
+    __syncthreads();
+    if (worker) stage_l2(s_part, pbase, nP);
+    __syncthreads();
+    __shared__ float s_fs[4][FA_HEADS_MAX_SPLITS], s_Ls[4];
+    if (threadIdx.x < 4)
+        split_merge_factors(s_part + threadIdx.x * a.n_splits * (D + 2), a.n_splits, D, s_fs[threadIdx.x],
+                            &s_Ls[threadIdx.x]);
+    __syncthreads();
+    if (worker)
+        for (int o = threadIdx.x; o < 4 * D; o += 128) {
+            const int t = o / D, e = o % D;
+            const float *pp = s_part + t * a.n_splits * (D + 2);
+            const float L = s_Ls[t];
+            float A = 0.0f;
+            for (int sp = 0; sp < a.n_splits; ++sp) A = __fmaf_rn(pp[sp * (D + 2) + e], s_fs[t][sp], A);
+            const float val = L == 0.0f ? 0.0f : __fdiv_rn(A, L);
+            if (a.oq) s_out[t * D + e] = val;
+            else reinterpret_cast<float *>(a.dst + (4 * hg + t) * a.d_nb1 + s * a.d_nb3)[e] = val;
+        }
+    if (a.oq) heads_quantize_out(a, s_out, s, hg, warp, lane);
+}
+
 // Decode attention with one query per (sequence, head) over f16 K/V whose heads lie
 // contiguously in a KV row (the Whisper decoder's self- and cross-attention caches):
 // a CTA takes 4 heads of one sequence and a range of KV positions, and every warp
@@ -428,77 +585,8 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
             }
         }
     };
-    // the U scores are independent: compute them all, then fold the block into the
-    // running softmax state with one rescale (a block-wise online softmax).  With U = 8
-    // the 8 lanes of a head finish the 8 dot products as a transpose-reduce: at each
-    // butterfly level a lane keeps half of its partial sums and adds the partner's half,
-    // so lane sl ends with the whole dot of position sl (the same pairs added in the same
-    // order as a per-position butterfly: bit-identical scores), takes one exp instead of
-    // 8, and the weights are gathered back by shuffles.
     auto consume = [&](int pb, const int4 (&kr)[U], const int4 (&vr)[U]) {
-        float sc[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            float kf[8];
-            load8<true>(reinterpret_cast<const char *>(&kr[u]), kf);
-            float d = 0.0f;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) d = __fmaf_rn(qv[e], kf[e], d);
-            sc[u] = d;
-        }
-        float wv[U];
-        float mnew;
-        if constexpr (U == 8) {
-            const bool b4 = sl & 4, b2 = sl & 2, b1 = sl & 1;
-            float r4[4], r2[2];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float keep = b4 ? sc[j + 4] : sc[j], send = b4 ? sc[j] : sc[j + 4];
-                r4[j] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 4));
-            }
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const float keep = b2 ? r4[j + 2] : r4[j], send = b2 ? r4[j] : r4[j + 2];
-                r2[j] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 2));
-            }
-            const float keep = b1 ? r2[1] : r2[0], send = b1 ? r2[0] : r2[1];
-            const float dot = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, 1));  // position pb + 4 sl
-            const float s1 = pb + 4 * sl < kv1 ? __fmul_rn(dot, a.scale) : -INFINITY;
-            float mb = s1;
-#pragma unroll
-            for (int o = 4; o > 0; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
-            mnew = fmaxf(mx, mb);                    // finite: position pb is valid
-            const float w1 = exp_f32(__fsub_rn(s1, mnew));  // invalid positions: exp(-inf) = 0
-#pragma unroll
-            for (int u = 0; u < U; ++u) wv[u] = __shfl_sync(0xffffffffu, w1, (lane & ~7) | u);
-        } else {
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                float d = sc[u];
-#pragma unroll
-                for (int o = 4; o > 0; o >>= 1) d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, o));
-                sc[u] = pb + 4 * u < kv1 ? __fmul_rn(d, a.scale) : -INFINITY;
-            }
-            float mb = sc[0];
-#pragma unroll
-            for (int u = 1; u < U; ++u) mb = fmaxf(mb, sc[u]);
-            mnew = fmaxf(mx, mb);
-#pragma unroll
-            for (int u = 0; u < U; ++u) wv[u] = exp_f32(__fsub_rn(sc[u], mnew));
-        }
-        const float corr = exp_f32(__fsub_rn(mx, mnew));  // mx = -inf -> 0
-        sm = __fmul_rn(sm, corr);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] = __fmul_rn(acc[e], corr);
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            float vf[8];
-            load8<true>(reinterpret_cast<const char *>(&vr[u]), vf);
-            sm = __fadd_rn(sm, wv[u]);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc[e] = __fmaf_rn(wv[u], vf[e], acc[e]);
-        }
-        mx = mnew;
+        heads_consume<U>(pb, kv1, a.scale, lane, sl, kr, vr, qv, mx, sm, acc);
     };
 
     int4 kA[U], vA[U], kB[U], vB[U];
@@ -545,69 +633,8 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
         pb = pn;
     }
 
-    // merge the 4 warps (disjoint positions, same heads) through shared memory
-    __shared__ float s_out[4 * D];  // the 4 heads' outputs when they leave as activation planes
-    __shared__ float s_m[4][4], s_s[4][4];
-    __shared__ float s_acc[4][4][D];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) s_acc[warp][hl][sl * 8 + e] = acc[e];
-    if (sl == 0) {
-        s_m[warp][hl] = mx;
-        s_s[warp][hl] = sm;
-    }
-    __shared__ float s_f[4][4], s_L[4], s_M[4];
-    __syncthreads();
-    if (threadIdx.x < 4) warp_merge_factors<4>(s_m, s_s, threadIdx.x, s_f, s_L, s_M);
-    __syncthreads();
-    for (int o = threadIdx.x; o < 4 * D; o += 128) {
-        const int t = o / D, e = o % D;
-        const float M = s_M[t], L = s_L[t];
-        float A = 0.0f;
-#pragma unroll
-        for (int w = 0; w < 4; ++w) A = __fmaf_rn(s_acc[w][t][e], s_f[w][t], A);
-        const int hh = 4 * hg + t;
-        if (a.n_splits == 1) {
-            const float val = L == 0.0f ? 0.0f : __fdiv_rn(A, L);
-            if (a.oq) s_out[t * D + e] = val;
-            else reinterpret_cast<float *>(a.dst + hh * a.d_nb1 + s * a.d_nb3)[e] = val;
-        } else {
-            const int64_t row = (int64_t)s * a.H + hh;
-            float *pp = a.partials + (row * a.n_splits + split) * (D + 2);
-            pp[e] = A;
-            if (e == 0) {
-                pp[D] = M;
-                pp[D + 1] = L;
-            }
-        }
-    }
-    if (a.n_splits == 1) {
-        if (a.oq) heads_quantize_out(a, s_out, s, hg, warp, lane);
-        return;
-    }
-    if (!cta_last_arrival(a.counters + blockIdx.x, (unsigned)a.n_splits)) return;
-    // the 4 heads' partials are contiguous ([head][split][D + 2]): stage them in shared
-    // memory with every load in flight, then merge in split order
-    __shared__ float s_part[4 * FA_HEADS_MAX_SPLITS * (D + 2)];
-    const int nP = 4 * a.n_splits * (D + 2);
-    const float *pbase = a.partials + ((int64_t)s * a.H + 4 * hg) * a.n_splits * (D + 2);
-    stage_l2(s_part, pbase, nP);
-    __syncthreads();
-    __shared__ float s_fs[4][FA_HEADS_MAX_SPLITS], s_Ls[4];
-    if (threadIdx.x < 4)
-        split_merge_factors(s_part + threadIdx.x * a.n_splits * (D + 2), a.n_splits, D, s_fs[threadIdx.x],
-                            &s_Ls[threadIdx.x]);
-    __syncthreads();
-    for (int o = threadIdx.x; o < 4 * D; o += 128) {
-        const int t = o / D, e = o % D;
-        const float *pp = s_part + t * a.n_splits * (D + 2);
-        const float L = s_Ls[t];
-        float A = 0.0f;
-        for (int sp = 0; sp < a.n_splits; ++sp) A = __fmaf_rn(pp[sp * (D + 2) + e], s_fs[t][sp], A);
-        const float val = L == 0.0f ? 0.0f : __fdiv_rn(A, L);
-        if (a.oq) s_out[t * D + e] = val;
-        else reinterpret_cast<float *>(a.dst + (4 * hg + t) * a.d_nb1 + s * a.d_nb3)[e] = val;
-    }
-    if (a.oq) heads_quantize_out(a, s_out, s, hg, warp, lane);
+    __shared__ __align__(16) float s_scratch[4 * FA_HEADS_MAX_SPLITS * (D + 2)];
+    heads_finish(a, acc, mx, sm, s, hg, split, warp, hl, sl, lane, s_scratch);
 }
 
 // Decode attention with grouped queries over head-major f16 caches (the Qwen decoder:
@@ -991,6 +1018,7 @@ static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const
                      ((uintptr_t)k->data & 15) == 0 && ((uintptr_t)v->data & 15) == 0 &&
                      (int64_t)a.S * a.HKV <= 0x7fffffffLL;
     if (heads || gqa) a.kv_static = kv_static;
+
     if (out_q8) {
         if (!((gqa && out_family == FAMILY_Q8_0) || (heads && D == 64)))
             return oasr_internal_fail(be, OASR_STATUS_FAILED,

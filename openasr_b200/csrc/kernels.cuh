@@ -83,6 +83,9 @@ int launch_mmv_float(oasr_backend *be, const oasr_weight *w, int64_t slice, cons
 bool mmq_q80_tc_supported(int type, int64_t N, int64_t K);
 cudaError_t build_q80_scales_t(oasr_weight *w, cudaStream_t st);
 cudaError_t build_q40_expanded(oasr_weight *w, cudaStream_t st);  // w->qs8 from a Q4_0 weight's nibble plane
+bool mmq_q4k_tc_supported(int type, int64_t K);
+size_t q4k_operand_bytes(int64_t N, int64_t K, int64_t slices, size_t *meta_bytes);  // h16 bytes; *meta_bytes k_meta
+cudaError_t build_q4k_operand(oasr_weight *w, cudaStream_t st);  // w->h16, w->k_meta from the raw Q4_K rows
 int launch_mmq(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int64_t M, int K,
                float *y, int64_t y_ld);
 

@@ -6,25 +6,31 @@
 //     isum = sum_j sc_j * <q4_j, q8_j>          (integers)
 //     msum = sum_j m_j * bsum32_j               (integers)
 //     term = (d_w*d_a)*isum - (dmin_w*d_a)*msum (f32)
-//   Here the 6-bit sub-scales are folded into the weight operand (sc*q <= 945,
-//   exact in fp16) and the q8_K activations are fp16 integers, so one
-//   tcgen05.mma.kind::f16 chain over the super-block yields isum exactly in
-//   the f32 accumulator; a second K=16 MMA of the 16-wide activation sums
-//   against the duplicated mins yields msum.  The epilogue forms `term` with
-//   the same roundings as ggml and adds the super-blocks in order, so the
-//   result equals the CPU oracle's bit for bit.
+//   At upload the 6-bit sub-scales are folded into the weight (sc*q <= 945, an
+//   fp16 integer) once, so the B operand is a plain fp16 matrix streamed by TMA;
+//   the q8_K activations are fp16 integers too.  tcgen05.mma.kind::f16 adds the
+//   products in f32, exact while every partial sum stays below 2^24 -- so each
+//   super-block accumulates as two 128-element halves in separate TMEM columns
+//   (|half| <= 128*945*127 = 15,361,920 < 2^24) and the epilogue's f32 add of
+//   the two exact halves is ggml's (float)isum (IEEE addition rounds the exact
+//   sum once).  msum is 8 products per output (|msum| <= 8*63*4064 < 2^24), done
+//   on the CUDA cores in integers: the activation's 32-quant sums split into a
+//   6-bit low byte and a signed high byte, 4 dp4a against the mins bytes, and the
+//   exact integer turned into a float by adding it to the bits of 1.5 * 2^23.  The epilogue forms `term` with ggml's
+//   roundings and adds the super-blocks in order, so the result equals the CPU
+//   oracle bit for bit for all inputs, the adversarial ones (all sub-scales 63,
+//   quants 15, activations +-127) included.
 //
-// CTA = 128 activation rows x 128 weight rows, 14 warps:
-//   warp 0      TMA producer of the activation tiles (128 x 64 fp16, SW128)
+// CTA = 128 activation rows x 128 weight rows, 18 warps:
+//   warp 0      TMA producer: activation and weight tiles (128 x 64 fp16, SW128),
+//               and per super-block the tile's weight metadata (d, dmin, 8 mins)
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2-5   weight transform: raw Q4_K blocks -> fp16 sc*q in the SW128
-//               K-major layout, plus the per-super-block min tiles
-//   warps 6-13  epilogue: TMEM -> registers, per-super-block scaling
-// TMEM: two accumulator sets (isum 128 cols + msum 128 cols) so the epilogue
-// of super-block s overlaps the MMAs of s+1.  Every mbarrier wait is bounded.
+//   warps 2-17  epilogue: warp w reads TMEM lane quarter w % 4, 32 of the columns
+// TMEM: two sets of (low half 128 cols + high half 128 cols) so the epilogue of
+// super-block s overlaps the MMAs of s+1.  Every mbarrier wait is bounded.
 //
-// Q8_0 runs on tcgen05 kind::i8 (mmq_q80_tc_kernel below); Q4_0 still uses the
-// K1 GEMV kernel over groups of 8 rows.
+// Q8_0 runs on tcgen05 kind::i8 (mmq_q80_tc_kernel below), Q4_0 on the same
+// kernel over its quants expanded to int8.
 #include <cudaTypedefs.h>
 
 #include "kernels.cuh"
@@ -35,29 +41,31 @@ namespace oasr {
 namespace q4k {
 constexpr int BM = 128;
 constexpr int BN = 128;
-constexpr int BK = 64;
-constexpr int STAGES = 3;
-constexpr int WSTAGES = 3;       // raw Q4_K super-block ring
-constexpr int TILE = 128 * 128;  // bytes of one 128-row x 128-byte operand tile
-constexpr int WTILE = 128 * 144; // 128 weight rows x one raw super-block (18 KB)
-constexpr int NTHREADS = 448;
+constexpr int BK = 64;               // fp16 elements per stage = one 128-byte swizzle row
+constexpr int STAGES = 5;
+constexpr int TILE = 128 * 128;      // bytes of one 128-row x 128-byte operand tile
+constexpr int META_COL = 4;          // 32-bit words per weight row: d, dmin (f32), mins 0-3, 4-7 (bytes)
+constexpr int META = BN * META_COL * 4;  // one tile's metadata of one super-block: 2048 B
+constexpr int MSTAGES = 2;
+constexpr int NEPI = 16;
+constexpr int NTHREADS = (2 + NEPI) * 32;
 constexpr int OFF_A = 0;
 constexpr int OFF_B = OFF_A + STAGES * TILE;
-constexpr int OFF_AMIN = OFF_B + STAGES * TILE;
-constexpr int OFF_BMIN = OFF_AMIN + 2 * TILE;
-constexpr int OFF_W = OFF_BMIN + 2 * TILE;
-constexpr int OFF_BAR = OFF_W + WSTAGES * WTILE;
-constexpr int NBAR = 3 * STAGES + 9 + 2 * WSTAGES;
+constexpr int OFF_META = OFF_B + STAGES * TILE;
+// per epilogue thread, two slots of its row's d_a and 16-wide sums of one super-block,
+// copied one super-block ahead with cp.async
+constexpr int OFF_ROWBS = OFF_META + MSTAGES * META;          // [2][NEPI * 32][32 B]
+constexpr int OFF_ROWD = OFF_ROWBS + 2 * NEPI * 32 * 32;      // [2][NEPI * 32] f32
+constexpr int OFF_BAR = OFF_ROWD + 2 * NEPI * 32 * 4;
+constexpr int NBAR = 2 * STAGES + 2 * MSTAGES + 4 + 1;
 constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+static_assert(META % 16 == 0, "bulk copies move multiples of 16 bytes");
 }  // namespace q4k
 
-static __device__ __forceinline__ int q4k_byte(const int4 &h, int i) {
-    const int w = i < 4 ? h.y : (i < 8 ? h.z : h.w);
-    return (w >> (8 * (i & 3))) & 0xFF;
-}
-static __device__ __forceinline__ void q4k_scale_min(const int4 &h, int j, int &sc, int &m) {
+static __device__ __forceinline__ int q4k_byte(const uint8_t *h, int i) { return h[4 + i]; }
+static __device__ __forceinline__ void q4k_scale_min(const uint8_t *h, int j, int &sc, int &m) {
     if (j < 4) {
         sc = q4k_byte(h, j) & 63;
         m = q4k_byte(h, j + 4) & 63;
@@ -67,42 +75,34 @@ static __device__ __forceinline__ void q4k_scale_min(const int4 &h, int j, int &
     }
 }
 
-// two nibble-sized values -> fp16 pair: v | 0x6400 is the half 1024 + v (v < 1024), minus 1024
-static __device__ __forceinline__ uint32_t u16x2_to_h2(uint32_t v2) {
-    const uint32_t x = v2 | 0x64006400u;
-    const __half2 r = __hsub2(*reinterpret_cast<const __half2 *>(&x), __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400)));
-    return *reinterpret_cast<const uint32_t *>(&r);
+static __device__ __forceinline__ void cp_async16(void *smem_dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");
 }
-
-// 8 consecutive K elements sc*nibble from 8 qs bytes (words w0, w1), low (sh=0) or high (sh=4) nibbles
-static __device__ __forceinline__ int4 q4k_chunk_f16(uint32_t w0, uint32_t w1, int sh, uint32_t sc) {
-    const uint32_t n0 = (w0 >> sh) & 0x0F0F0F0Fu, n1 = (w1 >> sh) & 0x0F0F0F0Fu;
-    int4 r;
-    r.x = (int)u16x2_to_h2(__byte_perm(n0, 0, 0x4140) * sc);
-    r.y = (int)u16x2_to_h2(__byte_perm(n0, 0, 0x4342) * sc);
-    r.z = (int)u16x2_to_h2(__byte_perm(n1, 0, 0x4140) * sc);
-    r.w = (int)u16x2_to_h2(__byte_perm(n1, 0, 0x4342) * sc);
-    return r;
+static __device__ __forceinline__ void cp_async4(void *smem_dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");
 }
+static __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+static __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+static __device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-__global__ void __launch_bounds__(448, 1)
+static __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+
+__global__ void __launch_bounds__(q4k::NTHREADS, 1)
     mmq_q4k_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
-                      int N, const __half *__restrict__ bs16h, const float *__restrict__ ad, int M, int K,
-                      float *__restrict__ y, int64_t y_ld, int *err) {
+                      const float *__restrict__ meta, int64_t meta_sb_stride, const __half *__restrict__ bs16h,
+                      const float *__restrict__ ad, int M, int K, int N, float *__restrict__ y, int64_t y_ld,
+                      int *err) {
     using namespace q4k;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = (uint64_t *)(smem + OFF_BAR);
-    uint64_t *full_a = bars;
-    uint64_t *full_b = bars + STAGES;
-    uint64_t *empty = bars + 2 * STAGES;
-    uint64_t *full_min = bars + 3 * STAGES;
-    uint64_t *empty_min = full_min + 2;
-    uint64_t *tmem_full = empty_min + 2;
+    uint64_t *full = bars;
+    uint64_t *empty = bars + STAGES;
+    uint64_t *meta_full = bars + 2 * STAGES;
+    uint64_t *meta_empty = meta_full + MSTAGES;
+    uint64_t *tmem_full = meta_empty + MSTAGES;
     uint64_t *tmem_empty = tmem_full + 2;
     uint64_t *done = tmem_empty + 2;
-    uint64_t *full_w = done + 1;
-    uint64_t *empty_w = full_w + WSTAGES;
     uint32_t *tmem_slot = (uint32_t *)(smem + OFF_MISC);
     volatile int *abort_flag = (volatile int *)(smem + OFF_MISC + 4);
 
@@ -112,19 +112,16 @@ __global__ void __launch_bounds__(448, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) {
-            mbar_init(&full_a[i], 1);
-            mbar_init(&full_b[i], 128);
+            mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&full_min[i], 128);
-            mbar_init(&empty_min[i], 1);
-            mbar_init(&tmem_full[i], 1);
-            mbar_init(&tmem_empty[i], 256);
+        for (int i = 0; i < MSTAGES; ++i) {
+            mbar_init(&meta_full[i], 1);
+            mbar_init(&meta_empty[i], NEPI);
         }
-        for (int i = 0; i < WSTAGES; ++i) {
-            mbar_init(&full_w[i], 1);
-            mbar_init(&empty_w[i], 128 + 256);  // transform + epilogue release a raw super-block
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tmem_full[i], 1);
+            mbar_init(&tmem_empty[i], NEPI);
         }
         mbar_init(done, 1);
         *abort_flag = 0;
@@ -138,32 +135,34 @@ __global__ void __launch_bounds__(448, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            // TMA producer: raw weight super-blocks (ring of WSTAGES) and activation tiles (ring of STAGES)
-            int issued_a = 0, issued_w = 0;
+            // TMA producer: operand tiles (ring of STAGES) and super-block metadata (ring of MSTAGES)
+            int issued = 0, issued_meta = 0;
             for (int kc = 0; kc < nkc; ++kc) {
                 const int sb = kc >> 2;
                 if ((kc & 3) == 0) {
-                    const int wb = sb % WSTAGES;
-                    if (!mbar_wait(&empty_w[wb], ((sb / WSTAGES) & 1) ^ 1, abort_flag, err)) break;
-                    mbar_arrive_expect_tx(&full_w[wb], WTILE);
-                    tma_load_2d(smem + OFF_W + wb * WTILE, &tmap_w, &full_w[wb], sb * 144, n0);
-                    issued_w = sb + 1;
+                    const int mb = sb % MSTAGES;
+                    if (!mbar_wait(&meta_empty[mb], ((sb / MSTAGES) & 1) ^ 1, abort_flag, err)) break;
+                    mbar_arrive_expect_tx(&meta_full[mb], META);
+                    bulk_load(smem + OFF_META + mb * META, meta + sb * meta_sb_stride + (int64_t)n0 * META_COL,
+                              META, &meta_full[mb]);
+                    issued_meta = sb + 1;
                 }
                 const int s = kc % STAGES;
                 if (!mbar_wait(&empty[s], ((kc / STAGES) & 1) ^ 1, abort_flag, err)) break;
-                mbar_arrive_expect_tx(&full_a[s], TILE);
-                tma_load_2d(smem + OFF_A + s * TILE, &tmap_a, &full_a[s], kc * BK, m0);
-                issued_a = kc + 1;
+                mbar_arrive_expect_tx(&full[s], 2 * TILE);
+                tma_load_2d(smem + OFF_A + s * TILE, &tmap_a, &full[s], kc * BK, m0);
+                tma_load_2d(smem + OFF_B + s * TILE, &tmap_w, &full[s], kc * BK, n0);
+                issued = kc + 1;
             }
             // no TMA write may still be in flight when the CTA exits
-            for (int kc = max(0, issued_a - STAGES); kc < issued_a; ++kc) {
+            for (int kc = max(0, issued - STAGES); kc < issued; ++kc) {
                 const long long t0 = clock64();
-                while (!mbar_try_wait(&full_a[kc % STAGES], (kc / STAGES) & 1) && clock64() - t0 < (1LL << 31)) {
+                while (!mbar_try_wait(&full[kc % STAGES], (kc / STAGES) & 1) && clock64() - t0 < (1LL << 31)) {
                 }
             }
-            for (int sb = max(0, issued_w - WSTAGES); sb < issued_w; ++sb) {
+            for (int sb = max(0, issued_meta - MSTAGES); sb < issued_meta; ++sb) {
                 const long long t0 = clock64();
-                while (!mbar_try_wait(&full_w[sb % WSTAGES], (sb / WSTAGES) & 1) && clock64() - t0 < (1LL << 31)) {
+                while (!mbar_try_wait(&meta_full[sb % MSTAGES], (sb / MSTAGES) & 1) && clock64() - t0 < (1LL << 31)) {
                 }
             }
         }
@@ -173,32 +172,25 @@ __global__ void __launch_bounds__(448, 1)
             bool ok = true;
             for (int sb = 0; sb < nsb && ok; ++sb) {
                 const int ab = sb & 1;
-                const uint32_t aph = (sb >> 1) & 1;
-                if (!mbar_wait(&tmem_empty[ab], aph ^ 1, abort_flag, err)) break;
+                if (!mbar_wait(&tmem_empty[ab], ((sb >> 1) & 1) ^ 1, abort_flag, err)) break;
                 tc_fence_after();
-                const uint32_t d_isum = tmem + ab * 256, d_msum = tmem + ab * 256 + 128;
                 for (int c = 0; c < 4 && ok; ++c) {
                     const int kc = sb * 4 + c, s = kc % STAGES;
-                    const uint32_t ph = (kc / STAGES) & 1;
-                    if (!mbar_wait(&full_a[s], ph, abort_flag, err) || !mbar_wait(&full_b[s], ph, abort_flag, err)) {
+                    if (!mbar_wait(&full[s], (kc / STAGES) & 1, abort_flag, err)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint64_t da = sw128_desc(smem_u32(smem + OFF_A + s * TILE));
                     const uint64_t db = sw128_desc(smem_u32(smem + OFF_B + s * TILE));
+                    // chunks 0-1 (K 0..127 of the super-block) -> low half, 2-3 -> high half
+                    const uint32_t d_acc = tmem + ab * 256 + (c >> 1) * 128;
 #pragma unroll
                     for (int k = 0; k < 4; ++k)  // 4 x K=16 (32 bytes) inside the 128-byte swizzle row
-                        umma_f16(d_isum, da + 2 * k, db + 2 * k, idesc, (c | k) != 0);
+                        umma_f16(d_acc, da + 2 * k, db + 2 * k, idesc, (c & 1) | k);
                     umma_commit(&empty[s]);
                 }
                 if (!ok) break;
-                const int mb = sb & 1;
-                if (!mbar_wait(&full_min[mb], (sb >> 1) & 1, abort_flag, err)) break;
-                tc_fence_after();
-                umma_f16(d_msum, sw128_desc(smem_u32(smem + OFF_AMIN + mb * TILE)),
-                         sw128_desc(smem_u32(smem + OFF_BMIN + mb * TILE)), idesc, 0);
-                umma_commit(&empty_min[mb]);
                 umma_commit(&tmem_full[ab]);
             }
             // every MMA issued above completes before TMEM is released
@@ -207,117 +199,108 @@ __global__ void __launch_bounds__(448, 1)
             while (!mbar_try_wait(done, 0) && clock64() - t0 < (1LL << 31)) {
             }
         }
-    } else if (warp < 6) {
-        // ---- weight transform: one weight row (and one activation min row) per thread ----
-        const int t = threadIdx.x - 64;
-        const int m = m0 + t;
-        const bool mv = m < M;
-        // activation 16-wide sums of the next super-block, one super-block ahead
-        int4 nb0 = make_int4(0, 0, 0, 0), nb1 = nb0;
-        if (mv) {
-            const __half *ap = bs16h + (int64_t)m * (K / 16);
-            nb0 = *reinterpret_cast<const int4 *>(ap);
-            nb1 = *reinterpret_cast<const int4 *>(ap + 8);
-        }
-        for (int kc = 0; kc < nkc; ++kc) {
-            const int s = kc % STAGES, sb = kc >> 2, c = kc & 3, wb = sb % WSTAGES;
-            if (c == 0 && !mbar_wait(&full_w[wb], (sb / WSTAGES) & 1, abort_flag, err)) break;
-            if (!mbar_wait(&empty[s], ((kc / STAGES) & 1) ^ 1, abort_flag, err)) break;
-            const uint8_t *wrow = smem + OFF_W + wb * WTILE + t * 144;  // rows past N are zero-filled by TMA
-            const int4 hdr = *reinterpret_cast<const int4 *>(wrow);
-            const int4 q0 = *reinterpret_cast<const int4 *>(wrow + 16 + 32 * c);
-            const int4 q1 = *reinterpret_cast<const int4 *>(wrow + 32 + 32 * c);
-            int sc0, mn0, sc1, mn1;
-            q4k_scale_min(hdr, 2 * c, sc0, mn0);
-            q4k_scale_min(hdr, 2 * c + 1, sc1, mn1);
-            uint8_t *bt = smem + OFF_B + s * TILE;
-            // chunk j = K elements 8j..8j+7 of this 64-wide slice: j < 4 low nibbles of
-            // qs bytes 8j..8j+7 (sub-block 2c), j >= 4 high nibbles (sub-block 2c+1)
-            *reinterpret_cast<int4 *>(bt + sw128_off(t, 0)) = q4k_chunk_f16(q0.x, q0.y, 0, sc0);
-            *reinterpret_cast<int4 *>(bt + sw128_off(t, 1)) = q4k_chunk_f16(q0.z, q0.w, 0, sc0);
-            *reinterpret_cast<int4 *>(bt + sw128_off(t, 2)) = q4k_chunk_f16(q1.x, q1.y, 0, sc0);
-            *reinterpret_cast<int4 *>(bt + sw128_off(t, 3)) = q4k_chunk_f16(q1.z, q1.w, 0, sc0);
-            *reinterpret_cast<int4 *>(bt + sw128_off(t, 4)) = q4k_chunk_f16(q0.x, q0.y, 4, sc1);
-            *reinterpret_cast<int4 *>(bt + sw128_off(t, 5)) = q4k_chunk_f16(q0.z, q0.w, 4, sc1);
-            *reinterpret_cast<int4 *>(bt + sw128_off(t, 6)) = q4k_chunk_f16(q1.x, q1.y, 4, sc1);
-            *reinterpret_cast<int4 *>(bt + sw128_off(t, 7)) = q4k_chunk_f16(q1.z, q1.w, 4, sc1);
-            if (c == 0) {
-                const int mb = sb & 1;
-                if (!mbar_wait(&empty_min[mb], ((sb >> 1) & 1) ^ 1, abort_flag, err)) break;
-                int mn[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    int scj;
-                    q4k_scale_min(hdr, j, scj, mn[j]);
-                }
-                __half2 hb[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) hb[j] = __halves2half2(__int2half_rn(mn[j]), __int2half_rn(mn[j]));
-                uint8_t *bm = smem + OFF_BMIN + mb * TILE;
-                *reinterpret_cast<int4 *>(bm + sw128_off(t, 0)) = *reinterpret_cast<int4 *>(&hb[0]);
-                *reinterpret_cast<int4 *>(bm + sw128_off(t, 1)) = *reinterpret_cast<int4 *>(&hb[4]);
-                uint8_t *am = smem + OFF_AMIN + mb * TILE;
-                *reinterpret_cast<int4 *>(am + sw128_off(t, 0)) = nb0;
-                *reinterpret_cast<int4 *>(am + sw128_off(t, 1)) = nb1;
-                if (mv && sb + 1 < nsb) {
-                    const __half *ap = bs16h + (int64_t)m * (K / 16) + (sb + 1) * 16;
-                    nb0 = *reinterpret_cast<const int4 *>(ap);
-                    nb1 = *reinterpret_cast<const int4 *>(ap + 8);
-                }
-                fence_proxy_async_smem();
-                mbar_arrive(&full_min[mb]);
-            }
-            fence_proxy_async_smem();
-            mbar_arrive(&full_b[s]);
-            if (c == 3) mbar_arrive(&empty_w[wb]);
-        }
     } else {
-        // ---- epilogue ----
-        const int e = warp - 6, q = warp & 3, hcol = e >> 2;
+        // ---- epilogue: one activation row per thread, 32 weight columns per warp ----
+        // (18 warps share the SM's four 16K-register sub-partitions, 5 warps on two of
+        // them: 96 registers per thread, so TMEM is read 8 columns at a time)
+        const int e = warp - 2, q = warp & 3, cg = e >> 2;
         const int row = m0 + 32 * q + lane;
         const bool rv = row < M;
-        float acc[64];
+        float2 acc[16];
 #pragma unroll
-        for (int i = 0; i < 64; ++i) acc[i] = 0.0f;
-        float da_next = rv ? __ldg(ad + (int64_t)row * nsb) : 0.0f;
+        for (int i = 0; i < 16; ++i) acc[i] = f2(0.0f, 0.0f);
+        uint8_t *rbs = smem + OFF_ROWBS + (e * 32 + lane) * 32;  // slot stride NEPI * 32 * 32
+        float *rd = reinterpret_cast<float *>(smem + OFF_ROWD) + e * 32 + lane;  // slot stride NEPI * 32
+        auto fetch_row = [&](int sb) {  // this row's d_a and 16-wide sums of super-block sb
+            if (rv) {
+                const int sl = sb & 1;
+                const __half *bp = bs16h + (int64_t)row * (K / 16) + sb * 16;
+                cp_async16(rbs + sl * NEPI * 32 * 32, bp);
+                cp_async16(rbs + sl * NEPI * 32 * 32 + 16, bp + 8);
+                cp_async4(rd + sl * NEPI * 32, ad + (int64_t)row * nsb + sb);
+            }
+            cp_async_commit();
+        };
+        fetch_row(0);
         for (int sb = 0; sb < nsb; ++sb) {
-            const int ab = sb & 1, wb = sb % WSTAGES;
-            const float da = da_next;
-            if (rv && sb + 1 < nsb) da_next = __ldg(ad + (int64_t)row * nsb + sb + 1);
-            if (!mbar_wait(&tmem_full[ab], (sb >> 1) & 1, abort_flag, err)) break;
-            // the raw super-block stays in its slot until this epilogue releases it, so its
-            // phase is still the one to observe (makes the TMA bytes visible to these threads)
-            if (!mbar_wait(&full_w[wb], (sb / WSTAGES) & 1, abort_flag, err)) break;
-            tc_fence_after();
-            const uint8_t *wsc = smem + OFF_W + wb * WTILE + 64 * hcol * 144;  // d, dmin of each weight row
-            const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(ab * 256 + 64 * hcol);
+            const int ab = sb & 1, mb = sb % MSTAGES;
+            if (sb + 1 < nsb) fetch_row(sb + 1);
+            else cp_async_commit();
+            cp_async_wait1();  // super-block sb's row data has landed
+            const float da = rd[(sb & 1) * NEPI * 32];
+            // the row's sums of the 32 quants of each sub-block (exact integers, |.| <= 4064)
+            // as b = 64 * bh + bl with bl in [0, 63] and bh in [-64, 63], 4 per word
+            uint32_t bl0 = 0, bl1 = 0, bh0 = 0, bh1 = 0;
+            {
+                const __half2 *hb = reinterpret_cast<const __half2 *>(rbs + (sb & 1) * NEPI * 32 * 32);
 #pragma unroll
-            for (int cb = 0; cb < 4; ++cb) {
-                uint32_t ri[16], rm[16];
-                tmem_ld16(tb + 16 * cb, ri);
-                tmem_ld16(tb + 128 + 16 * cb, rm);
-                tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const uint32_t dd = *reinterpret_cast<const uint32_t *>(wsc + (16 * cb + i) * 144);
-                    const float d = __fmul_rn(h2f((uint16_t)(dd & 0xFFFF)), da);
-                    const float dm = __fmul_rn(h2f((uint16_t)(dd >> 16)), da);
-                    acc[16 * cb + i] += __fsub_rn(__fmul_rn(d, __uint_as_float(ri[i])), __fmul_rn(dm, __uint_as_float(rm[i])));
+                for (int j = 0; j < 8; ++j) {
+                    const float2 v = __half22float2(hb[j]);
+                    const int b = __float_as_int(__fadd_rn(__fadd_rn(v.x, v.y), 12582912.0f)) - 0x4B400000;
+                    const uint32_t lo6 = (uint32_t)(b & 63), hi8 = (uint32_t)(b >> 6) & 0xFFu;
+                    if (j < 4) {
+                        bl0 |= lo6 << (8 * j);
+                        bh0 |= hi8 << (8 * j);
+                    } else {
+                        bl1 |= lo6 << (8 * (j - 4));
+                        bh1 |= hi8 << (8 * (j - 4));
+                    }
                 }
             }
-            tc_fence_before();
-            mbar_arrive(&tmem_empty[ab]);
-            mbar_arrive(&empty_w[wb]);
-        }
-        if (rv) {
-            float *yr = y + (int64_t)row * y_ld + n0 + 64 * hcol;
-            if (n0 + 64 * hcol + 64 <= N && (((uintptr_t)yr) & 15) == 0) {
+            if (!mbar_wait(&tmem_full[ab], (sb >> 1) & 1, abort_flag, err)) break;
+            if (!mbar_wait(&meta_full[mb], (sb / MSTAGES) & 1, abort_flag, err)) break;
+            tc_fence_after();
+            const uint4 *mt = reinterpret_cast<const uint4 *>(smem + OFF_META + mb * META) + 32 * cg;
+            const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(ab * 256 + 32 * cg);
+            // TMEM is read 8 columns at a time, one group ahead: the loads of group h + 1
+            // are in flight while group h is computed (tcgen05.wait::ld waits for all)
+            uint32_t lo[2][8], hi[2][8];
+            tmem_ld8(tb, lo[0]);
+            tmem_ld8(tb + 128, hi[0]);
+            tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 64; i += 4) *reinterpret_cast<float4 *>(yr + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+            for (int h = 0; h < 4; ++h) {
+                if (h + 1 < 4) {
+                    tmem_ld8(tb + 8 * (h + 1), lo[(h + 1) & 1]);
+                    tmem_ld8(tb + 128 + 8 * (h + 1), hi[(h + 1) & 1]);
+                }
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const uint4 mw = mt[8 * h + c];  // d, dmin, mins 0-3, mins 4-7 of this column
+                    // (float)isum: the f32 sum of the two exact halves rounds the exact sum once
+                    const float isum = __fadd_rn(__uint_as_float(lo[h & 1][c]), __uint_as_float(hi[h & 1][c]));
+                    // msum + the bits of 1.5 * 2^23, then as a float minus 1.5 * 2^23: exact
+                    const int ml = __dp4a((int)mw.w, (int)bl1, __dp4a((int)mw.z, (int)bl0, 0x4B400000));
+                    const int mh = __dp4a((int)mw.w, (int)bh1, __dp4a((int)mw.z, (int)bh0, 0));
+                    const float ms = __fsub_rn(__int_as_float(ml + 64 * mh), 12582912.0f);
+                    // ggml's term with its roundings; the scalar _rn intrinsics are never
+                    // contracted into a fused multiply-add
+                    const float d = __fmul_rn(__uint_as_float(mw.x), da), dm = __fmul_rn(__uint_as_float(mw.y), da);
+                    float &a = c & 1 ? acc[4 * h + (c >> 1)].y : acc[4 * h + (c >> 1)].x;
+                    a = __fadd_rn(a, __fsub_rn(__fmul_rn(d, isum), __fmul_rn(dm, ms)));
+                }
+                if (h + 1 < 4) tmem_ld_wait();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&tmem_empty[ab]);
+                mbar_arrive(&meta_empty[mb]);
+            }
+        }
+        cp_async_wait0();  // no row copy in flight past this point (also after an abort)
+        if (rv) {
+            float *yr = y + (int64_t)row * y_ld + n0 + 32 * cg;
+            if (n0 + 32 * cg + 32 <= N && (((uintptr_t)yr) & 15) == 0) {
+#pragma unroll
+                for (int i = 0; i < 16; i += 2)
+                    *reinterpret_cast<float4 *>(yr + 2 * i) = make_float4(acc[i].x, acc[i].y, acc[i + 1].x, acc[i + 1].y);
             } else {
 #pragma unroll
-                for (int i = 0; i < 64; ++i)
-                    if (n0 + 64 * hcol + i < N) yr[i] = acc[i];
+                for (int i = 0; i < 16; ++i) {
+                    if (n0 + 32 * cg + 2 * i < N) yr[2 * i] = acc[i].x;
+                    if (n0 + 32 * cg + 2 * i + 1 < N) yr[2 * i + 1] = acc[i].y;
+                }
             }
         }
     }
@@ -327,6 +310,60 @@ __global__ void __launch_bounds__(448, 1)
         tc_fence_after();
         tmem_dealloc(tmem, 512);
     }
+}
+
+// ---- Q4_K operand build (upload) ----------------------------------------------------------------
+// raw Q4_K rows [slices][N][K/256 x 144 B] ->
+//   h16  [slices][N][K] fp16: sc_j * q (element order of ggml's dequantize_row_q4_K:
+//        64-element chunk c holds the low nibbles of qs[32c..32c+31] (sub-block 2c)
+//        then their high nibbles (sub-block 2c+1))
+//   meta [slices][K/256][Np][4] words per weight row: d, dmin (f32), mins m_0..m_3 and
+//        m_4..m_7 (one byte each); rows >= N zero; Np = N rounded up to 128
+// One thread per (row, super-block).
+__global__ void q4k_operand_kernel(const uint8_t *__restrict__ qs, int64_t row_bytes, int64_t N, int nsb, int64_t Np,
+                                   int64_t total, __half *__restrict__ h16, float *__restrict__ meta) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / nsb;  // row over all slices
+        const int sb = (int)(i - r * nsb);
+        const int64_t sl = r / N, n = r - sl * N;
+        const uint8_t *blk = qs + r * row_bytes + (int64_t)sb * 144;
+        int sc[8], mn[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q4k_scale_min(blk, j, sc[j], mn[j]);
+        __half *dst = h16 + r * ((int64_t)nsb * 256) + (int64_t)sb * 256;
+        for (int c = 0; c < 4; ++c)
+            for (int l = 0; l < 32; ++l) {
+                const int v = blk[16 + 32 * c + l];
+                dst[64 * c + l] = __int2half_rn(sc[2 * c] * (v & 0xF));
+                dst[64 * c + 32 + l] = __int2half_rn(sc[2 * c + 1] * (v >> 4));
+            }
+        float *mp = meta + ((sl * nsb + sb) * Np + n) * 4;
+        mp[0] = h2f((uint16_t)(blk[0] | (blk[1] << 8)));
+        mp[1] = h2f((uint16_t)(blk[2] | (blk[3] << 8)));
+        uint32_t *mw = reinterpret_cast<uint32_t *>(mp);
+        mw[2] = (uint32_t)mn[0] | ((uint32_t)mn[1] << 8) | ((uint32_t)mn[2] << 16) | ((uint32_t)mn[3] << 24);
+        mw[3] = (uint32_t)mn[4] | ((uint32_t)mn[5] << 8) | ((uint32_t)mn[6] << 16) | ((uint32_t)mn[7] << 24);
+    }
+}
+
+bool mmq_q4k_tc_supported(int type, int64_t K) { return type == OASR_TYPE_Q4_K && K % 256 == 0; }
+
+size_t q4k_operand_bytes(int64_t N, int64_t K, int64_t slices, size_t *meta_bytes) {
+    const int64_t Np = (N + 127) / 128 * 128;
+    *meta_bytes = (size_t)(slices * (K / 256) * Np * 4) * sizeof(float);
+    return (size_t)(slices * N * K) * 2;
+}
+
+cudaError_t build_q4k_operand(oasr_weight *w, cudaStream_t st) {
+    const int64_t N = w->ne[1], K = w->ne[0], slices = w->ne[2] * w->ne[3];
+    const int64_t Np = (N + 127) / 128 * 128, nsb = K / 256, total = slices * N * nsb;
+    size_t mb = 0;
+    q4k_operand_bytes(N, K, slices, &mb);
+    cudaError_t e = cudaMemsetAsync(w->k_meta, 0, mb, st);  // pad rows: zero metadata
+    if (e != cudaSuccess) return e;
+    const unsigned grid = (unsigned)std::min<int64_t>((total + 255) / 256, 65535);
+    q4k_operand_kernel<<<grid, 256, 0, st>>>(w->qs, w->qs_row_bytes, N, (int)nsb, Np, total, w->h16, w->k_meta);
+    return cudaGetLastError();
 }
 
 // ---- Q8_0: tcgen05 kind::i8 -------------------------------------------------------------------
@@ -588,24 +625,26 @@ static int encode_2d(oasr_backend *be, CUtensorMap *map, CUtensorMapDataType dt,
 
 static int launch_q4k_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int64_t M, int K,
                          float *y, int64_t y_ld) {
-    const int64_t N = w->ne[1];
+    const int64_t N = w->ne[1], Np = (N + 127) / 128 * 128;
     CUtensorMap map_a, map_w;
     // activations: fp16 [M][K], 128 rows x 64 elements (128 B) per box, 128B swizzle
     int st = encode_2d(be, &map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.qs16, K, M, (uint64_t)K * 2, 64, 128,
                        CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
-    // raw Q4_K rows: bytes [N][K/256*144], 128 rows x one 144-byte super-block per box
-    st = encode_2d(be, &map_w, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->qs + slice * N * w->qs_row_bytes, w->qs_row_bytes, N,
-                   w->qs_row_bytes, 144, 128, CU_TENSOR_MAP_SWIZZLE_NONE);
+    // weights: the fp16 sc*q operand [N][K], same box
+    st = encode_2d(be, &map_w, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, w->h16 + slice * N * K, K, N, (uint64_t)K * 2, 64, 128,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
     static std::atomic<bool> attr_set{false};  // idempotent set-up; concurrent first calls set the same attribute
     if (!attr_set) {
         cudaFuncSetAttribute(mmq_q4k_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, q4k::SMEM_BYTES);
         attr_set = true;
     }
+    const int64_t meta_sb = Np * q4k::META_COL;
+    const float *meta = w->k_meta + slice * (K / 256) * meta_sb;
     dim3 grid((unsigned)((N + q4k::BN - 1) / q4k::BN), (unsigned)((M + q4k::BM - 1) / q4k::BM));
-    mmq_q4k_tc_kernel<<<grid, q4k::NTHREADS, q4k::SMEM_BYTES, be->stream>>>(map_a, map_w, (int)N, a.bs16h, a.d,
-                                                                            (int)M, K, y, y_ld, be->err_word);
+    mmq_q4k_tc_kernel<<<grid, q4k::NTHREADS, q4k::SMEM_BYTES, be->stream>>>(map_a, map_w, meta, meta_sb, a.bs16h, a.d,
+                                                                            (int)M, K, (int)N, y, y_ld, be->err_word);
     return oasr_internal_launch_check(be, "mmq_q4k_tc");
 }
 
@@ -642,7 +681,7 @@ static int launch_q80_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, 
 int launch_mmq(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int64_t M, int K,
                float *y, int64_t y_ld) {
     const bool k_family = w->type == OASR_TYPE_Q4_K;
-    if (k_family && a.qs16 && a.bs16h) return launch_q4k_tc(be, w, slice, a, M, K, y, y_ld);
+    if (k_family && w->h16 && a.qs16 && a.bs16h) return launch_q4k_tc(be, w, slice, a, M, K, y, y_ld);
     if (w->dT && (w->type == OASR_TYPE_Q8_0 || w->qs8) && (y_ld & 3) == 0)
         return launch_q80_tc(be, w, slice, a, M, K, y, y_ld);
     const int family = k_family ? FAMILY_Q8_K : FAMILY_Q8_0;

@@ -223,6 +223,40 @@ def test_q4k_tensor_core_gemm_is_bit_exact(gpu_backend, M, N, K):
     np.testing.assert_array_equal(got, ref)
 
 
+def _q4k_adversarial(N, K, seed):
+    """raw Q4_K rows whose every sub-scale and min is 63 and quants 12..15: sc * q
+    reaches 945 and a super-block's products all share one sign"""
+    rng = np.random.default_rng(seed)
+    nb = K // 256
+    w = np.zeros((N, nb, 144), np.uint8)
+    w[..., 0:2] = rng.uniform(1e-3, 2e-3, size=(N, nb)).astype(np.float16)[..., None].view(np.uint8)
+    w[..., 2:4] = rng.uniform(1e-3, 2e-3, size=(N, nb)).astype(np.float16)[..., None].view(np.uint8)
+    w[..., 4:16] = 0xFF
+    q = rng.integers(12, 16, size=(N, nb, 4, 2, 32))  # chunk c: low nibbles then high nibbles
+    w[..., 16:] = (q[..., 0, :] | (q[..., 1, :] << 4)).reshape(N, nb, 128).astype(np.uint8)
+    return w.reshape(N, nb * 144)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("sign", [1.0, -1.0])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 1280), (300, 200, 2048), (9, 128, 256)])
+def test_q4k_tensor_core_gemm_exact_beyond_2_24(gpu_backend, sign, M, N, K):
+    """Adversarial Q4_K case: sub-scales 63 x quants 12..15 against activations of
+    one sign near their block maximum (q8_K quants within a few steps of -+127), so
+    a super-block's integer dot reaches 256 x 945 x 127 > 2^24 and one f32
+    accumulation of its 256 products would round.  The GEMM accumulates each
+    super-block as two exact 128-element halves; the result equals the oracle's
+    integer arithmetic bit for bit."""
+    wq = _q4k_adversarial(N, K, 0x0A5A0C00 + M)
+    rng = np.random.default_rng(0x0A5A0C01 + N)
+    x = (sign * (1.0 + 0.05 * rng.random((M, K)))).astype(np.float32)
+    x[0, :256] = sign * 3.0  # a constant block: every quant -+127
+    got = _run(gpu_backend, wq, ob.Q4_K, N, K, x)
+    ref = oo.mul_mat(wq, ob.Q4_K, K, N, x)
+    assert np.abs(ref).max() > 0
+    np.testing.assert_array_equal(got, ref)
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("qt", [ob.Q8_0, ob.Q4_K])
 @pytest.mark.parametrize("N,K", [(17, 256), (100, 512), (51866, 1280), (40, 7680)])
