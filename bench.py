@@ -532,6 +532,39 @@ def _fa_roofline(be, torch, stream, n_layers_rot: int = 4, iters: int = 20) -> d
     return {"us": us, "bytes": nbytes}
 
 
+def whisper_step_bytes(cfg, B: int, n_prompt: int, n_new: int) -> dict:
+    """Algorithmic bytes of one Whisper decode step at batch B: every decoder weight once
+    (Q4_K decode tiles 144 B / 256 weights, the Q8_0 logits head 34 B / 32), the cross K/V
+    of every layer (f16, 1500 frames x (K | V)), the self K/V rows up to the mean cache
+    length of a batch's steps, the activations negligible."""
+    d, L, V, T = cfg.d_model, cfg.n_dec_layers, cfg.n_vocab, cfg.n_audio_ctx
+    per_layer = d * (3 * d + d + d + d + 4 * d) + 4 * d * d  # qkv, o, cross q, cross o, fc1, fc2
+    weights = L * per_layer * 144 // 256 + V * d * 34 // 32
+    cross = L * B * T * 2 * d * 2
+    steps = n_prompt - 1 + n_new
+    mean_kv = sum(p + 1 for p in range(steps)) / steps
+    self_kv = int(L * B * mean_kv * 2 * d * 2)
+    return {"weights": weights, "cross_kv": cross, "self_kv": self_kv, "total": weights + cross + self_kv}
+
+
+def _step_roofline(model, torch, stream, lens, B, n_new, toks_dev) -> dict:
+    """Per-step time of the Whisper decode graph: two generate calls from the same device
+    mel (encoder + prompt + n steps), n = n_new and n = 32, timed with CUDA events on the
+    bench stream; their difference over n_new - 32 steps is the step alone."""
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    ts = {}
+    for n in (n_new, 32):
+        model.generate_device(B, toks_dev, n_new=n)  # warm (graphs of this width exist)
+        e0, e1 = ev(), ev()
+        e0.record(stream)
+        for _ in range(3):
+            model.generate_device(B, toks_dev, n_new=n)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ts[n] = e0.elapsed_time(e1) / 3 * 1e3
+    return {"us": (ts[n_new] - ts[32]) / (n_new - 32), "batch_us": ts[n_new]}
+
+
 def run_b200(args) -> None:
     import torch
     import torch.distributed as dist
@@ -633,12 +666,21 @@ def run_b200(args) -> None:
         torch.cuda.synchronize()
         e2e_s = h0.elapsed_time(h1) / 1e3
         fa = _fa_roofline(be, torch, stream)
+        model.mel_device(pcm_dev[0], lens[0])
+        st = _step_roofline(model, torch, stream, lens[0], len(shard[0]), N_NEW, toks_dev)
     timed_audio = sum(audio_s[i % nb] for i in range(args.warmup, args.warmup + args.steps))
     dev_s, e2e_s, timed_audio = reduce_over_ranks(dev_s, e2e_s, timed_audio)
     job_times = gather_over_ranks(job_s)
     if rank == 0:
         peak, peak_kind = measured_peak_hbm()
         achieved = fa["bytes"] / (fa["us"] * 1e-6) / 1e9
+        sb = whisper_step_bytes(cfg, len(shard[0]), len(om.PROMPT[cfg.n_vocab]), N_NEW)
+        step_ach = sb["total"] / (st["us"] * 1e-6) / 1e9
+        step_line = {"bound": "hbm", "achieved": step_ach, "peak": peak, "unit": "GB/s", "frac": step_ach / peak,
+                     "step_us": st["us"], "algorithmic_bytes": sb,
+                     "how": "one decode step of the batch-8 graph (32 layers + logits head + argmax): rank 0's "
+                            "(generate 224 - generate 32) / 192 steps, CUDA events; bytes = every decoder weight "
+                            "once + all cross K/V + self K/V at the mean cache length"}
         job_audio = sum(lens_all) / 16000.0
         line = {
             "metric": RTFX_METRIC, "value": timed_audio / dev_s, "unit": "audio-s/s", "n_gpus": world,
@@ -675,7 +717,8 @@ def run_b200(args) -> None:
                          "peak_kind": peak_kind, "traffic": ncu_traffic_fa(), "algorithmic_bytes": fa["bytes"],
                          "avg_launch_us": fa["us"], "how": "same kernel and shapes timed alone on the bench stream "
                                                            "after the timed region from a CUDA graph of 20 launches, "
-                                                           "K/V rotated over 246 MB"},
+                                                           "K/V rotated over 246 MB",
+                         "step": step_line},
             "clocks": clocks,
         }
         if world == 1 and not args.no_job:
@@ -1067,6 +1110,13 @@ def run_b200_qwen(args) -> None:
     if rank == 0:
         peak, peak_kind = measured_peak_hbm()
         achieved = fa["bytes"] / (fa["us"] * 1e-6) / 1e9
+        sb = whisper_step_bytes(cfg, len(shard[0]), len(om.PROMPT[cfg.n_vocab]), N_NEW)
+        step_ach = sb["total"] / (st["us"] * 1e-6) / 1e9
+        step_line = {"bound": "hbm", "achieved": step_ach, "peak": peak, "unit": "GB/s", "frac": step_ach / peak,
+                     "step_us": st["us"], "algorithmic_bytes": sb,
+                     "how": "one decode step of the batch-8 graph (32 layers + logits head + argmax): rank 0's "
+                            "(generate 224 - generate 32) / 192 steps, CUDA events; bytes = every decoder weight "
+                            "once + all cross K/V + self K/V at the mean cache length"}
         tokens = B * NEW * args.steps * world
         line = {
             "metric": QWEN_METRIC.replace(f"greedy {QWEN_NEW}", f"greedy {NEW}"), "value": audio / dev_s,

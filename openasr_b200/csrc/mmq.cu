@@ -75,16 +75,6 @@ static __device__ __forceinline__ void q4k_scale_min(const uint8_t *h, int j, in
     }
 }
 
-static __device__ __forceinline__ void cp_async16(void *smem_dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");
-}
-static __device__ __forceinline__ void cp_async4(void *smem_dst, const void *src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");
-}
-static __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-static __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
-static __device__ __forceinline__ void cp_async_wait0() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-
 static __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 
 __global__ void __launch_bounds__(q4k::NTHREADS, 1)
