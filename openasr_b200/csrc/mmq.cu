@@ -56,7 +56,8 @@ constexpr int OFF_META = OFF_B + STAGES * TILE;
 // copied one super-block ahead with cp.async
 constexpr int OFF_ROWBS = OFF_META + MSTAGES * META;          // [2][NEPI * 32][32 B]
 constexpr int OFF_ROWD = OFF_ROWBS + 2 * NEPI * 32 * 32;      // [2][NEPI * 32] f32
-constexpr int OFF_BAR = OFF_ROWD + 2 * NEPI * 32 * 4;
+constexpr int OFF_REC = OFF_ROWD + 2 * NEPI * 32 * 4;         // [NEPI][32 rows][8 words] row records
+constexpr int OFF_BAR = OFF_REC + NEPI * 32 * 32;
 constexpr int NBAR = 2 * STAGES + 2 * MSTAGES + 4 + 1;
 constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
 constexpr int SMEM_BYTES = OFF_MISC + 16 + 1024;
@@ -75,7 +76,6 @@ static __device__ __forceinline__ void q4k_scale_min(const uint8_t *h, int j, in
     }
 }
 
-static __device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
 
 __global__ void __launch_bounds__(q4k::NTHREADS, 1)
     mmq_q4k_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
@@ -190,17 +190,24 @@ __global__ void __launch_bounds__(q4k::NTHREADS, 1)
             }
         }
     } else {
-        // ---- epilogue: one activation row per thread, 32 weight columns per warp ----
-        // (18 warps share the SM's four 16K-register sub-partitions, 5 warps on two of
-        // them: 96 registers per thread, so TMEM is read 8 columns at a time)
+        // ---- epilogue: warp w reads TMEM lane quarter w % 4 (32 rows), 32 weight columns ----
+        // TMEM is read in the 16x256b shape: a thread holds 2 rows x 2 columns of each 16-lane
+        // x 8-column block, so each column's metadata serves 4 of its outputs.  Lane l builds
+        // the record of row 32q + l (d_a and the sub-block sums) for the whole warp.
         const int e = warp - 2, q = warp & 3, cg = e >> 2;
         const int row = m0 + 32 * q + lane;
         const bool rv = row < M;
-        float2 acc[16];
+        const int r4 = lane >> 2, c2 = 2 * (lane & 3);
+        float acc[2][4][2][2];  // [16-row half][8-column group][row r4, r4 + 8][column c2, c2 + 1]
 #pragma unroll
-        for (int i = 0; i < 16; ++i) acc[i] = f2(0.0f, 0.0f);
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+#pragma unroll
+                for (int i = 0; i < 2; ++i) acc[h][k][i][0] = acc[h][k][i][1] = 0.0f;
         uint8_t *rbs = smem + OFF_ROWBS + (e * 32 + lane) * 32;  // slot stride NEPI * 32 * 32
         float *rd = reinterpret_cast<float *>(smem + OFF_ROWD) + e * 32 + lane;  // slot stride NEPI * 32
+        uint32_t *rec = reinterpret_cast<uint32_t *>(smem + OFF_REC) + e * 32 * 8;  // this warp's rows
         auto fetch_row = [&](int sb) {  // this row's d_a and 16-wide sums of super-block sb
             if (rv) {
                 const int sl = sb & 1;
@@ -217,11 +224,10 @@ __global__ void __launch_bounds__(q4k::NTHREADS, 1)
             if (sb + 1 < nsb) fetch_row(sb + 1);
             else cp_async_commit();
             cp_async_wait1();  // super-block sb's row data has landed
-            const float da = rd[(sb & 1) * NEPI * 32];
-            // the row's sums of the 32 quants of each sub-block (exact integers, |.| <= 4064)
-            // as b = 64 * bh + bl with bl in [0, 63] and bh in [-64, 63], 4 per word
-            uint32_t bl0 = 0, bl1 = 0, bh0 = 0, bh1 = 0;
             {
+                // the row's sums of the 32 quants of each sub-block (exact integers, |.| <= 4064)
+                // as b = 64 * bh + bl with bl in [0, 63] and bh in [-64, 63], 4 per word
+                uint32_t bl0 = 0, bl1 = 0, bh0 = 0, bh1 = 0;
                 const __half2 *hb = reinterpret_cast<const __half2 *>(rbs + (sb & 1) * NEPI * 32 * 32);
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
@@ -236,40 +242,50 @@ __global__ void __launch_bounds__(q4k::NTHREADS, 1)
                         bh1 |= hi8 << (8 * (j - 4));
                     }
                 }
+                *reinterpret_cast<uint4 *>(rec + lane * 8) = make_uint4(__float_as_uint(rd[(sb & 1) * NEPI * 32]), bl0, bl1, bh0);
+                rec[lane * 8 + 4] = bh1;
             }
+            __syncwarp();
             if (!mbar_wait(&tmem_full[ab], (sb >> 1) & 1, abort_flag, err)) break;
             if (!mbar_wait(&meta_full[mb], (sb / MSTAGES) & 1, abort_flag, err)) break;
             tc_fence_after();
             const uint4 *mt = reinterpret_cast<const uint4 *>(smem + OFF_META + mb * META) + 32 * cg;
             const uint32_t tb = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(ab * 256 + 32 * cg);
-            // TMEM is read 8 columns at a time, one group ahead: the loads of group h + 1
-            // are in flight while group h is computed (tcgen05.wait::ld waits for all)
-            uint32_t lo[2][8], hi[2][8];
-            tmem_ld8(tb, lo[0]);
-            tmem_ld8(tb + 128, hi[0]);
-            tmem_ld_wait();
 #pragma unroll
-            for (int h = 0; h < 4; ++h) {
-                if (h + 1 < 4) {
-                    tmem_ld8(tb + 8 * (h + 1), lo[(h + 1) & 1]);
-                    tmem_ld8(tb + 128 + 8 * (h + 1), hi[(h + 1) & 1]);
+            for (int h = 0; h < 2; ++h) {
+                // records of rows 16h + r4 and 16h + r4 + 8: d_a, bl0, bl1, bh0 | bh1
+                uint4 ra[2];
+                uint32_t rh[2];
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    ra[i] = *reinterpret_cast<const uint4 *>(rec + (16 * h + r4 + 8 * i) * 8);
+                    rh[i] = rec[(16 * h + r4 + 8 * i) * 8 + 4];
                 }
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const uint4 mw = mt[8 * h + c];  // d, dmin, mins 0-3, mins 4-7 of this column
-                    // (float)isum: the f32 sum of the two exact halves rounds the exact sum once
-                    const float isum = __fadd_rn(__uint_as_float(lo[h & 1][c]), __uint_as_float(hi[h & 1][c]));
-                    // msum + the bits of 1.5 * 2^23, then as a float minus 1.5 * 2^23: exact
-                    const int ml = __dp4a((int)mw.w, (int)bl1, __dp4a((int)mw.z, (int)bl0, 0x4B400000));
-                    const int mh = __dp4a((int)mw.w, (int)bh1, __dp4a((int)mw.z, (int)bh0, 0));
-                    const float ms = __fsub_rn(__int_as_float(ml + 64 * mh), 12582912.0f);
-                    // ggml's term with its roundings; the scalar _rn intrinsics are never
-                    // contracted into a fused multiply-add
-                    const float d = __fmul_rn(__uint_as_float(mw.x), da), dm = __fmul_rn(__uint_as_float(mw.y), da);
-                    float &a = c & 1 ? acc[4 * h + (c >> 1)].y : acc[4 * h + (c >> 1)].x;
-                    a = __fadd_rn(a, __fsub_rn(__fmul_rn(d, isum), __fmul_rn(dm, ms)));
+                for (int k = 0; k < 4; ++k) {
+                    uint32_t lo[4], hi[4];
+                    tmem_ld16x256(tb + ((uint32_t)(16 * h) << 16) + 8 * k, lo);
+                    tmem_ld16x256(tb + ((uint32_t)(16 * h) << 16) + 128 + 8 * k, hi);
+                    const uint4 mw[2] = {mt[8 * k + c2], mt[8 * k + c2 + 1]};  // d, dmin, mins 0-3, mins 4-7
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 2; ++i)
+#pragma unroll
+                        for (int j = 0; j < 2; ++j) {
+                            // (float)isum: the f32 sum of the two exact halves rounds the exact sum once
+                            const float isum = __fadd_rn(__uint_as_float(lo[2 * i + j]), __uint_as_float(hi[2 * i + j]));
+                            // msum + the bits of 1.5 * 2^23, then as a float minus 1.5 * 2^23: exact
+                            const int ml = __dp4a((int)mw[j].w, (int)ra[i].z, __dp4a((int)mw[j].z, (int)ra[i].y, 0x4B400000));
+                            const int mh = __dp4a((int)mw[j].w, (int)rh[i], __dp4a((int)mw[j].z, (int)ra[i].w, 0));
+                            const float ms = __fsub_rn(__int_as_float(ml + 64 * mh), 12582912.0f);
+                            // ggml's term with its roundings; the scalar _rn intrinsics are never
+                            // contracted into a fused multiply-add
+                            const float da = __uint_as_float(ra[i].x);
+                            const float d = __fmul_rn(__uint_as_float(mw[j].x), da);
+                            const float dm = __fmul_rn(__uint_as_float(mw[j].y), da);
+                            acc[h][k][i][j] = __fadd_rn(acc[h][k][i][j], __fsub_rn(__fmul_rn(d, isum), __fmul_rn(dm, ms)));
+                        }
                 }
-                if (h + 1 < 4) tmem_ld_wait();
             }
             tc_fence_before();
             __syncwarp();
@@ -279,20 +295,24 @@ __global__ void __launch_bounds__(q4k::NTHREADS, 1)
             }
         }
         cp_async_wait0();  // no row copy in flight past this point (also after an abort)
-        if (rv) {
-            float *yr = y + (int64_t)row * y_ld + n0 + 32 * cg;
-            if (n0 + 32 * cg + 32 <= N && (((uintptr_t)yr) & 15) == 0) {
 #pragma unroll
-                for (int i = 0; i < 16; i += 2)
-                    *reinterpret_cast<float4 *>(yr + 2 * i) = make_float4(acc[i].x, acc[i].y, acc[i + 1].x, acc[i + 1].y);
-            } else {
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    if (n0 + 32 * cg + 2 * i < N) yr[2 * i] = acc[i].x;
-                    if (n0 + 32 * cg + 2 * i + 1 < N) yr[2 * i + 1] = acc[i].y;
+            for (int i = 0; i < 2; ++i) {
+                const int rr = m0 + 32 * q + 16 * h + r4 + 8 * i;
+                if (rr >= M) continue;
+                float *yr = y + (int64_t)rr * y_ld + n0 + 32 * cg + c2;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int col = n0 + 32 * cg + 8 * k + c2;
+                    if (col + 1 < N && (((uintptr_t)(yr + 8 * k)) & 7) == 0) {
+                        *reinterpret_cast<float2 *>(yr + 8 * k) = make_float2(acc[h][k][i][0], acc[h][k][i][1]);
+                    } else {
+                        if (col < N) yr[8 * k] = acc[h][k][i][0];
+                        if (col + 1 < N) yr[8 * k + 1] = acc[h][k][i][1];
+                    }
                 }
             }
-        }
     }
     tc_fence_before();
     __syncthreads();

@@ -136,6 +136,14 @@ static __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]
                  : "r"(taddr)
                  : "memory");
 }
+// 16 lanes x 256 bits (8 columns): thread t gets (lane + t/4, column 2(t%4)), (lane + t/4,
+// column 2(t%4) + 1), (lane + t/4 + 8, column 2(t%4)), (lane + t/4 + 8, column 2(t%4) + 1)
+static __device__ __forceinline__ void tmem_ld16x256(uint32_t taddr, uint32_t (&r)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.16x256b.x1.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr)
+                 : "memory");
+}
 static __device__ __forceinline__ void tmem_ld_wait() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }

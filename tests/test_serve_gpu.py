@@ -104,3 +104,27 @@ def test_serve_rejects_bad_arguments(model, clips):
         model.serve(clips[:2], max_new=40, budgets=[0, 5])
     with pytest.raises(bk.GgmlBackendError):
         model.serve(clips[:2], max_new=448)
+
+
+@pytest.mark.gpu
+def test_serve_abort_between_steps_then_serve_again(gpu_backend, model, clips, serial):
+    """The backend's abort callback (ggml_abort_callback) is polled before each group of
+    serve steps: a predicate that turns true mid-serve ends the call with ABORTED, and
+    the next serve call starts from parked slots and is exact."""
+    from openasr_b200 import backend as bk
+
+    calls = {"n": 0}
+
+    def pred():
+        calls["n"] += 1
+        return calls["n"] >= 3  # the entry check and one group of steps pass
+
+    gpu_backend.set_abort_callback(pred)
+    try:
+        with pytest.raises(bk.Aborted):
+            model.serve(clips[:5], max_new=40, stop_at_eot=False, check_every=4)
+    finally:
+        gpu_backend.set_abort_callback(None)
+    assert calls["n"] >= 3
+    got, _ = model.serve(clips[:5], max_new=40, budgets=[7, 12, 3, 40, 9], stop_at_eot=False)
+    check(got, expected(serial[:5], [7, 12, 3, 40, 9]))
