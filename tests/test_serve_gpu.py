@@ -128,3 +128,21 @@ def test_serve_abort_between_steps_then_serve_again(gpu_backend, model, clips, s
     assert calls["n"] >= 3
     got, _ = model.serve(clips[:5], max_new=40, budgets=[7, 12, 3, 40, 9], stop_at_eot=False)
     check(got, expected(serial[:5], [7, 12, 3, 40, 9]))
+
+
+@pytest.mark.gpu
+def test_serve_large_v3_shape_equals_serial(gpu_backend):
+    """The serve loop on the large-v3 shape (20 heads: the 4-head decode attention and the
+    fused decoder GEMVs, Q4_K; 2 + 2 layers to keep it quick) at width 8 with refills and
+    a shrink: every request equals its serial transcription."""
+    cfg = om.WHISPER_LARGE_V3.replace(n_enc_layers=2, n_dec_layers=2, max_batch=8)
+    m = om.WhisperModel(gpu_backend, cfg, om.whisper_synthetic_pack(cfg, seed=0x0A5A0004))
+    try:
+        cs = [om.synthetic_audio(0x0A5A2100 + i, int(16000 * (5 + 2.5 * i))) for i in range(11)]
+        serial = [m.transcribe([c], n_new=24)[0] for c in cs]
+        budgets = [24, 3, 17, 9, 24, 1, 12, 20, 6, 14, 24]
+        got, st = m.serve(cs, max_new=24, budgets=budgets, stop_at_eot=False, check_every=4)
+        check(got, expected(serial, budgets))
+        assert st.max_width == 8 and st.admissions > 1
+    finally:
+        m.close()
