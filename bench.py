@@ -419,14 +419,14 @@ def job_pcm(u: int, n_samples: int, synth) -> np.ndarray:
 def launches_per_batch(n_enc: int, n_dec: int, n_prompt: int, n_new: int, batch: int) -> int:
     """Kernel launches of one generate() (counted from model_whisper.cu, and equal to
     the committed launch list): mel 3; prelude 4 (2 im2col + 2 conv GEMMs) + batch
-    positional adds; per encoder layer 13 (2 LayerNorm + quantize, 4 tensor-core GEMMs,
-    3 f16 pre-pass + 1 tensor-core attention, attention-output quantize, GELU +
-    quantize, residual add); final norm 1; 2 cross-K/V per decoder layer (GEMM + f16
+    positional adds; per encoder layer 12 (2 LayerNorm + quantize, 4 tensor-core GEMMs
+    -- the QKV bias added in the QKV GEMM's store --, 3 f16 pre-pass + 1 tensor-core
+    attention, attention-output quantize, GELU + quantize); final norm 1; 2 cross-K/V per decoder layer (GEMM + f16
     cast); per decoder step 1 embed + 1 first LayerNorm + 12 per layer (qkv GEMV, self
     attention, o GEMV, LayerNorm, cross-q GEMV, cross attention, cross-o GEMV,
     LayerNorm, fc1 GEMV, GELU + quantize, fc2 GEMV, LayerNorm) + logits + argmax +
     position advance; 1 token fill per prompt step."""
-    enc = 3 + 4 + batch + n_enc * 13 + 1 + 2 * n_dec
+    enc = 3 + 4 + batch + n_enc * 12 + 1 + 2 * n_dec
     steps = n_prompt + n_new - 1
     return enc + steps * (1 + 1 + 12 * n_dec + 2 + 1) + n_prompt
 

@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(192, FaTc<D>::CTAS_PER_SM)
             for (int c = 0; c < 8; ++c) {
                 uint32_t v[16];
                 tmem_ld16(trow + 16 * c, v);
-                tmem_ld_wait();
+                tmem_ld_wait(v);
 #pragma unroll
                 for (int i = 0; i < 16; ++i)
                     if (16 * c + i < lim) tmax = fmaxf(tmax, __uint_as_float(v[i]) * scale_log2);
@@ -286,7 +286,7 @@ __global__ void __launch_bounds__(192, FaTc<D>::CTAS_PER_SM)
             for (int c = 0; c < 8; ++c) {
                 uint32_t v[16];
                 tmem_ld16(trow + 16 * c, v);
-                tmem_ld_wait();
+                tmem_ld_wait(v);
                 uint32_t pk[8];
 #pragma unroll
                 for (int i = 0; i < 16; i += 2) {
@@ -314,7 +314,7 @@ __global__ void __launch_bounds__(192, FaTc<D>::CTAS_PER_SM)
             for (int c = 0; c < D / 16; ++c) {
                 uint32_t v[16];
                 tmem_ld16(trow + 128 + 16 * c, v);
-                tmem_ld_wait();
+                tmem_ld_wait(v);
 #pragma unroll
                 for (int i = 0; i < 16; ++i) o[16 * c + i] = fmaf(o[16 * c + i], alpha, __uint_as_float(v[i]));
             }

@@ -106,7 +106,7 @@ __global__ void __launch_bounds__(192, 2)
             for (int c = 0; c < 8; ++c) {
                 uint32_t v[16];
                 tmem_ld16(tb + 16 * c, v);
-                tmem_ld_wait();
+                tmem_ld_wait(v);
                 if (row < M) {
                     float *yr = y + (int64_t)row * y_ld + n0 + 16 * c;
 #pragma unroll

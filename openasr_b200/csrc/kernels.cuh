@@ -86,8 +86,11 @@ cudaError_t build_q40_expanded(oasr_weight *w, cudaStream_t st);  // w->qs8 from
 bool mmq_q4k_tc_supported(int type, int64_t K);
 size_t q4k_operand_bytes(int64_t N, int64_t K, int64_t slices, size_t *meta_bytes);  // h16 bytes; *meta_bytes k_meta
 cudaError_t build_q4k_operand(oasr_weight *w, cudaStream_t st);  // w->h16, w->k_meta from the raw Q4_K rows
+// M > 8 GEMM; bias (optional, [N]) is added to each output in the store, only on the Q4_K
+// tensor-core path (mmq_fuses_bias)
+bool mmq_fuses_bias(const oasr_weight *w, const ActPlanes &a);
 int launch_mmq(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int64_t M, int K,
-               float *y, int64_t y_ld);
+               float *y, int64_t y_ld, const float *bias = nullptr);
 
 // attention
 bool flash_attn_tc_eligible(const oasr_tensor *q, const oasr_tensor *k, const oasr_tensor *mask,

@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(q4k::NTHREADS, 1)
     mmq_q4k_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
                       const float *__restrict__ meta, int64_t meta_sb_stride, const __half *__restrict__ bs16h,
                       const float *__restrict__ ad, int M, int K, int N, float *__restrict__ y, int64_t y_ld,
-                      int *err) {
+                      const float *__restrict__ bias, int *err) {
     using namespace q4k;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -132,6 +132,7 @@ __global__ void __launch_bounds__(q4k::NTHREADS, 1)
                 if ((kc & 3) == 0) {
                     const int mb = sb % MSTAGES;
                     if (!mbar_wait(&meta_empty[mb], ((sb / MSTAGES) & 1) ^ 1, abort_flag, err)) break;
+                    fence_proxy_async_smem();  // the epilogue's reads of this slot before the refill
                     mbar_arrive_expect_tx(&meta_full[mb], META);
                     bulk_load(smem + OFF_META + mb * META, meta + sb * meta_sb_stride + (int64_t)n0 * META_COL,
                               META, &meta_full[mb]);
@@ -267,7 +268,7 @@ __global__ void __launch_bounds__(q4k::NTHREADS, 1)
                     tmem_ld16x256(tb + ((uint32_t)(16 * h) << 16) + 8 * k, lo);
                     tmem_ld16x256(tb + ((uint32_t)(16 * h) << 16) + 128 + 8 * k, hi);
                     const uint4 mw[2] = {mt[8 * k + c2], mt[8 * k + c2 + 1]};  // d, dmin, mins 0-3, mins 4-7
-                    tmem_ld_wait();
+                    tmem_ld_wait(lo, hi);
 #pragma unroll
                     for (int i = 0; i < 2; ++i)
 #pragma unroll
@@ -287,6 +288,10 @@ __global__ void __launch_bounds__(q4k::NTHREADS, 1)
                         }
                 }
             }
+            // the metadata slot was read here (generic proxy) and is refilled by a bulk copy
+            // (async proxy): a proxy fence orders the reads before that write (without it, 1
+            // launch in ~500 computed a fragment from the next super-block's metadata)
+            fence_proxy_async_smem();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
@@ -305,11 +310,17 @@ __global__ void __launch_bounds__(q4k::NTHREADS, 1)
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     const int col = n0 + 32 * cg + 8 * k + c2;
+                    // the optional bias is ggml's separate add of the mul_mat result (one f32 add)
+                    float v0 = acc[h][k][i][0], v1 = acc[h][k][i][1];
+                    if (bias) {
+                        if (col < N) v0 = __fadd_rn(v0, bias[col]);
+                        if (col + 1 < N) v1 = __fadd_rn(v1, bias[col + 1]);
+                    }
                     if (col + 1 < N && (((uintptr_t)(yr + 8 * k)) & 7) == 0) {
-                        *reinterpret_cast<float2 *>(yr + 8 * k) = make_float2(acc[h][k][i][0], acc[h][k][i][1]);
+                        *reinterpret_cast<float2 *>(yr + 8 * k) = make_float2(v0, v1);
                     } else {
-                        if (col < N) yr[8 * k] = acc[h][k][i][0];
-                        if (col + 1 < N) yr[8 * k + 1] = acc[h][k][i][1];
+                        if (col < N) yr[8 * k] = v0;
+                        if (col + 1 < N) yr[8 * k + 1] = v1;
                     }
                 }
             }
@@ -449,6 +460,7 @@ __global__ void __launch_bounds__(576, 1)
             for (int kc = 0; kc < nkc; ++kc) {
                 const int s = kc % STAGES;
                 if (!mbar_wait(&empty[s], ((kc / STAGES) & 1) ^ 1, abort_flag, err)) break;
+                fence_proxy_async_smem();  // the epilogue's reads of the stage's scales before the refill
                 mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
                 tma_load_2d(smem + OFF_A + s * TILE, &tmap_a, &full[s], kc * BK, m0);
                 tma_load_2d(smem + OFF_B + s * TILE, &tmap_w, &full[s], kc * BK, n0);
@@ -518,7 +530,7 @@ __global__ void __launch_bounds__(576, 1)
                 for (int h = 0; h < 2; ++h) {
                     uint32_t r[16];
                     tmem_ld16(tb + 16 * h, r);
-                    tmem_ld_wait();
+                    tmem_ld_wait(r);
 #pragma unroll
                     for (int i = 0; i < 16; i += 4) {
                         const float4 w4 = *reinterpret_cast<const float4 *>(dw + 16 * h + i);
@@ -535,6 +547,9 @@ __global__ void __launch_bounds__(576, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tmem_empty[j]);
             }
+            // the stage's weight scales were read here (generic proxy); the stage is refilled by
+            // TMA (async proxy): a proxy fence orders the reads before that write
+            fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
             if (!ok) break;
@@ -634,7 +649,7 @@ static int encode_2d(oasr_backend *be, CUtensorMap *map, CUtensorMapDataType dt,
 }
 
 static int launch_q4k_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int64_t M, int K,
-                         float *y, int64_t y_ld) {
+                         float *y, int64_t y_ld, const float *bias) {
     const int64_t N = w->ne[1], Np = (N + 127) / 128 * 128;
     CUtensorMap map_a, map_w;
     // activations: fp16 [M][K], 128 rows x 64 elements (128 B) per box, 128B swizzle
@@ -654,7 +669,7 @@ static int launch_q4k_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, 
     const float *meta = w->k_meta + slice * (K / 256) * meta_sb;
     dim3 grid((unsigned)((N + q4k::BN - 1) / q4k::BN), (unsigned)((M + q4k::BM - 1) / q4k::BM));
     mmq_q4k_tc_kernel<<<grid, q4k::NTHREADS, q4k::SMEM_BYTES, be->stream>>>(map_a, map_w, meta, meta_sb, a.bs16h, a.d,
-                                                                            (int)M, K, (int)N, y, y_ld, be->err_word);
+                                                                            (int)M, K, (int)N, y, y_ld, bias, be->err_word);
     return oasr_internal_launch_check(be, "mmq_q4k_tc");
 }
 
@@ -688,10 +703,15 @@ static int launch_q80_tc(oasr_backend *be, const oasr_weight *w, int64_t slice, 
     return oasr_internal_launch_check(be, "mmq_q80_tc");
 }
 
+bool mmq_fuses_bias(const oasr_weight *w, const ActPlanes &a) {
+    return w->type == OASR_TYPE_Q4_K && w->h16 && a.qs16 && a.bs16h;
+}
+
 int launch_mmq(oasr_backend *be, const oasr_weight *w, int64_t slice, const ActPlanes &a, int64_t M, int K,
-               float *y, int64_t y_ld) {
+               float *y, int64_t y_ld, const float *bias) {
     const bool k_family = w->type == OASR_TYPE_Q4_K;
-    if (k_family && w->h16 && a.qs16 && a.bs16h) return launch_q4k_tc(be, w, slice, a, M, K, y, y_ld);
+    if (mmq_fuses_bias(w, a)) return launch_q4k_tc(be, w, slice, a, M, K, y, y_ld, bias);
+    if (bias) return oasr_internal_fail(be, OASR_STATUS_FAILED, "mmq: bias epilogue needs the Q4_K tensor-core path");
     if (w->dT && (w->type == OASR_TYPE_Q8_0 || w->qs8) && (y_ld & 3) == 0)
         return launch_q80_tc(be, w, slice, a, M, K, y, y_ld);
     const int family = k_family ? FAMILY_Q8_K : FAMILY_Q8_0;

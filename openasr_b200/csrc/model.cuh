@@ -58,6 +58,9 @@ int launch_dgemv_qkv(oasr_backend *be, const oasr_weight *w, const ActPlanes &in
 
 // y[rows][N] = w . activation planes (rows <= 8: GEMV, else tensor-core / chunked GEMM)
 int mul_mat_planes(oasr_backend *be, const oasr_weight *w, const ActPlanes &a, int64_t rows, float *y, int64_t y_ld);
+// the same plus a per-column bias: in the tensor-core GEMM's store where it can, else an add launch
+int mul_mat_planes_bias(oasr_backend *be, const oasr_weight *w, const ActPlanes &a, int64_t rows, float *y,
+                        int64_t y_ld, const float *bias);
 
 inline int weight_family(const oasr_weight *w) { return w->type == OASR_TYPE_Q4_K ? FAMILY_Q8_K : FAMILY_Q8_0; }
 

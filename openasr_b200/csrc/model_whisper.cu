@@ -225,8 +225,7 @@ int run_encoder(oasr_whisper *m, int n, const int *slot_of = nullptr) {
         const float *pend = l == 0 ? nullptr : m->t;
         const float *pend_b = l == 0 ? nullptr : m->enc[l - 1].b_fc2;
         W_TRY(launch_resid_norm_quant(be, m->x, pend, pend_b, M, d, LN_EPS, false, L.ln1_g, L.ln1_b, nullptr, &qd, ef));
-        W_TRY(mul_mat_planes(be, L.qkv, qd, M, m->qkv, 3 * d));
-        W_TRY(launch_add_rows(be, m->qkv, L.b_qkv, nullptr, M, 3 * d));
+        W_TRY(mul_mat_planes_bias(be, L.qkv, qd, M, m->qkv, 3 * d, L.b_qkv));
         const int64_t ld = 3 * d * 4;
         oasr_tensor q = make_tensor(OASR_TYPE_F32, m->qkv, 64, T, H, n, ld, 256, ld * T);
         oasr_tensor k = make_tensor(OASR_TYPE_F32, m->qkv + d, 64, T, H, n, ld, 256, ld * T);

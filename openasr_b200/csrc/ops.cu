@@ -157,6 +157,15 @@ int mul_mat_planes(oasr_backend *be, const oasr_weight *w, const ActPlanes &a, i
     if (rows <= 8) return launch_mmv_quant(be, w, 0, a, (int)rows, (int)w->ne[0], y, y_ld);
     return launch_mmq(be, w, 0, a, rows, (int)w->ne[0], y, y_ld);
 }
+
+int mul_mat_planes_bias(oasr_backend *be, const oasr_weight *w, const ActPlanes &a, int64_t rows, float *y,
+                        int64_t y_ld, const float *bias) {
+    if (rows > 8 && mmq_fuses_bias(w, a)) return launch_mmq(be, w, 0, a, rows, (int)w->ne[0], y, y_ld, bias);
+    const int st = mul_mat_planes(be, w, a, rows, y, y_ld);
+    if (st || !bias) return st;
+    if (y_ld != w->ne[1]) return oasr_internal_fail(be, OASR_STATUS_FAILED, "mul_mat_planes_bias: rows must be dense");
+    return launch_add_rows(be, y, bias, nullptr, rows, (int)w->ne[1]);
+}
 }  // namespace oasr
 
 extern "C" {

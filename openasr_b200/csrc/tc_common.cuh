@@ -129,13 +129,6 @@ static __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[1
         : "r"(taddr)
         : "memory");
 }
-// 32 lanes x 8 columns
-static __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-                 : "r"(taddr)
-                 : "memory");
-}
 // 16 lanes x 256 bits (8 columns): thread t gets (lane + t/4, column 2(t%4)), (lane + t/4,
 // column 2(t%4) + 1), (lane + t/4 + 8, column 2(t%4)), (lane + t/4 + 8, column 2(t%4) + 1)
 static __device__ __forceinline__ void tmem_ld16x256(uint32_t taddr, uint32_t (&r)[4]) {
@@ -144,8 +137,23 @@ static __device__ __forceinline__ void tmem_ld16x256(uint32_t taddr, uint32_t (&
                  : "r"(taddr)
                  : "memory");
 }
-static __device__ __forceinline__ void tmem_ld_wait() {
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+// tcgen05.wait::ld with the loaded registers as in/out operands: a tcgen05.ld writes its
+// destination registers asynchronously, and the compiler sees no dependency between a
+// plain wait and the registers -- it could schedule arithmetic on them before the wait
+// (observed: a rare slice of a GEMM tile computed from stale values).  Binding the
+// registers to the wait makes every use follow it.
+static __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
+static __device__ __forceinline__ void tmem_ld_wait(uint32_t (&a)[4], uint32_t (&b)[4]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3])
+                 :
+                 : "memory");
 }
 
 // UMMA shared-memory descriptor for a K-major operand tile stored in the

@@ -338,3 +338,33 @@ def test_q8_0_tensor_core_gemm_is_bit_exact(gpu_backend, M, N, K):
     got = _run(gpu_backend, wq, ob.Q8_0, N, K, x)
     ref = oo.mul_mat(wq, ob.Q8_0, K, N, x)
     np.testing.assert_array_equal(got, ref)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qt,N,K", [(ob.Q4_K, 1280, 5120), (ob.Q8_0, 4096, 1024)])
+def test_tensor_core_gemm_repeatable(gpu_backend, qt, N, K):
+    """1500 launches of the same tensor-core GEMM give the same bits every time: the
+    kernels' shared-memory refills (weight metadata or scales read by the epilogue, then
+    overwritten by an asynchronous copy) are ordered by proxy fences.  Without them the
+    Q4_K GEMM computed a fragment from the next super-block's metadata about once per
+    500 launches."""
+    import torch
+
+    M = 1500
+    be = gpu_backend
+    w = be.upload_weight(_weights(N, K, qt, 0x0A5A0D00 + N), qt, [K, N])
+    try:
+        x = torch.from_numpy(oo.synth_normal(0x0A5A0D01, M * K).reshape(M, K)).cuda()
+        qa = torch.empty(be.act_bytes(qt, K, M), dtype=torch.uint8, device="cuda")
+        be.quantize_act(qt, x, qa)
+        ref = torch.empty((M, N), dtype=torch.float32, device="cuda")
+        y = torch.empty_like(ref)
+        be.mul_mat_qact(w, qa, M, ref)
+        bad = 0
+        for _ in range(1500):
+            be.mul_mat_qact(w, qa, M, y)
+            bad += int(not torch.equal(y, ref))
+        be.synchronize()
+        assert bad == 0, f"{bad} of 1500 launches differed"
+    finally:
+        w.free()
