@@ -1105,18 +1105,41 @@ def run_b200_qwen(args) -> None:
         torch.cuda.synchronize()
         e2e_s = h0.elapsed_time(h1) / 1e3
         fa = _qwen_fa_roofline(be, torch, stream, B, T + QWEN_NEW // 2)
+        # one decode step alone: (generate NEW - generate 32) / (NEW - 32) steps, CUDA events
+        qs = {}
+        for n in (NEW, 32):
+            model.generate_device(emb_dev[0], B, T, toks_dev, n)
+            q0, q1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            q0.record(stream)
+            for _ in range(3):
+                model.generate_device(emb_dev[0], B, T, toks_dev, n)
+            q1.record(stream)
+            torch.cuda.synchronize()
+            qs[n] = q0.elapsed_time(q1) / 3 * 1e3
+        step_us = (qs[NEW] - qs[32]) / (NEW - 32) if NEW > 32 else None
     audio = om.QWEN_PREFIX_SECONDS * B * args.steps
     dev_s, e2e_s, audio = reduce_over_ranks(dev_s, e2e_s, audio)
     if rank == 0:
         peak, peak_kind = measured_peak_hbm()
         achieved = fa["bytes"] / (fa["us"] * 1e-6) / 1e9
-        sb = whisper_step_bytes(cfg, len(shard[0]), len(om.PROMPT[cfg.n_vocab]), N_NEW)
-        step_ach = sb["total"] / (st["us"] * 1e-6) / 1e9
-        step_line = {"bound": "hbm", "achieved": step_ach, "peak": peak, "unit": "GB/s", "frac": step_ach / peak,
-                     "step_us": st["us"], "algorithmic_bytes": sb,
-                     "how": "one decode step of the batch-8 graph (32 layers + logits head + argmax): rank 0's "
-                            "(generate 224 - generate 32) / 192 steps, CUDA events; bytes = every decoder weight "
-                            "once + all cross K/V + self K/V at the mean cache length"}
+        # algorithmic bytes of one decode step: every Q8_0 weight once (28 layers of q|k|v,
+        # o, gate|up, down, and the tied 151936-row head; 34 B per 32 weights) + the K/V of the
+        # B sequences at the mean cache length (f16, 8 kv heads x 128, K and V)
+        d, L = cfg.d_model, cfg.n_layers
+        kvw = cfg.n_kv_heads * cfg.head_dim
+        per_layer = d * (cfg.n_heads * cfg.head_dim + 2 * kvw) + cfg.n_heads * cfg.head_dim * d + 3 * d * cfg.ffn
+        wbytes = (L * per_layer + cfg.n_vocab * d) * 34 // 32
+        mean_kv = T + (NEW - 1) / 2
+        kvbytes = int(L * B * mean_kv * 2 * kvw * 2)
+        step_line = None
+        if step_us:
+            sa = (wbytes + kvbytes) / (step_us * 1e-6) / 1e9
+            step_line = {"bound": "hbm", "achieved": sa, "peak": peak, "unit": "GB/s", "frac": sa / peak,
+                         "step_us": step_us, "algorithmic_bytes": {"weights": wbytes, "kv": kvbytes,
+                                                                   "total": wbytes + kvbytes},
+                         "how": f"one decode step of the batch-{B} graph (28 layers + logits head + argmax): rank "
+                                f"0's (generate {NEW} - generate 32) / {NEW - 32} steps, CUDA events; bytes = every "
+                                "weight once + K/V at the mean cache length"}
         tokens = B * NEW * args.steps * world
         line = {
             "metric": QWEN_METRIC.replace(f"greedy {QWEN_NEW}", f"greedy {NEW}"), "value": audio / dev_s,
@@ -1146,7 +1169,8 @@ def run_b200_qwen(args) -> None:
                          "algorithmic_bytes": fa["bytes"],
                          "avg_launch_us": fa["us"], "how": "same kernel and shapes through flash_attn_ext, timed alone "
                                                            "on the bench stream from a CUDA graph of 40 launches, "
-                                                           "caches rotated over 8 layers"},
+                                                           "caches rotated over 8 layers",
+                         "step": step_line},
             "clocks": clocks,
         }
         line["cpu_baseline"] = qwen_cpu_baseline()
