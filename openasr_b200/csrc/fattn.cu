@@ -21,6 +21,7 @@
 
 #include <mutex>
 #include <string>
+#include <type_traits>
 
 #include "kernels.cuh"
 #include "fmath.cuh"
@@ -382,6 +383,35 @@ static __device__ void heads_quantize_out(const FaArgs &a, const float *s_out, i
     else q80_chunk(v, q, a.od + s * (K / 32) + 8 * hg, lane);
 }
 
+// d plus the 8 products q_i k_i of two f16 octets as fused multiply-adds in element order
+// (i = 0..7; element 2j is the low half of word j).  fma.rn.f32.f16 takes f16 operands,
+// converts them to f32 exactly and rounds a * b + c once: each step is the value of
+// __fmaf_rn(float(q_i), float(k_i), d), without separate conversions of the operands.
+static __device__ __forceinline__ float dot8_f16(const int4 &q, const int4 &k, float d) {
+    asm("{\n\t.reg .f16 q0, q1, q2, q3, q4, q5, q6, q7, k0, k1, k2, k3, k4, k5, k6, k7;\n\t"
+        "mov.b32 {q0, q1}, %1;\n\tmov.b32 {q2, q3}, %2;\n\tmov.b32 {q4, q5}, %3;\n\tmov.b32 {q6, q7}, %4;\n\t"
+        "mov.b32 {k0, k1}, %5;\n\tmov.b32 {k2, k3}, %6;\n\tmov.b32 {k4, k5}, %7;\n\tmov.b32 {k6, k7}, %8;\n\t"
+        "fma.rn.f32.f16 %0, q0, k0, %0;\n\tfma.rn.f32.f16 %0, q1, k1, %0;\n\t"
+        "fma.rn.f32.f16 %0, q2, k2, %0;\n\tfma.rn.f32.f16 %0, q3, k3, %0;\n\t"
+        "fma.rn.f32.f16 %0, q4, k4, %0;\n\tfma.rn.f32.f16 %0, q5, k5, %0;\n\t"
+        "fma.rn.f32.f16 %0, q6, k6, %0;\n\tfma.rn.f32.f16 %0, q7, k7, %0;\n\t}"
+        : "+f"(d)
+        : "r"(q.x), "r"(q.y), "r"(q.z), "r"(q.w), "r"(k.x), "r"(k.y), "r"(k.z), "r"(k.w));
+    return d;
+}
+
+// 8 floats rounded to f16 and packed as the octet dot8_f16 takes
+static __device__ __forceinline__ int4 pack8_f16(const float (&x)[8]) {
+    int4 r;
+    uint32_t *w = reinterpret_cast<uint32_t *>(&r);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const __half2 h = __floats2half2_rn(x[2 * j], x[2 * j + 1]);
+        w[j] = *reinterpret_cast<const uint32_t *>(&h);
+    }
+    return r;
+}
+
 // One batch of a 4-head decode warp: U positions pb + 4u (u < U) of this lane group's
 // head, K / V as 16-byte pieces (8 dims) per lane; positions >= kv1 carry zero rows and
 // weight 0.  The U scores are independent: compute them all, then fold the block into the
@@ -393,18 +423,11 @@ static __device__ void heads_quantize_out(const FaArgs &a, const float *s_out, i
 // weights are gathered back by shuffles.
 template <int U>
 static __device__ __forceinline__ void heads_consume(int pb, int kv1, float scale, int lane, int sl,
-                                                     const int4 (&kr)[U], const int4 (&vr)[U], const float (&qv)[8],
+                                                     const int4 (&kr)[U], const int4 (&vr)[U], const int4 &qh,
                                                      float &mx, float &sm, float (&acc)[8]) {
     float sc[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-        float kf[8];
-        load8<true>(reinterpret_cast<const char *>(&kr[u]), kf);
-        float d = 0.0f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) d = __fmaf_rn(qv[e], kf[e], d);
-        sc[u] = d;
-    }
+    for (int u = 0; u < U; ++u) sc[u] = dot8_f16(qh, kr[u], 0.0f);
     float wv[U];
     float mnew;
     if constexpr (U == 8) {
@@ -560,6 +583,7 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
     const char *vb = a.v + h * a.v_nb2 + s * a.v_nb3 + sl * 16;
 
     float qv[8];
+    int4 qh;  // qv as f16 octet
     float mx = -INFINITY, sm = 0.0f, acc[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
@@ -586,7 +610,7 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
         }
     };
     auto consume = [&](int pb, const int4 (&kr)[U], const int4 (&vr)[U]) {
-        heads_consume<U>(pb, kv1, a.scale, lane, sl, kr, vr, qv, mx, sm, acc);
+        heads_consume<U>(pb, kv1, a.scale, lane, sl, kr, vr, qh, mx, sm, acc);
     };
 
     int4 kA[U], vA[U], kB[U], vB[U];
@@ -616,6 +640,7 @@ __global__ void __launch_bounds__(128, 2) fattn_heads_kernel(FaArgs a) {
             if (qb) x = __fadd_rn(x, qb[e]);
             qv[e] = __half2float(__float2half_rn(x));
         }
+        qh = pack8_f16(qv);
     }
     if (!early) range();
     int pb = kv0 + warp;
@@ -666,11 +691,10 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
         }
     }
 
-    float qv[G][16];
-    float mx[G], sm[G], acc[G][16];
+    int4 qh[G][2];  // the G query rows' 16 dims of this lane, rounded to f16
+    float mx_own = -INFINITY, sm[G], acc[G][16];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-        mx[g] = -INFINITY;
         sm[g] = 0.0f;
 #pragma unroll
         for (int e = 0; e < 16; ++e) acc[g][e] = 0.0f;
@@ -700,36 +724,54 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
             }
         }
     };
+    // One batch: the G x U partial dots of a lane (head g, position pb + 16 u at index
+    // g U + u) are finished by a transpose-reduce over the group's 8 lanes -- at each
+    // butterfly level a lane keeps half of its partial sums and adds the partner's half
+    // (the pairs of a per-position butterfly, added in the same order: bit-identical
+    // scores) -- so lane sl ends with the whole dot of index sl >> (3 - T) and takes
+    // the batch's exps for that index and its head; the weights and rescale factors
+    // are gathered back by shuffles.  The running maximum of head g lives on the lanes
+    // that finish its dots (mx_own); a factor of exactly 1 leaves the state as it is.
+    static_assert(U == 2, "the transposed batch holds two positions per lane group");
+    constexpr int NV = G * U, T = NV == 8 ? 3 : NV == 4 ? 2 : 1;
+    const int gbase = lane & ~7;
     auto consume = [&](int pb, const int4 (&kr)[U][2], const int4 (&vr)[U][2]) {
-        float sc[G][U];
+        float v[NV];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            float kf[16];
-            load8<true>(reinterpret_cast<const char *>(&kr[u][0]), *reinterpret_cast<float(*)[8]>(&kf[0]));
-            load8<true>(reinterpret_cast<const char *>(&kr[u][1]), *reinterpret_cast<float(*)[8]>(&kf[8]));
-            const bool valid = pb + 16 * u < kv1;
+        for (int u = 0; u < U; ++u)
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                float d = 0.0f;
+            for (int g = 0; g < G; ++g) v[g * U + u] = dot8_f16(qh[g][1], kr[u][1], dot8_f16(qh[g][0], kr[u][0], 0.0f));
+        int idx = 0;
+        auto level = [&](auto n_c, int bit) {  // keep n of 2n partial sums
+            constexpr int n = decltype(n_c)::value;
+            const bool b = sl & bit;
 #pragma unroll
-                for (int e = 0; e < 16; ++e) d = __fmaf_rn(qv[g][e], kf[e], d);
-#pragma unroll
-                for (int o = 4; o > 0; o >>= 1) d = __fadd_rn(d, __shfl_xor_sync(0xffffffffu, d, o));
-                sc[g][u] = valid ? __fmul_rn(d, a.scale) : -INFINITY;
+            for (int j = 0; j < n; ++j) {
+                const float keep = b ? v[j + n] : v[j], send = b ? v[j] : v[j + n];
+                v[j] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, bit));
             }
-        }
+            idx += b ? n : 0;
+        };
+        level(std::integral_constant<int, NV / 2>{}, 4);
+        if constexpr (T >= 2) level(std::integral_constant<int, NV / 4>{}, 2);
+        else v[0] = __fadd_rn(v[0], __shfl_xor_sync(0xffffffffu, v[0], 2));
+        if constexpr (T >= 3) level(std::integral_constant<int, 1>{}, 1);
+        else v[0] = __fadd_rn(v[0], __shfl_xor_sync(0xffffffffu, v[0], 1));
+        const float s1 = pb + 16 * (idx % U) < kv1 ? __fmul_rn(v[0], a.scale) : -INFINITY;
+        const float mb = fmaxf(s1, __shfl_xor_sync(0xffffffffu, s1, 8 >> T));  // the other position
+        const float mnew = fmaxf(mx_own, mb);
+        const float c1 = mnew == -INFINITY ? 1.0f : exp_f32(__fsub_rn(mx_own, mnew));  // mx = -inf -> 0
+        const float e1 = exp_f32(__fsub_rn(s1, mnew));
+        const float w1 = s1 == -INFINITY ? -1.0f : e1;  // -1: no weight (invisible position)
+        mx_own = mnew;
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-            float mb = sc[g][0];
+            const float corr = __shfl_sync(0xffffffffu, c1, gbase | ((g * U) << (3 - T)));
+            if (corr != 1.0f) {
+                sm[g] = __fmul_rn(sm[g], corr);
 #pragma unroll
-            for (int u = 1; u < U; ++u) mb = fmaxf(mb, sc[g][u]);
-            const float mnew = fmaxf(mx[g], mb);
-            if (mnew == -INFINITY) continue;      // nothing visible to this group yet
-            const float corr = exp_f32(__fsub_rn(mx[g], mnew));  // mx = -inf -> 0
-            sm[g] = __fmul_rn(sm[g], corr);
-#pragma unroll
-            for (int e = 0; e < 16; ++e) acc[g][e] = __fmul_rn(acc[g][e], corr);
-            mx[g] = mnew;
+                for (int e = 0; e < 16; ++e) acc[g][e] = __fmul_rn(acc[g][e], corr);
+            }
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -738,8 +780,8 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
             load8<true>(reinterpret_cast<const char *>(&vr[u][1]), *reinterpret_cast<float(*)[8]>(&vf[8]));
 #pragma unroll
             for (int g = 0; g < G; ++g) {
-                if (sc[g][u] == -INFINITY) continue;
-                const float w = exp_f32(__fsub_rn(sc[g][u], mx[g]));
+                const float w = __shfl_sync(0xffffffffu, w1, gbase | ((g * U + u) << (3 - T)));
+                if (w < 0.0f) continue;
                 sm[g] = __fadd_rn(sm[g], w);
 #pragma unroll
                 for (int e = 0; e < 16; ++e) acc[g][e] = __fmaf_rn(w, vf[e], acc[g][e]);
@@ -769,14 +811,17 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
 #pragma unroll
     for (int g = 0; g < G; ++g) {
         const float *qp = reinterpret_cast<const float *>(a.q + (hk * G + g) * a.q_nb2 + s * a.q_nb3) + sl * 16;
+        float x[16];
 #pragma unroll
         for (int e = 0; e < 16; e += 4) {
-            const float4 x = *reinterpret_cast<const float4 *>(qp + e);
-            qv[g][e] = __half2float(__float2half_rn(x.x));
-            qv[g][e + 1] = __half2float(__float2half_rn(x.y));
-            qv[g][e + 2] = __half2float(__float2half_rn(x.z));
-            qv[g][e + 3] = __half2float(__float2half_rn(x.w));
+            const float4 f = *reinterpret_cast<const float4 *>(qp + e);
+            x[e] = f.x;
+            x[e + 1] = f.y;
+            x[e + 2] = f.z;
+            x[e + 3] = f.w;
         }
+        qh[g][0] = pack8_f16(*reinterpret_cast<const float(*)[8]>(&x[0]));
+        qh[g][1] = pack8_f16(*reinterpret_cast<const float(*)[8]>(&x[8]));
     }
     int pb = wbase;
     if (!a_loaded && pb < kv1) load(pb + grp, kA, vA);
@@ -793,7 +838,11 @@ __global__ void __launch_bounds__(128) fattn_gqa_kernel(FaArgs a) {
         pb = pn;
     }
 
-    // merge the warp's 4 position groups (same dims, different positions)
+    // merge the warp's 4 position groups (same dims, different positions); head g's
+    // running maximum from the lanes that kept it
+    float mx[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) mx[g] = __shfl_sync(0xffffffffu, mx_own, gbase | ((g * U) << (3 - T)));
 #pragma unroll
     for (int g = 0; g < G; ++g) {
 #pragma unroll
@@ -1008,8 +1057,11 @@ static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const
     a.n_qtiles = (a.QG + QT - 1) / QT;
     a.scale = scale;
     // one query per (sequence, head), f16 heads contiguous in a KV row: the 4-head kernel
-    const bool heads = D == 64 && k->type == OASR_TYPE_F16 && a.NQ == 1 && a.G == 1 && !mask && a.H % 4 == 0 &&
-                       k->nb[2] == 2 * D && v->nb[2] == 2 * D && a.S * (int64_t)(a.H / 4) <= (1 << 16);
+    const bool heads = D == 64 && k->type == OASR_TYPE_F16 && v->type == OASR_TYPE_F16 && a.NQ == 1 && a.G == 1 &&
+                       !mask && a.H % 4 == 0 && k->nb[2] == 2 * D && v->nb[2] == 2 * D &&
+                       k->nb[1] % 16 == 0 && k->nb[3] % 16 == 0 && v->nb[1] % 16 == 0 && v->nb[3] % 16 == 0 &&
+                       ((uintptr_t)k->data & 15) == 0 && ((uintptr_t)v->data & 15) == 0 &&
+                       a.S * (int64_t)(a.H / 4) <= (1 << 16);
     // one query per (sequence, head) over head-major f16 caches with 256-byte rows: the GQA kernel
     const bool gqa = !heads && D == 128 && k->type == OASR_TYPE_F16 && v->type == OASR_TYPE_F16 && a.NQ == 1 &&
                      !mask && !q_bias && (a.G == 1 || a.G == 2 || a.G == 4) && k->nb[1] == 256 && v->nb[1] == 256 &&
