@@ -156,6 +156,7 @@ constexpr int FA_HEADS_U = 8;            // KV positions per warp load batch (do
 constexpr int FA_HEADS_MAX_SPLITS = 16;  // most KV splits of one query row (partials staged by the merging CTA)
 constexpr int FA_GQA_U = 2;              // KV positions per lane group and load batch (double buffered)
 constexpr int FA_SPLITS_HEADS = 7;       // KV splits of the 4-head decode kernel
+constexpr int FA_HEADS_SPLIT_MIN = 513;  // shorter caches run unsplit (4-head kernel)
 constexpr int FA_SPLITS_GQA = 4;         // KV splits of the GQA decode kernel
 
 template <int D, int QT, bool F16>
@@ -1090,7 +1091,10 @@ static int launch_flash_attn_split(oasr_backend *be, const oasr_tensor *q, const
     // positions per split.  Tickets exist for 2^16 groups.
     int n_splits = 1;
     if (groups <= (1 << 16)) {
-        if (heads) n_splits = std::min(FA_SPLITS_HEADS, a.NKV / 32);
+        // 4-head kernel: a cache of at most 512 positions (the decoder's self-attention,
+        // n_text_ctx 448) is one split per CTA -- the outputs are written directly, with no
+        // partials, tickets or merge, whose fixed cost exceeds the extra batches per warp
+        if (heads) n_splits = a.NKV < FA_HEADS_SPLIT_MIN ? 1 : std::min(FA_SPLITS_HEADS, a.NKV / 32);
         else if (gqa) n_splits = std::min(FA_SPLITS_GQA, a.NKV / 32);
         else n_splits = std::min(FA_HEADS_MAX_SPLITS, a.NKV / 64);
         n_splits = std::max(1, n_splits);

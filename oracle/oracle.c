@@ -925,12 +925,15 @@ void oo_norm_dev(const float *x, float *y, int64_t n, int64_t rows, float eps, i
 
 /* ---- decode attention, device order ------------------------------------------------- */
 #define FA_SPLITS_HEADS 7
+#define FA_HEADS_SPLIT_MIN 513 /* shorter caches run unsplit in the 4-head kernel */
 #define FA_SPLITS_GQA 4
 #define FA_SPLITS_MAX 16
 
 int oo_fa_device_splits(int kind, int64_t nkv_max, int64_t groups) {
     if (groups > (1 << 16)) return 1;
-    int64_t n = kind == OO_FAK_HEADS ? (nkv_max / 32 < FA_SPLITS_HEADS ? nkv_max / 32 : FA_SPLITS_HEADS)
+    int64_t n = kind == OO_FAK_HEADS ? (nkv_max < FA_HEADS_SPLIT_MIN                ? 1
+                                        : nkv_max / 32 < FA_SPLITS_HEADS ? nkv_max / 32
+                                                                         : FA_SPLITS_HEADS)
               : kind == OO_FAK_GQA   ? (nkv_max / 32 < FA_SPLITS_GQA ? nkv_max / 32 : FA_SPLITS_GQA)
                                      : (nkv_max / 64 < FA_SPLITS_MAX ? nkv_max / 64 : FA_SPLITS_MAX);
     return n < 1 ? 1 : (int)n;

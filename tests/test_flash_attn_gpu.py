@@ -336,7 +336,7 @@ def _fa_views(be, q, kview, vview, mask, scale):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("S", [1, 3, 8])
-@pytest.mark.parametrize("n_kv", [1, 5, 33, 448, 1500])
+@pytest.mark.parametrize("n_kv", [1, 5, 33, 448, 513, 1500])
 def test_heads_decode_kernel_is_bit_exact(gpu_backend, S, n_kv):
     """Whisper-large decoder layout (20 heads of 64, heads contiguous in a cache row):
     the 4-head kernel, self-attention cache [seq][pos][d] and the cross cache whose row

@@ -131,9 +131,9 @@ def test_static_fresh_backend_never_grows_scratch():
 def test_static_rejects_oversize_split(case):
     """Split plans depend on the shapes only, so both limits are reached on any device:
     300 query rows of 8 heads at D = 128 over 256 keys split 4 ways need ~5 MB of
-    partials (the array holds 4 MiB); 256 sequences of 20 heads in the 4-head layout are
-    1280 split groups (1024 tickets).  Each call must fail with the sizes named, launch
-    nothing, and leave the backend working."""
+    partials (the array holds 4 MiB); 130 sequences of 8 kv heads in the GQA layout over
+    128 keys are 1040 split groups (1024 tickets).  Each call must fail with the sizes
+    named, launch nothing, and leave the backend working."""
     import torch
 
     be = ob.Backend(0)
@@ -144,9 +144,12 @@ def test_static_rejects_oversize_split(case):
             q, k, v, _ = _inputs(12, 1, H, 1, NQ, 256, D, False)
             out = _out(1, H, NQ, D)
         else:
-            H, NQ, D = 20, 1, 64
-            q, k, v, _ = _heads_inputs(14, 256, H, 64)
-            out = _out(256, H, NQ, D)
+            S, H, NQ, D = 130, 8, 1, 128
+            g = torch.Generator(device="cuda").manual_seed(14)
+            q = torch.randn((S, H, NQ, D), generator=g, device="cuda", dtype=torch.float32)
+            k = torch.randn((S, H, 128, D), generator=g, device="cuda", dtype=torch.float32).half()
+            v = torch.randn((S, H, 128, D), generator=g, device="cuda", dtype=torch.float32).half()
+            out = _out(S, H, NQ, D)
         with pytest.raises(ob.GgmlBackendError) as ei:
             be.flash_attn_ext_static(q, k, v, None, 1.0 / np.sqrt(D), out)
         assert "static scratch holds" in str(ei.value)
